@@ -1,0 +1,290 @@
+// Python bindings of the sm_100a kernels.  Every entry point checks device, dtype, contiguity and
+// alignment, then launches on the current CUDA stream; nothing here allocates except where an
+// output is returned.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "gemm_sm100.cuh"
+#include "ops.h"
+
+namespace {
+
+using trida::bf16;
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == at::kBFloat16, #x " must be bfloat16")
+#define CHECK_F32(x) TORCH_CHECK((x).scalar_type() == at::kFloat, #x " must be float32")
+#define CHECK_ROWMAJOR(x) TORCH_CHECK((x).dim() == 2 && (x).stride(1) == 1, #x " must be a row-major matrix")
+
+int sm_count() {
+  static int n = 0;
+  if (!n) n = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  return n;
+}
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
+
+const bf16* cbf(const at::Tensor& t) { return reinterpret_cast<const bf16*>(t.data_ptr()); }
+bf16* mbf(const at::Tensor& t) { return reinterpret_cast<bf16*>(t.data_ptr()); }
+
+// D = alpha * op(A) op(B) + beta * C.  layout: 0 = TN (A[M,K], B[N,K]), 1 = TT (A[M,K], B[K,N]),
+// 2 = NT (A[K,M], B[K,N]).  All operands row-major 2-D views; D bf16 or fp32.
+void gemm(int64_t layout, const at::Tensor& A, const at::Tensor& B, const at::Tensor& D,
+          const c10::optional<at::Tensor>& C, double alpha, double beta, int64_t tile) {
+  CHECK_CUDA(A); CHECK_CUDA(B); CHECK_CUDA(D);
+  CHECK_BF16(A); CHECK_BF16(B);
+  CHECK_ROWMAJOR(A); CHECK_ROWMAJOR(B); CHECK_ROWMAJOR(D);
+  const bool f32 = D.scalar_type() == at::kFloat;
+  TORCH_CHECK(f32 || D.scalar_type() == at::kBFloat16, "D must be bf16 or fp32");
+  trida::GemmArgs a{};
+  int M, N, K;
+  if (layout == 0) { M = A.size(0); K = A.size(1); N = B.size(0); TORCH_CHECK(B.size(1) == K, "K mismatch"); }
+  else if (layout == 1) { M = A.size(0); K = A.size(1); N = B.size(1); TORCH_CHECK(B.size(0) == K, "K mismatch"); }
+  else { K = A.size(0); M = A.size(1); N = B.size(1); TORCH_CHECK(B.size(0) == K, "K mismatch"); }
+  TORCH_CHECK(D.size(0) == M && D.size(1) == N, "D shape mismatch");
+  a.M = M; a.N = N; a.K = K;
+  a.A = A.data_ptr(); a.lda = A.stride(0);
+  a.B = B.data_ptr(); a.ldb = B.stride(0);
+  a.D = D.data_ptr(); a.ldd = D.stride(0);
+  if (C.has_value() && C->defined()) {
+    CHECK_CUDA((*C)); CHECK_ROWMAJOR((*C));
+    TORCH_CHECK(C->scalar_type() == D.scalar_type(), "C dtype must match D");
+    TORCH_CHECK(C->size(0) == M && C->size(1) == N, "C shape mismatch");
+    a.C = C->data_ptr(); a.ldc = C->stride(0);
+  } else {
+    TORCH_CHECK(beta == 0.0, "beta != 0 needs a C operand");
+    a.C = nullptr; a.ldc = a.ldd;
+  }
+  a.alpha = (float)alpha; a.beta = (float)beta;
+  a.batch = 1;
+  a.strideA_batch = a.strideB_batch = a.strideC_batch = a.strideD_batch = 0;
+  if (M == 0 || N == 0) return;
+  TORCH_CHECK(K > 0, "K must be positive");
+  const int elemD = f32 ? 4 : 2;
+  TORCH_CHECK((a.lda * 2) % 16 == 0 && (a.ldb * 2) % 16 == 0 && (a.ldd * elemD) % 16 == 0,
+              "GEMM leading dimensions must be 16-byte multiples");
+  TORCH_CHECK(((uintptr_t)a.A % 16 == 0) && ((uintptr_t)a.B % 16 == 0) && ((uintptr_t)a.D % 16 == 0),
+              "GEMM operands must be 16-byte aligned");
+  c10::cuda::CUDAGuard g(A.device());
+  const int rc = trida::gemm_bf16((trida::GemmLayout)layout, f32, a, (int)tile, sm_count(), stream());
+  TORCH_CHECK(rc == 0, "sm100 GEMM failed with code ", rc, " (M=", M, " N=", N, " K=", K, " layout=", layout, ")");
+}
+
+std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, double eps, const at::Tensor& out) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(w); CHECK_ROWMAJOR(x); CHECK_ROWMAJOR(out);
+  const int M = x.size(0), D = x.size(1);
+  TORCH_CHECK(D % 8 == 0, "hidden size must be a multiple of 8");
+  auto rstd = at::empty({M}, x.options().dtype(at::kFloat));
+  trida::rmsnorm_fwd(cbf(x), x.stride(0), cbf(w), mbf(out), out.stride(0), rstd.data_ptr<float>(), M, D, (float)eps,
+                     stream());
+  return {out, rstd};
+}
+
+void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd,
+                 const c10::optional<at::Tensor>& dres, const at::Tensor& dx, const c10::optional<at::Tensor>& dw) {
+  CHECK_BF16(dy); CHECK_BF16(x); CHECK_ROWMAJOR(dy); CHECK_ROWMAJOR(x); CHECK_ROWMAJOR(dx);
+  const int M = x.size(0), D = x.size(1);
+  const bf16* pr = nullptr; int64_t ldr = 0;
+  if (dres.has_value() && dres->defined()) { CHECK_ROWMAJOR((*dres)); pr = cbf(*dres); ldr = dres->stride(0); }
+  float* pdw = nullptr;
+  if (dw.has_value() && dw->defined()) { CHECK_F32((*dw)); pdw = dw->data_ptr<float>(); }
+  trida::rmsnorm_bwd(cbf(dy), dy.stride(0), cbf(x), x.stride(0), cbf(w), rstd.data_ptr<float>(), pr, ldr, mbf(dx),
+                     dx.stride(0), pdw, M, D, sm_count(), stream());
+}
+
+at::Tensor qk_norm_rope_fwd(const at::Tensor& qkv, const at::Tensor& qw, const at::Tensor& kw,
+                            const at::Tensor& cos_t, const at::Tensor& sin_t, const at::Tensor& pos,
+                            const at::Tensor& q, const at::Tensor& k, int64_t Hq, int64_t Hkv, int64_t d,
+                            int64_t rd, double eps) {
+  CHECK_BF16(qkv); CHECK_ROWMAJOR(qkv); CHECK_F32(cos_t); CHECK_F32(sin_t);
+  TORCH_CHECK(pos.scalar_type() == at::kInt && pos.is_contiguous(), "pos must be contiguous int32");
+  TORCH_CHECK(q.is_contiguous() && k.is_contiguous(), "q/k outputs must be contiguous");
+  const int M = qkv.size(0);
+  auto rstd = at::empty({M, Hq + Hkv}, qkv.options().dtype(at::kFloat));
+  trida::qk_norm_rope_fwd(cbf(qkv), qkv.stride(0), cbf(qw), cbf(kw), cos_t.data_ptr<float>(),
+                          sin_t.data_ptr<float>(), pos.data_ptr<int>(), mbf(q), mbf(k), rstd.data_ptr<float>(), M,
+                          Hq, Hkv, d, rd, (float)eps, stream());
+  return rstd;
+}
+
+void qk_norm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Tensor& qkv, const at::Tensor& qw,
+                      const at::Tensor& kw, const at::Tensor& cos_t, const at::Tensor& sin_t, const at::Tensor& pos,
+                      const at::Tensor& rstd, const at::Tensor& dqkv, const c10::optional<at::Tensor>& dqw,
+                      const c10::optional<at::Tensor>& dkw, int64_t Hq, int64_t Hkv, int64_t d, int64_t rd) {
+  CHECK_ROWMAJOR(qkv); CHECK_ROWMAJOR(dqkv);
+  TORCH_CHECK(dq.is_contiguous() && dk.is_contiguous(), "dq/dk must be contiguous");
+  const int M = qkv.size(0);
+  float* pq = (dqw.has_value() && dqw->defined()) ? dqw->data_ptr<float>() : nullptr;
+  float* pk = (dkw.has_value() && dkw->defined()) ? dkw->data_ptr<float>() : nullptr;
+  trida::qk_norm_rope_bwd(cbf(dq), cbf(dk), cbf(qkv), qkv.stride(0), cbf(qw), cbf(kw), cos_t.data_ptr<float>(),
+                          sin_t.data_ptr<float>(), pos.data_ptr<int>(), rstd.data_ptr<float>(), mbf(dqkv),
+                          dqkv.stride(0), pq, pk, M, Hq, Hkv, d, rd, sm_count(), stream());
+}
+
+void swiglu_fwd(const at::Tensor& gu, const at::Tensor& out) {
+  CHECK_BF16(gu); CHECK_ROWMAJOR(gu); CHECK_ROWMAJOR(out);
+  const int M = gu.size(0), F = gu.size(1) / 2;
+  TORCH_CHECK(F % 8 == 0, "FFN size must be a multiple of 8");
+  trida::swiglu_fwd(cbf(gu), gu.stride(0), mbf(out), out.stride(0), M, F, sm_count(), stream());
+}
+
+void swiglu_bwd(const at::Tensor& da, const at::Tensor& gu, const at::Tensor& dgu) {
+  CHECK_ROWMAJOR(da); CHECK_ROWMAJOR(gu); CHECK_ROWMAJOR(dgu);
+  const int M = gu.size(0), F = gu.size(1) / 2;
+  trida::swiglu_bwd(cbf(da), da.stride(0), cbf(gu), gu.stride(0), mbf(dgu), dgu.stride(0), M, F, sm_count(),
+                    stream());
+}
+
+void embed_fwd(const at::Tensor& ids, const at::Tensor& table, const at::Tensor& out) {
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous(), "ids must be contiguous int64");
+  CHECK_BF16(table); CHECK_ROWMAJOR(table);
+  TORCH_CHECK(out.is_contiguous(), "out must be contiguous");
+  trida::embed_fwd(ids.data_ptr<int64_t>(), cbf(table), mbf(out), ids.numel(), table.size(1), stream());
+}
+
+void embed_bwd(const at::Tensor& ids, const at::Tensor& dout, const at::Tensor& dtable) {
+  CHECK_F32(dtable);
+  TORCH_CHECK(dout.is_contiguous(), "dout must be contiguous");
+  trida::embed_bwd(ids.data_ptr<int64_t>(), cbf(dout), dtable.data_ptr<float>(), ids.numel(), dtable.size(1),
+                   stream());
+}
+
+// meta: [B, T, 4] int32.  Returns (cls, fwd_list, fwd_cnt, bwd_list, bwd_cnt).
+std::vector<at::Tensor> bd_attn_plan(const at::Tensor& meta, int64_t flags) {
+  TORCH_CHECK(meta.scalar_type() == at::kInt && meta.is_contiguous() && meta.dim() == 3 && meta.size(2) == 4,
+              "meta must be contiguous int32 [B, T, 4]");
+  const int B = meta.size(0), T = meta.size(1);
+  const int nt = (T + 63) / 64, nq2 = (nt + 1) / 2;
+  TORCH_CHECK(nt < (1 << 14), "sequence too long for the tile lists");
+  auto o8 = meta.options().dtype(at::kByte);
+  auto o16 = meta.options().dtype(at::kShort);
+  auto o32 = meta.options().dtype(at::kInt);
+  auto cls = at::empty({B, nt, nt}, o8);
+  auto fl = at::empty({B, nq2, nt}, o16);
+  auto fc = at::empty({B, nq2}, o32);
+  auto bl = at::empty({B, nt, nt}, o16);
+  auto bc = at::empty({B, nt}, o32);
+  trida::bd_attn_plan(reinterpret_cast<const int4*>(meta.data_ptr<int>()), B, T, (int)flags, cls.data_ptr<uint8_t>(),
+                      fl.data_ptr<int16_t>(), fc.data_ptr<int>(), bl.data_ptr<int16_t>(), bc.data_ptr<int>(),
+                      stream());
+  return {cls, fl, fc, bl, bc};
+}
+
+// q [B,T,Hq,D], k [B,T,Hkv,D], v [B,T,Hkv,D] (token stride may differ: strided views allowed when
+// the innermost two dims are dense), o [B,T,Hq,D], lse [B,Hq,T].
+trida::AttnTensors attn_tensors(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+                                const at::Tensor& lse) {
+  for (auto* t : {&q, &k, &v, &o}) {
+    TORCH_CHECK(t->dim() == 4 && t->stride(3) == 1 && t->stride(2) == t->size(3), "attention operand layout");
+    CHECK_BF16((*t));
+    TORCH_CHECK(((uintptr_t)t->data_ptr() % 16) == 0 && (t->stride(1) % 8) == 0, "attention operand alignment");
+  }
+  CHECK_F32(lse);
+  trida::AttnTensors a;
+  a.q = cbf(q); a.k = cbf(k); a.v = cbf(v);
+  a.q_tok = q.stride(1); a.k_tok = k.stride(1); a.v_tok = v.stride(1);
+  a.q_b = q.stride(0); a.k_b = k.stride(0); a.v_b = v.stride(0);
+  a.o = mbf(o); a.o_tok = o.stride(1); a.o_b = o.stride(0);
+  a.lse = lse.data_ptr<float>();
+  a.B = q.size(0); a.T = q.size(1); a.Hq = q.size(2); a.Hkv = k.size(2); a.D = q.size(3);
+  TORCH_CHECK(a.Hq % a.Hkv == 0, "Hq must be a multiple of Hkv");
+  return a;
+}
+
+void bd_attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+                 const at::Tensor& lse, const at::Tensor& meta, const at::Tensor& fwd_list, const at::Tensor& fwd_cnt,
+                 int64_t flags, double scale) {
+  auto a = attn_tensors(q, k, v, o, lse);
+  const int rc = trida::bd_attn_fwd(a, reinterpret_cast<const int4*>(meta.data_ptr<int>()),
+                                    fwd_list.data_ptr<int16_t>(), fwd_cnt.data_ptr<int>(), (int)flags, (float)scale,
+                                    stream());
+  TORCH_CHECK(rc == 0, "bd_attn_fwd: unsupported head_dim ", a.D);
+}
+
+void bd_attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+                 const at::Tensor& lse, const at::Tensor& dout, const at::Tensor& dq, const at::Tensor& dk,
+                 const at::Tensor& dv, const at::Tensor& meta, const at::Tensor& bwd_list, const at::Tensor& bwd_cnt,
+                 int64_t flags, double scale) {
+  auto a = attn_tensors(q, k, v, o, lse);
+  for (auto* t : {&dout, &dq, &dk, &dv})
+    TORCH_CHECK(t->dim() == 4 && t->stride(3) == 1 && t->stride(2) == t->size(3), "attention grad layout");
+  auto dsum = at::empty({a.B, a.Hq, a.T}, lse.options());
+  auto dq_acc = at::empty({a.B, a.T, a.Hq, a.D}, lse.options());
+  const int rc = trida::bd_attn_bwd(a, cbf(dout), dout.stride(1), dout.stride(0), dsum.data_ptr<float>(),
+                                    dq_acc.data_ptr<float>(), mbf(dq), dq.stride(1), dq.stride(0), mbf(dk),
+                                    dk.stride(1), dk.stride(0), mbf(dv), dv.stride(1), dv.stride(0),
+                                    reinterpret_cast<const int4*>(meta.data_ptr<int>()), bwd_list.data_ptr<int16_t>(),
+                                    bwd_cnt.data_ptr<int>(), (int)flags, (float)scale, sm_count(), stream());
+  TORCH_CHECK(rc == 0, "bd_attn_bwd: unsupported head_dim ", a.D);
+}
+
+void ce_rows(const at::Tensor& logits, const at::Tensor& target, const c10::optional<at::Tensor>& weight,
+             double grad_scale, const at::Tensor& loss, const c10::optional<at::Tensor>& dlogits) {
+  CHECK_F32(logits); CHECK_ROWMAJOR(logits);
+  TORCH_CHECK(target.scalar_type() == at::kLong && target.is_contiguous(), "target must be contiguous int64");
+  TORCH_CHECK((logits.stride(0) % 4) == 0 && (logits.size(1) % 4) == 0, "logit rows must be float4-aligned");
+  const float* pw = (weight.has_value() && weight->defined()) ? weight->data_ptr<float>() : nullptr;
+  bf16* pd = nullptr; int64_t ldd = 0;
+  if (dlogits.has_value() && dlogits->defined()) { CHECK_ROWMAJOR((*dlogits)); pd = mbf(*dlogits); ldd = dlogits->stride(0); }
+  trida::ce_rows_fwd_bwd(logits.data_ptr<float>(), logits.stride(0), target.data_ptr<int64_t>(), pw,
+                         (float)grad_scale, logits.size(0), logits.size(1), loss.data_ptr<float>(), pd, ldd,
+                         stream());
+}
+
+// Global-norm clip: writes norm and clip coefficient (device scalars) from a list of fp32 buffers.
+void grad_norm(const std::vector<at::Tensor>& grads, double max_norm, const at::Tensor& norm_out,
+               const at::Tensor& coef_out) {
+  const int per = 256;
+  auto partial = at::empty({(int64_t)grads.size() * per}, norm_out.options());
+  for (size_t i = 0; i < grads.size(); ++i) {
+    CHECK_F32(grads[i]);
+    TORCH_CHECK(grads[i].is_contiguous(), "grad buffers must be contiguous");
+    trida::sumsq_partial(grads[i].data_ptr<float>(), grads[i].numel(), partial.data_ptr<float>() + i * per, per,
+                         stream());
+  }
+  trida::clip_coef(partial.data_ptr<float>(), (int)grads.size() * per, (float)max_norm, norm_out.data_ptr<float>(),
+                   coef_out.data_ptr<float>(), stream());
+}
+
+void adamw(const at::Tensor& param, const c10::optional<at::Tensor>& master, const at::Tensor& grad,
+           const at::Tensor& m, const at::Tensor& v, double lr, double beta1, double beta2, double eps, double wd,
+           int64_t step, const c10::optional<at::Tensor>& coef) {
+  CHECK_F32(grad); CHECK_F32(m); CHECK_F32(v);
+  TORCH_CHECK(grad.numel() == param.numel() && m.numel() == param.numel() && v.numel() == param.numel(), "size");
+  const float* pc = (coef.has_value() && coef->defined()) ? coef->data_ptr<float>() : nullptr;
+  if (master.has_value() && master->defined()) {
+    CHECK_F32((*master));
+    bf16* pb = param.scalar_type() == at::kBFloat16 ? mbf(param) : nullptr;
+    trida::adamw_step(master->data_ptr<float>(), pb, grad.data_ptr<float>(), m.data_ptr<float>(),
+                      v.data_ptr<float>(), param.numel(), lr, beta1, beta2, eps, wd, (int)step, pc, stream());
+  } else if (param.scalar_type() == at::kFloat) {
+    trida::adamw_step(param.data_ptr<float>(), nullptr, grad.data_ptr<float>(), m.data_ptr<float>(),
+                      v.data_ptr<float>(), param.numel(), lr, beta1, beta2, eps, wd, (int)step, pc, stream());
+  } else {
+    CHECK_BF16(param);
+    trida::adamw_step_bf16(mbf(param), grad.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+                           param.numel(), lr, beta1, beta2, eps, wd, (int)step, pc, stream());
+  }
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "trida_stack_b200 sm_100a kernels";
+  m.def("gemm", &gemm);
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);
+  m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("embed_fwd", &embed_fwd);
+  m.def("embed_bwd", &embed_bwd);
+  m.def("bd_attn_plan", &bd_attn_plan);
+  m.def("bd_attn_fwd", &bd_attn_fwd);
+  m.def("bd_attn_bwd", &bd_attn_bwd);
+  m.def("ce_rows", &ce_rows);
+  m.def("grad_norm", &grad_norm);
+  m.def("adamw", &adamw);
+}

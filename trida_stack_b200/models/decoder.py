@@ -1,0 +1,159 @@
+"""Native Qwen3 / Qwen3.5 decoder (no HF modules).
+
+Weights are stored fused for the tensor-core GEMMs -- ``wqkv = [q; k; v]`` and ``wgu = [gate; up]``
+-- and mapped to the HF safetensors names on load/save (``hf_state_dict`` /
+``load_hf_state_dict``), so checkpoints stay interchangeable with transformers.  The decoder math
+is HF's Qwen3 math (pre-norm residual blocks, per-head q/k RMSNorm, half-split RoPE, SwiGLU).
+"""
+import torch
+import torch.nn as nn
+
+from ..ops import blocks
+from .config import ModelConfig
+
+
+class AttentionLayer(nn.Module):
+    """Pre-norm attention sub-block + SwiGLU MLP sub-block (one HF decoder layer)."""
+
+    def __init__(self, cfg: ModelConfig, dtype):
+        super().__init__()
+        D, d = cfg.hidden_size, cfg.head_dim
+        q_out = cfg.n_heads * d * (2 if cfg.attn_output_gate else 1)
+        self.input_norm = nn.Parameter(torch.ones(D, dtype=dtype))
+        self.wqkv = nn.Parameter(torch.empty(q_out + 2 * cfg.n_kv_heads * d, D, dtype=dtype))
+        self.q_norm = nn.Parameter(torch.ones(d, dtype=dtype))
+        self.k_norm = nn.Parameter(torch.ones(d, dtype=dtype))
+        self.wo = nn.Parameter(torch.empty(D, cfg.n_heads * d, dtype=dtype))
+        self.post_norm = nn.Parameter(torch.ones(D, dtype=dtype))
+        self.wgu = nn.Parameter(torch.empty(2 * cfg.intermediate_size, D, dtype=dtype))
+        self.wdown = nn.Parameter(torch.empty(D, cfg.intermediate_size, dtype=dtype))
+        self.layer_type = "full_attention"
+
+    def forward(self, x, actx, cfg):
+        x = blocks.attn_block(x, self.input_norm, self.wqkv, self.q_norm, self.k_norm, self.wo, actx, cfg)
+        return blocks.mlp_block(x, self.post_norm, self.wgu, self.wdown, cfg.eps)
+
+    # HF <-> fused names
+    def hf_items(self, prefix, cfg):
+        d, Hq, Hkv, F = cfg.head_dim, cfg.n_heads, cfg.n_kv_heads, cfg.intermediate_size
+        qn = Hq * d * (2 if cfg.attn_output_gate else 1)
+        kn = Hkv * d
+        return [
+            (prefix + "input_layernorm.weight", self.input_norm, None),
+            (prefix + "self_attn.q_proj.weight", self.wqkv, (0, qn)),
+            (prefix + "self_attn.k_proj.weight", self.wqkv, (qn, qn + kn)),
+            (prefix + "self_attn.v_proj.weight", self.wqkv, (qn + kn, qn + 2 * kn)),
+            (prefix + "self_attn.q_norm.weight", self.q_norm, None),
+            (prefix + "self_attn.k_norm.weight", self.k_norm, None),
+            (prefix + "self_attn.o_proj.weight", self.wo, None),
+            (prefix + "post_attention_layernorm.weight", self.post_norm, None),
+            (prefix + "mlp.gate_proj.weight", self.wgu, (0, F)),
+            (prefix + "mlp.up_proj.weight", self.wgu, (F, 2 * F)),
+            (prefix + "mlp.down_proj.weight", self.wdown, None),
+        ]
+
+
+class Decoder(nn.Module):
+    """Token embedding -> decoder layers -> final RMSNorm; LM head tied or separate."""
+
+    def __init__(self, cfg: ModelConfig, dtype=torch.bfloat16, device=None):
+        super().__init__()
+        self.cfg = cfg
+        D = cfg.hidden_size
+        with torch.device(device or "cpu"):
+            self.embed = nn.Parameter(torch.empty(cfg.vocab_size, D, dtype=dtype))
+            layers = []
+            for t in cfg.layer_types:
+                if t == "linear_attention":
+                    from .gdn import GatedDeltaLayer
+                    layers.append(GatedDeltaLayer(cfg, dtype))
+                else:
+                    layers.append(AttentionLayer(cfg, dtype))
+            self.layers = nn.ModuleList(layers)
+            self.norm = nn.Parameter(torch.ones(D, dtype=dtype))
+            self.lm_head = None if cfg.tie_embeddings else nn.Parameter(torch.empty(cfg.vocab_size, D, dtype=dtype))
+        self.reset_parameters()
+
+    @property
+    def lm_weight(self):
+        return self.embed if self.lm_head is None else self.lm_head
+
+    @torch.no_grad()
+    def reset_parameters(self, generator=None):
+        """HF ``_init_weights``: N(0, initializer_range) for matrices, ones for norms."""
+        std = self.cfg.initializer_range
+        for name, p in self.named_parameters():
+            if p.dim() >= 2:
+                p.normal_(0.0, std, generator=generator)
+            elif name.endswith("A_log"):
+                p.copy_(torch.log(torch.empty_like(p, dtype=torch.float32).uniform_(0, 16, generator=generator)))
+            elif name.endswith("dt_bias"):
+                p.fill_(1.0)
+            elif name.endswith("conv_w"):
+                p.normal_(0.0, std, generator=generator)
+            else:
+                p.fill_(1.0)
+
+    def resize_vocab(self, new_size):
+        """Grow/shrink the vocabulary rows (HF ``resize_token_embeddings``): kept rows unchanged,
+        new rows initialised N(0, initializer_range)."""
+        old = self.cfg.vocab_size
+        if new_size == old:
+            return
+        with torch.no_grad():
+            for attr in ("embed", "lm_head"):
+                p = getattr(self, attr)
+                if p is None:
+                    continue
+                n = torch.empty(new_size, p.shape[1], dtype=p.dtype, device=p.device)
+                k = min(old, new_size)
+                n[:k] = p[:k]
+                if new_size > old:
+                    n[old:].normal_(0.0, self.cfg.initializer_range)
+                setattr(self, attr, nn.Parameter(n))
+        self.cfg.vocab_size = new_size
+
+    def embed_tokens(self, ids):
+        return blocks.embedding(ids, self.embed)
+
+    def forward(self, x, actx, layer_hook=None):
+        """x: embedded tokens [B*T, D] -> final-normed hidden states [B*T, D]."""
+        for i, layer in enumerate(self.layers):
+            x = layer_hook(i, layer, x) if layer_hook is not None else layer(x, actx, self.cfg)
+        return blocks.rmsnorm(x, self.norm, self.cfg.eps)
+
+    # ---------------------------------------------------------------- HF state dict mapping
+    def hf_items(self):
+        items = [("model.embed_tokens.weight", self.embed, None)]
+        for i, layer in enumerate(self.layers):
+            items += layer.hf_items(f"model.layers.{i}.", self.cfg)
+        items.append(("model.norm.weight", self.norm, None))
+        if self.lm_head is not None:
+            items.append(("lm_head.weight", self.lm_head, None))
+        return items
+
+    @torch.no_grad()
+    def hf_state_dict(self, dtype=None):
+        out = {}
+        for name, p, sl in self.hf_items():
+            t = p if sl is None else p[sl[0]:sl[1]]
+            out[name] = (t.to(dtype) if dtype is not None else t).detach().contiguous()
+        return out
+
+    @torch.no_grad()
+    def load_hf_state_dict(self, sd, strict=True):
+        missing = []
+        for name, p, sl in self.hf_items():
+            src = sd.get(name)
+            if src is None and name.startswith("model.") and ("model.language_model." + name[6:]) in sd:
+                src = sd["model.language_model." + name[6:]]
+            if src is None:
+                missing.append(name)
+                continue
+            dst = p if sl is None else p[sl[0]:sl[1]]
+            if tuple(src.shape) != tuple(dst.shape):
+                raise ValueError(f"{name}: checkpoint shape {tuple(src.shape)} != model {tuple(dst.shape)}")
+            dst.copy_(src.to(dst.dtype))
+        if strict and missing:
+            raise KeyError(f"missing weights: {missing[:8]}{'...' if len(missing) > 8 else ''}")
+        return missing
