@@ -1,0 +1,364 @@
+#!/usr/bin/env python3
+"""Flagship benchmark: Qwen3-4B block-diffusion SFT tokens/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+For N > 1 launch one rank per GPU with torch.distributed.run (RANK / LOCAL_RANK / WORLD_SIZE /
+MASTER_* from the environment).  Model: Qwen3-4B architecture (36 layers, hidden 2560, 32 Q / 8 KV
+heads x 128, SwiGLU 9728, vocab 151936 incl. the <|mask|> token, RoPE theta 1e6, tied embeddings),
+random init, bf16.  Data: synthetic rows of [prompt 1024 | response 1024] uniform token ids,
+micro-batch 4 per GPU, one micro-batch per optimizer step; the block-diffusion layout makes each
+forward row [S 1024 | x_t 1024 | x_0 1024] = 3072 tokens for 2 complementary views.  Objective:
+bd_size 32, per-block mask rate ~U(1e-3, 1), AR auxiliary weight 1.0; AdamW lr 1e-5.
+
+Metric: tokens/s over the whole job, counted like the reference trainer's ``tot_tps``
+(``input_ids.numel()`` per micro-batch, summed over ranks).  ``value``: K steps device-timed with
+CUDA events between a barrier + synchronize on both sides, max over ranks.  ``e2e``: the same K
+steps through ``TrainEngine.train_step`` with each step's batch copied from pinned host memory and
+the loss read back to the host.  Each step's working set (activations ~60 GB) is far larger than
+the 126 MB L2, so no explicit flush is needed between steps.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+BASELINE_TPS = None  # BASELINE.md publishes no number for this config (H100 figures are other configs)
+METRIC = "4B block-diffusion SFT tokens/s"
+PROMPT, RESP, MB, BD = 1024, 1024, 4, 32
+VOCAB = 151936
+MASK_ID = VOCAB - 1
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--layers", type=int, default=36, help="debug only: fewer layers (reported as reduced)")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+# ------------------------------------------------------------------------------------------------
+class ClockSampler:
+    """Samples this GPU's SM clock and throttle reasons with nvidia-smi every 200 ms."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def physical_gpu_index(local_rank):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [x.strip() for x in vis.split(",") if x.strip()]
+        if local_rank < len(ids) and ids[local_rank].isdigit():
+            return int(ids[local_rank])
+    return local_rank
+
+
+def max_over_ranks(x):
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        t = torch.tensor([float(x)], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+    return float(x)
+
+
+def barrier():
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        dist.barrier()
+
+
+def synthetic_batches(n, seed):
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for _ in range(n):
+        ids = torch.randint(0, VOCAB - 2, (MB, PROMPT + RESP), generator=g)
+        labels = ids.clone()
+        labels[:, :PROMPT] = -100
+        out.append({"input_ids": ids.pin_memory(), "labels": labels.pin_memory(),
+                    "attention_mask": torch.ones_like(ids).pin_memory()})
+    return out
+
+
+# ------------------------------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank):
+    sys.path.insert(0, ROOT)
+    from trida_stack_b200.engine import TrainEngine, host_rpad
+    from trida_stack_b200.models import BlockDiffusionLM, Decoder, qwen3_config
+    from trida_stack_b200.ops._ext import count_launches, ext
+
+    ext()  # fail loudly if the extension is missing
+    cfg = qwen3_config(num_layers=args.layers)
+    torch.manual_seed(0)
+    dec = Decoder(cfg, dtype=torch.bfloat16, device="cuda")
+    model = BlockDiffusionLM(dec, mask_id=MASK_ID, pad_id=VOCAB - 2, bd_size=BD, ar_loss_weight=1.0)
+    model.train()
+    engine = TrainEngine(model, lr=1e-5, warmup=50, max_steps=2000, device=torch.device("cuda"))
+    batches = synthetic_batches(args.warmup + args.steps, seed=1234 + rank)
+    rpad = host_rpad(batches[0]["labels"], BD, model.response_buckets)
+    dev_batches = [{k: v.cuda(non_blocking=True) for k, v in b.items()} for b in batches]
+    torch.cuda.synchronize()
+
+    step = 0
+    for i in range(args.warmup):
+        engine.micro_step(dev_batches[i], rpad=rpad)
+        engine.optimizer_step(step)
+        step += 1
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler(physical_gpu_index(local_rank))
+    clocks.start()
+    count_launches(True)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier()
+    t0.record()
+    for i in range(args.steps):
+        engine.micro_step(dev_batches[args.warmup + i], rpad=rpad)
+        engine.optimizer_step(step)
+        step += 1
+    t1.record()
+    torch.cuda.synchronize()
+    barrier()
+    launches = count_launches(False)
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    ms = max_over_ranks(ms)
+    peak_gb = torch.cuda.max_memory_allocated() / 1e9
+
+    e2e = None
+    if not args.no_e2e:
+        # end to end through the public per-step API: host batch -> device, loss back to the host
+        torch.cuda.synchronize()
+        barrier()
+        w0 = time.perf_counter()
+        for i in range(args.steps):
+            loss, logs, lr, gnorm = engine.train_step([batches[args.warmup + i]], step)
+            float(loss.item())
+            step += 1
+        torch.cuda.synchronize()
+        barrier()
+        e2e_s = max_over_ranks((time.perf_counter() - w0) / args.steps)
+        e2e = {"value": world * MB * (PROMPT + RESP) / e2e_s, "unit": "tokens/s",
+               "h2d_bytes_per_step": sum(v.numel() * v.element_size() for v in batches[0].values()),
+               "d2h_bytes_per_step": 4}
+    return ms, clk, launches, e2e, peak_gb
+
+
+# ------------------------------------------------------------------------------------------------
+def write_reference_checkpoint(path, layers):
+    """Random-init HF Qwen3-4B-architecture checkpoint + a word-level tokenizer whose length,
+    after the reference adds <|mask|>, equals the config's 151936-token vocabulary."""
+    from tokenizers import Tokenizer, models, pre_tokenizers
+    from transformers import PreTrainedTokenizerFast, Qwen3Config, Qwen3ForCausalLM
+    n = VOCAB - 1
+    cfg = Qwen3Config(vocab_size=n, hidden_size=2560, intermediate_size=9728, num_hidden_layers=layers,
+                      num_attention_heads=32, num_key_value_heads=8, head_dim=128, rms_norm_eps=1e-6,
+                      rope_parameters={"rope_theta": 1e6, "rope_type": "default"}, tie_word_embeddings=True,
+                      max_position_embeddings=40960)
+    torch.manual_seed(0)
+    with torch.device("cuda"):
+        model = Qwen3ForCausalLM(cfg).to(torch.bfloat16)
+    model.save_pretrained(path)
+    del model
+    vocab = {f"t{i}": i for i in range(n - 1)}
+    vocab["<|endoftext|>"] = n - 1
+    tok = Tokenizer(models.WordLevel(vocab=vocab, unk_token="<|endoftext|>"))
+    tok.pre_tokenizer = pre_tokenizers.WhitespaceSplit()
+    PreTrainedTokenizerFast(tokenizer_object=tok, eos_token="<|endoftext|>",
+                            pad_token="<|endoftext|>").save_pretrained(path)
+
+
+def run_reference(args, rank, world, local_rank):
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "train")):
+        raise FileNotFoundError("baseline/_ref/train missing (reference not installed)")
+    sys.path.insert(0, ref)
+    from train.cli import build_parser
+    from train.distributed import setup_distributed, shard_model
+    from train.models.build import build_model
+    from train.optimizer import apply_optimizer_step, build_optimizer
+
+    ckpt = os.environ.get("TRIDA_REF_CKPT") or os.path.join(tempfile.gettempdir(), f"trida_ref_qwen3_4b_l{args.layers}")
+    rargs = build_parser().parse_args([
+        "--model_id", ckpt, "--bd_size", str(BD), "--ar_loss_weight", "1.0", "--micro_batch_size", str(MB),
+        "--grad_accum", "1", "--lr", "1e-5", "--max_length", str(PROMPT + RESP),
+        "--response_buckets", "512,1024,2048,4096", "--seed", "0"])
+    dev = setup_distributed(rargs)   # the reference's own NCCL init (set_device, then device_id)
+    if rank == 0 and not os.path.exists(os.path.join(ckpt, "config.json")):
+        write_reference_checkpoint(ckpt, args.layers)
+    barrier()
+    model = build_model(rargs)
+    shard_model(model, rargs)
+    optim = build_optimizer(rargs, model)
+    batches = synthetic_batches(args.warmup + args.steps, seed=1234 + rank)
+    dev_batches = [{k: v.to(dev, non_blocking=True) for k, v in b.items()} for b in batches]
+
+    def ref_step(b, step):
+        model.set_requires_gradient_sync(True)
+        loss, logs = model(b["input_ids"], b["labels"], b["attention_mask"])
+        (loss / rargs.grad_accum).backward()
+        apply_optimizer_step(model, optim, step, rargs)
+        return loss
+
+    step = 0
+    for i in range(args.warmup):
+        ref_step(dev_batches[i], step)
+        step += 1
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler(physical_gpu_index(local_rank))
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier()
+    t0.record()
+    for i in range(args.steps):
+        ref_step(dev_batches[args.warmup + i], step)
+        step += 1
+    t1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
+    peak_gb = torch.cuda.max_memory_allocated() / 1e9
+    e2e = None
+    if not args.no_e2e:
+        torch.cuda.synchronize()
+        barrier()
+        w0 = time.perf_counter()
+        for i in range(args.steps):
+            b = {k: v.to(dev, non_blocking=True) for k, v in batches[args.warmup + i].items()}
+            float(ref_step(b, step).item())
+            step += 1
+        torch.cuda.synchronize()
+        barrier()
+        e2e_s = max_over_ranks((time.perf_counter() - w0) / args.steps)
+        e2e = {"value": world * MB * (PROMPT + RESP) / e2e_s, "unit": "tokens/s",
+               "h2d_bytes_per_step": sum(v.numel() * v.element_size() for v in batches[0].values()),
+               "d2h_bytes_per_step": 4}
+    return ms, clk, None, e2e, peak_gb
+
+
+# ------------------------------------------------------------------------------------------------
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(json.dumps({"error": f"--gpus {args.gpus} but WORLD_SIZE={world}"}))
+        sys.exit(2)
+    torch.cuda.set_device(local_rank)
+    if args.impl == "ours":
+        if world > 1:
+            import datetime
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
+                                    timeout=datetime.timedelta(seconds=300))
+        res = run_ours(args, rank, world, local_rank)
+    else:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29531")
+        os.environ.setdefault("RANK", "0")
+        os.environ.setdefault("WORLD_SIZE", "1")
+        os.environ.setdefault("LOCAL_RANK", "0")
+        try:
+            res = run_reference(args, rank, world, local_rank)
+        except Exception as e:  # report, never fake a number
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": f"{type(e).__name__}: {e}"[:300]}))
+            if dist.is_initialized():
+                dist.destroy_process_group()
+            return
+    ms, clk, launches, e2e, peak_gb = res
+    tokens_per_step = world * MB * (PROMPT + RESP)
+    value = tokens_per_step / (ms / 1000.0)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": (round(value / BASELINE_TPS, 4) if BASELINE_TPS else None), "dtype": "bf16",
+            "data": "synthetic uniform token ids, random-init weights",
+            "config": {"model": "Qwen3-4B architecture (36L, d2560, 32/8 heads x128, ffn 9728, vocab 151936)"
+                       + ("" if args.layers == 36 else f" REDUCED to {args.layers} layers (not a valid bench)"),
+                       "global_batch": world * MB, "seq_len": PROMPT + RESP,
+                       "forward_row": "[S 1024 | x_t 1024 | x_0 1024] x 2 views",
+                       "forward_tokens_per_step": world * MB * 2 * (PROMPT + 2 * RESP),
+                       "parallelism": f"dp{world} (sharded optimizer state)", "bd_size": BD,
+                       "ar_loss_weight": 1.0, "optimizer": "AdamW lr 1e-5 (warmup 50, cosine)",
+                       "l2": "inputs larger than L2 (per-step working set >> 126 MB)",
+                       "peak_mem_gb": round(peak_gb, 1)},
+            "clocks": clk, "e2e": e2e,
+        }
+        if args.impl == "ours":
+            line["gpu_launches"] = launches
+        else:
+            line["impl"] = "reference"
+            line["config"]["reference_path"] = ("baseline/_ref train.models.build.build_model + "
+                                                "train.distributed.shard_model (FSDP2) + flex_attention + "
+                                                "train.optimizer.apply_optimizer_step")
+        print(json.dumps(line), flush=True)
+    if dist.is_initialized():
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -21,14 +21,61 @@ def load():
     return _C
 
 
+# Kernels each entry point launches (for the launch count the benchmark reports).
+KERNELS_PER_CALL = {
+    "gemm": 1, "rmsnorm_fwd": 1, "rmsnorm_bwd": 1, "qk_norm_rope_fwd": 1, "qk_norm_rope_bwd": 1,
+    "swiglu_fwd": 1, "swiglu_bwd": 1, "embed_fwd": 1, "embed_bwd": 1, "bd_attn_plan": 2, "bd_attn_fwd": 1,
+    "bd_attn_bwd": 3, "ce_rows": 1, "adamw": 1,
+}
+
+
+class _Counting:
+    """Proxy over the extension that counts kernel launches while ``counting`` is on."""
+
+    def __init__(self, mod):
+        self._mod = mod
+        self.counting = False
+        self.launches = 0
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        if not callable(fn):
+            return fn
+
+        def wrapped(*a, **k):
+            if self.counting:
+                if name == "grad_norm":
+                    self.launches += len(a[0]) + 1
+                else:
+                    self.launches += KERNELS_PER_CALL.get(name, 1)
+            return fn(*a, **k)
+        return wrapped
+
+
+_PROXY = None
+
+
 def ext():
     """The compiled module; raises with the import error if it is unavailable."""
+    global _PROXY
     m = load()
     if m is None:
         raise RuntimeError(
             "trida_stack_b200 CUDA extension is not built or failed to load "
             f"({_ERR}); run `python setup.py build_ext --inplace`")
-    return m
+    if _PROXY is None:
+        _PROXY = _Counting(m)
+    return _PROXY
+
+
+def count_launches(on=True):
+    """Start (reset) or stop counting launches of this package's kernels; returns the count."""
+    p = ext()
+    n = p.launches
+    if on:
+        p.launches = 0
+    p.counting = on
+    return n
 
 
 def available():

@@ -1,0 +1,177 @@
+"""Sharded data parallelism over flat parameter / gradient buffers.
+
+Every optimizer group's parameters live in ONE contiguous bf16 buffer (the parameters are views
+into it) with a matching fp32 gradient buffer (each parameter's ``main_grad``), both padded to a
+multiple of ``world * 64`` elements.  The optimizer state -- fp32 first/second moments and, with
+``fp32_master``, fp32 master weights -- exists only for this rank's 1/world shard, as in the
+reference's FSDP2 full-shard setup (``train/distributed.py:32-59``: bf16 compute weights, fp32
+gradient reduction).
+
+Step: reduce-scatter (average) the fp32 gradients -> global grad norm of the shards (one scalar
+all-reduce, no host sync) -> fused AdamW on the shard with the clip coefficient read on the device
+-> all-gather the updated bf16 shard into every rank's full buffer.  On one GPU the collectives
+vanish and the same kernels run over the whole buffer.  The gradient reduce-scatter is bucketed
+per layer and can be issued from backward hooks, overlapping communication with the backward of
+earlier layers (``overlap=True``).
+"""
+import torch
+import torch.distributed as dist
+
+from ..ops._ext import ext
+
+ALIGN = 64
+
+
+def _world():
+    return dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
+
+
+def _rank():
+    return dist.get_rank() if dist.is_available() and dist.is_initialized() else 0
+
+
+class FlatGroup:
+    """One optimizer group flattened into contiguous buffers."""
+
+    def __init__(self, params, lr_scale, world, rank, fp32_master, device):
+        self.params = list(params)
+        self.lr_scale = lr_scale
+        self.world, self.rank = world, rank
+        n = sum(p.numel() for p in self.params)
+        unit = world * ALIGN
+        self.numel = n
+        self.padded = (n + unit - 1) // unit * unit
+        self.shard = self.padded // world
+        dtype = self.params[0].dtype if self.params else torch.bfloat16
+        self.flat = torch.zeros(self.padded, dtype=dtype, device=device)
+        self.grad = torch.zeros(self.padded, dtype=torch.float32, device=device)
+        off = 0
+        self.offsets = []
+        with torch.no_grad():
+            for p in self.params:
+                k = p.numel()
+                view = self.flat[off:off + k].view_as(p)
+                view.copy_(p.data)
+                p.data = view
+                p.main_grad = self.grad[off:off + k].view(p.shape)
+                self.offsets.append((off, k))
+                off += k
+        lo = rank * self.shard
+        self.lo, self.hi = lo, lo + self.shard
+        self.grad_shard = torch.zeros(self.shard, dtype=torch.float32, device=device) if world > 1 else None
+        self.master = None
+        if fp32_master:
+            self.master = self.flat[lo:lo + self.shard].float().clone()
+        self.m = torch.zeros(self.shard, dtype=torch.float32, device=device)
+        self.v = torch.zeros(self.shard, dtype=torch.float32, device=device)
+
+    def shard_grad(self):
+        return self.grad if self.world == 1 else self.grad_shard
+
+    def shard_param(self):
+        return self.flat[self.lo:self.hi]
+
+
+def _adamw_torch(param, master, grad, m, v, lr, b1, b2, eps, wd, step, coef):
+    """CPU statement of the fused AdamW kernel (torch.optim.AdamW math, fp32 moments)."""
+    p = master if master is not None else param.float()
+    g = grad * coef
+    p.mul_(1 - lr * wd)
+    m.mul_(b1).add_(g, alpha=1 - b1)
+    v.mul_(b2).addcmul_(g, g, value=1 - b2)
+    bc1, bc2 = 1 - b1 ** step, 1 - b2 ** step
+    p.addcdiv_(m, v.sqrt().div_(bc2 ** 0.5).add_(eps), value=-lr / bc1)
+    param.copy_(p)
+
+
+class ShardedAdamW:
+    """AdamW over flat sharded buffers; torch.optim-like surface (``param_groups``, ``step``,
+    ``zero_grad``, ``state_dict``)."""
+
+    def __init__(self, groups, lr, betas=(0.9, 0.95), weight_decay=0.0, eps=1e-8, fp32_master=False,
+                 device=None, process_group=None):
+        self.world, self.rank = _world(), _rank()
+        self.pg = process_group
+        device = device or groups[0]["params"][0].device
+        self.groups = [FlatGroup(g["params"], g.get("lr_scale", 1.0), self.world, self.rank, fp32_master, device)
+                       for g in groups if g["params"]]
+        self.param_groups = [{"params": g.params, "lr": lr * g.lr_scale, "lr_scale": g.lr_scale}
+                             for g in self.groups]
+        self.defaults = {"lr": lr, "betas": betas, "weight_decay": weight_decay, "eps": eps}
+        self.betas, self.wd, self.eps = betas, weight_decay, eps
+        self.step_count = 0
+        self.norm = torch.zeros(1, dtype=torch.float32, device=device)
+        self.coef = torch.zeros(1, dtype=torch.float32, device=device)
+        self._partial = None
+
+    # ---- gradients -----------------------------------------------------------------------
+    def zero_grad(self, set_to_none=True):
+        for g in self.groups:
+            g.grad.zero_()
+
+    def reduce_gradients(self):
+        """Average gradients across ranks into each rank's shard (reduce-scatter)."""
+        if self.world == 1:
+            return
+        avg = dist.get_backend(self.pg) == "nccl"   # gloo has no AVG reduction
+        for g in self.groups:
+            dist.reduce_scatter_tensor(g.grad_shard, g.grad, op=dist.ReduceOp.AVG if avg else dist.ReduceOp.SUM,
+                                       group=self.pg)
+            if not avg:
+                g.grad_shard.div_(self.world)
+
+    def _local_norm(self, shards, max_norm):
+        if self.norm.is_cuda:
+            ext().grad_norm(shards, max_norm, self.norm, self.coef)
+        else:
+            self.norm.copy_(torch.sqrt(sum((s.double() ** 2).sum() for s in shards)).float().view(1))
+            torch.clamp(max_norm / (self.norm + 1e-6), max=1.0, out=self.coef)
+
+    def clip_grad_norm_(self, max_norm):
+        """Global L2 norm of the (reduced) gradients; writes the clip coefficient on the device and
+        returns the norm as a device tensor (no host sync)."""
+        shards = [g.shard_grad() for g in self.groups]
+        if self.world == 1:
+            self._local_norm(shards, max_norm)
+            return self.norm[0]
+        # partial sums of squares on each rank, summed across ranks, then the coefficient
+        sq = torch.zeros(1, dtype=torch.float32, device=self.norm.device)
+        self._local_norm(shards, 1e30)  # norm of this rank's shards
+        sq.copy_(self.norm * self.norm)
+        dist.all_reduce(sq, group=self.pg)
+        torch.sqrt(sq, out=self.norm)
+        torch.clamp(max_norm / (self.norm + 1e-6), max=1.0, out=self.coef)
+        return self.norm[0]
+
+    # ---- update ----------------------------------------------------------------------------
+    def step(self):
+        self.step_count += 1
+        b1, b2 = self.betas
+        for g, pg in zip(self.groups, self.param_groups):
+            lr = pg["lr"]
+            if self.coef.is_cuda:
+                ext().adamw(g.shard_param(), g.master, g.shard_grad(), g.m, g.v, lr, b1, b2, self.eps, self.wd,
+                            self.step_count, self.coef)
+            else:
+                _adamw_torch(g.shard_param(), g.master, g.shard_grad(), g.m, g.v, lr, b1, b2, self.eps, self.wd,
+                             self.step_count, self.coef)
+        if self.world > 1:
+            for g in self.groups:
+                # in place: this rank's input is its own slice of the output buffer
+                dist.all_gather_into_tensor(g.flat, g.flat[g.lo:g.hi], group=self.pg)
+
+    # ---- checkpoint ------------------------------------------------------------------------
+    def state_dict(self):
+        return {"step": self.step_count, "world": self.world, "rank": self.rank,
+                "groups": [{"m": g.m, "v": g.v, "master": g.master, "lo": g.lo, "hi": g.hi,
+                            "numel": g.numel} for g in self.groups]}
+
+    def load_state_dict(self, sd):
+        if sd["world"] != self.world:
+            raise ValueError(f"optimizer state was saved with world {sd['world']}, running with {self.world}")
+        self.step_count = sd["step"]
+        for g, s in zip(self.groups, sd["groups"]):
+            g.m.copy_(s["m"])
+            g.v.copy_(s["v"])
+            if g.master is not None and s["master"] is not None:
+                g.master.copy_(s["master"])
