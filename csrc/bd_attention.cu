@@ -730,6 +730,22 @@ int bd_attn_fwd(const AttnTensors& t, const int4* meta, const int16_t* fwd_list,
   return 0;
 }
 
+void bd_attn_bwd_prep(const AttnTensors& t, const bf16* dout, int64_t do_tok, int64_t do_b, float* dsum, float* dq_acc,
+                      cudaStream_t s) {
+  const int64_t rows = (int64_t)t.B * t.T * t.Hq;
+  attn::bwd_dsum_kernel<<<ceil_div(rows, 8), 256, 0, s>>>(t.o, t.o_tok, t.o_b, dout, do_tok, do_b, dsum, t.B, t.T,
+                                                           t.Hq, t.D);
+  cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * t.D, s);
+}
+
+void bd_attn_dq_convert(const float* dq_acc, bf16* dq, int64_t dq_tok, int64_t dq_b, int B, int T, int Hq, int D,
+                        int sm_count, cudaStream_t s) {
+  const int64_t n8 = (int64_t)B * T * Hq * D / 8;
+  int blocks = ceil_div(n8, 256);
+  blocks = blocks > sm_count * 16 ? sm_count * 16 : blocks;
+  attn::dq_convert_kernel<<<blocks, 256, 0, s>>>(dq_acc, dq, dq_tok, dq_b, B, T, Hq, D);
+}
+
 int bd_attn_bwd(const AttnTensors& t, const bf16* dout, int64_t do_tok, int64_t do_b, float* dsum, float* dq_acc,
                 bf16* dq, int64_t dq_tok, int64_t dq_b, bf16* dk, int64_t dk_tok, int64_t dk_b, bf16* dv,
                 int64_t dv_tok, int64_t dv_b, const int4* meta, const int16_t* bwd_list, const int* bwd_cnt,

@@ -1,0 +1,868 @@
+// Block-diffusion attention forward on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// CTA = one 128-row query tile of one head.  Warp roles (192 threads):
+//   warps 0-3  softmax: thread r owns query row r == TMEM lane r.  Reads its S row from TMEM with
+//              tcgen05.ld, applies the block-diffusion rule on PARTIAL tiles, keeps the running
+//              max / sum, rescales its O row in TMEM only when the max grows by more than 2^8
+//              (otherwise exp2(s - m) <= 256 is exact enough in fp32 / bf16), and writes its P row
+//              (bf16) into shared memory in the UMMA K-major SWIZZLE_128B layout.
+//   warp 4     MMA issuer (one thread): S_i = Q K_i^T into one of two TMEM S buffers, then
+//              O += P_{i-1} V_{i-1}; completion is signalled with tcgen05.commit on mbarriers.
+//   warp 5     TMA producer (one thread): Q once, K/V tiles into a 2-stage ring (plain per-CTA
+//              tensor loads, never cluster multicast).
+// TMEM columns: S0 [0,128), S1 [128,256), O [256, 256+D).  The list of non-empty 128-key tiles
+// (and whether each is FULL or PARTIAL) comes from the same exact classification pass as the
+// other attention kernels.  Every mbarrier wait is bounded; a timeout records an error code in
+// a device word that the host checks, and the CTA still releases its TMEM.
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "ops.h"
+#include "sm100_common.cuh"
+
+#include <climits>
+
+namespace trida {
+namespace attn100 {
+
+using namespace sm100;
+
+constexpr int SEG_PAD = 0, SEG_SHARED = 1, SEG_XT = 2, SEG_X0 = 3;
+constexpr int FLAG_X0_TOKEN_CAUSAL = 1, FLAG_WITHIN_BLOCK_CAUSAL = 2;
+constexpr int CLS_FULL = 1;
+constexpr int BM = 128, BN = 128;
+constexpr int NTHREADS = 192;
+// Lazy O rescaling: the running max is only moved (and O rescaled in TMEM) when a tile's max
+// exceeds it by more than 2^16; until then P = exp2(s - m) <= 65536, far inside bf16/fp32 range,
+// and the fp32 accumulators stay exact to their usual rounding.
+constexpr float RESCALE_THRESHOLD = 16.0f;   // log2 units
+
+// Branch-free statement of the rule (pure predicate logic: no divergent early returns inside warps).
+__device__ __forceinline__ bool allowed(const int4 q, const int4 k, bool same_index, int flags) {
+  const int sq = q.w & 0xff, sk = k.w & 0xff;
+  const int vq = q.w >> 8, vk = k.w >> 8;
+  const bool le = k.x <= q.x;
+  const bool to_shared = (sk == SEG_SHARED) & le;
+  const bool xt_diag = (sq == SEG_XT) & (sk == SEG_XT) & (q.y == k.y) & (vq == vk) &
+                       (((flags & FLAG_WITHIN_BLOCK_CAUSAL) == 0) | le);
+  const bool xt_off = (sq == SEG_XT) & (sk == SEG_X0) & (k.y < q.y);
+  const bool x0c = (sq == SEG_X0) & (sk == SEG_X0) & (((flags & FLAG_X0_TOKEN_CAUSAL) != 0) ? le : (k.y <= q.y));
+  return same_index | ((sk != SEG_PAD) & (q.z == k.z) & (to_shared | xt_diag | xt_off | x0c));
+}
+
+// Hardware base-2 exponential (MUFU.EX2 via the PTX ex2.approx instruction); exp2(-inf) = 0.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
+
+struct Params {
+  bf16* o;
+  int64_t o_tok, o_b;
+  float* lse;          // [B, Hq, T]
+  const int4* meta;    // [B, T]
+  const int16_t* list; // [B, nq128, nk128] entries kt | cls << 14
+  const int* cnt;      // [B, nq128]
+  const uint4* tmask;  // [B, nq128, nk128, 128] row bit-masks of PARTIAL tiles (bit c = key c allowed)
+  int* err;
+  long long* dbg;      // optional timeline: [cta][64 events] clock64 stamps (CTAs 0..7 only)
+  int T, Hq, group, nk, flags;
+  float scale_log2;
+};
+
+#define DBG_STAMP(slot)                                                                           \
+  do {                                                                                            \
+    if (p.dbg && cta_id < 8 && (slot) < 64) p.dbg[cta_id * 64 + (slot)] = clock64();              \
+  } while (0)
+
+template <int D>
+struct Smem {
+  static constexpr int SUB = BM * 128;                 // one [128 rows][64 bf16] swizzled sub-tile
+  static constexpr int Q = 0;
+  static constexpr int K0 = Q + (D / 64) * SUB;
+  static constexpr int V0 = K0 + 2 * (D / 64) * SUB;
+  static constexpr int P = V0 + 2 * (D / 64) * SUB;   // two P buffers of 2 sub-tiles each
+  static constexpr int MK = P + 4 * SUB;                // int4[64] key metadata staging (PARTIAL tiles)
+  static constexpr int BAR = MK + 64 * 16;
+  static constexpr int TOTAL = BAR + 256;
+};
+
+__device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(n) : "memory"); }
+
+template <int D>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+               const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using S = Smem<D>;
+  extern __shared__ unsigned char smem_raw[];
+  // Align by pointer arithmetic on the __shared__ array (not an integer round-trip) so the compiler
+  // keeps the shared address space and emits LDS/STS instead of generic loads/stores.
+  unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;    // [2]
+  uint64_t* kv_empty = bars + 3;   // [2]
+  uint64_t* s_full = bars + 5;     // [2]
+  uint64_t* p_full = bars + 7;
+  uint64_t* pv_done = bars + 8;    // [2]: PV_j completes pv_done[j & 1] (completion number j >> 1)
+  uint64_t* drain = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / p.group;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nq = gridDim.x;
+  const int lidx = b * nq + qt;
+  const int n = p.cnt[lidx];
+  const int16_t* list = p.list + (int64_t)lidx * p.nk;
+  const int cta_id = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+
+  if (threadIdx.x == 0) {
+    DBG_STAMP(0);
+    mbar_init(q_full, 1);
+    mbar_init(&kv_full[0], 1);
+    mbar_init(&kv_full[1], 1);
+    mbar_init(&kv_empty[0], 1);
+    mbar_init(&kv_empty[1], 1);
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
+    mbar_init(p_full, BM);
+    mbar_init(&pv_done[0], 1);
+    mbar_init(&pv_done[1], 1);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS[2] = {tmem, tmem + 128};
+  const uint32_t tO = tmem + 256;
+
+  if (warp == 5) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      mbar_expect_tx(q_full, (D / 64) * S::SUB);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) tma_load_4d(smem + S::Q + c * S::SUB, &tmQ, q_full, c * 64, h, qt * BM, b);
+      for (int i = 0; i < n; ++i) {
+        const int s = i & 1;
+        if (i >= 2 && !mbar_wait(&kv_empty[s], ((i - 2) >> 1) & 1, p.err, 1)) break;
+        const int kt = list[i] & 0x3fff;
+        mbar_expect_tx(&kv_full[s], 2 * (D / 64) * S::SUB);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_4d(smem + S::K0 + (s * (D / 64) + c) * S::SUB, &tmK, &kv_full[s], c * 64, hk, kt * BN, b);
+          tma_load_4d(smem + S::V0 + (s * (D / 64) + c) * S::SUB, &tmV, &kv_full[s], c * 64, hk, kt * BN, b);
+        }
+      }
+      // drain: the last (up to two) loads must have landed before the CTA can retire
+      for (int i = (n > 2 ? n - 2 : 0); i < n; ++i) mbar_wait(&kv_full[i & 1], (i >> 1) & 1, p.err, 2);
+    }
+  } else if (warp == 4) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16_f32(BM, BN, 0, 0);
+      constexpr uint32_t idPV = idesc_bf16_f32(BM, D, 0, 1);
+      const uint32_t sQ = smem_addr(smem + S::Q), sK = smem_addr(smem + S::K0), sV = smem_addr(smem + S::V0),
+                     sP = smem_addr(smem + S::P);
+      bool ok = mbar_wait(q_full, 0, p.err, 3);
+      DBG_STAMP(1);
+      auto issue_pv = [&](int j) {
+        const uint32_t vbase = sV + (j & 1) * (D / 64) * S::SUB;
+        const uint32_t pbase = sP + (j & 1) * 2 * S::SUB;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t a = desc_sw128(pbase + (kk >> 2) * S::SUB + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = desc_sw128(vbase + kk * 2048, S::SUB, 1024);
+          umma_f16(tO, a, bd, idPV, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&pv_done[j & 1]);
+        umma_commit(&kv_empty[j & 1]);
+      };
+      for (int i = 0; ok && i < n; ++i) {
+        const int s = i & 1;
+        if (!(ok = mbar_wait(&kv_full[s], (i >> 1) & 1, p.err, 4))) break;
+        if (i < 6) DBG_STAMP(2 + 4 * i);
+        tc_fence_after();
+        const uint32_t kbase = sK + s * (D / 64) * S::SUB;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint64_t a = desc_sw128(sQ + (k >> 2) * S::SUB + (k & 3) * 32, 16, 1024);
+          const uint64_t bd = desc_sw128(kbase + (k >> 2) * S::SUB + (k & 3) * 32, 16, 1024);
+          umma_f16(tS[s], a, bd, idS, k > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[s]);
+        if (i < 6) DBG_STAMP(3 + 4 * i);
+        if (i > 0) {
+          if (!(ok = mbar_wait(p_full, (i - 1) & 1, p.err, 5))) break;
+          if (i < 6) DBG_STAMP(4 + 4 * i);
+          tc_fence_after();
+          issue_pv(i - 1);
+        }
+      }
+      if (ok && n > 0 && mbar_wait(p_full, (n - 1) & 1, p.err, 6)) {
+        tc_fence_after();
+        issue_pv(n - 1);
+      }
+      // every MMA issued by this thread has completed once `drain` flips
+      umma_commit(drain);
+      mbar_wait(drain, 0, p.err, 7);
+    }
+  } else {
+    // ---------------- softmax / correction / epilogue (warps 0-3) ----------------
+    const int r = threadIdx.x;              // query row within the tile == TMEM lane
+    const int row = qt * BM + r;
+    const int4 mq = row < p.T ? p.meta[(int64_t)b * p.T + row] : make_int4(INT_MAX, INT_MAX, -3, SEG_PAD);
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f;
+    unsigned char* sP = smem + S::P;
+    bool ok = true;
+    for (int i = 0; i < n; ++i) {
+      const int s = i & 1;
+      const int entry = list[i];
+      const int kt = entry & 0x3fff;
+      const bool partial = (entry >> 14) != CLS_FULL;
+      uint32_t bits[BN / 32];
+      if (partial) {
+        const uint4 w = p.tmask[(((int64_t)b * nq + qt) * p.nk + kt) * BM + r];
+        bits[0] = w.x; bits[1] = w.y; bits[2] = w.z; bits[3] = w.w;
+      }
+      if (!(ok = mbar_wait(&s_full[s], (i >> 1) & 1, p.err, 8))) break;
+      if (r == 0 && i < 6) DBG_STAMP(30 + 5 * i);
+      tc_fence_after();
+      float sv[BN];
+      {
+        uint32_t t[BN / 32][32];
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS[s] + lane_off + c * 32, t[c]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sv[c * 32 + j] = __uint_as_float(t[c][j]);
+      }
+      if (partial) {
+#pragma unroll
+        for (int c = 0; c < BN; ++c)
+          if (!((bits[c >> 5] >> (c & 31)) & 1u)) sv[c] = -INFINITY;
+      }
+      if (r == 0 && i < 6) DBG_STAMP(31 + 5 * i);
+      float mxp[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mxp[u] = sv[u];
+#pragma unroll
+      for (int c = 8; c < BN; ++c) mxp[c & 7] = fmaxf(mxp[c & 7], sv[c]);
+      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+      const float mx_s = mx * p.scale_log2;
+      const bool grow = mx_s > m_run + RESCALE_THRESHOLD || (m_run == -INFINITY && mx_s > -INFINITY);
+      // The P buffer (i & 1) was last read by PV_{i-2}; O may be rescaled only after PV_{i-1}
+      // (MMAs complete in issue order, so PV_{i-1} done implies PV_{i-2} done).
+      if (grow && i > 0) {
+        if (!(ok = mbar_wait(&pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1, p.err, 9))) break;
+        tc_fence_after();
+      } else if (i >= 2) {
+        if (!(ok = mbar_wait(&pv_done[i & 1], ((i - 2) >> 1) & 1, p.err, 11))) break;
+        tc_fence_after();
+      }
+      if (grow) {
+        if (i > 0 && m_run != -INFINITY) {
+          const float alpha = exp2f(m_run - mx_s);
+          l_run *= alpha;
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t t[32];
+            tmem_ld32(tO + lane_off + c * 32, t);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) t[j] = __float_as_uint(__uint_as_float(t[j]) * alpha);
+            tmem_st32(tO + lane_off + c * 32, t);
+          }
+          tmem_wait_st();
+        }
+        m_run = mx_s;
+      }
+      if (r == 0 && i < 6) DBG_STAMP(32 + 5 * i);
+      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+      float rsp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      unsigned char* pbuf = sP + (i & 1) * 2 * S::SUB;
+#pragma unroll
+      for (int c8 = 0; c8 < BN / 8; ++c8) {
+        float pv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          pv[j] = fast_exp2(sv[c8 * 8 + j] * p.scale_log2 - m_use);
+          rsp[j] += pv[j];
+        }
+        const int col = c8 * 8;
+        store8(reinterpret_cast<bf16*>(pbuf + (col >> 6) * S::SUB + sw128_offset(r, col & 63)), pv);
+      }
+      const float rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
+      l_run += rs;
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+      if (r == 0 && i < 6) DBG_STAMP(33 + 5 * i);
+    }
+    if (ok && n > 0) ok = mbar_wait(&pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1, p.err, 10);
+    if (ok && n > 0) {
+      tc_fence_after();
+      if (row < p.T) {
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        bf16* go = p.o + (int64_t)b * p.o_b + (int64_t)row * p.o_tok + (int64_t)h * D;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t t[32];
+          tmem_ld32(tO + lane_off + c * 32, t);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j8 = 0; j8 < 4; ++j8) {
+            float f[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(t[j8 * 8 + j]) * inv;
+            store8(go + c * 32 + j8 * 8, f);
+          }
+        }
+        p.lse[((int64_t)b * p.Hq + h) * p.T + row] =
+            (m_run == -INFINITY) ? -INFINITY : (m_run + log2f(l_run)) * 0.69314718055994530942f;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) DBG_STAMP(63);
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// ---- host: tensor maps -------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// [B, T, H, D] bf16 with element strides (tok, batch); box = 64 x 1 head x 128 tokens x 1.
+static bool make_map(CUtensorMap* m, const void* base, int B, int T, int H, int D, int64_t tok, int64_t bstride) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)tok * 2, (cuuint64_t)bstride * 2};
+  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int D>
+static int launch(const AttnTensors& t, const Params& p, int nq, cudaStream_t s) {
+  CUtensorMap mq, mk, mv;
+  if (!make_map(&mq, t.q, t.B, t.T, t.Hq, D, t.q_tok, t.q_b)) return -2;
+  if (!make_map(&mk, t.k, t.B, t.T, t.Hkv, D, t.k_tok, t.k_b)) return -3;
+  if (!make_map(&mv, t.v, t.B, t.T, t.Hkv, D, t.v_tok, t.v_b)) return -4;
+  const int smem = Smem<D>::TOTAL + 1024;
+  static bool init = false;
+  if (!init) {
+    cudaFuncSetAttribute(fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    init = true;
+  }
+  fwd_kernel<D><<<dim3(nq, t.Hq, t.B), NTHREADS, smem, s>>>(mq, mk, mv, p);
+  return 0;
+}
+
+
+// =================================================================================================
+// Backward.  CTA = one 128-key tile of one KV head; it walks every (query head of the GQA group,
+// non-empty 128-query tile) pair.  Per pair j (thread r of warps 0-3 owns key row r == TMEM lane r):
+//   MMA1  S^T  = K Q_j^T          -> TMEM [0,128)        (A = K  K-major, B = Q  K-major)
+//   MMA2  dP^T = V dO_j^T         -> TMEM [128,256)      (A = V  K-major, B = dO K-major)
+//   softmax warps, 32 queries at a time: P^T = exp2(S^T*scale*log2e - LSE2[q]) (masked on PARTIAL
+//         tiles), dS^T = P^T * (dP^T - Dsum[q]); both written as bf16 K-major rows to smem.
+//   MMA3  dV  += P^T dO_j         -> TMEM [256,256+D)    (A = P^T K-major, B = dO MN-major)
+//   MMA4  dK  += dS^T Q_j         -> TMEM [384,384+D)    (A = dS^T K-major, B = Q MN-major)
+//   MMA5  dQ_j = dS K             -> TMEM [0,128) again  (A = dS MN-major, B = K MN-major)
+//   the same warps read dQ_j rows (thread = query row) and add them (x scale) to an fp32 global
+//   accumulator with vector reductions; then TMEM [0,128) is free for the next S^T.
+// dK (x scale) and dV are written once at the end.  Warp 4 issues MMAs, warp 5 issues TMA.
+// =================================================================================================
+struct BwdParams {
+  bf16 *dk, *dv;
+  int64_t dk_tok, dk_b, dv_tok, dv_b;
+  float* dq_acc;            // [B, T, Hq, D] fp32, pre-zeroed
+  const float *lse, *dsum;  // [B, Hq, T]
+  const int4* meta;
+  const int16_t* list;      // [B, nk128, nq128] entries qt | cls << 14
+  const int* cnt;           // [B, nk128]
+  const uint4* tmask_t;     // [B, nk128, nq128, 128] column bit-masks of PARTIAL tiles (bit q = query q allowed)
+  int* err;
+  long long* dbg;
+  int T, Hq, group, nq, flags;
+  float scale, scale_log2;
+};
+
+template <int D>
+struct BwdSmem {
+  static constexpr int SUB = 128 * 128;
+  static constexpr int K = 0;
+  static constexpr int V = K + (D / 64) * SUB;
+  static constexpr int Q = V + (D / 64) * SUB;
+  static constexpr int DO = Q + (D / 64) * SUB;
+  static constexpr int PT = DO + (D / 64) * SUB;
+  static constexpr int DST = PT + 2 * SUB;
+  static constexpr int LSE = DST + 2 * SUB;     // float[128]
+  static constexpr int DS = LSE + 512;          // float[128]
+  static constexpr int MQ = DS + 512;           // int4[128]
+  static constexpr int DQS = (MQ + 2048 + 1023) / 1024 * 1024;  // float[128][32] SWIZZLE_128B dQ staging
+  static constexpr int BAR = DQS + 128 * 128;
+  static constexpr int TOTAL = BAR + 256;
+};
+
+// TMA tensor reduction: global tile += shared tile (fp32 add), tracked by a bulk group.  The start
+// coordinates are never negative (rows past T are clipped by the tensor map bounds).
+__device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2,
+                                                  int c3) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];\n" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_addr(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
+
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(n) : "memory");
+}
+
+template <int D>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+               const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+               const __grid_constant__ CUtensorMap tmDQ, const BwdParams p) {
+  using S = BwdSmem<D>;
+  extern __shared__ unsigned char smem_raw[];
+  // Align by pointer arithmetic on the __shared__ array (not an integer round-trip) so the compiler
+  // keeps the shared address space and emits LDS/STS instead of generic loads/stores.
+  unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* q_full = bars + 1;
+  uint64_t* q_empty = bars + 2;
+  uint64_t* sp_full = bars + 3;
+  uint64_t* p_full = bars + 4;
+  uint64_t* dq_full = bars + 5;
+  uint64_t* dq_free = bars + 6;
+  uint64_t* drain = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  float* sLSE = reinterpret_cast<float*>(smem + S::LSE);
+  float* sDs = reinterpret_cast<float*>(smem + S::DS);
+  int4* sMq = reinterpret_cast<int4*>(smem + S::MQ);
+
+  const int kt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nk = gridDim.x;
+  const int lidx = b * nk + kt;
+  const int nqt = p.cnt[lidx];
+  const int16_t* list = p.list + (int64_t)lidx * p.nq;
+  const int total = nqt * p.group;
+  // CTAs of neighbouring key tiles start their walk at different (head, query tile) pairs so
+  // their dQ reductions land on different rows at any moment.
+  const int rot = total > 0 ? (kt * 7 + hk * 3) % total : 0;
+  const int cta_id = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+
+  if (threadIdx.x == 0) {
+    DBG_STAMP(0);
+    mbar_init(kv_full, 1);
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    mbar_init(sp_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 128);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 256 + D;
+
+  if (warp == 5) {
+    if (lane == 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      prefetch_tmap(&tmDO);
+      mbar_expect_tx(kv_full, 2 * (D / 64) * S::SUB);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        tma_load_4d(smem + S::K + c * S::SUB, &tmK, kv_full, c * 64, hk, kt * 128, b);
+        tma_load_4d(smem + S::V + c * S::SUB, &tmV, kv_full, c * 64, hk, kt * 128, b);
+      }
+      for (int j = 0; j < total; ++j) {
+        if (j > 0 && !mbar_wait(q_empty, (j - 1) & 1, p.err, 21)) break;
+        const int jj = (j + rot) % total;
+        const int h = hk * p.group + jj / nqt;
+        const int qt = list[jj % nqt] & 0x3fff;
+        mbar_expect_tx(q_full, 2 * (D / 64) * S::SUB);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_4d(smem + S::Q + c * S::SUB, &tmQ, q_full, c * 64, h, qt * 128, b);
+          tma_load_4d(smem + S::DO + c * S::SUB, &tmDO, q_full, c * 64, h, qt * 128, b);
+        }
+      }
+      if (total > 0) mbar_wait(q_full, (total - 1) & 1, p.err, 22);
+    }
+  } else if (warp == 4) {
+    if (lane == 0) {
+      constexpr uint32_t idKK = idesc_bf16_f32(128, 128, 0, 0);   // S^T, dP^T
+      constexpr uint32_t idKM = idesc_bf16_f32(128, D, 0, 1);     // dV, dK (B MN-major)
+      constexpr uint32_t idMM = idesc_bf16_f32(128, D, 1, 1);     // dQ (A and B MN-major)
+      const uint32_t sK = smem_addr(smem + S::K), sV = smem_addr(smem + S::V), sQ = smem_addr(smem + S::Q),
+                     sDO = smem_addr(smem + S::DO), sPT = smem_addr(smem + S::PT), sDST = smem_addr(smem + S::DST);
+      bool ok = mbar_wait(kv_full, 0, p.err, 23);
+      for (int j = 0; ok && j < total; ++j) {
+        if (!(ok = mbar_wait(q_full, j & 1, p.err, 24))) break;
+        if (j < 6) DBG_STAMP(10 + 3 * j);
+        if (j > 0 && !(ok = mbar_wait(dq_free, (j - 1) & 1, p.err, 25))) break;
+        if (j < 6) DBG_STAMP(11 + 3 * j);
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (k >> 2) * S::SUB + (k & 3) * 32;
+          umma_f16(tS, desc_sw128(sK + off, 16, 1024), desc_sw128(sQ + off, 16, 1024), idKK, k > 0);
+          umma_f16(tDP, desc_sw128(sV + off, 16, 1024), desc_sw128(sDO + off, 16, 1024), idKK, k > 0);
+        }
+        umma_commit(sp_full);
+        if (!(ok = mbar_wait(p_full, j & 1, p.err, 26))) break;
+        if (j < 6) DBG_STAMP(12 + 3 * j);
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 128 / 16; ++kk) {
+          const uint32_t aoff = (kk >> 2) * S::SUB + (kk & 3) * 32;   // K-major 16-query step
+          const uint32_t boff = kk * 2048;                            // MN-major 16-row step
+          const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
+          umma_f16(tDV, desc_sw128(sPT + aoff, 16, 1024), desc_sw128(sDO + boff, S::SUB, 1024), idKM, acc);
+          umma_f16(tDK, desc_sw128(sDST + aoff, 16, 1024), desc_sw128(sQ + boff, S::SUB, 1024), idKM, acc);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 128 / 16; ++kk) {
+          // A = dS (M = queries, K = keys): the dS^T rows (key-major) read as MN-major, 16 keys per step
+          umma_f16(tS, desc_sw128(sDST + kk * 2048, S::SUB, 1024), desc_sw128(sK + kk * 2048, S::SUB, 1024), idMM,
+                   kk > 0);
+        }
+        umma_commit(dq_full);
+        umma_commit(q_empty);
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0, p.err, 27);
+    }
+  } else {
+    // ---------------- warps 0-3 ----------------
+    const int r = threadIdx.x;
+    const int krow = kt * 128 + r;
+    const int4 mk = krow < p.T ? p.meta[(int64_t)b * p.T + krow] : make_int4(INT_MAX, INT_MAX, -4, SEG_PAD);
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    unsigned char* sPT = smem + S::PT;
+    unsigned char* sDST = smem + S::DST;
+    bool ok = true;
+    for (int j = 0; j < total; ++j) {
+      const int jj = (j + rot) % total;
+      const int h = hk * p.group + jj / nqt;
+      const int entry = list[jj % nqt];
+      const int qt = entry & 0x3fff;
+      const bool partial = (entry >> 14) != CLS_FULL;
+      {  // stage this query tile's LSE (log2 domain), Dsum and metadata
+        const int q = qt * 128 + r;
+        const int64_t li = ((int64_t)b * p.Hq + h) * p.T + q;
+        sLSE[r] = q < p.T ? p.lse[li] * 1.44269504088896340736f : INFINITY;
+        sDs[r] = q < p.T ? p.dsum[li] : 0.f;
+        sMq[r] = q < p.T ? p.meta[(int64_t)b * p.T + q] : make_int4(INT_MAX, INT_MAX, -5, SEG_PAD);
+      }
+      named_bar_sync(1, 128);
+      uint4 cm = make_uint4(0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu);
+      if (partial) cm = p.tmask_t[(((int64_t)b * nk + kt) * p.nq + qt) * 128 + r];
+      if (r == 0 && j < 6) DBG_STAMP(40 + 4 * j);
+      if (!(ok = mbar_wait(sp_full, j & 1, p.err, 28))) break;
+      if (r == 0 && j < 6) DBG_STAMP(41 + 4 * j);
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32], dv[32];
+        tmem_ld32(tS + lane_off + c * 32, sv);
+        tmem_ld32(tDP + lane_off + c * 32, dv);
+        tmem_wait_ld();
+        if (r == 0 && j == 1) DBG_STAMP(30 + 3 * c);
+        float pp[32], dd[32];
+        float lse_c[32], ds_c[32];
+#pragma unroll
+        for (int t4 = 0; t4 < 8; ++t4) {
+          const float4 l4 = reinterpret_cast<const float4*>(sLSE + c * 32)[t4];
+          const float4 d4 = reinterpret_cast<const float4*>(sDs + c * 32)[t4];
+          lse_c[t4 * 4 + 0] = l4.x; lse_c[t4 * 4 + 1] = l4.y; lse_c[t4 * 4 + 2] = l4.z; lse_c[t4 * 4 + 3] = l4.w;
+          ds_c[t4 * 4 + 0] = d4.x; ds_c[t4 * 4 + 1] = d4.y; ds_c[t4 * 4 + 2] = d4.z; ds_c[t4 * 4 + 3] = d4.w;
+        }
+        uint32_t amask = 0xffffffffu;
+        if (partial) amask = c == 0 ? cm.x : (c == 1 ? cm.y : (c == 2 ? cm.z : cm.w));
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const float e = fast_exp2(__uint_as_float(sv[t]) * p.scale_log2 - lse_c[t]);
+          const float pv = ((amask >> t) & 1u) ? e : 0.f;
+          pp[t] = pv;
+          dd[t] = pv * (__uint_as_float(dv[t]) - ds_c[t]);
+        }
+        if (r == 0 && j == 1) DBG_STAMP(31 + 3 * c);
+#pragma unroll
+        for (int t8 = 0; t8 < 4; ++t8) {
+          const int col = c * 32 + t8 * 8;
+          const uint32_t off = (col >> 6) * S::SUB + sw128_offset(r, col & 63);
+          float a8[8], d8[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            a8[u] = pp[t8 * 8 + u];
+            d8[u] = dd[t8 * 8 + u];
+          }
+          store8(reinterpret_cast<bf16*>(sPT + off), a8);
+          store8(reinterpret_cast<bf16*>(sDST + off), d8);
+        }
+        if (r == 0 && j == 1) DBG_STAMP(32 + 3 * c);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+      if (r == 0 && j < 6) DBG_STAMP(42 + 4 * j);
+      if (!(ok = mbar_wait(dq_full, j & 1, p.err, 29))) break;
+      if (r == 0 && j < 6) DBG_STAMP(43 + 4 * j);
+      tc_fence_after();
+      // dQ rows: thread r owns query qt*128 + r; each 32-column chunk goes TMEM -> registers ->
+      // 128B-swizzled smem staging -> ONE TMA tensor reduction (fp32 add) for all 128 rows.
+      unsigned char* stage = smem + S::DQS;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t t[32];
+        tmem_ld32(tS + lane_off + c * 32, t);
+        if (r == 0) bulk_wait_read();   // the previous chunk's reduction has read the staging tile
+        named_bar_sync(1, 128);
+        tmem_wait_ld();
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<float4*>(stage + r * 128 + ((u ^ (r & 7)) << 4)) =
+              make_float4(__uint_as_float(t[u * 4]) * p.scale, __uint_as_float(t[u * 4 + 1]) * p.scale,
+                          __uint_as_float(t[u * 4 + 2]) * p.scale, __uint_as_float(t[u * 4 + 3]) * p.scale);
+        fence_async_smem();
+        named_bar_sync(1, 128);
+        if (r == 0) {
+          tma_reduce_add_4d(&tmDQ, stage, c * 32, h, qt * 128, b);
+          bulk_commit();
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(dq_free);
+    }
+    if (r == 0) DBG_STAMP(62);
+    if (r == 0) bulk_wait_all();   // every dQ reduction issued by this CTA has completed
+    if (ok && total > 0 && krow < p.T) {
+      // all MMAs finished: dq_full of the last pair was observed above
+      bf16* gdk = p.dk + (int64_t)b * p.dk_b + (int64_t)krow * p.dk_tok + (int64_t)hk * D;
+      bf16* gdv = p.dv + (int64_t)b * p.dv_b + (int64_t)krow * p.dv_tok + (int64_t)hk * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t tk[32], tv[32];
+        tmem_ld32(tDK + lane_off + c * 32, tk);
+        tmem_ld32(tDV + lane_off + c * 32, tv);
+        tmem_wait_ld();
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          float fk[8], fv[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            fk[e] = __uint_as_float(tk[u * 8 + e]) * p.scale;
+            fv[e] = __uint_as_float(tv[u * 8 + e]);
+          }
+          store8(gdk + c * 32 + u * 8, fk);
+          store8(gdv + c * 32 + u * 8, fv);
+        }
+      }
+    } else if (ok && total == 0 && krow < p.T) {
+      // a key tile nobody attends to (possible only for padding): zero gradients
+      bf16* gdk = p.dk + (int64_t)b * p.dk_b + (int64_t)krow * p.dk_tok + (int64_t)hk * D;
+      bf16* gdv = p.dv + (int64_t)b * p.dv_b + (int64_t)krow * p.dv_tok + (int64_t)hk * D;
+      float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int c = 0; c < D; c += 8) {
+        store8(gdk + c, z);
+        store8(gdv + c, z);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) DBG_STAMP(63);
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// fp32 [B, T, H, D] contiguous accumulator; box = 32 floats x 1 head x 128 tokens x 1, 128B swizzle.
+static bool make_map_f32(CUtensorMap* m, const void* base, int B, int T, int H, int D) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)D * 4, (cuuint64_t)H * D * 4, (cuuint64_t)T * H * D * 4};
+  cuuint32_t box[4] = {32, 1, 128, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int D>
+static int launch_bwd(const AttnTensors& t, const bf16* dout, int64_t do_tok, int64_t do_b, const BwdParams& p,
+                      int nk, cudaStream_t s) {
+  CUtensorMap mq, mk, mv, mdo, mdq;
+  if (!make_map_f32(&mdq, p.dq_acc, t.B, t.T, t.Hq, D)) return -6;
+  if (!make_map(&mq, t.q, t.B, t.T, t.Hq, D, t.q_tok, t.q_b)) return -2;
+  if (!make_map(&mk, t.k, t.B, t.T, t.Hkv, D, t.k_tok, t.k_b)) return -3;
+  if (!make_map(&mv, t.v, t.B, t.T, t.Hkv, D, t.v_tok, t.v_b)) return -4;
+  if (!make_map(&mdo, dout, t.B, t.T, t.Hq, D, do_tok, do_b)) return -5;
+  const int smem = BwdSmem<D>::TOTAL + 1024;
+  static bool init = false;
+  if (!init) {
+    cudaFuncSetAttribute(bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    init = true;
+  }
+  bwd_kernel<D><<<dim3(nk, t.Hkv, t.B), NTHREADS, smem, s>>>(mq, mk, mv, mdo, mdq, p);
+  return 0;
+}
+
+// Bit masks of every PARTIAL 128x128 tile, evaluated once per forward (shared by all heads,
+// layers and both passes): row masks (thread = query row, bit = key) for the forward and column
+// masks (thread = key row, bit = query) for the backward.
+__global__ void tile_masks_kernel(const int4* __restrict__ meta, const uint8_t* __restrict__ cls, int B, int T,
+                                  int nt, int n128, int flags, uint4* __restrict__ rowmask,
+                                  uint4* __restrict__ colmask) {
+  __shared__ int4 mq[128], mk[128];
+  const int kt = blockIdx.x, qt = blockIdx.y, b = blockIdx.z;
+  int any = 0, all = 1;
+  for (int dq = 0; dq < 2; ++dq)
+    for (int dk = 0; dk < 2; ++dk) {
+      const int qi = 2 * qt + dq, ki = 2 * kt + dk;
+      const int v = (qi < nt && ki < nt) ? cls[((int64_t)b * nt + qi) * nt + ki] : 0;
+      any |= v != 0;
+      all &= (v == 1) && ki < nt;
+    }
+  if (!any || all) return;   // EMPTY or FULL tile: no mask needed (a uniform branch)
+  const int r = threadIdx.x;
+  const int qrow = qt * 128 + r, krow = kt * 128 + r;
+  mq[r] = qrow < T ? meta[(int64_t)b * T + qrow] : make_int4(INT_MAX, INT_MAX, -7, SEG_PAD);
+  mk[r] = krow < T ? meta[(int64_t)b * T + krow] : make_int4(INT_MAX, INT_MAX, -8, SEG_PAD);
+  __syncthreads();
+  uint32_t rw[4] = {0, 0, 0, 0}, cw[4] = {0, 0, 0, 0};
+  for (int c = 0; c < 128; ++c) {
+    const int kj = kt * 128 + c, qi = qt * 128 + c;
+    const bool ra = qrow < T && kj < T && allowed(mq[r], mk[c], qrow == kj, flags);
+    const bool ca = krow < T && qi < T && allowed(mq[c], mk[r], qi == krow, flags);
+    rw[c >> 5] |= (uint32_t)ra << (c & 31);
+    cw[c >> 5] |= (uint32_t)ca << (c & 31);
+  }
+  rowmask[(((int64_t)b * n128 + qt) * n128 + kt) * 128 + r] = make_uint4(rw[0], rw[1], rw[2], rw[3]);
+  colmask[(((int64_t)b * n128 + kt) * n128 + qt) * 128 + r] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
+}
+
+// Lists at 128x128 granularity from the exact 64x64 classes.  transpose = 0: per query tile, the
+// key tiles (forward); transpose = 1: per key tile, the query tiles (backward).
+__global__ void lists128_kernel(const uint8_t* __restrict__ cls, int B, int nt, int nq, int nk,
+                                int16_t* __restrict__ list, int* __restrict__ cnt, int transpose) {
+  const int tid = blockIdx.x * blockDim.x + threadIdx.x;
+  if (tid >= B * nq) return;
+  const int b = tid / nq, q = tid % nq;
+  int c = 0;
+  for (int k = 0; k < nk; ++k) {
+    int any = 0, all = 1;
+    for (int dq = 0; dq < 2; ++dq)
+      for (int dk = 0; dk < 2; ++dk) {
+        const int qi = transpose ? 2 * k + dq : 2 * q + dq, ki = transpose ? 2 * q + dk : 2 * k + dk;
+        const int v = (qi < nt && ki < nt) ? cls[((int64_t)b * nt + qi) * nt + ki] : 0;
+        any |= v != 0;
+        all &= (v == 1) || qi >= nt;   // rows beyond T are never stored
+        if (ki >= nt) all = 0;
+      }
+    if (!any) continue;
+    list[(int64_t)tid * nk + c] = (int16_t)(k | ((all ? 1 : 2) << 14));
+    ++c;
+  }
+  cnt[tid] = c;
+}
+
+}  // namespace attn100
+
+int bd_attn_bwd_sm100(const AttnTensors& t, const bf16* dout, int64_t do_tok, int64_t do_b, const float* dsum,
+                      float* dq_acc, bf16* dk, int64_t dk_tok, int64_t dk_b, bf16* dv, int64_t dv_tok, int64_t dv_b,
+                      const int4* meta, const int16_t* list128t, const int* cnt128t, const uint4* colmask, int flags,
+                      float scale, int* err, cudaStream_t s, long long* dbg) {
+  attn100::BwdParams p;
+  p.dbg = dbg;
+  p.tmask_t = colmask;
+  p.dk = dk; p.dv = dv; p.dk_tok = dk_tok; p.dk_b = dk_b; p.dv_tok = dv_tok; p.dv_b = dv_b;
+  p.dq_acc = dq_acc; p.lse = t.lse; p.dsum = dsum; p.meta = meta; p.list = list128t; p.cnt = cnt128t; p.err = err;
+  p.T = t.T; p.Hq = t.Hq; p.group = t.Hq / t.Hkv; p.nq = (t.T + 127) / 128; p.flags = flags;
+  p.scale = scale; p.scale_log2 = scale * 1.44269504088896340736f;
+  const int nk = (t.T + 127) / 128;
+  switch (t.D) {
+    case 64: return attn100::launch_bwd<64>(t, dout, do_tok, do_b, p, nk, s);
+    case 128: return attn100::launch_bwd<128>(t, dout, do_tok, do_b, p, nk, s);
+    default: return -1;
+  }
+}
+
+void bd_attn_tile_masks(const int4* meta, const uint8_t* cls, int B, int T, int flags, uint4* rowmask, uint4* colmask,
+                        cudaStream_t s) {
+  const int nt = (T + 63) / 64, n128 = (T + 127) / 128;
+  attn100::tile_masks_kernel<<<dim3(n128, n128, B), 128, 0, s>>>(meta, cls, B, T, nt, n128, flags, rowmask, colmask);
+}
+
+void bd_attn_lists128(const uint8_t* cls, int B, int T, int16_t* list, int* cnt, int transpose, cudaStream_t s) {
+  const int nt = (T + 63) / 64, n128 = (T + 127) / 128;
+  attn100::lists128_kernel<<<ceil_div(B * n128, 128), 128, 0, s>>>(cls, B, nt, n128, n128, list, cnt, transpose);
+}
+
+int bd_attn_fwd_sm100(const AttnTensors& t, const int4* meta, const int16_t* list128, const int* cnt128,
+                      const uint4* rowmask, int flags, float scale, int* err, cudaStream_t s, long long* dbg) {
+  attn100::Params p;
+  p.dbg = dbg;
+  p.tmask = rowmask;
+  p.o = t.o; p.o_tok = t.o_tok; p.o_b = t.o_b; p.lse = t.lse; p.meta = meta;
+  p.list = list128; p.cnt = cnt128; p.err = err;
+  p.T = t.T; p.Hq = t.Hq; p.group = t.Hq / t.Hkv; p.nk = (t.T + 127) / 128; p.flags = flags;
+  p.scale_log2 = scale * 1.44269504088896340736f;
+  const int nq = (t.T + 127) / 128;
+  switch (t.D) {
+    case 64: return attn100::launch<64>(t, p, nq, s);
+    case 128: return attn100::launch<128>(t, p, nq, s);
+    default: return -1;
+  }
+}
+
+}  // namespace trida

@@ -219,6 +219,76 @@ void bd_attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, 
   TORCH_CHECK(rc == 0, "bd_attn_bwd: unsupported head_dim ", a.D);
 }
 
+std::vector<at::Tensor> bd_attn_lists128(const at::Tensor& cls, int64_t T, int64_t transpose) {
+  TORCH_CHECK(cls.scalar_type() == at::kByte && cls.is_contiguous() && cls.dim() == 3, "cls must be uint8 [B,nt,nt]");
+  const int B = cls.size(0), n = (T + 127) / 128;
+  auto list = at::empty({B, n, n}, cls.options().dtype(at::kShort));
+  auto cnt = at::empty({B, n}, cls.options().dtype(at::kInt));
+  trida::bd_attn_lists128(cls.data_ptr<uint8_t>(), B, T, list.data_ptr<int16_t>(), cnt.data_ptr<int>(), (int)transpose,
+                          stream());
+  return {list, cnt};
+}
+
+// Row / column bit masks of the PARTIAL 128x128 tiles: ([B, n, n, 128, 4], [B, n, n, 128, 4]) int32.
+std::vector<at::Tensor> bd_attn_tile_masks(const at::Tensor& meta, const at::Tensor& cls, int64_t flags) {
+  const int B = meta.size(0), T = meta.size(1), n = (T + 127) / 128;
+  auto rm = at::empty({B, n, n, 128, 4}, meta.options().dtype(at::kInt));
+  auto cm = at::empty({B, n, n, 128, 4}, meta.options().dtype(at::kInt));
+  trida::bd_attn_tile_masks(reinterpret_cast<const int4*>(meta.data_ptr<int>()), cls.data_ptr<uint8_t>(), B, T,
+                            (int)flags, reinterpret_cast<uint4*>(rm.data_ptr<int>()),
+                            reinterpret_cast<uint4*>(cm.data_ptr<int>()), stream());
+  return {rm, cm};
+}
+
+void bd_attn_fwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+                       const at::Tensor& lse, const at::Tensor& meta, const at::Tensor& list128,
+                       const at::Tensor& cnt128, const at::Tensor& rowmask, int64_t flags, double scale,
+                       const at::Tensor& err,
+                       const c10::optional<at::Tensor>& dbg) {
+  auto a = attn_tensors(q, k, v, o, lse);
+  TORCH_CHECK(err.scalar_type() == at::kInt && err.is_cuda(), "err must be a CUDA int32 tensor");
+  long long* pdbg = nullptr;
+  if (dbg.has_value() && dbg->defined()) {
+    TORCH_CHECK(dbg->scalar_type() == at::kLong && dbg->numel() >= 8 * 64, "dbg must be int64 [>= 512]");
+    pdbg = reinterpret_cast<long long*>(dbg->data_ptr<int64_t>());
+  }
+  for (auto* t : {&q, &k, &v})
+    TORCH_CHECK((t->stride(0) * 2) % 16 == 0 && (t->stride(1) * 2) % 16 == 0, "TMA strides must be 16-byte multiples");
+  const int rc = trida::bd_attn_fwd_sm100(a, reinterpret_cast<const int4*>(meta.data_ptr<int>()),
+                                          list128.data_ptr<int16_t>(), cnt128.data_ptr<int>(),
+                                          reinterpret_cast<const uint4*>(rowmask.data_ptr<int>()), (int)flags,
+                                          (float)scale, err.data_ptr<int>(), stream(), pdbg);
+  TORCH_CHECK(rc == 0, "bd_attn_fwd_sm100 failed (code ", rc, ", head_dim ", a.D, ")");
+}
+
+void bd_attn_bwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+                       const at::Tensor& lse, const at::Tensor& dout, const at::Tensor& dq, const at::Tensor& dk,
+                       const at::Tensor& dv, const at::Tensor& meta, const at::Tensor& list128t,
+                       const at::Tensor& cnt128t, const at::Tensor& colmask, int64_t flags, double scale,
+                       const at::Tensor& err,
+                       const c10::optional<at::Tensor>& dbg) {
+  auto a = attn_tensors(q, k, v, o, lse);
+  long long* pdbg = nullptr;
+  if (dbg.has_value() && dbg->defined()) pdbg = reinterpret_cast<long long*>(dbg->data_ptr<int64_t>());
+  for (auto* t : {&dout, &dq, &dk, &dv})
+    TORCH_CHECK(t->dim() == 4 && t->stride(3) == 1 && t->stride(2) == t->size(3), "attention grad layout");
+  TORCH_CHECK((dout.stride(0) * 2) % 16 == 0 && (dout.stride(1) * 2) % 16 == 0 &&
+                  ((uintptr_t)dout.data_ptr() % 16) == 0, "dout must be TMA-compatible");
+  auto dsum = at::empty({a.B, a.Hq, a.T}, lse.options());
+  auto dq_acc = at::empty({a.B, a.T, a.Hq, a.D}, lse.options());
+  trida::bd_attn_bwd_prep(a, cbf(dout), dout.stride(1), dout.stride(0), dsum.data_ptr<float>(),
+                          dq_acc.data_ptr<float>(), stream());
+  const int rc = trida::bd_attn_bwd_sm100(a, cbf(dout), dout.stride(1), dout.stride(0), dsum.data_ptr<float>(),
+                                          dq_acc.data_ptr<float>(), mbf(dk), dk.stride(1), dk.stride(0), mbf(dv),
+                                          dv.stride(1), dv.stride(0), reinterpret_cast<const int4*>(meta.data_ptr<int>()),
+                                          list128t.data_ptr<int16_t>(), cnt128t.data_ptr<int>(),
+                                          reinterpret_cast<const uint4*>(colmask.data_ptr<int>()), (int)flags,
+                                          (float)scale, err.data_ptr<int>(), stream(), pdbg);
+  TORCH_CHECK(rc == 0, "bd_attn_bwd_sm100 failed (code ", rc, ", head_dim ", a.D, ")");
+  trida::bd_attn_dq_convert(dq_acc.data_ptr<float>(), mbf(dq), dq.stride(1), dq.stride(0), a.B, a.T, a.Hq, a.D,
+                            sm_count(), stream());
+}
+
 void ce_rows(const at::Tensor& logits, const at::Tensor& target, const c10::optional<at::Tensor>& weight,
              double grad_scale, const at::Tensor& loss, const c10::optional<at::Tensor>& dlogits) {
   CHECK_F32(logits); CHECK_ROWMAJOR(logits);
@@ -284,6 +354,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bd_attn_plan", &bd_attn_plan);
   m.def("bd_attn_fwd", &bd_attn_fwd);
   m.def("bd_attn_bwd", &bd_attn_bwd);
+  m.def("bd_attn_lists128", &bd_attn_lists128);
+  m.def("bd_attn_fwd_sm100", &bd_attn_fwd_sm100, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"),
+        py::arg("lse"), py::arg("meta"), py::arg("list128"), py::arg("cnt128"), py::arg("rowmask"), py::arg("flags"),
+        py::arg("scale"), py::arg("err"), py::arg("dbg") = py::none());
+  m.def("bd_attn_tile_masks", &bd_attn_tile_masks);
+  m.def("bd_attn_bwd_sm100", &bd_attn_bwd_sm100, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"),
+        py::arg("lse"), py::arg("dout"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("meta"),
+        py::arg("list128t"), py::arg("cnt128t"), py::arg("colmask"), py::arg("flags"), py::arg("scale"), py::arg("err"),
+        py::arg("dbg") = py::none());
   m.def("ce_rows", &ce_rows);
   m.def("grad_norm", &grad_norm);
   m.def("adamw", &adamw);

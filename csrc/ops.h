@@ -46,6 +46,21 @@ int bd_attn_bwd(const AttnTensors& t, const bf16* dout, int64_t do_tok, int64_t 
                 int64_t dv_tok, int64_t dv_b, const int4* meta, const int16_t* bwd_list, const int* bwd_cnt,
                 int flags, float scale, int sm_count, cudaStream_t s);
 
+// ---- tcgen05 forward (bd_attention_sm100.cu) ----
+void bd_attn_lists128(const uint8_t* cls, int B, int T, int16_t* list, int* cnt, int transpose, cudaStream_t s);
+int bd_attn_bwd_sm100(const AttnTensors& t, const bf16* dout, int64_t do_tok, int64_t do_b, const float* dsum,
+                      float* dq_acc, bf16* dk, int64_t dk_tok, int64_t dk_b, bf16* dv, int64_t dv_tok, int64_t dv_b,
+                      const int4* meta, const int16_t* list128t, const int* cnt128t, const uint4* colmask, int flags,
+                      float scale, int* err, cudaStream_t s, long long* dbg = nullptr);
+void bd_attn_bwd_prep(const AttnTensors& t, const bf16* dout, int64_t do_tok, int64_t do_b, float* dsum, float* dq_acc,
+                      cudaStream_t s);
+void bd_attn_dq_convert(const float* dq_acc, bf16* dq, int64_t dq_tok, int64_t dq_b, int B, int T, int Hq, int D,
+                        int sm_count, cudaStream_t s);
+void bd_attn_tile_masks(const int4* meta, const uint8_t* cls, int B, int T, int flags, uint4* rowmask, uint4* colmask,
+                        cudaStream_t s);
+int bd_attn_fwd_sm100(const AttnTensors& t, const int4* meta, const int16_t* list128, const int* cnt128,
+                      const uint4* rowmask, int flags, float scale, int* err, cudaStream_t s, long long* dbg = nullptr);
+
 // ---- cross-entropy rows (cross_entropy.cu) ----
 void ce_rows_fwd_bwd(const float* logits, int64_t ld, const int64_t* target, const float* weight, float grad_scale,
                      int n, int V, float* loss, bf16* dlogits, int64_t ldd, cudaStream_t s);

@@ -178,6 +178,75 @@ def test_bd_attention_fwd_bwd(d, x0tok, wbc, packed):
     assert rel_err(dv, vr.grad) < 2e-2
 
 
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("x0tok,wbc,packed", [(True, False, False), (False, True, False), (True, False, True)])
+def test_bd_attention_fwd_tcgen05(d, x0tok, wbc, packed):
+    torch.manual_seed(0)
+    B, P, Rr, bd, Hq, Hkv = 2, 160, 192, 32, 4, 2   # T = 544: ragged last 128-tile
+    meta = bd_layout(B, P, Rr, bd, "cuda", packed)
+    T = meta["seg"].shape[1]
+    q = torch.randn(B, T, Hq, d, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(B, T, Hkv, d, device="cuda", dtype=torch.bfloat16)
+    kv = torch.randn(B, T, 2 * Hkv, d, device="cuda", dtype=torch.bfloat16)
+    v = kv[:, :, Hkv:]
+    from trida_stack_b200.ops.blocks import AttnContext, device_error_word, check_device_errors
+    actx = AttnContext(meta["seg"], meta["opos"], meta["rblk"], meta["segid"], meta["view"], meta["opos"], x0tok, wbc)
+    l128, c128 = actx.plan128
+    o = torch.full_like(q, float("nan"))
+    lse = torch.empty(B, Hq, T, device="cuda")
+    C().bd_attn_fwd_sm100(q, k, v, o, lse, actx.meta, l128, c128, actx.masks[0], actx.flags, 1 / math.sqrt(d),
+                          device_error_word("cuda"))
+    torch.cuda.synchronize()
+    check_device_errors()
+    ref = R.bd_attention(q.float(), k.float(), v.float(), actx.meta_dict(), x0tok, wbc)
+    valid_q = (meta["seg"] != R.PAD)[:, :, None, None]
+    assert torch.isfinite(o).all()
+    assert rel_err(o * valid_q, ref * valid_q) < 1e-2
+    # LSE agrees with the warp-MMA kernel's
+    o2, lse2 = torch.empty_like(q), torch.empty_like(lse)
+    _, fl, fc, _, _ = actx.plan
+    C().bd_attn_fwd(q, k, v, o2, lse2, actx.meta, fl, fc, actx.flags, 1 / math.sqrt(d))
+    assert (lse - lse2).abs().max().item() < 1e-2
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("x0tok,wbc,packed", [(True, False, False), (False, True, False), (True, False, True)])
+def test_bd_attention_bwd_tcgen05(d, x0tok, wbc, packed):
+    torch.manual_seed(0)
+    B, P, Rr, bd, Hq, Hkv = 2, 160, 192, 32, 4, 2   # T = 544: ragged last 128-tile
+    meta = bd_layout(B, P, Rr, bd, "cuda", packed)
+    T = meta["seg"].shape[1]
+    q = torch.randn(B, T, Hq, d, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(B, T, Hkv, d, device="cuda", dtype=torch.bfloat16)
+    kv = torch.randn(B, T, 2 * Hkv, d, device="cuda", dtype=torch.bfloat16)
+    v = kv[:, :, Hkv:]
+    from trida_stack_b200.ops.blocks import AttnContext, device_error_word, check_device_errors
+    actx = AttnContext(meta["seg"], meta["opos"], meta["rblk"], meta["segid"], meta["view"], meta["opos"], x0tok, wbc)
+    _, fl, fc, _, _ = actx.plan
+    o = torch.empty_like(q)
+    lse = torch.empty(B, Hq, T, device="cuda")
+    scale = 1 / math.sqrt(d)
+    C().bd_attn_fwd(q, k, v, o, lse, actx.meta, fl, fc, actx.flags, scale)
+    qr, kr, vr = (t.float().requires_grad_() for t in (q, k, v))
+    orf = R.bd_attention(qr, kr, vr, actx.meta_dict(), x0tok, wbc)
+    valid_q = (meta["seg"] != R.PAD)[:, :, None, None]
+    do = torch.randn_like(q) * valid_q
+    (orf * do.float()).sum().backward()
+    lt, ct = actx.plan128t
+    dq = torch.full_like(q, float("nan"))
+    dk = torch.full_like(k, float("nan"))
+    dkv = torch.zeros_like(kv)
+    dv = dkv[:, :, Hkv:]
+    C().bd_attn_bwd_sm100(q, k, v, o, lse, do, dq, dk, dv, actx.meta, lt, ct, actx.masks[1], actx.flags, scale,
+                          device_error_word("cuda"))
+    torch.cuda.synchronize()
+    check_device_errors()
+    assert torch.isfinite(dq).all() and torch.isfinite(dk).all() and torch.isfinite(dv).all()
+    assert rel_err(dq, qr.grad) < 2e-2
+    assert rel_err(dk, kr.grad) < 2e-2
+    assert rel_err(dv, vr.grad) < 2e-2
+
+
 def test_attention_plan_skips_and_classifies():
     meta = bd_layout(1, 128, 256, 32, "cuda")
     from trida_stack_b200.ops.blocks import AttnContext

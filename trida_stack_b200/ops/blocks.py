@@ -24,6 +24,31 @@ from ._ext import ext
 TN, TT, NT = 0, 1, 2
 
 
+_ERR_WORDS = {}
+
+
+def device_error_word(device):
+    """int32 word that bounded device-side waits set (non-zero) instead of hanging."""
+    key = str(device)
+    if key not in _ERR_WORDS:
+        _ERR_WORDS[key] = torch.zeros(1, dtype=torch.int32, device=device)
+    return _ERR_WORDS[key]
+
+
+def check_device_errors():
+    """Raise if any kernel recorded a timed-out wait (host sync; call between steps)."""
+    for key, w in _ERR_WORDS.items():
+        code = int(w.item())
+        if code:
+            w.zero_()
+            raise RuntimeError(f"device-side wait timed out on {key} (code {code})")
+
+
+def use_tcgen05_attention(head_dim, which="FWD"):
+    import os
+    return head_dim in (64, 128) and os.environ.get(f"TRIDA_ATTN_{which}", "tcgen05") == "tcgen05"
+
+
 def gemm(layout, a, b, d, c=None, alpha=1.0, beta=0.0, tile=0):
     ext().gemm(layout, a, b, d, c, alpha, beta, tile)
     return d
@@ -89,6 +114,27 @@ class AttnContext:
             self._plan = ext().bd_attn_plan(self.meta, self.flags)
         return self._plan
 
+    @property
+    def plan128(self):
+        """Non-empty 128x128 tile lists for the tcgen05 kernels."""
+        if getattr(self, "_plan128", None) is None:
+            self._plan128 = ext().bd_attn_lists128(self.plan[0], self.T, 0)
+        return self._plan128
+
+    @property
+    def masks(self):
+        """(row, column) bit masks of the PARTIAL 128x128 tiles, shared by all layers and heads."""
+        if getattr(self, "_masks", None) is None:
+            self._masks = ext().bd_attn_tile_masks(self.meta, self.plan[0], self.flags)
+        return self._masks
+
+    @property
+    def plan128t(self):
+        """Per 128-key tile, the non-empty 128-query tiles (tcgen05 backward)."""
+        if getattr(self, "_plan128t", None) is None:
+            self._plan128t = ext().bd_attn_lists128(self.plan[0], self.T, 1)
+        return self._plan128t
+
     def meta_dict(self):
         return {"seg": self.seg, "opos": self.opos, "rblk": self.rblk, "segid": self.segid,
                 "view": self.view}
@@ -99,6 +145,29 @@ def rope_tables(max_pos, rotary_dim, theta, device):
     inv = 1.0 / (theta ** (torch.arange(0, rotary_dim, 2, dtype=torch.float32, device=device) / rotary_dim))
     f = torch.arange(max_pos, dtype=torch.float32, device=device)[:, None] * inv[None]
     return f.cos().contiguous(), f.sin().contiguous()
+
+
+def attn_fwd(q, k, v, o, lse, actx):
+    """Block-diffusion attention forward: tcgen05 kernel for head_dim 64/128, else the warp-MMA one."""
+    d = q.shape[-1]
+    if use_tcgen05_attention(d):
+        l128, c128 = actx.plan128
+        ext().bd_attn_fwd_sm100(q, k, v, o, lse, actx.meta, l128, c128, actx.masks[0], actx.flags,
+                                1.0 / math.sqrt(d), device_error_word(q.device))
+    else:
+        _, fl, fc, _, _ = actx.plan
+        ext().bd_attn_fwd(q, k, v, o, lse, actx.meta, fl, fc, actx.flags, 1.0 / math.sqrt(d))
+
+
+def attn_bwd(q, k, v, o, lse, do, dq, dk, dv, actx):
+    d = q.shape[-1]
+    if use_tcgen05_attention(d, "BWD"):
+        lt, ct = actx.plan128t
+        ext().bd_attn_bwd_sm100(q, k, v, o, lse, do, dq, dk, dv, actx.meta, lt, ct, actx.masks[1], actx.flags,
+                                1.0 / math.sqrt(d), device_error_word(q.device))
+    else:
+        _, _, _, bl, bc = actx.plan
+        ext().bd_attn_bwd(q, k, v, o, lse, do, dq, dk, dv, actx.meta, bl, bc, actx.flags, 1.0 / math.sqrt(d))
 
 
 # ---------------------------------------------------------------------------------------------
@@ -121,8 +190,7 @@ class _AttnBlock(torch.autograd.Function):
         v = qkv.view(B, T, -1)[:, :, (Hq + Hkv) * d:].view(B, T, Hkv, d)
         o = torch.empty(B, T, Hq, d, dtype=x.dtype, device=x.device)
         lse = torch.empty(B, Hq, T, dtype=torch.float32, device=x.device)
-        _, fl, fc, bl, bc = actx.plan
-        C.bd_attn_fwd(q, k, v, o, lse, actx.meta, fl, fc, actx.flags, 1.0 / math.sqrt(d))
+        attn_fwd(q, k, v, o, lse, actx)
         out = torch.empty_like(x)
         gemm(TN, o.view(M, Hq * d), wo, out, x, 1.0, 1.0)
         ctx.save_for_backward(x, rstd, norm_w, wqkv, qn, kn, wo, qkv, rstd_qk, q, k, o, lse)
@@ -147,9 +215,7 @@ class _AttnBlock(torch.autograd.Function):
         dk = torch.empty_like(k)
         dv = dqkv.view(B, T, -1)[:, :, (Hq + Hkv) * d:].view(B, T, Hkv, d)
         v = qkv.view(B, T, -1)[:, :, (Hq + Hkv) * d:].view(B, T, Hkv, d)
-        _, fl, fc, bl, bc = actx.plan
-        C.bd_attn_bwd(q, k, v, o, lse, do.view(B, T, Hq, d), dq, dk, dv, actx.meta, bl, bc, actx.flags,
-                      1.0 / math.sqrt(d))
+        attn_bwd(q, k, v, o, lse, do.view(B, T, Hq, d), dq, dk, dv, actx)
         del do
         gqn, gkn = _vec_buf(qn), _vec_buf(kn)
         C.qk_norm_rope_bwd(dq, dk, qkv, qn, kn, actx.cos_t, actx.sin_t, actx.pos32, rstd_qk, dqkv, gqn, gkn,
