@@ -1,0 +1,140 @@
+"""Training orchestration on CPU: loop schedule, sync pattern, resume, checkpoint order, CLI,
+process-group setup order (same checks as the reference's train/test_training.py)."""
+import itertools
+from types import SimpleNamespace
+from unittest.mock import Mock
+
+import pytest
+import torch
+
+from trida_stack_b200 import checkpoint, distributed
+from trida_stack_b200 import train as trainer
+from trida_stack_b200.cli import build_parser
+from trida_stack_b200.data.loaders import TrainingLoaders
+from trida_stack_b200.engine import get_lr
+from trida_stack_b200.optimizer import build_optimizer
+
+
+class ToyModel(torch.nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.weight = torch.nn.Parameter(torch.tensor(1.0))
+        self.events = []
+
+    def set_requires_gradient_sync(self, enabled):
+        self.events.append(("sync", enabled))
+
+    def forward(self, ids, labels, mask, *, decision=None, **kwargs):
+        if decision is not None:
+            self.events.append(("decision", None))
+            return 2 * self.weight.square(), {"decision_acc": 1.0, "decision_questions": 1, "decision_tokens": 4}
+        self.events.append(("text", kwargs))
+        loss = self.weight.square()
+        return loss, {"diff_loss": loss.detach(), "ar_loss": loss.detach(), "ntok": 2}
+
+
+@pytest.mark.parametrize("mode", ["text", "mixed", "decision"])
+@pytest.mark.parametrize("resume", [False, True])
+def test_training_updates_sync_resume_and_checkpoint_boundaries(monkeypatch, mode, resume):
+    args = build_parser().parse_args([])
+    args.decision_only = mode == "decision"
+    args.decision_micro_per_step = 2
+    args.decision_loss_weight = 0.5
+    args.grad_accum = 2
+    args.grad_clip = 100
+    args.lr = 0.1
+    args.lr_min_ratio = 1
+    args.warmup = 0
+    args.max_steps = 3
+    args.log_every = 1
+    args.save_every = 2
+    args.resume = "checkpoint" if resume else None
+    model = ToyModel()
+    optim = torch.optim.SGD(model.parameters(), lr=args.lr)
+    batch = {k: torch.ones(1, 2, dtype=torch.long) for k in (
+        "input_ids", "labels", "attention_mask", "seg_id", "resp_pos", "resp_block", "turn_id",
+        "pixel_values", "image_grid_thw", "mrope_pos")}
+    text = [None, batch, batch, batch] if mode != "decision" else None
+    decision = itertools.repeat({"questions": [{"variant": 0}]}) if mode != "text" else None
+    saved, logs = [], []
+
+    def save(model, optimizer, step, args):
+        assert model.weight.grad is None
+        saved.append(step)
+
+    load = Mock(return_value=1)
+    monkeypatch.setattr(trainer, "load_train_state", load)
+    monkeypatch.setattr(trainer, "save_checkpoint", save)
+    monkeypatch.setattr(trainer, "log", logs.append)
+    trainer.run_training(args, "cpu", model, TrainingLoaders(text, decision), optim)
+    steps = 2 if resume else 3
+    factor = 0.6 if mode == "mixed" else 0.8
+    assert model.weight.item() == pytest.approx(factor ** steps, abs=1e-6)
+    assert saved == [2, 3]
+    assert len(logs) == steps
+    assert [e[1] for e in model.events if e[0] == "sync"] == {
+        "text": [False, True] * steps, "mixed": [False, False, False, True] * steps,
+        "decision": [False, True] * steps}[mode]
+    assert sum(e[0] == "text" for e in model.events) == (0 if mode == "decision" else 2 * steps)
+    assert load.call_count == int(resume)
+
+
+def test_lr_schedule_and_optimizer_groups():
+    args = build_parser().parse_args(["--lr", "1e-3", "--decision_head_lr_scale", "5"])
+    a = torch.nn.Parameter(torch.ones(10))
+    b = torch.nn.Parameter(torch.ones(3))
+    model = SimpleNamespace(param_groups=Mock(return_value=[{"params": [a], "lr_scale": 1.0},
+                                                            {"params": [b], "lr_scale": 5.0}]))
+    opt = build_optimizer(args, model, device=torch.device("cpu"))
+    assert opt.defaults["betas"] == (0.9, args.adam_beta2)
+    assert opt.param_groups[1]["lr_scale"] == 5.0
+    assert get_lr(0, 1, 2, 10, 0.1) == 0.5
+    assert get_lr(10, 1, 2, 10, 0.1) == 0.1
+
+
+def test_checkpoint_saves_weights_before_optimizer(monkeypatch):
+    events = []
+    monkeypatch.setattr(checkpoint, "save_hf", lambda *a: events.append(("weights", a[-1])))
+    monkeypatch.setattr(checkpoint, "save_train_state", lambda *a: events.append(("optimizer", a[-1])))
+    checkpoint.save_checkpoint(None, None, 12, None)
+    assert events == [("weights", "step_12"), ("optimizer", "step_12")]
+
+
+def test_distributed_binds_gpu_before_process_group(monkeypatch):
+    events = []
+    monkeypatch.setenv("LOCAL_RANK", "2")
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: True)
+    monkeypatch.setattr(torch.cuda, "set_device", lambda n: events.append(("device", n)))
+    monkeypatch.setattr(distributed.dist, "is_initialized", lambda: False)
+    monkeypatch.setattr(distributed.dist, "init_process_group",
+                        lambda backend, device_id, timeout: events.append((backend, str(device_id))))
+    monkeypatch.setattr(torch, "manual_seed", lambda seed: events.append(("seed", seed)))
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: 2)
+    distributed.setup_distributed(SimpleNamespace(seed=42))
+    assert events == [("device", 2), ("nccl", "cuda:2"), ("seed", 42)]
+
+
+@pytest.mark.parametrize("suffix,value,expected", [
+    ("data", "records.jsonl", "records.jsonl"), ("only", None, True), ("loss_weight", "0.5", 0.5),
+    ("micro_per_step", "2", 2), ("max_tokens", "1024", 1024), ("max_state", "384", 384),
+    ("head_dim", "32", 32), ("head_lr_scale", "5", 5.0)])
+def test_cli_accepts_decision_flags_and_rejects_legacy(suffix, value, expected):
+    p = build_parser()
+    extra = [] if value is None else [value]
+    assert getattr(p.parse_args([f"--decision_{suffix}", *extra]), f"decision_{suffix}") == expected
+    with pytest.raises(SystemExit) as e:
+        p.parse_args([f"--jev_{suffix}", *extra])
+    assert e.value.code == 2
+
+
+def test_help_is_torch_free():
+    import subprocess
+    import sys
+    code = ("import sys; sys.argv=['train.py','--help']; import builtins; real=builtins.__import__\n"
+            "def guard(n,*a,**k):\n    assert not n.startswith('torch'), n\n    return real(n,*a,**k)\n"
+            "builtins.__import__=guard\nexec(open('train.py').read())")
+    import os
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    assert "--model_id" in r.stdout

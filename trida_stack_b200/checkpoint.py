@@ -1,0 +1,152 @@
+"""Checkpoints in the reference layout (``train/checkpoint.py:14-105``):
+
+    save_dir/step_N/
+      config.json, model*.safetensors (+ model.safetensors.index.json)   HF-loadable weights
+      tokenizer files (with <|mask|>)                                    when a tokenizer is attached
+      block_diffusion.json  {bd_size, mask_id, ar_loss_weight}
+      jev_head.pt           {"head": {q.weight, q.bias, k.weight, k.bias}, "head_dim"}   decision head
+      train_state/ + train_state.json {global_step}                      with --save_optim_state
+
+Weights are written by rank 0 in bf16 (fp32 masters are cast); the sharded optimizer state is
+written with torch.distributed.checkpoint, one key set per rank, and restored only into a run with
+the same world size (exact resume); otherwise ``--resume`` is a warm restart.  Every early exit is
+decided identically on all ranks so the collective calls never diverge.
+"""
+import json
+import os
+
+import torch
+import torch.distributed as dist
+
+from .distributed import is_master, log
+
+SHARD_BYTES = 5 * 1024 ** 3
+
+
+def _barrier():
+    if dist.is_available() and dist.is_initialized():
+        dist.barrier()
+
+
+def write_hf_weights(state, out_dir, max_shard_bytes=SHARD_BYTES):
+    """Save ``state`` (name -> tensor) as safetensors shards + index (HF layout)."""
+    from safetensors.torch import save_file
+    os.makedirs(out_dir, exist_ok=True)
+    shards, cur, size = [], {}, 0
+    for name in state:
+        t = state[name].detach().to("cpu").contiguous()
+        nbytes = t.numel() * t.element_size()
+        if cur and size + nbytes > max_shard_bytes:
+            shards.append(cur)
+            cur, size = {}, 0
+        cur[name] = t
+        size += nbytes
+    if cur:
+        shards.append(cur)
+    if len(shards) == 1:
+        save_file(shards[0], os.path.join(out_dir, "model.safetensors"), metadata={"format": "pt"})
+        return
+    index = {"metadata": {"total_size": sum(t.numel() * t.element_size() for s in shards for t in s.values())},
+             "weight_map": {}}
+    for i, sh in enumerate(shards):
+        fname = f"model-{i + 1:05d}-of-{len(shards):05d}.safetensors"
+        save_file(sh, os.path.join(out_dir, fname), metadata={"format": "pt"})
+        for k in sh:
+            index["weight_map"][k] = fname
+    with open(os.path.join(out_dir, "model.safetensors.index.json"), "w") as f:
+        json.dump(index, f, indent=2)
+
+
+def read_hf_weights(path):
+    """name -> tensor from every ``*.safetensors`` file of an HF model dir."""
+    import glob
+    from safetensors.torch import load_file
+    files = sorted(glob.glob(os.path.join(path, "*.safetensors")))
+    if not files:
+        raise FileNotFoundError(f"no *.safetensors weights in {path}")
+    sd = {}
+    for f in files:
+        sd.update(load_file(f))
+    return sd
+
+
+def save_hf(model, args, tag):
+    out = os.path.join(args.save_dir, tag)
+    if is_master():
+        dec = model.decoder
+        state = dec.hf_state_dict(dtype=torch.bfloat16)
+        write_hf_weights(state, out)
+        cfg = dec.cfg.to_hf_dict()
+        cfg["dtype"] = "bfloat16"
+        cfg.pop("torch_dtype", None)
+        with open(os.path.join(out, "config.json"), "w") as f:
+            json.dump(cfg, f, indent=2)
+        if getattr(model, "tokenizer", None) is not None:
+            model.tokenizer.save_pretrained(out)
+        head = getattr(model, "decision_head", None)
+        if head is not None:
+            torch.save({"head": {k: v.detach().to("cpu", torch.bfloat16 if v.is_floating_point() else v.dtype)
+                                 for k, v in head.state_dict().items()},
+                        "head_dim": head.q.out_features}, os.path.join(out, "jev_head.pt"))
+        with open(os.path.join(out, "block_diffusion.json"), "w") as f:
+            json.dump({"bd_size": model.bd_size, "mask_id": model.mask_id,
+                       "ar_loss_weight": model.ar_loss_weight}, f, indent=2)
+        log(f"[save] wrote {out}")
+    _barrier()
+
+
+def _optim_state(optim):
+    sd = optim.state_dict()
+    r = sd["rank"]
+    flat = {"step": torch.tensor(sd["step"]), "world": torch.tensor(sd["world"])}
+    for i, g in enumerate(sd["groups"]):
+        flat[f"rank{r}.g{i}.m"] = g["m"]
+        flat[f"rank{r}.g{i}.v"] = g["v"]
+        if g["master"] is not None:
+            flat[f"rank{r}.g{i}.master"] = g["master"]
+    return flat
+
+
+def save_train_state(model, optim, global_step, args, tag):
+    if not args.save_optim_state:
+        return
+    import torch.distributed.checkpoint as dcp
+    out = os.path.join(args.save_dir, tag)
+    dcp.save({"optim": _optim_state(optim)}, checkpoint_id=os.path.join(out, "train_state"))
+    if is_master():
+        with open(os.path.join(out, "train_state.json"), "w") as f:
+            json.dump({"global_step": global_step}, f)
+    _barrier()
+
+
+def load_train_state(model, optim, resume_dir):
+    """Restore the optimizer + step when ``resume_dir`` has train state, else 0 (warm restart)."""
+    state_dir = os.path.join(resume_dir, "train_state")
+    meta = os.path.join(resume_dir, "train_state.json")
+    if not (os.path.isdir(state_dir) and os.path.exists(meta)):
+        log(f"[resume] {resume_dir} has no optimizer state -> warm restart (fresh optimizer, step 0)")
+        return 0
+    import torch.distributed.checkpoint as dcp
+    tmpl = _optim_state(optim)
+    dcp.load({"optim": tmpl}, checkpoint_id=state_dir)
+    sd = optim.state_dict()
+    if int(tmpl["world"]) != sd["world"]:
+        raise ValueError(f"train_state was written by {int(tmpl['world'])} ranks, this run has {sd['world']}")
+    r = sd["rank"]
+    for i, g in enumerate(sd["groups"]):
+        g["m"].copy_(tmpl[f"rank{r}.g{i}.m"])
+        g["v"].copy_(tmpl[f"rank{r}.g{i}.v"])
+        if g["master"] is not None:
+            g["master"].copy_(tmpl[f"rank{r}.g{i}.master"])
+    optim.step_count = int(tmpl["step"])
+    with open(meta) as f:
+        gs = int(json.load(f)["global_step"])
+    log(f"[resume] restored optimizer + global_step={gs} from {resume_dir}")
+    return gs
+
+
+def save_checkpoint(model, optim, global_step, args):
+    """Weights first, then the optional optimizer state, on every rank in the same order."""
+    tag = f"step_{global_step}"
+    save_hf(model, args, tag)
+    save_train_state(model, optim, global_step, args, tag)

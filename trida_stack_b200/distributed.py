@@ -54,3 +54,14 @@ def setup_distributed(args, backend=None, timeout_s=None):
         dev = torch.device("cpu")
     torch.manual_seed(args.seed)
     return dev
+
+
+def shard_model(model, args):
+    """Prepare the model for training.  Parameter/gradient sharding itself lives in the optimizer
+    (flat buffers, ``parallel.zero``), so this only sets train mode and reports sizes."""
+    model.train()
+    n_train = sum(p.numel() for p in model.parameters() if p.requires_grad)
+    n_all = sum(p.numel() for p in model.parameters())
+    log(f"[model] {args.model_id} on {world_size()} ranks | {'fp32 master' if args.fp32_master else 'bf16'} weights "
+        f"| trainable {n_train / 1e9:.2f}B of {n_all / 1e9:.2f}B params")
+    return model

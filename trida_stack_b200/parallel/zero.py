@@ -108,9 +108,21 @@ class ShardedAdamW:
     def zero_grad(self, set_to_none=True):
         for g in self.groups:
             g.grad.zero_()
+            for p in g.params:
+                p.grad = None
+
+    def collect_autograd_grads(self):
+        """Fold ordinary ``.grad`` tensors (CPU path, plain torch modules) into the flat fp32
+        buffers; the CUDA blocks write ``main_grad`` directly and leave ``.grad`` unset."""
+        for g in self.groups:
+            for p in g.params:
+                if p.grad is not None:
+                    p.main_grad.add_(p.grad.float())
+                    p.grad = None
 
     def reduce_gradients(self):
         """Average gradients across ranks into each rank's shard (reduce-scatter)."""
+        self.collect_autograd_grads()
         if self.world == 1:
             return
         avg = dist.get_backend(self.pg) == "nccl"   # gloo has no AVG reduction
