@@ -33,6 +33,8 @@ class AttentionLayer(nn.Module):
         x = blocks.attn_block(x, self.input_norm, self.wqkv, self.q_norm, self.k_norm, self.wo, actx, cfg)
         return blocks.mlp_block(x, self.post_norm, self.wgu, self.wdown, cfg.eps)
 
+    # q_proj rows of the gated (Qwen3.5) attention are per head [query (d) ; gate (d)]
+
     # HF <-> fused names
     def hf_items(self, prefix, cfg):
         d, Hq, Hkv, F = cfg.head_dim, cfg.n_heads, cfg.n_kv_heads, cfg.intermediate_size
@@ -132,12 +134,30 @@ class Decoder(nn.Module):
             items.append(("lm_head.weight", self.lm_head, None))
         return items
 
+    _CENTERED = ("input_layernorm.weight", "post_attention_layernorm.weight", "self_attn.q_norm.weight",
+                 "self_attn.k_norm.weight")
+
+    def _norm_offset(self, name):
+        """Qwen3.5 stores RMSNorm weights zero-centred (applied as 1 + w); the native layers keep the
+        effective weight, so 1 is added on load and removed on save."""
+        if not self.cfg.model_type.startswith("qwen3_5"):
+            return 0.0
+        return 1.0 if (name.endswith(self._CENTERED) or name == "model.norm.weight") else 0.0
+
+    @staticmethod
+    def _view(p, sl):
+        if sl is None:
+            return p
+        if sl == "conv":          # HF depthwise conv1d weight [C, 1, K] <-> native [C, K]
+            return p.unsqueeze(1)
+        return p[sl[0]:sl[1]]
+
     @torch.no_grad()
     def hf_state_dict(self, dtype=None):
         out = {}
         for name, p, sl in self.hf_items():
-            t = p if sl is None else p[sl[0]:sl[1]]
-            out[name] = (t.to(dtype) if dtype is not None else t).detach().contiguous()
+            t = self._view(p, sl).float() - self._norm_offset(name)
+            out[name] = t.to(dtype or p.dtype).detach().contiguous()
         return out
 
     @torch.no_grad()
@@ -150,10 +170,10 @@ class Decoder(nn.Module):
             if src is None:
                 missing.append(name)
                 continue
-            dst = p if sl is None else p[sl[0]:sl[1]]
+            dst = self._view(p, sl)
             if tuple(src.shape) != tuple(dst.shape):
                 raise ValueError(f"{name}: checkpoint shape {tuple(src.shape)} != model {tuple(dst.shape)}")
-            dst.copy_(src.to(dst.dtype))
+            dst.copy_((src.float() + self._norm_offset(name)).to(dst.dtype))
         if strict and missing:
             raise KeyError(f"missing weights: {missing[:8]}{'...' if len(missing) > 8 else ''}")
         return missing

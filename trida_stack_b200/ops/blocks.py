@@ -237,16 +237,26 @@ def _attn_block_ref(x, norm_w, wqkv, qn, kn, wo, actx, cfg):
     B, T, Hq, Hkv, d, eps = actx.B, actx.T, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.eps
     h = R.rmsnorm(x, norm_w, eps)
     qkv = h @ wqkv.t()
-    q = qkv[:, : Hq * d].view(B, T, Hq, d)
-    k = qkv[:, Hq * d:(Hq + Hkv) * d].view(B, T, Hkv, d)
-    v = qkv[:, (Hq + Hkv) * d:].view(B, T, Hkv, d)
+    gate = None
+    if cfg.attn_output_gate:
+        qg = qkv[:, : 2 * Hq * d].view(B, T, Hq, 2 * d)
+        q, gate = qg[..., :d], qg[..., d:].reshape(B * T, Hq * d)
+        k = qkv[:, 2 * Hq * d:(2 * Hq + Hkv) * d].view(B, T, Hkv, d)
+        v = qkv[:, (2 * Hq + Hkv) * d:].view(B, T, Hkv, d)
+    else:
+        q = qkv[:, : Hq * d].view(B, T, Hq, d)
+        k = qkv[:, Hq * d:(Hq + Hkv) * d].view(B, T, Hkv, d)
+        v = qkv[:, (Hq + Hkv) * d:].view(B, T, Hkv, d)
     q = R.rmsnorm(q, qn, eps)
     k = R.rmsnorm(k, kn, eps)
     cos, sin = R.rope_cos_sin(actx.pos, d, cfg.rope_theta, cfg.rotary_dim, dtype=torch.float32)
     q = R.apply_rope(q.float(), cos, sin).to(x.dtype)
     k = R.apply_rope(k.float(), cos, sin).to(x.dtype)
     o = R.bd_attention(q, k, v, actx.meta_dict(), actx.x0_token_causal, actx.within_block_causal)
-    return x + o.reshape(B * T, Hq * d) @ wo.t()
+    o = o.reshape(B * T, Hq * d)
+    if gate is not None:
+        o = o * torch.sigmoid(gate.float()).to(o.dtype)
+    return x + o @ wo.t()
 
 
 def attn_block(x, norm_w, wqkv, qn, kn, wo, actx, cfg):
