@@ -52,6 +52,8 @@ void gemm(int64_t layout, const at::Tensor& A, const at::Tensor& B, const at::Te
     TORCH_CHECK(C->scalar_type() == D.scalar_type(), "C dtype must match D");
     TORCH_CHECK(C->size(0) == M && C->size(1) == N, "C shape mismatch");
     a.C = C->data_ptr(); a.ldc = C->stride(0);
+    TORCH_CHECK((a.ldc * (f32 ? 4 : 2)) % 16 == 0 && (uintptr_t)a.C % 16 == 0,
+                "GEMM C operand must be 16-byte aligned with a 16-byte-multiple leading dimension");
   } else {
     TORCH_CHECK(beta == 0.0, "beta != 0 needs a C operand");
     a.C = nullptr; a.ldc = a.ldd;
@@ -69,6 +71,16 @@ void gemm(int64_t layout, const at::Tensor& A, const at::Tensor& B, const at::Te
   c10::cuda::CUDAGuard g(A.device());
   const int rc = trida::gemm_bf16((trida::GemmLayout)layout, f32, a, (int)tile, sm_count(), stream());
   TORCH_CHECK(rc == 0, "sm100 GEMM failed with code ", rc, " (M=", M, " N=", N, " K=", K, " layout=", layout, ")");
+}
+
+// Reads and clears the GEMM's device error word (host sync); 0 = no timed-out wait.
+int64_t gemm_error() {
+  int* w = trida::gemm_error_word();
+  if (!w) return 0;
+  int v = 0;
+  cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost);
+  if (v) cudaMemset(w, 0, sizeof(int));
+  return v;
 }
 
 std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, double eps, const at::Tensor& out) {
@@ -359,6 +371,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("lse"), py::arg("meta"), py::arg("list128"), py::arg("cnt128"), py::arg("rowmask"), py::arg("flags"),
         py::arg("scale"), py::arg("err"), py::arg("dbg") = py::none());
   m.def("bd_attn_tile_masks", &bd_attn_tile_masks);
+  m.def("gemm_error", &gemm_error);
   m.def("bd_attn_bwd_sm100", &bd_attn_bwd_sm100, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"),
         py::arg("lse"), py::arg("dout"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("meta"),
         py::arg("list128t"), py::arg("cnt128t"), py::arg("colmask"), py::arg("flags"), py::arg("scale"), py::arg("err"),

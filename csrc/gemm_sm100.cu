@@ -1,22 +1,320 @@
-// Layout/dtype dispatch for the sm_100a GEMM instantiations.
-#include "gemm_sm100.cuh"
-namespace trida {
-int gemm_tn_bf16(const GemmArgs&, int, int, cudaStream_t);
-int gemm_tn_f32(const GemmArgs&, int, int, cudaStream_t);
-int gemm_tt_bf16(const GemmArgs&, int, int, cudaStream_t);
-int gemm_nt_f32(const GemmArgs&, int, int, cudaStream_t);
-int gemm_nt_bf16(const GemmArgs&, int, int, cudaStream_t);
+// Persistent bf16 tensor-core GEMM for sm_100a written directly against tcgen05 / TMA.
+//
+//   D[M,N] = alpha * op(A) op(B) + beta * C        (fp32 accumulation in TMEM, D bf16 or fp32)
+//
+// One CTA per SM walks output tiles of 128 x 256 (grouped raster for L2 reuse).  Warp roles:
+//   warp 0      TMA producer: 64-deep K slices of A and B into a 4-stage shared-memory ring
+//               (plain per-CTA tensor loads, no cluster multicast);
+//   warp 1      MMA issuer (one thread): 4 x tcgen05.mma (K = 16) per K slice into one of two
+//               TMEM accumulators (128 lanes x 256 fp32 columns each), so the epilogue of tile i
+//               overlaps the mainloop of tile i + 1;
+//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, alpha / beta * C, convert, store.
+// Operand majorness follows the caller's row-major tensors: K-major operands are loaded with a
+// 64-element K box (UMMA K-major SWIZZLE_128B), MN-major operands with a 64-element MN box
+// (UMMA MN-major SWIZZLE_128B; LBO = one 64-wide MN atom).  Every mbarrier wait is bounded.
+#include <cudaTypedefs.h>
 
-int gemm_bf16(GemmLayout layout, bool d_fp32, const GemmArgs& a, int tile, int sm_count,
-              cudaStream_t stream) {
-  switch (layout) {
-    case GemmLayout::TN:
-      return d_fp32 ? gemm_tn_f32(a, tile, sm_count, stream) : gemm_tn_bf16(a, tile, sm_count, stream);
-    case GemmLayout::TT:
-      return d_fp32 ? -10 : gemm_tt_bf16(a, tile, sm_count, stream);
-    case GemmLayout::NT:
-      return d_fp32 ? gemm_nt_f32(a, tile, sm_count, stream) : gemm_nt_bf16(a, tile, sm_count, stream);
-  }
-  return -11;
+#include "common.cuh"
+#include "gemm_sm100.cuh"
+#include "sm100_common.cuh"
+
+namespace trida {
+namespace gemm100 {
+
+using namespace sm100;
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int NTHREADS = 192;
+constexpr int A_BYTES = BM * BK * 2;     // 16 KB
+constexpr int B_BYTES = BN * BK * 2;     // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 256 + 1024;
+constexpr int GROUP_M = 16;
+
+struct Params {
+  int M, N, K;
+  int a_kmajor, b_kmajor;
+  void* D;
+  int64_t ldd;
+  const void* C;
+  int64_t ldc;
+  float alpha, beta;
+  int d_fp32;
+  int* err;
+};
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::
+          "r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
+      : "memory");
 }
+
+__device__ __forceinline__ void tile_coords(int tile, int mt, int nt, int& m0, int& n0) {
+  const int per_group = GROUP_M * nt;
+  const int g = tile / per_group;
+  const int first_m = g * GROUP_M;
+  const int gm = (mt - first_m) < GROUP_M ? (mt - first_m) : GROUP_M;
+  const int in = tile % per_group;
+  m0 = (first_m + in % gm) * BM;
+  n0 = (in / gm) * BN;
+}
+
+// Load one K slice of an operand tile.  K-major: rows x 64 K  (box {64, rows_per_box}).
+// MN-major: 64 K rows x MN (box {64 MN, 64 K}); `width` MN elements in 64-wide atoms.
+__device__ __forceinline__ void load_operand(unsigned char* dst, const CUtensorMap* map, uint64_t* bar, int kmajor,
+                                             int mn0, int k0, int width) {
+  if (kmajor) {
+    // one box of {64 K, width rows} (width <= 256 rows per box)
+    tma_load_2d(dst, map, bar, k0, mn0);
+  } else {
+    for (int j = 0; j < width / 64; ++j) tma_load_2d(dst + j * (BK * 128), map, bar, mn0 + j * 64, k0);
+  }
+}
+
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kmajor, int kk) {
+  // kk = 16-element K step inside the 64-wide slice
+  if (kmajor) return desc_sw128(base + kk * 32, 16, 1024);
+  return desc_sw128(base + kk * 2048, BK * 128, 1024);
+}
+
+__global__ void __launch_bounds__(NTHREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = bars;                 // [STAGES]
+  uint64_t* empty = bars + STAGES;       // [STAGES]
+  uint64_t* acc_full = bars + 2 * STAGES;    // [2]
+  uint64_t* acc_empty = bars + 2 * STAGES + 2;  // [2]
+  uint64_t* drain = bars + 2 * STAGES + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 6);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = (p.M + BM - 1) / BM, nt = (p.N + BN - 1) / BN;
+  const int tiles = mt * nt;
+  const int kb = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tmA);
+      prefetch_tmap(&tmB);
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+        int m0, n0;
+        tile_coords(tile, mt, nt, m0, n0);
+        for (int k = 0; k < kb; ++k, ++it) {
+          const int s = it % STAGES;
+          if (it >= STAGES && !(ok = mbar_wait(&empty[s], ((it / STAGES) - 1) & 1, p.err, 101))) break;
+          unsigned char* st = smem + s * STAGE_BYTES;
+          mbar_expect_tx(&full[s], STAGE_BYTES);
+          load_operand(st, &tmA, &full[s], p.a_kmajor, m0, k * BK, BM);
+          load_operand(st + A_BYTES, &tmB, &full[s], p.b_kmajor, n0, k * BK, BN);
+        }
+      }
+      // the final (up to STAGES) loads must land before the CTA retires
+      for (int j = (it > STAGES ? it - STAGES : 0); ok && j < it; ++j)
+        mbar_wait(&full[j % STAGES], (j / STAGES) & 1, p.err, 102);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(BM, BN, p.a_kmajor ? 0 : 1, p.b_kmajor ? 0 : 1);
+      int it = 0, t = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++t) {
+        const int ab = t & 1;
+        if (t >= 2 && !(ok = mbar_wait(&acc_empty[ab], ((t >> 1) - 1) & 1, p.err, 103))) break;
+        tc_fence_after();
+        const uint32_t dcol = tmem + ab * BN;
+        for (int k = 0; k < kb; ++k, ++it) {
+          const int s = it % STAGES;
+          if (!(ok = mbar_wait(&full[s], (it / STAGES) & 1, p.err, 104))) break;
+          tc_fence_after();
+          const uint32_t a_base = smem_addr(smem + s * STAGE_BYTES);
+          const uint32_t b_base = a_base + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_f16(dcol, operand_desc(a_base, p.a_kmajor, kk), operand_desc(b_base, p.b_kmajor, kk), idesc,
+                     (k > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&acc_full[ab]);
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0, p.err, 105);
+    }
+  } else {
+    // epilogue warps 2..5: TMEM lane quarter = warp % 4
+    const int q = warp & 3;
+    const int r = q * 32 + lane;                       // accumulator row (TMEM lane)
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    int t = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+      const int ab = t & 1;
+      if (!mbar_wait(&acc_full[ab], (t >> 1) & 1, p.err, 106)) break;
+      tc_fence_after();
+      int m0, n0;
+      tile_coords(tile, mt, nt, m0, n0);
+      const int row = m0 + r;
+      const bool rok = row < p.M;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ab * BN + lane_off + c * 32, v);
+        tmem_wait_ld();
+        const int col0 = n0 + c * 32;
+        if (!rok || col0 >= p.N) continue;
+        float f[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) * p.alpha;
+        const bool full_cols = col0 + 32 <= p.N;
+        if (p.d_fp32) {
+          float* dst = reinterpret_cast<float*>(p.D) + (int64_t)row * p.ldd + col0;
+          const float* csrc = p.C ? reinterpret_cast<const float*>(p.C) + (int64_t)row * p.ldc + col0 : nullptr;
+          if (full_cols) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              float4 o = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
+              if (csrc && p.beta != 0.f) {
+                const float4 cv = *reinterpret_cast<const float4*>(csrc + j);
+                o.x += p.beta * cv.x; o.y += p.beta * cv.y; o.z += p.beta * cv.z; o.w += p.beta * cv.w;
+              }
+              *reinterpret_cast<float4*>(dst + j) = o;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < p.N) dst[j] = f[j] + ((csrc && p.beta != 0.f) ? p.beta * csrc[j] : 0.f);
+          }
+        } else {
+          bf16* dst = reinterpret_cast<bf16*>(p.D) + (int64_t)row * p.ldd + col0;
+          const bf16* csrc = p.C ? reinterpret_cast<const bf16*>(p.C) + (int64_t)row * p.ldc + col0 : nullptr;
+          if (full_cols) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              float o[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) o[e] = f[j + e];
+              if (csrc && p.beta != 0.f) {
+                float cv[8];
+                load8(csrc + j, cv);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) o[e] += p.beta * cv[e];
+              }
+              store8(dst + j, o);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < p.N)
+                dst[j] = __float2bfloat16(f[j] + ((csrc && p.beta != 0.f) ? p.beta * __bfloat162float(csrc[j]) : 0.f));
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[ab]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 2-D bf16 map over a row-major [rows, cols] matrix with leading dimension ld; box {64, box_rows}.
+static bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Device word the GEMM's bounded waits report into (allocated once per process).
+static int* err_word() {
+  static int* w = nullptr;
+  if (!w && cudaMalloc(&w, sizeof(int)) == cudaSuccess) cudaMemset(w, 0, sizeof(int));
+  return w;
+}
+
+}  // namespace gemm100
+
+int gemm_bf16(GemmLayout layout, bool d_fp32, const GemmArgs& a, int tile, int sm_count, cudaStream_t stream) {
+  using namespace gemm100;
+  (void)tile;
+  if (a.batch != 1) return -20;
+  Params p;
+  p.M = a.M; p.N = a.N; p.K = a.K;
+  p.D = a.D; p.ldd = a.ldd; p.C = a.C; p.ldc = a.ldc;
+  p.alpha = a.alpha; p.beta = a.beta; p.d_fp32 = d_fp32 ? 1 : 0;
+  p.err = err_word();
+  CUtensorMap mA, mB;
+  bool ok;
+  switch (layout) {
+    case GemmLayout::TN:   // A [M,K] K-major, B [N,K] K-major
+      p.a_kmajor = 1; p.b_kmajor = 1;
+      ok = make_map(&mA, a.A, a.M, a.K, a.lda, BM) && make_map(&mB, a.B, a.N, a.K, a.ldb, BN);
+      break;
+    case GemmLayout::TT:   // A [M,K] K-major, B [K,N] N-major
+      p.a_kmajor = 1; p.b_kmajor = 0;
+      ok = make_map(&mA, a.A, a.M, a.K, a.lda, BM) && make_map(&mB, a.B, a.K, a.N, a.ldb, BK);
+      break;
+    case GemmLayout::NT:   // A [K,M] M-major, B [K,N] N-major
+      p.a_kmajor = 0; p.b_kmajor = 0;
+      ok = make_map(&mA, a.A, a.K, a.M, a.lda, BK) && make_map(&mB, a.B, a.K, a.N, a.ldb, BK);
+      break;
+    default:
+      return -11;
+  }
+  if (!ok) return -12;
+  static bool init = false;
+  if (!init) {
+    cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    init = true;
+  }
+  const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
+  const int grid = tiles < sm_count ? tiles : sm_count;
+  gemm_kernel<<<grid, NTHREADS, SMEM_BYTES, stream>>>(mA, mB, p);
+  return cudaGetLastError() == cudaSuccess ? 0 : -13;
+}
+
+int* gemm_error_word() { return gemm100::err_word(); }
+
 }  // namespace trida

@@ -1,31 +1,15 @@
 """Builds the sm_100a CUDA extension in place: ``python setup.py build_ext --inplace``.
 
-Every kernel is compiled for ``-gencode arch=compute_100a,code=sm_100a`` only (B200).  The CUTLASS
-/ CuTe headers used by the tensor-core GEMM come from the CUTLASS source tree that ships inside the
-installed flashinfer package (headers only; no compiled library code is used).
+Every kernel is hand-written and compiled for ``-gencode arch=compute_100a,code=sm_100a`` only
+(B200); no third-party kernel library is compiled in.
 """
 import glob
-import importlib.util
 import os
 
 from setuptools import setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-
-
-def cutlass_include():
-    env = os.environ.get("CUTLASS_INCLUDE")
-    if env:
-        return env
-    spec = importlib.util.find_spec("flashinfer")
-    if spec is None or not spec.submodule_search_locations:
-        raise RuntimeError("CUTLASS headers not found: set CUTLASS_INCLUDE")
-    base = list(spec.submodule_search_locations)[0]
-    inc = os.path.join(base, "data", "cutlass", "include")
-    if not os.path.isdir(os.path.join(inc, "cute")):
-        raise RuntimeError(f"CUTLASS headers not found under {inc}: set CUTLASS_INCLUDE")
-    return inc
 
 
 NVCC_FLAGS = [
@@ -38,7 +22,7 @@ NVCC_FLAGS = [
 
 
 def extensions():
-    inc = [os.path.join(ROOT, "csrc"), cutlass_include()]
+    inc = [os.path.join(ROOT, "csrc")]
     srcs = sorted(glob.glob(os.path.join(ROOT, "csrc", "*.cu"))) + [os.path.join(ROOT, "csrc", "bindings.cpp")]
     return [CUDAExtension(
         name="trida_stack_b200._C",

@@ -42,6 +42,10 @@ def check_device_errors():
         if code:
             w.zero_()
             raise RuntimeError(f"device-side wait timed out on {key} (code {code})")
+    if _ERR_WORDS:
+        code = int(ext().gemm_error())
+        if code:
+            raise RuntimeError(f"GEMM mbarrier wait timed out (code {code})")
 
 
 def use_tcgen05_attention(head_dim, which="FWD"):
