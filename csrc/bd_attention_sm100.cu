@@ -9,7 +9,7 @@
 //   warp 4     MMA issuer (one thread): S_i = Q K_i^T into one of two TMEM S buffers, then
 //              O += P_{i-1} V_{i-1}; completion is signalled with tcgen05.commit on mbarriers.
 //   warp 5     TMA producer (one thread): Q once, K/V tiles into a 2-stage ring (plain per-CTA
-//              tensor loads, never cluster multicast).
+//              tensor loads, each CTA fetching its own tiles).
 // TMEM columns: S0 [0,128), S1 [128,256), O [256, 256+D).  The list of non-empty 128-key tiles
 // (and whether each is FULL or PARTIAL) comes from the same exact classification pass as the
 // other attention kernels.  Every mbarrier wait is bounded; a timeout records an error code in

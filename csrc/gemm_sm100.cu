@@ -4,7 +4,7 @@
 //
 // One CTA per SM walks output tiles of 128 x 256 (grouped raster for L2 reuse).  Warp roles:
 //   warp 0      TMA producer: 64-deep K slices of A and B into a 4-stage shared-memory ring
-//               (plain per-CTA tensor loads, no cluster multicast);
+//               (plain per-CTA tensor loads: every CTA fetches its own tiles);
 //   warp 1      MMA issuer (one thread): 4 x tcgen05.mma (K = 16) per K slice into one of two
 //               TMEM accumulators (128 lanes x 256 fp32 columns each), so the epilogue of tile i
 //               overlaps the mainloop of tile i + 1;

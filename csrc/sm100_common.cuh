@@ -1,5 +1,5 @@
 // Blackwell (sm_100a) building blocks written directly in PTX: mbarriers with bounded waits,
-// TMA tensor loads (no cluster multicast), tcgen05 MMA / TMEM alloc / ld / st / commit, and
+// TMA tensor loads (plain per-CTA loads), tcgen05 MMA / TMEM alloc / ld / st / commit, and
 // the UMMA shared-memory + instruction descriptors.
 //
 // Descriptor formats (bit positions as in CuTe's cute/arch/mma_sm100_desc.hpp):
