@@ -403,6 +403,7 @@ struct BwdParams {
   const int16_t* list; const int* cnt;
   int T, Hq, group, nt, flags;
   float scale, scale_log2;
+  int dcol0;                        // first head-dim column of dQ / dK / dV this launch produces
 };
 
 __device__ __forceinline__ void red_add_v2(float* addr, float a, float b) {
@@ -411,8 +412,10 @@ __device__ __forceinline__ void red_add_v2(float* addr, float a, float b) {
 
 // ---- backward: CTA = 64 keys (4 warps x 16) of one KV head, looping over the GQA group's query
 // heads and the non-empty 64-query tiles.  dK/dV accumulate in registers; dQ is reduced through
-// shared memory and added to an fp32 global accumulator.
-template <int D>
+// shared memory and added to an fp32 global accumulator.  A launch produces the DH head-dim columns
+// [dcol0, dcol0 + DH) of dQ / dK / dV (DH < D splits head_dim 256 over two launches that both
+// recompute S and dP, keeping the dK / dV accumulators within the register file).
+template <int D, int DH>
 __global__ void __launch_bounds__(128) bwd_kernel(const BwdParams p) {
   constexpr int BN = 64, BM = 64, NT = 128;
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -455,9 +458,10 @@ __global__ void __launch_bounds__(128) bwd_kernel(const BwdParams p) {
   if (total > 0) issue_q(0);
   cp_async_commit();
 
-  float dk[D / 8][4], dv[D / 8][4];
+  const int dc0 = p.dcol0;
+  float dk[DH / 8][4], dv[DH / 8][4];
 #pragma unroll
-  for (int i = 0; i < D / 8; ++i)
+  for (int i = 0; i < DH / 8; ++i)
 #pragma unroll
     for (int e = 0; e < 4; ++e) dk[i][e] = dv[i][e] = 0.f;
 
@@ -534,10 +538,10 @@ __global__ void __launch_bounds__(128) bwd_kernel(const BwdParams p) {
 #pragma unroll
       for (int kk = 0; kk < BM / 16; ++kk) {
 #pragma unroll
-        for (int dp = 0; dp < D / 16; ++dp) {
+        for (int dp = 0; dp < DH / 16; ++dp) {
           uint32_t bfr[4];
           const int row = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-          const int col = dp * 16 + (lane >> 4) * 8;
+          const int col = dc0 + dp * 16 + (lane >> 4) * 8;
           ldsm_x4_t(bfr, cdO + swz<D>(row, col));
           mma16816(dv[2 * dp], pf[kk], bfr[0], bfr[1]);
           mma16816(dv[2 * dp + 1], pf[kk], bfr[2], bfr[3]);
@@ -592,10 +596,10 @@ __global__ void __launch_bounds__(128) bwd_kernel(const BwdParams p) {
 #pragma unroll
     for (int kk = 0; kk < BM / 16; ++kk) {
 #pragma unroll
-      for (int dp = 0; dp < D / 16; ++dp) {
+      for (int dp = 0; dp < DH / 16; ++dp) {
         uint32_t bfr[4];
         const int row = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int col = dp * 16 + (lane >> 4) * 8;
+        const int col = dc0 + dp * 16 + (lane >> 4) * 8;
         ldsm_x4_t(bfr, cQ + swz<D>(row, col));
         mma16816(dk[2 * dp], dsf[kk], bfr[0], bfr[1]);
         mma16816(dk[2 * dp + 1], dsf[kk], bfr[2], bfr[3]);
@@ -614,18 +618,18 @@ __global__ void __launch_bounds__(128) bwd_kernel(const BwdParams p) {
       const int qlo = qt * BM + wr + (lane >> 2), qhi = qlo + 8;
       float* dqb = p.dq_acc + (int64_t)b * p.T * p.Hq * D + (int64_t)h * D;
 #pragma unroll
-      for (int dp = 0; dp < D / 16; ++dp) {
+      for (int dp = 0; dp < DH / 16; ++dp) {
         float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           uint32_t bfr[4];
           const int row = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-          const int col = dp * 16 + (lane >> 4) * 8;
+          const int col = dc0 + dp * 16 + (lane >> 4) * 8;
           ldsm_x4_t(bfr, sK + swz<D>(row, col));
           mma16816(acc0, af[kk], bfr[0], bfr[1]);
           mma16816(acc1, af[kk], bfr[2], bfr[3]);
         }
-        const int c0 = dp * 16 + (lane & 3) * 2;
+        const int c0 = dc0 + dp * 16 + (lane & 3) * 2;
         if (qlo < p.T) {
           red_add_v2(dqb + (int64_t)qlo * p.Hq * D + c0, acc0[0] * p.scale, acc0[1] * p.scale);
           red_add_v2(dqb + (int64_t)qlo * p.Hq * D + c0 + 8, acc1[0] * p.scale, acc1[1] * p.scale);
@@ -646,8 +650,8 @@ __global__ void __launch_bounds__(128) bwd_kernel(const BwdParams p) {
     bf16* gdk = p.dk + (int64_t)b * p.dk_b + (int64_t)row * p.dk_tok + (int64_t)hk * D;
     bf16* gdv = p.dv + (int64_t)b * p.dv_b + (int64_t)row * p.dv_tok + (int64_t)hk * D;
 #pragma unroll
-    for (int i = 0; i < D / 8; ++i) {
-      const int col = i * 8 + (lane & 3) * 2;
+    for (int i = 0; i < DH / 8; ++i) {
+      const int col = dc0 + i * 8 + (lane & 3) * 2;
       *reinterpret_cast<__nv_bfloat162*>(gdk + col) =
           __floats2bfloat162_rn(dk[i][2 * r] * p.scale, dk[i][2 * r + 1] * p.scale);
       *reinterpret_cast<__nv_bfloat162*>(gdv + col) = __floats2bfloat162_rn(dv[i][2 * r], dv[i][2 * r + 1]);
@@ -700,15 +704,19 @@ static void launch_fwd(const attn::FwdParams& p, int B, cudaStream_t s) {
 }
 
 template <int D>
-static void launch_bwd(const attn::BwdParams& p, int B, int Hkv, cudaStream_t s) {
+static void launch_bwd(attn::BwdParams p, int B, int Hkv, cudaStream_t s) {
+  constexpr int DH = D > 128 ? 128 : D;
   static bool init = false;
   const size_t sm = attn::bwd_smem<D>();
   if (!init) {
-    cudaFuncSetAttribute(attn::bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    cudaFuncSetAttribute(attn::bwd_kernel<D, DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     init = true;
   }
   dim3 grid(p.nt, Hkv, B);
-  attn::bwd_kernel<D><<<grid, 128, sm, s>>>(p);
+  for (int c0 = 0; c0 < D; c0 += DH) {
+    p.dcol0 = c0;
+    attn::bwd_kernel<D, DH><<<grid, 128, sm, s>>>(p);
+  }
 }
 
 int bd_attn_fwd(const AttnTensors& t, const int4* meta, const int16_t* fwd_list, const int* fwd_cnt, int flags,
@@ -766,7 +774,8 @@ int bd_attn_bwd(const AttnTensors& t, const bf16* dout, int64_t do_tok, int64_t 
   switch (t.D) {
     case 64: launch_bwd<64>(p, t.B, t.Hkv, s); break;
     case 128: launch_bwd<128>(p, t.B, t.Hkv, s); break;
-    default: return -1;   // head_dim 256 backward: dK/dV accumulators exceed this kernel's registers
+    case 256: launch_bwd<256>(p, t.B, t.Hkv, s); break;
+    default: return -1;
   }
   const int64_t n8 = rows * t.D / 8;
   int blocks = ceil_div(n8, 256);

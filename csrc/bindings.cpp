@@ -83,6 +83,148 @@ int64_t gemm_error() {
   return v;
 }
 
+// ---------------------------------------------------------------------------------------------
+// gated-delta-rule layers (gdn.cu).  Matrices are row-major 2-D views (row stride free, unit
+// column stride); `doc` is an optional uint8 [B, Lc] document-start mask of the clean stream.
+// ---------------------------------------------------------------------------------------------
+static trida::GdnParams gdn_params(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor& gb,
+                                   const at::Tensor& A_log, const at::Tensor& dt_bias,
+                                   const c10::optional<at::Tensor>& doc, int64_t B, int64_t T, int64_t Hk, int64_t Hv,
+                                   int64_t mode, int64_t L, int64_t V, int64_t bd, bool causal_clean, bool causal_noisy,
+                                   double scale) {
+  CHECK_CUDA(mixed); CHECK_BF16(mixed); CHECK_ROWMAJOR(mixed);
+  CHECK_BF16(ga); CHECK_BF16(gb); CHECK_ROWMAJOR(ga); CHECK_ROWMAJOR(gb);
+  TORCH_CHECK(ga.stride(0) == gb.stride(0), "gate views must share a row stride");
+  TORCH_CHECK(A_log.scalar_type() == at::kFloat && dt_bias.scalar_type() == at::kFloat, "A_log/dt_bias fp32");
+  TORCH_CHECK(mixed.size(0) == B * T && ga.size(0) == B * T && ga.size(1) == Hv, "GDN shape mismatch");
+  TORCH_CHECK(mixed.size(1) >= 2 * Hk * 128 + Hv * 128, "mixed too narrow");
+  TORCH_CHECK(mixed.stride(0) % 4 == 0, "mixed row stride must be a multiple of 4");
+  if (mode) TORCH_CHECK(T == (1 + V) * L, "two-stream rows must be (1 + V) * L tokens");
+  trida::GdnParams p{};
+  p.B = B; p.T = T; p.Hk = Hk; p.Hv = Hv; p.dk = 128; p.dvh = 128;
+  p.mode = mode; p.L = L; p.V = V; p.bd = bd; p.causal_clean = causal_clean; p.causal_noisy = causal_noisy;
+  if (doc.has_value() && doc->defined()) {
+    TORCH_CHECK(doc->scalar_type() == at::kByte && doc->is_contiguous(), "doc must be contiguous uint8");
+    TORCH_CHECK(doc->numel() == B * (mode ? L : T), "doc must be [B, Lc]");
+    p.doc = doc->data_ptr<uint8_t>();
+  }
+  p.mixed = cbf(mixed); p.ldm = mixed.stride(0);
+  p.ga = cbf(ga); p.gb = cbf(gb); p.ldg = ga.stride(0);
+  p.A_log = A_log.data_ptr<float>(); p.dt_bias = dt_bias.data_ptr<float>();
+  p.scale = (float)scale;
+  return p;
+}
+
+int64_t gdn_state_numel(int64_t B, int64_t T, int64_t Hv, int64_t mode, int64_t L, int64_t bd) {
+  trida::GdnParams p{};
+  p.B = B; p.T = T; p.Hv = Hv; p.mode = mode; p.L = L; p.bd = bd;
+  return trida::gdn_state_floats(p);
+}
+
+void gdn_fwd(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor& gb, const at::Tensor& A_log,
+             const at::Tensor& dt_bias, const c10::optional<at::Tensor>& doc, const at::Tensor& o, const at::Tensor& ckpt,
+             int64_t B, int64_t T, int64_t Hk, int64_t Hv, int64_t mode, int64_t L, int64_t V, int64_t bd,
+             bool causal_clean, bool causal_noisy, double scale) {
+  auto p = gdn_params(mixed, ga, gb, A_log, dt_bias, doc, B, T, Hk, Hv, mode, L, V, bd, causal_clean, causal_noisy, scale);
+  CHECK_BF16(o); TORCH_CHECK(o.is_contiguous() && o.numel() == B * T * Hv * 128, "o must be [B*T, Hv*128]");
+  TORCH_CHECK(ckpt.scalar_type() == at::kFloat && ckpt.numel() >= trida::gdn_state_floats(p), "ckpt too small");
+  p.ckpt = ckpt.data_ptr<float>(); p.o = mbf(o);
+  c10::cuda::CUDAGuard g(mixed.device());
+  const int rc = trida::gdn_fwd(p, stream());
+  TORCH_CHECK(rc == 0, "gdn_fwd failed with code ", rc);
+}
+
+void gdn_bwd(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor& gb, const at::Tensor& A_log,
+             const at::Tensor& dt_bias, const c10::optional<at::Tensor>& doc, const at::Tensor& ckpt,
+             const at::Tensor& d_o, const at::Tensor& dmixed, const at::Tensor& dga, const at::Tensor& dgb,
+             const at::Tensor& dA_log, const at::Tensor& ddt_bias, int64_t B, int64_t T, int64_t Hk, int64_t Hv,
+             int64_t mode, int64_t L, int64_t V, int64_t bd, bool causal_clean, bool causal_noisy, double scale) {
+  auto p = gdn_params(mixed, ga, gb, A_log, dt_bias, doc, B, T, Hk, Hv, mode, L, V, bd, causal_clean, causal_noisy, scale);
+  CHECK_BF16(d_o); TORCH_CHECK(d_o.is_contiguous() && d_o.numel() == B * T * Hv * 128, "d_o must be [B*T, Hv*128]");
+  CHECK_BF16(dmixed); CHECK_ROWMAJOR(dmixed); CHECK_BF16(dga); CHECK_BF16(dgb); CHECK_ROWMAJOR(dga);
+  TORCH_CHECK(dga.stride(0) == dgb.stride(0), "gate-gradient views must share a row stride");
+  TORCH_CHECK(dmixed.stride(0) % 4 == 0, "dmixed row stride must be a multiple of 4");
+  TORCH_CHECK(dA_log.scalar_type() == at::kFloat && ddt_bias.scalar_type() == at::kFloat, "fp32 gate grads");
+  const int64_t ns = trida::gdn_state_floats(p);
+  TORCH_CHECK(ckpt.numel() >= ns, "ckpt too small");
+  auto f32 = mixed.options().dtype(at::kFloat);
+  at::Tensor dqk = at::empty({B * T, Hv, 2, 128}, f32);
+  at::Tensor dgbuf = at::empty({B * T, Hv, 2}, f32);
+  at::Tensor dinit = mode ? at::empty({ns}, f32) : at::Tensor();
+  p.ckpt = ckpt.data_ptr<float>();
+  p.d_o = cbf(d_o);
+  p.dqk = dqk.data_ptr<float>(); p.dgb = dgbuf.data_ptr<float>();
+  p.dv = mbf(dmixed) + 2 * Hk * 128; p.lddv = dmixed.stride(0);
+  p.dinit = mode ? dinit.data_ptr<float>() : nullptr;
+  c10::cuda::CUDAGuard g(mixed.device());
+  const int rc = trida::gdn_bwd(p, mbf(dmixed), dmixed.stride(0), mbf(dga), mbf(dgb), dga.stride(0),
+                                dA_log.data_ptr<float>(), ddt_bias.data_ptr<float>(), stream());
+  TORCH_CHECK(rc == 0, "gdn_bwd failed with code ", rc);
+}
+
+static trida::ConvParams conv_params(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& doc,
+                                     int64_t B, int64_t T, int64_t mode, int64_t L, int64_t V, int64_t bd) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_ROWMAJOR(x); CHECK_BF16(w);
+  TORCH_CHECK(w.is_contiguous() && w.dim() == 2 && w.size(0) == x.size(1), "conv weight must be [C, K]");
+  TORCH_CHECK(x.size(0) == B * T && x.size(1) % 8 == 0 && x.stride(0) % 8 == 0, "conv input shape / stride");
+  trida::ConvParams p{};
+  p.B = B; p.T = T; p.C = x.size(1); p.K = w.size(1);
+  p.mode = mode; p.L = L; p.V = V; p.bd = bd;
+  if (doc.has_value() && doc->defined()) {
+    TORCH_CHECK(doc->scalar_type() == at::kByte && doc->is_contiguous(), "doc must be contiguous uint8");
+    p.doc = doc->data_ptr<uint8_t>();
+  }
+  p.x = cbf(x); p.ldx = x.stride(0); p.w = cbf(w);
+  return p;
+}
+
+void gdn_conv_fwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& y, const c10::optional<at::Tensor>& doc,
+                  int64_t B, int64_t T, int64_t mode, int64_t L, int64_t V, int64_t bd) {
+  auto p = conv_params(x, w, doc, B, T, mode, L, V, bd);
+  CHECK_BF16(y); CHECK_ROWMAJOR(y);
+  TORCH_CHECK(y.size(0) == x.size(0) && y.size(1) == x.size(1) && y.stride(0) % 8 == 0, "conv output shape");
+  p.y = mbf(y); p.ldy = y.stride(0);
+  c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(trida::gdn_conv_fwd(p, stream()) == 0, "gdn_conv_fwd failed");
+}
+
+void gdn_conv_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w, const at::Tensor& dx,
+                  const at::Tensor& dw, const c10::optional<at::Tensor>& doc, int64_t B, int64_t T, int64_t mode,
+                  int64_t L, int64_t V, int64_t bd) {
+  auto p = conv_params(x, w, doc, B, T, mode, L, V, bd);
+  CHECK_BF16(dy); CHECK_ROWMAJOR(dy); CHECK_BF16(dx); CHECK_ROWMAJOR(dx);
+  TORCH_CHECK(dy.stride(0) % 8 == 0 && dx.stride(0) % 8 == 0, "conv gradient strides");
+  TORCH_CHECK(dw.scalar_type() == at::kFloat && dw.numel() == w.numel(), "dw must be fp32 like w");
+  at::Tensor dpre = at::empty({x.size(0), x.size(1)}, x.options().dtype(at::kFloat));
+  c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(trida::gdn_conv_bwd(p, cbf(dy), dy.stride(0), dpre.data_ptr<float>(), mbf(dx), dx.stride(0),
+                                  dw.data_ptr<float>(), stream()) == 0, "gdn_conv_bwd failed");
+}
+
+void gdn_gnorm_fwd(const at::Tensor& o, const at::Tensor& z, const at::Tensor& w, const at::Tensor& y, int64_t H,
+                   double eps) {
+  CHECK_BF16(o); CHECK_BF16(z); CHECK_BF16(w); CHECK_BF16(y); CHECK_ROWMAJOR(z);
+  TORCH_CHECK(o.is_contiguous() && y.is_contiguous() && w.numel() == 128, "gated norm shapes");
+  const int64_t rows = z.size(0);
+  TORCH_CHECK(o.numel() == rows * H * 128 && z.size(1) == H * 128, "gated norm shapes");
+  c10::cuda::CUDAGuard g(o.device());
+  TORCH_CHECK(trida::gdn_gnorm_fwd(cbf(o), cbf(z), z.stride(0), cbf(w), mbf(y), rows, H, (float)eps, stream()) == 0,
+              "gdn_gnorm_fwd failed");
+}
+
+void gdn_gnorm_bwd(const at::Tensor& dy, const at::Tensor& o, const at::Tensor& z, const at::Tensor& w,
+                   const at::Tensor& d_o, const at::Tensor& dz, const at::Tensor& dw, int64_t H, double eps) {
+  CHECK_BF16(dy); CHECK_BF16(o); CHECK_BF16(z); CHECK_BF16(d_o); CHECK_BF16(dz); CHECK_ROWMAJOR(z);
+  CHECK_ROWMAJOR(dz);
+  TORCH_CHECK(dy.is_contiguous() && o.is_contiguous() && d_o.is_contiguous(), "gated norm grads contiguous");
+  TORCH_CHECK(dw.scalar_type() == at::kFloat && dw.numel() == 128, "dw fp32 [128]");
+  const int64_t rows = z.size(0);
+  c10::cuda::CUDAGuard g(o.device());
+  TORCH_CHECK(trida::gdn_gnorm_bwd(cbf(dy), cbf(o), cbf(z), z.stride(0), cbf(w), mbf(d_o), mbf(dz), dz.stride(0),
+                                   dw.data_ptr<float>(), rows, H, (float)eps, sm_count(), stream()) == 0,
+              "gdn_gnorm_bwd failed");
+}
+
 std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, double eps, const at::Tensor& out) {
   CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(w); CHECK_ROWMAJOR(x); CHECK_ROWMAJOR(out);
   const int M = x.size(0), D = x.size(1);
@@ -108,7 +250,7 @@ void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
 at::Tensor qk_norm_rope_fwd(const at::Tensor& qkv, const at::Tensor& qw, const at::Tensor& kw,
                             const at::Tensor& cos_t, const at::Tensor& sin_t, const at::Tensor& pos,
                             const at::Tensor& q, const at::Tensor& k, int64_t Hq, int64_t Hkv, int64_t d,
-                            int64_t rd, double eps) {
+                            int64_t rd, double eps, int64_t qstride) {
   CHECK_BF16(qkv); CHECK_ROWMAJOR(qkv); CHECK_F32(cos_t); CHECK_F32(sin_t);
   TORCH_CHECK(pos.scalar_type() == at::kInt && pos.is_contiguous(), "pos must be contiguous int32");
   TORCH_CHECK(q.is_contiguous() && k.is_contiguous(), "q/k outputs must be contiguous");
@@ -116,14 +258,15 @@ at::Tensor qk_norm_rope_fwd(const at::Tensor& qkv, const at::Tensor& qw, const a
   auto rstd = at::empty({M, Hq + Hkv}, qkv.options().dtype(at::kFloat));
   trida::qk_norm_rope_fwd(cbf(qkv), qkv.stride(0), cbf(qw), cbf(kw), cos_t.data_ptr<float>(),
                           sin_t.data_ptr<float>(), pos.data_ptr<int>(), mbf(q), mbf(k), rstd.data_ptr<float>(), M,
-                          Hq, Hkv, d, rd, (float)eps, stream());
+                          Hq, Hkv, d, rd, (float)eps, qstride ? qstride : d, stream());
   return rstd;
 }
 
 void qk_norm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Tensor& qkv, const at::Tensor& qw,
                       const at::Tensor& kw, const at::Tensor& cos_t, const at::Tensor& sin_t, const at::Tensor& pos,
                       const at::Tensor& rstd, const at::Tensor& dqkv, const c10::optional<at::Tensor>& dqw,
-                      const c10::optional<at::Tensor>& dkw, int64_t Hq, int64_t Hkv, int64_t d, int64_t rd) {
+                      const c10::optional<at::Tensor>& dkw, int64_t Hq, int64_t Hkv, int64_t d, int64_t rd,
+                      int64_t qstride) {
   CHECK_ROWMAJOR(qkv); CHECK_ROWMAJOR(dqkv);
   TORCH_CHECK(dq.is_contiguous() && dk.is_contiguous(), "dq/dk must be contiguous");
   const int M = qkv.size(0);
@@ -131,7 +274,22 @@ void qk_norm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Tens
   float* pk = (dkw.has_value() && dkw->defined()) ? dkw->data_ptr<float>() : nullptr;
   trida::qk_norm_rope_bwd(cbf(dq), cbf(dk), cbf(qkv), qkv.stride(0), cbf(qw), cbf(kw), cos_t.data_ptr<float>(),
                           sin_t.data_ptr<float>(), pos.data_ptr<int>(), rstd.data_ptr<float>(), mbf(dqkv),
-                          dqkv.stride(0), pq, pk, M, Hq, Hkv, d, rd, sm_count(), stream());
+                          dqkv.stride(0), pq, pk, M, Hq, Hkv, d, rd, qstride ? qstride : d, sm_count(), stream());
+}
+
+// y = o * sigmoid(gate) with the gate heads interleaved in qkv (head h: [q (d) | gate (d)]).
+void attn_gate_fwd(const at::Tensor& o, const at::Tensor& qkv, const at::Tensor& y, int64_t Hq, int64_t d) {
+  CHECK_BF16(o); CHECK_BF16(qkv); CHECK_ROWMAJOR(qkv);
+  TORCH_CHECK(o.is_contiguous() && y.is_contiguous() && d % 8 == 0 && qkv.stride(0) % 8 == 0, "gate shapes");
+  trida::attn_gate_fwd(cbf(o), cbf(qkv), qkv.stride(0), mbf(y), qkv.size(0), Hq, d, sm_count(), stream());
+}
+
+void attn_gate_bwd(const at::Tensor& dy, const at::Tensor& o, const at::Tensor& qkv, const at::Tensor& d_o,
+                   const at::Tensor& dqkv, int64_t Hq, int64_t d) {
+  CHECK_ROWMAJOR(qkv); CHECK_ROWMAJOR(dqkv);
+  TORCH_CHECK(dy.is_contiguous() && o.is_contiguous() && d_o.is_contiguous() && dqkv.stride(0) % 8 == 0, "gate shapes");
+  trida::attn_gate_bwd(cbf(dy), cbf(o), cbf(qkv), qkv.stride(0), mbf(d_o), mbf(dqkv), dqkv.stride(0), qkv.size(0), Hq,
+                       d, sm_count(), stream());
 }
 
 void swiglu_fwd(const at::Tensor& gu, const at::Tensor& out) {
@@ -357,8 +515,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
-  m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);
-  m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd);
+  m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd, py::arg("qkv"), py::arg("qw"), py::arg("kw"), py::arg("cos_t"),
+        py::arg("sin_t"), py::arg("pos"), py::arg("q"), py::arg("k"), py::arg("Hq"), py::arg("Hkv"), py::arg("d"),
+        py::arg("rd"), py::arg("eps"), py::arg("qstride") = 0);
+  m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd, py::arg("dq"), py::arg("dk"), py::arg("qkv"), py::arg("qw"),
+        py::arg("kw"), py::arg("cos_t"), py::arg("sin_t"), py::arg("pos"), py::arg("rstd"), py::arg("dqkv"),
+        py::arg("dqw"), py::arg("dkw"), py::arg("Hq"), py::arg("Hkv"), py::arg("d"), py::arg("rd"),
+        py::arg("qstride") = 0);
+  m.def("attn_gate_fwd", &attn_gate_fwd);
+  m.def("attn_gate_bwd", &attn_gate_bwd);
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("embed_fwd", &embed_fwd);
@@ -372,6 +537,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale"), py::arg("err"), py::arg("dbg") = py::none());
   m.def("bd_attn_tile_masks", &bd_attn_tile_masks);
   m.def("gemm_error", &gemm_error);
+  m.def("gdn_state_numel", &gdn_state_numel);
+  m.def("gdn_fwd", &gdn_fwd);
+  m.def("gdn_bwd", &gdn_bwd);
+  m.def("gdn_conv_fwd", &gdn_conv_fwd);
+  m.def("gdn_conv_bwd", &gdn_conv_bwd);
+  m.def("gdn_gnorm_fwd", &gdn_gnorm_fwd);
+  m.def("gdn_gnorm_bwd", &gdn_gnorm_bwd);
   m.def("bd_attn_bwd_sm100", &bd_attn_bwd_sm100, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"),
         py::arg("lse"), py::arg("dout"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("meta"),
         py::arg("list128t"), py::arg("cnt128t"), py::arg("colmask"), py::arg("flags"), py::arg("scale"), py::arg("err"),

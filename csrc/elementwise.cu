@@ -125,14 +125,15 @@ __global__ void qk_norm_rope_fwd_kernel(const bf16* __restrict__ qkv, int64_t ld
                                         const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                         const int* __restrict__ pos, bf16* __restrict__ q,
                                         bf16* __restrict__ k, float* __restrict__ rstd, int M, int Hq,
-                                        int Hkv, int d, int rd, float eps) {
+                                        int Hkv, int d, int rd, float eps, int qstride) {
   const int H = Hq + Hkv;
   const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (gw >= (int64_t)M * H) return;
   const int tok = (int)(gw / H), h = (int)(gw % H);
   const bool is_q = h < Hq;
-  const bf16* src = qkv + (int64_t)tok * ldqkv + (int64_t)h * d;
+  const int64_t hcol = is_q ? (int64_t)h * qstride : (int64_t)Hq * qstride + (int64_t)(h - Hq) * d;
+  const bf16* src = qkv + (int64_t)tok * ldqkv + hcol;
   const bf16* w = is_q ? qw : kw;
   bf16* dst = is_q ? (q + ((int64_t)tok * Hq + h) * d) : (k + ((int64_t)tok * Hkv + (h - Hq)) * d);
   float ss = 0.f;
@@ -166,7 +167,8 @@ __global__ void qk_norm_rope_bwd_kernel(const bf16* __restrict__ dq, const bf16*
                                         const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                         const int* __restrict__ pos, const float* __restrict__ rstd,
                                         bf16* __restrict__ dqkv, int64_t lddqkv, float* __restrict__ dqw,
-                                        float* __restrict__ dkw, int M, int Hq, int Hkv, int d, int rd) {
+                                        float* __restrict__ dkw, int M, int Hq, int Hkv, int d, int rd,
+                                        int qstride) {
   extern __shared__ float sdw_all[];  // [warps][2*d]: q weight grads then k weight grads
   const int nwarps = blockDim.x >> 5;
   float* sdw = sdw_all + (threadIdx.x >> 5) * 2 * d;
@@ -180,10 +182,11 @@ __global__ void qk_norm_rope_bwd_kernel(const bf16* __restrict__ dq, const bf16*
        gw += (int64_t)gridDim.x * (blockDim.x >> 5)) {
     const int tok = (int)(gw / H), h = (int)(gw % H);
     const bool is_q = h < Hq;
-    const bf16* src = qkv + (int64_t)tok * ldqkv + (int64_t)h * d;
+    const int64_t hcol = is_q ? (int64_t)h * qstride : (int64_t)Hq * qstride + (int64_t)(h - Hq) * d;
+    const bf16* src = qkv + (int64_t)tok * ldqkv + hcol;
     const bf16* w = is_q ? qw : kw;
     const bf16* g = is_q ? (dq + ((int64_t)tok * Hq + h) * d) : (dk + ((int64_t)tok * Hkv + (h - Hq)) * d);
-    bf16* out = dqkv + (int64_t)tok * lddqkv + (int64_t)h * d;
+    bf16* out = dqkv + (int64_t)tok * lddqkv + hcol;
     float* sw = sdw + (is_q ? 0 : d);
     const float r = rstd[gw];
     const int p = pos[tok];
@@ -229,23 +232,82 @@ __global__ void qk_norm_rope_bwd_kernel(const bf16* __restrict__ dq, const bf16*
 
 void qk_norm_rope_fwd(const bf16* qkv, int64_t ldqkv, const bf16* qw, const bf16* kw, const float* cos_t,
                       const float* sin_t, const int* pos, bf16* q, bf16* k, float* rstd, int M, int Hq,
-                      int Hkv, int d, int rd, float eps, cudaStream_t s) {
+                      int Hkv, int d, int rd, float eps, int qstride, cudaStream_t s) {
   const int warps = 8;
   const int64_t total = (int64_t)M * (Hq + Hkv);
   qk_norm_rope_fwd_kernel<<<ceil_div(total, warps), warps * 32, 0, s>>>(qkv, ldqkv, qw, kw, cos_t, sin_t, pos,
-                                                                       q, k, rstd, M, Hq, Hkv, d, rd, eps);
+                                                                       q, k, rstd, M, Hq, Hkv, d, rd, eps, qstride);
 }
 
 void qk_norm_rope_bwd(const bf16* dq, const bf16* dk, const bf16* qkv, int64_t ldqkv, const bf16* qw,
                       const bf16* kw, const float* cos_t, const float* sin_t, const int* pos,
                       const float* rstd, bf16* dqkv, int64_t lddqkv, float* dqw, float* dkw, int M, int Hq,
-                      int Hkv, int d, int rd, int sm_count, cudaStream_t s) {
+                      int Hkv, int d, int rd, int qstride, int sm_count, cudaStream_t s) {
   const int warps = 8;
   const int64_t total = (int64_t)M * (Hq + Hkv);
   int blocks = ceil_div(total, warps * 8);
   blocks = blocks > sm_count * 8 ? sm_count * 8 : blocks;
   qk_norm_rope_bwd_kernel<<<blocks, warps * 32, warps * 2 * d * sizeof(float), s>>>(
-      dq, dk, qkv, ldqkv, qw, kw, cos_t, sin_t, pos, rstd, dqkv, lddqkv, dqw, dkw, M, Hq, Hkv, d, rd);
+      dq, dk, qkv, ldqkv, qw, kw, cos_t, sin_t, pos, rstd, dqkv, lddqkv, dqw, dkw, M, Hq, Hkv, d, rd, qstride);
+}
+
+// ------------------------------------------------------------------------------------------
+// Sigmoid output gate of the gated attention (Qwen3.5 full-attention layers):
+//   y[t, h, :] = o[t, h, :] * sigmoid(gate[t, h, :]),  gate = qkv[t, h*2d + d : h*2d + 2d]
+// ------------------------------------------------------------------------------------------
+__global__ void attn_gate_fwd_kernel(const bf16* __restrict__ o, const bf16* __restrict__ qkv, int64_t ldqkv,
+                                     bf16* __restrict__ y, int M, int Hq, int d) {
+  const int vpr = Hq * d / 8;
+  const int64_t total = (int64_t)M * vpr;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int row = (int)(i / vpr), c = (int)(i % vpr) * 8;
+    const int h = c / d, e = c % d;
+    float ov[8], gv[8], out[8];
+    load8(o + (int64_t)row * Hq * d + c, ov);
+    load8(qkv + (int64_t)row * ldqkv + (int64_t)h * 2 * d + d + e, gv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[j] = ov[j] / (1.f + __expf(-gv[j]));
+    store8(y + (int64_t)row * Hq * d + c, out);
+  }
+}
+
+__global__ void attn_gate_bwd_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ o,
+                                     const bf16* __restrict__ qkv, int64_t ldqkv, bf16* __restrict__ d_o,
+                                     bf16* __restrict__ dqkv, int64_t lddqkv, int M, int Hq, int d) {
+  const int vpr = Hq * d / 8;
+  const int64_t total = (int64_t)M * vpr;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int row = (int)(i / vpr), c = (int)(i % vpr) * 8;
+    const int h = c / d, e = c % d;
+    float dv[8], ov[8], gv[8], dov[8], dgv[8];
+    load8(dy + (int64_t)row * Hq * d + c, dv);
+    load8(o + (int64_t)row * Hq * d + c, ov);
+    load8(qkv + (int64_t)row * ldqkv + (int64_t)h * 2 * d + d + e, gv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float sg = 1.f / (1.f + __expf(-gv[j]));
+      dov[j] = dv[j] * sg;
+      dgv[j] = dv[j] * ov[j] * sg * (1.f - sg);
+    }
+    store8(d_o + (int64_t)row * Hq * d + c, dov);
+    store8(dqkv + (int64_t)row * lddqkv + (int64_t)h * 2 * d + d + e, dgv);
+  }
+}
+
+void attn_gate_fwd(const bf16* o, const bf16* qkv, int64_t ldqkv, bf16* y, int M, int Hq, int d, int sm_count,
+                   cudaStream_t s) {
+  const int64_t total = (int64_t)M * Hq * d / 8;
+  int blocks = ceil_div(total, 256);
+  blocks = blocks > sm_count * 16 ? sm_count * 16 : blocks;
+  attn_gate_fwd_kernel<<<blocks, 256, 0, s>>>(o, qkv, ldqkv, y, M, Hq, d);
+}
+
+void attn_gate_bwd(const bf16* dy, const bf16* o, const bf16* qkv, int64_t ldqkv, bf16* d_o, bf16* dqkv,
+                   int64_t lddqkv, int M, int Hq, int d, int sm_count, cudaStream_t s) {
+  const int64_t total = (int64_t)M * Hq * d / 8;
+  int blocks = ceil_div(total, 256);
+  blocks = blocks > sm_count * 16 ? sm_count * 16 : blocks;
+  attn_gate_bwd_kernel<<<blocks, 256, 0, s>>>(dy, o, qkv, ldqkv, d_o, dqkv, lddqkv, M, Hq, d);
 }
 
 // ------------------------------------------------------------------------------------------

@@ -1,0 +1,930 @@
+// Gated-delta-rule (GDN) linear attention for the hybrid decoder (sm_100a).
+//
+// Behaviour follows the reference's hybrid layers: train/models/hybrid.py:215-324 (two-stream
+// recurrence: a causal pass over the clean stream, then every noisy block of every view restarted
+// from the clean state at the end of the previous block and read out at its own block end),
+// :137-212 (causal gated-delta rule with per-document resets), :327-451 (short depthwise conv +
+// SiLU, two-stream variant whose in-block taps read the noisy stream).
+//
+// Recurrence per value head (state S [dk=128, dv=128] in fp32; q, k L2-normalised, q * dk^-0.5):
+//     S' = exp(g) S ;  u = beta (v - S'^T k) ;  S = S' + k u^T ;  o = S^T q
+// Every value column of S evolves on its own, so a head is split over 8 CTAs of 16 columns and a
+// CTA keeps its 128 x 16 slice in registers: thread (column c, row part r) owns rows [16r, 16r+16)
+// of column c; the dot products over dk are 3-step shuffles inside each group of 8 lanes.
+//
+// Forward: fwd_clean walks the clean stream (or the whole causal row) in chunks, storing the state
+// at every chunk start (block starts in the two-stream layout) as the backward's checkpoints and
+// the noisy blocks' initial states; fwd_noisy runs every (block, view) of the noisy streams in
+// parallel from those states.
+// Backward: per chunk, recompute forward from the checkpoint with sub-checkpoints every SUB tokens,
+// then replay each sub-chunk keeping S' in registers and sweep it in reverse.  Gradients w.r.t. q
+// and k are sums over the 128 value columns: reduced across the 4 columns of a warp by shuffles,
+// across the CTA's 4 warps in shared memory and across the head's 8 CTAs (one thread-block
+// cluster) through distributed shared memory, so every dq / dk element is written exactly once.
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+#include "ops.h"
+
+namespace cgx = cooperative_groups;
+
+namespace trida {
+namespace gdn {
+
+constexpr int DK = 128, DV = 128;
+constexpr int CG = 16;          // value columns per CTA
+constexpr int NCG = DV / CG;    // CTAs per head (cluster size in the backward)
+constexpr int RP = 8;           // threads per column
+constexpr int RPT = DK / RP;    // rows per thread
+constexpr int NT = CG * RP;     // 128 threads
+constexpr int SUB = 4;          // backward replay sub-chunk
+constexpr int RED = 2 * DK + 4; // per-token reduction row: dq | dk | dbeta | dg (16-byte rows)
+constexpr int MAXCH = 64;
+
+struct Args {
+  int B, T, Hk, Hv;
+  int mode;                 // 0 causal, 1 two-stream
+  int L, V, bd;             // two-stream geometry
+  int causal_clean, causal_noisy;
+  int ch, nch;              // clean-stream chunk length and count
+  const uint8_t* doc;       // [B, Lc] document-start flags of the clean stream (may be null)
+  const bf16* mixed;        // [B*T, ldm]: q | k | v (conv output)
+  int64_t ldm;
+  const bf16* ga;           // gate pre-activation a [B*T, Hv] (row stride ldg)
+  const bf16* gb;           // gate pre-activation b
+  int64_t ldg;
+  const float* A_log;
+  const float* dt_bias;
+  float scale;
+  float* ckpt;              // [B, Hv, nch, NCG, RPT, NT]
+  bf16* o;                  // [B*T, Hv*DV]
+  const bf16* d_o;          // [B*T, Hv*DV]
+  float* dqk;               // [B*T, Hv, 2, DK]
+  float* dgb;               // [B*T, Hv, 2]  (dg, dbeta)
+  bf16* dv;                 // v-gradient rows [B*T, lddv] (head columns at hv*DV)
+  int64_t lddv;
+  float* dinit;             // [B, Hv, nch, NCG, RPT, NT]
+};
+
+struct Stage {
+  float* q;     // [ch][DK]
+  float* k;     // [ch][DK]
+  float* v;     // [ch][CG]
+  float* dO;    // [ch][CG]
+  float* al;    // [ch]
+  float* be;    // [ch]
+  float* ob;    // [ch][CG]  (forward output staging / backward dv staging)
+  int* rs;      // [ch]
+  float* sck;   // [ch/SUB][RPT][NT] (backward sub-checkpoints)
+  float* red;   // [2][SUB][RED]     (backward reduction rows)
+};
+
+__host__ __device__ inline size_t stage_floats(int ch, bool bwd) {
+  size_t n = (size_t)ch * (2 * DK + 3 * CG + 3);
+  if (bwd) n += (size_t)((ch + SUB - 1) / SUB) * RPT * NT + 2 * SUB * RED;
+  return n;
+}
+
+__device__ inline Stage carve(float* sm, int ch, bool bwd) {
+  Stage s;
+  s.q = sm; sm += ch * DK;
+  s.k = sm; sm += ch * DK;
+  s.v = sm; sm += ch * CG;
+  s.dO = sm; sm += ch * CG;
+  s.ob = sm; sm += ch * CG;
+  s.al = sm; sm += ch;
+  s.be = sm; sm += ch;
+  s.rs = reinterpret_cast<int*>(sm); sm += ch;
+  if (bwd) {
+    s.sck = sm; sm += ((ch + SUB - 1) / SUB) * RPT * NT;
+    s.red = sm;
+  }
+  return s;
+}
+
+__device__ __forceinline__ float rsum8(float x) {
+  x += __shfl_xor_sync(0xffffffffu, x, 1);
+  x += __shfl_xor_sync(0xffffffffu, x, 2);
+  x += __shfl_xor_sync(0xffffffffu, x, 4);
+  return x;
+}
+
+__device__ __forceinline__ float softplus_f(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+
+// Stage n tokens (row-relative indices tok0 .. tok0+n-1 of row b) for value head hv / columns cg:
+// L2-normalised q (times scale) and k of the head's key head, the CTA's v (and dO) columns, the
+// decay alpha = exp(g), beta, and reset flags (clean positions pos0.. when pos0 >= 0).
+__device__ void stage_tokens(const Args& a, const Stage& s, int b, int hv, int cg, int tok0, int n, int pos0,
+                             bool bwd) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hk = hv / (a.Hv / a.Hk);
+  const int Lc = a.mode ? a.L : a.T;
+  for (int j = warp; j < n; j += NT / 32) {
+    const int64_t row = (int64_t)b * a.T + tok0 + j;
+    const bf16* src = a.mixed + row * a.ldm;
+    float qv[4], kv[4];
+    const uint2 qr = *reinterpret_cast<const uint2*>(src + hk * DK + lane * 4);
+    const uint2 kr = *reinterpret_cast<const uint2*>(src + a.Hk * DK + hk * DK + lane * 4);
+    const bf16* qp = reinterpret_cast<const bf16*>(&qr);
+    const bf16* kp = reinterpret_cast<const bf16*>(&kr);
+    float sq = 0.f, sk = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      qv[e] = __bfloat162float(qp[e]);
+      kv[e] = __bfloat162float(kp[e]);
+      sq += qv[e] * qv[e];
+      sk += kv[e] * kv[e];
+    }
+    sq = warp_sum(sq);
+    sk = warp_sum(sk);
+    const float rq = rsqrtf(sq + 1e-6f) * a.scale, rk = rsqrtf(sk + 1e-6f);
+    *reinterpret_cast<float4*>(s.q + j * DK + lane * 4) = make_float4(qv[0] * rq, qv[1] * rq, qv[2] * rq, qv[3] * rq);
+    *reinterpret_cast<float4*>(s.k + j * DK + lane * 4) = make_float4(kv[0] * rk, kv[1] * rk, kv[2] * rk, kv[3] * rk);
+    if (lane < CG) {
+      s.v[j * CG + lane] = __bfloat162float(src[2 * a.Hk * DK + hv * DV + cg * CG + lane]);
+    } else if (bwd) {
+      s.dO[j * CG + lane - CG] = __bfloat162float(a.d_o[row * (int64_t)(a.Hv * DV) + hv * DV + cg * CG + lane - CG]);
+    }
+    if (lane == 0) {
+      const float av = __bfloat162float(a.ga[row * a.ldg + hv]) + a.dt_bias[hv];
+      const float bv = __bfloat162float(a.gb[row * a.ldg + hv]);
+      const float g = -expf(a.A_log[hv]) * softplus_f(av);
+      s.al[j] = expf(g);
+      s.be[j] = 1.f / (1.f + expf(-bv));
+      s.rs[j] = (pos0 >= 0 && a.doc != nullptr) ? (int)a.doc[(int64_t)b * Lc + pos0 + j] : 0;
+    }
+  }
+}
+
+__device__ __forceinline__ void load16(const float* p, float (&x)[RPT]) {
+#pragma unroll
+  for (int i = 0; i < RPT; i += 4) {
+    const float4 t = *reinterpret_cast<const float4*>(p + i);
+    x[i] = t.x; x[i + 1] = t.y; x[i + 2] = t.z; x[i + 3] = t.w;
+  }
+}
+
+// One recurrence step on the thread's slice; returns u (column scalar) and v - p.
+__device__ __forceinline__ void fwd_step(float (&S)[RPT], const float* kp, float al, float be, float vc, float& u,
+                                         float& vmp) {
+  float k[RPT];
+  load16(kp, k);
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < RPT; i += 2) {
+    a0 = fmaf(S[i], k[i], a0);
+    a1 = fmaf(S[i + 1], k[i + 1], a1);
+  }
+  const float p = al * rsum8(a0 + a1);
+  vmp = vc - p;
+  u = be * vmp;
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) S[i] = fmaf(al, S[i], k[i] * u);
+}
+
+__device__ __forceinline__ float readout(const float (&S)[RPT], const float* qp) {
+  float q[RPT];
+  load16(qp, q);
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < RPT; i += 2) {
+    a0 = fmaf(S[i], q[i], a0);
+    a1 = fmaf(S[i + 1], q[i + 1], a1);
+  }
+  return rsum8(a0 + a1);
+}
+
+__device__ __forceinline__ void store_o(const Args& a, const Stage& s, int b, int hv, int cg, int tok0, int n) {
+  for (int idx = threadIdx.x; idx < n * CG; idx += NT) {
+    const int j = idx / CG, c = idx % CG;
+    a.o[((int64_t)b * a.T + tok0 + j) * (a.Hv * DV) + hv * DV + cg * CG + c] = __float2bfloat16(s.ob[idx]);
+  }
+}
+
+__device__ __forceinline__ float* state_ptr(float* base, const Args& a, int b, int hv, int c, int cg) {
+  return base + ((((int64_t)b * a.Hv + hv) * a.nch + c) * NCG + cg) * (RPT * NT);
+}
+
+// ---------------------------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(NT) fwd_clean_kernel(const Args a) {
+  extern __shared__ float smem[];
+  const int cg = blockIdx.x, hv = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, col = tid / RP, rp = tid % RP;
+  const Stage s = carve(smem, a.ch, false);
+  const int Lc = a.mode ? a.L : a.T;
+  const bool tok_read = a.mode == 0 || a.causal_clean;
+  float S[RPT];
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) S[i] = 0.f;
+  for (int c = 0; c < a.nch; ++c) {
+    const int p0 = c * a.ch, n = min(a.ch, Lc - p0);
+    float* ck = state_ptr(a.ckpt, a, b, hv, c, cg);
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) ck[i * NT + tid] = S[i];
+    stage_tokens(a, s, b, hv, cg, p0, n, p0, false);
+    __syncthreads();
+    for (int j = 0; j < n; ++j) {
+      if (s.rs[j]) {
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) S[i] = 0.f;
+      }
+      float u, vmp;
+      fwd_step(S, s.k + j * DK + rp * RPT, s.al[j], s.be[j], s.v[j * CG + col], u, vmp);
+      if (tok_read) {
+        const float o = readout(S, s.q + j * DK + rp * RPT);
+        if (rp == 0) s.ob[j * CG + col] = o;
+      }
+    }
+    if (!tok_read) {
+      for (int j = 0; j < n; ++j) {
+        const float o = readout(S, s.q + j * DK + rp * RPT);
+        if (rp == 0) s.ob[j * CG + col] = o;
+      }
+    }
+    __syncthreads();
+    store_o(a, s, b, hv, cg, p0, n);
+    __syncthreads();
+  }
+}
+
+// Initial state of noisy block n of row b: the clean state at the start of block n, zero for the
+// first block and at a document start.
+__device__ __forceinline__ bool noisy_init(const Args& a, int b, int n) {
+  return n > 0 && !(a.doc != nullptr && a.doc[(int64_t)b * a.L + n * a.bd]);
+}
+
+__global__ void __launch_bounds__(NT) fwd_noisy_kernel(const Args a) {
+  extern __shared__ float smem[];
+  const int nb = a.L / a.bd;
+  const int cg = blockIdx.x, hv = blockIdx.y, n = blockIdx.z % nb, b = blockIdx.z / nb;
+  const int tid = threadIdx.x, col = tid / RP, rp = tid % RP;
+  const Stage s = carve(smem, a.bd, false);
+  float S0[RPT];
+  const bool from_clean = noisy_init(a, b, n);
+  const float* ck = state_ptr(a.ckpt, a, b, hv, n, cg);
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) S0[i] = from_clean ? ck[i * NT + tid] : 0.f;
+  for (int v = 0; v < a.V; ++v) {
+    const int tok0 = (1 + v) * a.L + n * a.bd;
+    stage_tokens(a, s, b, hv, cg, tok0, a.bd, -1, false);
+    __syncthreads();
+    float S[RPT];
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) S[i] = S0[i];
+    for (int j = 0; j < a.bd; ++j) {
+      float u, vmp;
+      fwd_step(S, s.k + j * DK + rp * RPT, s.al[j], s.be[j], s.v[j * CG + col], u, vmp);
+      if (a.causal_noisy) {
+        const float o = readout(S, s.q + j * DK + rp * RPT);
+        if (rp == 0) s.ob[j * CG + col] = o;
+      }
+    }
+    if (!a.causal_noisy) {
+      for (int j = 0; j < a.bd; ++j) {
+        const float o = readout(S, s.q + j * DK + rp * RPT);
+        if (rp == 0) s.ob[j * CG + col] = o;
+      }
+    }
+    __syncthreads();
+    store_o(a, s, b, hv, cg, tok0, a.bd);
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// backward
+// ---------------------------------------------------------------------------------------------
+// Sum x[16] (this thread's rows, its column) over the warp's 4 columns and add the 4 resulting
+// row sums into dst[row] (shared memory; the CTA's 4 warps add into the same row).
+__device__ __forceinline__ void col_reduce_add(const float (&x)[RPT], float* dst, int lane, int rp) {
+  const int h1 = (lane >> 4) & 1, h2 = (lane >> 3) & 1;
+  float y[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float send = h1 ? x[i] : x[i + 8];
+    const float keep = h1 ? x[i + 8] : x[i];
+    y[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+  float z[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float send = h2 ? y[i] : y[i + 4];
+    const float keep = h2 ? y[i + 4] : y[i];
+    z[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  const int r0 = rp * RPT + h1 * 8 + h2 * 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) atomicAdd(dst + r0 + i, z[i]);
+}
+
+struct Ctx {
+  int b, hv, cg, tid, col, rp, lane;
+  int par;
+};
+
+constexpr int FL_DQ = 1, FL_DK = 2, FL_SC = 4;
+
+// Cluster-wide reduction of the m reduction rows of parity `par` and the write of the results of
+// tokens tok0.. (row-relative): CTA rank r writes rows [16r, 16r+16) of dq / dk, rank 0 the
+// scalars.  One cluster barrier; the buffers are double-buffered by parity.
+__device__ void flush(const Args& a, const Stage& s, Ctx& x, int tok0, int m, int what) {
+  cgx::cluster_group cl = cgx::this_cluster();
+  cl.sync();
+  const int r = (int)cl.block_rank();
+  float* red = s.red + x.par * SUB * RED;
+  const int tid = x.tid;
+  if (tid < m * 8) {
+    const int t = tid >> 3, qd = (tid >> 2) & 1, f4 = tid & 3;
+    if (what & (qd ? FL_DK : FL_DQ)) {
+      const int off = t * RED + qd * DK + r * RPT + f4 * 4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int src = 0; src < NCG; ++src) {
+        const float4 w = *reinterpret_cast<const float4*>(cl.map_shared_rank(red + off, src));
+        acc.x += w.x; acc.y += w.y; acc.z += w.z; acc.w += w.w;
+      }
+      const int64_t row = (int64_t)x.b * a.T + tok0 + t;
+      *reinterpret_cast<float4*>(a.dqk + (row * a.Hv + x.hv) * (2 * DK) + qd * DK + r * RPT + f4 * 4) = acc;
+    }
+  } else if ((what & FL_SC) && r == 0 && tid >= 64 && tid < 64 + 2 * m) {
+    const int t = (tid - 64) >> 1, w = (tid - 64) & 1;   // w 0: dg (slot RED-1), 1: dbeta (slot RED-2)
+    float acc = 0.f;
+#pragma unroll
+    for (int src = 0; src < NCG; ++src) acc += *cl.map_shared_rank(red + t * RED + (w ? 2 * DK : 2 * DK + 1), src);
+    const int64_t row = (int64_t)x.b * a.T + tok0 + t;
+    a.dgb[(row * a.Hv + x.hv) * 2 + w] = acc;
+  }
+  x.par ^= 1;
+}
+
+__device__ __forceinline__ void zero_red(const Stage& s, const Ctx& x) {
+  float* red = s.red + x.par * SUB * RED;
+  for (int i = x.tid; i < SUB * RED; i += NT) red[i] = 0.f;
+  __syncthreads();
+}
+
+// Reverse pass over the n staged tokens (row-relative tok0..).  Sst: state entering token 0 (before
+// any reset); dS: on entry the gradient w.r.t. the state after the last token, on exit w.r.t. Sst.
+// end_read: every token read the state after the last token (block-end read-out).
+__device__ void bwd_segment(const Args& a, const Stage& s, Ctx& x, const float (&Sst)[RPT], float (&dS)[RPT], int tok0,
+                            int n, bool end_read) {
+  const int tid = x.tid, col = x.col, rp = x.rp, lane = x.lane;
+  float S[RPT];
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) S[i] = Sst[i];
+  // pass 1: forward with sub-checkpoints
+  for (int j = 0; j < n; ++j) {
+    if (j % SUB == 0) {
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) s.sck[((j / SUB) * RPT + i) * NT + tid] = S[i];
+    }
+    if (s.rs[j]) {
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) S[i] = 0.f;
+    }
+    float u, vmp;
+    fwd_step(S, s.k + j * DK + rp * RPT, s.al[j], s.be[j], s.v[j * CG + col], u, vmp);
+  }
+  if (end_read) {
+    // o_j = S_end^T q_j:  dS_end += sum_j q_j do_j^T ;  dq_j = S_end do_j
+    for (int j0 = 0; j0 < n; j0 += SUB) {
+      const int m = min(SUB, n - j0);
+      zero_red(s, x);
+      float* red = s.red + x.par * SUB * RED;
+      for (int t = 0; t < m; ++t) {
+        const int j = j0 + t;
+        const float doc = s.dO[j * CG + col];
+        float q[RPT], dq[RPT];
+        load16(s.q + j * DK + rp * RPT, q);
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) {
+          dq[i] = S[i] * doc;
+          dS[i] = fmaf(q[i], doc, dS[i]);
+        }
+        col_reduce_add(dq, red + t * RED, lane, rp);
+      }
+      flush(a, s, x, tok0 + j0, m, FL_DQ);
+    }
+  }
+  // pass 2: replay each sub-chunk (S' in registers) and sweep it in reverse
+  const int nsub = (n + SUB - 1) / SUB;
+  for (int sc = nsub - 1; sc >= 0; --sc) {
+    const int j0 = sc * SUB, m = min(SUB, n - j0);
+    zero_red(s, x);
+    float* red = s.red + x.par * SUB * RED;
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) S[i] = s.sck[(sc * RPT + i) * NT + tid];
+    float Sp[SUB][RPT], uu[SUB], vm[SUB];
+#pragma unroll
+    for (int t = 0; t < SUB; ++t) {
+      if (t < m) {
+        const int j = j0 + t;
+        if (s.rs[j]) {
+#pragma unroll
+          for (int i = 0; i < RPT; ++i) S[i] = 0.f;
+        }
+        const float al = s.al[j];
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) Sp[t][i] = al * S[i];
+        fwd_step(S, s.k + j * DK + rp * RPT, al, s.be[j], s.v[j * CG + col], uu[t], vm[t]);
+      }
+    }
+#pragma unroll
+    for (int t = SUB - 1; t >= 0; --t) {
+      if (t < m) {
+        const int j = j0 + t;
+        const float al = s.al[j], be = s.be[j];
+        const float doc = s.dO[j * CG + col];
+        float k[RPT], dq[RPT], dk[RPT];
+        load16(s.k + j * DK + rp * RPT, k);
+        if (!end_read) {
+          float q[RPT];
+          load16(s.q + j * DK + rp * RPT, q);
+#pragma unroll
+          for (int i = 0; i < RPT; ++i) {
+            dq[i] = fmaf(k[i], uu[t], Sp[t][i]) * doc;   // S_t = S' + k u^T
+            dS[i] = fmaf(q[i], doc, dS[i]);
+          }
+        }
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < RPT; i += 2) {
+          a0 = fmaf(dS[i], k[i], a0);
+          a1 = fmaf(dS[i + 1], k[i + 1], a1);
+        }
+        const float du = rsum8(a0 + a1);
+        const float dp = -be * du;
+        float g0 = 0.f, g1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) {
+          dk[i] = dS[i] * uu[t];
+          dS[i] = fmaf(k[i], dp, dS[i]);          // gradient w.r.t. S'
+          dk[i] = fmaf(Sp[t][i], dp, dk[i]);
+          if (i & 1) g1 = fmaf(dS[i], Sp[t][i], g1); else g0 = fmaf(dS[i], Sp[t][i], g0);
+          dS[i] *= al;
+        }
+        if (s.rs[j]) {
+#pragma unroll
+          for (int i = 0; i < RPT; ++i) dS[i] = 0.f;
+        }
+        if (rp == 0) s.ob[t * CG + col] = be * du;          // dv
+        float* rrow = red + t * RED;
+        if (!end_read) col_reduce_add(dq, rrow, lane, rp);
+        col_reduce_add(dk, rrow + DK, lane, rp);
+        float dbt = du * vm[t];                            // one column's share (same in its 8 lanes)
+        dbt += __shfl_xor_sync(0xffffffffu, dbt, 8);
+        dbt += __shfl_xor_sync(0xffffffffu, dbt, 16);
+        const float dg = warp_sum(g0 + g1);
+        if (lane == 0) {
+          atomicAdd(rrow + 2 * DK, dbt);
+          atomicAdd(rrow + 2 * DK + 1, dg);
+        }
+      }
+    }
+    flush(a, s, x, tok0 + j0, m, (end_read ? 0 : FL_DQ) | FL_DK | FL_SC);
+    for (int idx = tid; idx < m * CG; idx += NT) {
+      const int t = idx / CG, c = idx % CG;
+      a.dv[((int64_t)x.b * a.T + tok0 + j0 + t) * a.lddv + x.hv * DV + x.cg * CG + c] = __float2bfloat16(s.ob[idx]);
+    }
+  }
+}
+
+__global__ void __cluster_dims__(NCG, 1, 1) __launch_bounds__(NT) bwd_noisy_kernel(const Args a) {
+  extern __shared__ float smem[];
+  const int nb = a.L / a.bd;
+  Ctx x;
+  x.cg = blockIdx.x; x.hv = blockIdx.y;
+  const int n = blockIdx.z % nb;
+  x.b = blockIdx.z / nb;
+  x.tid = threadIdx.x; x.col = x.tid / RP; x.rp = x.tid % RP; x.lane = x.tid & 31; x.par = 0;
+  const Stage s = carve(smem, a.bd, true);
+  const bool from_clean = noisy_init(a, x.b, n);
+  float S0[RPT], dI[RPT];
+  const float* ck = state_ptr(a.ckpt, a, x.b, x.hv, n, x.cg);
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) {
+    S0[i] = from_clean ? ck[i * NT + x.tid] : 0.f;
+    dI[i] = 0.f;
+  }
+  for (int v = 0; v < a.V; ++v) {
+    const int tok0 = (1 + v) * a.L + n * a.bd;
+    stage_tokens(a, s, x.b, x.hv, x.cg, tok0, a.bd, -1, true);
+    __syncthreads();
+    float dS[RPT];
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) dS[i] = 0.f;
+    bwd_segment(a, s, x, S0, dS, tok0, a.bd, !a.causal_noisy);
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) dI[i] += dS[i];
+    __syncthreads();
+  }
+  float* di = state_ptr(a.dinit, a, x.b, x.hv, n, x.cg);
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) di[i * NT + x.tid] = from_clean ? dI[i] : 0.f;
+  cgx::this_cluster().sync();   // peers may still read this CTA's reduction rows
+}
+
+__global__ void __cluster_dims__(NCG, 1, 1) __launch_bounds__(NT) bwd_clean_kernel(const Args a) {
+  extern __shared__ float smem[];
+  Ctx x;
+  x.cg = blockIdx.x; x.hv = blockIdx.y; x.b = blockIdx.z;
+  x.tid = threadIdx.x; x.col = x.tid / RP; x.rp = x.tid % RP; x.lane = x.tid & 31; x.par = 0;
+  const Stage s = carve(smem, a.ch, true);
+  const int Lc = a.mode ? a.L : a.T;
+  const bool end_read = a.mode == 1 && !a.causal_clean;
+  float dS[RPT];
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) dS[i] = 0.f;
+  for (int c = a.nch - 1; c >= 0; --c) {
+    const int p0 = c * a.ch, n = min(a.ch, Lc - p0);
+    float Sst[RPT];
+    const float* ck = state_ptr(a.ckpt, a, x.b, x.hv, c, x.cg);
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) Sst[i] = ck[i * NT + x.tid];
+    stage_tokens(a, s, x.b, x.hv, x.cg, p0, n, p0, true);
+    __syncthreads();
+    bwd_segment(a, s, x, Sst, dS, p0, n, end_read);
+    if (a.mode == 1) {
+      const float* di = state_ptr(a.dinit, a, x.b, x.hv, c, x.cg);
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) dS[i] += di[i * NT + x.tid];
+    }
+    __syncthreads();
+  }
+  cgx::this_cluster().sync();   // peers may still read this CTA's reduction rows
+}
+
+// ---------------------------------------------------------------------------------------------
+// q/k L2-norm backward (summing the value heads that share a key head) and gate backward
+// ---------------------------------------------------------------------------------------------
+__global__ void post_bwd_kernel(const Args a, bf16* dmixed, int64_t lddm, bf16* dga, bf16* dgb_out, int64_t lddg,
+                                float* dA_log, float* ddt_bias) {
+  const int64_t row = blockIdx.x;                   // token b*T + t
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int rep = a.Hv / a.Hk;
+  const bf16* src = a.mixed + row * a.ldm;
+  for (int w = warp; w < 2 * a.Hk; w += nw) {
+    const int hk = w >> 1, isk = w & 1;
+    float xv[4], g[4] = {0.f, 0.f, 0.f, 0.f};
+    const bf16* xp = src + isk * a.Hk * DK + hk * DK + lane * 4;
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      xv[e] = __bfloat162float(xp[e]);
+      ss += xv[e] * xv[e];
+    }
+    for (int r = 0; r < rep; ++r) {
+      const float4 d = *reinterpret_cast<const float4*>(a.dqk + (row * a.Hv + hk * rep + r) * (2 * DK) + isk * DK + lane * 4);
+      g[0] += d.x; g[1] += d.y; g[2] += d.z; g[3] += d.w;
+    }
+    ss = warp_sum(ss);
+    const float rn = rsqrtf(ss + 1e-6f);
+    const float sc = isk ? 1.f : a.scale;
+    float dot = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      g[e] *= sc;
+      dot += xv[e] * rn * g[e];
+    }
+    dot = warp_sum(dot);
+    bf16* dp = dmixed + row * lddm + isk * a.Hk * DK + hk * DK + lane * 4;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) dp[e] = __float2bfloat16(rn * (g[e] - xv[e] * rn * dot));
+  }
+  for (int h = threadIdx.x; h < a.Hv; h += blockDim.x) {
+    const float dg = a.dgb[(row * a.Hv + h) * 2 + 0];
+    const float dbeta = a.dgb[(row * a.Hv + h) * 2 + 1];
+    const float xa = __bfloat162float(a.ga[row * a.ldg + h]) + a.dt_bias[h];
+    const float bv = __bfloat162float(a.gb[row * a.ldg + h]);
+    const float beta = 1.f / (1.f + expf(-bv));
+    const float eA = expf(a.A_log[h]);
+    const float sp = softplus_f(xa);
+    const float sig = xa > 20.f ? 1.f : 1.f / (1.f + expf(-xa));
+    const float da = dg * (-eA) * sig;
+    dga[row * lddg + h] = __float2bfloat16(da);
+    dgb_out[row * lddg + h] = __float2bfloat16(dbeta * beta * (1.f - beta));
+    atomicAdd(dA_log + h, dg * (-eA * sp));
+    atomicAdd(ddt_bias + h, da);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// short conv (depthwise, K taps, SiLU), causal or two-stream
+// ---------------------------------------------------------------------------------------------
+struct ConvArgs {
+  int B, T, C, K;
+  int mode, L, V, bd;
+  const uint8_t* doc;   // [B, Lc]
+  const bf16* x; int64_t ldx;
+  const bf16* w;        // [C, K]
+  bf16* y; int64_t ldy;
+};
+
+// Row-relative source token of tap `shift` (reads x[t - shift] in its stream) or -1 (zero pad).
+__device__ __forceinline__ int conv_src(const ConvArgs& a, int b, int t, int shift) {
+  int stream = 0, p = t;
+  if (a.mode) { stream = t / a.L; p = t - stream * a.L; }
+  if (p < shift) return -1;
+  const int Lc = a.mode ? a.L : a.T;
+  if (a.doc != nullptr) {
+    const uint8_t* d = a.doc + (int64_t)b * Lc;
+    for (int s = 0; s < shift; ++s)
+      if (d[p - s]) return -1;    // a document starts inside (p - shift, p]
+  }
+  if (stream == 0) return t - shift;
+  return (p % a.bd) >= shift ? t - shift : p - shift;   // in-block taps: noisy; earlier: clean
+}
+
+__global__ void conv_fwd_kernel(const ConvArgs a) {
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int cpr = a.C / 8;
+  if (gid >= (int64_t)a.B * a.T * cpr) return;
+  const int c8 = (int)(gid % cpr) * 8;
+  const int64_t row = gid / cpr;
+  const int b = (int)(row / a.T), t = (int)(row % a.T);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int j = 0; j < a.K; ++j) {
+    const int src = conv_src(a, b, t, a.K - 1 - j);
+    if (src < 0) continue;
+    float xv[8];
+    load8(a.x + ((int64_t)b * a.T + src) * a.ldx + c8, xv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = fmaf(__bfloat162float(a.w[(c8 + e) * a.K + j]), xv[e], acc[e]);
+  }
+  float out[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) out[e] = acc[e] / (1.f + expf(-acc[e]));
+  store8(a.y + row * a.ldy + c8, out);
+}
+
+// dpre = dy * silu'(pre) (fp32), and dw[c, j] += sum_t dpre * x[src]; block = 256 threads x 8
+// channels, looping over `tpb` tokens.
+__global__ void conv_bwd_pre_kernel(const ConvArgs a, const bf16* dy, int64_t lddy, float* dpre, float* dw, int tpb) {
+  const int c8 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c8 >= a.C) return;
+  const int64_t r0 = (int64_t)blockIdx.y * tpb;
+  const int64_t rows = (int64_t)a.B * a.T;
+  float wacc[4][8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) wacc[j][e] = 0.f;
+  for (int64_t row = r0; row < r0 + tpb && row < rows; ++row) {
+    const int b = (int)(row / a.T), t = (int)(row % a.T);
+    float xs[4][8], pre[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int src = j < a.K ? conv_src(a, b, t, a.K - 1 - j) : -1;
+      if (src >= 0) {
+        load8(a.x + ((int64_t)b * a.T + src) * a.ldx + c8, xs[j]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xs[j][e] = 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (j < a.K) pre[e] = fmaf(__bfloat162float(a.w[(c8 + e) * a.K + j]), xs[j][e], pre[e]);
+    }
+    float g[8], dyv[8];
+    load8(dy + row * lddy + c8, dyv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float sg = 1.f / (1.f + expf(-pre[e]));
+      g[e] = dyv[e] * sg * (1.f + pre[e] * (1.f - sg));
+    }
+    float4* dp = reinterpret_cast<float4*>(dpre + row * a.C + c8);
+    dp[0] = make_float4(g[0], g[1], g[2], g[3]);
+    dp[1] = make_float4(g[4], g[5], g[6], g[7]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) wacc[j][e] = fmaf(g[e], xs[j][e], wacc[j][e]);
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    for (int j = 0; j < a.K && j < 4; ++j) atomicAdd(dw + (c8 + e) * a.K + j, wacc[j][e]);
+}
+
+// dx[s] = sum over outputs t whose tap `shift` reads s of w[c, K-1-shift] * dpre[t].
+__global__ void conv_bwd_dx_kernel(const ConvArgs a, const float* dpre, bf16* dx, int64_t lddx) {
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int cpr = a.C / 8;
+  if (gid >= (int64_t)a.B * a.T * cpr) return;
+  const int c8 = (int)(gid % cpr) * 8;
+  const int64_t row = gid / cpr;
+  const int b = (int)(row / a.T), s = (int)(row % a.T);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  const int sstream = a.mode ? s / a.L : 0;
+  const int nview = (a.mode && sstream == 0) ? a.V : 0;
+  for (int shift = 0; shift < a.K; ++shift) {
+    float wv[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) wv[e] = __bfloat162float(a.w[(c8 + e) * a.K + (a.K - 1 - shift)]);
+    // candidate outputs: same stream s + shift; for a clean source also each view's s + shift
+    for (int cnd = 0; cnd <= nview; ++cnd) {
+      const int t = cnd == 0 ? s + shift : cnd * a.L + s + shift;
+      const int lim = a.mode ? (cnd == 0 ? (sstream + 1) * a.L : (cnd + 1) * a.L) : a.T;
+      if (t >= lim) continue;
+      if (conv_src(a, b, t, shift) != s) continue;
+      const float4* dp = reinterpret_cast<const float4*>(dpre + ((int64_t)b * a.T + t) * a.C + c8);
+      const float4 u0 = dp[0], u1 = dp[1];
+      acc[0] = fmaf(wv[0], u0.x, acc[0]); acc[1] = fmaf(wv[1], u0.y, acc[1]);
+      acc[2] = fmaf(wv[2], u0.z, acc[2]); acc[3] = fmaf(wv[3], u0.w, acc[3]);
+      acc[4] = fmaf(wv[4], u1.x, acc[4]); acc[5] = fmaf(wv[5], u1.y, acc[5]);
+      acc[6] = fmaf(wv[6], u1.z, acc[6]); acc[7] = fmaf(wv[7], u1.w, acc[7]);
+    }
+  }
+  store8(dx + row * lddx + c8, acc);
+}
+
+// ---------------------------------------------------------------------------------------------
+// gated RMSNorm over the head dim:  y = rmsnorm(o) * w * silu(z)   (one warp per token-head)
+// ---------------------------------------------------------------------------------------------
+__global__ void gnorm_fwd_kernel(const bf16* o, const bf16* z, int64_t ldz, const bf16* w, bf16* y, int64_t rows,
+                                 int H, float eps) {
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= rows * H) return;
+  const int64_t row = gw / H;
+  const int h = (int)(gw % H);
+  const bf16* op = o + gw * DV + lane * 4;
+  const bf16* zp = z + row * ldz + h * DV + lane * 4;
+  float ov[4], ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    ov[e] = __bfloat162float(op[e]);
+    ss += ov[e] * ov[e];
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / DV + eps);
+  bf16* yp = y + gw * DV + lane * 4;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float zv = __bfloat162float(zp[e]);
+    const float sz = zv / (1.f + expf(-zv));
+    yp[e] = __float2bfloat16(ov[e] * r * __bfloat162float(w[lane * 4 + e]) * sz);
+  }
+}
+
+__global__ void gnorm_bwd_kernel(const bf16* dy, const bf16* o, const bf16* z, int64_t ldz, const bf16* w, bf16* d_o,
+                                 bf16* dz, int64_t lddz, float* dw, int64_t rows, int H, float eps) {
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  float wacc[4] = {0.f, 0.f, 0.f, 0.f};
+  float wv[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) wv[e] = __bfloat162float(w[lane * 4 + e]);
+  for (int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; gw < rows * H; gw += nwarps) {
+    const int64_t row = gw / H;
+    const int h = (int)(gw % H);
+    float ov[4], zv[4], dyv[4], ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      ov[e] = __bfloat162float(o[gw * DV + lane * 4 + e]);
+      zv[e] = __bfloat162float(z[row * ldz + h * DV + lane * 4 + e]);
+      dyv[e] = __bfloat162float(dy[gw * DV + lane * 4 + e]);
+      ss += ov[e] * ov[e];
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / DV + eps);
+    float dn[4], dot = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float sg = 1.f / (1.f + expf(-zv[e]));
+      const float sz = zv[e] * sg;
+      const float nrm = ov[e] * r;
+      const float av = nrm * wv[e];
+      dz[row * lddz + h * DV + lane * 4 + e] = __float2bfloat16(dyv[e] * av * sg * (1.f + zv[e] * (1.f - sg)));
+      const float da = dyv[e] * sz;
+      wacc[e] = fmaf(da, nrm, wacc[e]);
+      dn[e] = da * wv[e];
+      dot += dn[e] * nrm;
+    }
+    dot = warp_sum(dot) / DV;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) d_o[gw * DV + lane * 4 + e] = __float2bfloat16(r * (dn[e] - ov[e] * r * dot));
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) atomicAdd(dw + lane * 4 + e, wacc[e]);
+}
+
+}  // namespace gdn
+
+// ---------------------------------------------------------------------------------------------
+// launchers
+// ---------------------------------------------------------------------------------------------
+static gdn::Args make_args(const GdnParams& p) {
+  gdn::Args a{};
+  a.B = p.B; a.T = p.T; a.Hk = p.Hk; a.Hv = p.Hv;
+  a.mode = p.mode; a.L = p.L; a.V = p.V; a.bd = p.bd;
+  a.causal_clean = p.causal_clean; a.causal_noisy = p.causal_noisy;
+  const int Lc = p.mode ? p.L : p.T;
+  a.ch = p.mode ? p.bd : 32;
+  a.nch = (Lc + a.ch - 1) / a.ch;
+  a.doc = p.doc;
+  a.mixed = p.mixed; a.ldm = p.ldm;
+  a.ga = p.ga; a.gb = p.gb; a.ldg = p.ldg;
+  a.A_log = p.A_log; a.dt_bias = p.dt_bias;
+  a.scale = p.scale;
+  a.ckpt = p.ckpt; a.o = p.o;
+  a.d_o = p.d_o; a.dqk = p.dqk; a.dgb = p.dgb; a.dv = p.dv; a.lddv = p.lddv; a.dinit = p.dinit;
+  return a;
+}
+
+int64_t gdn_state_floats(const GdnParams& p) {
+  const int Lc = p.mode ? p.L : p.T;
+  const int ch = p.mode ? p.bd : 32;
+  const int nch = (Lc + ch - 1) / ch;
+  return (int64_t)p.B * p.Hv * nch * gdn::DK * gdn::DV;
+}
+
+int gdn_fwd(const GdnParams& p, cudaStream_t st) {
+  using namespace gdn;
+  if (p.dk != DK || p.dvh != DV || p.Hv % p.Hk) return -1;
+  if (p.mode && (p.bd % SUB || p.bd > MAXCH || p.L % p.bd)) return -2;
+  const Args a = make_args(p);
+  static bool init = false;
+  if (!init) {
+    const int mx = (int)(stage_floats(MAXCH, false) * sizeof(float));
+    cudaFuncSetAttribute(fwd_clean_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+    cudaFuncSetAttribute(fwd_noisy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+    init = true;
+  }
+  const size_t sm_c = stage_floats(a.ch, false) * sizeof(float);
+  fwd_clean_kernel<<<dim3(NCG, a.Hv, a.B), NT, sm_c, st>>>(a);
+  if (a.mode && a.V > 0) {
+    const size_t sm_n = stage_floats(a.bd, false) * sizeof(float);
+    fwd_noisy_kernel<<<dim3(NCG, a.Hv, a.B * (a.L / a.bd)), NT, sm_n, st>>>(a);
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int gdn_bwd(const GdnParams& p, bf16* dmixed, int64_t lddm, bf16* dga, bf16* dgb, int64_t lddg, float* dA_log,
+            float* ddt_bias, cudaStream_t st) {
+  using namespace gdn;
+  if (p.dk != DK || p.dvh != DV || p.Hv % p.Hk) return -1;
+  if (p.mode && (p.bd % SUB || p.bd > MAXCH || p.L % p.bd)) return -2;
+  const Args a = make_args(p);
+  static bool init = false;
+  if (!init) {
+    const int mx = (int)(stage_floats(MAXCH, true) * sizeof(float));
+    cudaFuncSetAttribute(bwd_clean_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+    cudaFuncSetAttribute(bwd_noisy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+    init = true;
+  }
+  if (a.mode && a.V > 0) {
+    const size_t sm_n = stage_floats(a.bd, true) * sizeof(float);
+    bwd_noisy_kernel<<<dim3(NCG, a.Hv, a.B * (a.L / a.bd)), NT, sm_n, st>>>(a);
+  }
+  const size_t sm_c = stage_floats(a.ch, true) * sizeof(float);
+  bwd_clean_kernel<<<dim3(NCG, a.Hv, a.B), NT, sm_c, st>>>(a);
+  post_bwd_kernel<<<(unsigned)(a.B * (int64_t)a.T), 256, 0, st>>>(a, dmixed, lddm, dga, dgb, lddg, dA_log, ddt_bias);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+static gdn::ConvArgs conv_args(const ConvParams& p) {
+  gdn::ConvArgs a{};
+  a.B = p.B; a.T = p.T; a.C = p.C; a.K = p.K;
+  a.mode = p.mode; a.L = p.L; a.V = p.V; a.bd = p.bd;
+  a.doc = p.doc; a.x = p.x; a.ldx = p.ldx; a.w = p.w; a.y = p.y; a.ldy = p.ldy;
+  return a;
+}
+
+int gdn_conv_fwd(const ConvParams& p, cudaStream_t st) {
+  if (p.C % 8 || p.K > 4 || p.K < 1) return -1;
+  const gdn::ConvArgs a = conv_args(p);
+  const int64_t n = (int64_t)p.B * p.T * (p.C / 8);
+  gdn::conv_fwd_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int gdn_conv_bwd(const ConvParams& p, const bf16* dy, int64_t lddy, float* dpre, bf16* dx, int64_t lddx, float* dw,
+                 cudaStream_t st) {
+  if (p.C % 8 || p.K > 4 || p.K < 1) return -1;
+  const gdn::ConvArgs a = conv_args(p);
+  const int tpb = 64;
+  const int64_t rows = (int64_t)p.B * p.T;
+  dim3 g1((unsigned)((p.C / 8 + 255) / 256), (unsigned)((rows + tpb - 1) / tpb));
+  gdn::conv_bwd_pre_kernel<<<g1, 256, 0, st>>>(a, dy, lddy, dpre, dw, tpb);
+  const int64_t n = rows * (p.C / 8);
+  gdn::conv_bwd_dx_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a, dpre, dx, lddx);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int gdn_gnorm_fwd(const bf16* o, const bf16* z, int64_t ldz, const bf16* w, bf16* y, int64_t rows, int H, float eps,
+                  cudaStream_t st) {
+  const int64_t threads = rows * H * 32;
+  gdn::gnorm_fwd_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(o, z, ldz, w, y, rows, H, eps);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int gdn_gnorm_bwd(const bf16* dy, const bf16* o, const bf16* z, int64_t ldz, const bf16* w, bf16* d_o, bf16* dz,
+                  int64_t lddz, float* dw, int64_t rows, int H, float eps, int sm_count, cudaStream_t st) {
+  const int blocks = sm_count * 8;
+  gdn::gnorm_bwd_kernel<<<blocks, 256, 0, st>>>(dy, o, z, ldz, w, d_o, dz, lddz, dw, rows, H, eps);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+}  // namespace trida

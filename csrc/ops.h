@@ -17,11 +17,16 @@ void rmsnorm_bwd(const bf16* dy, int64_t lddy, const bf16* x, int64_t ldx, const
                  cudaStream_t s);
 void qk_norm_rope_fwd(const bf16* qkv, int64_t ldqkv, const bf16* qw, const bf16* kw, const float* cos_t,
                       const float* sin_t, const int* pos, bf16* q, bf16* k, float* rstd, int M, int Hq, int Hkv,
-                      int d, int rd, float eps, cudaStream_t s);
+                      int d, int rd, float eps, int qstride, cudaStream_t s);
 void qk_norm_rope_bwd(const bf16* dq, const bf16* dk, const bf16* qkv, int64_t ldqkv, const bf16* qw,
                       const bf16* kw, const float* cos_t, const float* sin_t, const int* pos, const float* rstd,
                       bf16* dqkv, int64_t lddqkv, float* dqw, float* dkw, int M, int Hq, int Hkv, int d, int rd,
-                      int sm_count, cudaStream_t s);
+                      int qstride, int sm_count, cudaStream_t s);
+// sigmoid output gate of the gated attention; gate head h at qkv columns [h*2d + d, h*2d + 2d)
+void attn_gate_fwd(const bf16* o, const bf16* qkv, int64_t ldqkv, bf16* y, int M, int Hq, int d, int sm_count,
+                   cudaStream_t s);
+void attn_gate_bwd(const bf16* dy, const bf16* o, const bf16* qkv, int64_t ldqkv, bf16* d_o, bf16* dqkv,
+                   int64_t lddqkv, int M, int Hq, int d, int sm_count, cudaStream_t s);
 void swiglu_fwd(const bf16* gu, int64_t ldgu, bf16* a, int64_t lda, int M, int F, int sm_count, cudaStream_t s);
 void swiglu_bwd(const bf16* da, int64_t ldda, const bf16* gu, int64_t ldgu, bf16* dgu, int64_t lddgu, int M,
                 int F, int sm_count, cudaStream_t s);
@@ -60,6 +65,45 @@ void bd_attn_tile_masks(const int4* meta, const uint8_t* cls, int B, int T, int 
                         cudaStream_t s);
 int bd_attn_fwd_sm100(const AttnTensors& t, const int4* meta, const int16_t* list128, const int* cnt128,
                       const uint4* rowmask, int flags, float scale, int* err, cudaStream_t s, long long* dbg = nullptr);
+
+// ---- gated-delta-rule linear attention (gdn.cu) ----
+struct GdnParams {
+  int B, T, Hk, Hv, dk, dvh;  // dk, dvh: key / value head dims (128)
+  int mode;                  // 0 causal, 1 two-stream [x0 ; xt_1..xt_V]
+  int L, V, bd;
+  int causal_clean, causal_noisy;
+  const uint8_t* doc;        // [B, Lc] document starts of the clean stream (or null)
+  const bf16* mixed; int64_t ldm;
+  const bf16* ga; const bf16* gb; int64_t ldg;
+  const float* A_log; const float* dt_bias;
+  float scale;
+  float* ckpt;               // gdn_state_floats() floats
+  bf16* o;
+  const bf16* d_o;
+  float* dqk;                // [B*T, Hv, 2, dk]
+  float* dgb;                // [B*T, Hv, 2]
+  bf16* dv; int64_t lddv;
+  float* dinit;              // gdn_state_floats() floats (two-stream backward)
+};
+int64_t gdn_state_floats(const GdnParams& p);
+int gdn_fwd(const GdnParams& p, cudaStream_t s);
+int gdn_bwd(const GdnParams& p, bf16* dmixed, int64_t lddm, bf16* dga, bf16* dgb, int64_t lddg, float* dA_log,
+            float* ddt_bias, cudaStream_t s);
+struct ConvParams {
+  int B, T, C, K;
+  int mode, L, V, bd;
+  const uint8_t* doc;
+  const bf16* x; int64_t ldx;
+  const bf16* w;
+  bf16* y; int64_t ldy;
+};
+int gdn_conv_fwd(const ConvParams& p, cudaStream_t s);
+int gdn_conv_bwd(const ConvParams& p, const bf16* dy, int64_t lddy, float* dpre, bf16* dx, int64_t lddx, float* dw,
+                 cudaStream_t s);
+int gdn_gnorm_fwd(const bf16* o, const bf16* z, int64_t ldz, const bf16* w, bf16* y, int64_t rows, int H, float eps,
+                  cudaStream_t s);
+int gdn_gnorm_bwd(const bf16* dy, const bf16* o, const bf16* z, int64_t ldz, const bf16* w, bf16* d_o, bf16* dz,
+                  int64_t lddz, float* dw, int64_t rows, int H, float eps, int sm_count, cudaStream_t s);
 
 // ---- cross-entropy rows (cross_entropy.cu) ----
 void ce_rows_fwd_bwd(const float* logits, int64_t ld, const int64_t* target, const float* weight, float grad_scale,

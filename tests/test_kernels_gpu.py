@@ -338,3 +338,44 @@ def test_blocks_match_cpu_reference():
     assert rel_err(gx1, gx0) < 3e-2
     for a, b in zip(gp1, gp0):
         assert rel_err(a, b) < 5e-2
+
+
+def test_gated_attention_block_d256_matches_cpu_reference():
+    """Qwen3.5 full-attention sub-block: head_dim 256, partial RoPE (64 of 256), q/gate interleaved
+    per head and the sigmoid output gate; GPU bf16 vs CPU fp32."""
+    torch.manual_seed(0)
+    from trida_stack_b200.models.config import ModelConfig
+    from trida_stack_b200.ops import blocks
+    cfg = ModelConfig.from_hf_dict({
+        "model_type": "qwen3_5_text", "vocab_size": 256, "hidden_size": 256, "intermediate_size": 512,
+        "num_hidden_layers": 1, "num_attention_heads": 4, "num_key_value_heads": 2, "head_dim": 256,
+        "partial_rotary_factor": 0.25, "layer_types": ["full_attention"], "rms_norm_eps": 1e-6})
+    assert cfg.attn_output_gate and cfg.rotary_dim == 64
+    d, Hq, Hkv, D = 256, cfg.n_heads, cfg.n_kv_heads, cfg.hidden_size
+    B, P, Rr, bd = 2, 64, 128, 32
+    meta = bd_layout(B, P, Rr, bd, "cpu")
+    T = meta["seg"].shape[1]
+    params = [torch.randn(D) * 0.1 + 1, torch.randn(2 * Hq * d + 2 * Hkv * d, D) * 0.05,
+              torch.randn(d) * 0.1 + 1, torch.randn(d) * 0.1 + 1, torch.randn(D, Hq * d) * 0.05]
+    x = torch.randn(B * T, D)
+    dy = torch.randn(B * T, D)
+
+    def run(dev, dtype):
+        ps = [p.detach().to(dev, dtype).requires_grad_() for p in params]
+        xx = x.detach().to(dev, dtype).requires_grad_()
+        m = {k: v.to(dev) for k, v in meta.items()}
+        cos_t = sin_t = None
+        if dev == "cuda":
+            cos_t, sin_t = blocks.rope_tables(4096, cfg.rotary_dim, cfg.rope_theta, dev)
+        actx = blocks.AttnContext(m["seg"], m["opos"], m["rblk"], m["segid"], m["view"], m["opos"], True, False,
+                                  cos_t, sin_t)
+        y = blocks.attn_block(xx, *ps, actx, cfg)
+        y.backward(dy.to(dev, dtype))
+        return y.float().cpu(), xx.grad.float().cpu(), [p.grad.float().cpu() for p in ps]
+
+    y0, gx0, gp0 = run("cpu", torch.float32)
+    y1, gx1, gp1 = run("cuda", torch.bfloat16)
+    assert rel_err(y1 - x, y0 - x) < 2e-2
+    assert rel_err(gx1, gx0) < 3e-2
+    for a, b in zip(gp1, gp0):
+        assert rel_err(a, b) < 5e-2

@@ -188,15 +188,22 @@ class _AttnBlock(torch.autograd.Function):
         qkv = torch.empty(M, wqkv.shape[0], dtype=x.dtype, device=x.device)
         gemm(TN, h, wqkv, qkv)
         del h
+        qs = 2 * d if cfg.attn_output_gate else d      # gated: per head [query (d) | gate (d)]
         q = torch.empty(B, T, Hq, d, dtype=x.dtype, device=x.device)
         k = torch.empty(B, T, Hkv, d, dtype=x.dtype, device=x.device)
-        rstd_qk = C.qk_norm_rope_fwd(qkv, qn, kn, actx.cos_t, actx.sin_t, actx.pos32, q, k, Hq, Hkv, d, rd, eps)
-        v = qkv.view(B, T, -1)[:, :, (Hq + Hkv) * d:].view(B, T, Hkv, d)
+        rstd_qk = C.qk_norm_rope_fwd(qkv, qn, kn, actx.cos_t, actx.sin_t, actx.pos32, q, k, Hq, Hkv, d, rd, eps, qs)
+        v = qkv.view(B, T, -1)[:, :, Hq * qs + Hkv * d:].view(B, T, Hkv, d)
         o = torch.empty(B, T, Hq, d, dtype=x.dtype, device=x.device)
         lse = torch.empty(B, Hq, T, dtype=torch.float32, device=x.device)
         attn_fwd(q, k, v, o, lse, actx)
         out = torch.empty_like(x)
-        gemm(TN, o.view(M, Hq * d), wo, out, x, 1.0, 1.0)
+        if cfg.attn_output_gate:
+            og = torch.empty(M, Hq * d, dtype=x.dtype, device=x.device)
+            C.attn_gate_fwd(o.view(M, Hq * d), qkv, og, Hq, d)
+            gemm(TN, og, wo, out, x, 1.0, 1.0)
+            del og
+        else:
+            gemm(TN, o.view(M, Hq * d), wo, out, x, 1.0, 1.0)
         ctx.save_for_backward(x, rstd, norm_w, wqkv, qn, kn, wo, qkv, rstd_qk, q, k, o, lse)
         ctx.actx, ctx.cfg = actx, cfg
         return out
@@ -209,21 +216,30 @@ class _AttnBlock(torch.autograd.Function):
         M, D = x.shape
         C = ext()
         dout = dout.contiguous()
-        # o_proj
+        qs = 2 * d if cfg.attn_output_gate else d
+        # o_proj (and the sigmoid output gate)
+        dqkv = torch.empty_like(qkv)
         do = torch.empty(M, Hq * d, dtype=x.dtype, device=x.device)
         gemm(TT, dout, wo, do)
-        g_wo = _wgrad(dout, o.view(M, Hq * d), wo)
+        if cfg.attn_output_gate:
+            og = torch.empty(M, Hq * d, dtype=x.dtype, device=x.device)
+            C.attn_gate_fwd(o.view(M, Hq * d), qkv, og, Hq, d)
+            g_wo = _wgrad(dout, og, wo)
+            d_o = og
+            C.attn_gate_bwd(do, o.view(M, Hq * d), qkv, d_o, dqkv, Hq, d)
+            do = d_o
+        else:
+            g_wo = _wgrad(dout, o.view(M, Hq * d), wo)
         # attention
-        dqkv = torch.empty_like(qkv)
         dq = torch.empty_like(q)
         dk = torch.empty_like(k)
-        dv = dqkv.view(B, T, -1)[:, :, (Hq + Hkv) * d:].view(B, T, Hkv, d)
-        v = qkv.view(B, T, -1)[:, :, (Hq + Hkv) * d:].view(B, T, Hkv, d)
+        dv = dqkv.view(B, T, -1)[:, :, Hq * qs + Hkv * d:].view(B, T, Hkv, d)
+        v = qkv.view(B, T, -1)[:, :, Hq * qs + Hkv * d:].view(B, T, Hkv, d)
         attn_bwd(q, k, v, o, lse, do.view(B, T, Hq, d), dq, dk, dv, actx)
         del do
         gqn, gkn = _vec_buf(qn), _vec_buf(kn)
         C.qk_norm_rope_bwd(dq, dk, qkv, qn, kn, actx.cos_t, actx.sin_t, actx.pos32, rstd_qk, dqkv, gqn, gkn,
-                           Hq, Hkv, d, rd)
+                           Hq, Hkv, d, rd, qs)
         del dq, dk
         # qkv_proj (recompute the normalised input)
         h = torch.empty_like(x)
