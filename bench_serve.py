@@ -1,0 +1,99 @@
+"""Self-speculative serving benchmark (the serving config of the reference's headline metric).
+
+Model: Qwen3.5-4B-style hybrid (32 layers, 3 gated-delta : 1 full attention, hidden 2560, FFN 9216,
+vocab 248320, full layers 16 Q / 4 KV x 256 with the output gate and partial RoPE, gated-delta
+16 key / 32 value heads x 128, conv 4), random init, bf16.  Load: ``--requests`` concurrent
+requests of ``--prompt`` uniform random tokens each, ``--max-new`` output tokens each, greedy.
+Decoding: self-speculative with ``--n`` causal rows per canvas (canvas of 2N-1 rows), or
+``--mode causal``.
+
+Reports (one JSON line): decode tokens/s (all generated tokens / device-timed decode phase),
+tokens per forward, p50 TTFT, and the device-timed prefill.  Random weights make the drafts
+nearly never match, so tokens per forward stays near its floor of 1 (the reference's ~2.3 is a
+trained-checkpoint figure); the throughput per forward is what the kernels determine.
+
+    python bench_serve.py [--requests 64 --prompt 512 --max-new 512 --n 16 --layers 32]
+"""
+import argparse
+import json
+import os
+import sys
+import time
+
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+
+def hybrid_config(layers):
+    from trida_stack_b200.models.config import ModelConfig
+    return ModelConfig.from_hf_dict({
+        "model_type": "qwen3_5_text", "vocab_size": 248320, "hidden_size": 2560, "intermediate_size": 9216,
+        "num_hidden_layers": layers, "num_attention_heads": 16, "num_key_value_heads": 4, "head_dim": 256,
+        "linear_num_key_heads": 16, "linear_num_value_heads": 32, "linear_key_head_dim": 128,
+        "linear_value_head_dim": 128, "linear_conv_kernel_dim": 4, "partial_rotary_factor": 0.25,
+        "rope_theta": 1e7, "layer_types": (["linear_attention"] * 3 + ["full_attention"]) * (layers // 4),
+        "tie_word_embeddings": True, "rms_norm_eps": 1e-6})
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--requests", type=int, default=64)
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--max-new", type=int, default=512)
+    ap.add_argument("--n", type=int, default=16, help="causal rows per canvas (canvas = 2N-1 rows)")
+    ap.add_argument("--mode", default="self-spec", choices=["self-spec", "causal"])
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--seed", type=int, default=0)
+    args = ap.parse_args()
+
+    from trida_stack_b200.models import Decoder
+    from trida_stack_b200.serve import Engine, Runtime, SamplingParams
+    torch.manual_seed(args.seed)
+    cfg = hybrid_config(args.layers)
+    dec = Decoder(cfg, dtype=torch.bfloat16, device="cuda")
+    mask_id = cfg.vocab_size - 1
+    max_len = args.prompt + args.max_new + 2 * args.n + 8
+    rt = Runtime(dec, max_slots=args.requests, max_len=max_len)
+    eng = Engine(rt, mask_id=mask_id, mode=args.mode, n=args.n, max_running=args.requests)
+    g = torch.Generator().manual_seed(args.seed)
+
+    def prompts(k):
+        return [torch.randint(0, cfg.vocab_size - 2, (args.prompt,), generator=g).tolist() for _ in range(k)]
+
+    # warm-up: a short run through every kernel shape
+    eng.generate(prompts(min(4, args.requests)), max_new_tokens=8)
+    torch.cuda.synchronize()
+
+    reqs = [eng.submit(__import__("trida_stack_b200.serve", fromlist=["Request"]).Request(
+        p, args.max_new, SamplingParams(temperature=0.0))) for p in prompts(args.requests)]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ev[0].record()
+    eng._admit()                       # batched prefill of all requests
+    ev[1].record()
+    f0 = eng.stats["forwards"]
+    while eng.running:
+        eng._decode()
+    ev[2].record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    prefill_ms = ev[0].elapsed_time(ev[1])
+    decode_ms = ev[1].elapsed_time(ev[2])
+    toks = sum(len(r.output) for r in reqs)
+    s = eng.summary(reqs)
+    steps = eng.stats["forwards"] - f0
+    print(json.dumps({
+        "metric": "self-spec decode tokens/s", "value": round(toks / (decode_ms / 1e3), 1), "unit": "tokens/s",
+        "tokens_per_forward": round(s["tokens_per_forward"], 3), "p50_ttft_ms": round(s["p50_ttft_s"] * 1e3, 2),
+        "prefill_ms": round(prefill_ms, 2), "decode_ms": round(decode_ms, 2), "decode_steps": steps,
+        "ms_per_step": round(decode_ms / max(steps, 1), 3), "wall_s": round(wall, 2), "tp": 1,
+        "config": {"model": f"Qwen3.5-4B-style hybrid ({args.layers}L)", "requests": args.requests,
+                   "prompt": args.prompt, "max_new": args.max_new, "mode": args.mode, "n": args.n,
+                   "canvas_rows": 2 * args.n - 1 if args.mode == "self-spec" else 1, "greedy": True},
+        "data": "synthetic uniform prompts, random-init weights", "dtype": "bf16"}))
+
+
+if __name__ == "__main__":
+    main()

@@ -124,11 +124,16 @@ int64_t gdn_state_numel(int64_t B, int64_t T, int64_t Hv, int64_t mode, int64_t 
 void gdn_fwd(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor& gb, const at::Tensor& A_log,
              const at::Tensor& dt_bias, const c10::optional<at::Tensor>& doc, const at::Tensor& o, const at::Tensor& ckpt,
              int64_t B, int64_t T, int64_t Hk, int64_t Hv, int64_t mode, int64_t L, int64_t V, int64_t bd,
-             bool causal_clean, bool causal_noisy, double scale) {
+             bool causal_clean, bool causal_noisy, double scale, const c10::optional<at::Tensor>& final_state) {
   auto p = gdn_params(mixed, ga, gb, A_log, dt_bias, doc, B, T, Hk, Hv, mode, L, V, bd, causal_clean, causal_noisy, scale);
   CHECK_BF16(o); TORCH_CHECK(o.is_contiguous() && o.numel() == B * T * Hv * 128, "o must be [B*T, Hv*128]");
   TORCH_CHECK(ckpt.scalar_type() == at::kFloat && ckpt.numel() >= trida::gdn_state_floats(p), "ckpt too small");
   p.ckpt = ckpt.data_ptr<float>(); p.o = mbf(o);
+  if (final_state.has_value() && final_state->defined()) {
+    TORCH_CHECK(final_state->scalar_type() == at::kFloat && final_state->is_contiguous() &&
+                final_state->numel() == B * Hv * 128 * 128, "final_state must be fp32 [B, Hv, 128, 128]");
+    p.final_state = final_state->data_ptr<float>();
+  }
   c10::cuda::CUDAGuard g(mixed.device());
   const int rc = trida::gdn_fwd(p, stream());
   TORCH_CHECK(rc == 0, "gdn_fwd failed with code ", rc);
@@ -160,6 +165,104 @@ void gdn_bwd(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor& gb
   const int rc = trida::gdn_bwd(p, mbf(dmixed), dmixed.stride(0), mbf(dga), mbf(dgb), dga.stride(0),
                                 dA_log.data_ptr<float>(), ddt_bias.data_ptr<float>(), stream());
   TORCH_CHECK(rc == 0, "gdn_bwd failed with code ", rc);
+}
+
+// ---------------------------------------------------------------------------------------------
+// serving decode step (serve.cu, gdn.cu canvas/commit)
+// ---------------------------------------------------------------------------------------------
+static void check_i32(const at::Tensor& t, int64_t n, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kInt && t.is_contiguous() && t.numel() == n, name,
+              " must be a contiguous int32 CUDA tensor of ", n, " elements");
+}
+
+void canvas_attention(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& slot,
+                      const at::Tensor& pos, const at::Tensor& out, int64_t blk, int64_t n_clean, int64_t max_keys,
+                      double scale) {
+  CHECK_BF16(q); CHECK_BF16(kc); CHECK_BF16(vc); CHECK_BF16(out);
+  TORCH_CHECK(q.dim() == 3 && q.is_contiguous() && out.is_contiguous() && kc.dim() == 4 && kc.is_contiguous() &&
+              vc.is_contiguous(), "canvas attention layouts");
+  const int64_t B = q.size(0) / blk;
+  check_i32(slot, B, "slot"); check_i32(pos, B, "pos");
+  const int Hq = q.size(1), D = q.size(2), Hkv = kc.size(2), maxlen = kc.size(1);
+  TORCH_CHECK(max_keys <= maxlen, "max_keys exceeds the cache length");
+  at::Tensor work = at::empty({trida::canvas_work_floats(B, blk, Hq, D, max_keys)}, q.options().dtype(at::kFloat));
+  c10::cuda::CUDAGuard g(q.device());
+  const int rc = trida::canvas_attention(cbf(q), cbf(kc), cbf(vc), slot.data_ptr<int>(), pos.data_ptr<int>(), mbf(out),
+                                         work.data_ptr<float>(), B, blk, n_clean, Hq, Hkv, D, maxlen, max_keys,
+                                         (float)scale, stream());
+  TORCH_CHECK(rc == 0, "canvas_attention failed with code ", rc);
+}
+
+void kv_append(const at::Tensor& k, const at::Tensor& v, const at::Tensor& kc, const at::Tensor& vc,
+               const at::Tensor& slot, const at::Tensor& pos, int64_t blk) {
+  CHECK_BF16(k); CHECK_BF16(v); CHECK_ROWMAJOR(v);
+  TORCH_CHECK(k.is_contiguous() && kc.is_contiguous() && vc.is_contiguous() && kc.dim() == 4, "kv_append layouts");
+  const int Hkv = kc.size(2), D = kc.size(3);
+  const int64_t B = k.numel() / (blk * Hkv * D);
+  TORCH_CHECK(v.size(0) == B * blk && v.size(1) == Hkv * D && v.stride(0) % 8 == 0, "v rows");
+  check_i32(slot, B, "slot"); check_i32(pos, B, "pos");
+  c10::cuda::CUDAGuard g(k.device());
+  trida::kv_append(cbf(k), cbf(v), v.stride(0), mbf(kc), mbf(vc), slot.data_ptr<int>(), pos.data_ptr<int>(), B, blk,
+                   Hkv, D, kc.size(1), stream());
+}
+
+void canvas_conv(const at::Tensor& x, const at::Tensor& win, const at::Tensor& w, const at::Tensor& y,
+                 const at::Tensor& slot, int64_t blk) {
+  CHECK_BF16(x); CHECK_ROWMAJOR(x); CHECK_BF16(win); CHECK_BF16(w); CHECK_ROWMAJOR(y);
+  const int C = x.size(1), K = w.size(1);
+  TORCH_CHECK(win.is_contiguous() && win.size(1) == K - 1 && win.size(2) == C && K <= 4, "conv window layout");
+  TORCH_CHECK(C % 8 == 0 && x.stride(0) % 8 == 0 && y.stride(0) % 8 == 0, "conv alignment");
+  const int64_t B = x.size(0) / blk;
+  check_i32(slot, B, "slot");
+  c10::cuda::CUDAGuard g(x.device());
+  trida::canvas_conv(cbf(x), x.stride(0), cbf(win), cbf(w), mbf(y), y.stride(0), slot.data_ptr<int>(), B, blk, C, K,
+                     stream());
+}
+
+void conv_commit(const at::Tensor& x, int64_t rows_per, const at::Tensor& win, const at::Tensor& slot,
+                 const at::Tensor& adv) {
+  CHECK_BF16(x); CHECK_ROWMAJOR(x); CHECK_BF16(win);
+  const int C = x.size(1), K = win.size(1) + 1;
+  TORCH_CHECK(win.is_contiguous() && win.size(2) == C && K <= 4 && x.stride(0) % 8 == 0, "conv window layout");
+  const int64_t B = slot.numel();
+  check_i32(slot, B, "slot"); check_i32(adv, B, "adv");
+  c10::cuda::CUDAGuard g(x.device());
+  trida::conv_commit(cbf(x), x.stride(0), rows_per, mbf(win), slot.data_ptr<int>(), adv.data_ptr<int>(), B, C, K,
+                     stream());
+}
+
+void gdn_canvas(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor& gb, const at::Tensor& A_log,
+                const at::Tensor& dt_bias, const at::Tensor& o, const at::Tensor& ssm, const at::Tensor& slot,
+                int64_t blk, int64_t Hk, int64_t Hv, int64_t n_clean, double scale) {
+  const int64_t B = mixed.size(0) / blk;
+  auto p = gdn_params(mixed, ga, gb, A_log, dt_bias, c10::nullopt, B, blk, Hk, Hv, 0, blk, 0, 32, true, false, scale);
+  CHECK_BF16(o); TORCH_CHECK(o.is_contiguous() && o.numel() == B * blk * Hv * 128, "o layout");
+  TORCH_CHECK(ssm.scalar_type() == at::kFloat && ssm.is_contiguous() && ssm.size(1) == Hv, "state cache layout");
+  check_i32(slot, B, "slot");
+  p.o = mbf(o);
+  c10::cuda::CUDAGuard g(mixed.device());
+  TORCH_CHECK(trida::gdn_canvas(p, ssm.data_ptr<float>(), slot.data_ptr<int>(), n_clean, stream()) == 0,
+              "gdn_canvas failed");
+}
+
+void gdn_commit(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor& gb, const at::Tensor& A_log,
+                const at::Tensor& dt_bias, const at::Tensor& ssm, const at::Tensor& slot, const at::Tensor& adv,
+                int64_t blk, int64_t Hk, int64_t Hv, double scale) {
+  const int64_t B = mixed.size(0) / blk;
+  auto p = gdn_params(mixed, ga, gb, A_log, dt_bias, c10::nullopt, B, blk, Hk, Hv, 0, blk, 0, 32, true, false, scale);
+  TORCH_CHECK(ssm.scalar_type() == at::kFloat && ssm.is_contiguous() && ssm.size(1) == Hv, "state cache layout");
+  check_i32(slot, B, "slot"); check_i32(adv, B, "adv");
+  c10::cuda::CUDAGuard g(mixed.device());
+  TORCH_CHECK(trida::gdn_commit(p, ssm.data_ptr<float>(), slot.data_ptr<int>(), adv.data_ptr<int>(), stream()) == 0,
+              "gdn_commit failed");
+}
+
+void argmax_rows(const at::Tensor& logits, const at::Tensor& out) {
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1, "fp32 logits rows");
+  TORCH_CHECK(out.scalar_type() == at::kLong && out.is_contiguous() && out.numel() == logits.size(0), "out int64");
+  c10::cuda::CUDAGuard g(logits.device());
+  trida::argmax_rows(logits.data_ptr<float>(), logits.stride(0), logits.size(0), logits.size(1), out.data_ptr<int64_t>(),
+                     stream());
 }
 
 static trida::ConvParams conv_params(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& doc,
@@ -538,7 +641,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bd_attn_tile_masks", &bd_attn_tile_masks);
   m.def("gemm_error", &gemm_error);
   m.def("gdn_state_numel", &gdn_state_numel);
-  m.def("gdn_fwd", &gdn_fwd);
+  m.def("gdn_fwd", &gdn_fwd, py::arg("mixed"), py::arg("ga"), py::arg("gb"), py::arg("A_log"), py::arg("dt_bias"),
+        py::arg("doc"), py::arg("o"), py::arg("ckpt"), py::arg("B"), py::arg("T"), py::arg("Hk"), py::arg("Hv"),
+        py::arg("mode"), py::arg("L"), py::arg("V"), py::arg("bd"), py::arg("causal_clean"), py::arg("causal_noisy"),
+        py::arg("scale"), py::arg("final_state") = py::none());
+  m.def("canvas_attention", &canvas_attention);
+  m.def("kv_append", &kv_append);
+  m.def("canvas_conv", &canvas_conv);
+  m.def("conv_commit", &conv_commit);
+  m.def("gdn_canvas", &gdn_canvas);
+  m.def("gdn_commit", &gdn_commit);
+  m.def("argmax_rows", &argmax_rows);
   m.def("gdn_bwd", &gdn_bwd);
   m.def("gdn_conv_fwd", &gdn_conv_fwd);
   m.def("gdn_conv_bwd", &gdn_conv_bwd);

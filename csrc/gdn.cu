@@ -64,6 +64,7 @@ struct Args {
   bf16* dv;                 // v-gradient rows [B*T, lddv] (head columns at hv*DV)
   int64_t lddv;
   float* dinit;             // [B, Hv, nch, NCG, RPT, NT]
+  float* final_state;       // optional [B, Hv, DK, DV] state after the last clean token (serving prefill)
 };
 
 struct Stage {
@@ -247,6 +248,65 @@ __global__ void __launch_bounds__(NT) fwd_clean_kernel(const Args a) {
     store_o(a, s, b, hv, cg, p0, n);
     __syncthreads();
   }
+  if (a.final_state != nullptr) {
+    float* f = a.final_state + ((int64_t)b * a.Hv + hv) * DK * DV + cg * CG + col;
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) f[(rp * RPT + i) * DV] = S[i];
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// serving: one canvas of T rows per request from the cached state (rows < n_clean token-causal,
+// the rest read the state after the last row), and the commit that advances the cached state by
+// adv[b] rows.  State cache [slots, Hv, DK, DV] fp32.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void load_state(const float* base, int col, int cg, int rp, float (&S)[RPT]) {
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) S[i] = base[(rp * RPT + i) * DV + cg * CG + col];
+}
+
+__global__ void __launch_bounds__(NT) canvas_kernel(const Args a, const float* ssm, const int* slot, int n_clean) {
+  extern __shared__ float smem[];
+  const int cg = blockIdx.x, hv = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, col = tid / RP, rp = tid % RP;
+  const Stage s = carve(smem, a.T, false);
+  float S[RPT];
+  load_state(ssm + ((int64_t)slot[b] * a.Hv + hv) * DK * DV, col, cg, rp, S);
+  stage_tokens(a, s, b, hv, cg, 0, a.T, -1, false);
+  __syncthreads();
+  for (int j = 0; j < a.T; ++j) {
+    float u, vmp;
+    fwd_step(S, s.k + j * DK + rp * RPT, s.al[j], s.be[j], s.v[j * CG + col], u, vmp);
+    if (j < n_clean) {
+      const float o = readout(S, s.q + j * DK + rp * RPT);
+      if (rp == 0) s.ob[j * CG + col] = o;
+    }
+  }
+  for (int j = n_clean; j < a.T; ++j) {
+    const float o = readout(S, s.q + j * DK + rp * RPT);
+    if (rp == 0) s.ob[j * CG + col] = o;
+  }
+  __syncthreads();
+  store_o(a, s, b, hv, cg, 0, a.T);
+}
+
+__global__ void __launch_bounds__(NT) commit_kernel(const Args a, float* ssm, const int* slot, const int* adv) {
+  extern __shared__ float smem[];
+  const int cg = blockIdx.x, hv = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, col = tid / RP, rp = tid % RP;
+  const Stage s = carve(smem, a.T, false);
+  const int n = min(adv[b], a.T);
+  float* base = ssm + ((int64_t)slot[b] * a.Hv + hv) * DK * DV;
+  float S[RPT];
+  load_state(base, col, cg, rp, S);
+  stage_tokens(a, s, b, hv, cg, 0, n, -1, false);
+  __syncthreads();
+  for (int j = 0; j < n; ++j) {
+    float u, vmp;
+    fwd_step(S, s.k + j * DK + rp * RPT, s.al[j], s.be[j], s.v[j * CG + col], u, vmp);
+  }
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) base[(rp * RPT + i) * DV + cg * CG + col] = S[i];
 }
 
 // Initial state of noisy block n of row b: the clean state at the start of block n, zero for the
@@ -830,6 +890,7 @@ static gdn::Args make_args(const GdnParams& p) {
   a.scale = p.scale;
   a.ckpt = p.ckpt; a.o = p.o;
   a.d_o = p.d_o; a.dqk = p.dqk; a.dgb = p.dgb; a.dv = p.dv; a.lddv = p.lddv; a.dinit = p.dinit;
+  a.final_state = p.final_state;
   return a;
 }
 
@@ -881,6 +942,29 @@ int gdn_bwd(const GdnParams& p, bf16* dmixed, int64_t lddm, bf16* dga, bf16* dgb
   const size_t sm_c = stage_floats(a.ch, true) * sizeof(float);
   bwd_clean_kernel<<<dim3(NCG, a.Hv, a.B), NT, sm_c, st>>>(a);
   post_bwd_kernel<<<(unsigned)(a.B * (int64_t)a.T), 256, 0, st>>>(a, dmixed, lddm, dga, dgb, lddg, dA_log, ddt_bias);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int gdn_canvas(const GdnParams& p, const float* ssm, const int* slot, int n_clean, cudaStream_t st) {
+  using namespace gdn;
+  if (p.dk != DK || p.dvh != DV || p.Hv % p.Hk || p.T > MAXCH) return -1;
+  Args a = make_args(p);
+  static bool init = false;
+  if (!init) {
+    const int mx = (int)(stage_floats(MAXCH, false) * sizeof(float));
+    cudaFuncSetAttribute(canvas_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+    cudaFuncSetAttribute(commit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+    init = true;
+  }
+  canvas_kernel<<<dim3(NCG, a.Hv, a.B), NT, stage_floats(a.T, false) * sizeof(float), st>>>(a, ssm, slot, n_clean);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int gdn_commit(const GdnParams& p, float* ssm, const int* slot, const int* adv, cudaStream_t st) {
+  using namespace gdn;
+  if (p.dk != DK || p.dvh != DV || p.Hv % p.Hk || p.T > MAXCH) return -1;
+  Args a = make_args(p);
+  commit_kernel<<<dim3(NCG, a.Hv, a.B), NT, stage_floats(a.T, false) * sizeof(float), st>>>(a, ssm, slot, adv);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 

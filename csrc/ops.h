@@ -84,9 +84,15 @@ struct GdnParams {
   float* dgb;                // [B*T, Hv, 2]
   bf16* dv; int64_t lddv;
   float* dinit;              // gdn_state_floats() floats (two-stream backward)
+  float* final_state;        // optional [B, Hv, dk, dvh] state after the last clean token
 };
 int64_t gdn_state_floats(const GdnParams& p);
 int gdn_fwd(const GdnParams& p, cudaStream_t s);
+// serving: canvas of p.T rows per request from the state cache [slots, Hv, dk, dvh]; commit
+// advances the cached state by adv[b] rows of the canvas (both read p.mixed / p.ga / p.gb rows
+// b * p.T + j).
+int gdn_canvas(const GdnParams& p, const float* ssm, const int* slot, int n_clean, cudaStream_t s);
+int gdn_commit(const GdnParams& p, float* ssm, const int* slot, const int* adv, cudaStream_t s);
 int gdn_bwd(const GdnParams& p, bf16* dmixed, int64_t lddm, bf16* dga, bf16* dgb, int64_t lddg, float* dA_log,
             float* ddt_bias, cudaStream_t s);
 struct ConvParams {
@@ -104,6 +110,19 @@ int gdn_gnorm_fwd(const bf16* o, const bf16* z, int64_t ldz, const bf16* w, bf16
                   cudaStream_t s);
 int gdn_gnorm_bwd(const bf16* dy, const bf16* o, const bf16* z, int64_t ldz, const bf16* w, bf16* d_o, bf16* dz,
                   int64_t lddz, float* dw, int64_t rows, int H, float eps, int sm_count, cudaStream_t s);
+
+// ---- serving decode step (serve.cu) ----
+int canvas_attention(const bf16* q, const bf16* kc, const bf16* vc, const int* slot, const int* pos, bf16* out,
+                     float* work, int B, int blk, int n_clean, int Hq, int Hkv, int D, int maxlen, int max_keys,
+                     float scale, cudaStream_t s);
+int64_t canvas_work_floats(int B, int blk, int Hq, int D, int max_keys);
+void kv_append(const bf16* k, const bf16* v, int64_t ldv, bf16* kc, bf16* vc, const int* slot, const int* pos, int B,
+               int blk, int Hkv, int D, int maxlen, cudaStream_t s);
+void canvas_conv(const bf16* x, int64_t ldx, const bf16* win, const bf16* w, bf16* y, int64_t ldy, const int* slot,
+                 int B, int blk, int C, int K, cudaStream_t s);
+void conv_commit(const bf16* x, int64_t ldx, int rows_per, bf16* win, const int* slot, const int* adv, int B, int C,
+                 int K, cudaStream_t s);
+void argmax_rows(const float* logits, int64_t ld, int rows, int V, int64_t* out, cudaStream_t s);
 
 // ---- cross-entropy rows (cross_entropy.cu) ----
 void ce_rows_fwd_bwd(const float* logits, int64_t ld, const int64_t* target, const float* weight, float grad_scale,

@@ -1,0 +1,94 @@
+"""Serving runtime and self-speculative engine on CPU: prefill logits match the model's causal
+forward, and greedy self-speculative decoding equals greedy autoregressive decoding."""
+import pytest
+import torch
+
+from trida_stack_b200.models import Decoder, ModelConfig, qwen3_config
+from trida_stack_b200.models.hybrid import HybridBlockDiffusionLM
+from trida_stack_b200.serve import Engine, Runtime, SamplingParams
+
+
+def tiny_hybrid(seed=0):
+    cfg = ModelConfig.from_hf_dict({
+        "model_type": "qwen3_5_text", "vocab_size": 97, "hidden_size": 64, "intermediate_size": 128,
+        "num_hidden_layers": 4, "num_attention_heads": 2, "num_key_value_heads": 1, "head_dim": 32,
+        "linear_num_key_heads": 2, "linear_num_value_heads": 4, "linear_key_head_dim": 16,
+        "linear_value_head_dim": 16, "linear_conv_kernel_dim": 4, "partial_rotary_factor": 0.5,
+        "layer_types": ["linear_attention"] * 3 + ["full_attention"], "tie_word_embeddings": True})
+    torch.manual_seed(seed)
+    dec = Decoder(cfg, dtype=torch.float32)
+    with torch.no_grad():
+        for n, p in dec.named_parameters():
+            if p.dim() >= 2:
+                p.normal_(0, 0.2)
+            elif n.endswith("A_log"):
+                p.copy_(torch.log(torch.empty_like(p).uniform_(0.5, 4)))
+            else:
+                p.copy_(1 + 0.1 * torch.randn_like(p))
+    return dec
+
+
+def tiny_dense(seed=0):
+    torch.manual_seed(seed)
+    cfg = qwen3_config(vocab_size=97, hidden_size=64, intermediate_size=128, num_layers=2, n_heads=4,
+                       n_kv_heads=2, head_dim=16)
+    dec = Decoder(cfg, dtype=torch.float32)
+    with torch.no_grad():
+        for p in dec.parameters():
+            if p.dim() >= 2:
+                p.normal_(0, 0.3)
+    return dec
+
+
+def full_logits(dec, ids):
+    m = HybridBlockDiffusionLM(dec, mask_id=96, ar_only=True)
+    with torch.no_grad():
+        actx = m._causal_rows(ids, None)
+        h = dec(dec.embed_tokens(ids), actx)
+        return (h @ dec.lm_weight.t()).view(ids.shape[0], ids.shape[1], -1)
+
+
+@pytest.mark.parametrize("make", [tiny_hybrid, tiny_dense])
+def test_prefill_and_canvas_match_causal_forward(make):
+    dec = make()
+    torch.manual_seed(1)
+    ids = torch.randint(0, 96, (2, 150))
+    ref = full_logits(dec, ids)
+    rt = Runtime(dec, max_slots=4, max_len=256)
+    slots = [rt.alloc(), rt.alloc()]
+    # prefill 130 tokens (3 chunks), then a fully causal canvas of the next 20
+    last = rt.prefill(slots, ids[:, :130].tolist())
+    torch.testing.assert_close(last, ref[:, 129], rtol=1e-4, atol=1e-4)
+    lg = rt.canvas(slots, ids[:, 130:150], 20)
+    torch.testing.assert_close(lg, ref[:, 130:150], rtol=1e-4, atol=1e-4)
+    # commit only 7 rows, then re-run the rest: the cache must continue from row 137
+    rt.commit(slots, [7, 7])
+    lg2 = rt.canvas(slots, ids[:, 137:150], 13)
+    torch.testing.assert_close(lg2, ref[:, 137:150], rtol=1e-4, atol=1e-4)
+    rt.commit(slots, [13, 13])
+
+
+@pytest.mark.parametrize("make", [tiny_hybrid, tiny_dense])
+@pytest.mark.parametrize("n", [2, 4])
+def test_greedy_self_spec_equals_autoregressive(make, n):
+    dec = make()
+    torch.manual_seed(2)
+    prompts = [torch.randint(0, 96, (L,)).tolist() for L in (9, 9, 14)]
+    ar = Engine(Runtime(dec, max_slots=4, max_len=256), mask_id=96, mode="causal")
+    ref = [r.output for r in ar.generate(prompts, max_new_tokens=40)]
+    ss = Engine(Runtime(dec, max_slots=4, max_len=256), mask_id=96, mode="self-spec", n=n)
+    reqs = ss.generate(prompts, max_new_tokens=40)
+    for r, want in zip(reqs, ref):
+        assert r.output == want
+        assert r.finish_reason == "length"
+    s = ss.summary(reqs)
+    assert s["tokens_per_forward"] >= 1.0
+
+
+def test_sampled_self_spec_runs_and_respects_eos():
+    dec = tiny_hybrid()
+    eng = Engine(Runtime(dec, max_slots=2, max_len=256), mask_id=96, mode="self-spec", n=3)
+    sp = SamplingParams(temperature=0.8, top_k=20, top_p=0.9, seed=3)
+    reqs = eng.generate([[1, 2, 3, 4, 5]], max_new_tokens=30, sampling=sp, eos=(7,))
+    r = reqs[0]
+    assert r.done and 7 not in r.output and len(r.output) <= 30

@@ -1,0 +1,73 @@
+"""Serving runtime on the CUDA kernels vs the CPU statement of the same step."""
+import copy
+
+import pytest
+import torch
+
+from trida_stack_b200.models import Decoder, ModelConfig, qwen3_config
+from trida_stack_b200.serve import Engine, Runtime
+
+pytestmark = pytest.mark.gpu
+
+
+def _hybrid(head_dim):
+    cfg = ModelConfig.from_hf_dict({
+        "model_type": "qwen3_5_text", "vocab_size": 512, "hidden_size": 256, "intermediate_size": 512,
+        "num_hidden_layers": 4, "num_attention_heads": 4, "num_key_value_heads": 2, "head_dim": head_dim,
+        "linear_num_key_heads": 2, "linear_num_value_heads": 4, "linear_key_head_dim": 128,
+        "linear_value_head_dim": 128, "linear_conv_kernel_dim": 4, "partial_rotary_factor": 0.25,
+        "layer_types": ["linear_attention"] * 3 + ["full_attention"], "tie_word_embeddings": True})
+    return cfg
+
+
+def _dense():
+    return qwen3_config(vocab_size=512, hidden_size=256, intermediate_size=512, num_layers=2, n_heads=4,
+                        n_kv_heads=2, head_dim=128)
+
+
+def _init(cfg, seed=0):
+    torch.manual_seed(seed)
+    dec = Decoder(cfg, dtype=torch.float32)
+    with torch.no_grad():
+        for n, p in dec.named_parameters():
+            if p.dim() >= 2:
+                p.normal_(0, 0.06)
+            elif n.endswith("A_log"):
+                p.copy_(torch.log(torch.empty_like(p).uniform_(0.5, 4)))
+            else:
+                p.copy_(1 + 0.1 * torch.randn_like(p))
+    return dec.to(torch.bfloat16).float()
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm()).item()
+
+
+@pytest.mark.parametrize("cfg", [_hybrid(256), _hybrid(128), _dense()], ids=["hybrid-d256", "hybrid-d128", "dense"])
+def test_cuda_runtime_matches_cpu(cfg):
+    dec = _init(cfg)
+    dec_g = copy.deepcopy(dec).to("cuda", torch.bfloat16)
+    torch.manual_seed(1)
+    ids = torch.randint(0, 500, (3, 90))
+    out = {}
+    for name, d in (("cpu", dec), ("gpu", dec_g)):
+        rt = Runtime(d, max_slots=4, max_len=256)
+        slots = [rt.alloc() for _ in range(3)]
+        last = rt.prefill(slots, ids[:, :70].tolist())
+        lg = rt.canvas(slots, ids[:, 70:77], 4)          # self-spec shaped canvas (N = 4)
+        rt.commit(slots, [1, 3, 4])
+        lg2 = rt.canvas(slots, ids[:, 77:84], 4)
+        rt.commit(slots, [4, 4, 4])
+        out[name] = [t.float().cpu() for t in (last, lg, lg2)]
+    for a, b in zip(out["gpu"], out["cpu"]):
+        assert _rel(a, b) < 3e-2, _rel(a, b)
+
+
+def test_cuda_self_spec_engine_runs():
+    dec = _init(_hybrid(256)).to("cuda", torch.bfloat16)
+    eng = Engine(Runtime(dec, max_slots=8, max_len=512), mask_id=511, mode="self-spec", n=4)
+    torch.manual_seed(2)
+    prompts = [torch.randint(0, 500, (40,)).tolist() for _ in range(6)]
+    reqs = eng.generate(prompts, max_new_tokens=50)
+    assert all(len(r.output) == 50 for r in reqs)
+    assert eng.summary(reqs)["tokens_per_forward"] >= 1.0

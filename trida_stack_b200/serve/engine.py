@@ -1,0 +1,310 @@
+"""Batched self-speculative (and autoregressive) decoding over the slot runtime.
+
+Self-speculation (the reference's ``HybridDiffusionSelfSpec``, variant ``bd_bidir_shift``;
+algorithm as stated in ``inference/zoro-1/mlx/trida_mlx/decode.py:1-17,293-386``), with
+``blk = 2N - 1`` canvas rows of which the first N are token-causal:
+
+    cold start : [t0, MASK x (2N-2)]              -> clean = row 0, specs = rows 1..N-1; commit 1
+    verify     : [pending, spec_1..spec_{N-1}, MASK x (N-1)]
+                 spec_j is accepted while it equals the causal prediction of row j-1;
+                 all accepted -> emit specs + row N-1, new specs = rows N..2N-2; commit N
+                 rejected at j -> emit accepted specs + correction; commit 1 + j; cold start next
+
+Row i of a canvas predicts canvas position i + 1 (shift read-out).  Cold starts and verifies have
+the same canvas shape, so every running request advances in ONE batched forward per step.  Greedy
+decoding is lossless (the output equals autoregressive greedy decoding token for token).  With
+temperature > 0 the ``strict_truncated`` policy applies: drafts come from the same top-k / top-p
+truncated distribution the verifier uses, accepted with probability ``min(1, p / q)`` and
+corrected from ``norm(max(0, p - q))``.
+
+``mode="causal"`` decodes one token per forward (a one-row canvas).
+"""
+import itertools
+import queue
+import threading
+import time
+from dataclasses import dataclass, field
+from typing import List, Optional
+
+import torch
+
+from .runtime import Runtime
+
+
+@dataclass
+class SamplingParams:
+    temperature: float = 0.0
+    top_k: int = 20
+    top_p: float = 0.95
+    seed: Optional[int] = None
+
+    @property
+    def greedy(self):
+        return self.temperature <= 0
+
+
+@dataclass
+class Request:
+    prompt: List[int]
+    max_new_tokens: int = 256
+    sampling: SamplingParams = field(default_factory=SamplingParams)
+    eos: tuple = ()
+    rid: int = 0
+    # results
+    output: List[int] = field(default_factory=list)
+    finish_reason: Optional[str] = None
+    forwards: int = 0
+    accept_hist: List[int] = field(default_factory=list)
+    t_submit: float = 0.0
+    t_first: Optional[float] = None
+    t_done: Optional[float] = None
+    # decode state
+    slot: int = -1
+    t0: Optional[int] = None
+    t0_emitted: bool = False
+    pending: Optional[int] = None
+    specs: Optional[List[int]] = None
+    spec_q: Optional[torch.Tensor] = None
+    gen: Optional[torch.Generator] = None
+    on_tokens: Optional[object] = None      # callable(list[int]) for streaming
+    done_event: threading.Event = field(default_factory=threading.Event)
+
+    @property
+    def done(self):
+        return self.finish_reason is not None
+
+
+def truncated_probs(logits, sp):
+    """Softmax of logits / T restricted to the top-k and top-p nucleus (rows renormalised)."""
+    x = logits.float() / max(sp.temperature, 1e-6)
+    if sp.top_k and sp.top_k > 0 and sp.top_k < x.shape[-1]:
+        kth = torch.topk(x, sp.top_k, dim=-1).values[..., -1:]
+        x = x.masked_fill(x < kth, float("-inf"))
+    p = torch.softmax(x, -1)
+    if sp.top_p and sp.top_p < 1.0:
+        sp_, idx = torch.sort(p, dim=-1, descending=True)
+        cum = sp_.cumsum(-1)
+        drop = (cum - sp_) > sp.top_p
+        sp_ = sp_.masked_fill(drop, 0.0)
+        p = torch.zeros_like(p).scatter(-1, idx, sp_)
+        p = p / p.sum(-1, keepdim=True)
+    return p
+
+
+class Engine:
+    """Continuous-batching decode engine over one ``Runtime``."""
+
+    def __init__(self, runtime: Runtime, mask_id: int, mode: str = "self-spec", n: int = 4,
+                 max_running: Optional[int] = None):
+        assert mode in ("self-spec", "causal")
+        self.rt = runtime
+        self.mask_id = mask_id
+        self.mode = mode
+        self.n = n if mode == "self-spec" else 1
+        self.blk = 2 * self.n - 1
+        self.max_running = min(max_running or runtime.max_slots, runtime.max_slots)
+        self.waiting: "queue.Queue[Request]" = queue.Queue()
+        self.running: List[Request] = []
+        self._ids = itertools.count()
+        self._lock = threading.Lock()
+        self._thread = None
+        self._stop = False
+        self.stats = {"forwards": 0, "tokens": 0, "steps": 0, "prefill_tokens": 0}
+
+    # ------------------------------------------------------------------ API
+    def submit(self, req: Request) -> Request:
+        req.rid = next(self._ids)
+        req.t_submit = time.perf_counter()
+        req.accept_hist = [0] * self.n
+        if req.sampling.seed is not None:
+            req.gen = torch.Generator(device=self.rt.device).manual_seed(req.sampling.seed)
+        self.waiting.put(req)
+        return req
+
+    def generate(self, prompts, max_new_tokens=256, sampling=None, eos=()):
+        """Synchronous batch generation (runs the loop in the caller's thread)."""
+        reqs = [self.submit(Request(list(p), max_new_tokens, sampling or SamplingParams(), tuple(eos)))
+                for p in prompts]
+        while not all(r.done for r in reqs):
+            self.step()
+        return reqs
+
+    def start(self):
+        if self._thread is None:
+            self._thread = threading.Thread(target=self._loop, daemon=True)
+            self._thread.start()
+
+    def stop(self):
+        self._stop = True
+        if self._thread is not None:
+            self._thread.join(timeout=30)
+
+    def _loop(self):
+        while not self._stop:
+            if not self.running and self.waiting.empty():
+                time.sleep(0.001)
+                continue
+            self.step()
+
+    # ------------------------------------------------------------------ scheduling
+    def step(self):
+        self._admit()
+        if self.running:
+            self._decode()
+        self.stats["steps"] += 1
+
+    def _admit(self):
+        new = []
+        while len(self.running) + len(new) < self.max_running and self.rt.free:
+            try:
+                req = self.waiting.get_nowait()
+            except queue.Empty:
+                break
+            req.slot = self.rt.alloc()
+            new.append(req)
+        if not new:
+            return
+        # batch prefills of equal prompt length
+        new.sort(key=lambda r: len(r.prompt))
+        for _, grp in itertools.groupby(new, key=lambda r: len(r.prompt)):
+            grp = list(grp)
+            logits = self.rt.prefill([r.slot for r in grp], [r.prompt for r in grp])
+            self.stats["prefill_tokens"] += sum(len(r.prompt) for r in grp)
+            for b, r in enumerate(grp):
+                r.t0 = self._pick(logits[b:b + 1], r)[0]
+                r.t0_emitted = False
+                if self.mode == "causal":
+                    self._emit(r, [r.t0])
+                    r.t0_emitted = True
+            self.running.extend(grp)
+        self._reap()
+
+    def _pick(self, logits, req):
+        if req.sampling.greedy:
+            return logits.argmax(-1).tolist()
+        p = truncated_probs(logits, req.sampling)
+        return torch.multinomial(p, 1, generator=req.gen).squeeze(-1).tolist()
+
+    def _emit(self, req, toks):
+        out = []
+        for t in toks:
+            if t in req.eos:
+                req.finish_reason = "stop"
+                break
+            out.append(t)
+            if len(req.output) + len(out) >= req.max_new_tokens:
+                req.finish_reason = "length"
+                break
+        if out:
+            if req.t_first is None:
+                req.t_first = time.perf_counter()
+            req.output.extend(out)
+            self.stats["tokens"] += len(out)
+            if req.on_tokens is not None:
+                req.on_tokens(out)
+
+    def _reap(self):
+        keep = []
+        for r in self.running:
+            if r.done:
+                r.t_done = time.perf_counter()
+                self.rt.release(r.slot)
+                r.done_event.set()
+                if r.on_tokens is not None:
+                    r.on_tokens(None)
+            else:
+                keep.append(r)
+        self.running = keep
+
+    # ------------------------------------------------------------------ one decode forward
+    def _decode(self):
+        reqs = self.running
+        slots = [r.slot for r in reqs]
+        n, blk, K = self.n, self.blk, self.n - 1
+        if self.mode == "causal":
+            toks = [[r.output[-1] if r.output else r.t0] for r in reqs]
+            logits = self.rt.canvas(slots, toks, 1)
+            self.rt.commit(slots, [1] * len(reqs))
+            self.stats["forwards"] += 1
+            for b, r in enumerate(reqs):
+                r.forwards += 1
+                self._emit(r, self._pick(logits[b], r))
+            self._reap()
+            return
+        canv = []
+        for r in reqs:
+            if r.specs is not None:
+                canv.append([r.pending] + r.specs + [self.mask_id] * (n - 1))
+            else:
+                canv.append([r.t0] + [self.mask_id] * (blk - 1))
+        logits = self.rt.canvas(slots, canv, n)
+        self.stats["forwards"] += 1
+        greedy = all(r.sampling.greedy for r in reqs)
+        am = logits.argmax(-1).tolist() if greedy else None
+        adv = []
+        for b, r in enumerate(reqs):
+            r.forwards += 1
+            if r.specs is not None:
+                acc, corr, clean, new_specs, new_q = self._verify(r, logits[b], am[b] if greedy else None)
+                if corr is not None:
+                    adv.append(1 + acc)
+                    r.accept_hist[acc] += 1
+                    self._emit(r, r.specs[:acc] + [corr])
+                    r.t0, r.t0_emitted = corr, True
+                    r.pending, r.specs, r.spec_q = None, None, None
+                else:
+                    adv.append(n)
+                    r.accept_hist[K] += 1
+                    self._emit(r, r.specs + [clean])
+                    r.pending, r.specs, r.spec_q = clean, new_specs, new_q
+            else:
+                if r.sampling.greedy:
+                    vals = am[b][:n] if greedy else logits[b, :n].argmax(-1).tolist()
+                    new_q = None
+                else:
+                    P = truncated_probs(logits[b, :n], r.sampling)
+                    vals = torch.multinomial(P, 1, generator=r.gen).squeeze(-1).tolist()
+                    new_q = P[1:n]
+                clean, new_specs = vals[0], vals[1:n]
+                adv.append(1)
+                self._emit(r, ([] if r.t0_emitted else [r.t0]) + [clean])
+                r.t0_emitted = True
+                r.pending, r.specs, r.spec_q = clean, new_specs, new_q
+        self.rt.commit(slots, adv)
+        self._reap()
+
+    def _verify(self, r, L, am):
+        n, blk, K = self.n, self.blk, self.n - 1
+        if r.sampling.greedy:
+            vals = am if am is not None else L.argmax(-1).tolist()
+            acc = 0
+            while acc < K and vals[acc] == r.specs[acc]:
+                acc += 1
+            corr = vals[acc] if acc < K else None
+            return acc, corr, vals[n - 1], vals[n:blk], None
+        P = truncated_probs(L, r.sampling)
+        sv = torch.tensor(r.specs, device=L.device)
+        p = P[:K].gather(1, sv[:, None])[:, 0]
+        q = r.spec_q.gather(1, sv[:, None])[:, 0]
+        ratio = torch.where(q > 0, p / q.clamp_min(1e-30), torch.zeros_like(p))
+        u = torch.rand(K, device=L.device, generator=r.gen)
+        accepted = ((ratio >= 1.0) | (u < ratio)).tolist()
+        acc = 0
+        while acc < K and accepted[acc]:
+            acc += 1
+        if acc < K:
+            resid = (P[acc] - r.spec_q[acc]).clamp_min(0.0)
+            rs = resid.sum()
+            resid = resid / rs if rs > 0 else P[acc]
+            corr = int(torch.multinomial(resid, 1, generator=r.gen))
+            return acc, corr, None, None, None
+        samp = torch.multinomial(P[n - 1:blk], 1, generator=r.gen).squeeze(-1).tolist()
+        return acc, None, samp[0], samp[1:], P[n:blk]
+
+    # ------------------------------------------------------------------ stats
+    def summary(self, reqs):
+        toks = sum(len(r.output) for r in reqs)
+        fwd = sum(r.forwards for r in reqs)
+        ttft = sorted((r.t_first - r.t_submit) for r in reqs if r.t_first is not None)
+        return {"tokens": toks, "forwards": fwd, "tokens_per_forward": toks / max(fwd, 1),
+                "p50_ttft_s": ttft[len(ttft) // 2] if ttft else None}

@@ -1,0 +1,312 @@
+"""Slot-based inference runtime: KV / gated-delta caches and the batched canvas step.
+
+The decode step of the self-speculative engine is one forward over a *canvas* of ``blk`` rows per
+active request: rows ``< n_clean`` are token-causal, the remaining rows see the whole canvas, and
+every row sees the request's cached prefix.  Full-attention layers append the canvas K/V to the
+slot's cache rows ``pos .. pos+blk`` (a later commit keeps the first ``adv``); gated-delta layers
+run the recurrence from the slot's cached state (clean rows read their own state, the rest read
+the state after the last row) and the commit advances that state and the conv window by ``adv``
+rows.  Reference semantics: ``inference/zoro-1/mlx/trida_mlx/model.py:282-330`` (canvas GDN),
+``:461-470`` (canvas mask), ``:486-507`` (commit); the reference serves through vLLM / SGLang
+(``inference/zoro-1/vllm/vllm_native_diffusion/qwen3_5_diffusion.py:1337-2094``).
+
+A prompt is prefilled as a sequence of fully causal canvas steps (``n_clean = blk``) of at most
+``PREFILL_CHUNK`` rows each, so prefill and decode share one code path.  On CUDA every op runs on
+the extension's kernels; on CPU the same step is stated in PyTorch (the oracle of the GPU path and
+the runtime of the CPU tests).
+"""
+import math
+
+import torch
+import torch.nn.functional as F
+
+from ..ops import gdn_reference as G
+from ..ops import reference as R
+
+PREFILL_CHUNK = 64
+
+
+class Runtime:
+    def __init__(self, decoder, max_slots=8, max_len=4096, device=None):
+        self.dec = decoder
+        self.cfg = cfg = decoder.cfg
+        p = next(decoder.parameters())
+        self.device = torch.device(device) if device is not None else p.device
+        self.dtype = p.dtype
+        self.cuda = self.device.type == "cuda"
+        self.max_slots, self.max_len = max_slots, max_len
+        self.kinds = [l.layer_type for l in decoder.layers]
+        d, Hkv = cfg.head_dim, cfg.n_kv_heads
+        self.kc, self.vc, self.ssm, self.win = {}, {}, {}, {}
+        for i, kind in enumerate(self.kinds):
+            if kind == "full_attention":
+                self.kc[i] = torch.zeros(max_slots, max_len, Hkv, d, dtype=self.dtype, device=self.device)
+                self.vc[i] = torch.zeros(max_slots, max_len, Hkv, d, dtype=self.dtype, device=self.device)
+            else:
+                Cc = 2 * cfg.lin_k_heads * cfg.lin_k_dim + cfg.lin_v_heads * cfg.lin_v_dim
+                self.ssm[i] = torch.zeros(max_slots, cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim,
+                                          dtype=torch.float32, device=self.device)
+                self.win[i] = torch.zeros(max_slots, cfg.conv_kernel - 1, Cc, dtype=self.dtype, device=self.device)
+        self.pos = [0] * max_slots
+        self.free = list(range(max_slots))[::-1]
+        self.pending = None
+        if self.cuda:
+            from ..ops import blocks
+            from ..ops._ext import ext
+            self.C = ext()
+            self.cos_t, self.sin_t = blocks.rope_tables(max_len, cfg.rotary_dim, cfg.rope_theta, self.device)
+            self.blocks = blocks
+            self._gdn_f32 = {i: (decoder.layers[i].A_log.float().contiguous(),
+                                 decoder.layers[i].dt_bias.float().contiguous()) for i in self.ssm}
+
+    # ------------------------------------------------------------------ slots
+    def alloc(self):
+        if not self.free:
+            raise RuntimeError("no free cache slot")
+        s = self.free.pop()
+        self.pos[s] = 0
+        for i in self.ssm:
+            self.ssm[i][s].zero_()
+            self.win[i][s].zero_()
+        return s
+
+    def release(self, s):
+        self.pos[s] = 0
+        self.free.append(s)
+
+    # ------------------------------------------------------------------ public steps
+    @torch.no_grad()
+    def prefill(self, slots, prompts):
+        """Feed equal-length prompts into fresh slots; returns fp32 logits of each last token [B, V]."""
+        L = len(prompts[0])
+        assert all(len(p) == L for p in prompts) and L >= 1
+        ids = torch.tensor(prompts, dtype=torch.long, device=self.device)
+        out = None
+        for c0 in range(0, L, PREFILL_CHUNK):
+            n = min(PREFILL_CHUNK, L - c0)
+            last = c0 + n == L
+            logits = self.canvas(slots, ids[:, c0:c0 + n], n, rows=(n - 1, n) if last else (0, 0))
+            self.commit(slots, [n] * len(slots))
+            if last:
+                out = logits[:, 0]
+        return out
+
+    @torch.no_grad()
+    def canvas(self, slots, tokens, n_clean, rows=None):
+        """One forward over a [B, blk] canvas per slot.  Returns fp32 logits [B, r1 - r0, V] for the
+        canvas rows ``rows = (r0, r1)`` (all rows by default).  Call ``commit`` afterwards."""
+        assert self.pending is None, "commit the previous canvas first"
+        tokens = torch.as_tensor(tokens, dtype=torch.long, device=self.device)
+        B, blk = tokens.shape
+        for s in slots:
+            if self.pos[s] + blk > self.max_len:
+                raise RuntimeError(f"slot {s}: sequence exceeds the cache length {self.max_len}")
+        r0, r1 = rows if rows is not None else (0, blk)
+        st = _Step(self, slots, B, blk, n_clean)
+        x = self.dec.embed_tokens(tokens.reshape(-1)) if self.cuda else self.dec.embed[tokens.reshape(-1)]
+        for i, layer in enumerate(self.dec.layers):
+            if self.kinds[i] == "full_attention":
+                x = self._attn(st, i, layer, x)
+            else:
+                x = self._gdn(st, i, layer, x)
+            x = self._mlp(layer, x)
+        self.pending = st
+        if r1 <= r0:
+            return torch.empty(B, 0, self.cfg.vocab_size, device=self.device)
+        h = x.view(B, blk, -1)[:, r0:r1].reshape(B * (r1 - r0), -1)
+        return self._logits(h).view(B, r1 - r0, -1)
+
+    @torch.no_grad()
+    def commit(self, slots, adv):
+        """Keep the first ``adv[b]`` canvas rows of every slot (1 <= adv <= n_clean)."""
+        st = self.pending
+        assert st is not None and list(slots) == list(st.slots)
+        assert all(1 <= a <= st.n_clean for a in adv)
+        if self.cuda:
+            adv_t = torch.tensor(adv, dtype=torch.int32, device=self.device)
+        cfg = self.cfg
+        for i, rec in st.gdn.items():
+            layer = self.dec.layers[i]
+            if self.cuda:
+                mixed, ga, gb, proj = rec
+                a_log, dtb = self._gdn_f32[i]
+                self.C.gdn_commit(mixed, ga, gb, a_log, dtb, self.ssm[i], st.slot_t, adv_t, st.blk,
+                                  cfg.lin_k_heads, cfg.lin_v_heads, cfg.lin_k_dim ** -0.5)
+                Cc = mixed.shape[1]
+                self.C.conv_commit(proj[:, :Cc], st.blk, self.win[i], st.slot_t, adv_t)
+            else:
+                q, k, v, g, beta, conv_in = rec
+                for b, s in enumerate(st.slots):
+                    S = self.ssm[i][s].clone()
+                    for t in range(adv[b]):
+                        S, _ = G._step(S, q[b, t], k[b, t], v[b, t], g[b, t], beta[b, t])
+                    self.ssm[i][s] = S
+                    K1 = cfg.conv_kernel - 1
+                    self.win[i][s] = conv_in[b, adv[b]:adv[b] + K1]
+        for b, s in enumerate(st.slots):
+            self.pos[s] += adv[b]
+        self.pending = None
+
+    # ------------------------------------------------------------------ layers
+    def _rms(self, x, w):
+        if self.cuda:
+            h = torch.empty_like(x)
+            self.C.rmsnorm_fwd(x, w, self.cfg.eps, h)
+            return h
+        return R.rmsnorm(x, w, self.cfg.eps)
+
+    def _lin(self, x, w, residual=None):
+        if self.cuda:
+            out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+            if residual is None:
+                self.blocks.gemm(self.blocks.TN, x, w, out)
+            else:
+                self.blocks.gemm(self.blocks.TN, x, w, out, residual, 1.0, 1.0)
+            return out
+        y = x @ w.t()
+        return y if residual is None else residual + y
+
+    def _mlp(self, layer, x):
+        h = self._rms(x, layer.post_norm)
+        gu = self._lin(h, layer.wgu)
+        if self.cuda:
+            a = torch.empty(gu.shape[0], gu.shape[1] // 2, dtype=gu.dtype, device=gu.device)
+            self.C.swiglu_fwd(gu, a)
+        else:
+            a = R.swiglu(gu)
+        return self._lin(a, layer.wdown, x)
+
+    def _logits(self, h):
+        h = self._rms(h, self.dec.norm)
+        W = self.dec.lm_weight
+        if self.cuda:
+            out = torch.empty(h.shape[0], W.shape[0], dtype=torch.float32, device=h.device)
+            self.blocks.gemm(self.blocks.TN, h, W, out)
+            return out
+        return (h @ W.t()).float()
+
+    def _attn(self, st, i, layer, x):
+        cfg = self.cfg
+        B, blk = st.B, st.blk
+        Hq, Hkv, d = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        qs = 2 * d if cfg.attn_output_gate else d
+        h = self._rms(x, layer.input_norm)
+        qkv = self._lin(h, layer.wqkv)
+        M = B * blk
+        if self.cuda:
+            q = torch.empty(M, Hq, d, dtype=x.dtype, device=x.device)
+            k = torch.empty(M, Hkv, d, dtype=x.dtype, device=x.device)
+            self.C.qk_norm_rope_fwd(qkv, layer.q_norm, layer.k_norm, self.cos_t, self.sin_t, st.rowpos32, q, k,
+                                    Hq, Hkv, d, cfg.rotary_dim, cfg.eps, qs)
+            v = qkv[:, Hq * qs + Hkv * d:]
+            self.C.kv_append(k, v, self.kc[i], self.vc[i], st.slot_t, st.pos_t, blk)
+            o = torch.empty(M, Hq, d, dtype=x.dtype, device=x.device)
+            self.C.canvas_attention(q, self.kc[i], self.vc[i], st.slot_t, st.pos_t, o, blk, st.n_clean, st.max_keys,
+                                    1.0 / math.sqrt(d))
+            o = o.view(M, Hq * d)
+            if cfg.attn_output_gate:
+                og = torch.empty_like(o)
+                self.C.attn_gate_fwd(o, qkv, og, Hq, d)
+                o = og
+            return self._lin(o, layer.wo, x)
+        # CPU statement
+        if cfg.attn_output_gate:
+            qg = qkv[:, :2 * Hq * d].view(M, Hq, 2 * d)
+            q, gate = qg[..., :d], qg[..., d:].reshape(M, Hq * d)
+        else:
+            q, gate = qkv[:, :Hq * d].view(M, Hq, d), None
+        k = qkv[:, Hq * qs:Hq * qs + Hkv * d].view(M, Hkv, d)
+        v = qkv[:, Hq * qs + Hkv * d:].view(M, Hkv, d)
+        q = R.rmsnorm(q, layer.q_norm, cfg.eps)
+        k = R.rmsnorm(k, layer.k_norm, cfg.eps)
+        cos, sin = R.rope_cos_sin(st.rowpos, d, cfg.rope_theta, cfg.rotary_dim)
+        q = R.apply_rope(q.float()[None], cos[None], sin[None])[0].to(x.dtype)
+        k = R.apply_rope(k.float()[None], cos[None], sin[None])[0].to(x.dtype)
+        q, k, v = q.view(B, blk, Hq, d), k.view(B, blk, Hkv, d), v.view(B, blk, Hkv, d)
+        outs = []
+        G_ = Hq // Hkv
+        r = torch.arange(blk)[:, None]
+        c = torch.arange(blk)[None, :]
+        inner = (c <= r) | (r >= st.n_clean)
+        for b, s in enumerate(st.slots):
+            p0 = self.pos[s]
+            self.kc[i][s, p0:p0 + blk] = k[b]
+            self.vc[i][s, p0:p0 + blk] = v[b]
+            K = self.kc[i][s, :p0 + blk].float().repeat_interleave(G_, 1)       # [Lk, Hq, d]
+            V = self.vc[i][s, :p0 + blk].float().repeat_interleave(G_, 1)
+            sc = torch.einsum("thd,khd->htk", q[b].float(), K) / math.sqrt(d)
+            mask = torch.cat([torch.ones(blk, p0, dtype=torch.bool), inner], 1)
+            sc = sc.masked_fill(~mask[None], float("-inf"))
+            outs.append(torch.einsum("htk,khd->thd", sc.softmax(-1), V))
+        o = torch.stack(outs).reshape(M, Hq * d).to(x.dtype)
+        if gate is not None:
+            o = o * torch.sigmoid(gate.float()).to(o.dtype)
+        return self._lin(o, layer.wo, x)
+
+    def _gdn(self, st, i, layer, x):
+        cfg = self.cfg
+        B, blk = st.B, st.blk
+        Hk, Hv, dk, dv = cfg.lin_k_heads, cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim
+        kd, vd = Hk * dk, Hv * dv
+        Cc = 2 * kd + vd
+        M = B * blk
+        h = self._rms(x, layer.input_norm)
+        proj = self._lin(h, layer.w_in)
+        z = proj[:, Cc:Cc + vd]
+        gb = proj[:, Cc + vd:Cc + vd + Hv]
+        ga = proj[:, Cc + vd + Hv:Cc + vd + 2 * Hv]
+        if self.cuda:
+            mixed = torch.empty(M, Cc, dtype=x.dtype, device=x.device)
+            self.C.canvas_conv(proj[:, :Cc], self.win[i], layer.conv_w, mixed, st.slot_t, blk)
+            a_log, dtb = self._gdn_f32[i]
+            o = torch.empty(M, vd, dtype=x.dtype, device=x.device)
+            self.C.gdn_canvas(mixed, ga, gb, a_log, dtb, o, self.ssm[i], st.slot_t, blk, Hk, Hv, st.n_clean, dk ** -0.5)
+            y = torch.empty(M, vd, dtype=x.dtype, device=x.device)
+            self.C.gdn_gnorm_fwd(o, z, layer.gnorm, y, Hv, cfg.eps)
+            st.gdn[i] = (mixed, ga, gb, proj)
+            return self._lin(y, layer.w_out, x)
+        # CPU statement
+        K1 = cfg.conv_kernel - 1
+        qkv = proj[:, :Cc].view(B, blk, Cc)
+        win = torch.stack([self.win[i][s] for s in st.slots])                  # [B, K-1, Cc]
+        conv_in = torch.cat([win.to(qkv.dtype), qkv], 1)                       # [B, K-1+blk, Cc]
+        w = layer.conv_w.float()
+        acc = sum(conv_in[:, j:j + blk].float() * w[:, j] for j in range(cfg.conv_kernel))
+        mixed = F.silu(acc).to(x.dtype)
+        q = G.l2norm(mixed[..., :kd].reshape(B, blk, Hk, dk).float()) * dk ** -0.5
+        k = G.l2norm(mixed[..., kd:2 * kd].reshape(B, blk, Hk, dk).float())
+        v = mixed[..., 2 * kd:].reshape(B, blk, Hv, dv).float()
+        rep = Hv // Hk
+        if rep > 1:
+            q, k = q.repeat_interleave(rep, 2), k.repeat_interleave(rep, 2)
+        g, beta = G.gates(ga.reshape(B, blk, Hv), gb.reshape(B, blk, Hv), layer.A_log, layer.dt_bias)
+        outs = []
+        for b, s in enumerate(st.slots):
+            S = self.ssm[i][s].clone()
+            ob = []
+            for t in range(blk):
+                S, o_t = G._step(S, q[b, t], k[b, t], v[b, t], g[b, t], beta[b, t])
+                ob.append(o_t)
+            for t in range(st.n_clean, blk):
+                ob[t] = torch.einsum("hkv,hk->hv", S, q[b, t])
+            outs.append(torch.stack(ob))
+        o = torch.stack(outs).to(x.dtype)                                      # [B, blk, Hv, dv]
+        y = G.gated_rmsnorm(o, z.reshape(B, blk, Hv, dv), layer.gnorm, cfg.eps)
+        st.gdn[i] = (q, k, v, g, beta, conv_in)
+        return self._lin(y.reshape(M, vd), layer.w_out, x)
+
+
+class _Step:
+    """Per-canvas bookkeeping shared by the layers and kept until the commit."""
+
+    def __init__(self, rt, slots, B, blk, n_clean):
+        self.slots, self.B, self.blk, self.n_clean = list(slots), B, blk, n_clean
+        pos = [rt.pos[s] for s in self.slots]
+        self.max_keys = max(pos) + blk
+        self.rowpos = torch.tensor([p + j for p in pos for j in range(blk)], dtype=torch.long)
+        self.gdn = {}
+        if rt.cuda:
+            dev = rt.device
+            self.slot_t = torch.tensor(self.slots, dtype=torch.int32, device=dev)
+            self.pos_t = torch.tensor(pos, dtype=torch.int32, device=dev)
+            self.rowpos32 = self.rowpos.to(dev, torch.int32)
