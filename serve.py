@@ -1,0 +1,133 @@
+#!/usr/bin/env python3
+"""Serve a Trida checkpoint over HTTP with the native engine (OpenAI-compatible + decisions).
+
+    python serve.py [model] --mode {self-spec,causal,decide} --port 30000 [--config decode.yaml]
+
+Flags follow the reference launcher (``inference/zoro-1/serve.py:193-222``); model resolution:
+positional > ``$TRIDA_DECIDE_MODEL`` (decide) > ``$TRIDA_MODEL``.  Checkpoints are local HF
+directories (``config.json`` + safetensors [+ ``decision_head.pt`` / ``jev_head.pt``,
+``temperature.json``, ``block_diffusion.json``]).  ``--random-init CONFIG_JSON`` serves a
+random-initialised model of that architecture (smoke tests without weights).
+
+Decode config (YAML, keys of ``configs/zoro1_self_spec_b15_g8.yaml``): ``block_size`` (canvas
+rows, 2N-1), ``gen_block_size`` (N), ``mask_id``, ``temperature``, ``top_k``, ``top_p``.
+One process serves one engine; ``--tp`` other than 1 is rejected here.
+"""
+import argparse
+import json
+import os
+import sys
+
+MODES = ("self-spec", "causal", "decide")
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("model", nargs="?", default=None)
+    ap.add_argument("--mode", default="self-spec", choices=MODES)
+    ap.add_argument("--port", type=int, default=30000)
+    ap.add_argument("--host", default="0.0.0.0")
+    ap.add_argument("--tp", type=int, default=1)
+    ap.add_argument("--mem-fraction", type=float, default=0.8)
+    ap.add_argument("--max-running", type=int, default=32)
+    ap.add_argument("--max-len", type=int, default=8192)
+    ap.add_argument("--cuda-graph-bs", default="1 2 4 8")
+    ap.add_argument("--dtype", default="bfloat16", choices=["bfloat16", "float32"])
+    ap.add_argument("--config", default=None, help="decode YAML (block_size, gen_block_size, mask_id, ...)")
+    ap.add_argument("--reasoning-parser", default="qwen3", choices=["qwen3", "deepseek-r1"])
+    ap.add_argument("--log", default=None)
+    ap.add_argument("--no-stats", action="store_true")
+    ap.add_argument("--no-shape", action="store_true")
+    ap.add_argument("--dry-run", action="store_true")
+    ap.add_argument("--random-init", default=None, help="serve a random-init model of this config.json")
+    ap.add_argument("--device", default=None)
+    return ap.parse_args(argv)
+
+
+def resolve_model(args):
+    if args.model:
+        return args.model
+    if args.mode == "decide" and os.environ.get("TRIDA_DECIDE_MODEL"):
+        return os.environ["TRIDA_DECIDE_MODEL"]
+    return os.environ.get("TRIDA_MODEL")
+
+
+def decode_config(path):
+    if not path:
+        return {}
+    import yaml
+    with open(path) as f:
+        return yaml.safe_load(f) or {}
+
+
+def build(args):
+    """(engine, tokenizer, model name, decider) for the arguments."""
+    import torch
+
+    from trida_stack_b200.models import Decoder, ModelConfig
+    from trida_stack_b200.models.build import MASK_TOKEN, load_decoder, load_tokenizer
+    from trida_stack_b200.serve import Engine, Runtime
+    dev = args.device or ("cuda" if torch.cuda.is_available() else "cpu")
+    dtype = torch.bfloat16 if args.dtype == "bfloat16" else torch.float32
+    path = resolve_model(args)
+    tok = None
+    if args.random_init:
+        with open(args.random_init) as f:
+            cfg = ModelConfig.from_hf_dict(json.load(f))
+        dec = Decoder(cfg, dtype=dtype, device=dev)
+        name = "random-init"
+    else:
+        if not path or not os.path.isdir(path):
+            raise SystemExit(f"model directory not found: {path!r} (give a local checkpoint directory)")
+        tok = load_tokenizer(path)
+        if args.mode == "decide":
+            dec = None          # the decision model below owns the decoder
+        else:
+            dec, _ = load_decoder(path, dev, dtype, tokenizer=tok, add_mask=args.mode != "causal")
+        name = os.path.basename(os.path.normpath(path))
+    dcfg = decode_config(args.config)
+    mask_id = dcfg.get("mask_id")
+    if mask_id is None and tok is not None:
+        mask_id = tok.convert_tokens_to_ids(MASK_TOKEN)
+    if mask_id is None and path and os.path.isfile(os.path.join(path, "block_diffusion.json")):
+        with open(os.path.join(path, "block_diffusion.json")) as f:
+            mask_id = json.load(f).get("mask_id")
+    n = int(dcfg.get("gen_block_size", (int(dcfg.get("block_size", 7)) + 1) // 2))
+    decider = None
+    if args.mode == "decide":
+        from trida_stack_b200.cli import build_parser
+        from trida_stack_b200.models.build import build_model
+        from trida_stack_b200.serve.decide import DecideEngine
+        ns = build_parser().parse_args(["--model_id", path, "--ar_only", "--decision_data", "serving"])
+        model = build_model(ns, torch.device(dev)).eval()
+        decider = DecideEngine(model, tok, DecideEngine.temperatures_from(path))
+        dec = model.decoder
+    if mask_id is None:
+        mask_id = dec.cfg.vocab_size - 1
+    rt = Runtime(dec, max_slots=args.max_running, max_len=args.max_len, device=dev)
+    engine = Engine(rt, mask_id=mask_id, mode="causal" if args.mode != "self-spec" else "self-spec", n=n,
+                    max_running=args.max_running)
+    return engine, tok, name, decider
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    if args.tp != 1:
+        raise SystemExit("serve.py runs one engine per process (--tp 1)")
+    if args.dry_run:
+        print(json.dumps({"model": resolve_model(args), "mode": args.mode, "port": args.port, "host": args.host,
+                          "config": decode_config(args.config)}))
+        return 0
+    engine, tok, name, decider = build(args)
+    if tok is None:
+        raise SystemExit("the HTTP server needs a tokenizer in the checkpoint directory")
+    from trida_stack_b200.serve.server import build_app
+    import uvicorn
+    engine.start()
+    app = build_app(engine, tok, name, decider)
+    uvicorn.run(app, host=args.host, port=args.port, log_level="warning")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

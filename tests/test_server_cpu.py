@@ -1,0 +1,96 @@
+"""HTTP server (OpenAI-compatible + System One) over the native engine, on CPU."""
+import json
+import socket
+import threading
+import time
+
+import pytest
+import requests
+
+from helpers import make_tokenizer
+from test_hybrid_cpu import tiny_qwen35
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+@pytest.fixture(scope="module")
+def server(tmp_path_factory):
+    import uvicorn
+
+    import serve as serve_cli
+    from trida_stack_b200.serve.server import build_app
+    path = tmp_path_factory.mktemp("ckpt")
+    tiny_qwen35(str(path))            # hybrid checkpoint (the decision head rides on the hybrid model)
+    tok = make_tokenizer(str(path), 295)
+    from trida_stack_b200.data.decision import SPECIAL
+    tok.add_special_tokens({"additional_special_tokens": SPECIAL})   # ids 295..299
+    tok.save_pretrained(str(path))
+    args = serve_cli.parse_args([str(path), "--mode", "decide", "--device", "cpu", "--dtype", "float32",
+                                 "--max-running", "4", "--max-len", "512"])
+    engine, tok, name, decider = serve_cli.build(args)
+    engine.start()
+    port = _free_port()
+    cfg = uvicorn.Config(build_app(engine, tok, name, decider), host="127.0.0.1", port=port, log_level="error")
+    srv = uvicorn.Server(cfg)
+    th = threading.Thread(target=srv.run, daemon=True)
+    th.start()
+    url = f"http://127.0.0.1:{port}"
+    for _ in range(200):
+        try:
+            if requests.get(url + "/health", timeout=1).ok:
+                break
+        except requests.ConnectionError:
+            time.sleep(0.05)
+    yield url
+    srv.should_exit = True
+    engine.stop()
+
+
+def test_models_and_health(server):
+    assert requests.get(server + "/health").json()["status"] == "ok"
+    data = requests.get(server + "/v1/models").json()["data"]
+    assert data and data[0]["object"] == "model"
+
+
+def test_completion_and_chat(server):
+    r = requests.post(server + "/v1/completions", json={"prompt": "t1 t2 t3 t4", "max_tokens": 6}).json()
+    assert r["usage"]["prompt_tokens"] == 4 and r["usage"]["completion_tokens"] <= 6
+    assert r["choices"][0]["finish_reason"] in ("stop", "length")
+    r = requests.post(server + "/v1/chat/completions",
+                      json={"messages": [{"role": "user", "content": "t5 t6"}], "max_tokens": 5}).json()
+    assert r["object"] == "chat.completion" and r["choices"][0]["message"]["role"] == "assistant"
+    assert r["usage"]["completion_tokens"] <= 5
+
+
+def test_chat_streaming(server):
+    with requests.post(server + "/v1/chat/completions", stream=True,
+                       json={"messages": [{"role": "user", "content": "t7"}], "max_tokens": 5, "stream": True}) as r:
+        lines = [l for l in r.iter_lines(decode_unicode=True) if l]
+    assert lines[-1] == "data: [DONE]"
+    last = json.loads(lines[-2][6:])
+    assert last["choices"][0]["finish_reason"] in ("stop", "length") and "usage" in last
+
+
+def test_systemone_decisions_and_validation(server):
+    body = {"state": {"user": "t1 t2"}, "questions": {
+        "q1": {"type": "choice", "instructions": "pick", "criteria": {"a": "t3", "b": "t4", "c": "t5"}},
+        "q2": {"type": "noul", "criteria": {"true": "t6", "false": "t7"}},
+        "q3": {"type": "score", "criteria": ["low", "mid", "high"]}}}
+    r = requests.post(server + "/v1/systemone", json=body)
+    assert r.status_code == 200, r.text
+    ans = r.json()["answers"]
+    assert ans["q1"]["choice"] in ("a", "b", "c")
+    assert abs(sum(ans["q1"]["probabilities"].values()) - 1) < 1e-4
+    assert isinstance(ans["q2"]["noul"], bool)
+    assert ans["q3"]["score"] in (0, 1, 2)
+    bad = requests.post(server + "/v1/systemone", json={"state": {}, "questions": {"q": {"type": "pick"}}})
+    assert bad.status_code == 422
+    assert bad.json()["detail"][0]["loc"][-1] == "type"
+    alias = requests.post(server + "/v1/decide", json={"request": body})
+    assert alias.status_code == 200 and set(alias.json()["answers"]) == {"q1", "q2", "q3"}

@@ -77,6 +77,10 @@ class DecideEngine:
         """``model``: a BlockDiffusionLM / HybridBlockDiffusionLM with a decision head."""
         if model.decision_head is None:
             raise ValueError("decide mode needs a checkpoint with a decision head (decision_head.pt)")
+        from ..data.decision import SPECIAL
+        missing = [t for t in SPECIAL if tokenizer.convert_tokens_to_ids(t) in (None, tokenizer.unk_token_id)]
+        if missing:
+            raise ValueError(f"tokenizer lacks the decision control tokens {missing}")
         self.model, self.tok = model, tokenizer
         self.temps = {"noul": 1.0, "choice": 1.0, "score": 1.0}
         self.temps.update(temperatures or {})
