@@ -45,6 +45,7 @@ def main():
     ap.add_argument("--mode", default="self-spec", choices=["self-spec", "causal"])
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-graphs", action="store_true", help="launch every kernel eagerly (no CUDA graphs)")
     args = ap.parse_args()
 
     from trida_stack_b200.models import Decoder
@@ -55,14 +56,14 @@ def main():
     mask_id = cfg.vocab_size - 1
     max_len = args.prompt + args.max_new + 2 * args.n + 8
     rt = Runtime(dec, max_slots=args.requests, max_len=max_len)
-    eng = Engine(rt, mask_id=mask_id, mode=args.mode, n=args.n, max_running=args.requests)
+    eng = Engine(rt, mask_id=mask_id, mode=args.mode, n=args.n, max_running=args.requests, graphs=not args.no_graphs)
     g = torch.Generator().manual_seed(args.seed)
 
     def prompts(k):
         return [torch.randint(0, cfg.vocab_size - 2, (args.prompt,), generator=g).tolist() for _ in range(k)]
 
-    # warm-up: a short run through every kernel shape
-    eng.generate(prompts(min(4, args.requests)), max_new_tokens=8)
+    # warm-up: a short run at the full batch (captures the decode graph of that batch size)
+    eng.generate(prompts(args.requests), max_new_tokens=6)
     torch.cuda.synchronize()
 
     reqs = [eng.submit(__import__("trida_stack_b200.serve", fromlist=["Request"]).Request(
@@ -91,7 +92,8 @@ def main():
         "ms_per_step": round(decode_ms / max(steps, 1), 3), "wall_s": round(wall, 2), "tp": 1,
         "config": {"model": f"Qwen3.5-4B-style hybrid ({args.layers}L)", "requests": args.requests,
                    "prompt": args.prompt, "max_new": args.max_new, "mode": args.mode, "n": args.n,
-                   "canvas_rows": 2 * args.n - 1 if args.mode == "self-spec" else 1, "greedy": True},
+                   "canvas_rows": 2 * args.n - 1 if args.mode == "self-spec" else 1, "greedy": True,
+                   "cuda_graphs": not args.no_graphs},
         "data": "synthetic uniform prompts, random-init weights", "dtype": "bf16"}))
 
 

@@ -69,7 +69,11 @@ void gemm(int64_t layout, const at::Tensor& A, const at::Tensor& B, const at::Te
   TORCH_CHECK(((uintptr_t)a.A % 16 == 0) && ((uintptr_t)a.B % 16 == 0) && ((uintptr_t)a.D % 16 == 0),
               "GEMM operands must be 16-byte aligned");
   c10::cuda::CUDAGuard g(A.device());
-  const int rc = trida::gemm_bf16((trida::GemmLayout)layout, f32, a, (int)tile, sm_count(), stream());
+  const int splits = trida::gemm_splitk(M, N, K, sm_count());
+  at::Tensor ws;
+  if (splits > 1) ws = at::empty({(int64_t)splits * M * N}, A.options().dtype(at::kFloat));
+  const int rc = trida::gemm_bf16((trida::GemmLayout)layout, f32, a, (int)tile, sm_count(), stream(), splits,
+                                  splits > 1 ? ws.data_ptr<float>() : nullptr);
   TORCH_CHECK(rc == 0, "sm100 GEMM failed with code ", rc, " (M=", M, " N=", N, " K=", K, " layout=", layout, ")");
 }
 
@@ -231,30 +235,35 @@ void conv_commit(const at::Tensor& x, int64_t rows_per, const at::Tensor& win, c
                      stream());
 }
 
+int64_t gdn_prep_numel(int64_t rows, int64_t Hk, int64_t Hv) { return trida::gdn_prep_floats(rows, Hk, Hv); }
+
+// State cache: fp32 [slots, Hv, 128 * 128] in the kernels' thread-native order.
 void gdn_canvas(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor& gb, const at::Tensor& A_log,
-                const at::Tensor& dt_bias, const at::Tensor& o, const at::Tensor& ssm, const at::Tensor& slot,
-                int64_t blk, int64_t Hk, int64_t Hv, int64_t n_clean, double scale) {
+                const at::Tensor& dt_bias, const at::Tensor& o, const at::Tensor& prep, const at::Tensor& ssm,
+                const at::Tensor& slot, int64_t blk, int64_t Hk, int64_t Hv, int64_t n_clean, double scale) {
   const int64_t B = mixed.size(0) / blk;
   auto p = gdn_params(mixed, ga, gb, A_log, dt_bias, c10::nullopt, B, blk, Hk, Hv, 0, blk, 0, 32, true, false, scale);
   CHECK_BF16(o); TORCH_CHECK(o.is_contiguous() && o.numel() == B * blk * Hv * 128, "o layout");
   TORCH_CHECK(ssm.scalar_type() == at::kFloat && ssm.is_contiguous() && ssm.size(1) == Hv, "state cache layout");
+  TORCH_CHECK(prep.scalar_type() == at::kFloat && prep.numel() >= trida::gdn_prep_floats(B * blk, Hk, Hv), "prep size");
   check_i32(slot, B, "slot");
   p.o = mbf(o);
   c10::cuda::CUDAGuard g(mixed.device());
-  TORCH_CHECK(trida::gdn_canvas(p, ssm.data_ptr<float>(), slot.data_ptr<int>(), n_clean, stream()) == 0,
-              "gdn_canvas failed");
+  TORCH_CHECK(trida::gdn_canvas(p, prep.data_ptr<float>(), ssm.data_ptr<float>(), slot.data_ptr<int>(), n_clean,
+                                stream()) == 0, "gdn_canvas failed");
 }
 
 void gdn_commit(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor& gb, const at::Tensor& A_log,
-                const at::Tensor& dt_bias, const at::Tensor& ssm, const at::Tensor& slot, const at::Tensor& adv,
-                int64_t blk, int64_t Hk, int64_t Hv, double scale) {
+                const at::Tensor& dt_bias, const at::Tensor& prep, const at::Tensor& ssm, const at::Tensor& slot,
+                const at::Tensor& adv, int64_t blk, int64_t Hk, int64_t Hv, double scale) {
   const int64_t B = mixed.size(0) / blk;
   auto p = gdn_params(mixed, ga, gb, A_log, dt_bias, c10::nullopt, B, blk, Hk, Hv, 0, blk, 0, 32, true, false, scale);
   TORCH_CHECK(ssm.scalar_type() == at::kFloat && ssm.is_contiguous() && ssm.size(1) == Hv, "state cache layout");
+  TORCH_CHECK(prep.scalar_type() == at::kFloat && prep.numel() >= trida::gdn_prep_floats(B * blk, Hk, Hv), "prep size");
   check_i32(slot, B, "slot"); check_i32(adv, B, "adv");
   c10::cuda::CUDAGuard g(mixed.device());
-  TORCH_CHECK(trida::gdn_commit(p, ssm.data_ptr<float>(), slot.data_ptr<int>(), adv.data_ptr<int>(), stream()) == 0,
-              "gdn_commit failed");
+  TORCH_CHECK(trida::gdn_commit(p, prep.data_ptr<float>(), ssm.data_ptr<float>(), slot.data_ptr<int>(),
+                                adv.data_ptr<int>(), stream()) == 0, "gdn_commit failed");
 }
 
 void argmax_rows(const at::Tensor& logits, const at::Tensor& out) {
@@ -649,6 +658,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kv_append", &kv_append);
   m.def("canvas_conv", &canvas_conv);
   m.def("conv_commit", &conv_commit);
+  m.def("gdn_prep_numel", &gdn_prep_numel);
   m.def("gdn_canvas", &gdn_canvas);
   m.def("gdn_commit", &gdn_commit);
   m.def("argmax_rows", &argmax_rows);

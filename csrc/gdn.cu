@@ -258,21 +258,75 @@ __global__ void __launch_bounds__(NT) fwd_clean_kernel(const Args a) {
 // ---------------------------------------------------------------------------------------------
 // serving: one canvas of T rows per request from the cached state (rows < n_clean token-causal,
 // the rest read the state after the last row), and the commit that advances the cached state by
-// adv[b] rows.  State cache [slots, Hv, DK, DV] fp32.
+// adv[b] rows.  The state cache is kept in the thread-native layout [slots, Hv, NCG, RPT, NT] so
+// every load / store is coalesced; a prep pass writes each row's L2-normalised q (times scale) and
+// k once ([rows, Hk, 2, DK] fp32) and its decay / beta ([rows, Hv, 2]) for both kernels.
 // ---------------------------------------------------------------------------------------------
-__device__ __forceinline__ void load_state(const float* base, int col, int cg, int rp, float (&S)[RPT]) {
+__global__ void prep_kernel(const Args a, float* qk, float* ab, int rows) {
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int per_row = 2 * a.Hk + 1;                 // q / k per key head, then one warp for the gates
+  if (gw >= (int64_t)rows * per_row) return;
+  const int64_t row = gw / per_row;
+  const int w = (int)(gw % per_row);
+  if (w < 2 * a.Hk) {
+    const int hk = w >> 1, isk = w & 1;
+    const bf16* src = a.mixed + row * a.ldm + isk * a.Hk * DK + hk * DK + lane * 4;
+    const uint2 raw = *reinterpret_cast<const uint2*>(src);
+    const bf16* e = reinterpret_cast<const bf16*>(&raw);
+    float v[4], ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < RPT; ++i) S[i] = base[(rp * RPT + i) * DV + cg * CG + col];
+    for (int i = 0; i < 4; ++i) {
+      v[i] = __bfloat162float(e[i]);
+      ss += v[i] * v[i];
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss + 1e-6f) * (isk ? 1.f : a.scale);
+    *reinterpret_cast<float4*>(qk + ((row * a.Hk + hk) * 2 + isk) * DK + lane * 4) =
+        make_float4(v[0] * r, v[1] * r, v[2] * r, v[3] * r);
+  } else {
+    for (int h = lane; h < a.Hv; h += 32) {
+      const float av = __bfloat162float(a.ga[row * a.ldg + h]) + a.dt_bias[h];
+      const float bv = __bfloat162float(a.gb[row * a.ldg + h]);
+      ab[(row * a.Hv + h) * 2] = expf(-expf(a.A_log[h]) * softplus_f(av));
+      ab[(row * a.Hv + h) * 2 + 1] = 1.f / (1.f + expf(-bv));
+    }
+  }
 }
 
-__global__ void __launch_bounds__(NT) canvas_kernel(const Args a, const float* ssm, const int* slot, int n_clean) {
+// Stage rows 0..n-1 of request b from the prep buffers (plain coalesced copies).
+__device__ __forceinline__ void stage_prepped(const Args& a, const Stage& s, const float* qk, const float* ab, int b,
+                                              int hv, int cg, int n) {
+  const int hk = hv / (a.Hv / a.Hk);
+  for (int idx = threadIdx.x; idx < n * (DK / 4) * 2; idx += NT) {
+    const int j = idx / (DK / 2), rem = idx % (DK / 2), isk = rem / (DK / 4), c4 = rem % (DK / 4);
+    const int64_t row = (int64_t)b * a.T + j;
+    const float4 v = *reinterpret_cast<const float4*>(qk + ((row * a.Hk + hk) * 2 + isk) * DK + c4 * 4);
+    *reinterpret_cast<float4*>((isk ? s.k : s.q) + j * DK + c4 * 4) = v;
+  }
+  for (int idx = threadIdx.x; idx < n * CG; idx += NT) {
+    const int j = idx / CG, c = idx % CG;
+    const int64_t row = (int64_t)b * a.T + j;
+    s.v[idx] = __bfloat162float(a.mixed[row * a.ldm + 2 * a.Hk * DK + hv * DV + cg * CG + c]);
+  }
+  for (int j = threadIdx.x; j < n; j += NT) {
+    const int64_t row = (int64_t)b * a.T + j;
+    s.al[j] = ab[(row * a.Hv + hv) * 2];
+    s.be[j] = ab[(row * a.Hv + hv) * 2 + 1];
+  }
+}
+
+__global__ void __launch_bounds__(NT) canvas_kernel(const Args a, const float* qk, const float* ab, const float* ssm,
+                                                    const int* slot, int n_clean) {
   extern __shared__ float smem[];
   const int cg = blockIdx.x, hv = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, col = tid / RP, rp = tid % RP;
   const Stage s = carve(smem, a.T, false);
+  const float* base = ssm + (((int64_t)slot[b] * a.Hv + hv) * NCG + cg) * (RPT * NT);
   float S[RPT];
-  load_state(ssm + ((int64_t)slot[b] * a.Hv + hv) * DK * DV, col, cg, rp, S);
-  stage_tokens(a, s, b, hv, cg, 0, a.T, -1, false);
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) S[i] = base[i * NT + tid];
+  stage_prepped(a, s, qk, ab, b, hv, cg, a.T);
   __syncthreads();
   for (int j = 0; j < a.T; ++j) {
     float u, vmp;
@@ -290,23 +344,25 @@ __global__ void __launch_bounds__(NT) canvas_kernel(const Args a, const float* s
   store_o(a, s, b, hv, cg, 0, a.T);
 }
 
-__global__ void __launch_bounds__(NT) commit_kernel(const Args a, float* ssm, const int* slot, const int* adv) {
+__global__ void __launch_bounds__(NT) commit_kernel(const Args a, const float* qk, const float* ab, float* ssm,
+                                                    const int* slot, const int* adv) {
   extern __shared__ float smem[];
   const int cg = blockIdx.x, hv = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, col = tid / RP, rp = tid % RP;
   const Stage s = carve(smem, a.T, false);
   const int n = min(adv[b], a.T);
-  float* base = ssm + ((int64_t)slot[b] * a.Hv + hv) * DK * DV;
+  float* base = ssm + (((int64_t)slot[b] * a.Hv + hv) * NCG + cg) * (RPT * NT);
   float S[RPT];
-  load_state(base, col, cg, rp, S);
-  stage_tokens(a, s, b, hv, cg, 0, n, -1, false);
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) S[i] = base[i * NT + tid];
+  stage_prepped(a, s, qk, ab, b, hv, cg, n);
   __syncthreads();
   for (int j = 0; j < n; ++j) {
     float u, vmp;
     fwd_step(S, s.k + j * DK + rp * RPT, s.al[j], s.be[j], s.v[j * CG + col], u, vmp);
   }
 #pragma unroll
-  for (int i = 0; i < RPT; ++i) base[(rp * RPT + i) * DV + cg * CG + col] = S[i];
+  for (int i = 0; i < RPT; ++i) base[i * NT + tid] = S[i];
 }
 
 // Initial state of noisy block n of row b: the clean state at the start of block n, zero for the
@@ -945,7 +1001,9 @@ int gdn_bwd(const GdnParams& p, bf16* dmixed, int64_t lddm, bf16* dga, bf16* dgb
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
-int gdn_canvas(const GdnParams& p, const float* ssm, const int* slot, int n_clean, cudaStream_t st) {
+int64_t gdn_prep_floats(int rows, int Hk, int Hv) { return (int64_t)rows * (2 * Hk * gdn::DK + 2 * Hv); }
+
+int gdn_canvas(const GdnParams& p, float* prep, const float* ssm, const int* slot, int n_clean, cudaStream_t st) {
   using namespace gdn;
   if (p.dk != DK || p.dvh != DV || p.Hv % p.Hk || p.T > MAXCH) return -1;
   Args a = make_args(p);
@@ -956,15 +1014,25 @@ int gdn_canvas(const GdnParams& p, const float* ssm, const int* slot, int n_clea
     cudaFuncSetAttribute(commit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
     init = true;
   }
-  canvas_kernel<<<dim3(NCG, a.Hv, a.B), NT, stage_floats(a.T, false) * sizeof(float), st>>>(a, ssm, slot, n_clean);
+  const int rows = a.B * a.T;
+  float* qk = prep;
+  float* ab = prep + (int64_t)rows * 2 * a.Hk * DK;
+  const int64_t warps = (int64_t)rows * (2 * a.Hk + 1);
+  prep_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(a, qk, ab, rows);
+  canvas_kernel<<<dim3(NCG, a.Hv, a.B), NT, stage_floats(a.T, false) * sizeof(float), st>>>(a, qk, ab, ssm, slot,
+                                                                                           n_clean);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
-int gdn_commit(const GdnParams& p, float* ssm, const int* slot, const int* adv, cudaStream_t st) {
+int gdn_commit(const GdnParams& p, const float* prep, float* ssm, const int* slot, const int* adv, cudaStream_t st) {
   using namespace gdn;
   if (p.dk != DK || p.dvh != DV || p.Hv % p.Hk || p.T > MAXCH) return -1;
   Args a = make_args(p);
-  commit_kernel<<<dim3(NCG, a.Hv, a.B), NT, stage_floats(a.T, false) * sizeof(float), st>>>(a, ssm, slot, adv);
+  const int rows = a.B * a.T;
+  const float* qk = prep;
+  const float* ab = prep + (int64_t)rows * 2 * a.Hk * DK;
+  commit_kernel<<<dim3(NCG, a.Hv, a.B), NT, stage_floats(a.T, false) * sizeof(float), st>>>(a, qk, ab, ssm, slot,
+                                                                                           adv);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 

@@ -41,6 +41,8 @@ struct Params {
   float alpha, beta;
   int d_fp32;
   int* err;
+  int splits, kb_per;     // split-K: units = tiles * splits, each over kb_per K blocks
+  float* ws;              // split-K partials [splits, M, N] fp32 (splits > 1)
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
@@ -93,7 +95,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mt = (p.M + BM - 1) / BM, nt = (p.N + BN - 1) / BN;
-  const int tiles = mt * nt;
+  const int units = mt * nt * p.splits;
   const int kb = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -120,10 +122,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       prefetch_tmap(&tmB);
       int it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+      for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
         int m0, n0;
-        tile_coords(tile, mt, nt, m0, n0);
-        for (int k = 0; k < kb; ++k, ++it) {
+        tile_coords(u / p.splits, mt, nt, m0, n0);
+        const int kbeg = (u % p.splits) * p.kb_per, kend = min(kb, kbeg + p.kb_per);
+        for (int k = kbeg; k < kend; ++k, ++it) {
           const int s = it % STAGES;
           if (it >= STAGES && !(ok = mbar_wait(&empty[s], ((it / STAGES) - 1) & 1, p.err, 101))) break;
           unsigned char* st = smem + s * STAGE_BYTES;
@@ -141,12 +144,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const uint32_t idesc = idesc_bf16_f32(BM, BN, p.a_kmajor ? 0 : 1, p.b_kmajor ? 0 : 1);
       int it = 0, t = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++t) {
+      for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++t) {
         const int ab = t & 1;
         if (t >= 2 && !(ok = mbar_wait(&acc_empty[ab], ((t >> 1) - 1) & 1, p.err, 103))) break;
         tc_fence_after();
         const uint32_t dcol = tmem + ab * BN;
-        for (int k = 0; k < kb; ++k, ++it) {
+        const int kbeg = (u % p.splits) * p.kb_per, kend = min(kb, kbeg + p.kb_per);
+        for (int k = kbeg; k < kend; ++k, ++it) {
           const int s = it % STAGES;
           if (!(ok = mbar_wait(&full[s], (it / STAGES) & 1, p.err, 104))) break;
           tc_fence_after();
@@ -155,7 +159,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
             umma_f16(dcol, operand_desc(a_base, p.a_kmajor, kk), operand_desc(b_base, p.b_kmajor, kk), idesc,
-                     (k > 0 || kk > 0) ? 1u : 0u);
+                     (k > kbeg || kk > 0) ? 1u : 0u);
           umma_commit(&empty[s]);
         }
         if (ok) umma_commit(&acc_full[ab]);
@@ -169,14 +173,40 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int r = q * 32 + lane;                       // accumulator row (TMEM lane)
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     int t = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++t) {
       const int ab = t & 1;
       if (!mbar_wait(&acc_full[ab], (t >> 1) & 1, p.err, 106)) break;
       tc_fence_after();
       int m0, n0;
-      tile_coords(tile, mt, nt, m0, n0);
+      tile_coords(u / p.splits, mt, nt, m0, n0);
       const int row = m0 + r;
       const bool rok = row < p.M;
+      if (p.splits > 1) {
+        // split-K partial: raw fp32 accumulator to the workspace (alpha / beta applied by the reduce)
+        float* wrow = p.ws + ((int64_t)(u % p.splits) * p.M + row) * p.N;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tmem + ab * BN + lane_off + c * 32, v);
+          tmem_wait_ld();
+          const int col0 = n0 + c * 32;
+          if (!rok || col0 >= p.N) continue;
+          if (col0 + 32 <= p.N && (p.N & 3) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(wrow + col0 + j) =
+                  make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                              __uint_as_float(v[j + 3]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < p.N) wrow[col0 + j] = __uint_as_float(v[j]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[ab]);
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t v[32];
@@ -241,6 +271,28 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+// D = alpha * sum_s ws[s] + beta * C   (split-K reduction; one thread per 4 columns)
+__global__ void splitk_reduce_kernel(const float* ws, int splits, int M, int N, float alpha, float beta,
+                                     const void* C, int64_t ldc, void* D, int64_t ldd, int d_fp32) {
+  const int64_t n4 = (int64_t)M * ((N + 3) / 4);
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < n4; g += (int64_t)gridDim.x * blockDim.x) {
+    const int row = (int)(g / ((N + 3) / 4)), c0 = (int)(g % ((N + 3) / 4)) * 4;
+    for (int c = c0; c < c0 + 4 && c < N; ++c) {
+      float acc = 0.f;
+      for (int sidx = 0; sidx < splits; ++sidx) acc += ws[((int64_t)sidx * M + row) * N + c];
+      acc *= alpha;
+      if (d_fp32) {
+        if (C != nullptr && beta != 0.f) acc += beta * reinterpret_cast<const float*>(C)[(int64_t)row * ldc + c];
+        reinterpret_cast<float*>(D)[(int64_t)row * ldd + c] = acc;
+      } else {
+        if (C != nullptr && beta != 0.f)
+          acc += beta * __bfloat162float(reinterpret_cast<const bf16*>(C)[(int64_t)row * ldc + c]);
+        reinterpret_cast<bf16*>(D)[(int64_t)row * ldd + c] = __float2bfloat16(acc);
+      }
+    }
+  }
+}
+
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -276,15 +328,33 @@ static int* err_word() {
 
 }  // namespace gemm100
 
-int gemm_bf16(GemmLayout layout, bool d_fp32, const GemmArgs& a, int tile, int sm_count, cudaStream_t stream) {
+int gemm_splitk(int M, int N, int K, int sm_count) {
+  using namespace gemm100;
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int kb = (K + BK - 1) / BK;
+  if (2 * tiles > sm_count || kb < 8) return 1;
+  int splits = sm_count / tiles;
+  if (splits > kb / 4) splits = kb / 4;
+  if (splits < 2) return 1;
+  const int kb_per = (kb + splits - 1) / splits;
+  return (kb + kb_per - 1) / kb_per;
+}
+
+int gemm_bf16(GemmLayout layout, bool d_fp32, const GemmArgs& a, int tile, int sm_count, cudaStream_t stream,
+              int splits, float* ws) {
   using namespace gemm100;
   (void)tile;
   if (a.batch != 1) return -20;
+  if (splits < 1 || (splits > 1 && ws == nullptr)) return -21;
   Params p;
   p.M = a.M; p.N = a.N; p.K = a.K;
   p.D = a.D; p.ldd = a.ldd; p.C = a.C; p.ldc = a.ldc;
   p.alpha = a.alpha; p.beta = a.beta; p.d_fp32 = d_fp32 ? 1 : 0;
   p.err = err_word();
+  const int kb = (a.K + BK - 1) / BK;
+  p.kb_per = (kb + splits - 1) / splits;
+  p.splits = (kb + p.kb_per - 1) / p.kb_per;
+  p.ws = ws;
   CUtensorMap mA, mB;
   bool ok;
   switch (layout) {
@@ -309,9 +379,15 @@ int gemm_bf16(GemmLayout layout, bool d_fp32, const GemmArgs& a, int tile, int s
     cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     init = true;
   }
-  const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
-  const int grid = tiles < sm_count ? tiles : sm_count;
+  const int units = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN) * p.splits;
+  const int grid = units < sm_count ? units : sm_count;
   gemm_kernel<<<grid, NTHREADS, SMEM_BYTES, stream>>>(mA, mB, p);
+  if (p.splits > 1) {
+    const int64_t n4 = (int64_t)a.M * ((a.N + 3) / 4);
+    const int blocks = (int)std::min<int64_t>((n4 + 255) / 256, (int64_t)sm_count * 8);
+    splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(ws, p.splits, a.M, a.N, a.alpha, a.beta, a.C, a.ldc, a.D, a.ldd,
+                                                    p.d_fp32);
+  }
   return cudaGetLastError() == cudaSuccess ? 0 : -13;
 }
 

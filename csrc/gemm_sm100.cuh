@@ -26,8 +26,12 @@ struct GemmArgs {
 
 // Returns 0 on success, a negative code otherwise.  `d_fp32` selects an fp32 D/C (weight-gradient
 // accumulation) instead of bf16.  `tile` is reserved (one tile shape is built).
+// `splits` > 1 splits K over that many CTAs per output tile (for skinny GEMMs that would leave SMs
+// idle): fp32 partials go to `ws` ([splits, M, N]) and a second kernel reduces them into D.
 int gemm_bf16(GemmLayout layout, bool d_fp32, const GemmArgs& a, int tile, int sm_count,
-              cudaStream_t stream);
+              cudaStream_t stream, int splits = 1, float* ws = nullptr);
+// K splits gemm_bf16 should use for this shape (1 = none).
+int gemm_splitk(int M, int N, int K, int sm_count);
 
 // Device int the GEMM's bounded mbarrier waits set (non-zero) on a timeout; null if unallocated.
 int* gemm_error_word();

@@ -91,8 +91,11 @@ int gdn_fwd(const GdnParams& p, cudaStream_t s);
 // serving: canvas of p.T rows per request from the state cache [slots, Hv, dk, dvh]; commit
 // advances the cached state by adv[b] rows of the canvas (both read p.mixed / p.ga / p.gb rows
 // b * p.T + j).
-int gdn_canvas(const GdnParams& p, const float* ssm, const int* slot, int n_clean, cudaStream_t s);
-int gdn_commit(const GdnParams& p, float* ssm, const int* slot, const int* adv, cudaStream_t s);
+// The state cache is thread-native; `prep` holds gdn_prep_floats(B * T, Hk, Hv) floats written by
+// gdn_canvas and read again by gdn_commit.
+int64_t gdn_prep_floats(int rows, int Hk, int Hv);
+int gdn_canvas(const GdnParams& p, float* prep, const float* ssm, const int* slot, int n_clean, cudaStream_t s);
+int gdn_commit(const GdnParams& p, const float* prep, float* ssm, const int* slot, const int* adv, cudaStream_t s);
 int gdn_bwd(const GdnParams& p, bf16* dmixed, int64_t lddm, bf16* dga, bf16* dgb, int64_t lddg, float* dA_log,
             float* ddt_bias, cudaStream_t s);
 struct ConvParams {

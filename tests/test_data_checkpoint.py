@@ -166,3 +166,29 @@ def test_sharded_optimizer_state_round_trip(tmp_path):
     assert step == 7 and opt2.step_count == 1
     torch.testing.assert_close(opt2.groups[0].m, opt.groups[0].m)
     torch.testing.assert_close(opt2.groups[0].v, opt.groups[0].v)
+
+
+def test_compat_names_and_decision_export(tmp_path):
+    import warnings
+
+    import torch
+
+    from test_hybrid_cpu import tiny_qwen35
+    from trida_stack_b200.export import export
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore", DeprecationWarning)
+        from trida_stack_b200 import hf_block_diffusion, hf_block_diffusion_hybrid, jev
+    assert hf_block_diffusion.HFBlockDiffusion.__name__ == "BlockDiffusionLM"
+    assert hf_block_diffusion_hybrid.HFBlockDiffusionHybrid.__name__ == "HybridBlockDiffusionLM"
+    assert callable(jev.jev_loss)
+    ck = tmp_path / "ck"
+    tiny_qwen35(str(ck))
+    torch.save({"head": {"q.weight": torch.zeros(8, 64), "q.bias": torch.zeros(8),
+                         "k.weight": torch.zeros(8, 64), "k.bias": torch.zeros(8)}, "head_dim": 8},
+               ck / "jev_head.pt")
+    out = export(str(ck), str(tmp_path / "kev"), temperature=1.5)
+    meta = torch.load(f"{out}/head.pt")
+    assert meta["weights"] == "full" and meta["head_dim"] == 8 and meta["temperature"] == 1.5
+    from safetensors import safe_open
+    with safe_open(f"{out}/model.safetensors", "pt") as s:
+        assert all(k.startswith("model.") for k in s.keys())

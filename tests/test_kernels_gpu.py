@@ -19,7 +19,8 @@ def rel_err(a, b):
     return ((a - b).norm() / b.norm().clamp_min(1e-12)).item()
 
 
-@pytest.mark.parametrize("M,N,K", [(512, 384, 256), (2048, 3072, 2560), (300, 136, 72)])
+@pytest.mark.parametrize("M,N,K", [(512, 384, 256), (2048, 3072, 2560), (300, 136, 72), (64, 2560, 9216),
+                                   (448, 2560, 4096), (100, 136, 1000)])
 def test_gemm_layouts(M, N, K):
     torch.manual_seed(0)
     dev = "cuda"

@@ -63,11 +63,16 @@ def test_cuda_runtime_matches_cpu(cfg):
         assert _rel(a, b) < 3e-2, _rel(a, b)
 
 
-def test_cuda_self_spec_engine_runs():
+@pytest.mark.parametrize("mode", ["self-spec", "causal"])
+def test_cuda_engine_graphs_match_eager(mode):
     dec = _init(_hybrid(256)).to("cuda", torch.bfloat16)
-    eng = Engine(Runtime(dec, max_slots=8, max_len=512), mask_id=511, mode="self-spec", n=4)
     torch.manual_seed(2)
     prompts = [torch.randint(0, 500, (40,)).tolist() for _ in range(6)]
-    reqs = eng.generate(prompts, max_new_tokens=50)
-    assert all(len(r.output) == 50 for r in reqs)
-    assert eng.summary(reqs)["tokens_per_forward"] >= 1.0
+    outs = []
+    for graphs in (False, True):
+        eng = Engine(Runtime(dec, max_slots=8, max_len=512), mask_id=511, mode=mode, n=4, graphs=graphs)
+        reqs = eng.generate(prompts, max_new_tokens=50)
+        assert all(len(r.output) == 50 for r in reqs)
+        assert eng.summary(reqs)["tokens_per_forward"] >= 1.0
+        outs.append([r.output for r in reqs])
+    assert outs[0] == outs[1]

@@ -95,9 +95,11 @@ class Engine:
     """Continuous-batching decode engine over one ``Runtime``."""
 
     def __init__(self, runtime: Runtime, mask_id: int, mode: str = "self-spec", n: int = 4,
-                 max_running: Optional[int] = None):
+                 max_running: Optional[int] = None, graphs: bool = False):
         assert mode in ("self-spec", "causal")
         self.rt = runtime
+        if graphs and runtime.cuda:
+            runtime.use_graphs()
         self.mask_id = mask_id
         self.mode = mode
         self.n = n if mode == "self-spec" else 1
@@ -181,7 +183,7 @@ class Engine:
 
     def _pick(self, logits, req):
         if req.sampling.greedy:
-            return logits.argmax(-1).tolist()
+            return self.rt.argmax(logits).tolist()
         p = truncated_probs(logits, req.sampling)
         return torch.multinomial(p, 1, generator=req.gen).squeeze(-1).tolist()
 
@@ -224,11 +226,14 @@ class Engine:
         if self.mode == "causal":
             toks = [[r.output[-1] if r.output else r.t0] for r in reqs]
             logits = self.rt.canvas(slots, toks, 1)
+            greedy = all(r.sampling.greedy for r in reqs)
+            am = self.rt.argmax(logits)[:, 0].tolist() if greedy else None
+            picks = [[am[b]] if greedy else self._pick(logits[b], r) for b, r in enumerate(reqs)]
             self.rt.commit(slots, [1] * len(reqs))
             self.stats["forwards"] += 1
             for b, r in enumerate(reqs):
                 r.forwards += 1
-                self._emit(r, self._pick(logits[b], r))
+                self._emit(r, picks[b])
             self._reap()
             return
         canv = []
@@ -240,7 +245,7 @@ class Engine:
         logits = self.rt.canvas(slots, canv, n)
         self.stats["forwards"] += 1
         greedy = all(r.sampling.greedy for r in reqs)
-        am = logits.argmax(-1).tolist() if greedy else None
+        am = self.rt.argmax(logits).tolist() if greedy else None
         adv = []
         for b, r in enumerate(reqs):
             r.forwards += 1

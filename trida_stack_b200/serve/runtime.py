@@ -38,18 +38,22 @@ class Runtime:
         self.kinds = [l.layer_type for l in decoder.layers]
         d, Hkv = cfg.head_dim, cfg.n_kv_heads
         self.kc, self.vc, self.ssm, self.win = {}, {}, {}, {}
+        nslot = max_slots + 1              # + one scratch slot that pads graph-captured batches
+        self.dummy = max_slots
         for i, kind in enumerate(self.kinds):
             if kind == "full_attention":
-                self.kc[i] = torch.zeros(max_slots, max_len, Hkv, d, dtype=self.dtype, device=self.device)
-                self.vc[i] = torch.zeros(max_slots, max_len, Hkv, d, dtype=self.dtype, device=self.device)
+                self.kc[i] = torch.zeros(nslot, max_len, Hkv, d, dtype=self.dtype, device=self.device)
+                self.vc[i] = torch.zeros(nslot, max_len, Hkv, d, dtype=self.dtype, device=self.device)
             else:
                 Cc = 2 * cfg.lin_k_heads * cfg.lin_k_dim + cfg.lin_v_heads * cfg.lin_v_dim
-                self.ssm[i] = torch.zeros(max_slots, cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim,
+                # fp32 state per value head; the CUDA kernels keep it in their thread-native order
+                self.ssm[i] = torch.zeros(nslot, cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim,
                                           dtype=torch.float32, device=self.device)
-                self.win[i] = torch.zeros(max_slots, cfg.conv_kernel - 1, Cc, dtype=self.dtype, device=self.device)
+                self.win[i] = torch.zeros(nslot, cfg.conv_kernel - 1, Cc, dtype=self.dtype, device=self.device)
         self.pos = [0] * max_slots
         self.free = list(range(max_slots))[::-1]
         self.pending = None
+        self._graphs = None
         if self.cuda:
             from ..ops import blocks
             from ..ops._ext import ext
@@ -91,18 +95,51 @@ class Runtime:
                 out = logits[:, 0]
         return out
 
+    def use_graphs(self, buckets=(1, 2, 4, 8, 16, 32, 64, 128)):
+        """Replay decode-shaped canvases (all rows read out) and their commits from CUDA graphs,
+        one per (padded batch, canvas) shape; batches are padded with the scratch slot."""
+        assert self.cuda, "CUDA graphs need the CUDA runtime"
+        self.graph_buckets = sorted(b for b in buckets if b <= self.max_slots) or [self.max_slots]
+        if self.graph_buckets[-1] < self.max_slots:
+            self.graph_buckets.append(self.max_slots)
+        self._graphs = {}
+
     @torch.no_grad()
     def canvas(self, slots, tokens, n_clean, rows=None):
         """One forward over a [B, blk] canvas per slot.  Returns fp32 logits [B, r1 - r0, V] for the
-        canvas rows ``rows = (r0, r1)`` (all rows by default).  Call ``commit`` afterwards."""
+        canvas rows ``rows = (r0, r1)`` (all rows by default).  Call ``commit`` afterwards.  With
+        graphs on, the returned tensor is a static buffer valid until the next canvas."""
         assert self.pending is None, "commit the previous canvas first"
-        tokens = torch.as_tensor(tokens, dtype=torch.long, device=self.device)
-        B, blk = tokens.shape
+        B = len(slots)
+        blk = len(tokens[0])
         for s in slots:
             if self.pos[s] + blk > self.max_len:
                 raise RuntimeError(f"slot {s}: sequence exceeds the cache length {self.max_len}")
         r0, r1 = rows if rows is not None else (0, blk)
+        if self._graphs is not None and (r0, r1) == (0, blk):
+            return self._canvas_graph(slots, tokens, n_clean)
+        tokens = torch.as_tensor(tokens, dtype=torch.long, device=self.device)
         st = _Step(self, slots, B, blk, n_clean)
+        x = self._forward(st, tokens)
+        self.pending = st
+        if r1 <= r0:
+            return torch.empty(B, 0, self.cfg.vocab_size, device=self.device)
+        h = x.view(B, blk, -1)[:, r0:r1].reshape(B * (r1 - r0), -1)
+        return self._logits(h).view(B, r1 - r0, -1)
+
+    def argmax(self, logits):
+        """Greedy tokens [B, rows] of fp32 logits [B, rows, V] (the argmax kernel on CUDA; taken
+        from the captured graph when ``logits`` is the graph's output)."""
+        g = self.pending
+        if isinstance(g, _Graph) and logits.data_ptr() == g.logits.data_ptr():
+            return g.am[:logits.shape[0]]
+        if not self.cuda:
+            return logits.argmax(-1)
+        out = torch.empty(logits.shape[:-1], dtype=torch.long, device=logits.device)
+        self.C.argmax_rows(logits.reshape(-1, logits.shape[-1]), out.view(-1))
+        return out
+
+    def _forward(self, st, tokens):
         x = self.dec.embed_tokens(tokens.reshape(-1)) if self.cuda else self.dec.embed[tokens.reshape(-1)]
         for i, layer in enumerate(self.dec.layers):
             if self.kinds[i] == "full_attention":
@@ -110,27 +147,63 @@ class Runtime:
             else:
                 x = self._gdn(st, i, layer, x)
             x = self._mlp(layer, x)
-        self.pending = st
-        if r1 <= r0:
-            return torch.empty(B, 0, self.cfg.vocab_size, device=self.device)
-        h = x.view(B, blk, -1)[:, r0:r1].reshape(B * (r1 - r0), -1)
-        return self._logits(h).view(B, r1 - r0, -1)
+        return x
+
+    def _canvas_graph(self, slots, tokens, n_clean):
+        B, blk = len(slots), len(tokens[0])
+        Bp = next(b for b in self.graph_buckets if b >= B)
+        key = (Bp, blk, n_clean)
+        g = self._graphs.get(key)
+        if g is None:
+            g = self._graphs[key] = _Graph(self, Bp, blk, n_clean)
+        pad = Bp - B
+        g.host_tok[:B] = torch.as_tensor(tokens, dtype=torch.long)
+        g.host_tok[B:] = 0
+        g.host_slot[:] = torch.tensor(list(slots) + [self.dummy] * pad, dtype=torch.int32)
+        pos = [self.pos[s] for s in slots] + [0] * pad
+        g.host_pos[:] = torch.tensor(pos, dtype=torch.int32)
+        g.host_rowpos[:] = (g.host_pos[:, None] + torch.arange(blk, dtype=torch.int32)[None]).reshape(-1)
+        g.st.tokens.copy_(g.host_tok, non_blocking=True)
+        g.st.slot_t.copy_(g.host_slot, non_blocking=True)
+        g.st.pos_t.copy_(g.host_pos, non_blocking=True)
+        g.st.rowpos32.copy_(g.host_rowpos, non_blocking=True)
+        g.fwd.replay()
+        g.st.slots = list(slots)
+        self.pending = g
+        return g.logits[:B]
 
     @torch.no_grad()
     def commit(self, slots, adv):
         """Keep the first ``adv[b]`` canvas rows of every slot (1 <= adv <= n_clean)."""
         st = self.pending
+        if isinstance(st, _Graph):
+            g = st
+            assert list(slots) == g.st.slots and all(1 <= a <= g.st.n_clean for a in adv)
+            g.host_adv[:len(adv)] = torch.tensor(adv, dtype=torch.int32)
+            g.host_adv[len(adv):] = 1
+            g.adv.copy_(g.host_adv, non_blocking=True)
+            g.com.replay()
+            for b, s in enumerate(slots):
+                self.pos[s] += adv[b]
+            self.pending = None
+            return
         assert st is not None and list(slots) == list(st.slots)
         assert all(1 <= a <= st.n_clean for a in adv)
         if self.cuda:
             adv_t = torch.tensor(adv, dtype=torch.int32, device=self.device)
+        self._commit_kernels(st, adv_t if self.cuda else None, adv)
+        for b, s in enumerate(st.slots):
+            self.pos[s] += adv[b]
+        self.pending = None
+
+    def _commit_kernels(self, st, adv_t, adv=None):
         cfg = self.cfg
         for i, rec in st.gdn.items():
             layer = self.dec.layers[i]
             if self.cuda:
-                mixed, ga, gb, proj = rec
+                mixed, ga, gb, proj, prep = rec
                 a_log, dtb = self._gdn_f32[i]
-                self.C.gdn_commit(mixed, ga, gb, a_log, dtb, self.ssm[i], st.slot_t, adv_t, st.blk,
+                self.C.gdn_commit(mixed, ga, gb, a_log, dtb, prep, self.ssm[i], st.slot_t, adv_t, st.blk,
                                   cfg.lin_k_heads, cfg.lin_v_heads, cfg.lin_k_dim ** -0.5)
                 Cc = mixed.shape[1]
                 self.C.conv_commit(proj[:, :Cc], st.blk, self.win[i], st.slot_t, adv_t)
@@ -143,9 +216,6 @@ class Runtime:
                     self.ssm[i][s] = S
                     K1 = cfg.conv_kernel - 1
                     self.win[i][s] = conv_in[b, adv[b]:adv[b] + K1]
-        for b, s in enumerate(st.slots):
-            self.pos[s] += adv[b]
-        self.pending = None
 
     # ------------------------------------------------------------------ layers
     def _rms(self, x, w):
@@ -260,10 +330,12 @@ class Runtime:
             self.C.canvas_conv(proj[:, :Cc], self.win[i], layer.conv_w, mixed, st.slot_t, blk)
             a_log, dtb = self._gdn_f32[i]
             o = torch.empty(M, vd, dtype=x.dtype, device=x.device)
-            self.C.gdn_canvas(mixed, ga, gb, a_log, dtb, o, self.ssm[i], st.slot_t, blk, Hk, Hv, st.n_clean, dk ** -0.5)
+            prep = torch.empty(self.C.gdn_prep_numel(M, Hk, Hv), dtype=torch.float32, device=x.device)
+            self.C.gdn_canvas(mixed, ga, gb, a_log, dtb, o, prep, self.ssm[i], st.slot_t, blk, Hk, Hv, st.n_clean,
+                              dk ** -0.5)
             y = torch.empty(M, vd, dtype=x.dtype, device=x.device)
             self.C.gdn_gnorm_fwd(o, z, layer.gnorm, y, Hv, cfg.eps)
-            st.gdn[i] = (mixed, ga, gb, proj)
+            st.gdn[i] = (mixed, ga, gb, proj, prep)
             return self._lin(y, layer.w_out, x)
         # CPU statement
         K1 = cfg.conv_kernel - 1
@@ -299,14 +371,58 @@ class Runtime:
 class _Step:
     """Per-canvas bookkeeping shared by the layers and kept until the commit."""
 
-    def __init__(self, rt, slots, B, blk, n_clean):
+    def __init__(self, rt, slots, B, blk, n_clean, static=False):
         self.slots, self.B, self.blk, self.n_clean = list(slots), B, blk, n_clean
+        self.gdn = {}
+        if static:      # device buffers refilled before every graph replay
+            dev = rt.device
+            self.max_keys = rt.max_len
+            self.tokens = torch.zeros(B, blk, dtype=torch.long, device=dev)
+            self.slot_t = torch.full((B,), rt.dummy, dtype=torch.int32, device=dev)
+            self.pos_t = torch.zeros(B, dtype=torch.int32, device=dev)
+            self.rowpos32 = torch.arange(blk, dtype=torch.int32, device=dev).repeat(B)
+            return
         pos = [rt.pos[s] for s in self.slots]
         self.max_keys = max(pos) + blk
         self.rowpos = torch.tensor([p + j for p in pos for j in range(blk)], dtype=torch.long)
-        self.gdn = {}
         if rt.cuda:
             dev = rt.device
             self.slot_t = torch.tensor(self.slots, dtype=torch.int32, device=dev)
             self.pos_t = torch.tensor(pos, dtype=torch.int32, device=dev)
             self.rowpos32 = self.rowpos.to(dev, torch.int32)
+
+
+class _Graph:
+    """A captured decode canvas (embedding -> logits of every row) and its commit for one
+    (padded batch, canvas rows, clean rows) shape.  Captured after one eager warm-up run on the
+    scratch slot, which also initialises every kernel's launch attributes."""
+
+    def __init__(self, rt, B, blk, n_clean):
+        self.st = _Step(rt, [rt.dummy] * B, B, blk, n_clean, static=True)
+        self.adv = torch.ones(B, dtype=torch.int32, device=rt.device)
+        self.host_tok = torch.zeros(B, blk, dtype=torch.long).pin_memory()
+        self.host_slot = torch.zeros(B, dtype=torch.int32).pin_memory()
+        self.host_pos = torch.zeros(B, dtype=torch.int32).pin_memory()
+        self.host_rowpos = torch.zeros(B * blk, dtype=torch.int32).pin_memory()
+        self.host_adv = torch.ones(B, dtype=torch.int32).pin_memory()
+
+        def fwd():
+            x = rt._forward(self.st, self.st.tokens)
+            lg = rt._logits(x).view(B, blk, -1)
+            return lg, rt.argmax(lg)
+
+        def com():
+            rt._commit_kernels(self.st, self.adv)
+
+        s = torch.cuda.Stream(device=rt.device)
+        s.wait_stream(torch.cuda.current_stream(rt.device))
+        with torch.cuda.stream(s):
+            fwd()
+            com()
+        torch.cuda.current_stream(rt.device).wait_stream(s)
+        self.fwd = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.fwd):
+            self.logits, self.am = fwd()
+        self.com = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.com):
+            com()
