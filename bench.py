@@ -47,6 +47,8 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--layers", type=int, default=36, help="debug only: fewer layers (reported as reduced)")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--comm", choices=["fused", "nccl"], default="nccl",
+                   help="multi-GPU optimizer traffic: fused peer-memory kernels or NCCL collectives")
     return p.parse_args()
 
 
@@ -150,7 +152,7 @@ def run_ours(args, rank, world, local_rank):
     dec = Decoder(cfg, dtype=torch.bfloat16, device="cuda")
     model = BlockDiffusionLM(dec, mask_id=MASK_ID, pad_id=VOCAB - 2, bd_size=BD, ar_loss_weight=1.0)
     model.train()
-    engine = TrainEngine(model, lr=1e-5, warmup=50, max_steps=2000, device=torch.device("cuda"))
+    engine = TrainEngine(model, lr=1e-5, warmup=50, max_steps=2000, device=torch.device("cuda"), comm=args.comm)
     batches = synthetic_batches(args.warmup + args.steps, seed=1234 + rank)
     rpad = host_rpad(batches[0]["labels"], BD, model.response_buckets)
     dev_batches = [{k: v.cuda(non_blocking=True) for k, v in b.items()} for b in batches]

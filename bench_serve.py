@@ -46,16 +46,34 @@ def main():
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-graphs", action="store_true", help="launch every kernel eagerly (no CUDA graphs)")
+    ap.add_argument("--tp", type=int, default=1, help="tensor-parallel ranks (launch with torchrun)")
     args = ap.parse_args()
 
     from trida_stack_b200.models import Decoder
     from trida_stack_b200.serve import Engine, Runtime, SamplingParams
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    tp = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", torch.cuda.current_device()))
+    if world != args.tp:
+        raise SystemExit(f"--tp {args.tp} but WORLD_SIZE={world}")
     torch.manual_seed(args.seed)
     cfg = hybrid_config(args.layers)
     dec = Decoder(cfg, dtype=torch.bfloat16, device="cuda")
     mask_id = cfg.vocab_size - 1
     max_len = args.prompt + args.max_new + 2 * args.n + 8
-    rt = Runtime(dec, max_slots=args.requests, max_len=max_len)
+    if world > 1:
+        from trida_stack_b200.serve.tp import TPContext, shard_decoder
+        dec = shard_decoder(dec, rank, world)
+        torch.cuda.empty_cache()
+        tp = TPContext(max_rows=args.requests * 64, hidden=cfg.hidden_size)
+    rt = Runtime(dec, max_slots=args.requests, max_len=max_len, tp=tp)
     eng = Engine(rt, mask_id=mask_id, mode=args.mode, n=args.n, max_running=args.requests, graphs=not args.no_graphs)
     g = torch.Generator().manual_seed(args.seed)
 
@@ -82,19 +100,37 @@ def main():
     wall = time.perf_counter() - t0
     prefill_ms = ev[0].elapsed_time(ev[1])
     decode_ms = ev[1].elapsed_time(ev[2])
+    if world > 1:      # device time, max over ranks
+        t = torch.tensor([prefill_ms, decode_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        prefill_ms, decode_ms = t.tolist()
+        tp.heap.check()
     toks = sum(len(r.output) for r in reqs)
     s = eng.summary(reqs)
     steps = eng.stats["forwards"] - f0
+    if rank != 0:
+        _finish(rt, world)
+        return
     print(json.dumps({
         "metric": "self-spec decode tokens/s", "value": round(toks / (decode_ms / 1e3), 1), "unit": "tokens/s",
         "tokens_per_forward": round(s["tokens_per_forward"], 3), "p50_ttft_ms": round(s["p50_ttft_s"] * 1e3, 2),
         "prefill_ms": round(prefill_ms, 2), "decode_ms": round(decode_ms, 2), "decode_steps": steps,
-        "ms_per_step": round(decode_ms / max(steps, 1), 3), "wall_s": round(wall, 2), "tp": 1,
+        "ms_per_step": round(decode_ms / max(steps, 1), 3), "wall_s": round(wall, 2), "tp": world,
         "config": {"model": f"Qwen3.5-4B-style hybrid ({args.layers}L)", "requests": args.requests,
                    "prompt": args.prompt, "max_new": args.max_new, "mode": args.mode, "n": args.n,
                    "canvas_rows": 2 * args.n - 1 if args.mode == "self-spec" else 1, "greedy": True,
                    "cuda_graphs": not args.no_graphs},
-        "data": "synthetic uniform prompts, random-init weights", "dtype": "bf16"}))
+        "data": "synthetic uniform prompts, random-init weights", "dtype": "bf16"}), flush=True)
+    _finish(rt, world)
+
+
+def _finish(rt, world):
+    if world > 1:
+        import torch.distributed as dist
+        rt._graphs = None          # graphs holding NCCL calls go before the process group
+        torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -77,6 +77,111 @@ void gemm(int64_t layout, const at::Tensor& A, const at::Tensor& B, const at::Te
   TORCH_CHECK(rc == 0, "sm100 GEMM failed with code ", rc, " (M=", M, " N=", N, " K=", K, " layout=", layout, ")");
 }
 
+// ---------------------------------------------------------------------------------------------
+// symmetric peer memory (symm.cu).  Buffers are raw cudaMalloc allocations (IPC-exportable),
+// wrapped as non-owning tensors; pointers travel as Python ints.
+// ---------------------------------------------------------------------------------------------
+int64_t symm_malloc(int64_t bytes) {
+  void* p = nullptr;
+  TORCH_CHECK(cudaMalloc(&p, bytes) == cudaSuccess, "symmetric buffer allocation of ", bytes, " bytes failed");
+  TORCH_CHECK(cudaMemset(p, 0, bytes) == cudaSuccess, "symmetric buffer clear failed");
+  return reinterpret_cast<int64_t>(p);
+}
+
+void symm_free(int64_t p) { cudaFree(reinterpret_cast<void*>(p)); }
+
+py::bytes symm_handle(int64_t p) {
+  unsigned char h[64];
+  TORCH_CHECK(trida::symm_ipc_handle(reinterpret_cast<void*>(p), h) == 0, "cudaIpcGetMemHandle failed");
+  return py::bytes(reinterpret_cast<const char*>(h), 64);
+}
+
+int64_t symm_open(py::bytes handle) {
+  std::string h = handle;
+  TORCH_CHECK(h.size() == 64, "IPC handle must be 64 bytes");
+  void* p = trida::symm_ipc_open(reinterpret_cast<const unsigned char*>(h.data()));
+  TORCH_CHECK(p != nullptr, "cudaIpcOpenMemHandle failed");
+  return reinterpret_cast<int64_t>(p);
+}
+
+void symm_close(int64_t p) { trida::symm_ipc_close(reinterpret_cast<void*>(p)); }
+
+at::Tensor symm_tensor(int64_t p, int64_t numel, at::ScalarType dtype, int64_t device) {
+  return torch::from_blob(reinterpret_cast<void*>(p), {numel}, [](void*) {},
+                          at::TensorOptions().dtype(dtype).device(at::kCUDA, device));
+}
+
+struct PtrArrays {
+  void* bufs[8];
+  unsigned* flags[8];
+};
+
+static PtrArrays ptr_arrays(const std::vector<int64_t>& bufs, const std::vector<int64_t>& flags) {
+  TORCH_CHECK(bufs.size() == flags.size() && bufs.size() >= 1 && bufs.size() <= 8, "1..8 ranks");
+  PtrArrays a{};
+  for (size_t i = 0; i < bufs.size(); ++i) {
+    a.bufs[i] = reinterpret_cast<void*>(bufs[i]);
+    a.flags[i] = reinterpret_cast<unsigned*>(flags[i]);
+  }
+  return a;
+}
+
+// ctr_done: int32 [2] on this rank's device (epoch counter, finished-CTA counter), zero at start.
+void symm_allreduce(const std::vector<int64_t>& bufs, const std::vector<int64_t>& flags, int64_t rank,
+                    const at::Tensor& ctr_done, int64_t off, int64_t n, const c10::optional<at::Tensor>& residual,
+                    const at::Tensor& out, const at::Tensor& err) {
+  TORCH_CHECK(ctr_done.scalar_type() == at::kInt && ctr_done.numel() >= 2, "ctr_done must be int32 [2]");
+  unsigned* cd = reinterpret_cast<unsigned*>(ctr_done.data_ptr<int>());
+  auto a = ptr_arrays(bufs, flags);
+  CHECK_BF16(out); TORCH_CHECK(out.is_contiguous() && out.numel() == n, "out must hold n elements");
+  const bf16* res = nullptr;
+  if (residual.has_value() && residual->defined()) {
+    CHECK_BF16((*residual)); TORCH_CHECK(residual->is_contiguous() && residual->numel() == n, "residual shape");
+    res = cbf(*residual);
+  }
+  const int rc = trida::symm_allreduce_bf16(a.bufs, a.flags, rank, bufs.size(), cd, cd + 1, off, n, res, mbf(out),
+                                            err.data_ptr<int>(), sm_count(), stream());
+  TORCH_CHECK(rc == 0, "symm_allreduce failed with code ", rc);
+}
+
+void symm_rs_sumsq(const std::vector<int64_t>& bufs, const std::vector<int64_t>& flags, int64_t rank, int64_t epoch,
+                   int64_t shard_off, int64_t shard_len, double scale, const at::Tensor& shard_out,
+                   const at::Tensor& partial, const at::Tensor& err) {
+  auto a = ptr_arrays(bufs, flags);
+  TORCH_CHECK(shard_out.scalar_type() == at::kFloat && shard_out.numel() == shard_len, "shard_out");
+  TORCH_CHECK(partial.scalar_type() == at::kFloat, "partial fp32");
+  const int rc = trida::symm_rs_sumsq(a.bufs, a.flags, rank, bufs.size(), (unsigned)epoch, shard_off, shard_len,
+                                      (float)scale, shard_out.data_ptr<float>(), partial.data_ptr<float>(),
+                                      partial.numel(), err.data_ptr<int>(), stream());
+  TORCH_CHECK(rc == 0, "symm_rs_sumsq failed with code ", rc);
+}
+
+void symm_norm_coef(const std::vector<int64_t>& partials, const std::vector<int64_t>& flags, int64_t rank,
+                    int64_t epoch, int64_t nblocks, double max_norm, const at::Tensor& norm, const at::Tensor& coef,
+                    const at::Tensor& err) {
+  auto a = ptr_arrays(partials, flags);
+  const int rc = trida::symm_norm_coef(a.bufs, a.flags, rank, partials.size(), (unsigned)epoch, nblocks,
+                                       (float)max_norm, norm.data_ptr<float>(), coef.data_ptr<float>(),
+                                       err.data_ptr<int>(), stream());
+  TORCH_CHECK(rc == 0, "symm_norm_coef failed with code ", rc);
+}
+
+void symm_adamw_ag(const std::vector<int64_t>& bufs, const std::vector<int64_t>& flags, int64_t rank, int64_t epoch,
+                   int64_t shard_off, int64_t shard_len, const at::Tensor& grad, const c10::optional<at::Tensor>& master,
+                   const at::Tensor& m, const at::Tensor& v, double lr, double b1, double b2, double eps, double wd,
+                   int64_t step, const c10::optional<at::Tensor>& coef, const at::Tensor& done, const at::Tensor& err) {
+  auto a = ptr_arrays(bufs, flags);
+  TORCH_CHECK(grad.numel() == shard_len && m.numel() == shard_len && v.numel() == shard_len, "shard sizes");
+  float* pm = (master.has_value() && master->defined()) ? master->data_ptr<float>() : nullptr;
+  const float* pc = (coef.has_value() && coef->defined()) ? coef->data_ptr<float>() : nullptr;
+  const int rc = trida::symm_adamw_ag(a.bufs, a.flags, rank, bufs.size(), (unsigned)epoch, shard_off, shard_len,
+                                      grad.data_ptr<float>(), pm, m.data_ptr<float>(), v.data_ptr<float>(), (float)lr,
+                                      (float)b1, (float)b2, (float)eps, (float)wd, (int)step, pc,
+                                      reinterpret_cast<unsigned*>(done.data_ptr<int>()), err.data_ptr<int>(),
+                                      sm_count(), stream());
+  TORCH_CHECK(rc == 0, "symm_adamw_ag failed with code ", rc);
+}
+
 // Reads and clears the GEMM's device error word (host sync); 0 = no timed-out wait.
 int64_t gemm_error() {
   int* w = trida::gemm_error_word();
@@ -649,6 +754,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale"), py::arg("err"), py::arg("dbg") = py::none());
   m.def("bd_attn_tile_masks", &bd_attn_tile_masks);
   m.def("gemm_error", &gemm_error);
+  m.def("symm_malloc", &symm_malloc);
+  m.def("symm_free", &symm_free);
+  m.def("symm_handle", &symm_handle);
+  m.def("symm_open", &symm_open);
+  m.def("symm_close", &symm_close);
+  m.def("symm_tensor", &symm_tensor);
+  m.def("symm_allreduce", &symm_allreduce);
+  m.def("symm_rs_sumsq", &symm_rs_sumsq);
+  m.def("symm_norm_coef", &symm_norm_coef);
+  m.def("symm_adamw_ag", &symm_adamw_ag);
   m.def("gdn_state_numel", &gdn_state_numel);
   m.def("gdn_fwd", &gdn_fwd, py::arg("mixed"), py::arg("ga"), py::arg("gb"), py::arg("A_log"), py::arg("dt_bias"),
         py::arg("doc"), py::arg("o"), py::arg("ckpt"), py::arg("B"), py::arg("T"), py::arg("Hk"), py::arg("Hv"),

@@ -23,13 +23,24 @@ namespace gemm100 {
 
 using namespace sm100;
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int BN = 256, BK = 64;
 constexpr int NTHREADS = 192;
-constexpr int A_BYTES = BM * BK * 2;     // 16 KB
 constexpr int B_BYTES = BN * BK * 2;     // 32 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 256 + 1024;
 constexpr int GROUP_M = 16;
+
+// MH = 128-row halves per tile: MH = 1 -> 128 x 256 tiles, 4-stage ring, two TMEM accumulators
+// (the epilogue of one tile overlaps the mainloop of the next); MH = 2 -> 256 x 256 tiles (two
+// MMAs share every B slice, 1.5x the FLOPs per byte staged), 3-stage ring, one accumulator
+// spanning all 512 TMEM columns.
+template <int MH>
+struct Cfg {
+  static constexpr int BM = 128 * MH;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = MH == 1 ? 4 : 3;
+  static constexpr int NACC = MH == 1 ? 2 : 1;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 256 + 1024;
+};
 
 struct Params {
   int M, N, K;
@@ -53,22 +64,21 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-__device__ __forceinline__ void tile_coords(int tile, int mt, int nt, int& m0, int& n0) {
+__device__ __forceinline__ void tile_coords(int tile, int mt, int nt, int bm, int& m0, int& n0) {
   const int per_group = GROUP_M * nt;
   const int g = tile / per_group;
   const int first_m = g * GROUP_M;
   const int gm = (mt - first_m) < GROUP_M ? (mt - first_m) : GROUP_M;
   const int in = tile % per_group;
-  m0 = (first_m + in % gm) * BM;
+  m0 = (first_m + in % gm) * bm;
   n0 = (in / gm) * BN;
 }
 
-// Load one K slice of an operand tile.  K-major: rows x 64 K  (box {64, rows_per_box}).
+// Load one K slice of an operand tile.  K-major: rows x 64 K  (box {64, rows}, rows <= 256).
 // MN-major: 64 K rows x MN (box {64 MN, 64 K}); `width` MN elements in 64-wide atoms.
 __device__ __forceinline__ void load_operand(unsigned char* dst, const CUtensorMap* map, uint64_t* bar, int kmajor,
                                              int mn0, int k0, int width) {
   if (kmajor) {
-    // one box of {64 K, width rows} (width <= 256 rows per box)
     tma_load_2d(dst, map, bar, k0, mn0);
   } else {
     for (int j = 0; j < width / 64; ++j) tma_load_2d(dst + j * (BK * 128), map, bar, mn0 + j * 64, k0);
@@ -81,15 +91,19 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kmajor, int 
   return desc_sw128(base + kk * 2048, BK * 128, 1024);
 }
 
+template <int MH>
 __global__ void __launch_bounds__(NTHREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+  using C_ = Cfg<MH>;
+  constexpr int BM = C_::BM, STAGES = C_::STAGES, NACC = C_::NACC;
+  constexpr int A_BYTES = C_::A_BYTES, STAGE_BYTES = C_::STAGE_BYTES;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  uint64_t* full = bars;                 // [STAGES]
-  uint64_t* empty = bars + STAGES;       // [STAGES]
-  uint64_t* acc_full = bars + 2 * STAGES;    // [2]
-  uint64_t* acc_empty = bars + 2 * STAGES + 2;  // [2]
+  uint64_t* full = bars;                       // [STAGES]
+  uint64_t* empty = bars + STAGES;             // [STAGES]
+  uint64_t* acc_full = bars + 2 * STAGES;      // [NACC]
+  uint64_t* acc_empty = bars + 2 * STAGES + 2; // [NACC]
   uint64_t* drain = bars + 2 * STAGES + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 6);
 
@@ -103,7 +117,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NACC; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 128);
     }
@@ -124,7 +138,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       bool ok = true;
       for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
         int m0, n0;
-        tile_coords(u / p.splits, mt, nt, m0, n0);
+        tile_coords(u / p.splits, mt, nt, BM, m0, n0);
         const int kbeg = (u % p.splits) * p.kb_per, kend = min(kb, kbeg + p.kb_per);
         for (int k = kbeg; k < kend; ++k, ++it) {
           const int s = it % STAGES;
@@ -141,12 +155,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(BM, BN, p.a_kmajor ? 0 : 1, p.b_kmajor ? 0 : 1);
+      const uint32_t idesc = idesc_bf16_f32(128, BN, p.a_kmajor ? 0 : 1, p.b_kmajor ? 0 : 1);
       int it = 0, t = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++t) {
-        const int ab = t & 1;
-        if (t >= 2 && !(ok = mbar_wait(&acc_empty[ab], ((t >> 1) - 1) & 1, p.err, 103))) break;
+        const int ab = t % NACC;
+        if (t >= NACC && !(ok = mbar_wait(&acc_empty[ab], ((t / NACC) - 1) & 1, p.err, 103))) break;
         tc_fence_after();
         const uint32_t dcol = tmem + ab * BN;
         const int kbeg = (u % p.splits) * p.kb_per, kend = min(kb, kbeg + p.kb_per);
@@ -157,9 +171,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const uint32_t a_base = smem_addr(smem + s * STAGE_BYTES);
           const uint32_t b_base = a_base + A_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            umma_f16(dcol, operand_desc(a_base, p.a_kmajor, kk), operand_desc(b_base, p.b_kmajor, kk), idesc,
-                     (k > kbeg || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t bdesc = operand_desc(b_base, p.b_kmajor, kk);
+#pragma unroll
+            for (int h = 0; h < MH; ++h)   // rows h*128.. of the A tile start 16 KB further in
+              umma_f16(dcol + h * BN, operand_desc(a_base + h * 16384, p.a_kmajor, kk), bdesc, idesc,
+                       (k > kbeg || kk > 0) ? 1u : 0u);
+          }
           umma_commit(&empty[s]);
         }
         if (ok) umma_commit(&acc_full[ab]);
@@ -174,12 +192,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     int t = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++t) {
-      const int ab = t & 1;
-      if (!mbar_wait(&acc_full[ab], (t >> 1) & 1, p.err, 106)) break;
+      const int ab = t % NACC;
+      if (!mbar_wait(&acc_full[ab], (t / NACC) & 1, p.err, 106)) break;
       tc_fence_after();
       int m0, n0;
-      tile_coords(u / p.splits, mt, nt, m0, n0);
-      const int row = m0 + r;
+      tile_coords(u / p.splits, mt, nt, BM, m0, n0);
+#pragma unroll 1
+      for (int h = 0; h < MH; ++h) {
+      const uint32_t acc = tmem + (ab + h) * BN + lane_off;
+      const int row = m0 + h * 128 + r;
       const bool rok = row < p.M;
       if (p.splits > 1) {
         // split-K partial: raw fp32 accumulator to the workspace (alpha / beta applied by the reduce)
@@ -187,7 +208,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t v[32];
-          tmem_ld32(tmem + ab * BN + lane_off + c * 32, v);
+          tmem_ld32(acc + c * 32, v);
           tmem_wait_ld();
           const int col0 = n0 + c * 32;
           if (!rok || col0 >= p.N) continue;
@@ -203,14 +224,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               if (col0 + j < p.N) wrow[col0 + j] = __uint_as_float(v[j]);
           }
         }
-        tc_fence_before();
-        mbar_arrive(&acc_empty[ab]);
         continue;
       }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t v[32];
-        tmem_ld32(tmem + ab * BN + lane_off + c * 32, v);
+        tmem_ld32(acc + c * 32, v);
         tmem_wait_ld();
         const int col0 = n0 + c * 32;
         if (!rok || col0 >= p.N) continue;
@@ -260,6 +279,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 dst[j] = __float2bfloat16(f[j] + ((csrc && p.beta != 0.f) ? p.beta * __bfloat162float(csrc[j]) : 0.f));
           }
         }
+      }
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[ab]);
@@ -330,7 +350,7 @@ static int* err_word() {
 
 int gemm_splitk(int M, int N, int K, int sm_count) {
   using namespace gemm100;
-  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int tiles = ((M + 127) / 128) * ((N + BN - 1) / BN);
   const int kb = (K + BK - 1) / BK;
   if (2 * tiles > sm_count || kb < 8) return 1;
   int splits = sm_count / tiles;
@@ -340,10 +360,29 @@ int gemm_splitk(int M, int N, int K, int sm_count) {
   return (kb + kb_per - 1) / kb_per;
 }
 
+template <int MH>
+static int launch(const CUtensorMap& mA, const CUtensorMap& mB, const gemm100::Params& p, int sm_count,
+                  cudaStream_t stream) {
+  using namespace gemm100;
+  static bool init = false;
+  if (!init) {
+    cudaFuncSetAttribute(gemm_kernel<MH>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<MH>::SMEM_BYTES);
+    init = true;
+  }
+  const int units = ((p.M + Cfg<MH>::BM - 1) / Cfg<MH>::BM) * ((p.N + BN - 1) / BN) * p.splits;
+  const int grid = units < sm_count ? units : sm_count;
+  gemm_kernel<MH><<<grid, NTHREADS, Cfg<MH>::SMEM_BYTES, stream>>>(mA, mB, p);
+  return 0;
+}
+
 int gemm_bf16(GemmLayout layout, bool d_fp32, const GemmArgs& a, int tile, int sm_count, cudaStream_t stream,
               int splits, float* ws) {
   using namespace gemm100;
-  (void)tile;
+  if (a.batch != 1) return -20;
+  // tile 1: 128 x 256 tiles; tile 2: 256 x 256; otherwise 256-row tiles when they still fill the GPU
+  const int tiles256 = ((a.M + 255) / 256) * ((a.N + BN - 1) / BN);
+  const int mh = tile == 1 ? 1 : tile == 2 ? 2 : (splits == 1 && 2 * tiles256 >= sm_count ? 2 : 1);
+  const int BM = 128 * mh;
   if (a.batch != 1) return -20;
   if (splits < 1 || (splits > 1 && ws == nullptr)) return -21;
   Params p;
@@ -374,14 +413,8 @@ int gemm_bf16(GemmLayout layout, bool d_fp32, const GemmArgs& a, int tile, int s
       return -11;
   }
   if (!ok) return -12;
-  static bool init = false;
-  if (!init) {
-    cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    init = true;
-  }
-  const int units = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN) * p.splits;
-  const int grid = units < sm_count ? units : sm_count;
-  gemm_kernel<<<grid, NTHREADS, SMEM_BYTES, stream>>>(mA, mB, p);
+  if (mh == 2) launch<2>(mA, mB, p, sm_count, stream);
+  else launch<1>(mA, mB, p, sm_count, stream);
   if (p.splits > 1) {
     const int64_t n4 = (int64_t)a.M * ((a.N + 3) / 4);
     const int blocks = (int)std::min<int64_t>((n4 + 255) / 256, (int64_t)sm_count * 8);

@@ -127,6 +127,24 @@ void conv_commit(const bf16* x, int64_t ldx, int rows_per, bf16* win, const int*
                  int K, cudaStream_t s);
 void argmax_rows(const float* logits, int64_t ld, int rows, int V, int64_t* out, cudaStream_t s);
 
+// ---- symmetric peer memory collectives (symm.cu) ----
+// bufs / flags: one pointer per rank (this rank's own at index `rank`, peers' IPC-mapped).
+int symm_allreduce_bf16(void* const* bufs, unsigned* const* flags, int rank, int world, unsigned* ctr, unsigned* done,
+                        int64_t off, int64_t n, const bf16* residual, bf16* out, int* err, int sm_count,
+                        cudaStream_t s);
+int symm_rs_sumsq(void* const* bufs, unsigned* const* flags, int rank, int world, unsigned epoch, int64_t shard_off,
+                  int64_t shard_len, float scale, float* shard_out, float* partial, int nblocks, int* err,
+                  cudaStream_t s);
+int symm_norm_coef(void* const* partials, unsigned* const* flags, int rank, int world, unsigned epoch, int nblocks,
+                   float max_norm, float* norm_out, float* coef_out, int* err, cudaStream_t s);
+int symm_adamw_ag(void* const* bufs, unsigned* const* flags, int rank, int world, unsigned epoch, int64_t shard_off,
+                  int64_t shard_len, const float* grad, float* master, float* m, float* v, float lr, float b1,
+                  float b2, float eps, float wd, int step, const float* coef, unsigned* done, int* err, int sm_count,
+                  cudaStream_t s);
+int symm_ipc_handle(void* ptr, unsigned char* out64);
+void* symm_ipc_open(const unsigned char* in64);
+void symm_ipc_close(void* p);
+
 // ---- cross-entropy rows (cross_entropy.cu) ----
 void ce_rows_fwd_bwd(const float* logits, int64_t ld, const int64_t* target, const float* weight, float grad_scale,
                      int n, int V, float* loss, bf16* dlogits, int64_t ldd, cudaStream_t s);

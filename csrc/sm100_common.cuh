@@ -24,10 +24,12 @@ namespace trida {
 namespace sm100 {
 
 // A waiting thread suspends inside try_wait until the phase completes or kSuspendNs elapses, so
-// waiters do not flood the shared-memory pipe with polls.  After kMaxPolls suspensions (~4 s) the
-// wait gives up and records an error, so a broken pipeline ends with an error flag, never a hang.
-constexpr uint32_t kSuspendNs = 1000000;   // 1 ms
-constexpr uint32_t kMaxPolls = 4000;
+// waiters do not flood the shared-memory pipe with polls.  The wait is bounded by wall time (the
+// global nanosecond timer, checked every 256 polls): after kWaitLimitNs it gives up and records an
+// error, so a broken pipeline ends with an error flag, never a hang.  The error word in global
+// memory is only read on that slow path, keeping the common wake-up latency at shared-memory speed.
+constexpr uint32_t kSuspendNs = 1000000;          // 1 ms
+constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -60,11 +62,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: returns false (and records `code` in *err) if the phase never completes.
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+  return t;
+}
+
+// Bounded wait: returns false (and records `code` in *err) if the phase never completes, or as
+// soon as another waiter has recorded an error.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-  for (uint32_t i = 0; i < kMaxPolls; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+    if ((i & 255) == 0) {
+      if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+      if (global_ns() - t0 > kWaitLimitNs) break;
+    }
   }
   atomicCAS(err, 0, code);
   return false;

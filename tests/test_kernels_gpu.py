@@ -380,3 +380,23 @@ def test_gated_attention_block_d256_matches_cpu_reference():
     assert rel_err(gx1, gx0) < 3e-2
     for a, b in zip(gp1, gp0):
         assert rel_err(a, b) < 5e-2
+
+
+@pytest.mark.parametrize("tile", [1, 2])
+def test_gemm_tile_shapes_ragged_all_layouts(tile):
+    """128- and 256-row tiles on ragged shapes (partial row halves, partial N tiles) in all layouts."""
+    torch.manual_seed(3)
+    M, N, K = 600, 520, 200
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+    y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C().gemm(0, x, w, y, None, 1.0, 0.0, tile)
+    assert rel_err(y, x.float() @ w.float().t()) < 1e-2
+    dy = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+    dx = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
+    C().gemm(1, dy, w, dx, None, 1.0, 0.0, tile)
+    assert rel_err(dx, dy.float() @ w.float()) < 1e-2
+    acc = torch.randn(N, K, device="cuda", dtype=torch.float32)
+    ref = acc + dy.float().t() @ x.float()
+    C().gemm(2, dy, x, acc, acc, 1.0, 1.0, tile)
+    assert rel_err(acc, ref) < 1e-3

@@ -92,3 +92,61 @@ def test_sampled_self_spec_runs_and_respects_eos():
     reqs = eng.generate([[1, 2, 3, 4, 5]], max_new_tokens=30, sampling=sp, eos=(7,))
     r = reqs[0]
     assert r.done and 7 not in r.output and len(r.output) <= 30
+
+
+class _ThreadTP:
+    """CPU stand-in for TPContext: W runtimes in W threads sum their row-parallel partials and
+    gather their argmax pairs through shared slots and a barrier."""
+
+    def __init__(self, shared, rank, world):
+        self.s, self.rank, self.world = shared, rank, world
+
+    def _exchange(self, t):
+        self.s["slots"][self.rank] = t
+        self.s["bar"].wait()
+        out = torch.stack(list(self.s["slots"]))
+        self.s["bar"].wait()
+        return out
+
+    def row_parallel(self, x, w, residual):
+        return residual + self._exchange(x @ w.t()).sum(0)
+
+    def gather(self, t):
+        return self._exchange(t)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tensor_parallel_shards_reproduce_full_model(world):
+    import threading
+
+    from trida_stack_b200.serve.tp import shard_decoder
+    dec = tiny_hybrid()
+    dec.cfg.lin_k_heads, dec.cfg.lin_v_heads = 2, 4          # tiny_hybrid's GDN heads
+    torch.manual_seed(3)
+    prompts = [torch.randint(0, 96, (12,)).tolist() for _ in range(2)]
+    ref = Engine(Runtime(dec, max_slots=4, max_len=128), mask_id=96, mode="self-spec", n=3)
+    want = [r.output for r in ref.generate(prompts, max_new_tokens=16)]
+    if 2 % world and dec.cfg.n_kv_heads < world:
+        pytest.skip("shape does not split")
+    shared = {"slots": [None] * world, "bar": threading.Barrier(world)}
+    outs = [None] * world
+    errs = []
+
+    def run(r):
+        try:
+            local = shard_decoder(dec, r, world)
+            eng = Engine(Runtime(local, max_slots=4, max_len=128, tp=_ThreadTP(shared, r, world)), mask_id=96,
+                         mode="self-spec", n=3)
+            outs[r] = [q.output for q in eng.generate(prompts, max_new_tokens=16)]
+        except Exception as e:   # surface in the main thread
+            errs.append(e)
+            shared["bar"].abort()
+
+    ths = [threading.Thread(target=run, args=(r,)) for r in range(world)]
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join(timeout=300)
+    assert not errs, errs
+    for o in outs:
+        assert o == want

@@ -16,7 +16,8 @@ def build_optimizer(args, model, device=None):
     groups = model.param_groups(projector_lr_scale=args.projector_lr_scale,
                                 decision_head_lr_scale=args.decision_head_lr_scale)
     opt = ShardedAdamW(groups, lr=args.lr, betas=(0.9, args.adam_beta2), weight_decay=args.weight_decay,
-                       fp32_master=getattr(args, "fp32_master", False), device=device)
+                       fp32_master=getattr(args, "fp32_master", False), device=device,
+                       comm=getattr(args, "comm", "nccl"))
     for g, src in zip(opt.param_groups, groups):
         g.setdefault("lr_scale", src.get("lr_scale", 1.0))
     if len(groups) > 1:

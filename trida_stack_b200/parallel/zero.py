@@ -31,9 +31,10 @@ def _rank():
 
 
 class FlatGroup:
-    """One optimizer group flattened into contiguous buffers."""
+    """One optimizer group flattened into contiguous buffers (symmetric peer buffers when a heap
+    is given, so the fused collectives can read and write them from every rank)."""
 
-    def __init__(self, params, lr_scale, world, rank, fp32_master, device):
+    def __init__(self, params, lr_scale, world, rank, fp32_master, device, heap=None):
         self.params = list(params)
         self.lr_scale = lr_scale
         self.world, self.rank = world, rank
@@ -43,8 +44,14 @@ class FlatGroup:
         self.padded = (n + unit - 1) // unit * unit
         self.shard = self.padded // world
         dtype = self.params[0].dtype if self.params else torch.bfloat16
-        self.flat = torch.zeros(self.padded, dtype=dtype, device=device)
-        self.grad = torch.zeros(self.padded, dtype=torch.float32, device=device)
+        self.flat_sym = self.grad_sym = None
+        if heap is not None:
+            self.flat_sym = heap.alloc(self.padded, dtype)
+            self.grad_sym = heap.alloc(self.padded, torch.float32)
+            self.flat, self.grad = self.flat_sym.local, self.grad_sym.local
+        else:
+            self.flat = torch.zeros(self.padded, dtype=dtype, device=device)
+            self.grad = torch.zeros(self.padded, dtype=torch.float32, device=device)
         off = 0
         self.offsets = []
         with torch.no_grad():
@@ -88,13 +95,26 @@ class ShardedAdamW:
     """AdamW over flat sharded buffers; torch.optim-like surface (``param_groups``, ``step``,
     ``zero_grad``, ``state_dict``)."""
 
+    NB = 296          # partial-sum blocks of the fused reduce-scatter (2 per SM)
+
     def __init__(self, groups, lr, betas=(0.9, 0.95), weight_decay=0.0, eps=1e-8, fp32_master=False,
-                 device=None, process_group=None):
+                 device=None, process_group=None, comm="nccl"):
         self.world, self.rank = _world(), _rank()
         self.pg = process_group
         device = device or groups[0]["params"][0].device
-        self.groups = [FlatGroup(g["params"], g.get("lr_scale", 1.0), self.world, self.rank, fp32_master, device)
+        # comm="fused": gradient reduce-scatter + norm + AdamW + parameter all-gather run as
+        # symmetric-memory kernels over NVLink (csrc/symm.cu); "nccl": NCCL collectives.
+        self.fused = comm == "fused" and self.world > 1 and torch.device(device).type == "cuda"
+        self.heap = None
+        if self.fused:
+            from .symm import SymmetricHeap
+            self.heap = SymmetricHeap(process_group)
+        self.groups = [FlatGroup(g["params"], g.get("lr_scale", 1.0), self.world, self.rank, fp32_master, device,
+                                 self.heap)
                        for g in groups if g["params"]]
+        if self.fused:
+            self.partials = self.heap.alloc(len(self.groups) * self.NB, torch.float32)
+        self._clipped = False
         self.param_groups = [{"params": g.params, "lr": lr * g.lr_scale, "lr_scale": g.lr_scale}
                              for g in self.groups]
         self.defaults = {"lr": lr, "betas": betas, "weight_decay": weight_decay, "eps": eps}
@@ -123,7 +143,15 @@ class ShardedAdamW:
     def reduce_gradients(self):
         """Average gradients across ranks into each rank's shard (reduce-scatter)."""
         self.collect_autograd_grads()
+        self._clipped = False
         if self.world == 1:
+            return
+        if self.fused:
+            h = self.heap
+            for i, g in enumerate(self.groups):
+                ext().symm_rs_sumsq(g.grad_sym.ptrs, h.flags.ptrs, h.rank, h.next_epoch(1), g.lo, g.shard,
+                                    1.0 / self.world, g.grad_shard,
+                                    self.partials.local[i * self.NB:(i + 1) * self.NB], h.err)
             return
         avg = dist.get_backend(self.pg) == "nccl"   # gloo has no AVG reduction
         for g in self.groups:
@@ -143,8 +171,14 @@ class ShardedAdamW:
         """Global L2 norm of the (reduced) gradients; writes the clip coefficient on the device and
         returns the norm as a device tensor (no host sync)."""
         shards = [g.shard_grad() for g in self.groups]
+        self._clipped = True
         if self.world == 1:
             self._local_norm(shards, max_norm)
+            return self.norm[0]
+        if self.fused:
+            h = self.heap
+            ext().symm_norm_coef(self.partials.ptrs, h.flags.ptrs, h.rank, h.next_epoch(3),
+                                 len(self.groups) * self.NB, max_norm, self.norm, self.coef, h.err)
             return self.norm[0]
         # partial sums of squares on each rank, summed across ranks, then the coefficient
         sq = torch.zeros(1, dtype=torch.float32, device=self.norm.device)
@@ -159,6 +193,14 @@ class ShardedAdamW:
     def step(self):
         self.step_count += 1
         b1, b2 = self.betas
+        if self.fused:
+            h = self.heap
+            coef = self.coef if self._clipped else None
+            for g, pg in zip(self.groups, self.param_groups):
+                ext().symm_adamw_ag(g.flat_sym.ptrs, h.flags.ptrs, h.rank, h.next_epoch(2), g.lo, g.shard,
+                                    g.grad_shard, g.master, g.m, g.v, pg["lr"], b1, b2, self.eps, self.wd,
+                                    self.step_count, coef, h.done, h.err)
+            return
         for g, pg in zip(self.groups, self.param_groups):
             lr = pg["lr"]
             if self.coef.is_cuda:

@@ -27,8 +27,11 @@ PREFILL_CHUNK = 64
 
 
 class Runtime:
-    def __init__(self, decoder, max_slots=8, max_len=4096, device=None):
+    def __init__(self, decoder, max_slots=8, max_len=4096, device=None, tp=None):
+        """``tp``: a ``serve.tp.TPContext`` when ``decoder`` is this rank's tensor-parallel shard
+        (``serve.tp.shard_decoder``); greedy decoding only."""
         self.dec = decoder
+        self.tp = tp
         self.cfg = cfg = decoder.cfg
         p = next(decoder.parameters())
         self.device = torch.device(device) if device is not None else p.device
@@ -134,9 +137,17 @@ class Runtime:
         if isinstance(g, _Graph) and logits.data_ptr() == g.logits.data_ptr():
             return g.am[:logits.shape[0]]
         if not self.cuda:
-            return logits.argmax(-1)
-        out = torch.empty(logits.shape[:-1], dtype=torch.long, device=logits.device)
-        self.C.argmax_rows(logits.reshape(-1, logits.shape[-1]), out.view(-1))
+            out = logits.argmax(-1)
+        else:
+            out = torch.empty(logits.shape[:-1], dtype=torch.long, device=logits.device)
+            self.C.argmax_rows(logits.reshape(-1, logits.shape[-1]), out.view(-1))
+        if self.tp is not None:
+            # vocabulary-parallel: every rank's (max, global index); the first maximum wins
+            val = logits.gather(-1, out.unsqueeze(-1)).squeeze(-1)
+            pair = torch.stack([val, (out + self.dec.vocab_offset).float()], -1)
+            allp = self.tp.gather(pair)                                      # [W, ..., 2]
+            best = allp[..., 0].argmax(0, keepdim=True)
+            out = allp[..., 1].gather(0, best).squeeze(0).long()
         return out
 
     def _forward(self, st, tokens):
@@ -226,6 +237,8 @@ class Runtime:
         return R.rmsnorm(x, w, self.cfg.eps)
 
     def _lin(self, x, w, residual=None):
+        if self.tp is not None and residual is not None:
+            return self.tp.row_parallel(x, w, residual)
         if self.cuda:
             out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
             if residual is None:
@@ -248,7 +261,7 @@ class Runtime:
 
     def _logits(self, h):
         h = self._rms(h, self.dec.norm)
-        W = self.dec.lm_weight
+        W = self.dec.lm_shard if self.tp is not None else self.dec.lm_weight
         if self.cuda:
             out = torch.empty(h.shape[0], W.shape[0], dtype=torch.float32, device=h.device)
             self.blocks.gemm(self.blocks.TN, h, W, out)

@@ -1,0 +1,137 @@
+"""Tensor-parallel serving: shard a decoder over the ranks of one node (one process per GPU).
+
+Megatron-style split (survey P4; the reference leaves TP to SGLang's engine flag):
+  full attention  query heads split (column-parallel ``[q|gate]``/k/v rows), key/value heads split
+                  or, with more ranks than KV heads, replicated so every rank holds the KV head of
+                  its query heads; ``o_proj`` row-parallel
+  gated delta     key / value heads split (``in_proj`` rows, conv channels, ``A_log``, ``dt_bias``);
+                  ``out_proj`` row-parallel
+  MLP             gate / up rows split, ``down_proj`` row-parallel
+  LM head         vocabulary split; greedy tokens come from each rank's (max, argmax) pair
+Each row-parallel GEMM writes its partial sum into this rank's symmetric peer buffer and one
+all-reduce kernel (``csrc/symm.cu``) reads every rank's partial over NVLink, adds the residual and
+writes the layer output -- no NCCL on the decode path.
+"""
+import copy
+
+import torch
+import torch.distributed as dist
+
+from ..parallel.symm import SymmetricHeap
+
+
+def _split(n, world, rank, what):
+    if n % world:
+        raise ValueError(f"{what} ({n}) must divide evenly over {world} ranks")
+    k = n // world
+    return rank * k, (rank + 1) * k
+
+
+def shard_decoder(dec, rank, world):
+    """A copy of ``dec`` holding this rank's shard (config head counts divided accordingly)."""
+    cfg = dec.cfg
+    local = copy.copy(dec)
+    local._modules = dict(dec._modules)          # own registries: the original stays untouched
+    local._parameters = dict(dec._parameters)
+    lcfg = copy.deepcopy(cfg)
+    Hq, Hkv, d = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+    q0, q1 = _split(Hq, world, rank, "query heads")
+    lcfg.n_heads = q1 - q0
+    if Hkv >= world:
+        k0, k1 = _split(Hkv, world, rank, "key/value heads")
+    else:                                     # replicate: the KV head of this rank's query heads
+        if world % Hkv or (Hq // Hkv) % (Hq // world):
+            raise ValueError(f"{world} ranks cannot share {Hkv} key/value heads of {Hq} query heads")
+        k0 = q0 // (Hq // Hkv)
+        k1 = k0 + 1
+    lcfg.n_kv_heads = k1 - k0
+    F = cfg.intermediate_size
+    f0, f1 = _split(F, world, rank, "FFN width")
+    lcfg.intermediate_size = f1 - f0
+    if cfg.layer_types and "linear_attention" in cfg.layer_types:
+        hk0, hk1 = _split(cfg.lin_k_heads, world, rank, "gated-delta key heads")
+        hv0, hv1 = _split(cfg.lin_v_heads, world, rank, "gated-delta value heads")
+        lcfg.lin_k_heads, lcfg.lin_v_heads = hk1 - hk0, hv1 - hv0
+    local.cfg = lcfg
+    layers = torch.nn.ModuleList()
+    with torch.no_grad():
+        for layer in dec.layers:
+            L = copy.copy(layer)
+            L._parameters = dict(layer._parameters)
+            P = lambda t: torch.nn.Parameter(t.contiguous(), requires_grad=False)   # noqa: E731
+            L.wgu = P(torch.cat([layer.wgu[f0:f1], layer.wgu[F + f0:F + f1]]))
+            L.wdown = P(layer.wdown[:, f0:f1])
+            if layer.layer_type == "full_attention":
+                qs = 2 * d if cfg.attn_output_gate else d
+                wq = layer.wqkv[:Hq * qs].view(Hq, qs, -1)[q0:q1].reshape(-1, layer.wqkv.shape[1])
+                wk = layer.wqkv[Hq * qs:Hq * qs + Hkv * d].view(Hkv, d, -1)[k0:k1].reshape(-1, layer.wqkv.shape[1])
+                wv = layer.wqkv[Hq * qs + Hkv * d:].view(Hkv, d, -1)[k0:k1].reshape(-1, layer.wqkv.shape[1])
+                L.wqkv = P(torch.cat([wq, wk, wv]))
+                L.wo = P(layer.wo.view(layer.wo.shape[0], Hq, d)[:, q0:q1].reshape(layer.wo.shape[0], -1))
+            else:
+                dk, dv = cfg.lin_k_dim, cfg.lin_v_dim
+                Hk, Hv = cfg.lin_k_heads, cfg.lin_v_heads
+                kd, vd = Hk * dk, Hv * dv
+                w = layer.w_in
+                rows = [w[hk0 * dk:hk1 * dk], w[kd + hk0 * dk:kd + hk1 * dk], w[2 * kd + hv0 * dv:2 * kd + hv1 * dv],
+                        w[2 * kd + vd + hv0 * dv:2 * kd + vd + hv1 * dv],
+                        w[2 * kd + 2 * vd + hv0:2 * kd + 2 * vd + hv1],
+                        w[2 * kd + 2 * vd + Hv + hv0:2 * kd + 2 * vd + Hv + hv1]]
+                L.w_in = P(torch.cat(rows))
+                c = layer.conv_w
+                L.conv_w = P(torch.cat([c[hk0 * dk:hk1 * dk], c[kd + hk0 * dk:kd + hk1 * dk],
+                                        c[2 * kd + hv0 * dv:2 * kd + hv1 * dv]]))
+                L.A_log = P(layer.A_log[hv0:hv1])
+                L.dt_bias = P(layer.dt_bias[hv0:hv1])
+                L.w_out = P(layer.w_out[:, hv0 * dv:hv1 * dv])
+            layers.append(L)
+    local.layers = layers
+    V = cfg.vocab_size
+    vp = (V + world - 1) // world
+    lm = dec.lm_weight
+    sl = lm[rank * vp:min(V, (rank + 1) * vp)]
+    if sl.shape[0] < vp:     # pad the last shard; padded rows never win the argmax
+        sl = torch.cat([sl, torch.zeros(vp - sl.shape[0], sl.shape[1], dtype=sl.dtype, device=sl.device)])
+    local.lm_shard = sl.contiguous()
+    local.vocab_offset = rank * vp
+    local.vocab_size_full = V
+    return local
+
+
+class TPContext:
+    """Per-process TP state: the process group, the symmetric buffers of the row-parallel
+    all-reduces (two, used alternately) and the vocabulary-parallel greedy pick."""
+
+    def __init__(self, max_rows, hidden, group=None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.heap = SymmetricHeap(group)
+        self.bufs = [self.heap.alloc(max_rows * hidden, torch.bfloat16) for _ in range(2)]
+        self.turn = 0
+        self.max_rows, self.hidden = max_rows, hidden
+
+    def next_buffer(self, rows):
+        if rows > self.max_rows:
+            raise RuntimeError(f"{rows} rows exceed the TP buffers ({self.max_rows})")
+        b = self.bufs[self.turn]
+        self.turn ^= 1
+        return b, b.local[:rows * self.hidden].view(rows, self.hidden)
+
+    def row_parallel(self, x, w, residual):
+        """residual + sum over ranks of x_r w_r^T: the GEMM writes this rank's partial into its
+        symmetric buffer, one all-reduce kernel sums all partials over NVLink (+ residual)."""
+        from ..ops import blocks
+        buf, part = self.next_buffer(x.shape[0])
+        blocks.gemm(blocks.TN, x, w, part)
+        return self.allreduce(buf, x.shape[0], residual)
+
+    def allreduce(self, buf, rows, residual):
+        out = torch.empty(rows, self.hidden, dtype=torch.bfloat16, device=residual.device)
+        self.heap.allreduce_(buf, 0, rows * self.hidden, out.view(-1), residual.contiguous().view(-1))
+        return out
+
+    def gather(self, t):
+        out = torch.empty((self.world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
+        return out
