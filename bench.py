@@ -47,7 +47,7 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--layers", type=int, default=36, help="debug only: fewer layers (reported as reduced)")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--comm", choices=["fused", "nccl"], default="nccl",
+    p.add_argument("--comm", choices=["fused", "nccl"], default="fused",
                    help="multi-GPU optimizer traffic: fused peer-memory kernels or NCCL collectives")
     return p.parse_args()
 
@@ -344,7 +344,10 @@ def main():
                        "global_batch": world * MB, "seq_len": PROMPT + RESP,
                        "forward_row": "[S 1024 | x_t 1024 | x_0 1024] x 2 views",
                        "forward_tokens_per_step": world * MB * 2 * (PROMPT + 2 * RESP),
-                       "parallelism": f"dp{world} (sharded optimizer state)", "bd_size": BD,
+                       "parallelism": f"dp{world} (sharded optimizer state; " + (
+                           "gradient reduce-scatter + AdamW + parameter all-gather fused over NVLink peer memory)"
+                           if args.comm == "fused" and world > 1 else "NCCL collectives)" if world > 1 else "single GPU)"),
+                       "bd_size": BD,
                        "ar_loss_weight": 1.0, "optimizer": "AdamW lr 1e-5 (warmup 50, cosine)",
                        "l2": "inputs larger than L2 (per-step working set >> 126 MB)",
                        "peak_mem_gb": round(peak_gb, 1)},

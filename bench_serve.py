@@ -4,7 +4,7 @@ Model: Qwen3.5-4B-style hybrid (32 layers, 3 gated-delta : 1 full attention, hid
 vocab 248320, full layers 16 Q / 4 KV x 256 with the output gate and partial RoPE, gated-delta
 16 key / 32 value heads x 128, conv 4), random init, bf16.  Load: ``--requests`` concurrent
 requests of ``--prompt`` uniform random tokens each, ``--max-new`` output tokens each, greedy.
-Decoding: self-speculative with ``--n`` causal rows per canvas (canvas of 2N-1 rows), or
+Decoding: self-speculative with ``--gen-block`` (N) causal rows per canvas (canvas of 2N-1 rows), or
 ``--mode causal``.
 
 Reports (one JSON line): decode tokens/s (all generated tokens / device-timed decode phase),
@@ -12,7 +12,7 @@ tokens per forward, p50 TTFT, and the device-timed prefill.  Random weights make
 nearly never match, so tokens per forward stays near its floor of 1 (the reference's ~2.3 is a
 trained-checkpoint figure); the throughput per forward is what the kernels determine.
 
-    python bench_serve.py [--requests 64 --prompt 512 --max-new 512 --n 16 --layers 32]
+    python bench_serve.py [--requests 64 --prompt 512 --max-new 512 --gen-block 16 --layers 32 --tp 1]
 """
 import argparse
 import json
@@ -41,7 +41,7 @@ def main():
     ap.add_argument("--requests", type=int, default=64)
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--max-new", type=int, default=512)
-    ap.add_argument("--n", type=int, default=16, help="causal rows per canvas (canvas = 2N-1 rows)")
+    ap.add_argument("--gen-block", type=int, default=16, help="N: causal rows per canvas (canvas = 2N-1 rows)")
     ap.add_argument("--mode", default="self-spec", choices=["self-spec", "causal"])
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--seed", type=int, default=0)
@@ -67,14 +67,14 @@ def main():
     cfg = hybrid_config(args.layers)
     dec = Decoder(cfg, dtype=torch.bfloat16, device="cuda")
     mask_id = cfg.vocab_size - 1
-    max_len = args.prompt + args.max_new + 2 * args.n + 8
+    max_len = args.prompt + args.max_new + 2 * args.gen_block + 8
     if world > 1:
         from trida_stack_b200.serve.tp import TPContext, shard_decoder
         dec = shard_decoder(dec, rank, world)
         torch.cuda.empty_cache()
         tp = TPContext(max_rows=args.requests * 64, hidden=cfg.hidden_size)
     rt = Runtime(dec, max_slots=args.requests, max_len=max_len, tp=tp)
-    eng = Engine(rt, mask_id=mask_id, mode=args.mode, n=args.n, max_running=args.requests, graphs=not args.no_graphs)
+    eng = Engine(rt, mask_id=mask_id, mode=args.mode, n=args.gen_block, max_running=args.requests, graphs=not args.no_graphs)
     g = torch.Generator().manual_seed(args.seed)
 
     def prompts(k):
@@ -117,8 +117,8 @@ def main():
         "prefill_ms": round(prefill_ms, 2), "decode_ms": round(decode_ms, 2), "decode_steps": steps,
         "ms_per_step": round(decode_ms / max(steps, 1), 3), "wall_s": round(wall, 2), "tp": world,
         "config": {"model": f"Qwen3.5-4B-style hybrid ({args.layers}L)", "requests": args.requests,
-                   "prompt": args.prompt, "max_new": args.max_new, "mode": args.mode, "n": args.n,
-                   "canvas_rows": 2 * args.n - 1 if args.mode == "self-spec" else 1, "greedy": True,
+                   "prompt": args.prompt, "max_new": args.max_new, "mode": args.mode, "n": args.gen_block,
+                   "canvas_rows": 2 * args.gen_block - 1 if args.mode == "self-spec" else 1, "greedy": True,
                    "cuda_graphs": not args.no_graphs},
         "data": "synthetic uniform prompts, random-init weights", "dtype": "bf16"}), flush=True)
     _finish(rt, world)
