@@ -39,7 +39,9 @@ struct Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = MH == 1 ? 4 : 3;
   static constexpr int NACC = MH == 1 ? 2 : 1;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 256 + 1024;
+  // epilogue staging: 4 warps x 2 buffers x (32 rows x 128 B), TMA-stored (128B swizzle)
+  static constexpr int EPI_BYTES = 4 * 2 * 4096;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 256 + 1024;
 };
 
 struct Params {
@@ -63,6 +65,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
       : "memory");
 }
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];\n" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_addr(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;\n" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
 
 __device__ __forceinline__ void tile_coords(int tile, int mt, int nt, int bm, int& m0, int& n0) {
   const int per_group = GROUP_M * nt;
@@ -93,19 +105,22 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kmajor, int 
 
 template <int MH>
 __global__ void __launch_bounds__(NTHREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmC, const Params p) {
   using C_ = Cfg<MH>;
   constexpr int BM = C_::BM, STAGES = C_::STAGES, NACC = C_::NACC;
   constexpr int A_BYTES = C_::A_BYTES, STAGE_BYTES = C_::STAGE_BYTES;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  unsigned char* epi = smem + STAGES * STAGE_BYTES;                 // 1024-aligned staging
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi + C_::EPI_BYTES);
   uint64_t* full = bars;                       // [STAGES]
   uint64_t* empty = bars + STAGES;             // [STAGES]
   uint64_t* acc_full = bars + 2 * STAGES;      // [NACC]
   uint64_t* acc_empty = bars + 2 * STAGES + 2; // [NACC]
   uint64_t* drain = bars + 2 * STAGES + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 6);
+  uint64_t* cbar = bars + 2 * STAGES + 8;      // [4 warps x 2 buffers] C-tile loads
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mt = (p.M + BM - 1) / BM, nt = (p.N + BN - 1) / BN;
@@ -122,6 +137,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_init(&acc_empty[b], 128);
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < 8; ++i) mbar_init(&cbar[i], 1);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
@@ -190,6 +206,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int q = warp & 3;
     const int r = q * 32 + lane;                       // accumulator row (TMEM lane)
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    int ebuf = 0;
+    uint32_t cpar[2] = {0u, 0u};
     int t = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++t) {
       const int ab = t % NACC;
@@ -226,64 +244,71 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         continue;
       }
+      // Chunks of 128 B per row (32 fp32 / 64 bf16 columns): scale (+ beta * C, C fetched by
+      // TMA into the staging tile), write the warp's 32 x 128 B tile in the 128B-swizzled layout
+      // and TMA-store it (clipped at the matrix edge by the tensor map); two staging buffers
+      // per warp so the next chunk fills while the previous store drains.
+      const int esz = p.d_fp32 ? 4 : 2;
+      const int cc = 128 / esz;                       // columns per chunk
+      const int row0 = m0 + h * 128 + q * 32;         // the warp's first row
+      const bool use_c = p.C != nullptr && p.beta != 0.f;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(acc + c * 32, v);
+      for (int ch = 0; ch < BN / cc; ++ch) {
+        uint32_t v0[32], v1[32];
+        tmem_ld32(acc + ch * cc, v0);
+        if (esz == 2) tmem_ld32(acc + ch * cc + 32, v1);
         tmem_wait_ld();
-        const int col0 = n0 + c * 32;
-        if (!rok || col0 >= p.N) continue;
-        float f[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) * p.alpha;
-        const bool full_cols = col0 + 32 <= p.N;
-        if (p.d_fp32) {
-          float* dst = reinterpret_cast<float*>(p.D) + (int64_t)row * p.ldd + col0;
-          const float* csrc = p.C ? reinterpret_cast<const float*>(p.C) + (int64_t)row * p.ldc + col0 : nullptr;
-          if (full_cols) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              float4 o = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
-              if (csrc && p.beta != 0.f) {
-                const float4 cv = *reinterpret_cast<const float4*>(csrc + j);
-                o.x += p.beta * cv.x; o.y += p.beta * cv.y; o.z += p.beta * cv.z; o.w += p.beta * cv.w;
-              }
-              *reinterpret_cast<float4*>(dst + j) = o;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < p.N) dst[j] = f[j] + ((csrc && p.beta != 0.f) ? p.beta * csrc[j] : 0.f);
+        const int col0 = n0 + ch * cc;
+        if (row0 >= p.M || col0 >= p.N) continue;     // warp-uniform
+        unsigned char* sb = epi + q * 8192 + ebuf * 4096;
+        if (lane == 0) bulk_wait_read1();             // the store issued from sb two chunks ago has read it
+        __syncwarp();
+        if (use_c) {
+          if (lane == 0) {
+            mbar_expect_tx(&cbar[q * 2 + ebuf], 4096);
+            tma_load_2d(sb, &tmC, &cbar[q * 2 + ebuf], col0, row0);
           }
-        } else {
-          bf16* dst = reinterpret_cast<bf16*>(p.D) + (int64_t)row * p.ldd + col0;
-          const bf16* csrc = p.C ? reinterpret_cast<const bf16*>(p.C) + (int64_t)row * p.ldc + col0 : nullptr;
-          if (full_cols) {
+          mbar_wait(&cbar[q * 2 + ebuf], cpar[ebuf], p.err, 107);
+          cpar[ebuf] ^= 1;
+        }
+        unsigned char* rowp = sb + lane * 128;
 #pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              float o[8];
-#pragma unroll
-              for (int e = 0; e < 8; ++e) o[e] = f[j + e];
-              if (csrc && p.beta != 0.f) {
-                float cv[8];
-                load8(csrc + j, cv);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) o[e] += p.beta * cv[e];
-              }
-              store8(dst + j, o);
+        for (int j = 0; j < 8; ++j) {
+          float4* cp = reinterpret_cast<float4*>(rowp + ((j ^ (lane & 7)) << 4));
+          if (esz == 4) {
+            float4 o = make_float4(__uint_as_float(v0[4 * j]) * p.alpha, __uint_as_float(v0[4 * j + 1]) * p.alpha,
+                                   __uint_as_float(v0[4 * j + 2]) * p.alpha, __uint_as_float(v0[4 * j + 3]) * p.alpha);
+            if (use_c) {
+              const float4 cv = *cp;
+              o.x += p.beta * cv.x; o.y += p.beta * cv.y; o.z += p.beta * cv.z; o.w += p.beta * cv.w;
             }
+            *cp = o;
           } else {
+            float o[8];
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < p.N)
-                dst[j] = __float2bfloat16(f[j] + ((csrc && p.beta != 0.f) ? p.beta * __bfloat162float(csrc[j]) : 0.f));
+            for (int e = 0; e < 8; ++e) o[e] = __uint_as_float(j < 4 ? v0[8 * j + e] : v1[8 * (j - 4) + e]) * p.alpha;
+            if (use_c) {
+              float cv[8];
+              load8(reinterpret_cast<const bf16*>(cp), cv);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) o[e] += p.beta * cv[e];
+            }
+            store8(reinterpret_cast<bf16*>(cp), o);
           }
         }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmD, sb, col0, row0);
+          bulk_commit();
+        }
+        ebuf ^= 1;
       }
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[ab]);
     }
+    if (lane == 0) bulk_wait_all();                   // every store of this warp has landed
   }
   tc_fence_before();
   __syncthreads();
@@ -326,6 +351,21 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+// Epilogue map over D or C: [rows, cols] row-major (bf16 or fp32), box {128 B of columns, 32 rows},
+// 128B swizzle (the staging layout the epilogue writes).
+static bool make_epi_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, bool fp32) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const int esz = fp32 ? 4 : 2;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * esz};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / esz), 32};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
+            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // 2-D bf16 map over a row-major [rows, cols] matrix with leading dimension ld; box {64, box_rows}.
 static bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
   auto fn = encode_fn();
@@ -361,8 +401,8 @@ int gemm_splitk(int M, int N, int K, int sm_count) {
 }
 
 template <int MH>
-static int launch(const CUtensorMap& mA, const CUtensorMap& mB, const gemm100::Params& p, int sm_count,
-                  cudaStream_t stream) {
+static int launch(const CUtensorMap& mA, const CUtensorMap& mB, const CUtensorMap& mD, const CUtensorMap& mC,
+                  const gemm100::Params& p, int sm_count, cudaStream_t stream) {
   using namespace gemm100;
   static bool init = false;
   if (!init) {
@@ -371,7 +411,7 @@ static int launch(const CUtensorMap& mA, const CUtensorMap& mB, const gemm100::P
   }
   const int units = ((p.M + Cfg<MH>::BM - 1) / Cfg<MH>::BM) * ((p.N + BN - 1) / BN) * p.splits;
   const int grid = units < sm_count ? units : sm_count;
-  gemm_kernel<MH><<<grid, NTHREADS, Cfg<MH>::SMEM_BYTES, stream>>>(mA, mB, p);
+  gemm_kernel<MH><<<grid, NTHREADS, Cfg<MH>::SMEM_BYTES, stream>>>(mA, mB, mD, mC, p);
   return 0;
 }
 
@@ -413,8 +453,15 @@ int gemm_bf16(GemmLayout layout, bool d_fp32, const GemmArgs& a, int tile, int s
       return -11;
   }
   if (!ok) return -12;
-  if (mh == 2) launch<2>(mA, mB, p, sm_count, stream);
-  else launch<1>(mA, mB, p, sm_count, stream);
+  CUtensorMap mD, mC;
+  if (!make_epi_map(&mD, a.D, a.M, a.N, a.ldd, d_fp32)) return -14;
+  if (a.C != nullptr && a.beta != 0.f) {
+    if (!make_epi_map(&mC, a.C, a.M, a.N, a.ldc, d_fp32)) return -15;
+  } else {
+    mC = mD;
+  }
+  if (mh == 2) launch<2>(mA, mB, mD, mC, p, sm_count, stream);
+  else launch<1>(mA, mB, mD, mC, p, sm_count, stream);
   if (p.splits > 1) {
     const int64_t n4 = (int64_t)a.M * ((a.N + 3) / 4);
     const int blocks = (int)std::min<int64_t>((n4 + 255) / 256, (int64_t)sm_count * 8);
