@@ -238,6 +238,8 @@ void gdn_fwd(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor& gb
   CHECK_BF16(o); TORCH_CHECK(o.is_contiguous() && o.numel() == B * T * Hv * 128, "o must be [B*T, Hv*128]");
   TORCH_CHECK(ckpt.scalar_type() == at::kFloat && ckpt.numel() >= trida::gdn_state_floats(p), "ckpt too small");
   p.ckpt = ckpt.data_ptr<float>(); p.o = mbf(o);
+  at::Tensor prep = at::empty({trida::gdn_prep_floats(B * T, Hk, Hv)}, mixed.options().dtype(at::kFloat));
+  p.prep = prep.data_ptr<float>();
   if (final_state.has_value() && final_state->defined()) {
     TORCH_CHECK(final_state->scalar_type() == at::kFloat && final_state->is_contiguous() &&
                 final_state->numel() == B * Hv * 128 * 128, "final_state must be fp32 [B, Hv, 128, 128]");
@@ -270,6 +272,8 @@ void gdn_bwd(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor& gb
   p.dqk = dqk.data_ptr<float>(); p.dgb = dgbuf.data_ptr<float>();
   p.dv = mbf(dmixed) + 2 * Hk * 128; p.lddv = dmixed.stride(0);
   p.dinit = mode ? dinit.data_ptr<float>() : nullptr;
+  at::Tensor prep = at::empty({trida::gdn_prep_floats(B * T, Hk, Hv)}, mixed.options().dtype(at::kFloat));
+  p.prep = prep.data_ptr<float>();
   c10::cuda::CUDAGuard g(mixed.device());
   const int rc = trida::gdn_bwd(p, mbf(dmixed), dmixed.stride(0), mbf(dga), mbf(dgb), dga.stride(0),
                                 dA_log.data_ptr<float>(), ddt_bias.data_ptr<float>(), stream());

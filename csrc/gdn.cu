@@ -9,8 +9,9 @@
 // Recurrence per value head (state S [dk=128, dv=128] in fp32; q, k L2-normalised, q * dk^-0.5):
 //     S' = exp(g) S ;  u = beta (v - S'^T k) ;  S = S' + k u^T ;  o = S^T q
 // Every value column of S evolves on its own, so a head is split over 8 CTAs of 16 columns and a
-// CTA keeps its 128 x 16 slice in registers: thread (column c, row part r) owns rows [16r, 16r+16)
-// of column c; the dot products over dk are 3-step shuffles inside each group of 8 lanes.
+// CTA keeps its 128 x 16 slice in registers: thread (column c, row part r) owns 16 rows of column
+// c (4 groups of 4, interleaved so shared-memory reads are conflict-free); the dot products over
+// dk are 3-step shuffles inside each group of 8 lanes.
 //
 // Forward: fwd_clean walks the clean stream (or the whole causal row) in chunks, storing the state
 // at every chunk start (block starts in the two-stream layout) as the backward's checkpoints and
@@ -65,6 +66,8 @@ struct Args {
   int64_t lddv;
   float* dinit;             // [B, Hv, nch, NCG, RPT, NT]
   float* final_state;       // optional [B, Hv, DK, DV] state after the last clean token (serving prefill)
+  const float* qk;          // prep: [B*T, Hk, 2, DK] L2-normalised q (times scale) and k
+  const float* ab;          // prep: [B*T, Hv, 2] decay exp(g) and beta
 };
 
 struct Stage {
@@ -112,55 +115,15 @@ __device__ __forceinline__ float rsum8(float x) {
 
 __device__ __forceinline__ float softplus_f(float x) { return x > 20.f ? x : log1pf(expf(x)); }
 
-// Stage n tokens (row-relative indices tok0 .. tok0+n-1 of row b) for value head hv / columns cg:
-// L2-normalised q (times scale) and k of the head's key head, the CTA's v (and dO) columns, the
-// decay alpha = exp(g), beta, and reset flags (clean positions pos0.. when pos0 >= 0).
-__device__ void stage_tokens(const Args& a, const Stage& s, int b, int hv, int cg, int tok0, int n, int pos0,
-                             bool bwd) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int hk = hv / (a.Hv / a.Hk);
-  const int Lc = a.mode ? a.L : a.T;
-  for (int j = warp; j < n; j += NT / 32) {
-    const int64_t row = (int64_t)b * a.T + tok0 + j;
-    const bf16* src = a.mixed + row * a.ldm;
-    float qv[4], kv[4];
-    const uint2 qr = *reinterpret_cast<const uint2*>(src + hk * DK + lane * 4);
-    const uint2 kr = *reinterpret_cast<const uint2*>(src + a.Hk * DK + hk * DK + lane * 4);
-    const bf16* qp = reinterpret_cast<const bf16*>(&qr);
-    const bf16* kp = reinterpret_cast<const bf16*>(&kr);
-    float sq = 0.f, sk = 0.f;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      qv[e] = __bfloat162float(qp[e]);
-      kv[e] = __bfloat162float(kp[e]);
-      sq += qv[e] * qv[e];
-      sk += kv[e] * kv[e];
-    }
-    sq = warp_sum(sq);
-    sk = warp_sum(sk);
-    const float rq = rsqrtf(sq + 1e-6f) * a.scale, rk = rsqrtf(sk + 1e-6f);
-    *reinterpret_cast<float4*>(s.q + j * DK + lane * 4) = make_float4(qv[0] * rq, qv[1] * rq, qv[2] * rq, qv[3] * rq);
-    *reinterpret_cast<float4*>(s.k + j * DK + lane * 4) = make_float4(kv[0] * rk, kv[1] * rk, kv[2] * rk, kv[3] * rk);
-    if (lane < CG) {
-      s.v[j * CG + lane] = __bfloat162float(src[2 * a.Hk * DK + hv * DV + cg * CG + lane]);
-    } else if (bwd) {
-      s.dO[j * CG + lane - CG] = __bfloat162float(a.d_o[row * (int64_t)(a.Hv * DV) + hv * DV + cg * CG + lane - CG]);
-    }
-    if (lane == 0) {
-      const float av = __bfloat162float(a.ga[row * a.ldg + hv]) + a.dt_bias[hv];
-      const float bv = __bfloat162float(a.gb[row * a.ldg + hv]);
-      const float g = -expf(a.A_log[hv]) * softplus_f(av);
-      s.al[j] = expf(g);
-      s.be[j] = 1.f / (1.f + expf(-bv));
-      s.rs[j] = (pos0 >= 0 && a.doc != nullptr) ? (int)a.doc[(int64_t)b * Lc + pos0 + j] : 0;
-    }
-  }
-}
+// Thread (column, row part rp) owns rows {32 f + 4 rp + e : f, e in 0..3} of its column, so the 8
+// row parts of a warp read one contiguous 128 B line of a staged q / k vector per float4 load
+// (conflict-free).  `p` points at the vector plus 4 rp.
+__device__ __forceinline__ int own_row(int rp, int i) { return (i >> 2) * 32 + rp * 4 + (i & 3); }
 
 __device__ __forceinline__ void load16(const float* p, float (&x)[RPT]) {
 #pragma unroll
   for (int i = 0; i < RPT; i += 4) {
-    const float4 t = *reinterpret_cast<const float4*>(p + i);
+    const float4 t = *reinterpret_cast<const float4*>(p + (i >> 2) * 32);
     x[i] = t.x; x[i + 1] = t.y; x[i + 2] = t.z; x[i + 3] = t.w;
   }
 }
@@ -207,60 +170,8 @@ __device__ __forceinline__ float* state_ptr(float* base, const Args& a, int b, i
 }
 
 // ---------------------------------------------------------------------------------------------
-// forward
-// ---------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(NT) fwd_clean_kernel(const Args a) {
-  extern __shared__ float smem[];
-  const int cg = blockIdx.x, hv = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x, col = tid / RP, rp = tid % RP;
-  const Stage s = carve(smem, a.ch, false);
-  const int Lc = a.mode ? a.L : a.T;
-  const bool tok_read = a.mode == 0 || a.causal_clean;
-  float S[RPT];
-#pragma unroll
-  for (int i = 0; i < RPT; ++i) S[i] = 0.f;
-  for (int c = 0; c < a.nch; ++c) {
-    const int p0 = c * a.ch, n = min(a.ch, Lc - p0);
-    float* ck = state_ptr(a.ckpt, a, b, hv, c, cg);
-#pragma unroll
-    for (int i = 0; i < RPT; ++i) ck[i * NT + tid] = S[i];
-    stage_tokens(a, s, b, hv, cg, p0, n, p0, false);
-    __syncthreads();
-    for (int j = 0; j < n; ++j) {
-      if (s.rs[j]) {
-#pragma unroll
-        for (int i = 0; i < RPT; ++i) S[i] = 0.f;
-      }
-      float u, vmp;
-      fwd_step(S, s.k + j * DK + rp * RPT, s.al[j], s.be[j], s.v[j * CG + col], u, vmp);
-      if (tok_read) {
-        const float o = readout(S, s.q + j * DK + rp * RPT);
-        if (rp == 0) s.ob[j * CG + col] = o;
-      }
-    }
-    if (!tok_read) {
-      for (int j = 0; j < n; ++j) {
-        const float o = readout(S, s.q + j * DK + rp * RPT);
-        if (rp == 0) s.ob[j * CG + col] = o;
-      }
-    }
-    __syncthreads();
-    store_o(a, s, b, hv, cg, p0, n);
-    __syncthreads();
-  }
-  if (a.final_state != nullptr) {
-    float* f = a.final_state + ((int64_t)b * a.Hv + hv) * DK * DV + cg * CG + col;
-#pragma unroll
-    for (int i = 0; i < RPT; ++i) f[(rp * RPT + i) * DV] = S[i];
-  }
-}
-
-// ---------------------------------------------------------------------------------------------
-// serving: one canvas of T rows per request from the cached state (rows < n_clean token-causal,
-// the rest read the state after the last row), and the commit that advances the cached state by
-// adv[b] rows.  The state cache is kept in the thread-native layout [slots, Hv, NCG, RPT, NT] so
-// every load / store is coalesced; a prep pass writes each row's L2-normalised q (times scale) and
-// k once ([rows, Hk, 2, DK] fp32) and its decay / beta ([rows, Hv, 2]) for both kernels.
+// prep: per token and key head the L2-normalised q (times scale) and k, per value head the decay
+// exp(g) and beta, computed once (fully parallel) so the sequential scans stage plain copies.
 // ---------------------------------------------------------------------------------------------
 __global__ void prep_kernel(const Args a, float* qk, float* ab, int rows) {
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -294,28 +205,89 @@ __global__ void prep_kernel(const Args a, float* qk, float* ab, int rows) {
   }
 }
 
-// Stage rows 0..n-1 of request b from the prep buffers (plain coalesced copies).
+// Stage n tokens (row-relative tok0 ..) of row b from the prep buffers: plain coalesced copies of
+// the normalised q / k, the CTA's v (and dO) columns, decay / beta and the reset flags (clean
+// positions pos0.. when pos0 >= 0).
 __device__ __forceinline__ void stage_prepped(const Args& a, const Stage& s, const float* qk, const float* ab, int b,
-                                              int hv, int cg, int n) {
+                                              int hv, int cg, int tok0, int n, int pos0, bool bwd) {
   const int hk = hv / (a.Hv / a.Hk);
+  const int Lc = a.mode ? a.L : a.T;
   for (int idx = threadIdx.x; idx < n * (DK / 4) * 2; idx += NT) {
     const int j = idx / (DK / 2), rem = idx % (DK / 2), isk = rem / (DK / 4), c4 = rem % (DK / 4);
-    const int64_t row = (int64_t)b * a.T + j;
+    const int64_t row = (int64_t)b * a.T + tok0 + j;
     const float4 v = *reinterpret_cast<const float4*>(qk + ((row * a.Hk + hk) * 2 + isk) * DK + c4 * 4);
     *reinterpret_cast<float4*>((isk ? s.k : s.q) + j * DK + c4 * 4) = v;
   }
   for (int idx = threadIdx.x; idx < n * CG; idx += NT) {
     const int j = idx / CG, c = idx % CG;
-    const int64_t row = (int64_t)b * a.T + j;
+    const int64_t row = (int64_t)b * a.T + tok0 + j;
     s.v[idx] = __bfloat162float(a.mixed[row * a.ldm + 2 * a.Hk * DK + hv * DV + cg * CG + c]);
+    if (bwd) s.dO[idx] = __bfloat162float(a.d_o[row * (int64_t)(a.Hv * DV) + hv * DV + cg * CG + c]);
   }
   for (int j = threadIdx.x; j < n; j += NT) {
-    const int64_t row = (int64_t)b * a.T + j;
+    const int64_t row = (int64_t)b * a.T + tok0 + j;
     s.al[j] = ab[(row * a.Hv + hv) * 2];
     s.be[j] = ab[(row * a.Hv + hv) * 2 + 1];
+    s.rs[j] = (pos0 >= 0 && a.doc != nullptr) ? (int)a.doc[(int64_t)b * Lc + pos0 + j] : 0;
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(NT) fwd_clean_kernel(const Args a) {
+  extern __shared__ float smem[];
+  const int cg = blockIdx.x, hv = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, col = tid / RP, rp = tid % RP;
+  const Stage s = carve(smem, a.ch, false);
+  const int Lc = a.mode ? a.L : a.T;
+  const bool tok_read = a.mode == 0 || a.causal_clean;
+  float S[RPT];
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) S[i] = 0.f;
+  for (int c = 0; c < a.nch; ++c) {
+    const int p0 = c * a.ch, n = min(a.ch, Lc - p0);
+    float* ck = state_ptr(a.ckpt, a, b, hv, c, cg);
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) ck[i * NT + tid] = S[i];
+    stage_prepped(a, s, a.qk, a.ab, b, hv, cg, p0, n, p0, false);
+    __syncthreads();
+    for (int j = 0; j < n; ++j) {
+      if (s.rs[j]) {
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) S[i] = 0.f;
+      }
+      float u, vmp;
+      fwd_step(S, s.k + j * DK + rp * 4, s.al[j], s.be[j], s.v[j * CG + col], u, vmp);
+      if (tok_read) {
+        const float o = readout(S, s.q + j * DK + rp * 4);
+        if (rp == 0) s.ob[j * CG + col] = o;
+      }
+    }
+    if (!tok_read) {
+      for (int j = 0; j < n; ++j) {
+        const float o = readout(S, s.q + j * DK + rp * 4);
+        if (rp == 0) s.ob[j * CG + col] = o;
+      }
+    }
+    __syncthreads();
+    store_o(a, s, b, hv, cg, p0, n);
+    __syncthreads();
+  }
+  if (a.final_state != nullptr) {
+    float* f = a.final_state + ((int64_t)b * a.Hv + hv) * DK * DV + cg * CG + col;
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) f[own_row(rp, i) * DV] = S[i];
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// serving: one canvas of T rows per request from the cached state (rows < n_clean token-causal,
+// the rest read the state after the last row), and the commit that advances the cached state by
+// adv[b] rows.  The state cache is kept in the thread-native layout [slots, Hv, NCG, RPT, NT] so
+// every load / store is coalesced; a prep pass writes each row's L2-normalised q (times scale) and
+// k once ([rows, Hk, 2, DK] fp32) and its decay / beta ([rows, Hv, 2]) for both kernels.
+// ---------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(NT) canvas_kernel(const Args a, const float* qk, const float* ab, const float* ssm,
                                                     const int* slot, int n_clean) {
   extern __shared__ float smem[];
@@ -326,18 +298,18 @@ __global__ void __launch_bounds__(NT) canvas_kernel(const Args a, const float* q
   float S[RPT];
 #pragma unroll
   for (int i = 0; i < RPT; ++i) S[i] = base[i * NT + tid];
-  stage_prepped(a, s, qk, ab, b, hv, cg, a.T);
+  stage_prepped(a, s, qk, ab, b, hv, cg, 0, a.T, -1, false);
   __syncthreads();
   for (int j = 0; j < a.T; ++j) {
     float u, vmp;
-    fwd_step(S, s.k + j * DK + rp * RPT, s.al[j], s.be[j], s.v[j * CG + col], u, vmp);
+    fwd_step(S, s.k + j * DK + rp * 4, s.al[j], s.be[j], s.v[j * CG + col], u, vmp);
     if (j < n_clean) {
-      const float o = readout(S, s.q + j * DK + rp * RPT);
+      const float o = readout(S, s.q + j * DK + rp * 4);
       if (rp == 0) s.ob[j * CG + col] = o;
     }
   }
   for (int j = n_clean; j < a.T; ++j) {
-    const float o = readout(S, s.q + j * DK + rp * RPT);
+    const float o = readout(S, s.q + j * DK + rp * 4);
     if (rp == 0) s.ob[j * CG + col] = o;
   }
   __syncthreads();
@@ -355,11 +327,11 @@ __global__ void __launch_bounds__(NT) commit_kernel(const Args a, const float* q
   float S[RPT];
 #pragma unroll
   for (int i = 0; i < RPT; ++i) S[i] = base[i * NT + tid];
-  stage_prepped(a, s, qk, ab, b, hv, cg, n);
+  stage_prepped(a, s, qk, ab, b, hv, cg, 0, n, -1, false);
   __syncthreads();
   for (int j = 0; j < n; ++j) {
     float u, vmp;
-    fwd_step(S, s.k + j * DK + rp * RPT, s.al[j], s.be[j], s.v[j * CG + col], u, vmp);
+    fwd_step(S, s.k + j * DK + rp * 4, s.al[j], s.be[j], s.v[j * CG + col], u, vmp);
   }
 #pragma unroll
   for (int i = 0; i < RPT; ++i) base[i * NT + tid] = S[i];
@@ -384,22 +356,22 @@ __global__ void __launch_bounds__(NT) fwd_noisy_kernel(const Args a) {
   for (int i = 0; i < RPT; ++i) S0[i] = from_clean ? ck[i * NT + tid] : 0.f;
   for (int v = 0; v < a.V; ++v) {
     const int tok0 = (1 + v) * a.L + n * a.bd;
-    stage_tokens(a, s, b, hv, cg, tok0, a.bd, -1, false);
+    stage_prepped(a, s, a.qk, a.ab, b, hv, cg, tok0, a.bd, -1, false);
     __syncthreads();
     float S[RPT];
 #pragma unroll
     for (int i = 0; i < RPT; ++i) S[i] = S0[i];
     for (int j = 0; j < a.bd; ++j) {
       float u, vmp;
-      fwd_step(S, s.k + j * DK + rp * RPT, s.al[j], s.be[j], s.v[j * CG + col], u, vmp);
+      fwd_step(S, s.k + j * DK + rp * 4, s.al[j], s.be[j], s.v[j * CG + col], u, vmp);
       if (a.causal_noisy) {
-        const float o = readout(S, s.q + j * DK + rp * RPT);
+        const float o = readout(S, s.q + j * DK + rp * 4);
         if (rp == 0) s.ob[j * CG + col] = o;
       }
     }
     if (!a.causal_noisy) {
       for (int j = 0; j < a.bd; ++j) {
-        const float o = readout(S, s.q + j * DK + rp * RPT);
+        const float o = readout(S, s.q + j * DK + rp * 4);
         if (rp == 0) s.ob[j * CG + col] = o;
       }
     }
@@ -430,7 +402,7 @@ __device__ __forceinline__ void col_reduce_add(const float (&x)[RPT], float* dst
     const float keep = h2 ? y[i + 4] : y[i];
     z[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
   }
-  const int r0 = rp * RPT + h1 * 8 + h2 * 4;
+  const int r0 = (2 * h1 + h2) * 32 + rp * 4;   // rows own_row(rp, 8 h1 + 4 h2 + 0..3)
 #pragma unroll
   for (int i = 0; i < 4; ++i) atomicAdd(dst + r0 + i, z[i]);
 }
@@ -501,7 +473,7 @@ __device__ void bwd_segment(const Args& a, const Stage& s, Ctx& x, const float (
       for (int i = 0; i < RPT; ++i) S[i] = 0.f;
     }
     float u, vmp;
-    fwd_step(S, s.k + j * DK + rp * RPT, s.al[j], s.be[j], s.v[j * CG + col], u, vmp);
+    fwd_step(S, s.k + j * DK + rp * 4, s.al[j], s.be[j], s.v[j * CG + col], u, vmp);
   }
   if (end_read) {
     // o_j = S_end^T q_j:  dS_end += sum_j q_j do_j^T ;  dq_j = S_end do_j
@@ -513,7 +485,7 @@ __device__ void bwd_segment(const Args& a, const Stage& s, Ctx& x, const float (
         const int j = j0 + t;
         const float doc = s.dO[j * CG + col];
         float q[RPT], dq[RPT];
-        load16(s.q + j * DK + rp * RPT, q);
+        load16(s.q + j * DK + rp * 4, q);
 #pragma unroll
         for (int i = 0; i < RPT; ++i) {
           dq[i] = S[i] * doc;
@@ -544,7 +516,7 @@ __device__ void bwd_segment(const Args& a, const Stage& s, Ctx& x, const float (
         const float al = s.al[j];
 #pragma unroll
         for (int i = 0; i < RPT; ++i) Sp[t][i] = al * S[i];
-        fwd_step(S, s.k + j * DK + rp * RPT, al, s.be[j], s.v[j * CG + col], uu[t], vm[t]);
+        fwd_step(S, s.k + j * DK + rp * 4, al, s.be[j], s.v[j * CG + col], uu[t], vm[t]);
       }
     }
 #pragma unroll
@@ -554,10 +526,10 @@ __device__ void bwd_segment(const Args& a, const Stage& s, Ctx& x, const float (
         const float al = s.al[j], be = s.be[j];
         const float doc = s.dO[j * CG + col];
         float k[RPT], dq[RPT], dk[RPT];
-        load16(s.k + j * DK + rp * RPT, k);
+        load16(s.k + j * DK + rp * 4, k);
         if (!end_read) {
           float q[RPT];
-          load16(s.q + j * DK + rp * RPT, q);
+          load16(s.q + j * DK + rp * 4, q);
 #pragma unroll
           for (int i = 0; i < RPT; ++i) {
             dq[i] = fmaf(k[i], uu[t], Sp[t][i]) * doc;   // S_t = S' + k u^T
@@ -626,7 +598,7 @@ __global__ void __cluster_dims__(NCG, 1, 1) __launch_bounds__(NT) bwd_noisy_kern
   }
   for (int v = 0; v < a.V; ++v) {
     const int tok0 = (1 + v) * a.L + n * a.bd;
-    stage_tokens(a, s, x.b, x.hv, x.cg, tok0, a.bd, -1, true);
+    stage_prepped(a, s, a.qk, a.ab, x.b, x.hv, x.cg, tok0, a.bd, -1, true);
     __syncthreads();
     float dS[RPT];
 #pragma unroll
@@ -659,7 +631,7 @@ __global__ void __cluster_dims__(NCG, 1, 1) __launch_bounds__(NT) bwd_clean_kern
     const float* ck = state_ptr(a.ckpt, a, x.b, x.hv, c, x.cg);
 #pragma unroll
     for (int i = 0; i < RPT; ++i) Sst[i] = ck[i * NT + x.tid];
-    stage_tokens(a, s, x.b, x.hv, x.cg, p0, n, p0, true);
+    stage_prepped(a, s, a.qk, a.ab, x.b, x.hv, x.cg, p0, n, p0, true);
     __syncthreads();
     bwd_segment(a, s, x, Sst, dS, p0, n, end_read);
     if (a.mode == 1) {
@@ -947,6 +919,8 @@ static gdn::Args make_args(const GdnParams& p) {
   a.ckpt = p.ckpt; a.o = p.o;
   a.d_o = p.d_o; a.dqk = p.dqk; a.dgb = p.dgb; a.dv = p.dv; a.lddv = p.lddv; a.dinit = p.dinit;
   a.final_state = p.final_state;
+  a.qk = p.prep;
+  a.ab = p.prep != nullptr ? p.prep + (int64_t)p.B * p.T * 2 * p.Hk * gdn::DK : nullptr;
   return a;
 }
 
@@ -969,6 +943,12 @@ int gdn_fwd(const GdnParams& p, cudaStream_t st) {
     cudaFuncSetAttribute(fwd_noisy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
     init = true;
   }
+  if (p.prep == nullptr) return -4;
+  {
+    const int64_t rows = (int64_t)a.B * a.T, warps = rows * (2 * a.Hk + 1);
+    prep_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(a, p.prep, p.prep + rows * 2 * a.Hk * DK,
+                                                                       (int)rows);
+  }
   const size_t sm_c = stage_floats(a.ch, false) * sizeof(float);
   fwd_clean_kernel<<<dim3(NCG, a.Hv, a.B), NT, sm_c, st>>>(a);
   if (a.mode && a.V > 0) {
@@ -990,6 +970,12 @@ int gdn_bwd(const GdnParams& p, bf16* dmixed, int64_t lddm, bf16* dga, bf16* dgb
     cudaFuncSetAttribute(bwd_clean_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
     cudaFuncSetAttribute(bwd_noisy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
     init = true;
+  }
+  if (p.prep == nullptr) return -4;
+  {
+    const int64_t rows = (int64_t)a.B * a.T, warps = rows * (2 * a.Hk + 1);
+    prep_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(a, p.prep, p.prep + rows * 2 * a.Hk * DK,
+                                                                       (int)rows);
   }
   if (a.mode && a.V > 0) {
     const size_t sm_n = stage_floats(a.bd, true) * sizeof(float);

@@ -85,6 +85,7 @@ struct GdnParams {
   bf16* dv; int64_t lddv;
   float* dinit;              // gdn_state_floats() floats (two-stream backward)
   float* final_state;        // optional [B, Hv, dk, dvh] state after the last clean token
+  float* prep;               // gdn_prep_floats(B * T, Hk, Hv) floats of scratch (training kernels)
 };
 int64_t gdn_state_floats(const GdnParams& p);
 int gdn_fwd(const GdnParams& p, cudaStream_t s);
