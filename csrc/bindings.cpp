@@ -146,13 +146,13 @@ void symm_allreduce(const std::vector<int64_t>& bufs, const std::vector<int64_t>
 
 void symm_rs_sumsq(const std::vector<int64_t>& bufs, const std::vector<int64_t>& flags, int64_t rank, int64_t epoch,
                    int64_t shard_off, int64_t shard_len, double scale, const at::Tensor& shard_out,
-                   const at::Tensor& partial, const at::Tensor& err) {
+                   const at::Tensor& partial, const at::Tensor& err, bool accumulate) {
   auto a = ptr_arrays(bufs, flags);
   TORCH_CHECK(shard_out.scalar_type() == at::kFloat && shard_out.numel() == shard_len, "shard_out");
   TORCH_CHECK(partial.scalar_type() == at::kFloat, "partial fp32");
   const int rc = trida::symm_rs_sumsq(a.bufs, a.flags, rank, bufs.size(), (unsigned)epoch, shard_off, shard_len,
                                       (float)scale, shard_out.data_ptr<float>(), partial.data_ptr<float>(),
-                                      partial.numel(), err.data_ptr<int>(), stream());
+                                      partial.numel(), accumulate ? 1 : 0, err.data_ptr<int>(), stream());
   TORCH_CHECK(rc == 0, "symm_rs_sumsq failed with code ", rc);
 }
 
@@ -765,7 +765,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_close", &symm_close);
   m.def("symm_tensor", &symm_tensor);
   m.def("symm_allreduce", &symm_allreduce);
-  m.def("symm_rs_sumsq", &symm_rs_sumsq);
+  m.def("symm_rs_sumsq", &symm_rs_sumsq, py::arg("bufs"), py::arg("flags"), py::arg("rank"), py::arg("epoch"),
+        py::arg("shard_off"), py::arg("shard_len"), py::arg("scale"), py::arg("shard_out"), py::arg("partial"),
+        py::arg("err"), py::arg("accumulate") = false);
   m.def("symm_norm_coef", &symm_norm_coef);
   m.def("symm_adamw_ag", &symm_adamw_ag);
   m.def("gdn_state_numel", &gdn_state_numel);

@@ -134,8 +134,8 @@ int symm_allreduce_bf16(void* const* bufs, unsigned* const* flags, int rank, int
                         int64_t off, int64_t n, const bf16* residual, bf16* out, int* err, int sm_count,
                         cudaStream_t s);
 int symm_rs_sumsq(void* const* bufs, unsigned* const* flags, int rank, int world, unsigned epoch, int64_t shard_off,
-                  int64_t shard_len, float scale, float* shard_out, float* partial, int nblocks, int* err,
-                  cudaStream_t s);
+                  int64_t shard_len, float scale, float* shard_out, float* partial, int nblocks, int accumulate,
+                  int* err, cudaStream_t s);
 int symm_norm_coef(void* const* partials, unsigned* const* flags, int rank, int world, unsigned epoch, int nblocks,
                    float max_norm, float* norm_out, float* coef_out, int* err, cudaStream_t s);
 int symm_adamw_ag(void* const* bufs, unsigned* const* flags, int rank, int world, unsigned epoch, int64_t shard_off,

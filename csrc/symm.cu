@@ -14,7 +14,7 @@
 //               buffers, so one barrier per call suffices (a rank only overwrites a buffer after
 //               every peer has entered the next all-reduce, i.e. finished reading it).
 //   rs_sumsq    reduce-scatter of fp32 gradient buffers: every rank reads its shard of all peers'
-//               gradients, sums, scales, keeps the shard and the shard's sum of squares.
+//               gradients, sums, scales, stores (or adds) the shard and its sum of squares.
 //   adamw_ag    sharded AdamW on the reduced shard with the bf16 result stored straight into
 //               every peer's parameter buffer (the all-gather fused into the update), then a
 //               closing barrier so no rank reads parameters that are still being written.
@@ -100,7 +100,7 @@ __global__ void allreduce_kernel(Peers P, int rank, int world, unsigned* ctr, un
 }
 
 __global__ void rs_sumsq_kernel(Peers P, int rank, int world, unsigned epoch, int64_t shard_off, int64_t shard_len,
-                                float scale, float* shard_out, float* partial, int* err) {
+                                float scale, float* shard_out, float* partial, int accumulate, int* err) {
   barrier(P, rank, world, epoch, 1, err, 202);
   float ss = 0.f;
   const int64_t n4 = shard_len / 4;
@@ -112,6 +112,10 @@ __global__ void rs_sumsq_kernel(Peers P, int rank, int world, unsigned epoch, in
       acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
     }
     acc.x *= scale; acc.y *= scale; acc.z *= scale; acc.w *= scale;
+    if (accumulate) {
+      const float4 o = reinterpret_cast<const float4*>(shard_out)[i];
+      acc.x += o.x; acc.y += o.y; acc.z += o.z; acc.w += o.w;
+    }
     reinterpret_cast<float4*>(shard_out)[i] = acc;
     ss += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
   }
@@ -214,11 +218,11 @@ int symm_allreduce_bf16(void* const* bufs, unsigned* const* flags, int rank, int
 }
 
 int symm_rs_sumsq(void* const* bufs, unsigned* const* flags, int rank, int world, unsigned epoch, int64_t shard_off,
-                  int64_t shard_len, float scale, float* shard_out, float* partial, int nblocks, int* err,
-                  cudaStream_t s) {
+                  int64_t shard_len, float scale, float* shard_out, float* partial, int nblocks, int accumulate,
+                  int* err, cudaStream_t s) {
   if (world > symm::MAXR || shard_len % 4) return -1;
   symm::rs_sumsq_kernel<<<nblocks, 256, 0, s>>>(make_peers(bufs, flags, world), rank, world, epoch, shard_off,
-                                                shard_len, scale, shard_out, partial, err);
+                                                shard_len, scale, shard_out, partial, accumulate, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 

@@ -400,3 +400,33 @@ def test_gemm_tile_shapes_ragged_all_layouts(tile):
     ref = acc + dy.float().t() @ x.float()
     C().gemm(2, dy, x, acc, acc, 1.0, 1.0, tile)
     assert rel_err(acc, ref) < 1e-3
+
+
+def test_streamed_layer_gradients_cuda_match_resident():
+    """On the CUDA blocks (weight gradients written into main_grad by the GEMM epilogue), streaming
+    each layer's gradients through the two-slot ring equals the resident full buffers."""
+    import copy
+
+    from trida_stack_b200.engine import TrainEngine
+    from trida_stack_b200.models import BlockDiffusionLM, Decoder, qwen3_config
+    torch.manual_seed(0)
+    cfg = qwen3_config(vocab_size=512, hidden_size=256, intermediate_size=512, num_layers=3, n_heads=4,
+                       n_kv_heads=2, head_dim=64)
+    dec = Decoder(cfg, dtype=torch.bfloat16, device="cuda")
+    outs = []
+    for stream, ckpt in ((False, "none"), (True, "none"), (True, "layer")):
+        m = BlockDiffusionLM(copy.deepcopy(dec), mask_id=511, pad_id=510, bd_size=32, ar_loss_weight=1.0,
+                             activation_checkpoint=ckpt)
+        m.train()
+        eng = TrainEngine(m, lr=1e-3, warmup=0, max_steps=10, device=torch.device("cuda"), grad_stream=stream)
+        g = torch.Generator().manual_seed(1)
+        torch.manual_seed(5)
+        for step in range(2):
+            ids = torch.randint(0, 509, (2, 128), generator=g)
+            labels = ids.clone()
+            labels[:, :64] = -100
+            eng.train_step([{"input_ids": ids, "labels": labels, "attention_mask": torch.ones_like(ids)}], step)
+        outs.append([p.detach().float().cpu() for p in m.parameters()])
+    for o in outs[1:]:
+        for a, b in zip(o, outs[0]):
+            assert rel_err(a, b) < 1e-3

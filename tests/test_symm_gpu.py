@@ -64,6 +64,28 @@ def _worker(rank, world, port, q):
             if comm == "fused":
                 opt.heap.check()
         perr = max(((a - b).abs().max() / (b.abs().max() + 1e-6)).item() for a, b in zip(outs["fused"], outs["nccl"]))
+        # streamed per-layer gradients through the ring (fused and NCCL reduce) vs resident buffers
+        for comm in ("nccl", "fused"):
+            params = [torch.nn.Parameter(b_.clone().to("cuda", torch.bfloat16)) for b_ in base]
+            groups = [{"params": [params[0]], "stream": True, "layer": 0},
+                      {"params": [params[1]], "stream": True, "layer": 1}, {"params": [params[2]]}]
+            opt = ShardedAdamW(groups, lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1, comm=comm)
+            for step in range(3):
+                opt.zero_grad()
+                g = torch.Generator().manual_seed(1000 * step + 7 * rank)
+                grads = [torch.randn(p_.shape, generator=g) for p_ in params]
+                for li in (1, 0):                     # backward order: last layer first
+                    opt.layer_stream.acquire(li)
+                    params[li].main_grad.copy_(grads[li])
+                    opt.layer_stream.release(li)
+                params[2].main_grad.copy_(grads[2])
+                opt.reduce_gradients()
+                opt.clip_grad_norm_(1.0)
+                opt.step()
+            torch.cuda.synchronize()
+            serr = max(((p_.detach().float().cpu() - r).abs().max() / (r.abs().max() + 1e-6)).item()
+                       for p_, r in zip(params, outs["nccl"]))
+            perr = max(perr, serr)
         q.put((rank, max(errs), perr))
     finally:
         dist.destroy_process_group()

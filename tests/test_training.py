@@ -138,3 +138,32 @@ def test_help_is_torch_free():
     r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
     assert "--model_id" in r.stdout
+
+
+def test_streamed_layer_gradients_match_resident():
+    """Per-layer gradient streaming (two-slot ring, reduce into the shard as each layer's backward
+    ends) gives the same update as the resident full-gradient buffers."""
+    import copy
+
+    from helpers import make_tiny_qwen3  # noqa: F401  (fixture module on sys.path)
+    from trida_stack_b200.engine import TrainEngine
+    from trida_stack_b200.models import BlockDiffusionLM, Decoder, qwen3_config
+    torch.manual_seed(0)
+    cfg = qwen3_config(vocab_size=97, hidden_size=32, intermediate_size=64, num_layers=3, n_heads=2,
+                       n_kv_heads=1, head_dim=16)
+    dec = Decoder(cfg, dtype=torch.float32)
+    outs = []
+    for stream in (False, True):
+        m = BlockDiffusionLM(copy.deepcopy(dec), mask_id=96, pad_id=95, bd_size=4, ar_loss_weight=1.0)
+        m.train()
+        eng = TrainEngine(m, lr=1e-2, warmup=0, max_steps=10, device=torch.device("cpu"), grad_stream=stream)
+        g = torch.Generator().manual_seed(1)
+        torch.manual_seed(5)                     # same noising draws in both runs
+        for step in range(2):
+            ids = torch.randint(0, 95, (2, 16), generator=g)
+            labels = ids.clone()
+            labels[:, :8] = -100
+            eng.train_step([{"input_ids": ids, "labels": labels, "attention_mask": torch.ones_like(ids)}], step)
+        outs.append([p.detach().clone() for p in m.parameters()])
+    for a, b in zip(*outs):
+        torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6)

@@ -79,15 +79,29 @@ class BlockDiffusionLM(nn.Module):
     def cfg(self):
         return self.decoder.cfg
 
-    def param_groups(self, projector_lr_scale=1.0, decision_head_lr_scale=1.0):
+    def param_groups(self, projector_lr_scale=1.0, decision_head_lr_scale=1.0, per_layer=False):
         """Optimizer groups tagged with ``lr_scale`` (order: backbone, projector, decision head --
-        the reference's frozen group order, ``block_diffusion.py:180-201``)."""
+        the reference's frozen group order, ``block_diffusion.py:180-201``).  ``per_layer`` splits
+        the backbone into the non-layer parameters plus one group per decoder layer, tagged
+        ``stream`` (gradients streamed through a two-slot ring, for models whose full fp32
+        gradients do not fit next to the optimizer state)."""
         backbone, head = [], []
         for name, p in self.named_parameters():
             if not p.requires_grad:
                 continue
             (head if name.startswith("jev_head.") else backbone).append(p)
-        groups = [{"params": backbone, "lr_scale": 1.0}]
+        if per_layer:
+            layer_ids = {}
+            for i, layer in enumerate(self.decoder.layers):
+                for p in layer.parameters():
+                    layer_ids[id(p)] = i
+            rest = [p for p in backbone if id(p) not in layer_ids]
+            groups = [{"params": rest, "lr_scale": 1.0}]
+            for i, layer in enumerate(self.decoder.layers):
+                groups.append({"params": [p for p in layer.parameters() if p.requires_grad], "lr_scale": 1.0,
+                               "stream": True, "layer": i})
+        else:
+            groups = [{"params": backbone, "lr_scale": 1.0}]
         if head:
             groups.append({"params": head, "lr_scale": decision_head_lr_scale})
         return groups
@@ -108,13 +122,20 @@ class BlockDiffusionLM(nn.Module):
 
     def run_stack(self, x, actx):
         mode = self.activation_checkpoint
-        if mode == "layer" and self.training and torch.is_grad_enabled():
-            from torch.utils.checkpoint import checkpoint
+        ckpt = mode == "layer" and self.training and torch.is_grad_enabled()
+        gs = getattr(self, "grad_stream", None) if torch.is_grad_enabled() else None
+        if not ckpt and gs is None:
+            return self.decoder(x, actx)
+        from torch.utils.checkpoint import checkpoint
 
-            def hook(i, layer, h):
-                return checkpoint(layer, h, actx, self.cfg, use_reentrant=False)
-            return self.decoder(x, actx, layer_hook=hook)
-        return self.decoder(x, actx)
+        def hook(i, layer, h):
+            if gs is not None and h.requires_grad:
+                h.register_hook(lambda g, i=i: gs.release(i))      # layer i's backward has run
+            out = checkpoint(layer, h, actx, self.cfg, use_reentrant=False) if ckpt else layer(h, actx, self.cfg)
+            if gs is not None and out.requires_grad:
+                out.register_hook(lambda g, i=i: gs.acquire(i))    # layer i's backward starts next
+            return out
+        return self.decoder(x, actx, layer_hook=hook)
 
     def _weights(self, rate_sel, pos_sel=None):
         n = rate_sel.numel()

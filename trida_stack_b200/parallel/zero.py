@@ -34,7 +34,7 @@ class FlatGroup:
     """One optimizer group flattened into contiguous buffers (symmetric peer buffers when a heap
     is given, so the fused collectives can read and write them from every rank)."""
 
-    def __init__(self, params, lr_scale, world, rank, fp32_master, device, heap=None):
+    def __init__(self, params, lr_scale, world, rank, fp32_master, device, heap=None, stream=False):
         self.params = list(params)
         self.lr_scale = lr_scale
         self.world, self.rank = world, rank
@@ -45,13 +45,19 @@ class FlatGroup:
         self.shard = self.padded // world
         dtype = self.params[0].dtype if self.params else torch.bfloat16
         self.flat_sym = self.grad_sym = None
+        self.stream = stream        # gradients live in a shared ring slot only while this group's backward runs
         if heap is not None:
             self.flat_sym = heap.alloc(self.padded, dtype)
-            self.grad_sym = heap.alloc(self.padded, torch.float32)
-            self.flat, self.grad = self.flat_sym.local, self.grad_sym.local
+            self.flat = self.flat_sym.local
+            if not stream:
+                self.grad_sym = heap.alloc(self.padded, torch.float32)
+                self.grad = self.grad_sym.local
         else:
             self.flat = torch.zeros(self.padded, dtype=dtype, device=device)
-            self.grad = torch.zeros(self.padded, dtype=torch.float32, device=device)
+            if not stream:
+                self.grad = torch.zeros(self.padded, dtype=torch.float32, device=device)
+        if stream:
+            self.grad = None
         off = 0
         self.offsets = []
         with torch.no_grad():
@@ -60,12 +66,13 @@ class FlatGroup:
                 view = self.flat[off:off + k].view_as(p)
                 view.copy_(p.data)
                 p.data = view
-                p.main_grad = self.grad[off:off + k].view(p.shape)
+                p.main_grad = self.grad[off:off + k].view(p.shape) if not stream else None
                 self.offsets.append((off, k))
                 off += k
         lo = rank * self.shard
         self.lo, self.hi = lo, lo + self.shard
-        self.grad_shard = torch.zeros(self.shard, dtype=torch.float32, device=device) if world > 1 else None
+        self.grad_shard = (torch.zeros(self.shard, dtype=torch.float32, device=device) if world > 1 or stream
+                           else None)
         self.master = None
         if fp32_master:
             self.master = self.flat[lo:lo + self.shard].float().clone()
@@ -73,10 +80,96 @@ class FlatGroup:
         self.v = torch.zeros(self.shard, dtype=torch.float32, device=device)
 
     def shard_grad(self):
-        return self.grad if self.world == 1 else self.grad_shard
+        return self.grad if (self.world == 1 and not self.stream) else self.grad_shard
 
     def shard_param(self):
         return self.flat[self.lo:self.hi]
+
+    def bind_grads(self, buf):
+        """Point every parameter's ``main_grad`` into ``buf`` (a zeroed ring slot)."""
+        for p, (off, k) in zip(self.params, self.offsets):
+            p.main_grad = buf[off:off + k].view(p.shape)
+
+    def unbind_grads(self):
+        for p in self.params:
+            p.main_grad = None
+
+
+class GradRing:
+    """Two fp32 gradient slots shared by the streamed groups (one decoder layer each): a group's
+    slot is bound when its backward starts and reduce-scattered into the group's fp32 shard (and
+    freed) when its backward ends, so full-size fp32 gradients exist for at most two layers."""
+
+    def __init__(self, opt, size, device):
+        self.opt = opt
+        self.slots = []
+        for _ in range(2):
+            if opt.fused:
+                b = opt.heap.alloc(size, torch.float32)
+                self.slots.append((b.local, b))
+            else:
+                self.slots.append((torch.zeros(size, dtype=torch.float32, device=device), None))
+        self.free = [0, 1]
+        self.held = {}
+        self.partial = torch.zeros(ShardedAdamW.NB, dtype=torch.float32, device=device)
+
+    def acquire(self, gi):
+        if gi in self.held:
+            return
+        if not self.free:
+            raise RuntimeError("gradient ring exhausted (more than two layers in backward at once)")
+        si = self.free.pop(0)
+        g = self.opt.groups[gi]
+        buf = self.slots[si][0][:g.padded]
+        buf.zero_()
+        g.bind_grads(buf)
+        self.held[gi] = si
+
+    def release(self, gi):
+        si = self.held.pop(gi, None)
+        if si is None:
+            return
+        o = self.opt
+        g = o.groups[gi]
+        local, sym = self.slots[si]
+        if o.world == 1:
+            g.grad_shard.add_(local[:g.padded])
+        elif o.fused:
+            h = o.heap
+            ext().symm_rs_sumsq(sym.ptrs, h.flags.ptrs, h.rank, h.next_epoch(1), g.lo, g.shard, 1.0 / o.world,
+                                g.grad_shard, self.partial, h.err, accumulate=True)
+        else:
+            tmp = torch.empty(g.shard, dtype=torch.float32, device=local.device)
+            avg = dist.get_backend(o.pg) == "nccl"
+            dist.reduce_scatter_tensor(tmp, local[:g.padded], op=dist.ReduceOp.AVG if avg else dist.ReduceOp.SUM,
+                                       group=o.pg)
+            if not avg:
+                tmp.div_(o.world)
+            g.grad_shard.add_(tmp)
+        g.unbind_grads()
+        self.free.append(si)
+
+    def flush(self):
+        for gi in list(self.held):
+            self.release(gi)
+
+
+class LayerGradStream:
+    """Hooks for the model's layer loop: ``acquire(i)`` when the gradient of layer i's output
+    arrives (its backward is about to run), ``release(i)`` when the gradient of its input arrives
+    (its backward has run)."""
+
+    def __init__(self, ring, layer_groups):
+        self.ring, self.map = ring, layer_groups    # layer index -> optimizer group index
+
+    def acquire(self, i):
+        if i in self.map:
+            self.ring.acquire(self.map[i])
+
+    def release(self, i):
+        if i in self.map:
+            self.ring.release(self.map[i])
+
 
 
 def _adamw_torch(param, master, grad, m, v, lr, b1, b2, eps, wd, step, coef):
@@ -109,12 +202,19 @@ class ShardedAdamW:
         if self.fused:
             from .symm import SymmetricHeap
             self.heap = SymmetricHeap(process_group)
+        groups = [g for g in groups if g["params"]]
         self.groups = [FlatGroup(g["params"], g.get("lr_scale", 1.0), self.world, self.rank, fp32_master, device,
-                                 self.heap)
-                       for g in groups if g["params"]]
+                                 self.heap, stream=bool(g.get("stream")))
+                       for g in groups]
         if self.fused:
             self.partials = self.heap.alloc(len(self.groups) * self.NB, torch.float32)
         self._clipped = False
+        self.ring = None
+        streamed = [g for g in self.groups if g.stream]
+        if streamed:
+            self.ring = GradRing(self, max(g.padded for g in streamed), device)
+            self.layer_stream = LayerGradStream(
+                self.ring, {gg["layer"]: i for i, gg in enumerate(groups) if gg.get("stream")})
         self.param_groups = [{"params": g.params, "lr": lr * g.lr_scale, "lr_scale": g.lr_scale}
                              for g in self.groups]
         self.defaults = {"lr": lr, "betas": betas, "weight_decay": weight_decay, "eps": eps}
@@ -127,7 +227,10 @@ class ShardedAdamW:
     # ---- gradients -----------------------------------------------------------------------
     def zero_grad(self, set_to_none=True):
         for g in self.groups:
-            g.grad.zero_()
+            if g.stream:
+                g.grad_shard.zero_()
+            else:
+                g.grad.zero_()
             for p in g.params:
                 p.grad = None
 
@@ -135,6 +238,8 @@ class ShardedAdamW:
         """Fold ordinary ``.grad`` tensors (CPU path, plain torch modules) into the flat fp32
         buffers; the CUDA blocks write ``main_grad`` directly and leave ``.grad`` unset."""
         for g in self.groups:
+            if g.stream:
+                continue
             for p in g.params:
                 if p.grad is not None:
                     p.main_grad.add_(p.grad.float())
@@ -144,17 +249,32 @@ class ShardedAdamW:
         """Average gradients across ranks into each rank's shard (reduce-scatter)."""
         self.collect_autograd_grads()
         self._clipped = False
+        if self.ring is not None:
+            self.ring.flush()       # a layer whose input needed no gradient never released its slot
+            for g in self.groups:   # plain-autograd (CPU) gradients of streamed groups, single process
+                if not g.stream:
+                    continue
+                for p, (off, k) in zip(g.params, g.offsets):
+                    if p.grad is not None:
+                        if self.world != 1:
+                            raise NotImplementedError("streamed gradients across ranks need the CUDA blocks")
+                        g.grad_shard[off:off + k].add_(p.grad.float().reshape(-1))
+                        p.grad = None
         if self.world == 1:
             return
         if self.fused:
             h = self.heap
             for i, g in enumerate(self.groups):
+                if g.stream:
+                    continue
                 ext().symm_rs_sumsq(g.grad_sym.ptrs, h.flags.ptrs, h.rank, h.next_epoch(1), g.lo, g.shard,
                                     1.0 / self.world, g.grad_shard,
                                     self.partials.local[i * self.NB:(i + 1) * self.NB], h.err)
             return
         avg = dist.get_backend(self.pg) == "nccl"   # gloo has no AVG reduction
         for g in self.groups:
+            if g.stream:
+                continue
             dist.reduce_scatter_tensor(g.grad_shard, g.grad, op=dist.ReduceOp.AVG if avg else dist.ReduceOp.SUM,
                                        group=self.pg)
             if not avg:
@@ -175,7 +295,7 @@ class ShardedAdamW:
         if self.world == 1:
             self._local_norm(shards, max_norm)
             return self.norm[0]
-        if self.fused:
+        if self.fused and self.ring is None:
             h = self.heap
             ext().symm_norm_coef(self.partials.ptrs, h.flags.ptrs, h.rank, h.next_epoch(3),
                                  len(self.groups) * self.NB, max_norm, self.norm, self.coef, h.err)
