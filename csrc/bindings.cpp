@@ -264,12 +264,11 @@ void gdn_bwd(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor& gb
   const int64_t ns = trida::gdn_state_floats(p);
   TORCH_CHECK(ckpt.numel() >= ns, "ckpt too small");
   auto f32 = mixed.options().dtype(at::kFloat);
-  at::Tensor dqk = at::empty({B * T, Hv, 2, 128}, f32);
-  at::Tensor dgbuf = at::empty({B * T, Hv, 2}, f32);
+  at::Tensor dpart = at::empty({trida::gdn_part_floats(p)}, f32);
   at::Tensor dinit = mode ? at::empty({ns}, f32) : at::Tensor();
   p.ckpt = ckpt.data_ptr<float>();
   p.d_o = cbf(d_o);
-  p.dqk = dqk.data_ptr<float>(); p.dgb = dgbuf.data_ptr<float>();
+  p.dpart = dpart.data_ptr<float>();
   p.dv = mbf(dmixed) + 2 * Hk * 128; p.lddv = dmixed.stride(0);
   p.dinit = mode ? dinit.data_ptr<float>() : nullptr;
   at::Tensor prep = at::empty({trida::gdn_prep_floats(B * T, Hk, Hv)}, mixed.options().dtype(at::kFloat));

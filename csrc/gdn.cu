@@ -19,22 +19,19 @@
 // parallel from those states.
 // Backward: per chunk, recompute forward from the checkpoint with sub-checkpoints every SUB tokens,
 // then replay each sub-chunk keeping S' in registers and sweep it in reverse.  Gradients w.r.t. q
-// and k are sums over the 128 value columns: reduced across the 4 columns of a warp by shuffles,
-// across the CTA's 4 warps in shared memory and across the head's 8 CTAs (one thread-block
-// cluster) through distributed shared memory, so every dq / dk element is written exactly once.
-#include <cooperative_groups.h>
-
+// and k are sums over the 128 value columns: reduced across the 4 columns of a warp by shuffles
+// and across the CTA's 4 warps in shared memory; each CTA then writes its partial rows (dq | dk |
+// dbeta | dg per token) to a global buffer with plain coalesced stores, and the closing pass sums
+// the head's 8 column groups (no inter-CTA synchronisation on the sequential path).
 #include "common.cuh"
 #include "ops.h"
-
-namespace cgx = cooperative_groups;
 
 namespace trida {
 namespace gdn {
 
 constexpr int DK = 128, DV = 128;
 constexpr int CG = 16;          // value columns per CTA
-constexpr int NCG = DV / CG;    // CTAs per head (cluster size in the backward)
+constexpr int NCG = DV / CG;    // CTAs per head
 constexpr int RP = 8;           // threads per column
 constexpr int RPT = DK / RP;    // rows per thread
 constexpr int NT = CG * RP;     // 128 threads
@@ -60,8 +57,7 @@ struct Args {
   float* ckpt;              // [B, Hv, nch, NCG, RPT, NT]
   bf16* o;                  // [B*T, Hv*DV]
   const bf16* d_o;          // [B*T, Hv*DV]
-  float* dqk;               // [B*T, Hv, 2, DK]
-  float* dgb;               // [B*T, Hv, 2]  (dg, dbeta)
+  float* dpart;             // [B*T, Hv, NCG, RED] per-CTA partial rows: dq | dk | dbeta | dg
   bf16* dv;                 // v-gradient rows [B*T, lddv] (head columns at hv*DV)
   int64_t lddv;
   float* dinit;             // [B, Hv, nch, NCG, RPT, NT]
@@ -80,12 +76,12 @@ struct Stage {
   float* ob;    // [ch][CG]  (forward output staging / backward dv staging)
   int* rs;      // [ch]
   float* sck;   // [ch/SUB][RPT][NT] (backward sub-checkpoints)
-  float* red;   // [2][SUB][RED]     (backward reduction rows)
+  float* red;   // [SUB][RED]        (backward reduction rows)
 };
 
 __host__ __device__ inline size_t stage_floats(int ch, bool bwd) {
   size_t n = (size_t)ch * (2 * DK + 3 * CG + 3);
-  if (bwd) n += (size_t)((ch + SUB - 1) / SUB) * RPT * NT + 2 * SUB * RED;
+  if (bwd) n += (size_t)((ch + SUB - 1) / SUB) * RPT * NT + SUB * RED;
   return n;
 }
 
@@ -414,42 +410,25 @@ struct Ctx {
 
 constexpr int FL_DQ = 1, FL_DK = 2, FL_SC = 4;
 
-// Cluster-wide reduction of the m reduction rows of parity `par` and the write of the results of
-// tokens tok0.. (row-relative): CTA rank r writes rows [16r, 16r+16) of dq / dk, rank 0 the
-// scalars.  One cluster barrier; the buffers are double-buffered by parity.
+// Write the CTA's m reduction rows (tokens tok0..) to its slot of the partial buffer: the fields
+// selected by `what` only, so the read-out pass (dq) and the sweep (dk, scalars) of one token can
+// write at different times.
 __device__ void flush(const Args& a, const Stage& s, Ctx& x, int tok0, int m, int what) {
-  cgx::cluster_group cl = cgx::this_cluster();
-  cl.sync();
-  const int r = (int)cl.block_rank();
-  float* red = s.red + x.par * SUB * RED;
-  const int tid = x.tid;
-  if (tid < m * 8) {
-    const int t = tid >> 3, qd = (tid >> 2) & 1, f4 = tid & 3;
-    if (what & (qd ? FL_DK : FL_DQ)) {
-      const int off = t * RED + qd * DK + r * RPT + f4 * 4;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int src = 0; src < NCG; ++src) {
-        const float4 w = *reinterpret_cast<const float4*>(cl.map_shared_rank(red + off, src));
-        acc.x += w.x; acc.y += w.y; acc.z += w.z; acc.w += w.w;
-      }
-      const int64_t row = (int64_t)x.b * a.T + tok0 + t;
-      *reinterpret_cast<float4*>(a.dqk + (row * a.Hv + x.hv) * (2 * DK) + qd * DK + r * RPT + f4 * 4) = acc;
-    }
-  } else if ((what & FL_SC) && r == 0 && tid >= 64 && tid < 64 + 2 * m) {
-    const int t = (tid - 64) >> 1, w = (tid - 64) & 1;   // w 0: dg (slot RED-1), 1: dbeta (slot RED-2)
-    float acc = 0.f;
-#pragma unroll
-    for (int src = 0; src < NCG; ++src) acc += *cl.map_shared_rank(red + t * RED + (w ? 2 * DK : 2 * DK + 1), src);
+  __syncthreads();
+  for (int idx = x.tid; idx < m * (RED / 4); idx += NT) {
+    const int t = idx / (RED / 4), f4 = idx % (RED / 4);
+    const int e = f4 * 4;
+    const bool want = e < DK ? (what & FL_DQ) : e < 2 * DK ? (what & FL_DK) : (what & FL_SC);
+    if (!want) continue;
     const int64_t row = (int64_t)x.b * a.T + tok0 + t;
-    a.dgb[(row * a.Hv + x.hv) * 2 + w] = acc;
+    *reinterpret_cast<float4*>(a.dpart + ((row * a.Hv + x.hv) * NCG + x.cg) * RED + e) =
+        *reinterpret_cast<const float4*>(s.red + t * RED + e);
   }
-  x.par ^= 1;
+  __syncthreads();
 }
 
 __device__ __forceinline__ void zero_red(const Stage& s, const Ctx& x) {
-  float* red = s.red + x.par * SUB * RED;
-  for (int i = x.tid; i < SUB * RED; i += NT) red[i] = 0.f;
+  for (int i = x.tid; i < SUB * RED; i += NT) s.red[i] = 0.f;
   __syncthreads();
 }
 
@@ -480,7 +459,7 @@ __device__ void bwd_segment(const Args& a, const Stage& s, Ctx& x, const float (
     for (int j0 = 0; j0 < n; j0 += SUB) {
       const int m = min(SUB, n - j0);
       zero_red(s, x);
-      float* red = s.red + x.par * SUB * RED;
+      float* red = s.red;
       for (int t = 0; t < m; ++t) {
         const int j = j0 + t;
         const float doc = s.dO[j * CG + col];
@@ -501,7 +480,7 @@ __device__ void bwd_segment(const Args& a, const Stage& s, Ctx& x, const float (
   for (int sc = nsub - 1; sc >= 0; --sc) {
     const int j0 = sc * SUB, m = min(SUB, n - j0);
     zero_red(s, x);
-    float* red = s.red + x.par * SUB * RED;
+    float* red = s.red;
 #pragma unroll
     for (int i = 0; i < RPT; ++i) S[i] = s.sck[(sc * RPT + i) * NT + tid];
     float Sp[SUB][RPT], uu[SUB], vm[SUB];
@@ -579,7 +558,7 @@ __device__ void bwd_segment(const Args& a, const Stage& s, Ctx& x, const float (
   }
 }
 
-__global__ void __cluster_dims__(NCG, 1, 1) __launch_bounds__(NT) bwd_noisy_kernel(const Args a) {
+__global__ void __launch_bounds__(NT) bwd_noisy_kernel(const Args a) {
   extern __shared__ float smem[];
   const int nb = a.L / a.bd;
   Ctx x;
@@ -611,10 +590,9 @@ __global__ void __cluster_dims__(NCG, 1, 1) __launch_bounds__(NT) bwd_noisy_kern
   float* di = state_ptr(a.dinit, a, x.b, x.hv, n, x.cg);
 #pragma unroll
   for (int i = 0; i < RPT; ++i) di[i * NT + x.tid] = from_clean ? dI[i] : 0.f;
-  cgx::this_cluster().sync();   // peers may still read this CTA's reduction rows
 }
 
-__global__ void __cluster_dims__(NCG, 1, 1) __launch_bounds__(NT) bwd_clean_kernel(const Args a) {
+__global__ void __launch_bounds__(NT) bwd_clean_kernel(const Args a) {
   extern __shared__ float smem[];
   Ctx x;
   x.cg = blockIdx.x; x.hv = blockIdx.y; x.b = blockIdx.z;
@@ -641,7 +619,6 @@ __global__ void __cluster_dims__(NCG, 1, 1) __launch_bounds__(NT) bwd_clean_kern
     }
     __syncthreads();
   }
-  cgx::this_cluster().sync();   // peers may still read this CTA's reduction rows
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -663,10 +640,12 @@ __global__ void post_bwd_kernel(const Args a, bf16* dmixed, int64_t lddm, bf16* 
       xv[e] = __bfloat162float(xp[e]);
       ss += xv[e] * xv[e];
     }
-    for (int r = 0; r < rep; ++r) {
-      const float4 d = *reinterpret_cast<const float4*>(a.dqk + (row * a.Hv + hk * rep + r) * (2 * DK) + isk * DK + lane * 4);
-      g[0] += d.x; g[1] += d.y; g[2] += d.z; g[3] += d.w;
-    }
+    for (int r = 0; r < rep; ++r)
+      for (int c = 0; c < NCG; ++c) {
+        const float4 d = *reinterpret_cast<const float4*>(
+            a.dpart + ((row * a.Hv + hk * rep + r) * NCG + c) * RED + isk * DK + lane * 4);
+        g[0] += d.x; g[1] += d.y; g[2] += d.z; g[3] += d.w;
+      }
     ss = warp_sum(ss);
     const float rn = rsqrtf(ss + 1e-6f);
     const float sc = isk ? 1.f : a.scale;
@@ -682,8 +661,12 @@ __global__ void post_bwd_kernel(const Args a, bf16* dmixed, int64_t lddm, bf16* 
     for (int e = 0; e < 4; ++e) dp[e] = __float2bfloat16(rn * (g[e] - xv[e] * rn * dot));
   }
   for (int h = threadIdx.x; h < a.Hv; h += blockDim.x) {
-    const float dg = a.dgb[(row * a.Hv + h) * 2 + 0];
-    const float dbeta = a.dgb[(row * a.Hv + h) * 2 + 1];
+    float dg = 0.f, dbeta = 0.f;
+    for (int c = 0; c < NCG; ++c) {
+      const float* pr = a.dpart + ((row * a.Hv + h) * NCG + c) * RED + 2 * DK;
+      dbeta += pr[0];
+      dg += pr[1];
+    }
     const float xa = __bfloat162float(a.ga[row * a.ldg + h]) + a.dt_bias[h];
     const float bv = __bfloat162float(a.gb[row * a.ldg + h]);
     const float beta = 1.f / (1.f + expf(-bv));
@@ -917,7 +900,7 @@ static gdn::Args make_args(const GdnParams& p) {
   a.A_log = p.A_log; a.dt_bias = p.dt_bias;
   a.scale = p.scale;
   a.ckpt = p.ckpt; a.o = p.o;
-  a.d_o = p.d_o; a.dqk = p.dqk; a.dgb = p.dgb; a.dv = p.dv; a.lddv = p.lddv; a.dinit = p.dinit;
+  a.d_o = p.d_o; a.dpart = p.dpart; a.dv = p.dv; a.lddv = p.lddv; a.dinit = p.dinit;
   a.final_state = p.final_state;
   a.qk = p.prep;
   a.ab = p.prep != nullptr ? p.prep + (int64_t)p.B * p.T * 2 * p.Hk * gdn::DK : nullptr;
@@ -930,6 +913,8 @@ int64_t gdn_state_floats(const GdnParams& p) {
   const int nch = (Lc + ch - 1) / ch;
   return (int64_t)p.B * p.Hv * nch * gdn::DK * gdn::DV;
 }
+
+int64_t gdn_part_floats(const GdnParams& p) { return (int64_t)p.B * p.T * p.Hv * gdn::NCG * gdn::RED; }
 
 int gdn_fwd(const GdnParams& p, cudaStream_t st) {
   using namespace gdn;

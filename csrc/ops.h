@@ -80,14 +80,14 @@ struct GdnParams {
   float* ckpt;               // gdn_state_floats() floats
   bf16* o;
   const bf16* d_o;
-  float* dqk;                // [B*T, Hv, 2, dk]
-  float* dgb;                // [B*T, Hv, 2]
+  float* dpart;              // gdn_part_floats(): per-CTA partial gradient rows (backward scratch)
   bf16* dv; int64_t lddv;
   float* dinit;              // gdn_state_floats() floats (two-stream backward)
   float* final_state;        // optional [B, Hv, dk, dvh] state after the last clean token
   float* prep;               // gdn_prep_floats(B * T, Hk, Hv) floats of scratch (training kernels)
 };
 int64_t gdn_state_floats(const GdnParams& p);
+int64_t gdn_part_floats(const GdnParams& p);
 int gdn_fwd(const GdnParams& p, cudaStream_t s);
 // serving: canvas of p.T rows per request from the state cache [slots, Hv, dk, dvh]; commit
 // advances the cached state by adv[b] rows of the canvas (both read p.mixed / p.ga / p.gb rows

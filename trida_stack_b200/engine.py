@@ -45,8 +45,7 @@ class TrainEngine:
                                     decision_head_lr_scale=decision_head_lr_scale, per_layer=grad_stream)
         self.optim = ShardedAdamW(groups, lr=lr, betas=betas, weight_decay=weight_decay, fp32_master=fp32_master,
                                   device=self.device, comm=comm)
-        if self.optim.ring is not None:
-            model.grad_stream = self.optim.layer_stream
+
         self.lr, self.warmup, self.max_steps, self.lr_min_ratio = lr, warmup, max_steps, lr_min_ratio
         self.grad_clip = grad_clip
 

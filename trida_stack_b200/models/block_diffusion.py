@@ -122,20 +122,13 @@ class BlockDiffusionLM(nn.Module):
 
     def run_stack(self, x, actx):
         mode = self.activation_checkpoint
-        ckpt = mode == "layer" and self.training and torch.is_grad_enabled()
-        gs = getattr(self, "grad_stream", None) if torch.is_grad_enabled() else None
-        if not ckpt and gs is None:
-            return self.decoder(x, actx)
-        from torch.utils.checkpoint import checkpoint
+        if mode == "layer" and self.training and torch.is_grad_enabled():
+            from torch.utils.checkpoint import checkpoint
 
-        def hook(i, layer, h):
-            if gs is not None and h.requires_grad:
-                h.register_hook(lambda g, i=i: gs.release(i))      # layer i's backward has run
-            out = checkpoint(layer, h, actx, self.cfg, use_reentrant=False) if ckpt else layer(h, actx, self.cfg)
-            if gs is not None and out.requires_grad:
-                out.register_hook(lambda g, i=i: gs.acquire(i))    # layer i's backward starts next
-            return out
-        return self.decoder(x, actx, layer_hook=hook)
+            def hook(i, layer, h):
+                return checkpoint(layer, h, actx, self.cfg, use_reentrant=False)
+            return self.decoder(x, actx, layer_hook=hook)
+        return self.decoder(x, actx)
 
     def _weights(self, rate_sel, pos_sel=None):
         n = rate_sel.numel()

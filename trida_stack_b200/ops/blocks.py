@@ -58,9 +58,22 @@ def gemm(layout, a, b, d, c=None, alpha=1.0, beta=0.0, tile=0):
     return d
 
 
+def main_grad(w):
+    """The fp32 gradient buffer of parameter ``w``: bound at construction (resident buffers) or on
+    first use inside a backward (streamed per-layer gradients: ``w._grad_acquire`` binds a ring
+    slot to the parameter's group); None for parameters outside the sharded optimizer."""
+    mg = getattr(w, "main_grad", None)
+    if mg is None:
+        acq = getattr(w, "_grad_acquire", None)
+        if acq is not None:
+            acq()
+            mg = w.main_grad
+    return mg
+
+
 def _wgrad(dy, x, w):
     """dW = dy^T x, accumulated into ``w.main_grad`` when present; else returned (fp32 -> w dtype)."""
-    mg = getattr(w, "main_grad", None)
+    mg = main_grad(w)
     if mg is not None:
         gemm(NT, dy, x, mg, mg, 1.0, 1.0)
         return None
@@ -71,7 +84,7 @@ def _wgrad(dy, x, w):
 
 def _vgrad(w, g):
     """Accumulate a vector-parameter gradient (fp32 ``g``) into main_grad, or return it."""
-    mg = getattr(w, "main_grad", None)
+    mg = main_grad(w)
     if mg is not None:
         mg.add_(g)
         return None
@@ -79,7 +92,7 @@ def _vgrad(w, g):
 
 
 def _vec_buf(w):
-    mg = getattr(w, "main_grad", None)
+    mg = main_grad(w)
     return mg if mg is not None else torch.zeros(w.shape, dtype=torch.float32, device=w.device)
 
 

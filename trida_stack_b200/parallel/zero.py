@@ -96,9 +96,11 @@ class FlatGroup:
 
 
 class GradRing:
-    """Two fp32 gradient slots shared by the streamed groups (one decoder layer each): a group's
-    slot is bound when its backward starts and reduce-scattered into the group's fp32 shard (and
-    freed) when its backward ends, so full-size fp32 gradients exist for at most two layers."""
+    """Two fp32 gradient slots shared by the streamed groups (one decoder layer each).  A group's
+    slot is bound to its parameters' ``main_grad`` by the first weight gradient its backward
+    writes, and reduce-scattered into the group's fp32 shard (then freed) when a third group needs
+    a slot or the step's reduction runs -- full-size fp32 gradients exist for at most two layers,
+    and the reduction of one layer overlaps the backward of the next."""
 
     def __init__(self, opt, size, device):
         self.opt = opt
@@ -117,7 +119,9 @@ class GradRing:
         if gi in self.held:
             return
         if not self.free:
-            raise RuntimeError("gradient ring exhausted (more than two layers in backward at once)")
+            # backward runs the layers one after another, so the group that took its slot first
+            # has finished: reduce it now and reuse its slot
+            self.release(next(iter(self.held)))
         si = self.free.pop(0)
         g = self.opt.groups[gi]
         buf = self.slots[si][0][:g.padded]
@@ -155,9 +159,8 @@ class GradRing:
 
 
 class LayerGradStream:
-    """Hooks for the model's layer loop: ``acquire(i)`` when the gradient of layer i's output
-    arrives (its backward is about to run), ``release(i)`` when the gradient of its input arrives
-    (its backward has run)."""
+    """Explicit per-layer control of the ring (layer index -> group): ``acquire(i)`` binds layer
+    i's slot, ``release(i)`` reduces it.  The training blocks bind slots lazily instead."""
 
     def __init__(self, ring, layer_groups):
         self.ring, self.map = ring, layer_groups    # layer index -> optimizer group index
@@ -213,6 +216,10 @@ class ShardedAdamW:
         streamed = [g for g in self.groups if g.stream]
         if streamed:
             self.ring = GradRing(self, max(g.padded for g in streamed), device)
+            for gi, g in enumerate(self.groups):
+                if g.stream:
+                    for p in g.params:   # bound lazily by the first gradient written in a backward
+                        p._grad_acquire = (lambda gi=gi: self.ring.acquire(gi))
             self.layer_stream = LayerGradStream(
                 self.ring, {gg["layer"]: i for i, gg in enumerate(groups) if gg.get("stream")})
         self.param_groups = [{"params": g.params, "lr": lr * g.lr_scale, "lr_scale": g.lr_scale}
