@@ -427,6 +427,11 @@ def test_streamed_layer_gradients_cuda_match_resident():
             labels[:, :64] = -100
             eng.train_step([{"input_ids": ids, "labels": labels, "attention_mask": torch.ones_like(ids)}], step)
         outs.append([p.detach().float().cpu() for p in m.parameters()])
+        if stream:
+            # every streamed weight gradient went through the ring, also under activation checkpointing
+            eng.micro_step({"input_ids": ids, "labels": labels, "attention_mask": torch.ones_like(ids)})
+            leaked = [n for n, p in m.named_parameters() if hasattr(p, "_grad_acquire") and p.grad is not None]
+            assert not leaked, leaked
     for o in outs[1:]:
         for a, b in zip(o, outs[0]):
             assert rel_err(a, b) < 1e-3

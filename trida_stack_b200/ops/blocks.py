@@ -217,13 +217,17 @@ class _AttnBlock(torch.autograd.Function):
             del og
         else:
             gemm(TN, o.view(M, Hq * d), wo, out, x, 1.0, 1.0)
-        ctx.save_for_backward(x, rstd, norm_w, wqkv, qn, kn, wo, qkv, rstd_qk, q, k, o, lse)
+        # parameters ride on ctx (not saved tensors): recomputation under activation checkpointing
+        # unpacks saved tensors as fresh aliases without the parameters' gradient-buffer attributes
+        ctx.save_for_backward(x, rstd, qkv, rstd_qk, q, k, o, lse)
+        ctx.params = (norm_w, wqkv, qn, kn, wo)
         ctx.actx, ctx.cfg = actx, cfg
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        x, rstd, norm_w, wqkv, qn, kn, wo, qkv, rstd_qk, q, k, o, lse = ctx.saved_tensors
+        x, rstd, qkv, rstd_qk, q, k, o, lse = ctx.saved_tensors
+        norm_w, wqkv, qn, kn, wo = ctx.params
         actx, cfg = ctx.actx, ctx.cfg
         B, T, Hq, Hkv, d, rd, eps = actx.B, actx.T, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.rotary_dim, cfg.eps
         M, D = x.shape
@@ -316,13 +320,15 @@ class _MlpBlock(torch.autograd.Function):
         C.swiglu_fwd(gu, a)
         out = torch.empty_like(x)
         gemm(TN, a, wd, out, x, 1.0, 1.0)
-        ctx.save_for_backward(x, rstd, norm_w, wgu, wd, gu)
+        ctx.save_for_backward(x, rstd, gu)
+        ctx.params = (norm_w, wgu, wd)
         ctx.eps = eps
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        x, rstd, norm_w, wgu, wd, gu = ctx.saved_tensors
+        x, rstd, gu = ctx.saved_tensors
+        norm_w, wgu, wd = ctx.params
         M, D = x.shape
         F = gu.shape[1] // 2
         C = ext()
@@ -361,12 +367,14 @@ class _Norm(torch.autograd.Function):
     def forward(ctx, x, w, eps):
         h = torch.empty_like(x)
         _, rstd = ext().rmsnorm_fwd(x, w, eps, h)
-        ctx.save_for_backward(x, w, rstd)
+        ctx.save_for_backward(x, rstd)
+        ctx.w = w
         return h
 
     @staticmethod
     def backward(ctx, dh):
-        x, w, rstd = ctx.saved_tensors
+        x, rstd = ctx.saved_tensors
+        w = ctx.w
         dx = torch.empty_like(x)
         gw = _vec_buf(w)
         ext().rmsnorm_bwd(dh.contiguous(), x, w, rstd, None, dx, gw)
@@ -385,13 +393,15 @@ class _Embed(torch.autograd.Function):
         ids = ids.reshape(-1).contiguous()
         out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
         ext().embed_fwd(ids, table, out)
-        ctx.save_for_backward(ids, table)
+        ctx.save_for_backward(ids)
+        ctx.table = table
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        ids, table = ctx.saved_tensors
-        mg = getattr(table, "main_grad", None)
+        ids, = ctx.saved_tensors
+        table = ctx.table
+        mg = main_grad(table)
         buf = mg if mg is not None else torch.zeros(table.shape, dtype=torch.float32, device=table.device)
         ext().embed_bwd(ids, dout.contiguous(), buf)
         return None, (None if mg is not None else buf.to(table.dtype))

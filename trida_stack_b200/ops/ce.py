@@ -14,7 +14,7 @@ import torch
 
 from . import reference as R
 from ._ext import ext
-from .blocks import NT, TN, TT, gemm
+from .blocks import main_grad, NT, TN, TT, gemm
 
 
 class _FusedLinearCE(torch.autograd.Function):
@@ -58,7 +58,7 @@ class _FusedLinearCE(torch.autograd.Function):
         gw = None
         if ctx.need_w:
             w = ctx.w
-            mg = getattr(w, "main_grad", None)
+            mg = main_grad(w)
             if mg is not None:
                 mg.addcmul_(dw, g)
             else:

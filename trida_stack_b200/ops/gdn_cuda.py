@@ -60,14 +60,16 @@ class _GdnBlock(torch.autograd.Function):
         C.gdn_gnorm_fwd(o, z, gnorm, y, Hv, cfg.eps)
         out = torch.empty_like(x)
         gemm(TN, y, w_out, out, x, 1.0, 1.0)
-        ctx.save_for_backward(x, rstd, norm_w, w_in, conv_w, dt_bias, A_log, gnorm, w_out, proj, mixed, o, ckpt)
+        ctx.save_for_backward(x, rstd, proj, mixed, o, ckpt)
+        ctx.params = (norm_w, w_in, conv_w, dt_bias, A_log, gnorm, w_out)   # see ops.blocks._AttnBlock
         ctx.geo = (B, T, Hk, Hv, dk, kd, vd, Cc, mode, L, V, bd, flags, scale)
         ctx.doc, ctx.eps = doc, cfg.eps
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        x, rstd, norm_w, w_in, conv_w, dt_bias, A_log, gnorm, w_out, proj, mixed, o, ckpt = ctx.saved_tensors
+        x, rstd, proj, mixed, o, ckpt = ctx.saved_tensors
+        norm_w, w_in, conv_w, dt_bias, A_log, gnorm, w_out = ctx.params
         B, T, Hk, Hv, dk, kd, vd, Cc, mode, L, V, bd, flags, scale = ctx.geo
         doc, eps = ctx.doc, ctx.eps
         M, D = x.shape
