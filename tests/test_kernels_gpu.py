@@ -341,9 +341,11 @@ def test_blocks_match_cpu_reference():
         assert rel_err(a, b) < 5e-2
 
 
-def test_gated_attention_block_d256_matches_cpu_reference():
+@pytest.mark.parametrize("mrope", [False, True])
+def test_gated_attention_block_d256_matches_cpu_reference(mrope):
     """Qwen3.5 full-attention sub-block: head_dim 256, partial RoPE (64 of 256), q/gate interleaved
-    per head and the sigmoid output gate; GPU bf16 vs CPU fp32."""
+    per head and the sigmoid output gate; GPU bf16 vs CPU fp32.  ``mrope``: per-token 3-D (t, h, w)
+    RoPE angles of vision-language rows instead of the shared position table."""
     torch.manual_seed(0)
     from trida_stack_b200.models.config import ModelConfig
     from trida_stack_b200.ops import blocks
@@ -370,6 +372,12 @@ def test_gated_attention_block_d256_matches_cpu_reference():
             cos_t, sin_t = blocks.rope_tables(4096, cfg.rotary_dim, cfg.rope_theta, dev)
         actx = blocks.AttnContext(m["seg"], m["opos"], m["rblk"], m["segid"], m["view"], m["opos"], True, False,
                                   cos_t, sin_t)
+        if mrope:
+            from trida_stack_b200.models.vision import mrope_angles
+            op = m["opos"].long()
+            t = torch.arange(T, device=dev)[None]
+            pos3 = torch.stack([op, op + t % 5, op + t % 3], 1)
+            actx.set_rope_angles(mrope_angles(pos3, cfg.rotary_dim, cfg.rope_theta, cfg.mrope_section))
         y = blocks.attn_block(xx, *ps, actx, cfg)
         y.backward(dy.to(dev, dtype))
         return y.float().cpu(), xx.grad.float().cpu(), [p.grad.float().cpu() for p in ps]

@@ -83,6 +83,8 @@ def save_hf(model, args, tag):
             json.dump(cfg, f, indent=2)
         if getattr(model, "tokenizer", None) is not None:
             model.tokenizer.save_pretrained(out)
+        if getattr(model, "image_processor", None) is not None:
+            model.image_processor.save_pretrained(out)
         head = getattr(model, "decision_head", None)
         if head is not None:
             torch.save({"head": {k: v.detach().to("cpu", torch.bfloat16 if v.is_floating_point() else v.dtype)

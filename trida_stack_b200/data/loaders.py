@@ -37,7 +37,9 @@ def build_data_loaders(args, model):
             dataset = sft.PackedMultiTurnRowDataset(base, tok, bd_size=args.bd_size, max_length=args.max_length,
                                                     max_response_length=args.max_response_length,
                                                     keep_all_reasoning=args.keep_all_reasoning,
-                                                    max_segments=args.max_segments)
+                                                    max_segments=args.max_segments,
+                                                    image_processor=getattr(model, "image_processor", None),
+                                                    max_image_pixels=args.max_image_pixels)
             collate = sft.StreamPackedMultiTurnCollator(tok, bd_size=args.bd_size, max_length=args.max_length,
                                                         length_buckets=buckets)
         elif args.pack:

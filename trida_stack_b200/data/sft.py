@@ -29,6 +29,7 @@ import torch.nn.functional as F
 from torch.utils.data import IterableDataset, get_worker_info
 
 from ..models.block_diffusion import bucketed_clean_len
+from .images import expand_image_pads, image_pad_id, image_refs, mrope_position_ids, process_images
 
 IGNORE = -100
 _PASSTHROUGH_FIELDS = ("reasoning_content", "tool_calls", "tool_call_id", "name")
@@ -60,11 +61,19 @@ def _ids_of(enc):
     return [int(t) for t in enc]
 
 
-def render(tokenizer, messages, tools, add_generation_prompt, keep_all_reasoning=False):
+def render(tokenizer, messages, tools, add_generation_prompt, keep_all_reasoning=False, image_counts=None):
+    """Token ids of a chat-template render; each ``<|image_pad|>`` placeholder is expanded to its
+    image's merged-patch count (a render with images but no counts raises)."""
     kw = {"keep_all_reasoning": keep_all_reasoning} if keep_all_reasoning else {}
     enc = tokenizer.apply_chat_template(messages, tools=tools, tokenize=True,
                                         add_generation_prompt=add_generation_prompt, **kw)
-    return _ids_of(enc)
+    ids = _ids_of(enc)
+    pad = image_pad_id(tokenizer)
+    if pad is not None and pad in ids:
+        if image_counts is None:
+            raise ValueError("conversation has images; only --pack --multiturn supports them")
+        ids = expand_image_pads(ids, pad, image_counts)
+    return ids
 
 
 def _render_pair(tokenizer, example, fn):
@@ -106,11 +115,16 @@ def build_sample(tokenizer, example, keep_all_reasoning=False):
     return {"input_ids": ids, "labels": labels}
 
 
-def build_sample_multiturn(tokenizer, example, bd_size, keep_all_reasoning=False):
+def build_sample_multiturn(tokenizer, example, bd_size, keep_all_reasoning=False, image_processor=None,
+                           max_image_pixels=1024 * 1024):
     """Every assistant turn supervised; adds ``resp_block`` (global block id, -1 off-response) and
     ``turn_id`` (assistant-turn ordinal, -1 off-response).  Turns that do not render as exact
     prefixes are left as conditioning.  A turn whose generation-prompt render does not match (e.g.
-    an empty think block) is located by the ``<|im_start|>assistant\\n`` header instead."""
+    an empty think block) is located by the ``<|im_start|>assistant\\n`` header instead.
+
+    Conversations with image parts need ``image_processor`` (else they are skipped) and add
+    ``pixel_values``, ``image_grid_thw`` and ``mrope_pos`` [3, T]; image tokens are never targets.
+    ``example["max_image_pixels"]`` overrides the cap for that conversation."""
     msgs = example.get("messages") or example.get("conversations")
     if not msgs:
         return None
@@ -118,11 +132,24 @@ def build_sample_multiturn(tokenizer, example, bd_size, keep_all_reasoning=False
     turns = [i for i, m in enumerate(msgs) if m["role"] == "assistant"]
     if not turns:
         return None
+    try:
+        refs = image_refs(msgs)
+    except ValueError:
+        return None
+    counts = None
+    if refs:
+        if image_processor is None:
+            return None
+        cap = example.get("max_image_pixels") or max_image_pixels
+        try:
+            pixel_values, grid, counts = process_images(image_processor, refs, example.get("image_root"), cap)
+        except Exception:
+            return None
 
     def all_renders(tools):
-        full = render(tokenizer, msgs, tools, False, keep_all_reasoning)
-        spans = [(render(tokenizer, msgs[:i], tools, True, keep_all_reasoning),
-                  render(tokenizer, msgs[:i + 1], tools, False, keep_all_reasoning)) for i in turns]
+        full = render(tokenizer, msgs, tools, False, keep_all_reasoning, counts)
+        spans = [(render(tokenizer, msgs[:i], tools, True, keep_all_reasoning, counts),
+                  render(tokenizer, msgs[:i + 1], tools, False, keep_all_reasoning, counts)) for i in turns]
         return full, spans
 
     res, tools = _render_pair(tokenizer, example, all_renders)
@@ -147,7 +174,7 @@ def build_sample_multiturn(tokenizer, example, bd_size, keep_all_reasoning=False
             if header is None:
                 header = tokenizer.encode("<|im_start|>assistant\n", add_special_tokens=False)
             try:
-                base = render(tokenizer, msgs[:turns[j]], tools, False, keep_all_reasoning)
+                base = render(tokenizer, msgs[:turns[j]], tools, False, keep_all_reasoning, counts)
             except Exception:
                 continue
             lo = len(base) + len(header)
@@ -160,9 +187,15 @@ def build_sample_multiturn(tokenizer, example, bd_size, keep_all_reasoning=False
         resp_block[span] = block + rb
         block += int(rb[-1]) + 1
         used += 1
+    if counts:
+        labels[ids == image_pad_id(tokenizer)] = IGNORE
     if used == 0 or int((labels != IGNORE).sum()) == 0:
         return None
-    return {"input_ids": ids, "labels": labels, "resp_block": resp_block, "turn_id": turn_id}
+    out = {"input_ids": ids, "labels": labels, "resp_block": resp_block, "turn_id": turn_id}
+    if counts:
+        out.update(pixel_values=pixel_values, image_grid_thw=grid,
+                   mrope_pos=mrope_position_ids(ids, grid, image_pad_id(tokenizer), image_processor.merge_size))
+    return out
 
 
 def _pad_to(t, n, value):
@@ -273,7 +306,22 @@ def pack_rows_to_batch(rows, pad_id, length_buckets, max_length):
         fills = {"input_ids": pad_id, "labels": IGNORE, "attention_mask": 0, "seg_id": -1, "resp_pos": -1}
         for k in cols:
             cols[k].append(_pad_to(torch.cat(parts[k]), L, fills[k]))
-    return {k: torch.stack(v) for k, v in cols.items()}
+    batch = {k: torch.stack(v) for k, v in cols.items()}
+    docs = [s for row in rows for s in row]
+    if any("mrope_pos" in s for s in docs):
+        # 3-D positions [B, 3, L] restart per doc (text docs: arange on all axes; row pad 0); image
+        # tensors concatenate in row-then-doc order = the order of their pad runs in input_ids
+        mrope = torch.zeros(len(rows), 3, L, dtype=torch.long)
+        for b, row in enumerate(rows):
+            off = 0
+            for s in row:
+                n = s["input_ids"].shape[0]
+                mrope[b, :, off:off + n] = s["mrope_pos"] if "mrope_pos" in s else torch.arange(n).expand(3, -1)
+                off += n
+        batch["mrope_pos"] = mrope
+        batch["pixel_values"] = torch.cat([s["pixel_values"] for s in docs if "pixel_values" in s])
+        batch["image_grid_thw"] = torch.cat([s["image_grid_thw"] for s in docs if "image_grid_thw" in s])
+    return batch
 
 
 class PackedSftCollator:
@@ -310,6 +358,9 @@ def block_align_doc(s, bd_size, pad_id):
     out = dict(s)
     for k, v in fills.items():
         out[k] = _pad_to(s[k], n + extra, v)
+    if "mrope_pos" in s:                   # the pad continues the doc's positions
+        nxt = int(s["mrope_pos"].max()) + 1
+        out["mrope_pos"] = torch.cat([s["mrope_pos"], torch.arange(nxt, nxt + extra).expand(3, -1)], 1)
     return out
 
 
@@ -330,7 +381,22 @@ def pack_rows_multiturn(rows, pad_id, bd_size, length_buckets, max_length):
             parts["turn_id"].append(s["turn_id"])
         for k in cols:
             cols[k].append(_pad_to(torch.cat(parts[k]), L, fills[k]))
-    return {k: torch.stack(v) for k, v in cols.items()}
+    batch = {k: torch.stack(v) for k, v in cols.items()}
+    docs = [s for row in rows for s in row]
+    if any("mrope_pos" in s for s in docs):
+        # 3-D positions [B, 3, L] restart per doc (text docs: arange on all axes; row pad 0); image
+        # tensors concatenate in row-then-doc order = the order of their pad runs in input_ids
+        mrope = torch.zeros(len(rows), 3, L, dtype=torch.long)
+        for b, row in enumerate(rows):
+            off = 0
+            for s in row:
+                n = s["input_ids"].shape[0]
+                mrope[b, :, off:off + n] = s["mrope_pos"] if "mrope_pos" in s else torch.arange(n).expand(3, -1)
+                off += n
+        batch["mrope_pos"] = mrope
+        batch["pixel_values"] = torch.cat([s["pixel_values"] for s in docs if "pixel_values" in s])
+        batch["image_grid_thw"] = torch.cat([s["image_grid_thw"] for s in docs if "image_grid_thw" in s])
+    return batch
 
 
 def stream_first_fit(docs, max_length, buffer_size=32, max_segments=0):
@@ -405,8 +471,10 @@ class PackedMultiTurnRowDataset(IterableDataset):
     """Whole conversations (every turn supervised), block-aligned, packed by buffered first-fit."""
 
     def __init__(self, base, tokenizer, bd_size, max_length=32768, max_response_length=32768,
-                 keep_all_reasoning=True, max_segments=0, buffer_size=32, **_ignored):
+                 keep_all_reasoning=True, max_segments=0, buffer_size=32, image_processor=None,
+                 max_image_pixels=1024 * 1024, **_ignored):
         self.base, self.tokenizer, self.pad_id = base, tokenizer, _pad_id(tokenizer)
+        self.image_processor, self.max_image_pixels = image_processor, max_image_pixels
         self.bd_size, self.max_length, self.max_response_length = bd_size, max_length, max_response_length
         self.keep_all_reasoning, self.max_segments, self.buffer_size = keep_all_reasoning, max_segments, buffer_size
         self.stats = {}
@@ -414,7 +482,8 @@ class PackedMultiTurnRowDataset(IterableDataset):
     def _docs(self):
         st = self.stats = {"packed": 0, "too_long": 0, "response_too_long": 0, "unusable": 0}
         for ex in self.base:
-            s = build_sample_multiturn(self.tokenizer, ex, self.bd_size, keep_all_reasoning=self.keep_all_reasoning)
+            s = build_sample_multiturn(self.tokenizer, ex, self.bd_size, keep_all_reasoning=self.keep_all_reasoning,
+                                       image_processor=self.image_processor, max_image_pixels=self.max_image_pixels)
             if s is None:
                 st["unusable"] += 1
                 continue

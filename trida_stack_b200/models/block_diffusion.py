@@ -71,7 +71,8 @@ class BlockDiffusionLM(nn.Module):
         self.activation_checkpoint = activation_checkpoint
         self.ce_chunk = ce_chunk
         self.tokenizer = tokenizer
-        self.is_vl = False
+        self.is_vl = decoder.cfg.is_vl
+        self.image_processor = None
         self._rope = {}
 
     # ------------------------------------------------------------------ helpers
@@ -85,11 +86,16 @@ class BlockDiffusionLM(nn.Module):
         the backbone into the non-layer parameters plus one group per decoder layer, tagged
         ``stream`` (gradients streamed through a two-slot ring, for models whose full fp32
         gradients do not fit next to the optimizer state)."""
-        backbone, head = [], []
+        backbone, projector, head = [], [], []
         for name, p in self.named_parameters():
             if not p.requires_grad:
                 continue
-            (head if name.startswith("jev_head.") else backbone).append(p)
+            if ".visual." in name and ".visual.merger." not in name:
+                raise RuntimeError(f"vision encoder parameter {name} is trainable; expected it frozen")
+            if name.startswith("jev_head."):
+                head.append(p)
+            else:
+                (projector if ".visual.merger." in name else backbone).append(p)
         if per_layer:
             layer_ids = {}
             for i, layer in enumerate(self.decoder.layers):
@@ -102,6 +108,8 @@ class BlockDiffusionLM(nn.Module):
                                "stream": True, "layer": i})
         else:
             groups = [{"params": backbone, "lr_scale": 1.0}]
+        if projector:
+            groups.append({"params": projector, "lr_scale": projector_lr_scale})
         if head:
             groups.append({"params": head, "lr_scale": decision_head_lr_scale})
         return groups
@@ -113,12 +121,18 @@ class BlockDiffusionLM(nn.Module):
             self._rope[key] = blocks.rope_tables(c.max_position, c.rotary_dim, c.rope_theta, device)
         return self._rope[key]
 
-    def make_actx(self, seg, opos, rblk, segid, view, pos, x0_token_causal):
+    def make_actx(self, seg, opos, rblk, segid, view, pos, x0_token_causal, pos3=None):
+        """``pos3`` [B, 3, T]: 3-D (t, h, w) RoPE positions of vision-language rows."""
         cos_t = sin_t = None
-        if seg.is_cuda:
+        if seg.is_cuda and pos3 is None:
             cos_t, sin_t = self.rope(seg.device)
-        return blocks.AttnContext(seg, opos, rblk, segid, view, pos, x0_token_causal, self.within_block_causal,
+        actx = blocks.AttnContext(seg, opos, rblk, segid, view, pos, x0_token_causal, self.within_block_causal,
                                   cos_t, sin_t)
+        if pos3 is not None:
+            from .vision import mrope_angles
+            c = self.cfg
+            actx.set_rope_angles(mrope_angles(pos3, c.rotary_dim, c.rope_theta, c.mrope_section))
+        return actx
 
     def run_stack(self, x, actx):
         mode = self.activation_checkpoint

@@ -89,6 +89,11 @@ def build_model(args, device=None):
             raise ValueError(f"{head_init} has head_dim {saved['head_dim']}, --decision_head_dim is {args.decision_head_dim}")
         model.decision_head.load_state_dict(saved["head"])
         log(f"[decision] pointer head initialised from {head_init}")
+    if model.is_vl:
+        from ..data.images import ImageProcessor
+        model.image_processor = ImageProcessor.from_pretrained(source) or ImageProcessor()
+        log(f"[model] vision-language checkpoint: frozen vision encoder, trainable projector | "
+            f"images capped at {args.max_image_pixels} px")
     if args.fp32_master:
         for p in model.parameters():
             p.data = p.data.float()

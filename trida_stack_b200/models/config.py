@@ -29,6 +29,11 @@ class ModelConfig:
     conv_kernel: int = 4
     # full-attention layers of the hybrid family gate their output with sigmoid(q_proj gate half)
     attn_output_gate: bool = False
+    # vision-language checkpoints: the ViT's config dict, the <|image_pad|> id and the interleaved
+    # 3-D RoPE split (frequencies per t / h / w axis)
+    vision: dict = None
+    image_token_id: int = 248056
+    mrope_section: tuple = (11, 11, 10)
     # raw HF dict (written back on save so the checkpoint stays loadable by transformers)
     hf: dict = field(default_factory=dict, repr=False)
 
@@ -39,6 +44,10 @@ class ModelConfig:
     @property
     def rotary_dim(self):
         return int(self.head_dim * self.partial_rotary_factor)
+
+    @property
+    def is_vl(self):
+        return self.vision is not None
 
     @property
     def is_hybrid(self):
@@ -77,6 +86,9 @@ class ModelConfig:
             lin_v_dim=d.get("linear_value_head_dim", 128),
             conv_kernel=d.get("linear_conv_kernel_dim", 4),
             attn_output_gate=hybrid_family,
+            vision=dict(full["vision_config"]) if isinstance(full.get("vision_config"), dict) else None,
+            image_token_id=int(full.get("image_token_id", 248056)),
+            mrope_section=tuple(rp.get("mrope_section") or (11, 11, 10)),
             hf=dict(full),
         )
 

@@ -75,6 +75,11 @@ class Decoder(nn.Module):
             self.norm = nn.Parameter(torch.ones(D, dtype=dtype))
             self.lm_head = None if cfg.tie_embeddings else nn.Parameter(torch.empty(cfg.vocab_size, D, dtype=dtype))
         self.reset_parameters()
+        self.visual = None
+        if cfg.is_vl:                          # vision-language checkpoint: ViT + merger, encoder frozen
+            from .vision import VisionConfig, VisionTower
+            self.visual = VisionTower(VisionConfig.from_dict(cfg.vision), dtype=dtype, device=device)
+            self.visual.freeze_encoder()
 
     @property
     def lm_weight(self):
@@ -85,6 +90,8 @@ class Decoder(nn.Module):
         """HF ``_init_weights``: N(0, initializer_range) for matrices, ones for norms."""
         std = self.cfg.initializer_range
         for name, p in self.named_parameters():
+            if name.startswith("visual."):
+                continue
             if p.dim() >= 2:
                 p.normal_(0.0, std, generator=generator)
             elif name.endswith("A_log"):
@@ -125,13 +132,21 @@ class Decoder(nn.Module):
         return blocks.rmsnorm(x, self.norm, self.cfg.eps)
 
     # ---------------------------------------------------------------- HF state dict mapping
+    @property
+    def text_prefix(self):
+        """Language-model weight prefix: ``model.language_model.`` in vision-language checkpoints."""
+        return "model.language_model." if self.cfg.is_vl else "model."
+
     def hf_items(self):
-        items = [("model.embed_tokens.weight", self.embed, None)]
+        base = self.text_prefix
+        items = [(base + "embed_tokens.weight", self.embed, None)]
         for i, layer in enumerate(self.layers):
-            items += layer.hf_items(f"model.layers.{i}.", self.cfg)
-        items.append(("model.norm.weight", self.norm, None))
+            items += layer.hf_items(f"{base}layers.{i}.", self.cfg)
+        items.append((base + "norm.weight", self.norm, None))
         if self.lm_head is not None:
             items.append(("lm_head.weight", self.lm_head, None))
+        if self.visual is not None:
+            items += self.visual.hf_items("model.visual.")
         return items
 
     _CENTERED = ("input_layernorm.weight", "post_attention_layernorm.weight", "self_attn.q_norm.weight",
@@ -142,7 +157,9 @@ class Decoder(nn.Module):
         effective weight, so 1 is added on load and removed on save."""
         if not self.cfg.model_type.startswith("qwen3_5"):
             return 0.0
-        return 1.0 if (name.endswith(self._CENTERED) or name == "model.norm.weight") else 0.0
+        if name.startswith("model.visual."):
+            return 0.0
+        return 1.0 if (name.endswith(self._CENTERED) or name == self.text_prefix + "norm.weight") else 0.0
 
     @staticmethod
     def _view(p, sl):
@@ -165,8 +182,11 @@ class Decoder(nn.Module):
         missing = []
         for name, p, sl in self.hf_items():
             src = sd.get(name)
-            if src is None and name.startswith("model.") and ("model.language_model." + name[6:]) in sd:
-                src = sd["model.language_model." + name[6:]]
+            if src is None:                    # text-only <-> vision-language naming of the same weights
+                for a, b in (("model.language_model.", "model."), ("model.", "model.language_model.")):
+                    if name.startswith(a) and (b + name[len(a):]) in sd:
+                        src = sd[b + name[len(a):]]
+                        break
             if src is None:
                 missing.append(name)
                 continue

@@ -54,13 +54,18 @@ class HybridBlockDiffusionLM(BlockDiffusionLM):
 
     # ----------------------------------------------------------------------------------------
     def forward(self, input_ids, labels, attention_mask, seg_id=None, resp_pos=None, resp_block=None,
-                turn_id=None, decision=None, rpad=None, **_images):
+                turn_id=None, decision=None, rpad=None, pixel_values=None, image_grid_thw=None, mrope_pos=None):
         if decision is not None:
             return self.forward_decision(decision)
+        images = pixel_values is not None
+        if images and (self.ar_only or self.linear_block_mode != "bidirectional"):
+            raise NotImplementedError("image inputs are supported only by the two-stream objective "
+                                      "(--linear_block_mode bidirectional)")
         if self.ar_only:
             return self.forward_ar(input_ids, labels, attention_mask, seg_id=seg_id)
         if self.linear_block_mode == "bidirectional":
-            return self.forward_flare(input_ids, labels, attention_mask, seg_id=seg_id, turn_id=turn_id)
+            return self.forward_flare(input_ids, labels, attention_mask, seg_id=seg_id, turn_id=turn_id,
+                                      pixel_values=pixel_values, image_grid_thw=image_grid_thw, mrope_pos=mrope_pos)
         raise NotImplementedError("hybrid causal-mode block diffusion (region-split linear layers) is not "
                                   "available in this build; use --linear_block_mode bidirectional")
 
@@ -86,7 +91,30 @@ class HybridBlockDiffusionLM(BlockDiffusionLM):
         nb, lb = view(~picked)
         return torch.cat([na, nb], 0), torch.cat([la, lb], 0), p_tok.repeat(2, 1)
 
-    def forward_flare(self, input_ids, labels, attention_mask, seg_id=None, turn_id=None):
+    def _scatter_images(self, x, input_ids, tokens, pixel_values, image_grid_thw):
+        """Vision features at every ``<|image_pad|>`` of the clean stream and of each noisy view
+        (image tokens are prompt tokens, never masked, so every stream holds the row's image tokens
+        at the same positions); features are consumed in row-major order of ``input_ids``."""
+        vis = self.decoder.visual
+        if vis is None:
+            raise ValueError("image inputs given but the checkpoint has no vision tower")
+        img = self.cfg.image_token_id
+        feats = vis(pixel_values, image_grid_thw).to(x.dtype)
+        row_img = input_ids == img
+        n = int(row_img.sum())
+        if n != feats.shape[0]:
+            raise ValueError(f"{n} image tokens but {feats.shape[0]} image features")
+        B, L = input_ids.shape
+        S = tokens.shape[1] // L
+        fidx = (torch.cumsum(row_img.reshape(-1).long(), 0) - 1).view(B, L).repeat(1, S).reshape(-1)
+        tok_img = (tokens == img).reshape(-1)
+        if not torch.equal(tok_img, row_img.repeat(1, S).reshape(-1)):
+            raise ValueError("an image token was masked in a noisy view (image tokens must be prompt tokens)")
+        where = torch.nonzero(tok_img).squeeze(1)
+        return x.index_put((where,), feats.index_select(0, fidx[where]))
+
+    def forward_flare(self, input_ids, labels, attention_mask, seg_id=None, turn_id=None, pixel_values=None,
+                      image_grid_thw=None, mrope_pos=None):
         dev = input_ids.device
         B, L = input_ids.shape
         assert L % self.bd_size == 0, "two-stream rows must be a multiple of bd_size (collator bucket)"
@@ -110,7 +138,8 @@ class HybridBlockDiffusionLM(BlockDiffusionLM):
         seg = torch.where(stream == 0, X0, XT)
         rblk = spos // self.bd_size
         segid = seg_id.repeat(1, S) if seg_id is not None else torch.zeros(B, T, dtype=torch.long, device=dev)
-        actx = self.make_actx(seg, spos, rblk, segid, stream, pos, self.ar_loss_weight > 0)
+        pos3 = mrope_pos.repeat(1, 1, S) if mrope_pos is not None else None   # every stream shares positions
+        actx = self.make_actx(seg, spos, rblk, segid, stream, pos, self.ar_loss_weight > 0, pos3=pos3)
         actx.linear = LinearLayout("two_stream", L=L, V=V, bd=self.bd_size, causal_clean=self.ar_loss_weight > 0,
                                    causal_noisy=self.within_block_causal,
                                    doc_start=doc_starts(seg_id) if seg_id is not None else None)
@@ -145,6 +174,8 @@ class HybridBlockDiffusionLM(BlockDiffusionLM):
             n_ar = 0
             rows, tgt, wts = d_rows, d_tgt, w_diff
         x = self.decoder.embed_tokens(tokens)
+        if pixel_values is not None:
+            x = self._scatter_images(x, input_ids, tokens, pixel_values, image_grid_thw)
         hidden = self.run_stack(x, actx)
         loss, ce = fused_linear_ce(hidden.index_select(0, rows), self.decoder.lm_weight, tgt, wts, chunk=self.ce_chunk)
         with torch.no_grad():

@@ -156,6 +156,15 @@ class AttnContext:
         return {"seg": self.seg, "opos": self.opos, "rblk": self.rblk, "segid": self.segid,
                 "view": self.view}
 
+    def set_rope_angles(self, ang):
+        """Per-token rotary angles [B, T, rotary_dim / 2] (3-D RoPE of vision-language rows) instead
+        of the shared position table: the CUDA path indexes per-token cos / sin rows by token."""
+        self.rope_angles = ang
+        if self.seg.is_cuda:
+            flat = ang.reshape(-1, ang.shape[-1]).float()
+            self.cos_t, self.sin_t = flat.cos().contiguous(), flat.sin().contiguous()
+            self.pos32 = torch.arange(flat.shape[0], dtype=torch.int32, device=ang.device)
+
 
 def rope_tables(max_pos, rotary_dim, theta, device):
     """fp32 cos/sin tables [max_pos, rotary_dim/2] (HF default RoPE, half-split pairs)."""
@@ -286,7 +295,11 @@ def _attn_block_ref(x, norm_w, wqkv, qn, kn, wo, actx, cfg):
         v = qkv[:, (Hq + Hkv) * d:].view(B, T, Hkv, d)
     q = R.rmsnorm(q, qn, eps)
     k = R.rmsnorm(k, kn, eps)
-    cos, sin = R.rope_cos_sin(actx.pos, d, cfg.rope_theta, cfg.rotary_dim, dtype=torch.float32)
+    ang = getattr(actx, "rope_angles", None)
+    if ang is not None:
+        cos, sin = torch.cat([ang, ang], -1).cos(), torch.cat([ang, ang], -1).sin()
+    else:
+        cos, sin = R.rope_cos_sin(actx.pos, d, cfg.rope_theta, cfg.rotary_dim, dtype=torch.float32)
     q = R.apply_rope(q.float(), cos, sin).to(x.dtype)
     k = R.apply_rope(k.float(), cos, sin).to(x.dtype)
     o = R.bd_attention(q, k, v, actx.meta_dict(), actx.x0_token_causal, actx.within_block_causal)
