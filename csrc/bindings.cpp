@@ -382,6 +382,21 @@ void argmax_rows(const at::Tensor& logits, const at::Tensor& out) {
                      stream());
 }
 
+// logits [B, R, V] fp32 (any batch / row strides, unit vocab stride) -> idx int64 [B, R], row max and
+// sum(exp(x - max)) fp32 [B, R]
+void conf_argmax_rows(const at::Tensor& logits, const at::Tensor& idx, const at::Tensor& mx, const at::Tensor& sum) {
+  TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == at::kFloat && logits.dim() == 3 && logits.stride(2) == 1,
+              "fp32 logits [B, R, V] with unit vocabulary stride");
+  const int64_t B = logits.size(0), R = logits.size(1);
+  TORCH_CHECK(idx.scalar_type() == at::kLong && idx.is_contiguous() && idx.numel() == B * R, "idx int64 [B, R]");
+  TORCH_CHECK(mx.scalar_type() == at::kFloat && mx.is_contiguous() && mx.numel() == B * R, "max fp32 [B, R]");
+  TORCH_CHECK(sum.scalar_type() == at::kFloat && sum.is_contiguous() && sum.numel() == B * R, "sum fp32 [B, R]");
+  c10::cuda::CUDAGuard g(logits.device());
+  trida::conf_argmax_rows(logits.data_ptr<float>(), (int)(B * R), (int)std::max<int64_t>(R, 1), logits.stride(0),
+                          logits.stride(1), (int)logits.size(2), idx.data_ptr<int64_t>(), mx.data_ptr<float>(),
+                          sum.data_ptr<float>(), stream());
+}
+
 static trida::ConvParams conv_params(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& doc,
                                      int64_t B, int64_t T, int64_t mode, int64_t L, int64_t V, int64_t bd) {
   CHECK_CUDA(x); CHECK_BF16(x); CHECK_ROWMAJOR(x); CHECK_BF16(w);
@@ -782,6 +797,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_canvas", &gdn_canvas);
   m.def("gdn_commit", &gdn_commit);
   m.def("argmax_rows", &argmax_rows);
+  m.def("conf_argmax_rows", &conf_argmax_rows);
   m.def("gdn_bwd", &gdn_bwd);
   m.def("gdn_conv_fwd", &gdn_conv_fwd);
   m.def("gdn_conv_bwd", &gdn_conv_bwd);

@@ -127,6 +127,8 @@ void canvas_conv(const bf16* x, int64_t ldx, const bf16* win, const bf16* w, bf1
 void conv_commit(const bf16* x, int64_t ldx, int rows_per, bf16* win, const int* slot, const int* adv, int B, int C,
                  int K, cudaStream_t s);
 void argmax_rows(const float* logits, int64_t ld, int rows, int V, int64_t* out, cudaStream_t s);
+void conf_argmax_rows(const float* logits, int rows, int rpb, int64_t sb, int64_t ld, int V, int64_t* idx,
+                      float* mx, float* sum, cudaStream_t s);
 
 // ---- symmetric peer memory collectives (symm.cu) ----
 // bufs / flags: one pointer per rank (this rank's own at index `rank`, peers' IPC-mapped).

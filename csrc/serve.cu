@@ -14,6 +14,7 @@
 //   canvas_conv   depthwise conv + SiLU over [cached window ; canvas rows].
 //   conv_commit   new window = last K-1 rows of [window ; first adv canvas rows].
 //   argmax_rows   greedy token per logits row.
+//   conf_argmax_rows  greedy token, row max and softmax normaliser per row (denoise gate).
 #include <cfloat>
 
 #include "common.cuh"
@@ -328,6 +329,64 @@ __global__ void argmax_rows_kernel(const float* logits, int64_t ld, int V, int64
   }
 }
 
+// Per logits row: first argmax, row max and sum(exp(x - max)) -- the greedy token and its softmax
+// probability (1 / sum) in one pass; with vocabulary-parallel shards the host combines (max, sum)
+// pairs across ranks.  Row r lives at logits + (r / rpb) * sb + (r % rpb) * ld.  One CTA per row.
+__global__ void conf_argmax_rows_kernel(const float* logits, int rpb, int64_t sb, int64_t ld, int V,
+                                        int64_t* out_idx, float* out_max, float* out_sum) {
+  const int r = blockIdx.x;
+  const float* row = logits + (int64_t)(r / rpb) * sb + (int64_t)(r % rpb) * ld;
+  float m = -INFINITY, z = 0.f;
+  int idx = 0x7fffffff;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) {
+    const float x = row[v];
+    if (x > m) {
+      z = z * __expf(m - x) + 1.f;
+      m = x;
+      idx = v;
+    } else {
+      z += __expf(x - m);
+    }
+  }
+  auto merge = [](float& m1, float& z1, int& i1, float m2, float z2, int i2) {
+    if (m2 > m1 || (m2 == m1 && i2 < i1)) {
+      z1 = z2 + (m1 == -INFINITY ? 0.f : z1 * __expf(m1 - m2));
+      m1 = m2;
+      i1 = i2;
+    } else {
+      z1 += (m2 == -INFINITY ? 0.f : z2 * __expf(m2 - m1));
+    }
+  };
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, o);
+    const float oz = __shfl_xor_sync(0xffffffffu, z, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    merge(m, z, idx, om, oz, oi);
+  }
+  __shared__ float sm[32], sz[32];
+  __shared__ int si[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { sm[warp] = m; sz[warp] = z; si[warp] = idx; }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    m = lane < nw ? sm[lane] : -INFINITY;
+    z = lane < nw ? sz[lane] : 0.f;
+    idx = lane < nw ? si[lane] : 0x7fffffff;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, m, o);
+      const float oz = __shfl_xor_sync(0xffffffffu, z, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      merge(m, z, idx, om, oz, oi);
+    }
+    if (lane == 0) {
+      out_idx[r] = idx;
+      out_max[r] = m;
+      out_sum[r] = z;
+    }
+  }
+}
+
 template <int D>
 size_t canvas_smem() { return (size_t)(64 * D + 4 * 64 * D) * 2; }
 
@@ -398,6 +457,11 @@ void conv_commit(const bf16* x, int64_t ldx, int rows_per, bf16* win, const int*
 
 void argmax_rows(const float* logits, int64_t ld, int rows, int V, int64_t* out, cudaStream_t s) {
   serve::argmax_rows_kernel<<<rows, 1024, 0, s>>>(logits, ld, V, out);
+}
+
+void conf_argmax_rows(const float* logits, int rows, int rpb, int64_t sb, int64_t ld, int V, int64_t* idx,
+                      float* mx, float* sum, cudaStream_t s) {
+  if (rows > 0) serve::conf_argmax_rows_kernel<<<rows, 1024, 0, s>>>(logits, rpb, sb, ld, V, idx, mx, sum);
 }
 
 }  // namespace trida

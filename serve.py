@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Serve a Trida checkpoint over HTTP with the native engine (OpenAI-compatible + decisions).
 
-    python serve.py [model] --mode {self-spec,causal,decide} --port 30000 [--config decode.yaml]
+    python serve.py [model] --mode {self-spec,causal,diffusion,decide} --port 30000 [--config decode.yaml]
 
 Flags follow the reference launcher (``inference/zoro-1/serve.py:193-222``); model resolution:
 positional > ``$TRIDA_DECIDE_MODEL`` (decide) > ``$TRIDA_MODEL``.  Checkpoints are local HF
@@ -10,15 +10,19 @@ directories (``config.json`` + safetensors [+ ``decision_head.pt`` / ``jev_head.
 random-initialised model of that architecture (smoke tests without weights).
 
 Decode config (YAML, keys of ``configs/zoro1_self_spec_b15_g8.yaml``): ``block_size`` (canvas
-rows, 2N-1), ``gen_block_size`` (N), ``mask_id``, ``temperature``, ``top_k``, ``top_p``.
-One process serves one engine; ``--tp`` other than 1 is rejected here.
+rows, 2N-1; in ``diffusion`` mode the denoised block length), ``gen_block_size`` (N), ``mask_id``,
+``temperature``, ``top_k``, ``top_p``; ``diffusion`` mode (pure block diffusion with the
+LowConfidenceShift gate) also reads ``threshold`` and ``max_steps``.  Decode steps replay from
+CUDA graphs for the ``--cuda-graph-bs`` batch sizes.  ``--tp N`` shards the model over N GPUs:
+launch with ``torchrun --nproc-per-node N``; rank 0 serves HTTP and every rank steps the same
+engine (requests are broadcast to the other ranks at each step).
 """
 import argparse
 import json
 import os
 import sys
 
-MODES = ("self-spec", "causal", "decide")
+MODES = ("self-spec", "causal", "diffusion", "decide")
 
 
 def parse_args(argv=None):
@@ -41,6 +45,7 @@ def parse_args(argv=None):
     ap.add_argument("--dry-run", action="store_true")
     ap.add_argument("--random-init", default=None, help="serve a random-init model of this config.json")
     ap.add_argument("--device", default=None)
+    ap.add_argument("--no-graphs", action="store_true", help="launch decode steps eagerly (no CUDA graphs)")
     return ap.parse_args(argv)
 
 
@@ -104,28 +109,68 @@ def build(args):
         dec = model.decoder
     if mask_id is None:
         mask_id = dec.cfg.vocab_size - 1
-    rt = Runtime(dec, max_slots=args.max_running, max_len=args.max_len, device=dev)
-    engine = Engine(rt, mask_id=mask_id, mode="causal" if args.mode != "self-spec" else "self-spec", n=n,
-                    max_running=args.max_running)
+    tp = None
+    if args.tp > 1:
+        import torch.distributed as dist
+
+        from trida_stack_b200.serve.tp import TPContext, shard_decoder
+        dec = shard_decoder(dec, dist.get_rank(), dist.get_world_size())
+        tp = TPContext(max_rows=args.max_running * 64, hidden=dec.cfg.hidden_size)
+    rt = Runtime(dec, max_slots=args.max_running, max_len=args.max_len, device=dev, tp=tp)
+    mode = args.mode if args.mode in ("self-spec", "diffusion") else "causal"
+    graphs = dev.startswith("cuda") and not args.no_graphs
+    engine = Engine(rt, mask_id=mask_id, mode=mode, n=n, max_running=args.max_running, graphs=graphs,
+                    block_size=int(dcfg.get("block_size", 8)), threshold=float(dcfg.get("threshold", 0.9)),
+                    max_steps=dcfg.get("max_steps"))
+    if graphs:
+        rt.use_graphs(tuple(int(b) for b in args.cuda_graph_bs.split()))
     return engine, tok, name, decider
+
+
+def _init_tp(args):
+    """torchrun-launched TP ranks: NCCL for the shards' collectives, gloo for the request stream."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world != args.tp:
+        raise SystemExit(f"--tp {args.tp} needs torchrun --nproc-per-node {args.tp} (WORLD_SIZE={world})")
+    if args.mode == "decide":
+        raise SystemExit("decide mode runs on one GPU (--tp 1)")
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    args.device = f"cuda:{local}"
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    return dist.new_group(backend="gloo", timeout=datetime.timedelta(days=1))
 
 
 def main(argv=None):
     args = parse_args(argv)
-    if args.tp != 1:
-        raise SystemExit("serve.py runs one engine per process (--tp 1)")
     if args.dry_run:
         print(json.dumps({"model": resolve_model(args), "mode": args.mode, "port": args.port, "host": args.host,
-                          "config": decode_config(args.config)}))
+                          "tp": args.tp, "config": decode_config(args.config)}))
         return 0
+    ctrl = _init_tp(args) if args.tp > 1 else None
     engine, tok, name, decider = build(args)
     if tok is None:
         raise SystemExit("the HTTP server needs a tokenizer in the checkpoint directory")
+    driver = None
+    if ctrl is not None:
+        from trida_stack_b200.serve.lockstep import LockstepDriver
+        driver = LockstepDriver(engine, ctrl)
+        if driver.rank != 0:
+            driver.run_follower()       # steps in lock-step until rank 0 sends the stop flag
+            return 0
     from trida_stack_b200.serve.server import build_app
     import uvicorn
-    engine.start()
+    (driver or engine).start()
     app = build_app(engine, tok, name, decider)
-    uvicorn.run(app, host=args.host, port=args.port, log_level="warning")
+    try:
+        uvicorn.run(app, host=args.host, port=args.port, log_level="warning")
+    finally:
+        if driver is not None:
+            driver.stop()
     return 0
 
 

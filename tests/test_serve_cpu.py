@@ -150,3 +150,111 @@ def test_tensor_parallel_shards_reproduce_full_model(world):
     assert not errs, errs
     for o in outs:
         assert o == want
+
+
+def _manual_block(dec, prompt, Bk, threshold, max_steps, mask_id=96):
+    """First denoised block of greedy LowConfidenceShift decoding, stepped by hand."""
+    rt = Runtime(dec, max_slots=2, max_len=256)
+    s = rt.alloc()
+    t0 = int(rt.prefill([s], [prompt])[0].argmax())
+    canvas = [t0] + [mask_id] * (Bk - 1)
+    rounds = 0
+    while mask_id in canvas[1:]:
+        lg = rt.canvas([s], [canvas], 1)[0]
+        rt.discard()
+        p = torch.softmax(lg[:Bk - 1].double(), -1)
+        conf, pred = p.max(-1)
+        rounds += 1
+        masked = [i for i in range(1, Bk) if canvas[i] == mask_id]
+        if rounds >= max_steps:
+            take = masked
+        else:
+            take = [i for i in masked if conf[i - 1] > threshold] or [max(masked, key=lambda i: conf[i - 1])]
+        for i in take:
+            canvas[i] = int(pred[i - 1])
+    return [t0] + canvas[1:], rounds
+
+
+@pytest.mark.parametrize("make", [tiny_hybrid, tiny_dense])
+@pytest.mark.parametrize("threshold", [0.0, 0.05, 2.0])
+def test_diffusion_decode_low_confidence_shift(make, threshold):
+    dec = make()
+    torch.manual_seed(4)
+    Bk = 4
+    prompts = [torch.randint(0, 96, (L,)).tolist() for L in (9, 13)]
+    eng = Engine(Runtime(dec, max_slots=4, max_len=256), mask_id=96, mode="diffusion", block_size=Bk,
+                 threshold=threshold)
+    reqs = eng.generate(prompts, max_new_tokens=3 * Bk + 1)
+    for p, r in zip(prompts, reqs):
+        assert len(r.output) == 3 * Bk + 1
+        # the first block follows the gate rule
+        blk, rounds = _manual_block(dec, p, Bk, threshold, Bk - 1)
+        assert r.output[:Bk] == blk
+        if threshold == 0.0:
+            assert rounds == 1            # everything passes in the first round
+        if threshold == 2.0:
+            assert rounds == Bk - 1       # one forced token per round
+        # every block seed is the causal (greedy AR) continuation of what precedes it
+        ref = full_logits(dec, torch.tensor([p + r.output[:-1]]))[0]
+        for j in range(0, len(r.output), Bk):
+            assert int(ref[len(p) + j - 1].argmax()) == r.output[j]
+
+
+def test_sampled_diffusion_decode_respects_eos():
+    dec = tiny_dense()
+    torch.manual_seed(7)
+    eng = Engine(Runtime(dec, max_slots=4, max_len=256), mask_id=96, mode="diffusion", block_size=4,
+                 threshold=0.3)
+    sp = SamplingParams(temperature=1.0, top_k=10, top_p=0.9, seed=3)
+    reqs = eng.generate([[1, 2, 3, 4, 5]] * 2, max_new_tokens=30, sampling=sp, eos=(7,))
+    for r in reqs:
+        assert r.finish_reason in ("stop", "length") and 7 not in r.output
+
+
+def _lockstep_rank(rank, world, port, out):
+    import os
+
+    import torch.distributed as dist
+
+    from trida_stack_b200.serve.lockstep import LockstepDriver
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        eng = Engine(Runtime(tiny_dense(), max_slots=4, max_len=256), mask_id=96, mode="self-spec", n=3,
+                     max_running=2)
+        drv = LockstepDriver(eng)
+        if rank == 0:
+            reqs = [eng.submit(__import__("trida_stack_b200.serve", fromlist=["Request"]).Request(
+                [1 + i, 2, 3, 4 + i], 12, SamplingParams(temperature=0.0 if i % 2 == 0 else 1.0)))
+                for i in range(5)]
+            while not all(r.done for r in reqs):
+                drv.step_leader()
+            drv._stop = True
+            drv.step_leader()
+        else:
+            drv.run_follower()
+            reqs = drv.submitted
+        out.put((rank, [r.output for r in reqs]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_lockstep_driver_keeps_ranks_identical():
+    """Tensor-parallel serving front end: requests (incl. sampled ones without a seed) reach every
+    rank in the same order and every rank decodes the same tokens (gloo, 2 CPU ranks)."""
+    import socket
+
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    procs = [ctx.Process(target=_lockstep_rank, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(out.get(timeout=240) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res[0] == res[1] and len(res[0]) == 5 and all(len(o) > 0 for o in res[0])

@@ -63,7 +63,7 @@ def test_cuda_runtime_matches_cpu(cfg):
         assert _rel(a, b) < 3e-2, _rel(a, b)
 
 
-@pytest.mark.parametrize("mode", ["self-spec", "causal"])
+@pytest.mark.parametrize("mode", ["self-spec", "causal", "diffusion"])
 def test_cuda_engine_graphs_match_eager(mode):
     dec = _init(_hybrid(256)).to("cuda", torch.bfloat16)
     torch.manual_seed(2)
@@ -76,3 +76,21 @@ def test_cuda_engine_graphs_match_eager(mode):
         assert eng.summary(reqs)["tokens_per_forward"] >= 1.0
         outs.append([r.output for r in reqs])
     assert outs[0] == outs[1]
+
+
+def test_conf_argmax_rows_matches_softmax():
+    """Fused greedy token + softmax probability per row (strided rows of a canvas) vs fp32 torch."""
+    from trida_stack_b200.ops._ext import ext
+    torch.manual_seed(0)
+    lg = torch.randn(5, 9, 248320, device="cuda") * 3
+    lg[1, 2, 77] = 40.0                               # a confident row
+    view = lg[:, :8]                                  # non-contiguous batch stride
+    idx = torch.empty(5, 8, dtype=torch.long, device="cuda")
+    mx = torch.empty(5, 8, device="cuda")
+    z = torch.empty(5, 8, device="cuda")
+    ext().conf_argmax_rows(view, idx, mx, z)
+    p = torch.softmax(view.double(), -1)
+    conf, ref = p.max(-1)
+    assert torch.equal(idx, ref)
+    torch.testing.assert_close((1.0 / z).double(), conf, rtol=1e-4, atol=1e-6)
+    torch.testing.assert_close(mx, view.max(-1).values)

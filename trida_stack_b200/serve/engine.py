@@ -18,6 +18,16 @@ truncated distribution the verifier uses, accepted with probability ``min(1, p /
 corrected from ``norm(max(0, p - q))``.
 
 ``mode="causal"`` decodes one token per forward (a one-row canvas).
+
+``mode="diffusion"`` is pure block-diffusion decoding with the LowConfidenceShift gate (the
+reference's SGLang ``LowConfidenceShiftHybridDiffusion`` and vLLM ``_denoise_shift_step``,
+``inference/zoro-1/vllm/vllm_native_diffusion/qwen3_5_diffusion.py:449-632``): a block canvas
+``[seed, MASK x (B-1)]`` whose row 0 is token-causal and whose other rows see the whole canvas is
+denoised in rounds; position i reads the prediction of row i-1 (softmax in fp32); masked
+positions whose confidence exceeds ``threshold`` are committed, and when none does the single most
+confident one is forced; the last allowed round commits every remaining mask.  A finished block is
+then run once more as clean token-causal rows, which advances the caches and yields the next seed
+from its last row.
 """
 import itertools
 import queue
@@ -63,6 +73,8 @@ class Request:
     t0: Optional[int] = None
     t0_emitted: bool = False
     pending: Optional[int] = None
+    canvas: Optional[List[int]] = None        # diffusion mode: the block being denoised
+    rounds: int = 0
     specs: Optional[List[int]] = None
     spec_q: Optional[torch.Tensor] = None
     gen: Optional[torch.Generator] = None
@@ -95,17 +107,21 @@ class Engine:
     """Continuous-batching decode engine over one ``Runtime``."""
 
     def __init__(self, runtime: Runtime, mask_id: int, mode: str = "self-spec", n: int = 4,
-                 max_running: Optional[int] = None, graphs: bool = False):
-        assert mode in ("self-spec", "causal")
+                 max_running: Optional[int] = None, graphs: bool = False, block_size: int = 8,
+                 threshold: float = 0.9, max_steps: Optional[int] = None):
+        assert mode in ("self-spec", "causal", "diffusion")
         self.rt = runtime
         if graphs and runtime.cuda:
             runtime.use_graphs()
         self.mask_id = mask_id
         self.mode = mode
         self.n = n if mode == "self-spec" else 1
-        self.blk = 2 * self.n - 1
+        self.blk = 2 * self.n - 1 if mode != "diffusion" else block_size
+        self.threshold = threshold
+        self.max_steps = max_steps or max(block_size - 1, 1)
         self.max_running = min(max_running or runtime.max_slots, runtime.max_slots)
         self.waiting: "queue.Queue[Request]" = queue.Queue()
+        self.inbox: "Optional[queue.Queue[Request]]" = None   # set by a lock-step (TP) driver
         self.running: List[Request] = []
         self._ids = itertools.count()
         self._lock = threading.Lock()
@@ -118,10 +134,13 @@ class Engine:
         req.rid = next(self._ids)
         req.t_submit = time.perf_counter()
         req.accept_hist = [0] * self.n
+        self._seed_request(req)
+        (self.inbox if self.inbox is not None else self.waiting).put(req)
+        return req
+
+    def _seed_request(self, req):
         if req.sampling.seed is not None:
             req.gen = torch.Generator(device=self.rt.device).manual_seed(req.sampling.seed)
-        self.waiting.put(req)
-        return req
 
     def generate(self, prompts, max_new_tokens=256, sampling=None, eos=()):
         """Synchronous batch generation (runs the loop in the caller's thread)."""
@@ -175,9 +194,11 @@ class Engine:
             for b, r in enumerate(grp):
                 r.t0 = self._pick(logits[b:b + 1], r)[0]
                 r.t0_emitted = False
-                if self.mode == "causal":
+                if self.mode in ("causal", "diffusion"):
                     self._emit(r, [r.t0])
                     r.t0_emitted = True
+                if self.mode == "diffusion":
+                    r.canvas, r.rounds = [r.t0] + [self.mask_id] * (self.blk - 1), 0
             self.running.extend(grp)
         self._reap()
 
@@ -220,6 +241,8 @@ class Engine:
 
     # ------------------------------------------------------------------ one decode forward
     def _decode(self):
+        if self.mode == "diffusion":
+            return self._decode_diffusion()
         reqs = self.running
         slots = [r.slot for r in reqs]
         n, blk, K = self.n, self.blk, self.n - 1
@@ -277,6 +300,54 @@ class Engine:
                 r.pending, r.specs, r.spec_q = clean, new_specs, new_q
         self.rt.commit(slots, adv)
         self._reap()
+
+    def _decode_diffusion(self):
+        Bk, M = self.blk, self.mask_id
+        den = [r for r in self.running if M in r.canvas[1:]]
+        fin = [r for r in self.running if M not in r.canvas[1:]]
+        if den:                                          # one denoise round
+            logits = self.rt.canvas([r.slot for r in den], [r.canvas for r in den], 1)
+            greedy = all(r.sampling.greedy for r in den)
+            if greedy:
+                idx, conf = self.rt.conf_argmax(logits[:, :Bk - 1])
+                idx, conf = idx.tolist(), conf.tolist()
+            self.rt.discard()
+            self.stats["forwards"] += 1
+            for b, r in enumerate(den):
+                if greedy:
+                    pred, cf = idx[b], conf[b]
+                else:
+                    pred, cf = self._sample_rows(logits[b, :Bk - 1], r)
+                r.forwards += 1
+                r.rounds += 1
+                masked = [i for i in range(1, Bk) if r.canvas[i] == M]
+                if r.rounds >= self.max_steps:
+                    take = masked
+                else:
+                    take = [i for i in masked if cf[i - 1] > self.threshold]
+                    if not take:
+                        take = [max(masked, key=lambda i: cf[i - 1])]
+                for i in take:
+                    r.canvas[i] = pred[i - 1]
+        if fin:                                          # commit finished blocks causally
+            slots = [r.slot for r in fin]
+            logits = self.rt.canvas(slots, [r.canvas for r in fin], Bk)
+            greedy = all(r.sampling.greedy for r in fin)
+            am = self.rt.argmax(logits)[:, Bk - 1].tolist() if greedy else None
+            seeds = [am[b] if greedy else self._pick(logits[b, Bk - 1:Bk], r)[0] for b, r in enumerate(fin)]
+            self.rt.commit(slots, [Bk] * len(fin))
+            self.stats["forwards"] += 1
+            for b, r in enumerate(fin):
+                r.forwards += 1
+                self._emit(r, r.canvas[1:] + [seeds[b]])
+                r.canvas, r.rounds = [seeds[b]] + [M] * (Bk - 1), 0
+        self._reap()
+
+    def _sample_rows(self, L, r):
+        """Sampled denoise read-out: a token per row from the truncated distribution and its probability."""
+        P = truncated_probs(L, r.sampling)
+        tok = torch.multinomial(P, 1, generator=r.gen)
+        return tok.squeeze(-1).tolist(), P.gather(1, tok).squeeze(-1).tolist()
 
     def _verify(self, r, L, am):
         n, blk, K = self.n, self.blk, self.n - 1

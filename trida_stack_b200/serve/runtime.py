@@ -150,6 +150,32 @@ class Runtime:
             out = allp[..., 1].gather(0, best).squeeze(0).long()
         return out
 
+    def conf_argmax(self, logits):
+        """Greedy token and its softmax probability per row of fp32 logits [B, R, V] (``R`` may be a
+        row slice of a canvas's logits): one fused pass on CUDA; vocabulary-parallel shards combine
+        their (max, normaliser, index) triples across ranks."""
+        if not self.cuda:
+            p = torch.softmax(logits.float(), -1)
+            conf, idx = p.max(-1)
+            return idx, conf
+        B, R, _ = logits.shape
+        idx = torch.empty(B, R, dtype=torch.long, device=logits.device)
+        mx = torch.empty(B, R, dtype=torch.float32, device=logits.device)
+        z = torch.empty(B, R, dtype=torch.float32, device=logits.device)
+        self.C.conf_argmax_rows(logits, idx, mx, z)
+        if self.tp is None:
+            return idx, 1.0 / z
+        trip = torch.stack([mx, z, (idx + self.dec.vocab_offset).float()], -1)
+        allt = self.tp.gather(trip)                                          # [W, B, R, 3]
+        M = allt[..., 0].max(0).values
+        Z = (allt[..., 1] * torch.exp(allt[..., 0] - M[None])).sum(0)
+        best = allt[..., 0].argmax(0, keepdim=True)
+        return allt[..., 2].gather(0, best).squeeze(0).long(), 1.0 / Z
+
+    def discard(self):
+        """Drop the last canvas without committing any row (a denoise round)."""
+        self.pending = None
+
     def _forward(self, st, tokens):
         x = self.dec.embed_tokens(tokens.reshape(-1)) if self.cuda else self.dec.embed[tokens.reshape(-1)]
         for i, layer in enumerate(self.dec.layers):
