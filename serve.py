@@ -124,6 +124,8 @@ def build(args):
                     max_steps=dcfg.get("max_steps"))
     if graphs:
         rt.use_graphs(tuple(int(b) for b in args.cuda_graph_bs.split()))
+    if not args.no_stats:
+        engine.stats_interval = 10.0
     return engine, tok, name, decider
 
 
@@ -145,8 +147,31 @@ def _init_tp(args):
     return dist.new_group(backend="gloo", timeout=datetime.timedelta(days=1))
 
 
+class _Tee:
+    """Write-through to the console and a log file (``--log``)."""
+
+    def __init__(self, *streams):
+        self.streams = streams
+
+    def write(self, data):
+        for s in self.streams:
+            s.write(data)
+            s.flush()
+        return len(data)
+
+    def flush(self):
+        for s in self.streams:
+            s.flush()
+
+    def isatty(self):
+        return False
+
+
 def main(argv=None):
     args = parse_args(argv)
+    if args.log:
+        fh = open(args.log, "a", buffering=1)
+        sys.stdout, sys.stderr = _Tee(sys.__stdout__, fh), _Tee(sys.__stderr__, fh)
     if args.dry_run:
         print(json.dumps({"model": resolve_model(args), "mode": args.mode, "port": args.port, "host": args.host,
                           "tp": args.tp, "config": decode_config(args.config)}))

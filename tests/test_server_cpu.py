@@ -94,3 +94,61 @@ def test_systemone_decisions_and_validation(server):
     assert bad.json()["detail"][0]["loc"][-1] == "type"
     alias = requests.post(server + "/v1/decide", json={"request": body})
     assert alias.status_code == 200 and set(alias.json()["answers"]) == {"q1", "q2", "q3"}
+
+
+def test_eval_client_task_sweep_and_merge(server, tmp_path):
+    """eval.py against the served engine: a local GSM8K file, the summary fields, tokens per forward
+    from /v1/stats, the fixed-output sweep (ignore_eos) and shard merging."""
+    import eval as E
+    port = int(server.rsplit(":", 1)[1])
+    data = tmp_path / "gsm8k.jsonl"
+    data.write_text("\n".join(json.dumps({"question": f"t{i} t{i + 1}", "answer": f"x #### {i}"}) for i in range(4)))
+    outs = []
+    for shard in ("0/2", "1/2"):
+        out = tmp_path / f"r{shard[0]}"
+        s = E.main(["gsm8k", "--data", str(data), "--port", str(port), "--max-tokens", "6", "--max-workers", "2",
+                    "--shard", shard, "--out", str(out)])
+        assert s["n"] == 2 and s["errors"] == 0 and s["forward"]["tok_per_fwd"] is not None
+        assert (out / "requests.jsonl").exists()
+        outs.append(str(out))
+    merged = E.merge(outs)
+    assert merged["n"] == 4 and merged["shards"] == 2
+    res = E.main(["sweep", "--data", str(data), "--port", str(port), "--concurrency", "1", "2", "--limit", "2",
+                  "--warmup", "0", "--max-tokens", "5"])
+    assert [r["concurrency"] for r in res] == [1, 2]
+    assert all(r["n_ok"] == 2 and r["tokens"] == 10 for r in res)     # ignore_eos: exactly max_tokens each
+    st = requests.get(server + "/v1/stats").json()
+    assert st["forwards"] > 0 and st["tokens"] > 0
+
+
+def test_router_fails_over_and_streams(server):
+    """Data-parallel router: a dead replica is skipped, streamed answers pass through, stats add up."""
+    import uvicorn
+
+    from trida_stack_b200.serve.router import build_app
+    dead = f"http://127.0.0.1:{_free_port()}"
+    port = _free_port()
+    srv = uvicorn.Server(uvicorn.Config(build_app([dead, server], timeout=60), host="127.0.0.1", port=port,
+                                        log_level="error"))
+    threading.Thread(target=srv.run, daemon=True).start()
+    url = f"http://127.0.0.1:{port}"
+    for _ in range(200):
+        try:
+            if requests.get(url + "/health", timeout=1).ok:
+                break
+        except requests.ConnectionError:
+            time.sleep(0.05)
+    try:
+        for _ in range(3):
+            r = requests.post(url + "/v1/chat/completions",
+                              json={"messages": [{"role": "user", "content": "t5 t6"}], "max_tokens": 4}).json()
+            assert r["object"] == "chat.completion"
+        with requests.post(url + "/v1/chat/completions", stream=True,
+                           json={"messages": [{"role": "user", "content": "t7"}], "max_tokens": 4,
+                                 "stream": True}) as r:
+            lines = [l for l in r.iter_lines(decode_unicode=True) if l]
+        assert lines[-1] == "data: [DONE]"
+        assert requests.get(url + "/v1/stats").json()["replicas"] == 1
+        assert requests.get(url + "/v1/models").json()["data"]
+    finally:
+        srv.should_exit = True

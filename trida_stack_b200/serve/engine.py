@@ -128,6 +128,8 @@ class Engine:
         self._thread = None
         self._stop = False
         self.stats = {"forwards": 0, "tokens": 0, "steps": 0, "prefill_tokens": 0}
+        self.stats_interval = 0.0            # seconds between stats lines on stdout (0 = off)
+        self._stats_t = time.perf_counter()
 
     # ------------------------------------------------------------------ API
     def submit(self, req: Request) -> Request:
@@ -173,6 +175,12 @@ class Engine:
         if self.running:
             self._decode()
         self.stats["steps"] += 1
+        if self.stats_interval and time.perf_counter() - self._stats_t >= self.stats_interval:
+            self._stats_t = time.perf_counter()
+            st = self.stats
+            print(f"[trida-engine] mode={self.mode} running={len(self.running)} fwd={st['forwards']} "
+                  f"tok={st['tokens']} tok/fwd={st['tokens'] / max(st['forwards'], 1):.3f} "
+                  f"prefill_tok={st['prefill_tokens']}", flush=True)
 
     def _admit(self):
         new = []

@@ -105,7 +105,8 @@ def build_app(engine, tokenizer, model_name, decider=None):
     async def run(ids, body, stream_cb=None):
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
-        req = Request(ids, int(body.get("max_tokens") or body.get("max_completion_tokens") or 512), sampling(body), eos)
+        req = Request(ids, int(body.get("max_tokens") or body.get("max_completion_tokens") or 512), sampling(body),
+                      () if body.get("ignore_eos") else eos)
         req.on_tokens = lambda toks: loop.call_soon_threadsafe(q.put_nowait, toks)
         engine.submit(req)
         while True:
@@ -119,6 +120,14 @@ def build_app(engine, tokenizer, model_name, decider=None):
     @app.get("/health")
     async def health():
         return {"status": "ok"}
+
+    @app.get("/v1/stats")
+    async def stats():
+        """Cumulative engine counters (forwards, emitted tokens, prefill tokens) and tokens per forward."""
+        st = dict(engine.stats)
+        st.update(mode=engine.mode, gen_block=engine.n, running=len(engine.running),
+                  tok_per_fwd=round(st["tokens"] / st["forwards"], 4) if st["forwards"] else None)
+        return st
 
     @app.get("/v1/models")
     async def models():
