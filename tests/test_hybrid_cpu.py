@@ -108,3 +108,25 @@ def test_two_stream_objective_and_decision_backward():
     dl, dlog = m(None, None, None, decision=batch)
     dl.backward()
     assert m.jev_head.q.weight.grad is not None and math.isfinite(dl.item())
+
+
+def test_block_bidirectional_reference_scan():
+    """Single-stream block-bidirectional recurrence: one-token blocks reduce to the causal scan, and a
+    block's read-out depends on later tokens of the same block but never on later blocks."""
+    torch.manual_seed(0)
+    B, T, H, d = 2, 12, 2, 8
+    q, k = G.l2norm(torch.randn(B, T, H, d)), G.l2norm(torch.randn(B, T, H, d))
+    v = torch.randn(B, T, H, d)
+    g = -torch.rand(B, T, H)
+    beta = torch.rand(B, T, H)
+    o1, S1 = G.gdn_block_bidirectional(q, k, v, g, beta, torch.arange(T).expand(B, -1))
+    oc, _ = G.gdn_causal(q, k, v, g, beta)
+    torch.testing.assert_close(o1, oc, rtol=1e-5, atol=1e-5)
+    blocks = (torch.arange(T) // 4).expand(B, -1)
+    o4, S4 = G.gdn_block_bidirectional(q, k, v, g, beta, blocks)
+    torch.testing.assert_close(S4, S1, rtol=1e-5, atol=1e-5)       # the exit state stays causal
+    v2 = v.clone()
+    v2[:, 6] += 1.0                                                # a token in block 1
+    o5, _ = G.gdn_block_bidirectional(q, k, v2, g, beta, blocks)
+    assert torch.allclose(o5[:, :4], o4[:, :4])                    # earlier block untouched
+    assert not torch.allclose(o5[:, 4], o4[:, 4])                  # same block: read-out sees the future

@@ -119,6 +119,39 @@ def gdn_causal(q, k, v, g, beta, doc_start=None, readout_block=0):
     return o, None
 
 
+def gdn_block_bidirectional(q, k, v, g, beta, block_ids, initial_state=None):
+    """Block-local bidirectional recurrence (the reference's research-level single-stream variant,
+    ``train/models/hybrid.py:461-536``, superseded there by the two-stream form).
+
+    ``block_ids`` [B, T] tags each token with its diffusion block (contiguous equal ids).  A block's
+    entry state E is the causal state after everything before it; the forward sub-scan from E over
+    the block gives the causal outputs, a backward sub-scan from E over the block's tokens in
+    reverse gives a second read-out, and every token outputs their mean.  The next block enters
+    with the forward (causal) exit state.  Inputs [B, T, H, d] (q, k L2-normalised, q not scaled);
+    returns (o [B, T, H, dv] fp32, final state [B, H, dk, dv])."""
+    B, T, H, dk = q.shape
+    dv = v.shape[-1]
+    qs, kf, vf, gf, bf = q.float() * dk ** -0.5, k.float(), v.float(), g.float(), beta.float()
+    start = torch.ones(B, T, dtype=torch.bool, device=q.device)
+    start[:, 1:] = block_ids[:, 1:] != block_ids[:, :-1]
+    last = torch.ones(B, T, dtype=torch.bool, device=q.device)
+    last[:, :-1] = block_ids[:, 1:] != block_ids[:, :-1]
+    S = (torch.zeros(B, H, dk, dv, dtype=torch.float32, device=q.device) if initial_state is None
+         else initial_state.float())
+    entry, entries, fwd = S, [], []
+    for t in range(T):
+        entry = torch.where(start[:, t][:, None, None, None], S, entry)
+        entries.append(entry)
+        S, o = _step(S, qs[:, t], kf[:, t], vf[:, t], gf[:, t], bf[:, t])
+        fwd.append(o)
+    bwd = [None] * T
+    R = torch.zeros_like(S)
+    for t in range(T - 1, -1, -1):
+        R = torch.where(last[:, t][:, None, None, None], entries[t], R)
+        R, bwd[t] = _step(R, qs[:, t], kf[:, t], vf[:, t], gf[:, t], bf[:, t])
+    return 0.5 * (torch.stack(fwd, 1) + torch.stack(bwd, 1)), S
+
+
 def gdn_two_stream(q, k, v, g, beta, L, V, bd, causal_clean=True, causal_noisy=False, doc_start=None):
     """Two-stream recurrence over a ``[x0 ; xt_1..xt_V]`` row ([B, (1+V)L, H, d] inputs)."""
     B, T, H, dk = q.shape
