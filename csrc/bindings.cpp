@@ -144,6 +144,41 @@ void symm_allreduce(const std::vector<int64_t>& bufs, const std::vector<int64_t>
   TORCH_CHECK(rc == 0, "symm_allreduce failed with code ", rc);
 }
 
+// Row-parallel GEMM with the tensor-parallel all-reduce in its epilogue:
+// D = sum over ranks of A_r B_r^T (+ residual).  recv / flags: every rank's receive buffer
+// ([2][world][mcap][N] bf16) and counters ([2][tiles_cap][4] u32); ctr_done: int32 [2], zero at start.
+void gemm_allreduce(const at::Tensor& A, const at::Tensor& B, const at::Tensor& D,
+                    const c10::optional<at::Tensor>& residual, const std::vector<int64_t>& recv,
+                    const std::vector<int64_t>& flags, int64_t rank, const at::Tensor& ctr_done, int64_t mcap,
+                    int64_t tiles_cap) {
+  CHECK_CUDA(A); CHECK_CUDA(B); CHECK_CUDA(D);
+  CHECK_BF16(A); CHECK_BF16(B); CHECK_BF16(D);
+  CHECK_ROWMAJOR(A); CHECK_ROWMAJOR(B); CHECK_ROWMAJOR(D);
+  TORCH_CHECK(ctr_done.scalar_type() == at::kInt && ctr_done.numel() >= 2, "ctr_done must be int32 [2]");
+  auto pa = ptr_arrays(recv, flags);
+  trida::GemmArgs a{};
+  a.M = A.size(0); a.K = A.size(1); a.N = B.size(0);
+  TORCH_CHECK(B.size(1) == a.K && D.size(0) == a.M && D.size(1) == a.N, "shape mismatch");
+  a.A = A.data_ptr(); a.lda = A.stride(0);
+  a.B = B.data_ptr(); a.ldb = B.stride(0);
+  a.D = D.data_ptr(); a.ldd = D.stride(0);
+  a.alpha = 1.f; a.beta = 0.f; a.C = nullptr; a.ldc = a.ldd;
+  if (residual.has_value() && residual->defined()) {
+    CHECK_BF16((*residual)); CHECK_ROWMAJOR((*residual));
+    TORCH_CHECK(residual->size(0) == a.M && residual->size(1) == a.N, "residual shape");
+    a.C = residual->data_ptr(); a.ldc = residual->stride(0); a.beta = 1.f;
+  }
+  a.batch = 1;
+  if (a.M == 0) return;
+  TORCH_CHECK((a.lda * 2) % 16 == 0 && (a.ldb * 2) % 16 == 0 && (a.ldd * 2) % 16 == 0 && (a.ldc * 2) % 16 == 0,
+              "GEMM leading dimensions must be 16-byte multiples");
+  c10::cuda::CUDAGuard g(A.device());
+  unsigned* cd = reinterpret_cast<unsigned*>(ctr_done.data_ptr<int>());
+  trida::GemmAllreduce ar{(int)recv.size(), (int)rank, (int)tiles_cap, mcap, pa.bufs, pa.flags, cd, cd + 1};
+  const int rc = trida::gemm_bf16_allreduce(a, ar, sm_count(), stream());
+  TORCH_CHECK(rc == 0, "fused GEMM + all-reduce failed with code ", rc, " (M=", a.M, " N=", a.N, " K=", a.K, ")");
+}
+
 void symm_rs_sumsq(const std::vector<int64_t>& bufs, const std::vector<int64_t>& flags, int64_t rank, int64_t epoch,
                    int64_t shard_off, int64_t shard_len, double scale, const at::Tensor& shard_out,
                    const at::Tensor& partial, const at::Tensor& err, bool accumulate) {
@@ -779,6 +814,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_close", &symm_close);
   m.def("symm_tensor", &symm_tensor);
   m.def("symm_allreduce", &symm_allreduce);
+  m.def("gemm_allreduce", &gemm_allreduce);
   m.def("symm_rs_sumsq", &symm_rs_sumsq, py::arg("bufs"), py::arg("flags"), py::arg("rank"), py::arg("epoch"),
         py::arg("shard_off"), py::arg("shard_len"), py::arg("scale"), py::arg("shard_out"), py::arg("partial"),
         py::arg("err"), py::arg("accumulate") = false);

@@ -9,6 +9,15 @@
 //               TMEM accumulators (128 lanes x 256 fp32 columns each), so the epilogue of tile i
 //               overlaps the mainloop of tile i + 1;
 //   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, alpha / beta * C, convert, store.
+// Fused all-reduce epilogue (tensor-parallel row-parallel layers, ``gemm_bf16_allreduce``): the
+// epilogue warps push each tile's bf16 partial from registers into every rank's receive buffer over
+// NVLink (plain stores to peer memory), release the TMEM accumulator to the next tile, bump one
+// arrival counter per (tile, warp) on every rank, then wait until all ranks' partials of their rows
+// have arrived in this GPU's own buffer, sum them (+ residual) and TMA-store the result: the
+// GEMM and its all-reduce are one kernel, and the exchange of tile i overlaps the mainloop of
+// tile i + 1.  Receive buffers and counters alternate between two parities by a device-side call
+// counter (graph-capturable); a waiter resets its counter after use, which is safe because a rank
+// can only start the next same-parity call after this rank has finished the current one.
 // Operand majorness follows the caller's row-major tensors: K-major operands are loaded with a
 // 64-element K box (UMMA K-major SWIZZLE_128B), MN-major operands with a 64-element MN box
 // (UMMA MN-major SWIZZLE_128B; LBO = one 64-wide MN atom).  Every mbarrier wait is bounded.
@@ -56,7 +65,44 @@ struct Params {
   int* err;
   int splits, kb_per;     // split-K: units = tiles * splits, each over kb_per K blocks
   float* ws;              // split-K partials [splits, M, N] fp32 (splits > 1)
+  // fused all-reduce (ar_world > 1): per destination rank, its receive buffer
+  // [2 parities][world][mcap][N] bf16 and its arrival counters [2][tiles_cap][4 warps]
+  int ar_world, ar_rank, ar_tiles_cap;
+  int64_t ar_mcap;
+  bf16* ar_recv[8];
+  unsigned* ar_flag[8];
+  unsigned* ar_ctr;       // this rank's call counter (the call's epoch = *ar_ctr + 1)
+  unsigned* ar_done;      // CTAs finished in this call (the last one advances ar_ctr)
 };
+
+__device__ __forceinline__ void red_release_sys(unsigned* p, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Poll a counter until it reaches `target`; gives up after kWaitLimitNs (error word set).
+__device__ __forceinline__ bool wait_count(const unsigned* f, unsigned target, int* err, int code) {
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (ld_acquire_sys(f) >= target) return true;
+    if ((it & 255u) == 255u) {
+      if (global_ns() - t0 > kWaitLimitNs) {
+        atomicExch(err, code);
+        return false;
+      }
+      __nanosleep(200);
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
   asm volatile(
@@ -209,12 +255,120 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     int ebuf = 0;
     uint32_t cpar[2] = {0u, 0u};
     int t = 0;
+    const bool fused = p.ar_world > 1;
+    const unsigned epoch = fused ? *reinterpret_cast<volatile unsigned*>(p.ar_ctr) + 1u : 0u;
+    const int par = (int)(epoch & 1u);
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++t) {
       const int ab = t % NACC;
       if (!mbar_wait(&acc_full[ab], (t / NACC) & 1, p.err, 106)) break;
       tc_fence_after();
       int m0, n0;
       tile_coords(u / p.splits, mt, nt, BM, m0, n0);
+      if (fused) {
+        // ---- phase 1: this rank's partial rows -> every rank's receive buffer (slot ar_rank)
+        const int W = p.ar_world;
+#pragma unroll 1
+        for (int h = 0; h < MH; ++h) {
+          const uint32_t acc = tmem + (ab + h) * BN + lane_off;
+          const int row = m0 + h * 128 + r;
+          const bool rok = row < p.M;
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld32(acc + c * 32, v);
+            tmem_wait_ld();
+            const int col0 = n0 + c * 32;
+            if (!rok || col0 >= p.N) continue;
+            uint4 pk[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              pk[j] = make_uint4(pack_bf16x2(__uint_as_float(v[8 * j]), __uint_as_float(v[8 * j + 1])),
+                                 pack_bf16x2(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3])),
+                                 pack_bf16x2(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5])),
+                                 pack_bf16x2(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7])));
+            const int64_t off = ((int64_t)(par * W + p.ar_rank) * p.ar_mcap + row) * p.N + col0;
+#pragma unroll 1
+            for (int d = 0; d < W; ++d) {
+              uint4* dst = reinterpret_cast<uint4*>(p.ar_recv[(p.ar_rank + d) % W] + off);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) dst[j] = pk[j];
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[ab]);                 // the accumulator is free for the next tile
+        const int64_t fidx = ((int64_t)par * p.ar_tiles_cap + u) * 4 + q;
+        asm volatile("fence.acq_rel.sys;\n" ::: "memory");
+        __syncwarp();
+        if (lane == 0)
+          for (int d = 0; d < W; ++d) red_release_sys(p.ar_flag[(p.ar_rank + d) % W] + fidx, 1u);
+        // ---- phase 2: wait for every rank's partial of this warp's rows, sum (+ C), TMA-store D
+        int ok = 1;
+        if (lane == 0) {
+          unsigned* f = p.ar_flag[p.ar_rank] + fidx;
+          ok = wait_count(f, (unsigned)W, p.err, 110) ? 1 : 0;
+          if (ok) *reinterpret_cast<volatile unsigned*>(f) = 0u;
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        __syncwarp();
+        if (!ok) continue;
+        const bool use_c = p.C != nullptr && p.beta != 0.f;
+        const bf16* own = p.ar_recv[p.ar_rank];
+#pragma unroll 1
+        for (int h = 0; h < MH; ++h) {
+          const int row0 = m0 + h * 128 + q * 32;
+          const int row = row0 + lane;
+          const bool rok = row < p.M;
+#pragma unroll 1
+          for (int ch = 0; ch < BN / 64; ++ch) {
+            const int col0 = n0 + ch * 64;
+            if (row0 >= p.M || col0 >= p.N) continue;   // warp-uniform
+            unsigned char* sb = epi + q * 8192 + ebuf * 4096;
+            if (lane == 0) bulk_wait_read1();
+            __syncwarp();
+            if (use_c) {
+              if (lane == 0) {
+                mbar_expect_tx(&cbar[q * 2 + ebuf], 4096);
+                tma_load_2d(sb, &tmC, &cbar[q * 2 + ebuf], col0, row0);
+              }
+              mbar_wait(&cbar[q * 2 + ebuf], cpar[ebuf], p.err, 107);
+              cpar[ebuf] ^= 1;
+            }
+            unsigned char* rowp = sb + lane * 128;
+#pragma unroll 1
+            for (int j = 0; j < 8; ++j) {
+              float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+              if (rok) {
+#pragma unroll 1
+                for (int sidx = 0; sidx < W; ++sidx) {
+                  float x[8];
+                  load8(own + ((int64_t)(par * W + sidx) * p.ar_mcap + row) * p.N + col0 + 8 * j, x);
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) o[e] += x[e];
+                }
+              }
+              bf16* cp = reinterpret_cast<bf16*>(rowp + ((j ^ (lane & 7)) << 4));
+#pragma unroll
+              for (int e = 0; e < 8; ++e) o[e] *= p.alpha;
+              if (use_c) {
+                float cv[8];
+                load8(cp, cv);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) o[e] += p.beta * cv[e];
+              }
+              store8(cp, o);
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmD, sb, col0, row0);
+              bulk_commit();
+            }
+            ebuf ^= 1;
+          }
+        }
+        continue;
+      }
 #pragma unroll 1
       for (int h = 0; h < MH; ++h) {
       const uint32_t acc = tmem + (ab + h) * BN + lane_off;
@@ -314,6 +468,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, 512);
+  if (p.ar_world > 1 && threadIdx.x == 0) {         // the last CTA of the call advances the counter
+    __threadfence();
+    if (atomicAdd(p.ar_done, 1u) == gridDim.x - 1) {
+      *p.ar_done = 0u;
+      *p.ar_ctr = *reinterpret_cast<volatile unsigned*>(p.ar_ctr) + 1u;
+      __threadfence();
+    }
+  }
 }
 
 // D = alpha * sum_s ws[s] + beta * C   (split-K reduction; one thread per 4 columns)
@@ -430,6 +592,9 @@ int gemm_bf16(GemmLayout layout, bool d_fp32, const GemmArgs& a, int tile, int s
   p.D = a.D; p.ldd = a.ldd; p.C = a.C; p.ldc = a.ldc;
   p.alpha = a.alpha; p.beta = a.beta; p.d_fp32 = d_fp32 ? 1 : 0;
   p.err = err_word();
+  p.ar_world = 1; p.ar_rank = 0; p.ar_tiles_cap = 0; p.ar_mcap = 0;
+  p.ar_ctr = nullptr; p.ar_done = nullptr;
+  for (int i = 0; i < 8; ++i) { p.ar_recv[i] = nullptr; p.ar_flag[i] = nullptr; }
   const int kb = (a.K + BK - 1) / BK;
   p.kb_per = (kb + splits - 1) / splits;
   p.splits = (kb + p.kb_per - 1) / p.kb_per;
@@ -468,6 +633,39 @@ int gemm_bf16(GemmLayout layout, bool d_fp32, const GemmArgs& a, int tile, int s
     splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(ws, p.splits, a.M, a.N, a.alpha, a.beta, a.C, a.ldc, a.D, a.ldd,
                                                     p.d_fp32);
   }
+  return cudaGetLastError() == cudaSuccess ? 0 : -13;
+}
+
+int gemm_bf16_allreduce(const GemmArgs& a, const GemmAllreduce& ar, int sm_count, cudaStream_t stream) {
+  using namespace gemm100;
+  if (ar.world < 2 || ar.world > 8 || ar.rank < 0 || ar.rank >= ar.world) return -30;
+  if (a.N % 64 != 0 || a.M > ar.mcap) return -31;
+  const int tiles = ((a.M + 127) / 128) * ((a.N + BN - 1) / BN);
+  if (tiles > ar.tiles_cap) return -32;
+  Params p;
+  p.M = a.M; p.N = a.N; p.K = a.K;
+  p.D = a.D; p.ldd = a.ldd; p.C = a.C; p.ldc = a.ldc;
+  p.alpha = a.alpha; p.beta = a.beta; p.d_fp32 = 0;
+  p.err = err_word();
+  p.kb_per = (a.K + BK - 1) / BK;
+  p.splits = 1;
+  p.ws = nullptr;
+  p.a_kmajor = 1; p.b_kmajor = 1;
+  p.ar_world = ar.world; p.ar_rank = ar.rank; p.ar_tiles_cap = ar.tiles_cap; p.ar_mcap = ar.mcap;
+  p.ar_ctr = ar.ctr; p.ar_done = ar.done;
+  for (int i = 0; i < 8; ++i) {
+    p.ar_recv[i] = i < ar.world ? reinterpret_cast<bf16*>(ar.recv[i]) : nullptr;
+    p.ar_flag[i] = i < ar.world ? ar.flags[i] : nullptr;
+  }
+  CUtensorMap mA, mB, mD, mC;
+  if (!make_map(&mA, a.A, a.M, a.K, a.lda, 128) || !make_map(&mB, a.B, a.N, a.K, a.ldb, BN)) return -12;
+  if (!make_epi_map(&mD, a.D, a.M, a.N, a.ldd, false)) return -14;
+  if (a.C != nullptr && a.beta != 0.f) {
+    if (!make_epi_map(&mC, a.C, a.M, a.N, a.ldc, false)) return -15;
+  } else {
+    mC = mD;
+  }
+  launch<1>(mA, mB, mD, mC, p, sm_count, stream);
   return cudaGetLastError() == cudaSuccess ? 0 : -13;
 }
 

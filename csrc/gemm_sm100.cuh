@@ -33,6 +33,20 @@ int gemm_bf16(GemmLayout layout, bool d_fp32, const GemmArgs& a, int tile, int s
 // K splits gemm_bf16 should use for this shape (1 = none).
 int gemm_splitk(int M, int N, int K, int sm_count);
 
+// Tensor-parallel row-parallel GEMM with the all-reduce fused into the epilogue (TN layout, bf16 D,
+// D = alpha * sum over ranks of A_r B_r^T + beta * C).  `recv[r]` / `flags[r]`: rank r's receive
+// buffer ([2][world][mcap][N] bf16) and arrival counters ([2][tiles_cap][4] u32, zeroed once), as
+// mapped into this process; `ctr` / `done`: this rank's call counter and finished-CTA count.
+struct GemmAllreduce {
+  int world, rank, tiles_cap;
+  int64_t mcap;
+  void* const* recv;
+  unsigned* const* flags;
+  unsigned* ctr;
+  unsigned* done;
+};
+int gemm_bf16_allreduce(const GemmArgs& a, const GemmAllreduce& ar, int sm_count, cudaStream_t stream);
+
 // Device int the GEMM's bounded mbarrier waits set (non-zero) on a timeout; null if unallocated.
 int* gemm_error_word();
 

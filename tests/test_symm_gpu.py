@@ -107,3 +107,72 @@ def test_symmetric_collectives_match_nccl():
         assert ar_err < 2e-2, (rank, ar_err)
         assert opt_err < 2e-2, (rank, opt_err)
     assert all(p.exitcode == 0 for p in procs)
+
+
+def _fused_worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from trida_stack_b200.serve.tp import TPContext
+        tp = TPContext(max_rows=1200, hidden=2560)
+        assert tp.fused
+        errs = []
+        g = torch.Generator("cuda").manual_seed(10 + rank)
+        for M in (70, 448, 1100, 448):
+            x = torch.randn(M, 512, device="cuda", dtype=torch.bfloat16, generator=g)
+            w = torch.randn(2560, 512, device="cuda", dtype=torch.bfloat16, generator=g) * 0.05
+            res = torch.randn(M, 2560, device="cuda", dtype=torch.bfloat16)
+            dist.broadcast(res, 0)
+            out = tp.row_parallel(x, w, res)
+            ref = (x.float() @ w.float().t()).to(torch.bfloat16).float()
+            dist.all_reduce(ref)
+            ref += res.float()
+            errs.append(((out.float() - ref).abs().max() / ref.abs().max()).item())
+        # replayed from a CUDA graph: the call counter (and buffer parity) lives on the device
+        x = torch.randn(448, 512, device="cuda", dtype=torch.bfloat16, generator=g)
+        w = torch.randn(2560, 512, device="cuda", dtype=torch.bfloat16, generator=g) * 0.05
+        res = torch.zeros(448, 2560, device="cuda", dtype=torch.bfloat16)
+        ref = (x.float() @ w.float().t()).to(torch.bfloat16).float()
+        dist.all_reduce(ref)
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=s):
+                o1 = tp.row_parallel(x, w, res)
+                o2 = tp.row_parallel(x, w, o1)
+        for _ in range(3):
+            gr.replay()
+            torch.cuda.synchronize()
+            errs.append(((o2.float() - 2 * ref).abs().max() / (2 * ref).abs().max()).item())
+        del gr
+        from trida_stack_b200.ops._ext import ext
+        assert int(ext().gemm_error()) == 0
+        q.put((rank, max(errs)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_gemm_allreduce_matches_nccl():
+    """Row-parallel GEMM with the all-reduce in its epilogue (pushes over NVLink, per-tile arrival
+    counters) vs GEMM + NCCL all-reduce, eager and replayed from a CUDA graph, on 2 GPUs."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_fused_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    res = [q.get(timeout=5) for _ in range(2)]
+    for rank, err in res:
+        assert err < 2e-2, (rank, err)
+    assert all(p.exitcode == 0 for p in procs)

@@ -100,16 +100,29 @@ def shard_decoder(dec, rank, world):
 
 class TPContext:
     """Per-process TP state: the process group, the symmetric buffers of the row-parallel
-    all-reduces (two, used alternately) and the vocabulary-parallel greedy pick."""
+    all-reduces and the vocabulary-parallel greedy pick.
 
-    def __init__(self, max_rows, hidden, group=None):
+    ``fused=True`` (default): every row-parallel GEMM runs the all-reduce in its own epilogue
+    (``csrc/gemm_sm100.cu``, ``gemm_bf16_allreduce``): partial tiles are pushed over NVLink into
+    every rank's receive buffer as they come out of the tensor cores and each rank sums its rows
+    as soon as all ranks' tiles have arrived -- one kernel per layer output.  ``fused=False`` keeps
+    the two-kernel path (GEMM into a symmetric buffer, then a one-shot all-reduce kernel)."""
+
+    def __init__(self, max_rows, hidden, group=None, fused=True):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.heap = SymmetricHeap(group)
-        self.bufs = [self.heap.alloc(max_rows * hidden, torch.bfloat16) for _ in range(2)]
-        self.turn = 0
         self.max_rows, self.hidden = max_rows, hidden
+        self.fused = fused and hidden % 64 == 0
+        self.turn = 0
+        if self.fused:
+            self.tiles_cap = -(-max_rows // 128) * -(-hidden // 256)
+            self.recv = self.heap.alloc(2 * self.world * max_rows * hidden, torch.bfloat16)
+            self.flags = self.heap.alloc(2 * self.tiles_cap * 4, torch.int32)
+            self.ctr_done = torch.zeros(2, dtype=torch.int32, device="cuda")
+        else:
+            self.bufs = [self.heap.alloc(max_rows * hidden, torch.bfloat16) for _ in range(2)]
 
     def next_buffer(self, rows):
         if rows > self.max_rows:
@@ -119,10 +132,17 @@ class TPContext:
         return b, b.local[:rows * self.hidden].view(rows, self.hidden)
 
     def row_parallel(self, x, w, residual):
-        """residual + sum over ranks of x_r w_r^T: the GEMM writes this rank's partial into its
-        symmetric buffer, one all-reduce kernel sums all partials over NVLink (+ residual)."""
+        """residual + sum over ranks of x_r w_r^T."""
         from ..ops import blocks
-        buf, part = self.next_buffer(x.shape[0])
+        rows = x.shape[0]
+        if self.fused:
+            if rows > self.max_rows:
+                raise RuntimeError(f"{rows} rows exceed the TP buffers ({self.max_rows})")
+            out = torch.empty(rows, self.hidden, dtype=torch.bfloat16, device=x.device)
+            blocks.ext().gemm_allreduce(x.contiguous(), w, out, residual.contiguous(), self.recv.ptrs,
+                                        self.flags.ptrs, self.rank, self.ctr_done, self.max_rows, self.tiles_cap)
+            return out
+        buf, part = self.next_buffer(rows)
         blocks.gemm(blocks.TN, x, w, part)
         return self.allreduce(buf, x.shape[0], residual)
 
