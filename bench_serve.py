@@ -42,11 +42,13 @@ def main():
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--max-new", type=int, default=512)
     ap.add_argument("--gen-block", type=int, default=16, help="N: causal rows per canvas (canvas = 2N-1 rows)")
-    ap.add_argument("--mode", default="self-spec", choices=["self-spec", "causal"])
+    ap.add_argument("--mode", default="self-spec", choices=["self-spec", "causal", "diffusion"])
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-graphs", action="store_true", help="launch every kernel eagerly (no CUDA graphs)")
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel ranks (launch with torchrun)")
+    ap.add_argument("--tp-unfused", action="store_true",
+                    help="TP all-reduce as a separate kernel after the GEMM instead of in its epilogue")
     args = ap.parse_args()
 
     from trida_stack_b200.models import Decoder
@@ -72,7 +74,7 @@ def main():
         from trida_stack_b200.serve.tp import TPContext, shard_decoder
         dec = shard_decoder(dec, rank, world)
         torch.cuda.empty_cache()
-        tp = TPContext(max_rows=args.requests * 64, hidden=cfg.hidden_size)
+        tp = TPContext(max_rows=args.requests * 64, hidden=cfg.hidden_size, fused=not args.tp_unfused)
     rt = Runtime(dec, max_slots=args.requests, max_len=max_len, tp=tp)
     eng = Engine(rt, mask_id=mask_id, mode=args.mode, n=args.gen_block, max_running=args.requests, graphs=not args.no_graphs)
     g = torch.Generator().manual_seed(args.seed)
@@ -119,7 +121,9 @@ def main():
         "config": {"model": f"Qwen3.5-4B-style hybrid ({args.layers}L)", "requests": args.requests,
                    "prompt": args.prompt, "max_new": args.max_new, "mode": args.mode, "n": args.gen_block,
                    "canvas_rows": 2 * args.gen_block - 1 if args.mode == "self-spec" else 1, "greedy": True,
-                   "cuda_graphs": not args.no_graphs},
+                   "cuda_graphs": not args.no_graphs,
+                   "tp_allreduce": ("fused into the GEMM epilogue" if not args.tp_unfused else "separate kernel")
+                   if world > 1 else None},
         "data": "synthetic uniform prompts, random-init weights", "dtype": "bf16"}), flush=True)
     _finish(rt, world)
 

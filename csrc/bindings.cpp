@@ -181,13 +181,20 @@ void gemm_allreduce(const at::Tensor& A, const at::Tensor& B, const at::Tensor& 
 
 void symm_rs_sumsq(const std::vector<int64_t>& bufs, const std::vector<int64_t>& flags, int64_t rank, int64_t epoch,
                    int64_t shard_off, int64_t shard_len, double scale, const at::Tensor& shard_out,
-                   const at::Tensor& partial, const at::Tensor& err, bool accumulate) {
+                   const at::Tensor& partial, const at::Tensor& err, bool accumulate,
+                   const c10::optional<at::Tensor>& done, int64_t close_slot) {
   auto a = ptr_arrays(bufs, flags);
   TORCH_CHECK(shard_out.scalar_type() == at::kFloat && shard_out.numel() == shard_len, "shard_out");
   TORCH_CHECK(partial.scalar_type() == at::kFloat, "partial fp32");
+  unsigned* dn = nullptr;
+  if (done.has_value() && done->defined()) {
+    TORCH_CHECK(done->scalar_type() == at::kInt && done->numel() >= 1, "done must be int32");
+    dn = reinterpret_cast<unsigned*>(done->data_ptr<int>());
+  }
   const int rc = trida::symm_rs_sumsq(a.bufs, a.flags, rank, bufs.size(), (unsigned)epoch, shard_off, shard_len,
                                       (float)scale, shard_out.data_ptr<float>(), partial.data_ptr<float>(),
-                                      partial.numel(), accumulate ? 1 : 0, err.data_ptr<int>(), stream());
+                                      partial.numel(), accumulate ? 1 : 0, err.data_ptr<int>(), dn, (int)close_slot,
+                                      stream());
   TORCH_CHECK(rc == 0, "symm_rs_sumsq failed with code ", rc);
 }
 
@@ -817,7 +824,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_allreduce", &gemm_allreduce);
   m.def("symm_rs_sumsq", &symm_rs_sumsq, py::arg("bufs"), py::arg("flags"), py::arg("rank"), py::arg("epoch"),
         py::arg("shard_off"), py::arg("shard_len"), py::arg("scale"), py::arg("shard_out"), py::arg("partial"),
-        py::arg("err"), py::arg("accumulate") = false);
+        py::arg("err"), py::arg("accumulate") = false, py::arg("done") = py::none(), py::arg("close_slot") = -1);
   m.def("symm_norm_coef", &symm_norm_coef);
   m.def("symm_adamw_ag", &symm_adamw_ag);
   m.def("gdn_state_numel", &gdn_state_numel);

@@ -137,7 +137,7 @@ int symm_allreduce_bf16(void* const* bufs, unsigned* const* flags, int rank, int
                         cudaStream_t s);
 int symm_rs_sumsq(void* const* bufs, unsigned* const* flags, int rank, int world, unsigned epoch, int64_t shard_off,
                   int64_t shard_len, float scale, float* shard_out, float* partial, int nblocks, int accumulate,
-                  int* err, cudaStream_t s);
+                  int* err, unsigned* done, int close_slot, cudaStream_t s);
 int symm_norm_coef(void* const* partials, unsigned* const* flags, int rank, int world, unsigned epoch, int nblocks,
                    float max_norm, float* norm_out, float* coef_out, int* err, cudaStream_t s);
 int symm_adamw_ag(void* const* bufs, unsigned* const* flags, int rank, int world, unsigned epoch, int64_t shard_off,

@@ -14,7 +14,8 @@
 //               buffers, so one barrier per call suffices (a rank only overwrites a buffer after
 //               every peer has entered the next all-reduce, i.e. finished reading it).
 //   rs_sumsq    reduce-scatter of fp32 gradient buffers: every rank reads its shard of all peers'
-//               gradients, sums, scales, stores (or adds) the shard and its sum of squares.
+//               gradients, sums, scales, stores (or adds) the shard and its sum of squares;
+//               optionally a closing barrier so the source buffer can be reused right after.
 //   adamw_ag    sharded AdamW on the reduced shard with the bf16 result stored straight into
 //               every peer's parameter buffer (the all-gather fused into the update), then a
 //               closing barrier so no rank reads parameters that are still being written.
@@ -99,8 +100,12 @@ __global__ void allreduce_kernel(Peers P, int rank, int world, unsigned* ctr, un
   }
 }
 
+// close_slot >= 0: a closing barrier on that flag slot -- the last CTA to finish reading signals
+// every peer and waits for theirs, so when the kernel completes no rank still reads this rank's
+// gradient buffer (it may be reused at once).
 __global__ void rs_sumsq_kernel(Peers P, int rank, int world, unsigned epoch, int64_t shard_off, int64_t shard_len,
-                                float scale, float* shard_out, float* partial, int accumulate, int* err) {
+                                float scale, float* shard_out, float* partial, int accumulate, int* err,
+                                unsigned* done, int close_slot) {
   barrier(P, rank, world, epoch, 1, err, 202);
   float ss = 0.f;
   const int64_t n4 = shard_len / 4;
@@ -122,6 +127,25 @@ __global__ void rs_sumsq_kernel(Peers P, int rank, int world, unsigned epoch, in
   __shared__ float sred[32];
   ss = block_sum(ss, sred);
   if (threadIdx.x == 0) partial[blockIdx.x] = ss;
+  if (close_slot >= 0 && threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(done, 1u) == gridDim.x - 1) {
+      *done = 0u;
+      __threadfence_system();
+      for (int r = 0; r < world; ++r) st_release(P.flag[r] + close_slot * MAXR + rank, epoch);
+      for (int r = 0; r < world; ++r) {
+        const unsigned* f = P.flag[rank] + close_slot * MAXR + r;
+        long long polls = 0;
+        while ((int)(ld_acquire(f) - epoch) < 0) {
+          if (++polls > kMaxPolls) {
+            atomicExch(err, 206);
+            break;
+          }
+          if (polls > 64) __nanosleep(256);
+        }
+      }
+    }
+  }
 }
 
 __global__ void adamw_ag_kernel(Peers P, int rank, int world, unsigned epoch, int64_t shard_off, int64_t shard_len,
@@ -219,10 +243,12 @@ int symm_allreduce_bf16(void* const* bufs, unsigned* const* flags, int rank, int
 
 int symm_rs_sumsq(void* const* bufs, unsigned* const* flags, int rank, int world, unsigned epoch, int64_t shard_off,
                   int64_t shard_len, float scale, float* shard_out, float* partial, int nblocks, int accumulate,
-                  int* err, cudaStream_t s) {
+                  int* err, unsigned* done, int close_slot, cudaStream_t s) {
   if (world > symm::MAXR || shard_len % 4) return -1;
+  if (close_slot >= 0 && done == nullptr) return -2;
   symm::rs_sumsq_kernel<<<nblocks, 256, 0, s>>>(make_peers(bufs, flags, world), rank, world, epoch, shard_off,
-                                                shard_len, scale, shard_out, partial, accumulate, err);
+                                                shard_len, scale, shard_out, partial, accumulate, err, done,
+                                                close_slot);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 

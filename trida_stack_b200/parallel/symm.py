@@ -11,7 +11,8 @@ import torch.distributed as dist
 
 from ..ops._ext import ext
 
-NSLOTS = 4          # barrier slots: all-reduce, reduce-scatter, AdamW close, norm
+NSLOTS = 5          # barrier slots: all-reduce, reduce-scatter, AdamW close, norm, streamed reduce-scatter close
+RING_CLOSE_SLOT = 4
 MAXR = 8
 
 

@@ -18,6 +18,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops._ext import ext
+from .symm import RING_CLOSE_SLOT
 
 ALIGN = 64
 
@@ -98,9 +99,14 @@ class FlatGroup:
 class GradRing:
     """Two fp32 gradient slots shared by the streamed groups (one decoder layer each).  A group's
     slot is bound to its parameters' ``main_grad`` by the first weight gradient its backward
-    writes, and reduce-scattered into the group's fp32 shard (then freed) when a third group needs
-    a slot or the step's reduction runs -- full-size fp32 gradients exist for at most two layers,
-    and the reduction of one layer overlaps the backward of the next."""
+    writes.  Backward runs the layers one after another, so when the next group binds a slot the
+    previous group's gradients are complete: its reduce-scatter into the fp32 shard is issued then,
+    on a side stream with a quarter of the SMs' worth of CTAs, and runs under the next layer's
+    backward.  A slot is zeroed for reuse only after the event of the reduction that last read it
+    (whose closing barrier guarantees every rank has finished reading it).  Full-size fp32
+    gradients exist for at most two layers."""
+
+    RS_BLOCKS = 64
 
     def __init__(self, opt, size, device):
         self.opt = opt
@@ -113,16 +119,21 @@ class GradRing:
                 self.slots.append((torch.zeros(size, dtype=torch.float32, device=device), None))
         self.free = [0, 1]
         self.held = {}
-        self.partial = torch.zeros(ShardedAdamW.NB, dtype=torch.float32, device=device)
+        self.ready = [None, None]
+        cuda = torch.device(device).type == "cuda"
+        self.comm = torch.cuda.Stream(device=device) if (cuda and opt.world > 1) else None
+        self.partial = torch.zeros(self.RS_BLOCKS, dtype=torch.float32, device=device)
+        self.done = torch.zeros(1, dtype=torch.int32, device=device) if cuda else None
 
     def acquire(self, gi):
         if gi in self.held:
             return
-        if not self.free:
-            # backward runs the layers one after another, so the group that took its slot first
-            # has finished: reduce it now and reuse its slot
-            self.release(next(iter(self.held)))
+        for other in list(self.held):          # the previous layer's backward has finished
+            self.release(other)
         si = self.free.pop(0)
+        if self.ready[si] is not None:
+            torch.cuda.current_stream().wait_event(self.ready[si])
+            self.ready[si] = None
         g = self.opt.groups[gi]
         buf = self.slots[si][0][:g.padded]
         buf.zero_()
@@ -136,12 +147,27 @@ class GradRing:
         o = self.opt
         g = o.groups[gi]
         local, sym = self.slots[si]
+        if self.comm is not None:
+            self.comm.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(self.comm):
+                self._reduce(g, local, sym)
+                ev = torch.cuda.Event()
+                ev.record(self.comm)
+            self.ready[si] = ev
+        else:
+            self._reduce(g, local, sym)
+        g.unbind_grads()
+        self.free.append(si)
+
+    def _reduce(self, g, local, sym):
+        o = self.opt
         if o.world == 1:
             g.grad_shard.add_(local[:g.padded])
         elif o.fused:
             h = o.heap
             ext().symm_rs_sumsq(sym.ptrs, h.flags.ptrs, h.rank, h.next_epoch(1), g.lo, g.shard, 1.0 / o.world,
-                                g.grad_shard, self.partial, h.err, accumulate=True)
+                                g.grad_shard, self.partial, h.err, accumulate=True, done=self.done,
+                                close_slot=RING_CLOSE_SLOT)
         else:
             tmp = torch.empty(g.shard, dtype=torch.float32, device=local.device)
             avg = dist.get_backend(o.pg) == "nccl"
@@ -150,12 +176,12 @@ class GradRing:
             if not avg:
                 tmp.div_(o.world)
             g.grad_shard.add_(tmp)
-        g.unbind_grads()
-        self.free.append(si)
 
     def flush(self):
         for gi in list(self.held):
             self.release(gi)
+        if self.comm is not None:
+            torch.cuda.current_stream().wait_stream(self.comm)
 
 
 class LayerGradStream:
