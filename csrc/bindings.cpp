@@ -524,16 +524,20 @@ void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
                      dx.stride(0), pdw, M, D, sm_count(), stream());
 }
 
-at::Tensor qk_norm_rope_fwd(const at::Tensor& qkv, const at::Tensor& qw, const at::Tensor& kw,
-                            const at::Tensor& cos_t, const at::Tensor& sin_t, const at::Tensor& pos,
-                            const at::Tensor& q, const at::Tensor& k, int64_t Hq, int64_t Hkv, int64_t d,
-                            int64_t rd, double eps, int64_t qstride) {
+// qw / kw None: RoPE without the per-head RMSNorm
+at::Tensor qk_norm_rope_fwd(const at::Tensor& qkv, const c10::optional<at::Tensor>& qw,
+                            const c10::optional<at::Tensor>& kw, const at::Tensor& cos_t, const at::Tensor& sin_t,
+                            const at::Tensor& pos, const at::Tensor& q, const at::Tensor& k, int64_t Hq, int64_t Hkv,
+                            int64_t d, int64_t rd, double eps, int64_t qstride) {
   CHECK_BF16(qkv); CHECK_ROWMAJOR(qkv); CHECK_F32(cos_t); CHECK_F32(sin_t);
   TORCH_CHECK(pos.scalar_type() == at::kInt && pos.is_contiguous(), "pos must be contiguous int32");
   TORCH_CHECK(q.is_contiguous() && k.is_contiguous(), "q/k outputs must be contiguous");
+  const bool has_q = qw.has_value() && qw->defined(), has_k = kw.has_value() && kw->defined();
+  TORCH_CHECK(has_q == has_k, "q and k norm weights must both be given or both be None");
   const int M = qkv.size(0);
   auto rstd = at::empty({M, Hq + Hkv}, qkv.options().dtype(at::kFloat));
-  trida::qk_norm_rope_fwd(cbf(qkv), qkv.stride(0), cbf(qw), cbf(kw), cos_t.data_ptr<float>(),
+  trida::qk_norm_rope_fwd(cbf(qkv), qkv.stride(0), has_q ? cbf(*qw) : nullptr, has_k ? cbf(*kw) : nullptr,
+                          cos_t.data_ptr<float>(),
                           sin_t.data_ptr<float>(), pos.data_ptr<int>(), mbf(q), mbf(k), rstd.data_ptr<float>(), M,
                           Hq, Hkv, d, rd, (float)eps, qstride ? qstride : d, stream());
   return rstd;

@@ -136,27 +136,33 @@ __global__ void qk_norm_rope_fwd_kernel(const bf16* __restrict__ qkv, int64_t ld
   const bf16* src = qkv + (int64_t)tok * ldqkv + hcol;
   const bf16* w = is_q ? qw : kw;
   bf16* dst = is_q ? (q + ((int64_t)tok * Hq + h) * d) : (k + ((int64_t)tok * Hkv + (h - Hq)) * d);
-  float ss = 0.f;
-  for (int c = lane; c < d; c += 32) {
-    const float v = __bfloat162float(src[c]);
-    ss += v * v;
+  // null norm weights: RoPE only (models without per-head q / k RMSNorm)
+  float r = 1.f;
+  if (w != nullptr) {
+    float ss = 0.f;
+    for (int c = lane; c < d; c += 32) {
+      const float v = __bfloat162float(src[c]);
+      ss += v * v;
+    }
+    ss = warp_sum(ss);
+    r = rsqrtf(ss / (float)d + eps);
   }
-  ss = warp_sum(ss);
-  const float r = rsqrtf(ss / (float)d + eps);
   if (lane == 0) rstd[gw] = r;
   const int half = rd >> 1;
   const int p = pos[tok];
   const float* ct = cos_t + (int64_t)p * half;
   const float* st = sin_t + (int64_t)p * half;
   for (int i = lane; i < half; i += 32) {
-    const float x1 = __bfloat162float(src[i]) * r * __bfloat162float(w[i]);
-    const float x2 = __bfloat162float(src[i + half]) * r * __bfloat162float(w[i + half]);
+    const float w1 = w != nullptr ? __bfloat162float(w[i]) : 1.f;
+    const float w2 = w != nullptr ? __bfloat162float(w[i + half]) : 1.f;
+    const float x1 = __bfloat162float(src[i]) * r * w1;
+    const float x2 = __bfloat162float(src[i + half]) * r * w2;
     const float c = ct[i], s = st[i];
     dst[i] = __float2bfloat16(x1 * c - x2 * s);
     dst[i + half] = __float2bfloat16(x2 * c + x1 * s);
   }
   for (int i = rd + lane; i < d; i += 32)
-    dst[i] = __float2bfloat16(__bfloat162float(src[i]) * r * __bfloat162float(w[i]));
+    dst[i] = __float2bfloat16(__bfloat162float(src[i]) * r * (w != nullptr ? __bfloat162float(w[i]) : 1.f));
 }
 
 // Backward: dy (grad of the roped output) -> d(normalised) by the inverse rotation, then the

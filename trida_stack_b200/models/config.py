@@ -34,6 +34,12 @@ class ModelConfig:
     vision: dict = None
     image_token_id: int = 248056
     mrope_section: tuple = (11, 11, 10)
+    # 3-D RoPE frequency layout: "interleaved" t,h,w,t,h,w,... (Qwen3.5) or "chunked" t..t h..h w..w (GLM)
+    mrope_layout: str = "interleaved"
+    # GLM-style layers: no per-head q / k RMSNorm; RMSNorm on the attention and MLP outputs before
+    # each residual add
+    qk_norm: bool = True
+    post_norms: bool = False
     # raw HF dict (written back on save so the checkpoint stays loadable by transformers)
     hf: dict = field(default_factory=dict, repr=False)
 

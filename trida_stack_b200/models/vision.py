@@ -245,11 +245,20 @@ def mrope_axis(half, section):
     return ax
 
 
-def mrope_angles(pos3, rotary_dim, theta, section):
+def mrope_axis_chunked(half, section):
+    """Chunked layout (GLM): the first ``section[0]`` frequencies read t, the next ``section[1]`` h,
+    the rest w."""
+    ax = torch.full((half,), 2, dtype=torch.long)
+    ax[:section[0]] = 0
+    ax[section[0]:section[0] + section[1]] = 1
+    return ax
+
+
+def mrope_angles(pos3, rotary_dim, theta, section, layout="interleaved"):
     """Rotary angles [B, T, rotary_dim / 2] for 3-D positions ``pos3`` [B, 3, T]; a token whose three
     positions agree gets exactly the 1-D RoPE angles."""
     half = rotary_dim // 2
     inv = 1.0 / (theta ** (torch.arange(0, rotary_dim, 2, dtype=torch.float32, device=pos3.device) / rotary_dim))
-    ax = mrope_axis(half, section).to(pos3.device)
+    ax = (mrope_axis_chunked if layout == "chunked" else mrope_axis)(half, section).to(pos3.device)
     p = pos3.float().permute(0, 2, 1)                                          # [B, T, 3]
     return torch.gather(p, 2, ax[None, None].expand(p.shape[0], p.shape[1], -1)) * inv

@@ -54,6 +54,9 @@ class Runtime:
                                           dtype=torch.float32, device=self.device)
                 self.win[i] = torch.zeros(nslot, cfg.conv_kernel - 1, Cc, dtype=self.dtype, device=self.device)
         self.pos = [0] * max_slots
+        # RoPE position = cache index + delta (3-D RoPE prompts advance positions more slowly than
+        # cache rows; an optional offset shifts every generated token)
+        self.rope_delta = [0] * max_slots
         self.free = list(range(max_slots))[::-1]
         self.pending = None
         self._graphs = None
@@ -61,7 +64,7 @@ class Runtime:
             from ..ops import blocks
             from ..ops._ext import ext
             self.C = ext()
-            self.cos_t, self.sin_t = blocks.rope_tables(max_len, cfg.rotary_dim, cfg.rope_theta, self.device)
+            self.cos_t, self.sin_t = blocks.rope_tables(max_len + 64, cfg.rotary_dim, cfg.rope_theta, self.device)
             self.blocks = blocks
             self._gdn_f32 = {i: (decoder.layers[i].A_log.float().contiguous(),
                                  decoder.layers[i].dt_bias.float().contiguous()) for i in self.ssm}
@@ -72,6 +75,7 @@ class Runtime:
             raise RuntimeError("no free cache slot")
         s = self.free.pop()
         self.pos[s] = 0
+        self.rope_delta[s] = 0
         for i in self.ssm:
             self.ssm[i][s].zero_()
             self.win[i][s].zero_()
@@ -83,19 +87,43 @@ class Runtime:
 
     # ------------------------------------------------------------------ public steps
     @torch.no_grad()
-    def prefill(self, slots, prompts):
-        """Feed equal-length prompts into fresh slots; returns fp32 logits of each last token [B, V]."""
+    def prefill(self, slots, prompts, vis=None, pos_offset=0):
+        """Feed equal-length prompts into fresh slots; returns fp32 logits of each last token [B, V].
+
+        ``vis`` (vision-language prompts): per slot ``None`` or ``(features [n_img, D], pos3 [3, L])``
+        -- the image features replace the embeddings of the prompt's image tokens in order and the
+        prompt rows use 3-D RoPE; later tokens continue from the prompt's largest position + 1
+        (+ ``pos_offset``)."""
         L = len(prompts[0])
         assert all(len(p) == L for p in prompts) and L >= 1
         ids = torch.tensor(prompts, dtype=torch.long, device=self.device)
+        ang = inject = None
+        if vis is not None and any(v is not None for v in vis):
+            pos3 = torch.stack([v[1] if v is not None else torch.arange(L).expand(3, -1) for v in vis]).to(self.device)
+            ang = self.dec.rope_angles(pos3) if hasattr(self.dec, "rope_angles") else None
+            img = ids == self.cfg.image_token_id
+            feats = torch.cat([v[0] for v in vis if v is not None]).to(self.device, self.dtype)
+            if int(img.sum()) != feats.shape[0]:
+                raise ValueError(f"{int(img.sum())} image tokens but {feats.shape[0]} image features")
+            fidx = torch.full(ids.shape, -1, dtype=torch.long, device=self.device)
+            fidx[img] = torch.arange(feats.shape[0], device=self.device)
+            inject = (fidx, feats)
+            for b, s in enumerate(slots):
+                self.rope_delta[s] = int(pos3[b].max()) + 1 - L
         out = None
         for c0 in range(0, L, PREFILL_CHUNK):
             n = min(PREFILL_CHUNK, L - c0)
             last = c0 + n == L
-            logits = self.canvas(slots, ids[:, c0:c0 + n], n, rows=(n - 1, n) if last else (0, 0))
+            extra = {}
+            if inject is not None:
+                extra = {"inject": (inject[0][:, c0:c0 + n], inject[1]),
+                         "rope_ang": ang[:, c0:c0 + n] if ang is not None else None}
+            logits = self.canvas(slots, ids[:, c0:c0 + n], n, rows=(n - 1, n) if last else (0, 0), **extra)
             self.commit(slots, [n] * len(slots))
             if last:
                 out = logits[:, 0]
+        for s in slots:
+            self.rope_delta[s] += pos_offset
         return out
 
     def use_graphs(self, buckets=(1, 2, 4, 8, 16, 32, 64, 128)):
@@ -108,7 +136,7 @@ class Runtime:
         self._graphs = {}
 
     @torch.no_grad()
-    def canvas(self, slots, tokens, n_clean, rows=None):
+    def canvas(self, slots, tokens, n_clean, rows=None, inject=None, rope_ang=None):
         """One forward over a [B, blk] canvas per slot.  Returns fp32 logits [B, r1 - r0, V] for the
         canvas rows ``rows = (r0, r1)`` (all rows by default).  Call ``commit`` afterwards.  With
         graphs on, the returned tensor is a static buffer valid until the next canvas."""
@@ -119,10 +147,11 @@ class Runtime:
             if self.pos[s] + blk > self.max_len:
                 raise RuntimeError(f"slot {s}: sequence exceeds the cache length {self.max_len}")
         r0, r1 = rows if rows is not None else (0, blk)
-        if self._graphs is not None and (r0, r1) == (0, blk):
+        if self._graphs is not None and (r0, r1) == (0, blk) and inject is None and rope_ang is None:
             return self._canvas_graph(slots, tokens, n_clean)
         tokens = torch.as_tensor(tokens, dtype=torch.long, device=self.device)
         st = _Step(self, slots, B, blk, n_clean)
+        st.inject, st.rope_ang = inject, rope_ang
         x = self._forward(st, tokens)
         self.pending = st
         if r1 <= r0:
@@ -178,6 +207,12 @@ class Runtime:
 
     def _forward(self, st, tokens):
         x = self.dec.embed_tokens(tokens.reshape(-1)) if self.cuda else self.dec.embed[tokens.reshape(-1)]
+        if getattr(st, "inject", None) is not None:
+            fidx, feats = st.inject
+            sel = fidx.reshape(-1) >= 0
+            if bool(sel.any()):
+                x = x.clone()
+                x[sel] = feats[fidx.reshape(-1)[sel]].to(x.dtype)
         for i, layer in enumerate(self.dec.layers):
             if self.kinds[i] == "full_attention":
                 x = self._attn(st, i, layer, x)
@@ -199,7 +234,8 @@ class Runtime:
         g.host_slot[:] = torch.tensor(list(slots) + [self.dummy] * pad, dtype=torch.int32)
         pos = [self.pos[s] for s in slots] + [0] * pad
         g.host_pos[:] = torch.tensor(pos, dtype=torch.int32)
-        g.host_rowpos[:] = (g.host_pos[:, None] + torch.arange(blk, dtype=torch.int32)[None]).reshape(-1)
+        rp = torch.tensor([self.pos[s] + self.rope_delta[s] for s in slots] + [0] * pad, dtype=torch.int32)
+        g.host_rowpos[:] = (rp[:, None] + torch.arange(blk, dtype=torch.int32)[None]).reshape(-1)
         g.st.tokens.copy_(g.host_tok, non_blocking=True)
         g.st.slot_t.copy_(g.host_slot, non_blocking=True)
         g.st.pos_t.copy_(g.host_pos, non_blocking=True)
@@ -283,7 +319,16 @@ class Runtime:
             self.C.swiglu_fwd(gu, a)
         else:
             a = R.swiglu(gu)
-        return self._lin(a, layer.wdown, x)
+        return self._out(a, layer.wdown, x, getattr(layer, "post_mlp_norm", None))
+
+    def _out(self, a, w, x, post_norm):
+        """Sub-block output: ``x + a w^T`` (residual fused into the GEMM epilogue), or GLM's
+        ``x + RMSNorm(a w^T)`` when the layer normalises its outputs."""
+        if post_norm is None:
+            return self._lin(a, w, x)
+        if self.tp is not None:
+            raise NotImplementedError("tensor parallelism for layers with output norms")
+        return x + self._rms(self._lin(a, w), post_norm)
 
     def _logits(self, h):
         h = self._rms(h, self.dec.norm)
@@ -302,10 +347,16 @@ class Runtime:
         h = self._rms(x, layer.input_norm)
         qkv = self._lin(h, layer.wqkv)
         M = B * blk
+        ang = getattr(st, "rope_ang", None)
         if self.cuda:
             q = torch.empty(M, Hq, d, dtype=x.dtype, device=x.device)
             k = torch.empty(M, Hkv, d, dtype=x.dtype, device=x.device)
-            self.C.qk_norm_rope_fwd(qkv, layer.q_norm, layer.k_norm, self.cos_t, self.sin_t, st.rowpos32, q, k,
+            cos_t, sin_t, rp = self.cos_t, self.sin_t, st.rowpos32
+            if ang is not None:                      # per-row tables (3-D RoPE prompt rows)
+                fa = ang.reshape(M, -1).float()
+                cos_t, sin_t = fa.cos().contiguous(), fa.sin().contiguous()
+                rp = torch.arange(M, dtype=torch.int32, device=x.device)
+            self.C.qk_norm_rope_fwd(qkv, layer.q_norm, layer.k_norm, cos_t, sin_t, rp, q, k,
                                     Hq, Hkv, d, cfg.rotary_dim, cfg.eps, qs)
             v = qkv[:, Hq * qs + Hkv * d:]
             self.C.kv_append(k, v, self.kc[i], self.vc[i], st.slot_t, st.pos_t, blk)
@@ -317,7 +368,7 @@ class Runtime:
                 og = torch.empty_like(o)
                 self.C.attn_gate_fwd(o, qkv, og, Hq, d)
                 o = og
-            return self._lin(o, layer.wo, x)
+            return self._out(o, layer.wo, x, getattr(layer, "post_attn_norm", None))
         # CPU statement
         if cfg.attn_output_gate:
             qg = qkv[:, :2 * Hq * d].view(M, Hq, 2 * d)
@@ -326,9 +377,14 @@ class Runtime:
             q, gate = qkv[:, :Hq * d].view(M, Hq, d), None
         k = qkv[:, Hq * qs:Hq * qs + Hkv * d].view(M, Hkv, d)
         v = qkv[:, Hq * qs + Hkv * d:].view(M, Hkv, d)
-        q = R.rmsnorm(q, layer.q_norm, cfg.eps)
-        k = R.rmsnorm(k, layer.k_norm, cfg.eps)
-        cos, sin = R.rope_cos_sin(st.rowpos, d, cfg.rope_theta, cfg.rotary_dim)
+        if layer.q_norm is not None:
+            q = R.rmsnorm(q, layer.q_norm, cfg.eps)
+            k = R.rmsnorm(k, layer.k_norm, cfg.eps)
+        if ang is not None:
+            a2 = torch.cat([ang, ang], -1).reshape(M, -1)
+            cos, sin = a2.cos(), a2.sin()
+        else:
+            cos, sin = R.rope_cos_sin(st.rowpos, d, cfg.rope_theta, cfg.rotary_dim)
         q = R.apply_rope(q.float()[None], cos[None], sin[None])[0].to(x.dtype)
         k = R.apply_rope(k.float()[None], cos[None], sin[None])[0].to(x.dtype)
         q, k, v = q.view(B, blk, Hq, d), k.view(B, blk, Hkv, d), v.view(B, blk, Hkv, d)
@@ -350,7 +406,7 @@ class Runtime:
         o = torch.stack(outs).reshape(M, Hq * d).to(x.dtype)
         if gate is not None:
             o = o * torch.sigmoid(gate.float()).to(o.dtype)
-        return self._lin(o, layer.wo, x)
+        return self._out(o, layer.wo, x, getattr(layer, "post_attn_norm", None))
 
     def _gdn(self, st, i, layer, x):
         cfg = self.cfg
@@ -423,7 +479,8 @@ class _Step:
             return
         pos = [rt.pos[s] for s in self.slots]
         self.max_keys = max(pos) + blk
-        self.rowpos = torch.tensor([p + j for p in pos for j in range(blk)], dtype=torch.long)
+        self.rowpos = torch.tensor([p + rt.rope_delta[s] + j for p, s in zip(pos, self.slots) for j in range(blk)],
+                                   dtype=torch.long)
         if rt.cuda:
             dev = rt.device
             self.slot_t = torch.tensor(self.slots, dtype=torch.int32, device=dev)
