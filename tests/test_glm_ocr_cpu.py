@@ -79,3 +79,24 @@ def test_runtime_image_prefill_and_decode_match_statement():
         full = dec.forward_ref(ids2, mrope_position_ids(ids2, grid, IMG), feats)
     torch.testing.assert_close(last[0], full[len(ids) - 1], rtol=1e-4, atol=1e-4)
     torch.testing.assert_close(lg[0], full[len(ids):], rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("pos_offset", [0, 1])
+def test_ocr_self_spec_equals_causal_with_images(pos_offset):
+    """An image request decoded by draft / verify rounds gives the causal decoder's greedy tokens
+    (same RoPE layout on both sides, including GravityOCR's one-position offset)."""
+    from trida_stack_b200.serve import Engine, Request, SamplingParams
+    hf, cfg = tiny_hf()
+    dec = native(hf, cfg)
+    torch.manual_seed(4)
+    ids, grid, px = _sample()
+    outs = []
+    for mode in ("causal", "draft-verify"):
+        eng = Engine(Runtime(dec, max_slots=2, max_len=128), mask_id=299, mode=mode, block_size=6,
+                     pos_offset=pos_offset)
+        r = eng.submit(Request(ids.tolist(), 20, SamplingParams()))
+        r.images = (px, grid)
+        while not r.done:
+            eng.step()
+        outs.append(r.output)
+    assert outs[0] == outs[1] and len(outs[0]) == 20

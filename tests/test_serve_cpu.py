@@ -258,3 +258,27 @@ def test_lockstep_driver_keeps_ranks_identical():
     for p in procs:
         p.join(timeout=60)
     assert res[0] == res[1] and len(res[0]) == 5 and all(len(o) > 0 for o in res[0])
+
+
+@pytest.mark.parametrize("make", [tiny_hybrid, tiny_dense])
+def test_greedy_draft_verify_equals_autoregressive(make):
+    """GravityOCR-style fresh-window self-speculation (draft [seed, MASK x B], causal verify) commits
+    exactly the greedy autoregressive tokens."""
+    dec = make()
+    torch.manual_seed(3)
+    prompts = [torch.randint(0, 96, (L,)).tolist() for L in (9, 9, 14)]
+    ar = Engine(Runtime(dec, max_slots=4, max_len=256), mask_id=96, mode="causal")
+    ref = [r.output for r in ar.generate(prompts, max_new_tokens=30)]
+    dv = Engine(Runtime(dec, max_slots=4, max_len=256), mask_id=96, mode="draft-verify", block_size=4)
+    reqs = dv.generate(prompts, max_new_tokens=30)
+    assert [r.output for r in reqs] == ref
+    assert all(r.forwards > 0 for r in reqs)
+
+
+def test_sampled_draft_verify_runs_and_respects_eos():
+    dec = tiny_dense()
+    eng = Engine(Runtime(dec, max_slots=4, max_len=256), mask_id=96, mode="draft-verify", block_size=4)
+    sp = SamplingParams(temperature=1.0, top_k=10, top_p=0.9, seed=5)
+    reqs = eng.generate([[1, 2, 3, 4, 5]] * 2, max_new_tokens=25, sampling=sp, eos=(7,))
+    for r in reqs:
+        assert r.finish_reason in ("stop", "length") and 7 not in r.output

@@ -19,6 +19,15 @@ corrected from ``norm(max(0, p - q))``.
 
 ``mode="causal"`` decodes one token per forward (a one-row canvas).
 
+``mode="draft-verify"`` is GravityOCR's self-speculation (``inference/gravityocr/sglang/python/sglang/
+srt/speculative/selfspec_diffusion_worker.py``: the "fresh-window" draft): every round runs a draft
+forward over ``[seed, MASK x B]`` (row 0 token-causal, the masks see the whole window; draft i+1 =
+read-out of row i) and a causal verify forward over ``[seed, draft_1..draft_B]``; the longest
+prefix of drafts equal to the verifier's choices is kept, plus the verifier's token after it as the
+next seed (greedy; with sampling a draft is kept with the probability the verifier gives it and the
+first rejection is redrawn from the verifier's distribution without the rejected token).  The
+prompt may carry images (``Request.images``), encoded by the model's vision tower at admission.
+
 ``mode="diffusion"`` is pure block-diffusion decoding with the LowConfidenceShift gate (the
 reference's SGLang ``LowConfidenceShiftHybridDiffusion`` and vLLM ``_denoise_shift_step``,
 ``inference/zoro-1/vllm/vllm_native_diffusion/qwen3_5_diffusion.py:449-632``): a block canvas
@@ -74,6 +83,7 @@ class Request:
     t0_emitted: bool = False
     pending: Optional[int] = None
     canvas: Optional[List[int]] = None        # diffusion mode: the block being denoised
+    images: Optional[tuple] = None            # (pixel_values, image_grid_thw) of the prompt's images
     rounds: int = 0
     specs: Optional[List[int]] = None
     spec_q: Optional[torch.Tensor] = None
@@ -108,15 +118,16 @@ class Engine:
 
     def __init__(self, runtime: Runtime, mask_id: int, mode: str = "self-spec", n: int = 4,
                  max_running: Optional[int] = None, graphs: bool = False, block_size: int = 8,
-                 threshold: float = 0.9, max_steps: Optional[int] = None):
-        assert mode in ("self-spec", "causal", "diffusion")
+                 threshold: float = 0.9, max_steps: Optional[int] = None, pos_offset: int = 0):
+        assert mode in ("self-spec", "causal", "diffusion", "draft-verify")
         self.rt = runtime
         if graphs and runtime.cuda:
             runtime.use_graphs()
         self.mask_id = mask_id
         self.mode = mode
         self.n = n if mode == "self-spec" else 1
-        self.blk = 2 * self.n - 1 if mode != "diffusion" else block_size
+        self.blk = {"diffusion": block_size, "draft-verify": block_size + 1}.get(mode, 2 * self.n - 1)
+        self.pos_offset = pos_offset     # RoPE shift of every generated token (GravityOCR's layout: 1)
         self.threshold = threshold
         self.max_steps = max_steps or max(block_size - 1, 1)
         self.max_running = min(max_running or runtime.max_slots, runtime.max_slots)
@@ -135,7 +146,7 @@ class Engine:
     def submit(self, req: Request) -> Request:
         req.rid = next(self._ids)
         req.t_submit = time.perf_counter()
-        req.accept_hist = [0] * self.n
+        req.accept_hist = [0] * (self.blk if self.mode == "draft-verify" else self.n)
         self._seed_request(req)
         (self.inbox if self.inbox is not None else self.waiting).put(req)
         return req
@@ -197,18 +208,36 @@ class Engine:
         new.sort(key=lambda r: len(r.prompt))
         for _, grp in itertools.groupby(new, key=lambda r: len(r.prompt)):
             grp = list(grp)
-            logits = self.rt.prefill([r.slot for r in grp], [r.prompt for r in grp])
+            vis = [self._vision(r) for r in grp]
+            logits = self.rt.prefill([r.slot for r in grp], [r.prompt for r in grp],
+                                     vis=vis if any(v is not None for v in vis) else None,
+                                     pos_offset=self.pos_offset)
             self.stats["prefill_tokens"] += sum(len(r.prompt) for r in grp)
             for b, r in enumerate(grp):
                 r.t0 = self._pick(logits[b:b + 1], r)[0]
                 r.t0_emitted = False
-                if self.mode in ("causal", "diffusion"):
+                if self.mode in ("causal", "diffusion", "draft-verify"):
                     self._emit(r, [r.t0])
                     r.t0_emitted = True
                 if self.mode == "diffusion":
                     r.canvas, r.rounds = [r.t0] + [self.mask_id] * (self.blk - 1), 0
             self.running.extend(grp)
         self._reap()
+
+    def _vision(self, r):
+        """(image features, 3-D positions) of a request with images, else None."""
+        if r.images is None:
+            return None
+        from ..data.images import mrope_position_ids
+        vis_model = self.rt.dec.visual
+        if vis_model is None:
+            raise ValueError("the model has no vision tower")
+        pv, grid = r.images
+        p = next(vis_model.parameters())
+        with torch.no_grad():
+            feats = vis_model(pv.to(p.device), grid)
+        merge = getattr(vis_model, "c").spatial_merge_size
+        return feats, mrope_position_ids(torch.tensor(r.prompt), grid, self.rt.cfg.image_token_id, merge)
 
     def _pick(self, logits, req):
         if req.sampling.greedy:
@@ -251,6 +280,8 @@ class Engine:
     def _decode(self):
         if self.mode == "diffusion":
             return self._decode_diffusion()
+        if self.mode == "draft-verify":
+            return self._decode_draft_verify()
         reqs = self.running
         slots = [r.slot for r in reqs]
         n, blk, K = self.n, self.blk, self.n - 1
@@ -350,6 +381,57 @@ class Engine:
                 self._emit(r, r.canvas[1:] + [seeds[b]])
                 r.canvas, r.rounds = [seeds[b]] + [M] * (Bk - 1), 0
         self._reap()
+
+    def _decode_draft_verify(self):
+        reqs = self.running
+        slots = [r.slot for r in reqs]
+        K, M = self.blk, self.mask_id
+        # draft: a fresh window [seed, MASK x (K-1)], read out shifted (row i proposes token i+1)
+        lg = self.rt.canvas(slots, [[r.t0] + [M] * (K - 1) for r in reqs], 1)
+        drafts = self.rt.argmax(lg)[:, :K - 1].tolist()
+        self.rt.discard()
+        # verify: the causal path over [seed, drafts]
+        lg = self.rt.canvas(slots, [[r.t0] + drafts[b] for b, r in enumerate(reqs)], K)
+        greedy = all(r.sampling.greedy for r in reqs)
+        am = self.rt.argmax(lg).tolist() if greedy else None
+        self.stats["forwards"] += 2
+        adv, outs = [], []
+        for b, r in enumerate(reqs):
+            r.forwards += 2
+            d = drafts[b]
+            if r.sampling.greedy:
+                p = am[b] if greedy else lg[b].argmax(-1).tolist()
+                acc = 0
+                while acc < K - 1 and d[acc] == p[acc]:
+                    acc += 1
+                bonus = p[acc]
+            else:
+                acc, bonus = self._verify_sampled(r, lg[b], d)
+            r.accept_hist[min(acc, len(r.accept_hist) - 1)] += 1
+            adv.append(1 + acc)
+            outs.append(d[:acc] + [bonus])
+        self.rt.commit(slots, adv)
+        for b, r in enumerate(reqs):
+            self._emit(r, outs[b])
+            r.t0 = outs[b][-1]
+        self._reap()
+
+    def _verify_sampled(self, r, L, d):
+        """Speculative sampling against a deterministic draft: keep draft j with probability p_j(d_j);
+        at the first rejection draw from p_j with d_j removed; after a full block draw the bonus."""
+        P = truncated_probs(L, r.sampling)                     # [K, V]
+        K1 = len(d)
+        for j in range(K1):
+            pj = float(P[j, d[j]])
+            u = float(torch.rand((), device=L.device, generator=r.gen))
+            if u < pj:
+                continue
+            resid = P[j].clone()
+            resid[d[j]] = 0.0
+            z = resid.sum()
+            resid = resid / z if z > 0 else P[j]
+            return j, int(torch.multinomial(resid, 1, generator=r.gen))
+        return K1, int(torch.multinomial(P[K1], 1, generator=r.gen))
 
     def _sample_rows(self, L, r):
         """Sampled denoise read-out: a token per row from the truncated distribution and its probability."""
