@@ -100,3 +100,95 @@ def test_ocr_self_spec_equals_causal_with_images(pos_offset):
             eng.step()
         outs.append(r.output)
     assert outs[0] == outs[1] and len(outs[0]) == 20
+
+
+def test_glm_image_processor_matches_transformers():
+    import numpy as np
+    from PIL import Image
+
+    from trida_stack_b200.data.images import ImageProcessor
+    try:
+        from transformers.models.glm4v.image_processing_pil_glm4v import Glm4vImageProcessorPil
+    except ImportError:
+        pytest.skip("transformers GLM-V PIL image processor not available")
+    size = {"shortest_edge": 12544, "longest_edge": 28 * 28 * 2 * 600}
+    hf = Glm4vImageProcessorPil(size=size, patch_size=14, temporal_patch_size=2, merge_size=2)
+    ours = ImageProcessor(patch_size=14, temporal_patch_size=2, merge_size=2, min_pixels=size["shortest_edge"],
+                          max_pixels=size["longest_edge"], image_mean=hf.image_mean, image_std=hf.image_std,
+                          glm=True)
+    rng = np.random.default_rng(0)
+    imgs = [Image.fromarray(rng.integers(0, 255, (h, w, 3), dtype=np.uint8))
+            for h, w in ((100, 70), (300, 900), (20, 64), (64, 128))]
+    ref = hf(images=imgs, return_tensors="pt")
+    pv, grid = ours(imgs)
+    assert torch.equal(grid, ref["image_grid_thw"].long())
+    torch.testing.assert_close(pv, ref["pixel_values"].float(), rtol=1e-5, atol=1e-5)
+
+
+def _ckpt(tmp_path):
+    """A tiny GravityOCR-layout checkpoint: config, weights, tokenizer, processor, block_diffusion.json."""
+    import json as _json
+
+    from helpers import make_tokenizer
+    hf, cfg = tiny_hf()
+    hf.save_pretrained(str(tmp_path))
+    make_tokenizer(str(tmp_path), 300)
+    _json.dump({"image_processor": {"image_processor_type": "Glm46VImageProcessor", "patch_size": 4,
+                                    "temporal_patch_size": 2, "merge_size": 2,
+                                    "size": {"shortest_edge": 64, "longest_edge": 2 * 24 * 24},
+                                    "image_mean": [0.5, 0.5, 0.5], "image_std": [0.5, 0.5, 0.5]}},
+               open(tmp_path / "processor_config.json", "w"))
+    _json.dump({"bd_size": 5, "mask_id": 298, "ar_loss_weight": 1.0}, open(tmp_path / "block_diffusion.json", "w"))
+    return str(tmp_path)
+
+
+def test_ocr_server_self_spec_and_security(tmp_path, monkeypatch):
+    import threading
+    import time
+
+    import requests
+    import uvicorn
+
+    import ocr_request
+    import serve_gravityocr as S
+    from trida_stack_b200.serve.ocr import build_ocr_app
+    path = _ckpt(tmp_path)
+    outs = {}
+    for mode in ("causal", "self-spec"):
+        args = S.parse_args([path, "--mode", mode, "--device", "cpu", "--dtype", "float32", "--max-running", "2",
+                             "--context", "256", "--pos-offset", "0"])
+        engine, tok, proc, eos = S.build(args)
+        assert proc.glm and proc.patch_size == 4
+        engine.start()
+        import socket
+        sk = socket.socket()
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+        sk.close()
+        srv = uvicorn.Server(uvicorn.Config(build_ocr_app(engine, tok, proc, api_key="k3y", context=256, eos=()),
+                                            host="127.0.0.1", port=port, log_level="error"))
+        threading.Thread(target=srv.run, daemon=True).start()
+        url = f"http://127.0.0.1:{port}"
+        for _ in range(200):
+            try:
+                if requests.get(url + "/health", timeout=1).ok:
+                    break
+            except requests.ConnectionError:
+                time.sleep(0.05)
+        try:
+            png, mime = ocr_request.synthetic_png("t1 t2")
+            body = ocr_request.build_body(png, mime, "Text Recognition:", "glm-ocr", 12)
+            assert requests.post(url + "/v1/chat/completions", json=body).status_code == 401
+            r = ocr_request.send(body, url, 60, api_key="k3y")
+            assert r["usage"]["completion_tokens"] == 12 and r["choices"][0]["finish_reason"] == "length"
+            bad = dict(body)
+            bad["messages"] = [{"role": "user", "content": [{"type": "image_url",
+                                                             "image_url": {"url": "http://example.com/x.png"}}]}]
+            rb = requests.post(url + "/v1/chat/completions", json=bad, headers={"Authorization": "Bearer k3y"})
+            assert rb.status_code == 400
+            outs[mode] = (r["choices"][0]["message"]["content"], r["usage"]["forwards"])
+        finally:
+            srv.should_exit = True
+            engine.stop()
+    # self-speculation reproduces causal decoding (greedy, same RoPE layout) in fewer forwards
+    assert outs["self-spec"][0] == outs["causal"][0]

@@ -74,18 +74,24 @@ def load_image(ref, image_root=None):
     return img.convert("RGB")
 
 
-def fit_size(height, width, factor, min_pixels, max_pixels):
-    """(h, w) multiples of ``factor`` nearest the input, rescaled into ``[min_pixels, max_pixels]``."""
+def fit_size(height, width, factor, min_pixels, max_pixels, frames=1, upscale_small=False):
+    """(h, w) multiples of ``factor`` nearest the input, rescaled so ``frames * h * w`` lies in
+    ``[min_pixels, max_pixels]``.  GLM-style processors count the temporal frames in the pixel
+    budget (``frames`` = temporal patch size) and first scale up images with a side below
+    ``factor`` (``upscale_small``)."""
+    if upscale_small and (height < factor or width < factor):
+        sc = max(factor / height, factor / width)
+        height, width = int(height * sc), int(width * sc)
     if max(height, width) / min(height, width) > 200:
         raise ValueError(f"image aspect ratio {max(height, width) / min(height, width):.1f} exceeds 200")
     h = round(height / factor) * factor
     w = round(width / factor) * factor
-    if h * w > max_pixels:
-        s = math.sqrt(height * width / max_pixels)
+    if frames * h * w > max_pixels:
+        s = math.sqrt(frames * height * width / max_pixels)
         h = max(factor, math.floor(height / s / factor) * factor)
         w = max(factor, math.floor(width / s / factor) * factor)
-    elif h * w < min_pixels:
-        s = math.sqrt(min_pixels / (height * width))
+    elif frames * h * w < min_pixels:
+        s = math.sqrt(min_pixels / (frames * height * width))
         h = math.ceil(height * s / factor) * factor
         w = math.ceil(width * s / factor) * factor
     return h, w
@@ -96,31 +102,37 @@ class ImageProcessor:
 
     def __init__(self, patch_size=16, temporal_patch_size=2, merge_size=2, min_pixels=56 * 56,
                  max_pixels=28 * 28 * 1280, image_mean=(0.5, 0.5, 0.5), image_std=(0.5, 0.5, 0.5),
-                 rescale_factor=1.0 / 255, raw=None):
+                 rescale_factor=1.0 / 255, raw=None, glm=False):
         self.patch_size, self.temporal_patch_size, self.merge_size = patch_size, temporal_patch_size, merge_size
         self.min_pixels, self.max_pixels = min_pixels, max_pixels
         self.image_mean = np.asarray(image_mean, dtype=np.float32)
         self.image_std = np.asarray(image_std, dtype=np.float32)
         self.rescale_factor = rescale_factor
         self.raw = raw
+        self.glm = glm              # GLM-V resize rule (frames in the pixel budget, small images scaled up)
 
     @classmethod
-    def from_dict(cls, d):
+    def from_dict(cls, d, glm=None):
+        if isinstance(d.get("image_processor"), dict):      # processor_config.json nests it
+            d = d["image_processor"]
+        if glm is None:
+            glm = "glm" in str(d.get("image_processor_type", "")).lower()
         size = d.get("size") or {}
         return cls(patch_size=d.get("patch_size", 16), temporal_patch_size=d.get("temporal_patch_size", 2),
                    merge_size=d.get("merge_size", 2),
                    min_pixels=d.get("min_pixels") or size.get("shortest_edge") or 56 * 56,
                    max_pixels=d.get("max_pixels") or size.get("longest_edge") or 28 * 28 * 1280,
                    image_mean=d.get("image_mean", (0.5, 0.5, 0.5)), image_std=d.get("image_std", (0.5, 0.5, 0.5)),
-                   rescale_factor=d.get("rescale_factor", 1.0 / 255), raw=dict(d))
+                   rescale_factor=d.get("rescale_factor", 1.0 / 255), raw=dict(d), glm=glm)
 
     @classmethod
-    def from_pretrained(cls, path):
-        f = os.path.join(path, "preprocessor_config.json")
-        if not os.path.exists(f):
-            return None
-        with open(f) as fh:
-            return cls.from_dict(json.load(fh))
+    def from_pretrained(cls, path, glm=None):
+        for name in ("preprocessor_config.json", "processor_config.json"):
+            f = os.path.join(path, name)
+            if os.path.exists(f):
+                with open(f) as fh:
+                    return cls.from_dict(json.load(fh), glm=glm)
+        return None
 
     def to_dict(self):
         d = dict(self.raw or {})
@@ -141,7 +153,10 @@ class ImageProcessor:
         p, m, tp = self.patch_size, self.merge_size, self.temporal_patch_size
         cap = self.max_pixels if max_pixels is None else min(self.max_pixels, max_pixels)
         W0, H0 = img.size
-        h, w = fit_size(H0, W0, p * m, self.min_pixels, cap)
+        if self.glm:
+            h, w = fit_size(H0, W0, p * m, self.min_pixels, cap, frames=tp, upscale_small=True)
+        else:
+            h, w = fit_size(H0, W0, p * m, self.min_pixels, cap)
         if (h, w) != (H0, W0):
             img = img.resize((w, h), Image.BICUBIC)
         a = np.asarray(img, dtype=np.float32) * self.rescale_factor
