@@ -94,3 +94,42 @@ def test_conf_argmax_rows_matches_softmax():
     assert torch.equal(idx, ref)
     torch.testing.assert_close((1.0 / z).double(), conf, rtol=1e-4, atol=1e-6)
     torch.testing.assert_close(mx, view.max(-1).values)
+
+
+def test_glm_ocr_runtime_cuda_matches_cpu():
+    """GLM-OCR text decoder on the serving kernels (RoPE-only q / k path, output norms, image prefill
+    with per-token 3-D RoPE tables, draft / verify canvases) vs the CPU statement of the same steps."""
+    from trida_stack_b200.data.images import mrope_position_ids
+    from trida_stack_b200.models.glm_ocr import GlmOcrDecoder, glm_ocr_config
+    torch.manual_seed(0)
+    cfg = glm_ocr_config({
+        "model_type": "glm_ocr", "image_token_id": 500,
+        "text_config": {"vocab_size": 512, "hidden_size": 256, "intermediate_size": 512, "num_hidden_layers": 2,
+                        "num_attention_heads": 4, "num_key_value_heads": 2, "head_dim": 128,
+                        "rope_parameters": {"rope_theta": 10000.0, "partial_rotary_factor": 0.5,
+                                            "mrope_section": [8, 12, 12]}}})
+    dec = GlmOcrDecoder(cfg, dtype=torch.float32)
+    with torch.no_grad():
+        for p in dec.parameters():
+            if p.dim() == 1:
+                p.add_(0.1 * torch.randn_like(p))
+    dec = dec.to(torch.bfloat16).float()
+    dec_g = copy.deepcopy(dec).to("cuda", torch.bfloat16)
+    grid = torch.tensor([[1, 8, 12]])
+    ids = torch.tensor([5, 6, 7] + [500] * 24 + list(range(10, 40)))
+    feats = torch.randn(24, 256) * 0.5
+    pos3 = mrope_position_ids(ids, grid, 500)
+    out = {}
+    for name, d in (("cpu", dec), ("gpu", dec_g)):
+        rt = Runtime(d, max_slots=2, max_len=256)
+        s = rt.alloc()
+        last = rt.prefill([s], [ids.tolist()], vis=[(feats, pos3)], pos_offset=1)
+        draft = rt.canvas([s], [[7] + [511] * 8], 1)
+        rt.discard()
+        ver = rt.canvas([s], [[7, 8, 9, 10, 11, 12, 13, 14, 15]], 9)
+        rt.commit([s], [4])
+        nxt = rt.canvas([s], [[20, 21, 22]], 3)
+        rt.commit([s], [3])
+        out[name] = [t.float().cpu() for t in (last, draft, ver, nxt)]
+    for a, b in zip(out["gpu"], out["cpu"]):
+        assert _rel(a, b) < 3e-2, _rel(a, b)
