@@ -150,7 +150,8 @@ void symm_allreduce(const std::vector<int64_t>& bufs, const std::vector<int64_t>
 void gemm_allreduce(const at::Tensor& A, const at::Tensor& B, const at::Tensor& D,
                     const c10::optional<at::Tensor>& residual, const std::vector<int64_t>& recv,
                     const std::vector<int64_t>& flags, int64_t rank, const at::Tensor& ctr_done, int64_t mcap,
-                    int64_t tiles_cap) {
+                    int64_t tiles_cap, const c10::optional<at::Tensor>& ws,
+                    const c10::optional<at::Tensor>& tile_ctr) {
   CHECK_CUDA(A); CHECK_CUDA(B); CHECK_CUDA(D);
   CHECK_BF16(A); CHECK_BF16(B); CHECK_BF16(D);
   CHECK_ROWMAJOR(A); CHECK_ROWMAJOR(B); CHECK_ROWMAJOR(D);
@@ -174,7 +175,18 @@ void gemm_allreduce(const at::Tensor& A, const at::Tensor& B, const at::Tensor& 
               "GEMM leading dimensions must be 16-byte multiples");
   c10::cuda::CUDAGuard g(A.device());
   unsigned* cd = reinterpret_cast<unsigned*>(ctr_done.data_ptr<int>());
-  trida::GemmAllreduce ar{(int)recv.size(), (int)rank, (int)tiles_cap, mcap, pa.bufs, pa.flags, cd, cd + 1};
+  float* wsp = nullptr;
+  int64_t ws_units = 0;
+  unsigned* tc = nullptr;
+  if (ws.has_value() && ws->defined() && tile_ctr.has_value() && tile_ctr->defined()) {
+    TORCH_CHECK(ws->scalar_type() == at::kFloat && ws->is_contiguous(), "ws must be contiguous fp32");
+    TORCH_CHECK(tile_ctr->scalar_type() == at::kInt && tile_ctr->numel() >= tiles_cap * 4, "tile_ctr int32 [tiles_cap*4]");
+    wsp = ws->data_ptr<float>();
+    ws_units = ws->numel() / (128 * 256);
+    tc = reinterpret_cast<unsigned*>(tile_ctr->data_ptr<int>());
+  }
+  trida::GemmAllreduce ar{(int)recv.size(), (int)rank, (int)tiles_cap, mcap, pa.bufs, pa.flags, cd, cd + 1,
+                          wsp, ws_units, tc};
   const int rc = trida::gemm_bf16_allreduce(a, ar, sm_count(), stream());
   TORCH_CHECK(rc == 0, "fused GEMM + all-reduce failed with code ", rc, " (M=", a.M, " N=", a.N, " K=", a.K, ")");
 }
@@ -825,7 +837,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_close", &symm_close);
   m.def("symm_tensor", &symm_tensor);
   m.def("symm_allreduce", &symm_allreduce);
-  m.def("gemm_allreduce", &gemm_allreduce);
+  m.def("gemm_allreduce", &gemm_allreduce, py::arg("A"), py::arg("B"), py::arg("D"), py::arg("residual"),
+        py::arg("recv"), py::arg("flags"), py::arg("rank"), py::arg("ctr_done"), py::arg("mcap"),
+        py::arg("tiles_cap"), py::arg("ws") = py::none(), py::arg("tile_ctr") = py::none());
   m.def("symm_rs_sumsq", &symm_rs_sumsq, py::arg("bufs"), py::arg("flags"), py::arg("rank"), py::arg("epoch"),
         py::arg("shard_off"), py::arg("shard_len"), py::arg("scale"), py::arg("shard_out"), py::arg("partial"),
         py::arg("err"), py::arg("accumulate") = false, py::arg("done") = py::none(), py::arg("close_slot") = -1);

@@ -73,6 +73,8 @@ struct Params {
   unsigned* ar_flag[8];
   unsigned* ar_ctr;       // this rank's call counter (the call's epoch = *ar_ctr + 1)
   unsigned* ar_done;      // CTAs finished in this call (the last one advances ar_ctr)
+  float* ar_ws;           // split-K: fp32 partial tiles [tiles * splits][128][256] (this GPU)
+  unsigned* ar_tile_ctr;  // split-K: arrivals per (tile, epilogue warp), reset by the last arrival
 };
 
 __device__ __forceinline__ void red_release_sys(unsigned* p, unsigned v) {
@@ -265,8 +267,36 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       int m0, n0;
       tile_coords(u / p.splits, mt, nt, BM, m0, n0);
       if (fused) {
-        // ---- phase 1: this rank's partial rows -> every rank's receive buffer (slot ar_rank)
         const int W = p.ar_world;
+        const int tile = u / p.splits;
+        const bool ksplit = p.splits > 1;                // MH == 1 whenever the all-reduce is fused
+        if (ksplit) {
+          // ---- phase 0 (split K): stash this split's fp32 rows; the warp arriving last for these
+          // 32 rows of the tile sums all splits and carries on, the others are done with the tile
+          float* wrow = p.ar_ws + ((int64_t)u * 128 + r) * BN;     // u = tile * splits + split
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld32(tmem + ab * BN + lane_off + c * 32, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(wrow + c * 32 + j) =
+                  make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                              __uint_as_float(v[j + 3]));
+          }
+          tc_fence_before();
+          mbar_arrive(&acc_empty[ab]);
+          __threadfence();
+          __syncwarp();
+          int last = 0;
+          if (lane == 0) last = atomicAdd(p.ar_tile_ctr + tile * 4 + q, 1u) == (unsigned)(p.splits - 1);
+          last = __shfl_sync(0xffffffffu, last, 0);
+          if (!last) continue;
+          __threadfence();
+          if (lane == 0) p.ar_tile_ctr[tile * 4 + q] = 0u;
+        }
+        // ---- phase 1: this rank's partial rows -> every rank's receive buffer (slot ar_rank)
 #pragma unroll 1
         for (int h = 0; h < MH; ++h) {
           const uint32_t acc = tmem + (ab + h) * BN + lane_off;
@@ -274,18 +304,33 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const bool rok = row < p.M;
 #pragma unroll 1
           for (int c = 0; c < BN / 32; ++c) {
-            uint32_t v[32];
-            tmem_ld32(acc + c * 32, v);
-            tmem_wait_ld();
+            float f[32];
+            if (ksplit) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) f[j] = 0.f;
+              for (int sidx = 0; sidx < p.splits; ++sidx) {
+                const float4* src = reinterpret_cast<const float4*>(
+                    p.ar_ws + ((int64_t)(tile * p.splits + sidx) * 128 + r) * BN + c * 32);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const float4 x = src[j];
+                  f[4 * j] += x.x; f[4 * j + 1] += x.y; f[4 * j + 2] += x.z; f[4 * j + 3] += x.w;
+                }
+              }
+            } else {
+              uint32_t v[32];
+              tmem_ld32(acc + c * 32, v);
+              tmem_wait_ld();
+#pragma unroll
+              for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+            }
             const int col0 = n0 + c * 32;
             if (!rok || col0 >= p.N) continue;
             uint4 pk[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j)
-              pk[j] = make_uint4(pack_bf16x2(__uint_as_float(v[8 * j]), __uint_as_float(v[8 * j + 1])),
-                                 pack_bf16x2(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3])),
-                                 pack_bf16x2(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5])),
-                                 pack_bf16x2(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7])));
+              pk[j] = make_uint4(pack_bf16x2(f[8 * j], f[8 * j + 1]), pack_bf16x2(f[8 * j + 2], f[8 * j + 3]),
+                                 pack_bf16x2(f[8 * j + 4], f[8 * j + 5]), pack_bf16x2(f[8 * j + 6], f[8 * j + 7]));
             const int64_t off = ((int64_t)(par * W + p.ar_rank) * p.ar_mcap + row) * p.N + col0;
 #pragma unroll 1
             for (int d = 0; d < W; ++d) {
@@ -295,9 +340,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
           }
         }
-        tc_fence_before();
-        mbar_arrive(&acc_empty[ab]);                 // the accumulator is free for the next tile
-        const int64_t fidx = ((int64_t)par * p.ar_tiles_cap + u) * 4 + q;
+        if (!ksplit) {
+          tc_fence_before();
+          mbar_arrive(&acc_empty[ab]);               // the accumulator is free for the next tile
+        }
+        const int64_t fidx = ((int64_t)par * p.ar_tiles_cap + tile) * 4 + q;
         asm volatile("fence.acq_rel.sys;\n" ::: "memory");
         __syncwarp();
         if (lane == 0)
@@ -593,7 +640,7 @@ int gemm_bf16(GemmLayout layout, bool d_fp32, const GemmArgs& a, int tile, int s
   p.alpha = a.alpha; p.beta = a.beta; p.d_fp32 = d_fp32 ? 1 : 0;
   p.err = err_word();
   p.ar_world = 1; p.ar_rank = 0; p.ar_tiles_cap = 0; p.ar_mcap = 0;
-  p.ar_ctr = nullptr; p.ar_done = nullptr;
+  p.ar_ctr = nullptr; p.ar_done = nullptr; p.ar_ws = nullptr; p.ar_tile_ctr = nullptr;
   for (int i = 0; i < 8; ++i) { p.ar_recv[i] = nullptr; p.ar_flag[i] = nullptr; }
   const int kb = (a.K + BK - 1) / BK;
   p.kb_per = (kb + splits - 1) / splits;
@@ -647,12 +694,17 @@ int gemm_bf16_allreduce(const GemmArgs& a, const GemmAllreduce& ar, int sm_count
   p.D = a.D; p.ldd = a.ldd; p.C = a.C; p.ldc = a.ldc;
   p.alpha = a.alpha; p.beta = a.beta; p.d_fp32 = 0;
   p.err = err_word();
-  p.kb_per = (a.K + BK - 1) / BK;
-  p.splits = 1;
+  // skinny products split K over otherwise idle SMs; the split partials are summed by the last
+  // arriving CTA of each tile before the exchange (workspace: ws_units tiles of 128 x 256 fp32)
+  const int kb = (a.K + BK - 1) / BK;
+  int splits = (ar.ws != nullptr && ar.tile_ctr != nullptr) ? gemm_splitk(a.M, a.N, a.K, sm_count) : 1;
+  while (splits > 1 && (int64_t)tiles * splits > ar.ws_units) --splits;
+  p.kb_per = (kb + splits - 1) / splits;
+  p.splits = (kb + p.kb_per - 1) / p.kb_per;
   p.ws = nullptr;
   p.a_kmajor = 1; p.b_kmajor = 1;
   p.ar_world = ar.world; p.ar_rank = ar.rank; p.ar_tiles_cap = ar.tiles_cap; p.ar_mcap = ar.mcap;
-  p.ar_ctr = ar.ctr; p.ar_done = ar.done;
+  p.ar_ctr = ar.ctr; p.ar_done = ar.done; p.ar_ws = ar.ws; p.ar_tile_ctr = ar.tile_ctr;
   for (int i = 0; i < 8; ++i) {
     p.ar_recv[i] = i < ar.world ? reinterpret_cast<bf16*>(ar.recv[i]) : nullptr;
     p.ar_flag[i] = i < ar.world ? ar.flags[i] : nullptr;

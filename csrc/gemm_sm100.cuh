@@ -44,6 +44,11 @@ struct GemmAllreduce {
   unsigned* const* flags;
   unsigned* ctr;
   unsigned* done;
+  // optional split K for skinny products: fp32 workspace of ws_units 128 x 256 tiles and arrival
+  // counters [tiles_cap][4] (zeroed once), both in this GPU's memory; null = no split
+  float* ws;
+  int64_t ws_units;
+  unsigned* tile_ctr;
 };
 int gemm_bf16_allreduce(const GemmArgs& a, const GemmAllreduce& ar, int sm_count, cudaStream_t stream);
 

@@ -73,7 +73,8 @@ def test_cuda_engine_graphs_match_eager(mode):
         eng = Engine(Runtime(dec, max_slots=8, max_len=512), mask_id=511, mode=mode, n=4, graphs=graphs)
         reqs = eng.generate(prompts, max_new_tokens=50)
         assert all(len(r.output) == 50 for r in reqs)
-        assert eng.summary(reqs)["tokens_per_forward"] >= 1.0
+        if mode != "diffusion":           # pure diffusion pays a commit forward per block
+            assert eng.summary(reqs)["tokens_per_forward"] >= 1.0
         outs.append([r.output for r in reqs])
     assert outs[0] == outs[1]
 

@@ -123,9 +123,9 @@ def _fused_worker(rank, world, port, q):
         assert tp.fused
         errs = []
         g = torch.Generator("cuda").manual_seed(10 + rank)
-        for M in (70, 448, 1100, 448):
-            x = torch.randn(M, 512, device="cuda", dtype=torch.bfloat16, generator=g)
-            w = torch.randn(2560, 512, device="cuda", dtype=torch.bfloat16, generator=g) * 0.05
+        for M, K in ((70, 512), (448, 512), (1100, 512), (448, 4608), (448, 512)):   # split K and whole tiles
+            x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16, generator=g)
+            w = torch.randn(2560, K, device="cuda", dtype=torch.bfloat16, generator=g) * 0.05
             res = torch.randn(M, 2560, device="cuda", dtype=torch.bfloat16)
             dist.broadcast(res, 0)
             out = tp.row_parallel(x, w, res)

@@ -121,6 +121,10 @@ class TPContext:
             self.recv = self.heap.alloc(2 * self.world * max_rows * hidden, torch.bfloat16)
             self.flags = self.heap.alloc(2 * self.tiles_cap * 4, torch.int32)
             self.ctr_done = torch.zeros(2, dtype=torch.int32, device="cuda")
+            # split-K scratch for skinny (decode) products: one 128 x 256 fp32 tile per SM
+            sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+            self.ws = torch.empty(sms * 128 * 256, dtype=torch.float32, device="cuda")
+            self.tile_ctr = torch.zeros(self.tiles_cap * 4, dtype=torch.int32, device="cuda")
         else:
             self.bufs = [self.heap.alloc(max_rows * hidden, torch.bfloat16) for _ in range(2)]
 
@@ -140,7 +144,8 @@ class TPContext:
                 raise RuntimeError(f"{rows} rows exceed the TP buffers ({self.max_rows})")
             out = torch.empty(rows, self.hidden, dtype=torch.bfloat16, device=x.device)
             blocks.ext().gemm_allreduce(x.contiguous(), w, out, residual.contiguous(), self.recv.ptrs,
-                                        self.flags.ptrs, self.rank, self.ctr_done, self.max_rows, self.tiles_cap)
+                                        self.flags.ptrs, self.rank, self.ctr_done, self.max_rows, self.tiles_cap,
+                                        self.ws, self.tile_ctr)
             return out
         buf, part = self.next_buffer(rows)
         blocks.gemm(blocks.TN, x, w, part)
