@@ -122,6 +122,7 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;\n" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
 
 __device__ __forceinline__ void tile_coords(int tile, int mt, int nt, int bm, int& m0, int& n0) {
@@ -296,49 +297,58 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           __threadfence();
           if (lane == 0) p.ar_tile_ctr[tile * 4 + q] = 0u;
         }
-        // ---- phase 1: this rank's partial rows -> every rank's receive buffer (slot ar_rank)
+        // ---- phase 1: this rank's partial rows -> every rank's receive buffer (slot ar_rank).
+        // Each 32-row x 64-column chunk is packed to bf16 in the warp's swizzled staging tile, then
+        // copied out by 8 lanes per row so every store instruction writes four whole 128-byte row
+        // segments (NVLink-friendly) instead of 32 scattered 16-byte pieces.
+        const int row0 = m0 + q * 32;                    // MH == 1 whenever the all-reduce is fused
+        if (lane == 0) bulk_wait_read0();                // no earlier TMA store still reads staging
+        __syncwarp();
 #pragma unroll 1
-        for (int h = 0; h < MH; ++h) {
-          const uint32_t acc = tmem + (ab + h) * BN + lane_off;
-          const int row = m0 + h * 128 + r;
-          const bool rok = row < p.M;
-#pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            float f[32];
-            if (ksplit) {
+        for (int ch = 0; ch < BN / 64; ++ch) {
+          float f[64];
+          if (ksplit) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) f[j] = 0.f;
-              for (int sidx = 0; sidx < p.splits; ++sidx) {
-                const float4* src = reinterpret_cast<const float4*>(
-                    p.ar_ws + ((int64_t)(tile * p.splits + sidx) * 128 + r) * BN + c * 32);
+            for (int j = 0; j < 64; ++j) f[j] = 0.f;
+            for (int sidx = 0; sidx < p.splits; ++sidx) {
+              const float4* src = reinterpret_cast<const float4*>(
+                  p.ar_ws + ((int64_t)(tile * p.splits + sidx) * 128 + r) * BN + ch * 64);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                  const float4 x = src[j];
-                  f[4 * j] += x.x; f[4 * j + 1] += x.y; f[4 * j + 2] += x.z; f[4 * j + 3] += x.w;
-                }
+              for (int j = 0; j < 16; ++j) {
+                const float4 x = src[j];
+                f[4 * j] += x.x; f[4 * j + 1] += x.y; f[4 * j + 2] += x.z; f[4 * j + 3] += x.w;
               }
-            } else {
-              uint32_t v[32];
-              tmem_ld32(acc + c * 32, v);
-              tmem_wait_ld();
-#pragma unroll
-              for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
             }
-            const int col0 = n0 + c * 32;
-            if (!rok || col0 >= p.N) continue;
-            uint4 pk[4];
+          } else {
+            uint32_t v0[32], v1[32];
+            tmem_ld32(tmem + ab * BN + lane_off + ch * 64, v0);
+            tmem_ld32(tmem + ab * BN + lane_off + ch * 64 + 32, v1);
+            tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              pk[j] = make_uint4(pack_bf16x2(f[8 * j], f[8 * j + 1]), pack_bf16x2(f[8 * j + 2], f[8 * j + 3]),
-                                 pack_bf16x2(f[8 * j + 4], f[8 * j + 5]), pack_bf16x2(f[8 * j + 6], f[8 * j + 7]));
-            const int64_t off = ((int64_t)(par * W + p.ar_rank) * p.ar_mcap + row) * p.N + col0;
-#pragma unroll 1
-            for (int d = 0; d < W; ++d) {
-              uint4* dst = reinterpret_cast<uint4*>(p.ar_recv[(p.ar_rank + d) % W] + off);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) dst[j] = pk[j];
-            }
+            for (int j = 0; j < 32; ++j) { f[j] = __uint_as_float(v0[j]); f[32 + j] = __uint_as_float(v1[j]); }
           }
+          const int col0 = n0 + ch * 64;
+          if (row0 >= p.M || col0 >= p.N) continue;      // warp-uniform
+          unsigned char* sb = epi + q * 8192 + (ch & 1) * 4096;
+          unsigned char* rowp = sb + lane * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<uint4*>(rowp + ((j ^ (lane & 7)) << 4)) =
+                make_uint4(pack_bf16x2(f[8 * j], f[8 * j + 1]), pack_bf16x2(f[8 * j + 2], f[8 * j + 3]),
+                           pack_bf16x2(f[8 * j + 4], f[8 * j + 5]), pack_bf16x2(f[8 * j + 6], f[8 * j + 7]));
+          __syncwarp();
+          const int seg = lane & 7;
+#pragma unroll 1
+          for (int it = 0; it < 8; ++it) {
+            const int rr = it * 4 + (lane >> 3);
+            if (row0 + rr >= p.M) continue;
+            const uint4 val = *reinterpret_cast<const uint4*>(sb + rr * 128 + ((seg ^ (rr & 7)) << 4));
+            const int64_t off = ((int64_t)(par * W + p.ar_rank) * p.ar_mcap + row0 + rr) * p.N + col0 + seg * 8;
+#pragma unroll 1
+            for (int d = 0; d < W; ++d)
+              *reinterpret_cast<uint4*>(p.ar_recv[(p.ar_rank + d) % W] + off) = val;
+          }
+          __syncwarp();
         }
         if (!ksplit) {
           tc_fence_before();
@@ -352,67 +362,63 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // ---- phase 2: wait for every rank's partial of this warp's rows, sum (+ C), TMA-store D
         int ok = 1;
         if (lane == 0) {
-          unsigned* f = p.ar_flag[p.ar_rank] + fidx;
-          ok = wait_count(f, (unsigned)W, p.err, 110) ? 1 : 0;
-          if (ok) *reinterpret_cast<volatile unsigned*>(f) = 0u;
+          unsigned* fl = p.ar_flag[p.ar_rank] + fidx;
+          ok = wait_count(fl, (unsigned)W, p.err, 110) ? 1 : 0;
+          if (ok) *reinterpret_cast<volatile unsigned*>(fl) = 0u;
         }
         ok = __shfl_sync(0xffffffffu, ok, 0);
         __syncwarp();
         if (!ok) continue;
         const bool use_c = p.C != nullptr && p.beta != 0.f;
         const bf16* own = p.ar_recv[p.ar_rank];
+        ebuf = 0;
 #pragma unroll 1
-        for (int h = 0; h < MH; ++h) {
-          const int row0 = m0 + h * 128 + q * 32;
-          const int row = row0 + lane;
-          const bool rok = row < p.M;
-#pragma unroll 1
-          for (int ch = 0; ch < BN / 64; ++ch) {
-            const int col0 = n0 + ch * 64;
-            if (row0 >= p.M || col0 >= p.N) continue;   // warp-uniform
-            unsigned char* sb = epi + q * 8192 + ebuf * 4096;
-            if (lane == 0) bulk_wait_read1();
-            __syncwarp();
-            if (use_c) {
-              if (lane == 0) {
-                mbar_expect_tx(&cbar[q * 2 + ebuf], 4096);
-                tma_load_2d(sb, &tmC, &cbar[q * 2 + ebuf], col0, row0);
-              }
-              mbar_wait(&cbar[q * 2 + ebuf], cpar[ebuf], p.err, 107);
-              cpar[ebuf] ^= 1;
-            }
-            unsigned char* rowp = sb + lane * 128;
-#pragma unroll 1
-            for (int j = 0; j < 8; ++j) {
-              float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-              if (rok) {
-#pragma unroll 1
-                for (int sidx = 0; sidx < W; ++sidx) {
-                  float x[8];
-                  load8(own + ((int64_t)(par * W + sidx) * p.ar_mcap + row) * p.N + col0 + 8 * j, x);
-#pragma unroll
-                  for (int e = 0; e < 8; ++e) o[e] += x[e];
-                }
-              }
-              bf16* cp = reinterpret_cast<bf16*>(rowp + ((j ^ (lane & 7)) << 4));
-#pragma unroll
-              for (int e = 0; e < 8; ++e) o[e] *= p.alpha;
-              if (use_c) {
-                float cv[8];
-                load8(cp, cv);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) o[e] += p.beta * cv[e];
-              }
-              store8(cp, o);
-            }
-            fence_async_smem();
-            __syncwarp();
+        for (int ch = 0; ch < BN / 64; ++ch) {
+          const int col0 = n0 + ch * 64;
+          if (row0 >= p.M || col0 >= p.N) continue;      // warp-uniform
+          unsigned char* sb = epi + q * 8192 + ebuf * 4096;
+          if (lane == 0) bulk_wait_read1();
+          __syncwarp();
+          if (use_c) {
             if (lane == 0) {
-              tma_store_2d(&tmD, sb, col0, row0);
-              bulk_commit();
+              mbar_expect_tx(&cbar[q * 2 + ebuf], 4096);
+              tma_load_2d(sb, &tmC, &cbar[q * 2 + ebuf], col0, row0);
             }
-            ebuf ^= 1;
+            mbar_wait(&cbar[q * 2 + ebuf], cpar[ebuf], p.err, 107);
+            cpar[ebuf] ^= 1;
           }
+          const int seg = lane & 7;
+#pragma unroll 1
+          for (int it = 0; it < 8; ++it) {               // 8 lanes per row: coalesced 128-byte reads
+            const int rr = it * 4 + (lane >> 3);
+            float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (row0 + rr < p.M) {
+#pragma unroll 1
+              for (int sidx = 0; sidx < W; ++sidx) {
+                float x[8];
+                load8(own + ((int64_t)(par * W + sidx) * p.ar_mcap + row0 + rr) * p.N + col0 + seg * 8, x);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) o[e] += x[e];
+              }
+            }
+            bf16* cp = reinterpret_cast<bf16*>(sb + rr * 128 + ((seg ^ (rr & 7)) << 4));
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] *= p.alpha;
+            if (use_c) {
+              float cv[8];
+              load8(cp, cv);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) o[e] += p.beta * cv[e];
+            }
+            store8(cp, o);
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmD, sb, col0, row0);
+            bulk_commit();
+          }
+          ebuf ^= 1;
         }
         continue;
       }
