@@ -47,8 +47,8 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-graphs", action="store_true", help="launch every kernel eagerly (no CUDA graphs)")
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel ranks (launch with torchrun)")
-    ap.add_argument("--tp-unfused", action="store_true",
-                    help="TP all-reduce as a separate kernel after the GEMM instead of in its epilogue")
+    ap.add_argument("--tp-fused", action="store_true",
+                    help="TP all-reduce in the GEMM epilogue instead of a separate kernel after the GEMM")
     args = ap.parse_args()
 
     from trida_stack_b200.models import Decoder
@@ -74,7 +74,7 @@ def main():
         from trida_stack_b200.serve.tp import TPContext, shard_decoder
         dec = shard_decoder(dec, rank, world)
         torch.cuda.empty_cache()
-        tp = TPContext(max_rows=args.requests * 64, hidden=cfg.hidden_size, fused=not args.tp_unfused)
+        tp = TPContext(max_rows=args.requests * 64, hidden=cfg.hidden_size, fused=args.tp_fused)
     rt = Runtime(dec, max_slots=args.requests, max_len=max_len, tp=tp)
     eng = Engine(rt, mask_id=mask_id, mode=args.mode, n=args.gen_block, max_running=args.requests, graphs=not args.no_graphs)
     g = torch.Generator().manual_seed(args.seed)
@@ -122,7 +122,7 @@ def main():
                    "prompt": args.prompt, "max_new": args.max_new, "mode": args.mode, "n": args.gen_block,
                    "canvas_rows": 2 * args.gen_block - 1 if args.mode == "self-spec" else 1, "greedy": True,
                    "cuda_graphs": not args.no_graphs,
-                   "tp_allreduce": ("fused into the GEMM epilogue" if not args.tp_unfused else "separate kernel")
+                   "tp_allreduce": ("fused into the GEMM epilogue" if args.tp_fused else "separate peer-memory kernel")
                    if world > 1 else None},
         "data": "synthetic uniform prompts, random-init weights", "dtype": "bf16"}), flush=True)
     _finish(rt, world)

@@ -119,7 +119,7 @@ def _fused_worker(rank, world, port, q):
                             device_id=torch.device("cuda", rank))
     try:
         from trida_stack_b200.serve.tp import TPContext
-        tp = TPContext(max_rows=1200, hidden=2560)
+        tp = TPContext(max_rows=1200, hidden=2560, fused=True)
         assert tp.fused
         errs = []
         g = torch.Generator("cuda").manual_seed(10 + rank)

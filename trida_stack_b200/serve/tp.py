@@ -102,13 +102,16 @@ class TPContext:
     """Per-process TP state: the process group, the symmetric buffers of the row-parallel
     all-reduces and the vocabulary-parallel greedy pick.
 
-    ``fused=True`` (default): every row-parallel GEMM runs the all-reduce in its own epilogue
+    ``fused=False`` (default): the GEMM writes this rank's partial into its symmetric buffer and a
+    one-shot all-reduce kernel pulls every rank's partial over NVLink and adds the residual.
+    ``fused=True``: every row-parallel GEMM runs the all-reduce in its own epilogue
     (``csrc/gemm_sm100.cu``, ``gemm_bf16_allreduce``): partial tiles are pushed over NVLink into
     every rank's receive buffer as they come out of the tensor cores and each rank sums its rows
-    as soon as all ranks' tiles have arrived -- one kernel per layer output.  ``fused=False`` keeps
-    the two-kernel path (GEMM into a symmetric buffer, then a one-shot all-reduce kernel)."""
+    as soon as all ranks' tiles have arrived -- one kernel per layer output.  Measured on 2 B200s it
+    is still about twice as slow as the two-kernel path on decode and prefill shapes, so it is
+    opt-in until its exchange is faster."""
 
-    def __init__(self, max_rows, hidden, group=None, fused=True):
+    def __init__(self, max_rows, hidden, group=None, fused=False):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
