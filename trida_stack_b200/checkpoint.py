@@ -123,6 +123,7 @@ def save_train_state(model, optim, global_step, args, tag):
 
 def load_train_state(model, optim, resume_dir):
     """Restore the optimizer + step when ``resume_dir`` has train state, else 0 (warm restart)."""
+    verify_manifest(resume_dir)
     state_dir = os.path.join(resume_dir, "train_state")
     meta = os.path.join(resume_dir, "train_state.json")
     if not (os.path.isdir(state_dir) and os.path.exists(meta)):
@@ -147,8 +148,70 @@ def load_train_state(model, optim, resume_dir):
     return gs
 
 
+MANIFEST = "manifest.json"
+
+
+class CheckpointCorrupt(RuntimeError):
+    pass
+
+
+def _digest(path, chunk=1 << 24):
+    import hashlib
+    h = hashlib.sha256()
+    with open(path, "rb") as f:
+        while True:
+            b = f.read(chunk)
+            if not b:
+                break
+            h.update(b)
+    return h.hexdigest()
+
+
+def write_manifest(ckpt_dir):
+    """Record size and SHA-256 of every file under ``ckpt_dir`` (written last, by one rank)."""
+    files = {}
+    for root, _, names in os.walk(ckpt_dir):
+        for n in sorted(names):
+            full = os.path.join(root, n)
+            rel = os.path.relpath(full, ckpt_dir)
+            if rel == MANIFEST:
+                continue
+            files[rel] = {"bytes": os.path.getsize(full), "sha256": _digest(full)}
+    tmp = os.path.join(ckpt_dir, MANIFEST + ".tmp")
+    with open(tmp, "w") as f:
+        json.dump({"files": files}, f, indent=1)
+    os.replace(tmp, os.path.join(ckpt_dir, MANIFEST))
+
+
+def verify_manifest(ckpt_dir):
+    """Raise ``CheckpointCorrupt`` if a file listed in the manifest is missing, truncated or altered;
+    a checkpoint without a manifest (written by another tool) is accepted as is."""
+    path = os.path.join(ckpt_dir, MANIFEST)
+    if not os.path.exists(path):
+        return False
+    with open(path) as f:
+        files = json.load(f)["files"]
+    bad = []
+    for rel, meta in files.items():
+        full = os.path.join(ckpt_dir, rel)
+        if not os.path.exists(full):
+            bad.append(f"{rel}: missing")
+        elif os.path.getsize(full) != meta["bytes"]:
+            bad.append(f"{rel}: {os.path.getsize(full)} bytes, manifest says {meta['bytes']}")
+        elif _digest(full) != meta["sha256"]:
+            bad.append(f"{rel}: content differs from the manifest")
+    if bad:
+        raise CheckpointCorrupt(f"checkpoint {ckpt_dir} is damaged: " + "; ".join(bad[:8]))
+    return True
+
+
 def save_checkpoint(model, optim, global_step, args):
-    """Weights first, then the optional optimizer state, on every rank in the same order."""
+    """Weights first, then the optional optimizer state, on every rank in the same order; rank 0
+    then writes the integrity manifest."""
     tag = f"step_{global_step}"
     save_hf(model, args, tag)
     save_train_state(model, optim, global_step, args, tag)
+    _barrier()
+    if is_master() and os.environ.get("TRIDA_CKPT_MANIFEST", "1") != "0":
+        write_manifest(os.path.join(args.save_dir, tag))
+    _barrier()

@@ -58,6 +58,9 @@ def load_decoder(path, device, dtype=torch.bfloat16, tokenizer=None, add_mask=Tr
 def build_model(args, device=None):
     source = args.resume or args.model_id
     if args.resume:
+        from ..checkpoint import verify_manifest
+        if verify_manifest(args.resume):
+            log(f"[resume] {args.resume}: every file matches its manifest")
         log(f"[resume] loading model weights from {args.resume}")
     device = device or (torch.device("cuda") if torch.cuda.is_available() else torch.device("cpu"))
     tok = load_tokenizer(source, args.trust_remote_code)

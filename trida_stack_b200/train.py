@@ -7,6 +7,7 @@ summed across ranks for the periodic log; checkpoints every ``--save_every`` ste
 reduces gradients once per step anyway, which is the same schedule).
 """
 import sys
+import os
 import time
 
 import torch
@@ -82,7 +83,35 @@ def _fresh():
 
 
 def run_training(args, dev, model, loaders, optim):
-    """Resume if asked, train to ``max_steps``, save the final checkpoint."""
+    """Resume if asked, train to ``max_steps``, save the final checkpoint.  With several ranks a
+    heartbeat thread watches the others (``parallel.health``): a rank that fails tells the rest,
+    and a rank that goes silent for ``$TRIDA_HEARTBEAT_TIMEOUT`` seconds (default 120) stops the
+    others at their next step boundary instead of at the process-group timeout."""
+    hb = None
+    if world_size() > 1 and os.environ.get("TRIDA_HEARTBEAT", "1") != "0":
+        from .parallel.health import Heartbeat
+        hb = Heartbeat(timeout=float(os.environ.get("TRIDA_HEARTBEAT_TIMEOUT", "120"))).start()
+    try:
+        _run_training(args, dev, model, loaders, optim, hb)
+    except BaseException as e:
+        if hb is not None:
+            hb.fail(f"{type(e).__name__}: {str(e)[:200]}")
+        raise
+    finally:
+        if hb is not None:
+            hb.stop()
+
+
+def _boundary(hb, step, args):
+    if hb is not None:
+        hb.beat(step)
+        hb.check()
+    if step % args.log_every == 0:
+        from .parallel.health import check_device
+        check_device()
+
+
+def _run_training(args, dev, model, loaders, optim, hb):
     loader, decision_iter = loaders.text, loaders.decision
     run = None
     if args.wandb and is_master():
@@ -97,6 +126,7 @@ def run_training(args, dev, model, loaders, optim):
         decision_micro_steps(model, decision_iter, args, dev, running)
         lr, gnorm = apply_optimizer_step(model, optim, step, args)
         step += 1
+        _boundary(hb, step, args)
         if step % args.log_every == 0:
             log_decision_progress(args, dev, running, step, lr, gnorm, t0, run)
             running, t0 = _fresh(), time.time()
@@ -132,6 +162,7 @@ def run_training(args, dev, model, loaders, optim):
                 decision_micro_steps(model, decision_iter, args, dev, running)
             lr, gnorm = apply_optimizer_step(model, optim, step, args)
             step += 1
+            _boundary(hb, step, args)
             if step % args.log_every == 0:
                 log_text_progress(args, dev, running, step, lr, gnorm, t0, run, decision_iter)
                 running, t0 = _fresh(), time.time()
