@@ -212,6 +212,7 @@ def save_checkpoint(model, optim, global_step, args):
     save_hf(model, args, tag)
     save_train_state(model, optim, global_step, args, tag)
     _barrier()
-    if is_master() and os.environ.get("TRIDA_CKPT_MANIFEST", "1") != "0":
-        write_manifest(os.path.join(args.save_dir, tag))
+    out = os.path.join(args.save_dir, tag) if getattr(args, "save_dir", None) else None
+    if out and os.path.isdir(out) and is_master() and os.environ.get("TRIDA_CKPT_MANIFEST", "1") != "0":
+        write_manifest(out)
     _barrier()
