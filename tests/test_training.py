@@ -167,3 +167,31 @@ def test_streamed_layer_gradients_match_resident():
         outs.append([p.detach().clone() for p in m.parameters()])
     for a, b in zip(*outs):
         torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6)
+
+
+def test_step_tracer_and_request_trace(tmp_path, monkeypatch):
+    """--profile_* window: one JSON line per traced step with per-phase times (phases repeated by
+    gradient accumulation are summed); $TRIDA_TRACE_JSONL: one line per finished request."""
+    import json as _json
+
+    from trida_stack_b200.utils.trace import StepTracer
+    tr = StepTracer(start=2, steps=2, out_dir=str(tmp_path / "prof"), rank=0, device="cpu")
+    for step in range(6):
+        tr.begin(step)
+        for _ in range(2):
+            with tr.phase("forward"):
+                sum(range(1000))
+            with tr.phase("backward"):
+                sum(range(2000))
+        tr.end(tokens=8)
+    recs = [_json.loads(l) for l in open(tmp_path / "prof" / "rank0.jsonl")]
+    assert [r["step"] for r in recs] == [2, 3]
+    assert all(r["forward_ms"] > 0 and r["backward_ms"] > 0 and r["total_ms"] >= r["forward_ms"] for r in recs)
+    monkeypatch.setenv("TRIDA_TRACE_JSONL", str(tmp_path / "req.jsonl"))
+    from test_serve_cpu import tiny_dense
+
+    from trida_stack_b200.serve import Engine, Runtime
+    eng = Engine(Runtime(tiny_dense(), max_slots=2, max_len=128), mask_id=96, mode="self-spec", n=2)
+    eng.generate([[1, 2, 3], [4, 5, 6, 7]], max_new_tokens=6)
+    lines = [_json.loads(l) for l in open(tmp_path / "req.jsonl")]
+    assert len(lines) == 2 and all(l["output_tokens"] == 6 and l["forwards"] > 0 for l in lines)

@@ -140,6 +140,8 @@ class Engine:
         self._stop = False
         self.stats = {"forwards": 0, "tokens": 0, "steps": 0, "prefill_tokens": 0}
         self.stats_interval = 0.0            # seconds between stats lines on stdout (0 = off)
+        from ..utils.trace import RequestTrace
+        self.trace = RequestTrace.from_env()  # $TRIDA_TRACE_JSONL: one line per finished request
         self._stats_t = time.perf_counter()
 
     # ------------------------------------------------------------------ API
@@ -269,6 +271,8 @@ class Engine:
             if r.done:
                 r.t_done = time.perf_counter()
                 self.rt.release(r.slot)
+                if self.trace is not None:
+                    self.trace.write(r, self.mode)
                 r.done_event.set()
                 if r.on_tokens is not None:
                     r.on_tokens(None)

@@ -112,6 +112,9 @@ def _boundary(hb, step, args):
 
 
 def _run_training(args, dev, model, loaders, optim, hb):
+    from .distributed import rank as _rank
+    from .utils.trace import StepTracer
+    tracer = StepTracer(args.profile_start, args.profile_steps, args.profile_dir, _rank(), dev)
     loader, decision_iter = loaders.text, loaders.decision
     run = None
     if args.wandb and is_master():
@@ -138,17 +141,22 @@ def _run_training(args, dev, model, loaders, optim, hb):
             if batch is None:
                 continue
             is_boundary = (micro + 1) % args.grad_accum == 0
+            if micro % args.grad_accum == 0:
+                tracer.begin(step)
             _sync(model, is_boundary and decision_iter is None)
             host_labels = batch["labels"]
-            dev_batch = {k: (v.to(dev, non_blocking=True) if torch.is_tensor(v) else v) for k, v in batch.items()}
+            with tracer.phase("h2d"):
+                dev_batch = {k: (v.to(dev, non_blocking=True) if torch.is_tensor(v) else v) for k, v in batch.items()}
             extra = {k: dev_batch[k] for k in ("seg_id", "resp_pos", "resp_block", "turn_id", "pixel_values",
                                               "image_grid_thw", "mrope_pos") if k in dev_batch}
             if (getattr(model, "bd_size", None) and not getattr(model, "ar_only", False) and "seg_id" not in batch
                     and "resp_block" not in batch and torch.is_tensor(host_labels) and host_labels.device.type == "cpu"):
                 from .engine import host_rpad
                 extra["rpad"] = host_rpad(host_labels, model.bd_size, model.response_buckets)
-            loss, logs = model(dev_batch["input_ids"], dev_batch["labels"], dev_batch["attention_mask"], **extra)
-            (loss / args.grad_accum).backward()
+            with tracer.phase("forward"):
+                loss, logs = model(dev_batch["input_ids"], dev_batch["labels"], dev_batch["attention_mask"], **extra)
+            with tracer.phase("backward"):
+                (loss / args.grad_accum).backward()
             running["loss"] += loss.item()
             running["diff"] += float(logs["diff_loss"])
             running["ar"] += float(logs["ar_loss"])
@@ -159,8 +167,11 @@ def _run_training(args, dev, model, loaders, optim, hb):
             if not is_boundary:
                 continue
             if decision_iter is not None:
-                decision_micro_steps(model, decision_iter, args, dev, running)
-            lr, gnorm = apply_optimizer_step(model, optim, step, args)
+                with tracer.phase("decision"):
+                    decision_micro_steps(model, decision_iter, args, dev, running)
+            with tracer.phase("optimizer"):
+                lr, gnorm = apply_optimizer_step(model, optim, step, args)
+            tracer.end(tokens=int(batch["input_ids"].numel()))
             step += 1
             _boundary(hb, step, args)
             if step % args.log_every == 0:
