@@ -1,14 +1,19 @@
 // Block-diffusion attention forward on the 5th-generation tensor cores (tcgen05 + TMEM).
 //
-// CTA = one 128-row query tile of one head.  Warp roles (192 threads):
-//   warps 0-3  softmax: thread r owns query row r == TMEM lane r.  Reads its S row from TMEM with
-//              tcgen05.ld, applies the block-diffusion rule on PARTIAL tiles, keeps the running
-//              max / sum, rescales its O row in TMEM only when the max grows by more than 2^8
-//              (otherwise exp2(s - m) <= 256 is exact enough in fp32 / bf16), and writes its P row
-//              (bf16) into shared memory in the UMMA K-major SWIZZLE_128B layout.
-//   warp 4     MMA issuer (one thread): S_i = Q K_i^T into one of two TMEM S buffers, then
+// CTA = one 128-row query tile of one head.  Warp roles (320 threads):
+//   warps 0-7  softmax, two warpgroups splitting every row: thread (half, r) owns columns
+//              [64 half, 64 half + 64) of query row r == TMEM lane r (warps w and w + 4 share a
+//              TMEM lane quarter), so two warps per SM sub-partition hide each other's exp /
+//              max / pack latencies.  Each reads its half S row with tcgen05.ld, applies the
+//              block-diffusion rule on PARTIAL tiles, exchanges its half-row max with its partner
+//              through shared memory (named barrier per warp pair), keeps the running max / sum,
+//              rescales its half of the O row in TMEM only when the max grows by more than 2^16,
+//              and writes its half P row (bf16) into shared memory in the UMMA K-major
+//              SWIZZLE_128B layout.  Control flow is identical in both halves (a timed-out wait
+//              skips work but keeps meeting the pair barrier), so a pair can never split.
+//   warp 8     MMA issuer (one thread): S_i = Q K_i^T into one of two TMEM S buffers, then
 //              O += P_{i-1} V_{i-1}; completion is signalled with tcgen05.commit on mbarriers.
-//   warp 5     TMA producer (one thread): Q once, K/V tiles into a 2-stage ring (plain per-CTA
+//   warp 9     TMA producer (one thread): Q once, K/V tiles into a 2-stage ring (plain per-CTA
 //              tensor loads, each CTA fetching its own tiles).
 // TMEM columns: S0 [0,128), S1 [128,256), O [256, 256+D).  The list of non-empty 128-key tiles
 // (and whether each is FULL or PARTIAL) comes from the same exact classification pass as the
@@ -31,7 +36,8 @@ constexpr int SEG_PAD = 0, SEG_SHARED = 1, SEG_XT = 2, SEG_X0 = 3;
 constexpr int FLAG_X0_TOKEN_CAUSAL = 1, FLAG_WITHIN_BLOCK_CAUSAL = 2;
 constexpr int CLS_FULL = 1;
 constexpr int BM = 128, BN = 128;
-constexpr int NTHREADS = 192;
+constexpr int NTHREADS = 192;        // backward
+constexpr int FWD_THREADS = 320;     // forward: 8 softmax warps + MMA warp + TMA warp
 // Lazy O rescaling: the running max is only moved (and O rescaled in TMEM) when a tile's max
 // exceeds it by more than 2^16; until then P = exp2(s - m) <= 65536, far inside bf16/fp32 range,
 // and the fp32 accumulators stay exact to their usual rounding.
@@ -83,15 +89,15 @@ struct Smem {
   static constexpr int K0 = Q + (D / 64) * SUB;
   static constexpr int V0 = K0 + 2 * (D / 64) * SUB;
   static constexpr int P = V0 + 2 * (D / 64) * SUB;   // two P buffers of 2 sub-tiles each
-  static constexpr int MK = P + 4 * SUB;                // int4[64] key metadata staging (PARTIAL tiles)
-  static constexpr int BAR = MK + 64 * 16;
+  static constexpr int XCH = P + 4 * SUB;               // float[2 halves][128 rows]: half-row max / sum exchange
+  static constexpr int BAR = XCH + 2 * 128 * 4;
   static constexpr int TOTAL = BAR + 256;
 };
 
 __device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(n) : "memory"); }
 
 template <int D>
-__global__ void __launch_bounds__(NTHREADS, 1)
+__global__ void __launch_bounds__(FWD_THREADS, 1)
     fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, const Params p) {
   using S = Smem<D>;
@@ -127,7 +133,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     mbar_init(&kv_empty[1], 1);
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
-    mbar_init(p_full, BM);
+    mbar_init(p_full, 2 * BM);
     mbar_init(&pv_done[0], 1);
     mbar_init(&pv_done[1], 1);
     mbar_init(drain, 1);
@@ -141,7 +147,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint32_t tS[2] = {tmem, tmem + 128};
   const uint32_t tO = tmem + 256;
 
-  if (warp == 5) {
+  if (warp == 9) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       prefetch_tmap(&tmQ);
@@ -164,7 +170,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       // drain: the last (up to two) loads must have landed before the CTA can retire
       for (int i = (n > 2 ? n - 2 : 0); i < n; ++i) mbar_wait(&kv_full[i & 1], (i >> 1) & 1, p.err, 2);
     }
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16_f32(BM, BN, 0, 0);
@@ -215,11 +221,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_wait(drain, 0, p.err, 7);
     }
   } else {
-    // ---------------- softmax / correction / epilogue (warps 0-3) ----------------
-    const int r = threadIdx.x;              // query row within the tile == TMEM lane
+    // ---------------- softmax / correction / epilogue (warps 0-7) ----------------
+    const int half = warp >> 2;             // columns [64 half, 64 half + 64) of the tile
+    const int r = (warp & 3) * 32 + lane;   // query row within the tile == TMEM lane
     const int row = qt * BM + r;
+    const int bar_id = 1 + (warp & 3);      // named barrier of warps (w, w + 4)
     const int4 mq = row < p.T ? p.meta[(int64_t)b * p.T + row] : make_int4(INT_MAX, INT_MAX, -3, SEG_PAD);
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    float* xch = reinterpret_cast<float*>(smem + S::XCH);
     float m_run = -INFINITY, l_run = 0.f;
     unsigned char* sP = smem + S::P;
     bool ok = true;
@@ -228,98 +237,108 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int entry = list[i];
       const int kt = entry & 0x3fff;
       const bool partial = (entry >> 14) != CLS_FULL;
-      uint32_t bits[BN / 32];
+      uint32_t bits[2];
       if (partial) {
         const uint4 w = p.tmask[(((int64_t)b * nq + qt) * p.nk + kt) * BM + r];
-        bits[0] = w.x; bits[1] = w.y; bits[2] = w.z; bits[3] = w.w;
+        bits[0] = half ? w.z : w.x;
+        bits[1] = half ? w.w : w.y;
       }
-      if (!(ok = mbar_wait(&s_full[s], (i >> 1) & 1, p.err, 8))) break;
-      if (r == 0 && i < 6) DBG_STAMP(30 + 5 * i);
-      tc_fence_after();
-      float sv[BN];
-      {
-        uint32_t t[BN / 32][32];
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS[s] + lane_off + c * 32, t[c]);
+      if (ok) ok = mbar_wait(&s_full[s], (i >> 1) & 1, p.err, 8);
+      float sv[64];
+      float mx = -INFINITY;
+      if (ok) {
+        tc_fence_after();
+        uint32_t t[2][32];
+        tmem_ld32(tS[s] + lane_off + half * 64, t[0]);
+        tmem_ld32(tS[s] + lane_off + half * 64 + 32, t[1]);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
           for (int j = 0; j < 32; ++j) sv[c * 32 + j] = __uint_as_float(t[c][j]);
+        if (partial) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (!((bits[c >> 5] >> (c & 31)) & 1u)) sv[c] = -INFINITY;
+        }
+        float mxp[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mxp[u] = sv[u];
+#pragma unroll
+        for (int c = 8; c < 64; ++c) mxp[c & 7] = fmaxf(mxp[c & 7], sv[c]);
+        mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                   fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
       }
-      if (partial) {
-#pragma unroll
-        for (int c = 0; c < BN; ++c)
-          if (!((bits[c >> 5] >> (c & 31)) & 1u)) sv[c] = -INFINITY;
-      }
-      if (r == 0 && i < 6) DBG_STAMP(31 + 5 * i);
-      float mxp[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) mxp[u] = sv[u];
-#pragma unroll
-      for (int c = 8; c < BN; ++c) mxp[c & 7] = fmaxf(mxp[c & 7], sv[c]);
-      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+      // row max over both halves (the pair meets the barrier even after a timed-out wait)
+      xch[half * BM + r] = mx;
+      named_sync(bar_id, 64);
+      mx = fmaxf(mx, xch[(1 - half) * BM + r]);
+      named_sync(bar_id, 64);                           // both read before the next tile's write
       const float mx_s = mx * p.scale_log2;
       const bool grow = mx_s > m_run + RESCALE_THRESHOLD || (m_run == -INFINITY && mx_s > -INFINITY);
       // The P buffer (i & 1) was last read by PV_{i-2}; O may be rescaled only after PV_{i-1}
       // (MMAs complete in issue order, so PV_{i-1} done implies PV_{i-2} done).
-      if (grow && i > 0) {
-        if (!(ok = mbar_wait(&pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1, p.err, 9))) break;
-        tc_fence_after();
-      } else if (i >= 2) {
-        if (!(ok = mbar_wait(&pv_done[i & 1], ((i - 2) >> 1) & 1, p.err, 11))) break;
-        tc_fence_after();
+      if (ok) {
+        if (grow && i > 0) {
+          ok = mbar_wait(&pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1, p.err, 9);
+          tc_fence_after();
+        } else if (i >= 2) {
+          ok = mbar_wait(&pv_done[i & 1], ((i - 2) >> 1) & 1, p.err, 11);
+          tc_fence_after();
+        }
       }
       if (grow) {
-        if (i > 0 && m_run != -INFINITY) {
+        if (ok && i > 0 && m_run != -INFINITY) {
           const float alpha = exp2f(m_run - mx_s);
           l_run *= alpha;
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < D / 64; ++c) {            // this half's D / 2 columns of the O row
             uint32_t t[32];
-            tmem_ld32(tO + lane_off + c * 32, t);
+            const uint32_t col = tO + lane_off + half * (D / 2) + c * 32;
+            tmem_ld32(col, t);
             tmem_wait_ld();
 #pragma unroll
             for (int j = 0; j < 32; ++j) t[j] = __float_as_uint(__uint_as_float(t[j]) * alpha);
-            tmem_st32(tO + lane_off + c * 32, t);
+            tmem_st32(col, t);
           }
           tmem_wait_st();
         }
         m_run = mx_s;
       }
-      if (r == 0 && i < 6) DBG_STAMP(32 + 5 * i);
-      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-      float rsp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      unsigned char* pbuf = sP + (i & 1) * 2 * S::SUB;
+      if (ok) {
+        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+        float rsp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        unsigned char* pbuf = sP + (i & 1) * 2 * S::SUB + half * S::SUB;
 #pragma unroll
-      for (int c8 = 0; c8 < BN / 8; ++c8) {
-        float pv[8];
+        for (int c8 = 0; c8 < 8; ++c8) {
+          float pv[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          pv[j] = fast_exp2(sv[c8 * 8 + j] * p.scale_log2 - m_use);
-          rsp[j] += pv[j];
+          for (int j = 0; j < 8; ++j) {
+            pv[j] = fast_exp2(sv[c8 * 8 + j] * p.scale_log2 - m_use);
+            rsp[j] += pv[j];
+          }
+          store8(reinterpret_cast<bf16*>(pbuf + sw128_offset(r, c8 * 8)), pv);
         }
-        const int col = c8 * 8;
-        store8(reinterpret_cast<bf16*>(pbuf + (col >> 6) * S::SUB + sw128_offset(r, col & 63)), pv);
+        l_run += ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
+        fence_async_smem();
       }
-      const float rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
-      l_run += rs;
-      fence_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
-      if (r == 0 && i < 6) DBG_STAMP(33 + 5 * i);
     }
     if (ok && n > 0) ok = mbar_wait(&pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1, p.err, 10);
+    // row sum over both halves
+    xch[half * BM + r] = l_run;
+    named_sync(bar_id, 64);
+    const float l_tot = l_run + xch[(1 - half) * BM + r];
     if (ok && n > 0) {
       tc_fence_after();
       if (row < p.T) {
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        bf16* go = p.o + (int64_t)b * p.o_b + (int64_t)row * p.o_tok + (int64_t)h * D;
+        const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+        bf16* go = p.o + (int64_t)b * p.o_b + (int64_t)row * p.o_tok + (int64_t)h * D + half * (D / 2);
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < D / 64; ++c) {
           uint32_t t[32];
-          tmem_ld32(tO + lane_off + c * 32, t);
+          tmem_ld32(tO + lane_off + half * (D / 2) + c * 32, t);
           tmem_wait_ld();
 #pragma unroll
           for (int j8 = 0; j8 < 4; ++j8) {
@@ -329,8 +348,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             store8(go + c * 32 + j8 * 8, f);
           }
         }
-        p.lse[((int64_t)b * p.Hq + h) * p.T + row] =
-            (m_run == -INFINITY) ? -INFINITY : (m_run + log2f(l_run)) * 0.69314718055994530942f;
+        if (half == 0)
+          p.lse[((int64_t)b * p.Hq + h) * p.T + row] =
+              (m_run == -INFINITY) ? -INFINITY : (m_run + log2f(l_tot)) * 0.69314718055994530942f;
       }
     }
   }
@@ -381,7 +401,7 @@ static int launch(const AttnTensors& t, const Params& p, int nq, cudaStream_t s)
     cudaFuncSetAttribute(fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     init = true;
   }
-  fwd_kernel<D><<<dim3(nq, t.Hq, t.B), NTHREADS, smem, s>>>(mq, mk, mv, p);
+  fwd_kernel<D><<<dim3(nq, t.Hq, t.B), FWD_THREADS, smem, s>>>(mq, mk, mv, p);
   return 0;
 }
 
