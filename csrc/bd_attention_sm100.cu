@@ -106,14 +106,18 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   // keeps the shared address space and emits LDS/STS instead of generic loads/stores.
   unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR);
+  // K and V have rings of their own: a K slot is free once its S MMA has run, a V slot once its PV
+  // MMA has, so K_{i+1} streams in while the softmax of tile i runs instead of after PV_{i-1}.
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;    // [2]
-  uint64_t* kv_empty = bars + 3;   // [2]
+  uint64_t* k_full = bars + 1;     // [2]
+  uint64_t* k_empty = bars + 3;    // [2]
   uint64_t* s_full = bars + 5;     // [2]
   uint64_t* p_full = bars + 7;
   uint64_t* pv_done = bars + 8;    // [2]: PV_j completes pv_done[j & 1] (completion number j >> 1)
   uint64_t* drain = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* v_full = bars + 11;    // [2]
+  uint64_t* v_empty = bars + 13;   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h / p.group;
@@ -127,10 +131,12 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   if (threadIdx.x == 0) {
     DBG_STAMP(0);
     mbar_init(q_full, 1);
-    mbar_init(&kv_full[0], 1);
-    mbar_init(&kv_full[1], 1);
-    mbar_init(&kv_empty[0], 1);
-    mbar_init(&kv_empty[1], 1);
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(&k_full[j], 1);
+      mbar_init(&k_empty[j], 1);
+      mbar_init(&v_full[j], 1);
+      mbar_init(&v_empty[j], 1);
+    }
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
     mbar_init(p_full, 2 * BM);
@@ -156,19 +162,26 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       mbar_expect_tx(q_full, (D / 64) * S::SUB);
 #pragma unroll
       for (int c = 0; c < D / 64; ++c) tma_load_4d(smem + S::Q + c * S::SUB, &tmQ, q_full, c * 64, h, qt * BM, b);
-      for (int i = 0; i < n; ++i) {
+      bool ok = true;
+      for (int i = 0; ok && i < n; ++i) {
         const int s = i & 1;
-        if (i >= 2 && !mbar_wait(&kv_empty[s], ((i - 2) >> 1) & 1, p.err, 1)) break;
         const int kt = list[i] & 0x3fff;
-        mbar_expect_tx(&kv_full[s], 2 * (D / 64) * S::SUB);
+        if (i >= 2 && !(ok = mbar_wait(&k_empty[s], ((i - 2) >> 1) & 1, p.err, 1))) break;
+        mbar_expect_tx(&k_full[s], (D / 64) * S::SUB);
 #pragma unroll
-        for (int c = 0; c < D / 64; ++c) {
-          tma_load_4d(smem + S::K0 + (s * (D / 64) + c) * S::SUB, &tmK, &kv_full[s], c * 64, hk, kt * BN, b);
-          tma_load_4d(smem + S::V0 + (s * (D / 64) + c) * S::SUB, &tmV, &kv_full[s], c * 64, hk, kt * BN, b);
-        }
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_4d(smem + S::K0 + (s * (D / 64) + c) * S::SUB, &tmK, &k_full[s], c * 64, hk, kt * BN, b);
+        if (i >= 2 && !(ok = mbar_wait(&v_empty[s], ((i - 2) >> 1) & 1, p.err, 12))) break;
+        mbar_expect_tx(&v_full[s], (D / 64) * S::SUB);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_4d(smem + S::V0 + (s * (D / 64) + c) * S::SUB, &tmV, &v_full[s], c * 64, hk, kt * BN, b);
       }
       // drain: the last (up to two) loads must have landed before the CTA can retire
-      for (int i = (n > 2 ? n - 2 : 0); i < n; ++i) mbar_wait(&kv_full[i & 1], (i >> 1) & 1, p.err, 2);
+      for (int i = (n > 2 ? n - 2 : 0); ok && i < n; ++i) {
+        mbar_wait(&k_full[i & 1], (i >> 1) & 1, p.err, 2);
+        mbar_wait(&v_full[i & 1], (i >> 1) & 1, p.err, 2);
+      }
     }
   } else if (warp == 8) {
     // ---------------- MMA issuer ----------------
@@ -180,6 +193,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       bool ok = mbar_wait(q_full, 0, p.err, 3);
       DBG_STAMP(1);
       auto issue_pv = [&](int j) {
+        if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, p.err, 13)) return false;
+        tc_fence_after();
         const uint32_t vbase = sV + (j & 1) * (D / 64) * S::SUB;
         const uint32_t pbase = sP + (j & 1) * 2 * S::SUB;
 #pragma unroll
@@ -189,11 +204,12 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
           umma_f16(tO, a, bd, idPV, (j > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&pv_done[j & 1]);
-        umma_commit(&kv_empty[j & 1]);
+        umma_commit(&v_empty[j & 1]);
+        return true;
       };
       for (int i = 0; ok && i < n; ++i) {
         const int s = i & 1;
-        if (!(ok = mbar_wait(&kv_full[s], (i >> 1) & 1, p.err, 4))) break;
+        if (!(ok = mbar_wait(&k_full[s], (i >> 1) & 1, p.err, 4))) break;
         if (i < 6) DBG_STAMP(2 + 4 * i);
         tc_fence_after();
         const uint32_t kbase = sK + s * (D / 64) * S::SUB;
@@ -204,12 +220,13 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
           umma_f16(tS[s], a, bd, idS, k > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[s]);
+        umma_commit(&k_empty[s]);
         if (i < 6) DBG_STAMP(3 + 4 * i);
         if (i > 0) {
           if (!(ok = mbar_wait(p_full, (i - 1) & 1, p.err, 5))) break;
           if (i < 6) DBG_STAMP(4 + 4 * i);
           tc_fence_after();
-          issue_pv(i - 1);
+          if (!(ok = issue_pv(i - 1))) break;
         }
       }
       if (ok && n > 0 && mbar_wait(p_full, (n - 1) & 1, p.err, 6)) {
