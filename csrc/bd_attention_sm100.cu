@@ -96,10 +96,18 @@ struct Smem {
 
 __device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(n) : "memory"); }
 
+// TMA tensor store of one staged [128 rows][64 bf16] swizzled sub-tile (rows past T are clipped).
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];\n" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_addr(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
 template <int D>
 __global__ void __launch_bounds__(FWD_THREADS, 1)
     fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-               const __grid_constant__ CUtensorMap tmV, const Params p) {
+               const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, const Params p) {
   using S = Smem<D>;
   extern __shared__ unsigned char smem_raw[];
   // Align by pointer arithmetic on the __shared__ array (not an integer round-trip) so the compiler
@@ -261,6 +269,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         bits[1] = half ? w.w : w.y;
       }
       if (ok) ok = mbar_wait(&s_full[s], (i >> 1) & 1, p.err, 8);
+      if (threadIdx.x == 0 && i < 6) DBG_STAMP(30 + 5 * i);
       float sv[64];
       float mx = -INFINITY;
       if (ok) {
@@ -291,6 +300,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       named_sync(bar_id, 64);
       mx = fmaxf(mx, xch[(1 - half) * BM + r]);
       named_sync(bar_id, 64);                           // both read before the next tile's write
+      if (threadIdx.x == 0 && i < 6) DBG_STAMP(31 + 5 * i);
       const float mx_s = mx * p.scale_log2;
       const bool grow = mx_s > m_run + RESCALE_THRESHOLD || (m_run == -INFINITY && mx_s > -INFINITY);
       // The P buffer (i & 1) was last read by PV_{i-2}; O may be rescaled only after PV_{i-1}
@@ -304,6 +314,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
           tc_fence_after();
         }
       }
+      if (threadIdx.x == 0 && i < 6) DBG_STAMP(32 + 5 * i);
       if (grow) {
         if (ok && i > 0 && m_run != -INFINITY) {
           const float alpha = exp2f(m_run - mx_s);
@@ -341,34 +352,46 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       }
       tc_fence_before();
       mbar_arrive(p_full);
+      if (threadIdx.x == 0 && i < 6) DBG_STAMP(33 + 5 * i);
     }
     if (ok && n > 0) ok = mbar_wait(&pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1, p.err, 10);
+    if (threadIdx.x == 0) DBG_STAMP(60);
     // row sum over both halves
     xch[half * BM + r] = l_run;
     named_sync(bar_id, 64);
     const float l_tot = l_run + xch[(1 - half) * BM + r];
-    if (ok && n > 0) {
+    // epilogue: O / l staged as bf16 in the (now idle) P buffer in the swizzled layout of the O
+    // tensor map, then written by TMA as whole 128-row sub-tiles (coalesced; rows past T clipped)
+    const bool store = ok && n > 0;
+    if (store) {
       tc_fence_after();
-      if (row < p.T) {
-        const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
-        bf16* go = p.o + (int64_t)b * p.o_b + (int64_t)row * p.o_tok + (int64_t)h * D + half * (D / 2);
+      const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
 #pragma unroll
-        for (int c = 0; c < D / 64; ++c) {
-          uint32_t t[32];
-          tmem_ld32(tO + lane_off + half * (D / 2) + c * 32, t);
-          tmem_wait_ld();
+      for (int c = 0; c < D / 64; ++c) {
+        uint32_t t[32];
+        tmem_ld32(tO + lane_off + half * (D / 2) + c * 32, t);
+        tmem_wait_ld();
 #pragma unroll
-          for (int j8 = 0; j8 < 4; ++j8) {
-            float f[8];
+        for (int j8 = 0; j8 < 4; ++j8) {
+          float f[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(t[j8 * 8 + j]) * inv;
-            store8(go + c * 32 + j8 * 8, f);
-          }
+          for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(t[j8 * 8 + j]) * inv;
+          const int col = half * (D / 2) + c * 32 + j8 * 8;
+          store8(reinterpret_cast<bf16*>(sP + (col >> 6) * S::SUB + sw128_offset(r, col & 63)), f);
         }
-        if (half == 0)
-          p.lse[((int64_t)b * p.Hq + h) * p.T + row] =
-              (m_run == -INFINITY) ? -INFINITY : (m_run + log2f(l_tot)) * 0.69314718055994530942f;
       }
+      if (half == 0 && row < p.T)
+        p.lse[((int64_t)b * p.Hq + h) * p.T + row] =
+            (m_run == -INFINITY) ? -INFINITY : (m_run + log2f(l_tot)) * 0.69314718055994530942f;
+      fence_async_smem();
+    }
+    named_sync(5, 256);                                 // the whole O tile is staged
+    if (threadIdx.x == 0 && store) {
+      if (threadIdx.x == 0) DBG_STAMP(61);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) tma_store_4d(&tmO, sP + c * S::SUB, c * 64, h, qt * BM, b);
+      asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+      asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
     }
   }
   tc_fence_before();
@@ -408,17 +431,18 @@ static bool make_map(CUtensorMap* m, const void* base, int B, int T, int H, int 
 
 template <int D>
 static int launch(const AttnTensors& t, const Params& p, int nq, cudaStream_t s) {
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mo;
   if (!make_map(&mq, t.q, t.B, t.T, t.Hq, D, t.q_tok, t.q_b)) return -2;
   if (!make_map(&mk, t.k, t.B, t.T, t.Hkv, D, t.k_tok, t.k_b)) return -3;
   if (!make_map(&mv, t.v, t.B, t.T, t.Hkv, D, t.v_tok, t.v_b)) return -4;
+  if (!make_map(&mo, t.o, t.B, t.T, t.Hq, D, t.o_tok, t.o_b)) return -5;
   const int smem = Smem<D>::TOTAL + 1024;
   static bool init = false;
   if (!init) {
     cudaFuncSetAttribute(fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     init = true;
   }
-  fwd_kernel<D><<<dim3(nq, t.Hq, t.B), FWD_THREADS, smem, s>>>(mq, mk, mv, p);
+  fwd_kernel<D><<<dim3(nq, t.Hq, t.B), FWD_THREADS, smem, s>>>(mq, mk, mv, mo, p);
   return 0;
 }
 
