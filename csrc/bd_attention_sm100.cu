@@ -465,6 +465,7 @@ struct BwdParams {
   bf16 *dk, *dv;
   int64_t dk_tok, dk_b, dv_tok, dv_b;
   float* dq_acc;            // [B, T, Hq, D] fp32, pre-zeroed
+  float *dk_acc, *dv_acc;   // [B, T, Hkv, D] fp32, pre-zeroed (partials of the group's query heads)
   const float *lse, *dsum;  // [B, Hq, T]
   const int4* meta;
   const int16_t* list;      // [B, nk128, nq128] entries qt | cls << 14
@@ -520,7 +521,8 @@ template <int D>
 __global__ void __launch_bounds__(NTHREADS, 1)
     bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-               const __grid_constant__ CUtensorMap tmDQ, const BwdParams p) {
+               const __grid_constant__ CUtensorMap tmDQ, const __grid_constant__ CUtensorMap tmDK,
+               const __grid_constant__ CUtensorMap tmDV, const BwdParams p) {
   using S = BwdSmem<D>;
   extern __shared__ unsigned char smem_raw[];
   // Align by pointer arithmetic on the __shared__ array (not an integer round-trip) so the compiler
@@ -540,16 +542,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   float* sDs = reinterpret_cast<float*>(smem + S::DS);
   int4* sMq = reinterpret_cast<int4*>(smem + S::MQ);
 
-  const int kt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  // one CTA per (key tile, query head): the GQA group's heads are separate CTAs whose dK / dV
+  // partials meet in fp32 accumulators (TMA reduce-add), so no CTA walks group x query tiles
+  const int kt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / p.group;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = gridDim.x;
   const int lidx = b * nk + kt;
   const int nqt = p.cnt[lidx];
   const int16_t* list = p.list + (int64_t)lidx * p.nq;
-  const int total = nqt * p.group;
-  // CTAs of neighbouring key tiles start their walk at different (head, query tile) pairs so
-  // their dQ reductions land on different rows at any moment.
-  const int rot = total > 0 ? (kt * 7 + hk * 3) % total : 0;
+  const int total = nqt;
+  // CTAs of neighbouring key tiles start their walk at different query tiles so their dQ
+  // reductions land on different rows at any moment.
+  const int rot = total > 0 ? (kt * 7 + h * 3) % total : 0;
   const int cta_id = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
 
   if (threadIdx.x == 0) {
@@ -586,8 +591,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int j = 0; j < total; ++j) {
         if (j > 0 && !mbar_wait(q_empty, (j - 1) & 1, p.err, 21)) break;
         const int jj = (j + rot) % total;
-        const int h = hk * p.group + jj / nqt;
-        const int qt = list[jj % nqt] & 0x3fff;
+        const int qt = list[jj] & 0x3fff;
         mbar_expect_tx(q_full, 2 * (D / 64) * S::SUB);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
@@ -652,10 +656,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     bool ok = true;
     for (int j = 0; j < total; ++j) {
       const int jj = (j + rot) % total;
-      const int h = hk * p.group + jj / nqt;
-      const int entry = list[jj % nqt];
+      const int entry = list[jj];
       const int qt = entry & 0x3fff;
       const bool partial = (entry >> 14) != CLS_FULL;
+      if (r == 0) bulk_wait_read();   // the previous pair's dQ reductions have read PT / DST
       {  // stage this query tile's LSE (log2 domain), Dsum and metadata
         const int q = qt * 128 + r;
         const int64_t li = ((int64_t)b * p.Hq + h) * p.T + q;
@@ -718,65 +722,68 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (!(ok = mbar_wait(dq_full, j & 1, p.err, 29))) break;
       if (r == 0 && j < 6) DBG_STAMP(43 + 4 * j);
       tc_fence_after();
-      // dQ rows: thread r owns query qt*128 + r; each 32-column chunk goes TMEM -> registers ->
-      // 128B-swizzled smem staging -> ONE TMA tensor reduction (fp32 add) for all 128 rows.
-      unsigned char* stage = smem + S::DQS;
+      // dQ rows: thread r owns query qt*128 + r.  All D/32 chunks go TMEM -> registers -> the
+      // P^T / dS^T buffers (idle until the next pair's softmax; 16 KB 128B-swizzled fp32 chunks)
+      // -> D/32 TMA tensor reductions (fp32 add) issued together after one barrier.
+      unsigned char* stage = smem + S::PT;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t t[32];
         tmem_ld32(tS + lane_off + c * 32, t);
-        if (r == 0) bulk_wait_read();   // the previous chunk's reduction has read the staging tile
-        named_bar_sync(1, 128);
         tmem_wait_ld();
+        unsigned char* sc = stage + c * (128 * 128);
 #pragma unroll
         for (int u = 0; u < 8; ++u)
-          *reinterpret_cast<float4*>(stage + r * 128 + ((u ^ (r & 7)) << 4)) =
+          *reinterpret_cast<float4*>(sc + r * 128 + ((u ^ (r & 7)) << 4)) =
               make_float4(__uint_as_float(t[u * 4]) * p.scale, __uint_as_float(t[u * 4 + 1]) * p.scale,
                           __uint_as_float(t[u * 4 + 2]) * p.scale, __uint_as_float(t[u * 4 + 3]) * p.scale);
+      }
+      tc_fence_before();
+      mbar_arrive(dq_free);                              // TMEM [0,128) may take the next S^T
+      fence_async_smem();
+      named_bar_sync(1, 128);
+      if (r == 0) {
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) tma_reduce_add_4d(&tmDQ, stage + c * (128 * 128), c * 32, h, qt * 128, b);
+        bulk_commit();
+      }
+    }
+    if (r == 0) DBG_STAMP(62);
+    if (r == 0) bulk_wait_read();   // the last dQ reductions have read PT / DST
+    named_bar_sync(1, 128);
+    if (ok && total > 0) {
+      // dK (x scale) and dV partials of this query head: staged like dQ, added by TMA into the
+      // fp32 accumulators shared by the group's heads (rows past T are clipped by the map)
+      unsigned char* stage = smem + S::PT;
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which) {
+        const uint32_t src = which == 0 ? tDK : tDV;
+        const float mul = which == 0 ? p.scale : 1.f;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t t[32];
+          tmem_ld32(src + lane_off + c * 32, t);
+          tmem_wait_ld();
+          unsigned char* sc = stage + c * (128 * 128);
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<float4*>(sc + r * 128 + ((u ^ (r & 7)) << 4)) =
+                make_float4(__uint_as_float(t[u * 4]) * mul, __uint_as_float(t[u * 4 + 1]) * mul,
+                            __uint_as_float(t[u * 4 + 2]) * mul, __uint_as_float(t[u * 4 + 3]) * mul);
+        }
         fence_async_smem();
         named_bar_sync(1, 128);
         if (r == 0) {
-          tma_reduce_add_4d(&tmDQ, stage, c * 32, h, qt * 128, b);
-          bulk_commit();
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(dq_free);
-    }
-    if (r == 0) DBG_STAMP(62);
-    if (r == 0) bulk_wait_all();   // every dQ reduction issued by this CTA has completed
-    if (ok && total > 0 && krow < p.T) {
-      // all MMAs finished: dq_full of the last pair was observed above
-      bf16* gdk = p.dk + (int64_t)b * p.dk_b + (int64_t)krow * p.dk_tok + (int64_t)hk * D;
-      bf16* gdv = p.dv + (int64_t)b * p.dv_b + (int64_t)krow * p.dv_tok + (int64_t)hk * D;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t tk[32], tv[32];
-        tmem_ld32(tDK + lane_off + c * 32, tk);
-        tmem_ld32(tDV + lane_off + c * 32, tv);
-        tmem_wait_ld();
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          float fk[8], fv[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            fk[e] = __uint_as_float(tk[u * 8 + e]) * p.scale;
-            fv[e] = __uint_as_float(tv[u * 8 + e]);
-          }
-          store8(gdk + c * 32 + u * 8, fk);
-          store8(gdv + c * 32 + u * 8, fv);
+          for (int c = 0; c < D / 32; ++c)
+            tma_reduce_add_4d(which == 0 ? &tmDK : &tmDV, stage + c * (128 * 128), c * 32, hk, kt * 128, b);
+          bulk_commit();
+          bulk_wait_read();
         }
-      }
-    } else if (ok && total == 0 && krow < p.T) {
-      // a key tile nobody attends to (possible only for padding): zero gradients
-      bf16* gdk = p.dk + (int64_t)b * p.dk_b + (int64_t)krow * p.dk_tok + (int64_t)hk * D;
-      bf16* gdv = p.dv + (int64_t)b * p.dv_b + (int64_t)krow * p.dv_tok + (int64_t)hk * D;
-      float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int c = 0; c < D; c += 8) {
-        store8(gdk + c, z);
-        store8(gdv + c, z);
+        named_bar_sync(1, 128);
       }
     }
+    if (r == 0) bulk_wait_all();    // every reduction issued by this CTA has completed
   }
   tc_fence_before();
   __syncthreads();
@@ -802,8 +809,10 @@ static bool make_map_f32(CUtensorMap* m, const void* base, int B, int T, int H, 
 template <int D>
 static int launch_bwd(const AttnTensors& t, const bf16* dout, int64_t do_tok, int64_t do_b, const BwdParams& p,
                       int nk, cudaStream_t s) {
-  CUtensorMap mq, mk, mv, mdo, mdq;
+  CUtensorMap mq, mk, mv, mdo, mdq, mdk, mdv;
   if (!make_map_f32(&mdq, p.dq_acc, t.B, t.T, t.Hq, D)) return -6;
+  if (!make_map_f32(&mdk, p.dk_acc, t.B, t.T, t.Hkv, D)) return -7;
+  if (!make_map_f32(&mdv, p.dv_acc, t.B, t.T, t.Hkv, D)) return -8;
   if (!make_map(&mq, t.q, t.B, t.T, t.Hq, D, t.q_tok, t.q_b)) return -2;
   if (!make_map(&mk, t.k, t.B, t.T, t.Hkv, D, t.k_tok, t.k_b)) return -3;
   if (!make_map(&mv, t.v, t.B, t.T, t.Hkv, D, t.v_tok, t.v_b)) return -4;
@@ -814,7 +823,7 @@ static int launch_bwd(const AttnTensors& t, const bf16* dout, int64_t do_tok, in
     cudaFuncSetAttribute(bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     init = true;
   }
-  bwd_kernel<D><<<dim3(nk, t.Hkv, t.B), NTHREADS, smem, s>>>(mq, mk, mv, mdo, mdq, p);
+  bwd_kernel<D><<<dim3(nk, t.Hq, t.B), NTHREADS, smem, s>>>(mq, mk, mv, mdo, mdq, mdk, mdv, p);
   return 0;
 }
 
@@ -880,10 +889,11 @@ __global__ void lists128_kernel(const uint8_t* __restrict__ cls, int B, int nt, 
 }  // namespace attn100
 
 int bd_attn_bwd_sm100(const AttnTensors& t, const bf16* dout, int64_t do_tok, int64_t do_b, const float* dsum,
-                      float* dq_acc, bf16* dk, int64_t dk_tok, int64_t dk_b, bf16* dv, int64_t dv_tok, int64_t dv_b,
-                      const int4* meta, const int16_t* list128t, const int* cnt128t, const uint4* colmask, int flags,
-                      float scale, int* err, cudaStream_t s, long long* dbg) {
+                      float* dq_acc, float* dk_acc, float* dv_acc, bf16* dk, int64_t dk_tok, int64_t dk_b, bf16* dv,
+                      int64_t dv_tok, int64_t dv_b, const int4* meta, const int16_t* list128t, const int* cnt128t,
+                      const uint4* colmask, int flags, float scale, int* err, cudaStream_t s, long long* dbg) {
   attn100::BwdParams p;
+  p.dk_acc = dk_acc; p.dv_acc = dv_acc;
   p.dbg = dbg;
   p.tmask_t = colmask;
   p.dk = dk; p.dv = dv; p.dk_tok = dk_tok; p.dk_b = dk_b; p.dv_tok = dv_tok; p.dv_b = dv_b;

@@ -739,17 +739,24 @@ void bd_attn_bwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tenso
                   ((uintptr_t)dout.data_ptr() % 16) == 0, "dout must be TMA-compatible");
   auto dsum = at::empty({a.B, a.Hq, a.T}, lse.options());
   auto dq_acc = at::empty({a.B, a.T, a.Hq, a.D}, lse.options());
+  // dK / dV partials of the GQA group's query heads meet in fp32 (one CTA per key tile and query head)
+  auto dkv_acc = at::zeros({2, a.B, a.T, a.Hkv, a.D}, lse.options());
+  float* dk_acc = dkv_acc.data_ptr<float>();
+  float* dv_acc = dk_acc + (int64_t)a.B * a.T * a.Hkv * a.D;
   trida::bd_attn_bwd_prep(a, cbf(dout), dout.stride(1), dout.stride(0), dsum.data_ptr<float>(),
                           dq_acc.data_ptr<float>(), stream());
   const int rc = trida::bd_attn_bwd_sm100(a, cbf(dout), dout.stride(1), dout.stride(0), dsum.data_ptr<float>(),
-                                          dq_acc.data_ptr<float>(), mbf(dk), dk.stride(1), dk.stride(0), mbf(dv),
-                                          dv.stride(1), dv.stride(0), reinterpret_cast<const int4*>(meta.data_ptr<int>()),
+                                          dq_acc.data_ptr<float>(), dk_acc, dv_acc, mbf(dk), dk.stride(1), dk.stride(0),
+                                          mbf(dv), dv.stride(1), dv.stride(0),
+                                          reinterpret_cast<const int4*>(meta.data_ptr<int>()),
                                           list128t.data_ptr<int16_t>(), cnt128t.data_ptr<int>(),
                                           reinterpret_cast<const uint4*>(colmask.data_ptr<int>()), (int)flags,
                                           (float)scale, err.data_ptr<int>(), stream(), pdbg);
   TORCH_CHECK(rc == 0, "bd_attn_bwd_sm100 failed (code ", rc, ", head_dim ", a.D, ")");
   trida::bd_attn_dq_convert(dq_acc.data_ptr<float>(), mbf(dq), dq.stride(1), dq.stride(0), a.B, a.T, a.Hq, a.D,
                             sm_count(), stream());
+  trida::bd_attn_dq_convert(dk_acc, mbf(dk), dk.stride(1), dk.stride(0), a.B, a.T, a.Hkv, a.D, sm_count(), stream());
+  trida::bd_attn_dq_convert(dv_acc, mbf(dv), dv.stride(1), dv.stride(0), a.B, a.T, a.Hkv, a.D, sm_count(), stream());
 }
 
 void ce_rows(const at::Tensor& logits, const at::Tensor& target, const c10::optional<at::Tensor>& weight,
