@@ -25,7 +25,7 @@ def load():
 KERNELS_PER_CALL = {
     "gemm": 1, "rmsnorm_fwd": 1, "rmsnorm_bwd": 1, "qk_norm_rope_fwd": 1, "qk_norm_rope_bwd": 1,
     "swiglu_fwd": 1, "swiglu_bwd": 1, "embed_fwd": 1, "embed_bwd": 1, "bd_attn_plan": 2, "bd_attn_fwd": 1,
-    "bd_attn_bwd": 3, "ce_rows": 1, "adamw": 1, "bd_attn_lists128": 1, "bd_attn_fwd_sm100": 1, "bd_attn_bwd_sm100": 3, "bd_attn_tile_masks": 1,
+    "bd_attn_bwd": 3, "ce_rows": 1, "adamw": 1, "bd_attn_lists128": 1, "bd_attn_fwd_sm100": 1, "bd_attn_bwd_sm100": 5, "bd_attn_tile_masks": 1,
     "gemm_error": 0, "gdn_state_numel": 0, "gdn_fwd": 2, "gdn_bwd": 3, "gdn_conv_fwd": 1, "gdn_conv_bwd": 2,
     "gdn_gnorm_fwd": 1, "gdn_gnorm_bwd": 1, "attn_gate_fwd": 1, "attn_gate_bwd": 1,
     "canvas_attention": 2, "kv_append": 1, "canvas_conv": 1, "conv_commit": 1, "gdn_canvas": 2, "gdn_prep_numel": 0, "gdn_commit": 1,
