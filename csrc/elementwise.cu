@@ -1,6 +1,8 @@
 // Bandwidth-bound kernels of the decoder: RMSNorm, per-head q/k RMSNorm + RoPE, SwiGLU,
 // embedding gather/scatter, and residual helpers.  All math in fp32, storage in bf16,
 // 16-byte vector accesses where the row layout allows it.
+#include <initializer_list>
+
 #include "common.cuh"
 #include "ops.h"
 
@@ -93,9 +95,149 @@ __global__ void rmsnorm_bwd_kernel(const bf16* __restrict__ dy, int64_t lddy, co
     }
 }
 
+// Row-per-CTA variants for D = 256 k (<= 8192 forward, <= 5120 backward): D / 8 threads, each owning the same 8 columns of
+// every row it visits (one 16-byte access per tensor and row), grid-stride over rows with the
+// next row's loads issued before the current row's block reduction, so every thread keeps two
+// rows of loads in flight.  The per-row sum goes through a double-buffered shared slot per warp
+// (one barrier per row).  The backward keeps its 8 columns of dw in registers across all rows
+// and adds them once per CTA.
+__device__ __forceinline__ bf16x8 ld_stream8(const bf16* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return *reinterpret_cast<bf16x8*>(&v);
+}
+
+__device__ __forceinline__ void unpack8(const bf16x8& v, float (&f)[8]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(v.h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+// sum of v over the CTA; red holds 2 x 32 floats, par alternates per call
+__device__ __forceinline__ float cta_row_sum(float v, float (*red)[32], int par) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[par][threadIdx.x >> 5] = v;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  float t = 0.f;
+  for (int i = 0; i < nw; ++i) t += red[par][i];
+  return t;
+}
+
+__global__ void __launch_bounds__(1024) rmsnorm_fwd_cta_kernel(const bf16* __restrict__ x, int64_t ldx,
+                                                               const bf16* __restrict__ w, bf16* __restrict__ y,
+                                                               int64_t ldy, float* __restrict__ rstd_out, int M,
+                                                               float eps) {
+  __shared__ float red[2][32];
+  const int D = blockDim.x * 8, e0 = threadIdx.x * 8;
+  float g[8];
+  load8(w + e0, g);
+  int row = blockIdx.x, par = 0;
+  bf16x8 cur = row < M ? ld_stream8(x + (int64_t)row * ldx + e0) : bf16x8{};
+  for (; row < M; row += gridDim.x, par ^= 1) {
+    const int nrow = row + gridDim.x;
+    const bf16x8 nxt = nrow < M ? ld_stream8(x + (int64_t)nrow * ldx + e0) : bf16x8{};
+    float f[8];
+    unpack8(cur, f);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+    const float r = rsqrtf(cta_row_sum(ss, red, par) / (float)D + eps);
+    if (threadIdx.x == 0 && rstd_out) rstd_out[row] = r;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = f[i] * r * g[i];
+    store8(y + (int64_t)row * ldy + e0, f);
+    cur = nxt;
+  }
+}
+
+__global__ void __launch_bounds__(640) rmsnorm_bwd_cta_kernel(const bf16* dy, int64_t lddy, const bf16* x,
+                                                               int64_t ldx, const bf16* __restrict__ w,
+                                                               const float* __restrict__ rstd, const bf16* dres,
+                                                               int64_t lddres, bf16* dx, int64_t lddx,
+                                                               float* __restrict__ dw, int M) {
+  __shared__ float red[2][32];
+  const int D = blockDim.x * 8, e0 = threadIdx.x * 8;
+  float g[8], acc[8];
+  load8(w + e0, g);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  int row = blockIdx.x, par = 0;
+  bf16x8 cx{}, cd{}, cr{};
+  if (row < M) {
+    cx = ld_stream8(x + (int64_t)row * ldx + e0);
+    cd = ld_stream8(dy + (int64_t)row * lddy + e0);
+    if (dres) cr = ld_stream8(dres + (int64_t)row * lddres + e0);
+  }
+  for (; row < M; row += gridDim.x, par ^= 1) {
+    const int nrow = row + gridDim.x;
+    bf16x8 nx{}, nd{}, nr{};
+    if (nrow < M) {
+      nx = ld_stream8(x + (int64_t)nrow * ldx + e0);
+      nd = ld_stream8(dy + (int64_t)nrow * lddy + e0);
+      if (dres) nr = ld_stream8(dres + (int64_t)nrow * lddres + e0);
+    }
+    const float r = rstd[row];
+    float f[8], d[8], o[8];
+    unpack8(cx, f);
+    unpack8(cd, d);
+    if (dres) {
+      unpack8(cr, o);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = 0.f;
+    }
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dot += d[i] * g[i] * f[i];
+    dot = cta_row_sum(dot, red, par) * r / (float)D;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float xh = f[i] * r;
+      o[i] += r * (d[i] * g[i] - xh * dot);
+      acc[i] += d[i] * xh;
+    }
+    store8(dx + (int64_t)row * lddx + e0, o);
+    cx = nx;
+    cd = nd;
+    cr = nr;
+  }
+  if (dw && blockIdx.x < M) {
+    atomicAdd(reinterpret_cast<float4*>(dw + e0), make_float4(acc[0], acc[1], acc[2], acc[3]));
+    atomicAdd(reinterpret_cast<float4*>(dw + e0 + 4), make_float4(acc[4], acc[5], acc[6], acc[7]));
+  }
+}
+
+static int cta_row_blocks(const void* kernel, int threads, int M) {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  int per_sm = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0);
+  const int blocks = sms * (per_sm > 0 ? per_sm : 1);
+  return blocks < M ? blocks : (M > 0 ? M : 1);
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+static bool cta_row_ok(int D, int max_threads) { return D % 256 == 0 && D / 8 <= max_threads; }
+
 void rmsnorm_fwd(const bf16* x, int64_t ldx, const bf16* w, bf16* y, int64_t ldy, float* rstd, int M,
                  int D, float eps, cudaStream_t s) {
   const int warps = 8;
+  if (cta_row_ok(D, 1024) && ldx % 8 == 0 && ldy % 8 == 0 && aligned16(x) && aligned16(y) && aligned16(w)) {
+    const int threads = D / 8;
+    rmsnorm_fwd_cta_kernel<<<cta_row_blocks((const void*)rmsnorm_fwd_cta_kernel, threads, M), threads, 0, s>>>(
+        x, ldx, w, y, ldy, rstd, M, eps);
+    return;
+  }
   rmsnorm_fwd_kernel<<<ceil_div(M, warps), warps * 32, 0, s>>>(x, ldx, w, y, ldy, rstd, M, D, eps);
 }
 
@@ -103,6 +245,14 @@ void rmsnorm_bwd(const bf16* dy, int64_t lddy, const bf16* x, int64_t ldx, const
                  const bf16* dres, int64_t lddres, bf16* dx, int64_t lddx, float* dw, int M, int D,
                  int sm_count, cudaStream_t s) {
   const int warps = 8;
+  if (cta_row_ok(D, 640) && lddy % 8 == 0 && ldx % 8 == 0 && lddx % 8 == 0 && (!dres || lddres % 8 == 0) &&
+      aligned16(dy) && aligned16(x) && aligned16(w) && aligned16(dx) && (!dres || aligned16(dres)) &&
+      (!dw || aligned16(dw))) {
+    const int threads = D / 8;
+    rmsnorm_bwd_cta_kernel<<<cta_row_blocks((const void*)rmsnorm_bwd_cta_kernel, threads, M), threads, 0, s>>>(
+        dy, lddy, x, ldx, w, rstd, dres, lddres, dx, lddx, dw, M);
+    return;
+  }
   const size_t smem = (size_t)warps * D * sizeof(float);
   static size_t configured = 0;
   if (smem > 48 * 1024 && smem > configured) {
@@ -236,11 +386,218 @@ __global__ void qk_norm_rope_bwd_kernel(const bf16* __restrict__ dq, const bf16*
   }
 }
 
+// Vector variants for d in {64, 128, 256} and rd a multiple of 16: one warp per token walks all
+// its heads, d / 8 lanes to a head (8 consecutive elements and one 16-byte access per lane), so
+// 32 / (d / 8) heads move per step and four steps' loads are issued together.  The token's
+// position, its cos / sin values and both norm weights are read once per token.  The RoPE
+// partner of element e < rd/2 is e + rd/2, rd/16 lanes away in the same head, fetched with one
+// shuffle; per-head sums reduce over the head's d / 8 lanes.
+template <int D>
+struct QkLane {
+  static constexpr int LPH = D / 8, HPW = 32 / LPH;
+  int sub, e0, partner;
+  bool roped, first;
+  __device__ QkLane(int lane, int rd) {
+    sub = lane / LPH;
+    const int j = lane % LPH, hl = rd >> 4;
+    e0 = j * 8;
+    roped = e0 < rd;
+    first = e0 < (rd >> 1);
+    partner = sub * LPH + (roped ? (first ? j + hl : j - hl) : j);
+  }
+};
+
+__device__ __forceinline__ void load_rope8(const float* cos_t, const float* sin_t, int64_t base, float (&c)[8],
+                                           float (&sn)[8]) {
+  const float4 c0 = *reinterpret_cast<const float4*>(cos_t + base);
+  const float4 c1 = *reinterpret_cast<const float4*>(cos_t + base + 4);
+  const float4 s0 = *reinterpret_cast<const float4*>(sin_t + base);
+  const float4 s1 = *reinterpret_cast<const float4*>(sin_t + base + 4);
+  c[0] = c0.x; c[1] = c0.y; c[2] = c0.z; c[3] = c0.w; c[4] = c1.x; c[5] = c1.y; c[6] = c1.z; c[7] = c1.w;
+  sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w; sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+}
+
+template <int D>
+__global__ void __launch_bounds__(256) qk_norm_rope_fwd_vec_kernel(
+    const bf16* __restrict__ qkv, int64_t ldqkv, const bf16* __restrict__ qw, const bf16* __restrict__ kw,
+    const float* __restrict__ cos_t, const float* __restrict__ sin_t, const int* __restrict__ pos,
+    bf16* __restrict__ q, bf16* __restrict__ k, float* __restrict__ rstd, int M, int Hq, int Hkv, int rd,
+    float eps, int qstride) {
+  using L = QkLane<D>;
+  constexpr int UNR = 4;
+  const int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (tok >= M) return;  // warp-uniform
+  const L ln(threadIdx.x & 31, rd);
+  const int H = Hq + Hkv, half = rd >> 1;
+  const bool norm = qw != nullptr;
+  float c[8], sn[8], wq[8], wk[8];
+  if (ln.roped) load_rope8(cos_t, sin_t, (int64_t)pos[tok] * half + (ln.first ? ln.e0 : ln.e0 - half), c, sn);
+  if (norm) {
+    load8(qw + ln.e0, wq);
+    load8(kw + ln.e0, wk);
+  }
+  const float sg = ln.first ? -1.f : 1.f;  // first half: x1 c - x2 s;  second half: x2 c + x1 s
+  const bf16* src = qkv + (int64_t)tok * ldqkv + ln.e0;
+  for (int hb = 0; hb < H; hb += L::HPW * UNR) {
+    float f[UNR][8];
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) {
+      const int h = hb + u * L::HPW + ln.sub;
+      if (h < H) {
+        load8(src + (h < Hq ? (int64_t)h * qstride : (int64_t)Hq * qstride + (int64_t)(h - Hq) * D), f[u]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[u][i] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) {
+      const int h = hb + u * L::HPW + ln.sub;
+      const bool is_q = h < Hq;
+      float r = 1.f;
+      if (norm) {
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss += f[u][i] * f[u][i];
+#pragma unroll
+        for (int o = L::LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        r = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[u][i] *= r * (is_q ? wq[i] : wk[i]);
+      }
+      float px[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) px[i] = __shfl_sync(0xffffffffu, f[u][i], ln.partner);
+      if (ln.roped)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[u][i] = f[u][i] * c[i] + sg * px[i] * sn[i];
+      if (h < H) {
+        if (ln.e0 == 0) rstd[(int64_t)tok * H + h] = r;
+        bf16* dst = is_q ? (q + ((int64_t)tok * Hq + h) * D) : (k + ((int64_t)tok * Hkv + (h - Hq)) * D);
+        store8(dst + ln.e0, f[u]);
+      }
+    }
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(256) qk_norm_rope_bwd_vec_kernel(
+    const bf16* __restrict__ dq, const bf16* __restrict__ dk, const bf16* __restrict__ qkv, int64_t ldqkv,
+    const bf16* __restrict__ qw, const bf16* __restrict__ kw, const float* __restrict__ cos_t,
+    const float* __restrict__ sin_t, const int* __restrict__ pos, const float* __restrict__ rstd,
+    bf16* __restrict__ dqkv, int64_t lddqkv, float* __restrict__ dqw, float* __restrict__ dkw, int M, int Hq,
+    int Hkv, int rd, int qstride) {
+  using L = QkLane<D>;
+  constexpr int UNR = 2;
+  __shared__ float sred[8][2][D];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const L ln(lane, rd);
+  const int H = Hq + Hkv, half = rd >> 1;
+  float wq[8], wk[8], accq[8], acck[8];
+  load8(qw + ln.e0, wq);
+  load8(kw + ln.e0, wk);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) accq[i] = acck[i] = 0.f;
+  const float sg = ln.first ? 1.f : -1.f;  // inverse rotation: dn1 = g1 c + g2 s,  dn2 = g2 c - g1 s
+  for (int tok = blockIdx.x * (blockDim.x >> 5) + warp; tok < M; tok += gridDim.x * (blockDim.x >> 5)) {
+    float c[8], sn[8];
+    if (ln.roped) load_rope8(cos_t, sin_t, (int64_t)pos[tok] * half + (ln.first ? ln.e0 : ln.e0 - half), c, sn);
+    const bf16* xrow = qkv + (int64_t)tok * ldqkv + ln.e0;
+    bf16* orow = dqkv + (int64_t)tok * lddqkv + ln.e0;
+    for (int hb = 0; hb < H; hb += L::HPW * UNR) {
+      float g[UNR][8], xs[UNR][8], r[UNR];
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const int h = hb + u * L::HPW + ln.sub;
+        if (h < H) {
+          const bool is_q = h < Hq;
+          load8((is_q ? dq + ((int64_t)tok * Hq + h) * D : dk + ((int64_t)tok * Hkv + (h - Hq)) * D) + ln.e0, g[u]);
+          load8(xrow + (is_q ? (int64_t)h * qstride : (int64_t)Hq * qstride + (int64_t)(h - Hq) * D), xs[u]);
+          r[u] = rstd[(int64_t)tok * H + h];
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) g[u][i] = xs[u][i] = 0.f;
+          r[u] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const int h = hb + u * L::HPW + ln.sub;
+        const bool is_q = h < Hq;
+        float pg[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pg[i] = __shfl_sync(0xffffffffu, g[u][i], ln.partner);
+        if (ln.roped)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) g[u][i] = g[u][i] * c[i] + sg * pg[i] * sn[i];
+        float dot = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          xs[u][i] *= r[u];  // xhat
+          dot += g[u][i] * (is_q ? wq[i] : wk[i]) * xs[u][i];
+        }
+#pragma unroll
+        for (int o = L::LPH / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        dot /= (float)D;
+        if (h < H) {
+          float o[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            o[i] = r[u] * (g[u][i] * (is_q ? wq[i] : wk[i]) - xs[u][i] * dot);
+            const float t = g[u][i] * xs[u][i];
+            if (is_q) accq[i] += t; else acck[i] += t;
+          }
+          store8(orow + (is_q ? (int64_t)h * qstride : (int64_t)Hq * qstride + (int64_t)(h - Hq) * D), o);
+        }
+      }
+    }
+  }
+  // the head groups of a warp own the same columns: fold them, then the warps, then global
+#pragma unroll
+  for (int o = L::LPH; o < 32; o <<= 1)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      accq[i] += __shfl_xor_sync(0xffffffffu, accq[i], o);
+      acck[i] += __shfl_xor_sync(0xffffffffu, acck[i], o);
+    }
+  if (ln.sub == 0)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      sred[warp][0][ln.e0 + i] = accq[i];
+      sred[warp][1][ln.e0 + i] = acck[i];
+    }
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  for (int e = threadIdx.x; e < 2 * D; e += blockDim.x) {
+    float t = 0.f;
+    for (int wi = 0; wi < nw; ++wi) t += sred[wi][e / D][e % D];
+    float* dst = e < D ? (dqw ? dqw + e : nullptr) : (dkw ? dkw + (e - D) : nullptr);
+    if (dst) atomicAdd(dst, t);
+  }
+}
+
+static bool qk_vec_ok(int d, int rd, int64_t ldqkv, int qstride, std::initializer_list<const void*> ptrs) {
+  if (!(d == 64 || d == 128 || d == 256) || rd % 16 != 0 || rd > d || ldqkv % 8 != 0 || qstride % 8 != 0)
+    return false;
+  for (const void* p : ptrs)
+    if (p != nullptr && !aligned16(p)) return false;
+  return true;
+}
+
 void qk_norm_rope_fwd(const bf16* qkv, int64_t ldqkv, const bf16* qw, const bf16* kw, const float* cos_t,
                       const float* sin_t, const int* pos, bf16* q, bf16* k, float* rstd, int M, int Hq,
                       int Hkv, int d, int rd, float eps, int qstride, cudaStream_t s) {
   const int warps = 8;
   const int64_t total = (int64_t)M * (Hq + Hkv);
+  if (qk_vec_ok(d, rd, ldqkv, qstride, {qkv, qw, kw, cos_t, sin_t, q, k})) {
+    const int blocks = ceil_div(M, warps);  // one warp per token
+#define TRIDA_QK_FWD(DD)                                                                                  \
+  qk_norm_rope_fwd_vec_kernel<DD><<<blocks, warps * 32, 0, s>>>(qkv, ldqkv, qw, kw, cos_t, sin_t, pos, q, k, \
+                                                                rstd, M, Hq, Hkv, rd, eps, qstride)
+    if (d == 64) TRIDA_QK_FWD(64); else if (d == 128) TRIDA_QK_FWD(128); else TRIDA_QK_FWD(256);
+#undef TRIDA_QK_FWD
+    return;
+  }
   qk_norm_rope_fwd_kernel<<<ceil_div(total, warps), warps * 32, 0, s>>>(qkv, ldqkv, qw, kw, cos_t, sin_t, pos,
                                                                        q, k, rstd, M, Hq, Hkv, d, rd, eps, qstride);
 }
@@ -251,6 +608,17 @@ void qk_norm_rope_bwd(const bf16* dq, const bf16* dk, const bf16* qkv, int64_t l
                       int Hkv, int d, int rd, int qstride, int sm_count, cudaStream_t s) {
   const int warps = 8;
   const int64_t total = (int64_t)M * (Hq + Hkv);
+  if (qk_vec_ok(d, rd, ldqkv, qstride, {dq, dk, qkv, qw, kw, cos_t, sin_t, dqkv}) && lddqkv % 8 == 0) {
+    int64_t blocks = ceil_div(M, warps * 4);  // one warp per token, about 4 tokens a warp
+    blocks = blocks > sm_count * 6 ? sm_count * 6 : blocks;
+#define TRIDA_QK_BWD(DD)                                                                                   \
+  qk_norm_rope_bwd_vec_kernel<DD><<<(int)blocks, warps * 32, 0, s>>>(dq, dk, qkv, ldqkv, qw, kw, cos_t, sin_t, \
+                                                                     pos, rstd, dqkv, lddqkv, dqw, dkw, M, Hq,  \
+                                                                     Hkv, rd, qstride)
+    if (d == 64) TRIDA_QK_BWD(64); else if (d == 128) TRIDA_QK_BWD(128); else TRIDA_QK_BWD(256);
+#undef TRIDA_QK_BWD
+    return;
+  }
   int blocks = ceil_div(total, warps * 8);
   blocks = blocks > sm_count * 8 ? sm_count * 8 : blocks;
   qk_norm_rope_bwd_kernel<<<blocks, warps * 32, warps * 2 * d * sizeof(float), s>>>(

@@ -54,9 +54,12 @@ def test_gemm_tiles(tile):
     assert rel_err(d, a.float() @ b.float().t()) < 1e-2
 
 
-def test_rmsnorm_fwd_bwd():
+@pytest.mark.parametrize("M,D,res", [(1000, 2560, True), (777, 2560, False), (300, 5120, True), (129, 1536, False),
+                                     (64, 1000, True)])
+def test_rmsnorm_fwd_bwd(M, D, res):
+    """Row-resident kernels (D = 256 k, x / dy kept in registers up to D = 2560, re-read above) and
+    the general loop kernel (D = 1000)."""
     torch.manual_seed(0)
-    M, D = 1000, 2560
     x = torch.randn(M, D, device="cuda", dtype=torch.bfloat16)
     w = (1 + 0.1 * torch.randn(D, device="cuda")).to(torch.bfloat16)
     y = torch.empty_like(x)
@@ -65,20 +68,25 @@ def test_rmsnorm_fwd_bwd():
     wr = w.float().requires_grad_()
     yr = xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + 1e-6) * wr
     assert rel_err(y, yr) < 1e-2
+    torch.testing.assert_close(rstd, torch.rsqrt(x.float().pow(2).mean(-1) + 1e-6), rtol=1e-4, atol=1e-5)
     dy = torch.randn_like(x)
-    dres = torch.randn_like(x)
+    dres = torch.randn_like(x) if res else None
     yr.backward(dy.float())
     dx = torch.empty_like(x)
     dw = torch.zeros(D, device="cuda")
     C().rmsnorm_bwd(dy, x, w, rstd, dres, dx, dw)
-    assert rel_err(dx, xr.grad + dres.float()) < 1e-2
+    assert rel_err(dx, xr.grad + (dres.float() if res else 0)) < 1e-2
     assert rel_err(dw, wr.grad) < 1e-3
 
 
-@pytest.mark.parametrize("d,rd", [(128, 128), (256, 64)])
-def test_qk_norm_rope(d, rd):
+@pytest.mark.parametrize("d,rd,shape", [(128, 128, (2, 96, 4, 2)), (256, 64, (2, 96, 4, 2)),
+                                        (128, 64, (1, 95, 4, 1)), (64, 64, (1, 95, 4, 1)),
+                                        (128, 96, (2, 33, 4, 2)), (128, 72, (2, 33, 4, 2))])
+def test_qk_norm_rope(d, rd, shape):
+    """Vector kernels (d in 64 / 128 / 256, rd a multiple of 16; an odd head count leaves the last
+    warp's second head group empty) and the per-element kernels (rd = 72)."""
     torch.manual_seed(0)
-    B, T, Hq, Hkv = 2, 96, 4, 2
+    B, T, Hq, Hkv = shape
     M = B * T
     qkv = torch.randn(M, (Hq + 2 * Hkv) * d, device="cuda", dtype=torch.bfloat16)
     qw = (1 + 0.1 * torch.randn(d, device="cuda")).to(torch.bfloat16)
@@ -107,6 +115,11 @@ def test_qk_norm_rope(d, rd):
                          dkw, Hq, Hkv, d, rd)
     assert rel_err(dqkv[:, :(Hq + Hkv) * d], src.grad[:, :(Hq + Hkv) * d]) < 1e-2
     assert rel_err(dqw, qwr.grad) < 1e-2 and rel_err(dkw, kwr.grad) < 1e-2
+    # RoPE only (no per-head norm weights): the rotation of the raw q / k
+    C().qk_norm_rope_fwd(qkv, None, None, cos_t, sin_t, pos.int().reshape(-1).contiguous(), q, k, Hq, Hkv, d, rd,
+                         1e-6)
+    assert rel_err(q, R.apply_rope(qs.detach(), cos, sin)) < 1e-2
+    assert rel_err(k, R.apply_rope(ks.detach(), cos, sin)) < 1e-2
 
 
 def test_swiglu():

@@ -4,6 +4,8 @@
     python -m trida_stack_b200.ops.kernel_bench --op attn_fwd|attn_bwd [--rows 4]
     python -m trida_stack_b200.ops.kernel_bench --op gdn_fwd|gdn_bwd [--length 3072]
     python -m trida_stack_b200.ops.kernel_bench --op canvas_attn|canvas_gdn [--requests 64 --blk 7]
+    python -m trida_stack_b200.ops.kernel_bench --op rmsnorm_fwd|rmsnorm_bwd|qk_rope_fwd|qk_rope_bwd|
+                                                     swiglu_fwd|swiglu_bwd [--m 24576 --hidden 2560]
 
 Each run does ``--warmup`` untimed launches, then times ``--iters`` launches and prints one JSON
 line with the mean time, the achieved rate and its fraction of the measured B200 peaks in
@@ -173,15 +175,60 @@ def bench_canvas(a, which):
     return ms, {"state_gbs": nbytes / ms / 1e6}, None, nbytes
 
 
+def bench_elementwise(a):
+    """Bandwidth-bound kernels of a decoder layer on the config-2 shapes (Qwen3-4B: hidden 2560,
+    32 / 8 heads x 128, ffn 9728); bytes are the algorithmic reads + writes of one launch."""
+    from .blocks import rope_tables
+    from ._ext import ext
+    C = ext()
+    M, D, F, Hq, Hkv, d = a.m, a.hidden, a.ffn, a.heads, a.kv_heads, 128
+    bf = dict(device="cuda", dtype=torch.bfloat16)
+    if a.op.startswith("rmsnorm"):
+        x, w = torch.randn(M, D, **bf), torch.ones(D, **bf)
+        y = torch.empty_like(x)
+        _, rstd = C.rmsnorm_fwd(x, w, 1e-6, y)
+        if a.op == "rmsnorm_fwd":
+            return _time(lambda: C.rmsnorm_fwd(x, w, 1e-6, y), a.warmup, a.iters), {}, None, 2 * M * D * 2
+        dy, dres, dx, dw = torch.randn_like(x), torch.randn_like(x), torch.empty_like(x), torch.zeros(D, device="cuda")
+        return (_time(lambda: C.rmsnorm_bwd(dy, x, w, rstd, dres, dx, dw), a.warmup, a.iters), {}, None,
+                4 * M * D * 2)
+    if a.op.startswith("qk_rope"):
+        qkv = torch.randn(M, (Hq + 2 * Hkv) * d, **bf)
+        qw, kw = torch.ones(d, **bf), torch.ones(d, **bf)
+        cos_t, sin_t = rope_tables(4096, d, 1e6, "cuda")
+        pos = (torch.arange(M, device="cuda", dtype=torch.int32) % 4096).contiguous()
+        q, k = torch.empty(M, Hq, d, **bf), torch.empty(M, Hkv, d, **bf)
+        rstd = C.qk_norm_rope_fwd(qkv, qw, kw, cos_t, sin_t, pos, q, k, Hq, Hkv, d, d, 1e-6)
+        qk_bytes = M * (Hq + Hkv) * d * 2
+        if a.op == "qk_rope_fwd":
+            return (_time(lambda: C.qk_norm_rope_fwd(qkv, qw, kw, cos_t, sin_t, pos, q, k, Hq, Hkv, d, d, 1e-6),
+                          a.warmup, a.iters), {}, None, 2 * qk_bytes)
+        dqkv = torch.empty_like(qkv)
+        dqw, dkw = torch.zeros(d, device="cuda"), torch.zeros(d, device="cuda")
+        return (_time(lambda: C.qk_norm_rope_bwd(q, k, qkv, qw, kw, cos_t, sin_t, pos, rstd, dqkv, dqw, dkw, Hq,
+                                                 Hkv, d, d), a.warmup, a.iters), {}, None, 3 * qk_bytes)
+    gu = torch.randn(M, 2 * F, **bf)
+    act = torch.empty(M, F, **bf)
+    if a.op == "swiglu_fwd":
+        return _time(lambda: C.swiglu_fwd(gu, act), a.warmup, a.iters), {}, None, 3 * M * F * 2
+    dgu = torch.empty_like(gu)
+    return _time(lambda: C.swiglu_bwd(act, gu, dgu), a.warmup, a.iters), {}, None, 5 * M * F * 2
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--op", required=True,
-                    choices=["gemm", "attn_fwd", "attn_bwd", "gdn_fwd", "gdn_bwd", "canvas_attn", "canvas_gdn"])
+                    choices=["gemm", "attn_fwd", "attn_bwd", "gdn_fwd", "gdn_bwd", "canvas_attn", "canvas_gdn",
+                             "rmsnorm_fwd", "rmsnorm_bwd", "qk_rope_fwd", "qk_rope_bwd", "swiglu_fwd", "swiglu_bwd"])
     ap.add_argument("--m", type=int, default=24576)
     ap.add_argument("--n", type=int, default=6144)
     ap.add_argument("--k", type=int, default=2560)
     ap.add_argument("--layout", default="tn", choices=["tn", "tt", "nt"])
     ap.add_argument("--tile", type=int, default=0)
+    ap.add_argument("--hidden", type=int, default=2560)
+    ap.add_argument("--ffn", type=int, default=9728)
+    ap.add_argument("--heads", type=int, default=32)
+    ap.add_argument("--kv-heads", type=int, default=8)
     ap.add_argument("--rows", type=int, default=4, help="attention: forward rows (2 views x micro-batch)")
     ap.add_argument("--length", type=int, default=3072, help="gated delta: stream length L")
     ap.add_argument("--requests", type=int, default=64)
@@ -195,6 +242,9 @@ def main():
         ms, extra, flops, nbytes = bench_attn(a, a.op == "attn_bwd")
     elif a.op.startswith("gdn"):
         ms, extra, flops, nbytes = bench_gdn(a, a.op == "gdn_bwd")
+    elif a.op.split("_")[0] in ("rmsnorm", "qk", "swiglu"):
+        ms, extra, flops, nbytes = bench_elementwise(a)
+        extra = {"gbs": nbytes / ms / 1e6}
     else:
         ms, extra, flops, nbytes = bench_canvas(a, a.op)
     pk = _peaks()
