@@ -36,7 +36,7 @@ constexpr int SEG_PAD = 0, SEG_SHARED = 1, SEG_XT = 2, SEG_X0 = 3;
 constexpr int FLAG_X0_TOKEN_CAUSAL = 1, FLAG_WITHIN_BLOCK_CAUSAL = 2;
 constexpr int CLS_FULL = 1;
 constexpr int BM = 128, BN = 128;
-constexpr int NTHREADS = 192;        // backward
+constexpr int NTHREADS = 320;        // backward: 8 softmax-gradient warps + MMA warp + TMA warp
 constexpr int FWD_THREADS = 320;     // forward: 8 softmax warps + MMA warp + TMA warp
 // Lazy O rescaling: the running max is only moved (and O rescaled in TMEM) when a tile's max
 // exceeds it by more than 2^16; until then P = exp2(s - m) <= 65536, far inside bf16/fp32 range,
@@ -448,18 +448,20 @@ static int launch(const AttnTensors& t, const Params& p, int nq, cudaStream_t s)
 
 
 // =================================================================================================
-// Backward.  CTA = one 128-key tile of one KV head; it walks every (query head of the GQA group,
-// non-empty 128-query tile) pair.  Per pair j (thread r of warps 0-3 owns key row r == TMEM lane r):
+// Backward.  CTA = one 128-key tile of one query head; it walks the non-empty 128-query tiles of
+// its key tile.  Per pair j (warps 0-7: thread (g, r) owns key row r == TMEM lane r and query
+// columns [64 g, 64 g + 64)):
 //   MMA1  S^T  = K Q_j^T          -> TMEM [0,128)        (A = K  K-major, B = Q  K-major)
 //   MMA2  dP^T = V dO_j^T         -> TMEM [128,256)      (A = V  K-major, B = dO K-major)
-//   softmax warps, 32 queries at a time: P^T = exp2(S^T*scale*log2e - LSE2[q]) (masked on PARTIAL
-//         tiles), dS^T = P^T * (dP^T - Dsum[q]); both written as bf16 K-major rows to smem.
+//   softmax-gradient warps, 32 queries at a time: P^T = exp2(S^T*scale*log2e - LSE2[q]) (masked
+//         on PARTIAL tiles), dS^T = P^T * (dP^T - Dsum[q]); both written as bf16 K-major rows to smem.
 //   MMA3  dV  += P^T dO_j         -> TMEM [256,256+D)    (A = P^T K-major, B = dO MN-major)
 //   MMA4  dK  += dS^T Q_j         -> TMEM [384,384+D)    (A = dS^T K-major, B = Q MN-major)
 //   MMA5  dQ_j = dS K             -> TMEM [0,128) again  (A = dS MN-major, B = K MN-major)
-//   the same warps read dQ_j rows (thread = query row) and add them (x scale) to an fp32 global
-//   accumulator with vector reductions; then TMEM [0,128) is free for the next S^T.
-// dK (x scale) and dV are written once at the end.  Warp 4 issues MMAs, warp 5 issues TMA.
+//   the same warps stage dQ_j (x scale, fp32) in the idle P^T / dS^T buffers and one thread adds
+//   it to the fp32 dQ accumulator with TMA tensor reductions; TMEM [0,128) is then free again.
+// At the end dK (x scale) and dV are added the same way into fp32 per-KV-head accumulators (the
+// GQA group's query heads are separate CTAs).  Warp 8 issues MMAs, warp 9 issues TMA loads.
 // =================================================================================================
 struct BwdParams {
   bf16 *dk, *dv;
@@ -488,9 +490,7 @@ struct BwdSmem {
   static constexpr int DST = PT + 2 * SUB;
   static constexpr int LSE = DST + 2 * SUB;     // float[128]
   static constexpr int DS = LSE + 512;          // float[128]
-  static constexpr int MQ = DS + 512;           // int4[128]
-  static constexpr int DQS = (MQ + 2048 + 1023) / 1024 * 1024;  // float[128][32] SWIZZLE_128B dQ staging
-  static constexpr int BAR = DQS + 128 * 128;
+  static constexpr int BAR = DS + 512;
   static constexpr int TOTAL = BAR + 256;
 };
 
@@ -540,7 +540,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
   float* sLSE = reinterpret_cast<float*>(smem + S::LSE);
   float* sDs = reinterpret_cast<float*>(smem + S::DS);
-  int4* sMq = reinterpret_cast<int4*>(smem + S::MQ);
 
   // one CTA per (key tile, query head): the GQA group's heads are separate CTAs whose dK / dV
   // partials meet in fp32 accumulators (TMA reduce-add), so no CTA walks group x query tiles
@@ -563,9 +562,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
     mbar_init(sp_full, 1);
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 256);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, 128);
+    mbar_init(dq_free, 256);
     mbar_init(drain, 1);
     fence_barrier_init();
   }
@@ -576,7 +575,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 256 + D;
 
-  if (warp == 5) {
+  if (warp == 9) {
     if (lane == 0) {
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
@@ -601,7 +600,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       if (total > 0) mbar_wait(q_full, (total - 1) & 1, p.err, 22);
     }
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     if (lane == 0) {
       constexpr uint32_t idKK = idesc_bf16_f32(128, 128, 0, 0);   // S^T, dP^T
       constexpr uint32_t idKM = idesc_bf16_f32(128, D, 0, 1);     // dV, dK (B MN-major)
@@ -646,11 +645,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_wait(drain, 0, p.err, 27);
     }
   } else {
-    // ---------------- warps 0-3 ----------------
-    const int r = threadIdx.x;
-    const int krow = kt * 128 + r;
-    const int4 mk = krow < p.T ? p.meta[(int64_t)b * p.T + krow] : make_int4(INT_MAX, INT_MAX, -4, SEG_PAD);
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    // ---------------- warps 0-7: two warpgroups, g = threadIdx.x / 128 ----------------
+    // Thread (g, r) owns key row r (TMEM lane r; warps w and w + 4 share a lane quarter) and the
+    // query columns [64 g, 64 g + 64) of S^T / dP^T, so two warps per SM sub-partition overlap
+    // each other's TMEM loads, exponentials and packing.  The dQ, dK and dV read-outs split their
+    // D / 32 column chunks between the two groups the same way.
+    const int r = threadIdx.x & 127, g = threadIdx.x >> 7;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    constexpr int CPG = D / 64;                 // 32-column read-out chunks per group
     unsigned char* sPT = smem + S::PT;
     unsigned char* sDST = smem + S::DST;
     bool ok = true;
@@ -659,28 +661,30 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int entry = list[jj];
       const int qt = entry & 0x3fff;
       const bool partial = (entry >> 14) != CLS_FULL;
-      if (r == 0) bulk_wait_read();   // the previous pair's dQ reductions have read PT / DST
-      {  // stage this query tile's LSE (log2 domain), Dsum and metadata
+      if (threadIdx.x == 0) bulk_wait_read();   // the previous pair's dQ reductions have read PT / DST
+      if (g == 0) {  // stage this query tile's LSE (log2 domain) and Dsum
         const int q = qt * 128 + r;
         const int64_t li = ((int64_t)b * p.Hq + h) * p.T + q;
         sLSE[r] = q < p.T ? p.lse[li] * 1.44269504088896340736f : INFINITY;
         sDs[r] = q < p.T ? p.dsum[li] : 0.f;
-        sMq[r] = q < p.T ? p.meta[(int64_t)b * p.T + q] : make_int4(INT_MAX, INT_MAX, -5, SEG_PAD);
       }
-      named_bar_sync(1, 128);
-      uint4 cm = make_uint4(0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu);
-      if (partial) cm = p.tmask_t[(((int64_t)b * nk + kt) * p.nq + qt) * 128 + r];
-      if (r == 0 && j < 6) DBG_STAMP(40 + 4 * j);
+      named_bar_sync(1, 256);
+      uint2 cm = make_uint2(0xffffffffu, 0xffffffffu);
+      if (partial) {
+        const uint4 m4 = p.tmask_t[(((int64_t)b * nk + kt) * p.nq + qt) * 128 + r];
+        cm = g == 0 ? make_uint2(m4.x, m4.y) : make_uint2(m4.z, m4.w);
+      }
+      if (threadIdx.x == 0 && j < 6) DBG_STAMP(40 + 4 * j);
       if (!(ok = mbar_wait(sp_full, j & 1, p.err, 28))) break;
-      if (r == 0 && j < 6) DBG_STAMP(41 + 4 * j);
+      if (threadIdx.x == 0 && j < 6) DBG_STAMP(41 + 4 * j);
       tc_fence_after();
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = 2 * g + cc;
         uint32_t sv[32], dv[32];
         tmem_ld32(tS + lane_off + c * 32, sv);
         tmem_ld32(tDP + lane_off + c * 32, dv);
         tmem_wait_ld();
-        if (r == 0 && j == 1) DBG_STAMP(30 + 3 * c);
         float pp[32], dd[32];
         float lse_c[32], ds_c[32];
 #pragma unroll
@@ -690,8 +694,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           lse_c[t4 * 4 + 0] = l4.x; lse_c[t4 * 4 + 1] = l4.y; lse_c[t4 * 4 + 2] = l4.z; lse_c[t4 * 4 + 3] = l4.w;
           ds_c[t4 * 4 + 0] = d4.x; ds_c[t4 * 4 + 1] = d4.y; ds_c[t4 * 4 + 2] = d4.z; ds_c[t4 * 4 + 3] = d4.w;
         }
-        uint32_t amask = 0xffffffffu;
-        if (partial) amask = c == 0 ? cm.x : (c == 1 ? cm.y : (c == 2 ? cm.z : cm.w));
+        const uint32_t amask = cc == 0 ? cm.x : cm.y;
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
           const float e = fast_exp2(__uint_as_float(sv[t]) * p.scale_log2 - lse_c[t]);
@@ -699,7 +702,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           pp[t] = pv;
           dd[t] = pv * (__uint_as_float(dv[t]) - ds_c[t]);
         }
-        if (r == 0 && j == 1) DBG_STAMP(31 + 3 * c);
 #pragma unroll
         for (int t8 = 0; t8 < 4; ++t8) {
           const int col = c * 32 + t8 * 8;
@@ -713,21 +715,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           store8(reinterpret_cast<bf16*>(sPT + off), a8);
           store8(reinterpret_cast<bf16*>(sDST + off), d8);
         }
-        if (r == 0 && j == 1) DBG_STAMP(32 + 3 * c);
       }
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
-      if (r == 0 && j < 6) DBG_STAMP(42 + 4 * j);
+      if (threadIdx.x == 0 && j < 6) DBG_STAMP(42 + 4 * j);
       if (!(ok = mbar_wait(dq_full, j & 1, p.err, 29))) break;
-      if (r == 0 && j < 6) DBG_STAMP(43 + 4 * j);
+      if (threadIdx.x == 0 && j < 6) DBG_STAMP(43 + 4 * j);
       tc_fence_after();
-      // dQ rows: thread r owns query qt*128 + r.  All D/32 chunks go TMEM -> registers -> the
-      // P^T / dS^T buffers (idle until the next pair's softmax; 16 KB 128B-swizzled fp32 chunks)
-      // -> D/32 TMA tensor reductions (fp32 add) issued together after one barrier.
+      // dQ rows: lane r holds query qt*128 + r.  Each group moves its D/64 chunks TMEM ->
+      // registers -> the P^T / dS^T buffers (idle until the next pair's softmax; 16 KB
+      // 128B-swizzled fp32 chunks) -> D/32 TMA tensor reductions (fp32 add) after one barrier.
       unsigned char* stage = smem + S::PT;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int cc = 0; cc < CPG; ++cc) {
+        const int c = g * CPG + cc;
         uint32_t t[32];
         tmem_ld32(tS + lane_off + c * 32, t);
         tmem_wait_ld();
@@ -741,16 +743,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tc_fence_before();
       mbar_arrive(dq_free);                              // TMEM [0,128) may take the next S^T
       fence_async_smem();
-      named_bar_sync(1, 128);
-      if (r == 0) {
+      named_bar_sync(1, 256);
+      if (threadIdx.x == 0) {
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) tma_reduce_add_4d(&tmDQ, stage + c * (128 * 128), c * 32, h, qt * 128, b);
         bulk_commit();
       }
     }
-    if (r == 0) DBG_STAMP(62);
-    if (r == 0) bulk_wait_read();   // the last dQ reductions have read PT / DST
-    named_bar_sync(1, 128);
+    if (threadIdx.x == 0) DBG_STAMP(62);
+    if (threadIdx.x == 0) bulk_wait_read();   // the last dQ reductions have read PT / DST
+    named_bar_sync(1, 256);
     if (ok && total > 0) {
       // dK (x scale) and dV partials of this query head: staged like dQ, added by TMA into the
       // fp32 accumulators shared by the group's heads (rows past T are clipped by the map)
@@ -760,7 +762,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint32_t src = which == 0 ? tDK : tDV;
         const float mul = which == 0 ? p.scale : 1.f;
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int cc = 0; cc < CPG; ++cc) {
+          const int c = g * CPG + cc;
           uint32_t t[32];
           tmem_ld32(src + lane_off + c * 32, t);
           tmem_wait_ld();
@@ -772,18 +775,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                             __uint_as_float(t[u * 4 + 2]) * mul, __uint_as_float(t[u * 4 + 3]) * mul);
         }
         fence_async_smem();
-        named_bar_sync(1, 128);
-        if (r == 0) {
+        named_bar_sync(1, 256);
+        if (threadIdx.x == 0) {
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c)
             tma_reduce_add_4d(which == 0 ? &tmDK : &tmDV, stage + c * (128 * 128), c * 32, hk, kt * 128, b);
           bulk_commit();
           bulk_wait_read();
         }
-        named_bar_sync(1, 128);
+        named_bar_sync(1, 256);
       }
     }
-    if (r == 0) bulk_wait_all();    // every reduction issued by this CTA has completed
+    if (threadIdx.x == 0) bulk_wait_all();    // every reduction issued by this CTA has completed
   }
   tc_fence_before();
   __syncthreads();

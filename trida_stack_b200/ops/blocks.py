@@ -15,11 +15,14 @@ On CPU every block runs the plain-PyTorch statement of the same math under autog
 (``ops.reference``), which is also the numerics oracle for the GPU path.
 """
 import math
+import os
 
 import torch
 
 from . import reference as R
 from ._ext import ext
+
+_MLP_RECOMPUTE = os.environ.get("TRIDA_MLP_RECOMPUTE", "0") == "1"
 
 TN, TT, NT = 0, 1, 2
 
@@ -333,21 +336,25 @@ class _MlpBlock(torch.autograd.Function):
         C.swiglu_fwd(gu, a)
         out = torch.empty_like(x)
         gemm(TN, a, wd, out, x, 1.0, 1.0)
-        ctx.save_for_backward(x, rstd, gu)
+        # keeping a (M x F bf16) saves one SwiGLU pass in the backward; TRIDA_MLP_RECOMPUTE=1
+        # trades it back for memory
+        keep = not _MLP_RECOMPUTE
+        ctx.save_for_backward(x, rstd, gu, a if keep else None)
         ctx.params = (norm_w, wgu, wd)
         ctx.eps = eps
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        x, rstd, gu = ctx.saved_tensors
+        x, rstd, gu, a = ctx.saved_tensors
         norm_w, wgu, wd = ctx.params
         M, D = x.shape
         F = gu.shape[1] // 2
         C = ext()
         dout = dout.contiguous()
-        a = torch.empty(M, F, dtype=x.dtype, device=x.device)
-        C.swiglu_fwd(gu, a)
+        if a is None:
+            a = torch.empty(M, F, dtype=x.dtype, device=x.device)
+            C.swiglu_fwd(gu, a)
         g_wd = _wgrad(dout, a, wd)
         da = a
         gemm(TT, dout, wd, da)
