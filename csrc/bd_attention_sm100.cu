@@ -88,8 +88,7 @@ struct Smem {
   static constexpr int Q = 0;
   static constexpr int K0 = Q + (D / 64) * SUB;
   static constexpr int V0 = K0 + 2 * (D / 64) * SUB;
-  static constexpr int P = V0 + 2 * (D / 64) * SUB;   // two P buffers of 2 sub-tiles each
-  static constexpr int XCH = P + 4 * SUB;               // float[2 halves][128 rows]: half-row max / sum exchange
+  static constexpr int XCH = V0 + 2 * (D / 64) * SUB;  // float[2 halves][128 rows]: half-row max / sum exchange
   static constexpr int BAR = XCH + 2 * 128 * 4;
   static constexpr int TOTAL = BAR + 256;
 };
@@ -125,6 +124,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   uint64_t* drain = bars + 10;
   uint64_t* v_full = bars + 11;    // [2]
   uint64_t* v_empty = bars + 13;   // [2]
+  uint64_t* q_tmem = bars + 15;    // the softmax warps have copied Q into TMEM
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -148,6 +148,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
     mbar_init(p_full, 2 * BM);
+    mbar_init(q_tmem, 2 * BM);
     mbar_init(&pv_done[0], 1);
     mbar_init(&pv_done[1], 1);
     mbar_init(drain, 1);
@@ -160,6 +161,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS[2] = {tmem, tmem + 128};
   const uint32_t tO = tmem + 256;
+  const uint32_t tQ = tmem + 256 + D;     // Q as the A operand: D / 2 columns of bf16 pairs
 
   if (warp == 9) {
     // ---------------- TMA producer ----------------
@@ -193,39 +195,42 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     }
   } else if (warp == 8) {
     // ---------------- MMA issuer ----------------
+    // A operands come from TMEM (Q copied there once by the softmax warps, P_i written over S_i),
+    // so each MMA reads only its B tile (K_i or V_i) from shared memory.
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16_f32(BM, BN, 0, 0);
       constexpr uint32_t idPV = idesc_bf16_f32(BM, D, 0, 1);
-      const uint32_t sQ = smem_addr(smem + S::Q), sK = smem_addr(smem + S::K0), sV = smem_addr(smem + S::V0),
-                     sP = smem_addr(smem + S::P);
-      bool ok = mbar_wait(q_full, 0, p.err, 3);
+      const uint32_t sK = smem_addr(smem + S::K0), sV = smem_addr(smem + S::V0);
+      bool ok = mbar_wait(q_tmem, 0, p.err, 3);
       DBG_STAMP(1);
       auto issue_pv = [&](int j) {
         if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, p.err, 13)) return false;
         tc_fence_after();
         const uint32_t vbase = sV + (j & 1) * (D / 64) * S::SUB;
-        const uint32_t pbase = sP + (j & 1) * 2 * S::SUB;
+        const uint32_t pcol = tS[j & 1];
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t a = desc_sw128(pbase + (kk >> 2) * S::SUB + (kk & 3) * 32, 16, 1024);
+          // keys [16 kk, 16 kk + 16): written by half kk / 4 at column 64 (kk / 4) + 8 (kk % 4)
           const uint64_t bd = desc_sw128(vbase + kk * 2048, S::SUB, 1024);
-          umma_f16(tO, a, bd, idPV, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ts(tO, pcol + (kk >> 2) * 64 + (kk & 3) * 8, bd, idPV, (j > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&pv_done[j & 1]);
         umma_commit(&v_empty[j & 1]);
         return true;
       };
+      tc_fence_after();
       for (int i = 0; ok && i < n; ++i) {
         const int s = i & 1;
         if (!(ok = mbar_wait(&k_full[s], (i >> 1) & 1, p.err, 4))) break;
+        // S_i goes over P_{i-2} in TMEM: PV_{i-2} must have read it
+        if (i >= 2 && !(ok = mbar_wait(&pv_done[s], ((i - 2) >> 1) & 1, p.err, 11))) break;
         if (i < 6) DBG_STAMP(2 + 4 * i);
         tc_fence_after();
         const uint32_t kbase = sK + s * (D / 64) * S::SUB;
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
-          const uint64_t a = desc_sw128(sQ + (k >> 2) * S::SUB + (k & 3) * 32, 16, 1024);
           const uint64_t bd = desc_sw128(kbase + (k >> 2) * S::SUB + (k & 3) * 32, 16, 1024);
-          umma_f16(tS[s], a, bd, idS, k > 0 ? 1u : 0u);
+          umma_f16_ts(tS[s], tQ + k * 8, bd, idS, k > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[s]);
         umma_commit(&k_empty[s]);
@@ -255,8 +260,26 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     float* xch = reinterpret_cast<float*>(smem + S::XCH);
     float m_run = -INFINITY, l_run = 0.f;
-    unsigned char* sP = smem + S::P;
     bool ok = true;
+    {  // copy this thread's half of Q row r from the TMA tile (128B-swizzled) into TMEM
+      ok = mbar_wait(q_full, 0, p.err, 14);
+      if (ok) {
+        constexpr int NW = D / 4;                       // 32-bit words (bf16 pairs) per half row
+        uint32_t w[NW];
+#pragma unroll
+        for (int u = 0; u < D / 16; ++u) {
+          const int e = half * (D / 2) + u * 8;
+          const uint4 v = *reinterpret_cast<const uint4*>(smem + S::Q + (e >> 6) * S::SUB + r * 128 +
+                                                          ((((e & 63) >> 3) ^ (r & 7)) << 4));
+          w[4 * u] = v.x; w[4 * u + 1] = v.y; w[4 * u + 2] = v.z; w[4 * u + 3] = v.w;
+        }
+        if constexpr (D == 128) tmem_st32(tQ + lane_off + half * NW, w);
+        else tmem_st16(tQ + lane_off + half * NW, w);
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      mbar_arrive(q_tmem);
+    }
     for (int i = 0; i < n; ++i) {
       const int s = i & 1;
       const int entry = list[i];
@@ -303,16 +326,11 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       if (threadIdx.x == 0 && i < 6) DBG_STAMP(31 + 5 * i);
       const float mx_s = mx * p.scale_log2;
       const bool grow = mx_s > m_run + RESCALE_THRESHOLD || (m_run == -INFINITY && mx_s > -INFINITY);
-      // The P buffer (i & 1) was last read by PV_{i-2}; O may be rescaled only after PV_{i-1}
-      // (MMAs complete in issue order, so PV_{i-1} done implies PV_{i-2} done).
-      if (ok) {
-        if (grow && i > 0) {
-          ok = mbar_wait(&pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1, p.err, 9);
-          tc_fence_after();
-        } else if (i >= 2) {
-          ok = mbar_wait(&pv_done[i & 1], ((i - 2) >> 1) & 1, p.err, 11);
-          tc_fence_after();
-        }
+      // O may be rescaled only after PV_{i-1} has completed (P_i overwrites S_i in TMEM, whose
+      // buffer the MMA warp reused only after PV_{i-2} completed)
+      if (ok && grow && i > 0) {
+        ok = mbar_wait(&pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1, p.err, 9);
+        tc_fence_after();
       }
       if (threadIdx.x == 0 && i < 6) DBG_STAMP(32 + 5 * i);
       if (grow) {
@@ -334,9 +352,11 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         m_run = mx_s;
       }
       if (ok) {
+        // P_i (bf16 pairs) overwrites this half's own S_i columns in TMEM: 32 columns starting at
+        // column 64 half, the A operand of PV_i
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
         float rsp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        unsigned char* pbuf = sP + (i & 1) * 2 * S::SUB + half * S::SUB;
+        uint32_t pw[32];
 #pragma unroll
         for (int c8 = 0; c8 < 8; ++c8) {
           float pv[8];
@@ -345,10 +365,15 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
             pv[j] = fast_exp2(sv[c8 * 8 + j] * p.scale_log2 - m_use);
             rsp[j] += pv[j];
           }
-          store8(reinterpret_cast<bf16*>(pbuf + sw128_offset(r, c8 * 8)), pv);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const __nv_bfloat162 t2 = __floats2bfloat162_rn(pv[2 * j], pv[2 * j + 1]);
+            pw[c8 * 4 + j] = *reinterpret_cast<const uint32_t*>(&t2);
+          }
         }
+        tmem_st32(tS[s] + lane_off + half * 64, pw);
+        tmem_wait_st();
         l_run += ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
-        fence_async_smem();
       }
       tc_fence_before();
       mbar_arrive(p_full);
@@ -360,8 +385,9 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     xch[half * BM + r] = l_run;
     named_sync(bar_id, 64);
     const float l_tot = l_run + xch[(1 - half) * BM + r];
-    // epilogue: O / l staged as bf16 in the (now idle) P buffer in the swizzled layout of the O
+    // epilogue: O / l staged as bf16 in the (now idle) Q tile in the swizzled layout of the O
     // tensor map, then written by TMA as whole 128-row sub-tiles (coalesced; rows past T clipped)
+    unsigned char* sO = smem + S::Q;
     const bool store = ok && n > 0;
     if (store) {
       tc_fence_after();
@@ -377,7 +403,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
 #pragma unroll
           for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(t[j8 * 8 + j]) * inv;
           const int col = half * (D / 2) + c * 32 + j8 * 8;
-          store8(reinterpret_cast<bf16*>(sP + (col >> 6) * S::SUB + sw128_offset(r, col & 63)), f);
+          store8(reinterpret_cast<bf16*>(sO + (col >> 6) * S::SUB + sw128_offset(r, col & 63)), f);
         }
       }
       if (half == 0 && row < p.T)
@@ -389,7 +415,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     if (threadIdx.x == 0 && store) {
       if (threadIdx.x == 0) DBG_STAMP(61);
 #pragma unroll
-      for (int c = 0; c < D / 64; ++c) tma_store_4d(&tmO, sP + c * S::SUB, c * 64, h, qt * BM, b);
+      for (int c = 0; c < D / 64; ++c) tma_store_4d(&tmO, sO + c * S::SUB, c * 64, h, qt * BM, b);
       asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
       asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
     }
