@@ -507,13 +507,16 @@ struct BwdParams {
 
 template <int D>
 struct BwdSmem {
+  // K, V once per CTA; Q_j / dO_j double-buffered so pair j+1's tiles load while pair j runs, and
+  // once pair j's MMAs have run its slot stages dQ_j for the TMA reductions; dS^T (bf16, K-major
+  // rows = keys) is the A operand of dK and dQ.  P^T lives in TMEM only.
   static constexpr int SUB = 128 * 128;
+  static constexpr int T = (D / 64) * SUB;      // one [128 rows][D] bf16 tile
   static constexpr int K = 0;
-  static constexpr int V = K + (D / 64) * SUB;
-  static constexpr int Q = V + (D / 64) * SUB;
-  static constexpr int DO = Q + (D / 64) * SUB;
-  static constexpr int PT = DO + (D / 64) * SUB;
-  static constexpr int DST = PT + 2 * SUB;
+  static constexpr int V = K + T;
+  static constexpr int Q = V + T;               // [2] tiles
+  static constexpr int DO = Q + 2 * T;          // [2] tiles
+  static constexpr int DST = DO + 2 * T;
   static constexpr int LSE = DST + 2 * SUB;     // float[128]
   static constexpr int DS = LSE + 512;          // float[128]
   static constexpr int BAR = DS + 512;
@@ -556,14 +559,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR);
   uint64_t* kv_full = bars + 0;
-  uint64_t* q_full = bars + 1;
-  uint64_t* q_empty = bars + 2;
-  uint64_t* sp_full = bars + 3;
-  uint64_t* p_full = bars + 4;
-  uint64_t* dq_full = bars + 5;
-  uint64_t* dq_free = bars + 6;
-  uint64_t* drain = bars + 7;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  uint64_t* q_full = bars + 1;    // [2]
+  uint64_t* q_empty = bars + 3;   // [2]
+  uint64_t* sp_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* dq_full = bars + 7;   // every MMA of the pair has completed (dQ_j is in TMEM)
+  uint64_t* dq_free = bars + 8;   // the softmax warps have read dQ_j out of TMEM
+  uint64_t* drain = bars + 9;
+  uint64_t* slot_free = bars + 10; // [2]: the dQ reductions staged in a Q / dO slot have read it
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   float* sLSE = reinterpret_cast<float*>(smem + S::LSE);
   float* sDs = reinterpret_cast<float*>(smem + S::DS);
 
@@ -574,9 +578,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = gridDim.x;
   const int lidx = b * nk + kt;
-  const int nqt = p.cnt[lidx];
+  const int total = p.cnt[lidx];
   const int16_t* list = p.list + (int64_t)lidx * p.nq;
-  const int total = nqt;
   // CTAs of neighbouring key tiles start their walk at different query tiles so their dQ
   // reductions land on different rows at any moment.
   const int rot = total > 0 ? (kt * 7 + h * 3) % total : 0;
@@ -585,8 +588,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (threadIdx.x == 0) {
     DBG_STAMP(0);
     mbar_init(kv_full, 1);
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&slot_free[i], 1);
+    }
     mbar_init(sp_full, 1);
     mbar_init(p_full, 256);
     mbar_init(dq_full, 1);
@@ -599,51 +605,67 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // TMEM: S^T [0,128) then P^T (bf16 pairs, written over it); dP^T [128,256) then dQ_j; dV; dK
   const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 256 + D;
 
   if (warp == 9) {
+    // ---------------- TMA producer ----------------
     if (lane == 0) {
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
       prefetch_tmap(&tmDO);
-      mbar_expect_tx(kv_full, 2 * (D / 64) * S::SUB);
+      mbar_expect_tx(kv_full, 2 * S::T);
 #pragma unroll
       for (int c = 0; c < D / 64; ++c) {
         tma_load_4d(smem + S::K + c * S::SUB, &tmK, kv_full, c * 64, hk, kt * 128, b);
         tma_load_4d(smem + S::V + c * S::SUB, &tmV, kv_full, c * 64, hk, kt * 128, b);
       }
       for (int j = 0; j < total; ++j) {
-        if (j > 0 && !mbar_wait(q_empty, (j - 1) & 1, p.err, 21)) break;
-        const int jj = (j + rot) % total;
-        const int qt = list[jj] & 0x3fff;
-        mbar_expect_tx(q_full, 2 * (D / 64) * S::SUB);
+        const int s = j & 1;
+        // slot s held pair j-2: its MMAs have run and the dQ_{j-2} reductions staged there have read it
+        if (j >= 2 && !mbar_wait(&q_empty[s], ((j - 2) >> 1) & 1, p.err, 21)) break;
+        if (j >= 2 && !mbar_wait(&slot_free[s], ((j - 2) >> 1) & 1, p.err, 31)) break;
+        const int qt = list[(j + rot) % total] & 0x3fff;
+        mbar_expect_tx(&q_full[s], 2 * S::T);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
-          tma_load_4d(smem + S::Q + c * S::SUB, &tmQ, q_full, c * 64, h, qt * 128, b);
-          tma_load_4d(smem + S::DO + c * S::SUB, &tmDO, q_full, c * 64, h, qt * 128, b);
+          tma_load_4d(smem + S::Q + s * S::T + c * S::SUB, &tmQ, &q_full[s], c * 64, h, qt * 128, b);
+          tma_load_4d(smem + S::DO + s * S::T + c * S::SUB, &tmDO, &q_full[s], c * 64, h, qt * 128, b);
         }
       }
-      if (total > 0) mbar_wait(q_full, (total - 1) & 1, p.err, 22);
+      // the last (up to two) loads must have landed before the CTA can retire
+      for (int j = (total > 2 ? total - 2 : 0); j < total; ++j) mbar_wait(&q_full[j & 1], (j >> 1) & 1, p.err, 22);
     }
   } else if (warp == 8) {
+    // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idKK = idesc_bf16_f32(128, 128, 0, 0);   // S^T, dP^T
-      constexpr uint32_t idKM = idesc_bf16_f32(128, D, 0, 1);     // dV, dK (B MN-major)
+      constexpr uint32_t idKM = idesc_bf16_f32(128, D, 0, 1);     // dV (A from TMEM), dK (B MN-major)
       constexpr uint32_t idMM = idesc_bf16_f32(128, D, 1, 1);     // dQ (A and B MN-major)
-      const uint32_t sK = smem_addr(smem + S::K), sV = smem_addr(smem + S::V), sQ = smem_addr(smem + S::Q),
-                     sDO = smem_addr(smem + S::DO), sPT = smem_addr(smem + S::PT), sDST = smem_addr(smem + S::DST);
+      const uint32_t sK = smem_addr(smem + S::K), sV = smem_addr(smem + S::V), sQ0 = smem_addr(smem + S::Q),
+                     sDO0 = smem_addr(smem + S::DO), sDST = smem_addr(smem + S::DST);
       bool ok = mbar_wait(kv_full, 0, p.err, 23);
       for (int j = 0; ok && j < total; ++j) {
-        if (!(ok = mbar_wait(q_full, j & 1, p.err, 24))) break;
+        const int s = j & 1;
+        const uint32_t sQ = sQ0 + s * S::T, sDO = sDO0 + s * S::T;
+        if (!(ok = mbar_wait(&q_full[s], (j >> 1) & 1, p.err, 24))) break;
+        // S^T_j goes over P^T_{j-1}: every MMA of pair j-1 (dV read P^T) has completed
+        if (j > 0 && !(ok = mbar_wait(dq_full, (j - 1) & 1, p.err, 25))) break;
         if (j < 6) DBG_STAMP(10 + 3 * j);
-        if (j > 0 && !(ok = mbar_wait(dq_free, (j - 1) & 1, p.err, 25))) break;
-        if (j < 6) DBG_STAMP(11 + 3 * j);
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
           const uint32_t off = (k >> 2) * S::SUB + (k & 3) * 32;
           umma_f16(tS, desc_sw128(sK + off, 16, 1024), desc_sw128(sQ + off, 16, 1024), idKK, k > 0);
+        }
+        // dP^T_j goes over dQ_{j-1}: the softmax warps have read it out
+        if (j > 0 && !(ok = mbar_wait(dq_free, (j - 1) & 1, p.err, 30))) break;
+        if (j < 6) DBG_STAMP(11 + 3 * j);
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (k >> 2) * S::SUB + (k & 3) * 32;
           umma_f16(tDP, desc_sw128(sV + off, 16, 1024), desc_sw128(sDO + off, 16, 1024), idKK, k > 0);
         }
         umma_commit(sp_full);
@@ -652,20 +674,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 128 / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * S::SUB + (kk & 3) * 32;   // K-major 16-query step
+          // queries [16 kk, 16 kk + 16): P^T written by group kk / 4 at column 64 (kk / 4) + 8 (kk % 4)
+          const uint32_t aoff = (kk >> 2) * S::SUB + (kk & 3) * 32;   // K-major 16-query step (dS^T)
           const uint32_t boff = kk * 2048;                            // MN-major 16-row step
           const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
-          umma_f16(tDV, desc_sw128(sPT + aoff, 16, 1024), desc_sw128(sDO + boff, S::SUB, 1024), idKM, acc);
+          umma_f16_ts(tDV, tS + (kk >> 2) * 64 + (kk & 3) * 8, desc_sw128(sDO + boff, S::SUB, 1024), idKM, acc);
           umma_f16(tDK, desc_sw128(sDST + aoff, 16, 1024), desc_sw128(sQ + boff, S::SUB, 1024), idKM, acc);
         }
 #pragma unroll
         for (int kk = 0; kk < 128 / 16; ++kk) {
           // A = dS (M = queries, K = keys): the dS^T rows (key-major) read as MN-major, 16 keys per step
-          umma_f16(tS, desc_sw128(sDST + kk * 2048, S::SUB, 1024), desc_sw128(sK + kk * 2048, S::SUB, 1024), idMM,
+          umma_f16(tDP, desc_sw128(sDST + kk * 2048, S::SUB, 1024), desc_sw128(sK + kk * 2048, S::SUB, 1024), idMM,
                    kk > 0);
         }
         umma_commit(dq_full);
-        umma_commit(q_empty);
+        umma_commit(&q_empty[s]);
       }
       umma_commit(drain);
       mbar_wait(drain, 0, p.err, 27);
@@ -679,7 +702,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int r = threadIdx.x & 127, g = threadIdx.x >> 7;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     constexpr int CPG = D / 64;                 // 32-column read-out chunks per group
-    unsigned char* sPT = smem + S::PT;
     unsigned char* sDST = smem + S::DST;
     bool ok = true;
     for (int j = 0; j < total; ++j) {
@@ -687,7 +709,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int entry = list[jj];
       const int qt = entry & 0x3fff;
       const bool partial = (entry >> 14) != CLS_FULL;
-      if (threadIdx.x == 0) bulk_wait_read();   // the previous pair's dQ reductions have read PT / DST
       if (g == 0) {  // stage this query tile's LSE (log2 domain) and Dsum
         const int q = qt * 128 + r;
         const int64_t li = ((int64_t)b * p.Hq + h) * p.T + q;
@@ -728,61 +749,83 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           pp[t] = pv;
           dd[t] = pv * (__uint_as_float(dv[t]) - ds_c[t]);
         }
+        // P^T (bf16 pairs, the A operand of dV) over this group's first S^T chunk: columns
+        // [64 g + 16 cc, 64 g + 16 cc + 16), whose S^T values are already in registers
+        uint32_t pw[16];
+#pragma unroll
+        for (int t2 = 0; t2 < 16; ++t2) {
+          const __nv_bfloat162 v2 = __floats2bfloat162_rn(pp[2 * t2], pp[2 * t2 + 1]);
+          pw[t2] = *reinterpret_cast<const uint32_t*>(&v2);
+        }
+        tmem_st16(tS + lane_off + g * 64 + cc * 16, pw);
 #pragma unroll
         for (int t8 = 0; t8 < 4; ++t8) {
           const int col = c * 32 + t8 * 8;
           const uint32_t off = (col >> 6) * S::SUB + sw128_offset(r, col & 63);
-          float a8[8], d8[8];
+          float d8[8];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            a8[u] = pp[t8 * 8 + u];
-            d8[u] = dd[t8 * 8 + u];
-          }
-          store8(reinterpret_cast<bf16*>(sPT + off), a8);
+          for (int u = 0; u < 8; ++u) d8[u] = dd[t8 * 8 + u];
           store8(reinterpret_cast<bf16*>(sDST + off), d8);
         }
       }
+      tmem_wait_st();
       fence_async_smem();
       tc_fence_before();
+      if (threadIdx.x == 0 && j > 0) {   // pair j-1's dQ reductions have read their slot by now
+        bulk_wait_read();
+        mbar_arrive(&slot_free[(j - 1) & 1]);
+      }
       mbar_arrive(p_full);
       if (threadIdx.x == 0 && j < 6) DBG_STAMP(42 + 4 * j);
       if (!(ok = mbar_wait(dq_full, j & 1, p.err, 29))) break;
       if (threadIdx.x == 0 && j < 6) DBG_STAMP(43 + 4 * j);
       tc_fence_after();
-      // dQ rows: lane r holds query qt*128 + r.  Each group moves its D/64 chunks TMEM ->
-      // registers -> the P^T / dS^T buffers (idle until the next pair's softmax; 16 KB
-      // 128B-swizzled fp32 chunks) -> D/32 TMA tensor reductions (fp32 add) after one barrier.
-      unsigned char* stage = smem + S::PT;
-#pragma unroll 1
-      for (int cc = 0; cc < CPG; ++cc) {
-        const int c = g * CPG + cc;
-        uint32_t t[32];
-        tmem_ld32(tS + lane_off + c * 32, t);
-        tmem_wait_ld();
-        unsigned char* sc = stage + c * (128 * 128);
+      // dQ_j rows (lane r = query qt*128 + r): read this group's chunks, release TMEM for dP^T_{j+1},
+      // then stage them (x scale, fp32, 128B-swizzled 16 KB chunks) in this pair's Q / dO slot,
+      // idle now that its MMAs have run (pair j+1 is already in the other slot), and add them to the
+      // fp32 accumulator with TMA tensor reductions that overlap pair j+1; the producer refills the
+      // slot once they have read it (slot_free, signalled during pair j+1).
+      {
+        uint32_t t[CPG][32];
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
-          *reinterpret_cast<float4*>(sc + r * 128 + ((u ^ (r & 7)) << 4)) =
-              make_float4(__uint_as_float(t[u * 4]) * p.scale, __uint_as_float(t[u * 4 + 1]) * p.scale,
-                          __uint_as_float(t[u * 4 + 2]) * p.scale, __uint_as_float(t[u * 4 + 3]) * p.scale);
-      }
-      tc_fence_before();
-      mbar_arrive(dq_free);                              // TMEM [0,128) may take the next S^T
-      fence_async_smem();
-      named_bar_sync(1, 256);
-      if (threadIdx.x == 0) {
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) tma_reduce_add_4d(&tmDQ, stage + c * (128 * 128), c * 32, h, qt * 128, b);
-        bulk_commit();
+        for (int cc = 0; cc < CPG; ++cc) tmem_ld32(tDP + lane_off + (g * CPG + cc) * 32, t[cc]);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(dq_free);
+        const int sl = j & 1;
+#pragma unroll
+        for (int cc = 0; cc < CPG; ++cc) {
+          const int c = g * CPG + cc;       // chunks [0, D/64) in the Q tile, the rest in the dO tile
+          unsigned char* sc = c < D / 64 ? smem + S::Q + sl * S::T + c * S::SUB
+                                         : smem + S::DO + sl * S::T + (c - D / 64) * S::SUB;
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<float4*>(sc + r * 128 + ((u ^ (r & 7)) << 4)) =
+                make_float4(__uint_as_float(t[cc][u * 4]) * p.scale, __uint_as_float(t[cc][u * 4 + 1]) * p.scale,
+                            __uint_as_float(t[cc][u * 4 + 2]) * p.scale, __uint_as_float(t[cc][u * 4 + 3]) * p.scale);
+        }
+        fence_async_smem();
+        named_bar_sync(1, 256);
+        if (threadIdx.x == 0) {
+          for (int c = 0; c < D / 32; ++c) {
+            const unsigned char* sc = c < D / 64 ? smem + S::Q + sl * S::T + c * S::SUB
+                                                 : smem + S::DO + sl * S::T + (c - D / 64) * S::SUB;
+            tma_reduce_add_4d(&tmDQ, sc, c * 32, h, qt * 128, b);
+          }
+          bulk_commit();
+        }
       }
     }
     if (threadIdx.x == 0) DBG_STAMP(62);
-    if (threadIdx.x == 0) bulk_wait_read();   // the last dQ reductions have read PT / DST
+    if (threadIdx.x == 0) {
+      bulk_wait_read();                         // the last dQ reductions have read their slot
+      if (ok && total > 0) mbar_arrive(&slot_free[(total - 1) & 1]);
+    }
     named_bar_sync(1, 256);
     if (ok && total > 0) {
-      // dK (x scale) and dV partials of this query head: staged like dQ, added by TMA into the
-      // fp32 accumulators shared by the group's heads (rows past T are clipped by the map)
-      unsigned char* stage = smem + S::PT;
+      // dK (x scale) and dV partials of this query head, staged in the idle Q / dO tiles and added
+      // by TMA into the fp32 accumulators shared by the group's heads (rows past T are clipped)
+      unsigned char* stage = smem + S::Q;
 #pragma unroll 1
       for (int which = 0; which < 2; ++which) {
         const uint32_t src = which == 0 ? tDK : tDV;
