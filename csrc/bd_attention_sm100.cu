@@ -704,27 +704,41 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     constexpr int CPG = D / 64;                 // 32-column read-out chunks per group
     unsigned char* sDST = smem + S::DST;
     bool ok = true;
+    // Per-pair inputs (list entry, LSE / Dsum of the query row, PARTIAL-tile mask) are loaded one
+    // pair ahead, during the softmax of the previous pair, so no global round trip sits between
+    // two pairs.
+    int e_next = total > 0 ? list[rot % total] : 0;
+    float lse_next = INFINITY, ds_next = 0.f;
+    uint2 cm_next = make_uint2(0xffffffffu, 0xffffffffu);
+    auto fetch = [&](int e) {
+      const int qn = (e & 0x3fff) * 128 + r;
+      if (g == 0) {
+        const int64_t li = ((int64_t)b * p.Hq + h) * p.T + qn;
+        lse_next = qn < p.T ? p.lse[li] * 1.44269504088896340736f : INFINITY;
+        ds_next = qn < p.T ? p.dsum[li] : 0.f;
+      }
+      cm_next = make_uint2(0xffffffffu, 0xffffffffu);
+      if ((e >> 14) != CLS_FULL) {
+        const uint4 m4 = p.tmask_t[(((int64_t)b * nk + kt) * p.nq + (e & 0x3fff)) * 128 + r];
+        cm_next = g == 0 ? make_uint2(m4.x, m4.y) : make_uint2(m4.z, m4.w);
+      }
+    };
+    if (total > 0) fetch(e_next);
     for (int j = 0; j < total; ++j) {
-      const int jj = (j + rot) % total;
-      const int entry = list[jj];
+      const int entry = e_next;
       const int qt = entry & 0x3fff;
-      const bool partial = (entry >> 14) != CLS_FULL;
-      if (g == 0) {  // stage this query tile's LSE (log2 domain) and Dsum
-        const int q = qt * 128 + r;
-        const int64_t li = ((int64_t)b * p.Hq + h) * p.T + q;
-        sLSE[r] = q < p.T ? p.lse[li] * 1.44269504088896340736f : INFINITY;
-        sDs[r] = q < p.T ? p.dsum[li] : 0.f;
+      const uint2 cm = cm_next;
+      if (g == 0) {  // this query tile's LSE (log2 domain) and Dsum
+        sLSE[r] = lse_next;
+        sDs[r] = ds_next;
       }
+      if (j + 1 < total) e_next = list[(j + 1 + rot) % total];
       named_bar_sync(1, 256);
-      uint2 cm = make_uint2(0xffffffffu, 0xffffffffu);
-      if (partial) {
-        const uint4 m4 = p.tmask_t[(((int64_t)b * nk + kt) * p.nq + qt) * 128 + r];
-        cm = g == 0 ? make_uint2(m4.x, m4.y) : make_uint2(m4.z, m4.w);
-      }
       if (threadIdx.x == 0 && j < 6) DBG_STAMP(40 + 4 * j);
       if (!(ok = mbar_wait(sp_full, j & 1, p.err, 28))) break;
       if (threadIdx.x == 0 && j < 6) DBG_STAMP(41 + 4 * j);
       tc_fence_after();
+      if (j + 1 < total) fetch(e_next);
 #pragma unroll 1
       for (int cc = 0; cc < 2; ++cc) {
         const int c = 2 * g + cc;
