@@ -708,14 +708,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // pair ahead, during the softmax of the previous pair, so no global round trip sits between
     // two pairs.
     int e_next = total > 0 ? list[rot % total] : 0;
-    float lse_next = INFINITY, ds_next = 0.f;
+    float lse_next = -INFINITY, ds_next = 0.f;
     uint2 cm_next = make_uint2(0xffffffffu, 0xffffffffu);
     auto fetch = [&](int e) {
       const int qn = (e & 0x3fff) * 128 + r;
       if (g == 0) {
         const int64_t li = ((int64_t)b * p.Hq + h) * p.T + qn;
-        lse_next = qn < p.T ? p.lse[li] * 1.44269504088896340736f : INFINITY;
-        ds_next = qn < p.T ? p.dsum[li] : 0.f;
+        lse_next = qn < p.T ? -p.lse[li] * 1.44269504088896340736f : -INFINITY;   // staged negated
+        ds_next = qn < p.T ? -p.dsum[li] : 0.f;
       }
       cm_next = make_uint2(0xffffffffu, 0xffffffffu);
       if ((e >> 14) != CLS_FULL) {
@@ -728,7 +728,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int entry = e_next;
       const int qt = entry & 0x3fff;
       const uint2 cm = cm_next;
-      if (g == 0) {  // this query tile's LSE (log2 domain) and Dsum
+      if (g == 0) {  // this query tile's -LSE (log2 domain) and -Dsum
         sLSE[r] = lse_next;
         sDs[r] = ds_next;
       }
@@ -739,57 +739,68 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (threadIdx.x == 0 && j < 6) DBG_STAMP(41 + 4 * j);
       tc_fence_after();
       if (j + 1 < total) fetch(e_next);
-#pragma unroll 1
-      for (int cc = 0; cc < 2; ++cc) {
-        const int c = 2 * g + cc;
-        uint32_t sv[32], dv[32];
-        tmem_ld32(tS + lane_off + c * 32, sv);
-        tmem_ld32(tDP + lane_off + c * 32, dv);
+      // four 16-query sub-chunks of this group's 64 columns; the next sub-chunk's S^T / dP^T loads
+      // are in flight while the current one is computed
+      uint32_t sv[2][16], dv[2][16];
+      tmem_ld16(tS + lane_off + g * 64, sv[0]);
+      tmem_ld16(tDP + lane_off + g * 64, dv[0]);
+#pragma unroll
+      for (int sc = 0; sc < 4; ++sc) {
+        const int cur = sc & 1;
+        const int q0 = g * 64 + sc * 16;            // first query column of the sub-chunk
         tmem_wait_ld();
-        float pp[32], dd[32];
-        float lse_c[32], ds_c[32];
-#pragma unroll
-        for (int t4 = 0; t4 < 8; ++t4) {
-          const float4 l4 = reinterpret_cast<const float4*>(sLSE + c * 32)[t4];
-          const float4 d4 = reinterpret_cast<const float4*>(sDs + c * 32)[t4];
-          lse_c[t4 * 4 + 0] = l4.x; lse_c[t4 * 4 + 1] = l4.y; lse_c[t4 * 4 + 2] = l4.z; lse_c[t4 * 4 + 3] = l4.w;
-          ds_c[t4 * 4 + 0] = d4.x; ds_c[t4 * 4 + 1] = d4.y; ds_c[t4 * 4 + 2] = d4.z; ds_c[t4 * 4 + 3] = d4.w;
+        if (sc < 3) {
+          tmem_ld16(tS + lane_off + q0 + 16, sv[cur ^ 1]);
+          tmem_ld16(tDP + lane_off + q0 + 16, dv[cur ^ 1]);
         }
-        const uint32_t amask = cc == 0 ? cm.x : cm.y;
+        const uint32_t amask = ((sc < 2 ? cm.x : cm.y) >> ((sc & 1) * 16)) & 0xffffu;
+        // two queries per packed fp32x2 step: x = S^T * scale_log2 - LSE2, P^T = exp2(x) (masked
+        // on PARTIAL tiles), dS^T = P^T * (dP^T - Dsum); P^T and dS^T packed to bf16 pairs
+        const uint64_t scale2 = f2pack(p.scale_log2, p.scale_log2);
+        uint32_t pw[8], dw[8];
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const float e = fast_exp2(__uint_as_float(sv[t]) * p.scale_log2 - lse_c[t]);
-          const float pv = ((amask >> t) & 1u) ? e : 0.f;
-          pp[t] = pv;
-          dd[t] = pv * (__uint_as_float(dv[t]) - ds_c[t]);
+        for (int t4 = 0; t4 < 4; ++t4) {
+          const float4 l4 = reinterpret_cast<const float4*>(sLSE + q0)[t4];
+          const float4 d4 = reinterpret_cast<const float4*>(sDs + q0)[t4];
+#pragma unroll
+          for (int u2 = 0; u2 < 2; ++u2) {
+            const int t = t4 * 4 + u2 * 2;
+            const uint64_t x = f2fma(f2pack(__uint_as_float(sv[cur][t]), __uint_as_float(sv[cur][t + 1])), scale2,
+                                     u2 == 0 ? f2pack(l4.x, l4.y) : f2pack(l4.z, l4.w));
+            const float2 xf = f2unpack(x);
+            float e0 = fast_exp2(xf.x), e1 = fast_exp2(xf.y);
+            if (amask != 0xffffu) {
+              e0 = ((amask >> t) & 1u) ? e0 : 0.f;
+              e1 = ((amask >> (t + 1)) & 1u) ? e1 : 0.f;
+            }
+            const uint64_t dd = f2mul(f2pack(e0, e1),
+                                      f2add(f2pack(__uint_as_float(dv[cur][t]), __uint_as_float(dv[cur][t + 1])),
+                                            u2 == 0 ? f2pack(d4.x, d4.y) : f2pack(d4.z, d4.w)));
+            const float2 df = f2unpack(dd);
+            const __nv_bfloat162 pb = __floats2bfloat162_rn(e0, e1);
+            const __nv_bfloat162 db = __floats2bfloat162_rn(df.x, df.y);
+            pw[t >> 1] = *reinterpret_cast<const uint32_t*>(&pb);
+            dw[t >> 1] = *reinterpret_cast<const uint32_t*>(&db);
+          }
         }
-        // P^T (bf16 pairs, the A operand of dV) over this group's first S^T chunk: columns
-        // [64 g + 16 cc, 64 g + 16 cc + 16), whose S^T values are already in registers
-        uint32_t pw[16];
+        // P^T (bf16 pairs, the A operand of dV) over S^T columns [64 g + 8 sc, 64 g + 8 sc + 8),
+        // whose values were loaded with sub-chunk sc / 2
+        tmem_st8(tS + lane_off + g * 64 + sc * 8, pw);
 #pragma unroll
-        for (int t2 = 0; t2 < 16; ++t2) {
-          const __nv_bfloat162 v2 = __floats2bfloat162_rn(pp[2 * t2], pp[2 * t2 + 1]);
-          pw[t2] = *reinterpret_cast<const uint32_t*>(&v2);
-        }
-        tmem_st16(tS + lane_off + g * 64 + cc * 16, pw);
-#pragma unroll
-        for (int t8 = 0; t8 < 4; ++t8) {
-          const int col = c * 32 + t8 * 8;
-          const uint32_t off = (col >> 6) * S::SUB + sw128_offset(r, col & 63);
-          float d8[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) d8[u] = dd[t8 * 8 + u];
-          store8(reinterpret_cast<bf16*>(sDST + off), d8);
+        for (int t8 = 0; t8 < 2; ++t8) {
+          const int col = q0 + t8 * 8;
+          *reinterpret_cast<uint4*>(sDST + (col >> 6) * S::SUB + sw128_offset(r, col & 63)) =
+              make_uint4(dw[t8 * 4], dw[t8 * 4 + 1], dw[t8 * 4 + 2], dw[t8 * 4 + 3]);
         }
       }
       tmem_wait_st();
       fence_async_smem();
       tc_fence_before();
-      if (threadIdx.x == 0 && j > 0) {   // pair j-1's dQ reductions have read their slot by now
-        bulk_wait_read();
+      mbar_arrive(p_full);
+      if (threadIdx.x == 0 && j > 0) {   // pair j-1's dQ reductions have read their slot (this
+        bulk_wait_read();                 // thread is idle until the MMAs of pair j complete)
         mbar_arrive(&slot_free[(j - 1) & 1]);
       }
-      mbar_arrive(p_full);
       if (threadIdx.x == 0 && j < 6) DBG_STAMP(42 + 4 * j);
       if (!(ok = mbar_wait(dq_full, j & 1, p.err, 29))) break;
       if (threadIdx.x == 0 && j < 6) DBG_STAMP(43 + 4 * j);
