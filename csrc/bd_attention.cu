@@ -336,6 +336,68 @@ __global__ void bwd_dsum_kernel(const bf16* __restrict__ o, int64_t o_tok, int64
   if (lane == 0) dsum[((int64_t)b * Hq + h) * T + t] = acc;
 }
 
+// Backward prologue of the tcgen05 path: Dsum[b, h, t] = sum_d O * dO for every query row, and
+// the fp32 dQ / dK / dV accumulators of the same rows set to zero in the same pass (a row
+// (b, t, h) zeroes dQ[b, t, h] and, when h is the first head of its GQA group, dK / dV[b, t, h /
+// group]).  D / 8 lanes per row (8 bf16 each), and four rows per lane group loaded before the
+// first reduction so each lane keeps 128 bytes in flight.
+template <int D>
+__global__ void __launch_bounds__(256) bwd_prep_kernel(const bf16* __restrict__ o, int64_t o_tok, int64_t o_b,
+                                                       const bf16* __restrict__ dout, int64_t do_tok, int64_t do_b,
+                                                       float* __restrict__ dsum, float* __restrict__ dq_acc,
+                                                       float* __restrict__ dk_acc, float* __restrict__ dv_acc, int B,
+                                                       int T, int Hq, int group) {
+  constexpr int LPR = D / 8, RPW = 32 / LPR, U = 4;
+  const int lane = threadIdx.x & 31, sub = lane / LPR, j = lane % LPR;
+  const int64_t rows = (int64_t)B * T * Hq;
+  const int Hkv = Hq / group;
+  const int64_t step = (int64_t)gridDim.x * (blockDim.x >> 5) * RPW * U;
+  for (int64_t base = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW * U; base < rows;
+       base += step) {
+    float a[U][8], g[U][8];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t row = base + u * RPW + sub;
+      if (row < rows) {
+        const int h = (int)(row % Hq);
+        const int64_t bt = row / Hq;
+        const int t = (int)(bt % T), b = (int)(bt / T);
+        load8(o + (int64_t)b * o_b + (int64_t)t * o_tok + (int64_t)h * D + j * 8, a[u]);
+        load8(dout + (int64_t)b * do_b + (int64_t)t * do_tok + (int64_t)h * D + j * 8, g[u]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a[u][i] = g[u][i] = 0.f;
+      }
+    }
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      float acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc += a[u][i] * g[u][i];
+#pragma unroll
+      for (int off = LPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+      const int64_t row = base + u * RPW + sub;
+      if (row < rows) {
+        const int h = (int)(row % Hq);
+        const int64_t bt = row / Hq;
+        const int t = (int)(bt % T), b = (int)(bt / T);
+        if (j == 0) dsum[((int64_t)b * Hq + h) * T + t] = acc;
+        float* q = dq_acc + row * D + j * 8;
+        reinterpret_cast<float4*>(q)[0] = z;
+        reinterpret_cast<float4*>(q)[1] = z;
+        if (dk_acc != nullptr && h % group == 0) {
+          const int64_t kr = (bt * Hkv + h / group) * D + j * 8;
+          reinterpret_cast<float4*>(dk_acc + kr)[0] = z;
+          reinterpret_cast<float4*>(dk_acc + kr)[1] = z;
+          reinterpret_cast<float4*>(dv_acc + kr)[0] = z;
+          reinterpret_cast<float4*>(dv_acc + kr)[1] = z;
+        }
+      }
+    }
+  }
+}
+
 struct BwdParams {
   const bf16 *q, *k, *v, *dout;
   int64_t q_tok, k_tok, v_tok, do_tok;
@@ -684,11 +746,30 @@ int bd_attn_fwd(const AttnTensors& t, const int4* meta, const int16_t* fwd_list,
 }
 
 void bd_attn_bwd_prep(const AttnTensors& t, const bf16* dout, int64_t do_tok, int64_t do_b, float* dsum, float* dq_acc,
-                      cudaStream_t s) {
+                      float* dk_acc, float* dv_acc, int sm_count, cudaStream_t s) {
   const int64_t rows = (int64_t)t.B * t.T * t.Hq;
+  const bool vec = (t.D == 64 || t.D == 128 || t.D == 256) && t.o_tok % 8 == 0 && t.o_b % 8 == 0 &&
+                   do_tok % 8 == 0 && do_b % 8 == 0 && (reinterpret_cast<uintptr_t>(t.o) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(dout) & 15) == 0;
+  if (vec) {
+    const int64_t per_block = 8 * (256 / t.D) * 4;   // rows a block covers per step
+    int64_t blocks = (rows + per_block - 1) / per_block;
+    blocks = blocks > (int64_t)sm_count * 8 ? (int64_t)sm_count * 8 : blocks;
+    const int group = t.Hq / t.Hkv;
+#define TRIDA_PREP(DD)                                                                                        \
+  attn::bwd_prep_kernel<DD><<<(int)blocks, 256, 0, s>>>(t.o, t.o_tok, t.o_b, dout, do_tok, do_b, dsum, dq_acc, \
+                                                        dk_acc, dv_acc, t.B, t.T, t.Hq, group)
+    if (t.D == 64) TRIDA_PREP(64); else if (t.D == 128) TRIDA_PREP(128); else TRIDA_PREP(256);
+#undef TRIDA_PREP
+    return;
+  }
   attn::bwd_dsum_kernel<<<ceil_div(rows, 8), 256, 0, s>>>(t.o, t.o_tok, t.o_b, dout, do_tok, do_b, dsum, t.B, t.T,
                                                            t.Hq, t.D);
   cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * t.D, s);
+  if (dk_acc != nullptr) {
+    cudaMemsetAsync(dk_acc, 0, sizeof(float) * (int64_t)t.B * t.T * t.Hkv * t.D, s);
+    cudaMemsetAsync(dv_acc, 0, sizeof(float) * (int64_t)t.B * t.T * t.Hkv * t.D, s);
+  }
 }
 
 void bd_attn_dq_convert(const float* dq_acc, bf16* dq, int64_t dq_tok, int64_t dq_b, int B, int T, int Hq, int D,

@@ -740,11 +740,12 @@ void bd_attn_bwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tenso
   auto dsum = at::empty({a.B, a.Hq, a.T}, lse.options());
   auto dq_acc = at::empty({a.B, a.T, a.Hq, a.D}, lse.options());
   // dK / dV partials of the GQA group's query heads meet in fp32 (one CTA per key tile and query head)
-  auto dkv_acc = at::zeros({2, a.B, a.T, a.Hkv, a.D}, lse.options());
+  // (zeroed, with dQ's accumulator, by the prologue kernel that computes Dsum)
+  auto dkv_acc = at::empty({2, a.B, a.T, a.Hkv, a.D}, lse.options());
   float* dk_acc = dkv_acc.data_ptr<float>();
   float* dv_acc = dk_acc + (int64_t)a.B * a.T * a.Hkv * a.D;
   trida::bd_attn_bwd_prep(a, cbf(dout), dout.stride(1), dout.stride(0), dsum.data_ptr<float>(),
-                          dq_acc.data_ptr<float>(), stream());
+                          dq_acc.data_ptr<float>(), dk_acc, dv_acc, sm_count(), stream());
   const int rc = trida::bd_attn_bwd_sm100(a, cbf(dout), dout.stride(1), dout.stride(0), dsum.data_ptr<float>(),
                                           dq_acc.data_ptr<float>(), dk_acc, dv_acc, mbf(dk), dk.stride(1), dk.stride(0),
                                           mbf(dv), dv.stride(1), dv.stride(0),

@@ -58,7 +58,7 @@ int bd_attn_bwd_sm100(const AttnTensors& t, const bf16* dout, int64_t do_tok, in
                       int64_t dv_tok, int64_t dv_b, const int4* meta, const int16_t* list128t, const int* cnt128t,
                       const uint4* colmask, int flags, float scale, int* err, cudaStream_t s, long long* dbg);
 void bd_attn_bwd_prep(const AttnTensors& t, const bf16* dout, int64_t do_tok, int64_t do_b, float* dsum, float* dq_acc,
-                      cudaStream_t s);
+                      float* dk_acc, float* dv_acc, int sm_count, cudaStream_t s);
 void bd_attn_dq_convert(const float* dq_acc, bf16* dq, int64_t dq_tok, int64_t dq_b, int B, int T, int Hq, int D,
                         int sm_count, cudaStream_t s);
 void bd_attn_tile_masks(const int4* meta, const uint8_t* cls, int B, int T, int flags, uint4* rowmask, uint4* colmask,

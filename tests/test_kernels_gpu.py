@@ -315,6 +315,30 @@ def test_adamw_matches_torch():
     assert rel_err(p, ref.detach()) < 1e-5
 
 
+@pytest.mark.parametrize("n,offset", [(100003, 0), (4096, 3)])
+def test_adamw_bf16_params_match_torch(n, offset):
+    """bf16 parameters updated in place (8-wide vector kernel plus scalar tail; an offset view
+    takes the unaligned path) against torch AdamW in fp32 with the parameter rounded to bf16
+    after every step."""
+    torch.manual_seed(0)
+    base = torch.randn(n + offset, device="cuda").to(torch.bfloat16)
+    p = base[offset:]
+    g = torch.randn(n, device="cuda")
+    ref = p.float().clone().requires_grad_()
+    opt = torch.optim.AdamW([ref], lr=1e-3, betas=(0.9, 0.95), weight_decay=0.1, eps=1e-8)
+    m = torch.zeros(n, device="cuda")
+    v = torch.zeros(n, device="cuda")
+    for step in range(1, 4):
+        ref.grad = g.clone()
+        opt.step()
+        with torch.no_grad():
+            ref.copy_(ref.bfloat16().float())
+        C().adamw(p, None, g, m, v, 1e-3, 0.9, 0.95, 1e-8, 0.1, step, None)
+    assert rel_err(p, ref.detach()) < 2e-3
+    torch.testing.assert_close(m, opt.state[ref]["exp_avg"], rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(v, opt.state[ref]["exp_avg_sq"], rtol=1e-5, atol=1e-7)
+
+
 def test_blocks_match_cpu_reference():
     """Whole attention + MLP sub-blocks, forward and backward, GPU bf16 vs CPU fp32."""
     torch.manual_seed(0)
