@@ -147,6 +147,32 @@ void symm_allreduce(const std::vector<int64_t>& bufs, const std::vector<int64_t>
 // Row-parallel GEMM with the tensor-parallel all-reduce in its epilogue:
 // D = sum over ranks of A_r B_r^T (+ residual).  recv / flags: every rank's receive buffer
 // ([2][world][mcap][N] bf16) and counters ([2][tiles_cap][4] u32); ctr_done: int32 [2], zero at start.
+// gu = A . B^T with B = [gate; up] ([2F, K]) and act = silu(gate) * up, one kernel (TN, bf16)
+void gemm_swiglu(const at::Tensor& A, const at::Tensor& B, const at::Tensor& D, const at::Tensor& act,
+                 int64_t tile) {
+  CHECK_CUDA(A); CHECK_CUDA(B); CHECK_CUDA(D); CHECK_CUDA(act);
+  CHECK_BF16(A); CHECK_BF16(B); CHECK_BF16(D); CHECK_BF16(act);
+  CHECK_ROWMAJOR(A); CHECK_ROWMAJOR(B); CHECK_ROWMAJOR(D); CHECK_ROWMAJOR(act);
+  const int M = A.size(0), K = A.size(1), N = B.size(0), F = N / 2;
+  TORCH_CHECK(B.size(1) == K && N % 128 == 0, "B must be [2F, K] with F a multiple of 64");
+  TORCH_CHECK(D.size(0) == M && D.size(1) == N && act.size(0) == M && act.size(1) == F, "output shapes");
+  if (M == 0) return;
+  trida::GemmArgs a{};
+  a.M = M; a.N = N; a.K = K;
+  a.A = A.data_ptr(); a.lda = A.stride(0);
+  a.B = B.data_ptr(); a.ldb = B.stride(0);
+  a.D = D.data_ptr(); a.ldd = D.stride(0);
+  a.C = nullptr; a.ldc = a.ldd;
+  a.alpha = 1.f; a.beta = 0.f; a.batch = 1;
+  TORCH_CHECK((a.lda * 2) % 16 == 0 && (a.ldb * 2) % 16 == 0 && (a.ldd * 2) % 16 == 0 && (act.stride(0) * 2) % 16 == 0,
+              "GEMM leading dimensions must be 16-byte multiples");
+  TORCH_CHECK((uintptr_t)a.A % 16 == 0 && (uintptr_t)a.B % 16 == 0 && (uintptr_t)a.D % 16 == 0 &&
+                  (uintptr_t)act.data_ptr() % 16 == 0, "GEMM operands must be 16-byte aligned");
+  c10::cuda::CUDAGuard g(A.device());
+  const int rc = trida::gemm_bf16_swiglu(a, act.data_ptr(), act.stride(0), F, (int)tile, sm_count(), stream());
+  TORCH_CHECK(rc == 0, "gemm_bf16_swiglu failed (code ", rc, ")");
+}
+
 void gemm_allreduce(const at::Tensor& A, const at::Tensor& B, const at::Tensor& D,
                     const c10::optional<at::Tensor>& residual, const std::vector<int64_t>& recv,
                     const std::vector<int64_t>& flags, int64_t rank, const at::Tensor& ctr_done, int64_t mcap,
@@ -814,6 +840,8 @@ void adamw(const at::Tensor& param, const c10::optional<at::Tensor>& master, con
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "trida_stack_b200 sm_100a kernels";
   m.def("gemm", &gemm);
+  m.def("gemm_swiglu", &gemm_swiglu, py::arg("A"), py::arg("B"), py::arg("D"), py::arg("act"),
+        py::arg("tile") = 0);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd, py::arg("qkv"), py::arg("qw"), py::arg("kw"), py::arg("cos_t"),

@@ -75,6 +75,10 @@ struct Params {
   unsigned* ar_done;      // CTAs finished in this call (the last one advances ar_ctr)
   float* ar_ws;           // split-K: fp32 partial tiles [tiles * splits][128][256] (this GPU)
   unsigned* ar_tile_ctr;  // split-K: arrivals per (tile, epilogue warp), reset by the last arrival
+  // SwiGLU mode (glu_f > 0, TN, B = [gate; up] with glu_f rows each): a tile covers 128 features,
+  // its B slice stacks the 128 gate rows over the matching 128 up rows, and the epilogue writes
+  // both halves back to D = gu [M, 2 glu_f] plus E = silu(gate) * up [M, glu_f]
+  int glu_f;
 };
 
 __device__ __forceinline__ void red_release_sys(unsigned* p, unsigned v) {
@@ -155,7 +159,8 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kmajor, int 
 template <int MH>
 __global__ void __launch_bounds__(NTHREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmC, const Params p) {
+                const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmC,
+                const __grid_constant__ CUtensorMap tmE, const Params p) {
   using C_ = Cfg<MH>;
   constexpr int BM = C_::BM, STAGES = C_::STAGES, NACC = C_::NACC;
   constexpr int A_BYTES = C_::A_BYTES, STAGE_BYTES = C_::STAGE_BYTES;
@@ -172,7 +177,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t* cbar = bars + 2 * STAGES + 8;      // [4 warps x 2 buffers] C-tile loads
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mt = (p.M + BM - 1) / BM, nt = (p.N + BN - 1) / BN;
+  const int mt = (p.M + BM - 1) / BM, nt = p.glu_f > 0 ? (p.glu_f + 127) / 128 : (p.N + BN - 1) / BN;
   const int units = mt * nt * p.splits;
   const int kb = (p.K + BK - 1) / BK;
 
@@ -211,7 +216,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           unsigned char* st = smem + s * STAGE_BYTES;
           mbar_expect_tx(&full[s], STAGE_BYTES);
           load_operand(st, &tmA, &full[s], p.a_kmajor, m0, k * BK, BM);
-          load_operand(st + A_BYTES, &tmB, &full[s], p.b_kmajor, n0, k * BK, BN);
+          if (p.glu_f > 0) {   // 128 gate rows, then the 128 up rows of the same features
+            tma_load_2d(st + A_BYTES, &tmB, &full[s], k * BK, n0 >> 1);
+            tma_load_2d(st + A_BYTES + 128 * 128, &tmB, &full[s], k * BK, p.glu_f + (n0 >> 1));
+          } else {
+            load_operand(st + A_BYTES, &tmB, &full[s], p.b_kmajor, n0, k * BK, BN);
+          }
         }
       }
       // the final (up to STAGES) loads must land before the CTA retires
@@ -451,6 +461,62 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         continue;
       }
+      if (p.glu_f > 0) {
+        // SwiGLU tile: accumulator columns [0, 128) are the gate features nf0.., [128, 256) the up
+        // features of the same indices.  Each 64-column chunk is packed to bf16 and TMA-stored at
+        // its natural column of gu; a gate chunk stays in registers until its up chunk is read and
+        // gives silu(gate) * up from the bf16-rounded values, TMA-stored into E.
+        const int row0 = m0 + h * 128 + q * 32;
+        const int nf0 = n0 >> 1;
+        auto stage_store = [&](const uint32_t (&w)[32], const CUtensorMap* map, int col) {
+          unsigned char* sb = epi + q * 8192 + ebuf * 4096;
+          if (lane == 0) bulk_wait_read1();           // the store issued from sb two chunks ago has read it
+          __syncwarp();
+          unsigned char* rowp = sb + lane * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<uint4*>(rowp + ((j ^ (lane & 7)) << 4)) =
+                make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(map, sb, col, row0);
+            bulk_commit();
+          }
+          ebuf ^= 1;
+        };
+        auto load_pack = [&](int col, uint32_t (&w)[32]) {
+          uint32_t v0[32], v1[32];
+          tmem_ld32(acc + col, v0);
+          tmem_ld32(acc + col + 32, v1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            w[i] = pack_bf16x2(__uint_as_float(v0[2 * i]) * p.alpha, __uint_as_float(v0[2 * i + 1]) * p.alpha);
+            w[16 + i] = pack_bf16x2(__uint_as_float(v1[2 * i]) * p.alpha, __uint_as_float(v1[2 * i + 1]) * p.alpha);
+          }
+        };
+        // feature chunk k: gate columns [64 k, 64 k + 64), up columns [128 + 64 k, ...)
+#pragma unroll 1
+        for (int k = 0; k < 2; ++k) {
+          const int f0 = nf0 + k * 64;
+          if (row0 >= p.M || f0 >= p.glu_f) continue;   // warp-uniform; glu_f is a multiple of 64
+          uint32_t gw[32], uw[32];
+          load_pack(k * 64, gw);
+          stage_store(gw, &tmD, f0);
+          load_pack(128 + k * 64, uw);
+          stage_store(uw, &tmD, p.glu_f + f0);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float2 g2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw[i]));
+            const float2 u2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&uw[i]));
+            gw[i] = pack_bf16x2(__fdividef(g2.x, 1.f + __expf(-g2.x)) * u2.x,
+                                __fdividef(g2.y, 1.f + __expf(-g2.y)) * u2.y);
+          }
+          stage_store(gw, &tmE, f0);
+        }
+        continue;
+      }
       // Chunks of 128 B per row (32 fp32 / 64 bf16 columns): scale (+ beta * C, C fetched by
       // TMA into the staging tile), write the warp's 32 x 128 B tile in the 128B-swizzled layout
       // and TMA-store it (clipped at the matrix edge by the tensor map); two staging buffers
@@ -617,16 +683,17 @@ int gemm_splitk(int M, int N, int K, int sm_count) {
 
 template <int MH>
 static int launch(const CUtensorMap& mA, const CUtensorMap& mB, const CUtensorMap& mD, const CUtensorMap& mC,
-                  const gemm100::Params& p, int sm_count, cudaStream_t stream) {
+                  const CUtensorMap& mE, const gemm100::Params& p, int sm_count, cudaStream_t stream) {
   using namespace gemm100;
   static bool init = false;
   if (!init) {
     cudaFuncSetAttribute(gemm_kernel<MH>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<MH>::SMEM_BYTES);
     init = true;
   }
-  const int units = ((p.M + Cfg<MH>::BM - 1) / Cfg<MH>::BM) * ((p.N + BN - 1) / BN) * p.splits;
+  const int nt = p.glu_f > 0 ? (p.glu_f + 127) / 128 : (p.N + BN - 1) / BN;
+  const int units = ((p.M + Cfg<MH>::BM - 1) / Cfg<MH>::BM) * nt * p.splits;
   const int grid = units < sm_count ? units : sm_count;
-  gemm_kernel<MH><<<grid, NTHREADS, Cfg<MH>::SMEM_BYTES, stream>>>(mA, mB, mD, mC, p);
+  gemm_kernel<MH><<<grid, NTHREADS, Cfg<MH>::SMEM_BYTES, stream>>>(mA, mB, mD, mC, mE, p);
   return 0;
 }
 
@@ -645,6 +712,7 @@ int gemm_bf16(GemmLayout layout, bool d_fp32, const GemmArgs& a, int tile, int s
   p.D = a.D; p.ldd = a.ldd; p.C = a.C; p.ldc = a.ldc;
   p.alpha = a.alpha; p.beta = a.beta; p.d_fp32 = d_fp32 ? 1 : 0;
   p.err = err_word();
+  p.glu_f = 0;
   p.ar_world = 1; p.ar_rank = 0; p.ar_tiles_cap = 0; p.ar_mcap = 0;
   p.ar_ctr = nullptr; p.ar_done = nullptr; p.ar_ws = nullptr; p.ar_tile_ctr = nullptr;
   for (int i = 0; i < 8; ++i) { p.ar_recv[i] = nullptr; p.ar_flag[i] = nullptr; }
@@ -678,8 +746,8 @@ int gemm_bf16(GemmLayout layout, bool d_fp32, const GemmArgs& a, int tile, int s
   } else {
     mC = mD;
   }
-  if (mh == 2) launch<2>(mA, mB, mD, mC, p, sm_count, stream);
-  else launch<1>(mA, mB, mD, mC, p, sm_count, stream);
+  if (mh == 2) launch<2>(mA, mB, mD, mC, mD, p, sm_count, stream);
+  else launch<1>(mA, mB, mD, mC, mD, p, sm_count, stream);
   if (p.splits > 1) {
     const int64_t n4 = (int64_t)a.M * ((a.N + 3) / 4);
     const int blocks = (int)std::min<int64_t>((n4 + 255) / 256, (int64_t)sm_count * 8);
@@ -700,6 +768,7 @@ int gemm_bf16_allreduce(const GemmArgs& a, const GemmAllreduce& ar, int sm_count
   p.D = a.D; p.ldd = a.ldd; p.C = a.C; p.ldc = a.ldc;
   p.alpha = a.alpha; p.beta = a.beta; p.d_fp32 = 0;
   p.err = err_word();
+  p.glu_f = 0;
   // skinny products split K over otherwise idle SMs; the split partials are summed by the last
   // arriving CTA of each tile before the exchange (workspace: ws_units tiles of 128 x 256 fp32)
   const int kb = (a.K + BK - 1) / BK;
@@ -723,7 +792,34 @@ int gemm_bf16_allreduce(const GemmArgs& a, const GemmAllreduce& ar, int sm_count
   } else {
     mC = mD;
   }
-  launch<1>(mA, mB, mD, mC, p, sm_count, stream);
+  launch<1>(mA, mB, mD, mC, mD, p, sm_count, stream);
+  return cudaGetLastError() == cudaSuccess ? 0 : -13;
+}
+
+int gemm_bf16_swiglu(const GemmArgs& a, void* act, int64_t ld_act, int F, int tile, int sm_count,
+                     cudaStream_t stream) {
+  using namespace gemm100;
+  if (a.batch != 1 || F <= 0 || F % 64 != 0 || a.N != 2 * F) return -40;
+  if (a.C != nullptr && a.beta != 0.f) return -41;
+  const int tiles256 = ((a.M + 255) / 256) * ((F + 127) / 128);
+  const int mh = tile == 1 ? 1 : tile == 2 ? 2 : (2 * tiles256 >= sm_count ? 2 : 1);
+  Params p;
+  p.M = a.M; p.N = a.N; p.K = a.K;
+  p.D = a.D; p.ldd = a.ldd; p.C = nullptr; p.ldc = a.ldd;
+  p.alpha = a.alpha; p.beta = 0.f; p.d_fp32 = 0;
+  p.err = err_word();
+  p.glu_f = F;
+  p.ar_world = 1; p.ar_rank = 0; p.ar_tiles_cap = 0; p.ar_mcap = 0;
+  p.ar_ctr = nullptr; p.ar_done = nullptr; p.ar_ws = nullptr; p.ar_tile_ctr = nullptr;
+  for (int i = 0; i < 8; ++i) { p.ar_recv[i] = nullptr; p.ar_flag[i] = nullptr; }
+  const int kb = (a.K + BK - 1) / BK;
+  p.splits = 1; p.kb_per = kb; p.ws = nullptr;
+  p.a_kmajor = 1; p.b_kmajor = 1;
+  CUtensorMap mA, mB, mD, mE;
+  if (!make_map(&mA, a.A, a.M, a.K, a.lda, 128 * mh) || !make_map(&mB, a.B, a.N, a.K, a.ldb, 128)) return -12;
+  if (!make_epi_map(&mD, a.D, a.M, a.N, a.ldd, false) || !make_epi_map(&mE, act, a.M, F, ld_act, false)) return -14;
+  if (mh == 2) launch<2>(mA, mB, mD, mD, mE, p, sm_count, stream);
+  else launch<1>(mA, mB, mD, mD, mE, p, sm_count, stream);
   return cudaGetLastError() == cudaSuccess ? 0 : -13;
 }
 

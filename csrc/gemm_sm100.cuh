@@ -52,6 +52,12 @@ struct GemmAllreduce {
 };
 int gemm_bf16_allreduce(const GemmArgs& a, const GemmAllreduce& ar, int sm_count, cudaStream_t stream);
 
+// Gate / up projection with SwiGLU in the epilogue (TN, bf16): B = [gate; up] ([2F, K], F a multiple
+// of 64), D = gu = alpha * A B^T ([M, 2F]) and act = silu(gu[:, :F]) * gu[:, F:] ([M, F]) from the
+// bf16-rounded gu values, in one kernel.  `tile`: 0 picks the tile height, 1 = 128 rows, 2 = 256.
+int gemm_bf16_swiglu(const GemmArgs& a, void* act, int64_t ld_act, int F, int tile, int sm_count,
+                     cudaStream_t stream);
+
 // Device int the GEMM's bounded mbarrier waits set (non-zero) on a timeout; null if unallocated.
 int* gemm_error_word();
 

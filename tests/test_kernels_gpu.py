@@ -122,6 +122,30 @@ def test_qk_norm_rope(d, rd, shape):
     assert rel_err(k, R.apply_rope(ks.detach(), cos, sin)) < 1e-2
 
 
+@pytest.mark.parametrize("M,K,F", [(777, 512, 320), (2048, 640, 1280), (130, 2560, 9728)])
+def test_gemm_swiglu_epilogue(M, K, F):
+    """Gate / up GEMM with SwiGLU in the epilogue: gu matches the plain GEMM and act matches the
+    SwiGLU kernel applied to that gu (both from the same bf16-rounded values), for both tile heights.  F = 320 leaves half
+    of the last 128-feature tile past the end; (2048, 1280) takes the 256-row tiles."""
+    torch.manual_seed(0)
+    x = (torch.randn(M, K, device="cuda") * 0.5).to(torch.bfloat16)
+    w = (torch.randn(2 * F, K, device="cuda") / K ** 0.5).to(torch.bfloat16)
+    gu = torch.empty(M, 2 * F, device="cuda", dtype=torch.bfloat16)
+    act = torch.empty(M, F, device="cuda", dtype=torch.bfloat16)
+    C().gemm_swiglu(x, w, gu, act)
+    ref = torch.empty_like(gu)
+    C().gemm(0, x, w, ref, None, 1.0, 0.0, 0)
+    torch.testing.assert_close(gu, ref, rtol=1e-2, atol=1e-2)     # the plain GEMM may split K
+    act_ref = torch.empty_like(act)
+    C().swiglu_fwd(gu, act_ref)
+    torch.testing.assert_close(act, act_ref, rtol=1e-2, atol=1e-3)
+    for tile in (1, 2):
+        act2 = torch.empty_like(act)
+        C().gemm_swiglu(x, w, gu, act2, tile)
+        torch.testing.assert_close(act2, act, rtol=0, atol=0)
+    assert rel_err(gu, x.float() @ w.float().t()) < 1e-2
+
+
 def test_swiglu():
     torch.manual_seed(0)
     M, F = 777, 9728

@@ -29,7 +29,7 @@ KERNELS_PER_CALL = {
     "gemm_error": 0, "gdn_state_numel": 0, "gdn_fwd": 2, "gdn_bwd": 3, "gdn_conv_fwd": 1, "gdn_conv_bwd": 2,
     "gdn_gnorm_fwd": 1, "gdn_gnorm_bwd": 1, "attn_gate_fwd": 1, "attn_gate_bwd": 1,
     "canvas_attention": 2, "kv_append": 1, "canvas_conv": 1, "conv_commit": 1, "gdn_canvas": 2, "gdn_prep_numel": 0, "gdn_commit": 1,
-    "argmax_rows": 1, "conf_argmax_rows": 1, "gemm_allreduce": 1, "symm_malloc": 0, "symm_free": 0, "symm_handle": 0, "symm_open": 0, "symm_close": 0,
+    "argmax_rows": 1, "conf_argmax_rows": 1, "gemm_swiglu": 1, "gemm_allreduce": 1, "symm_malloc": 0, "symm_free": 0, "symm_handle": 0, "symm_open": 0, "symm_close": 0,
     "symm_tensor": 0, "symm_allreduce": 1, "symm_rs_sumsq": 1, "symm_norm_coef": 1, "symm_adamw_ag": 1,
 }
 

@@ -330,10 +330,13 @@ class _MlpBlock(torch.autograd.Function):
         h = torch.empty_like(x)
         _, rstd = C.rmsnorm_fwd(x, norm_w, eps, h)
         gu = torch.empty(M, F2, dtype=x.dtype, device=x.device)
-        gemm(TN, h, wgu, gu)
-        del h
         a = torch.empty(M, F2 // 2, dtype=x.dtype, device=x.device)
-        C.swiglu_fwd(gu, a)
+        if F2 % 128 == 0:
+            C.gemm_swiglu(h, wgu, gu, a)        # SwiGLU in the GEMM epilogue
+        else:
+            gemm(TN, h, wgu, gu)
+            C.swiglu_fwd(gu, a)
+        del h
         out = torch.empty_like(x)
         gemm(TN, a, wd, out, x, 1.0, 1.0)
         # keeping a (M x F bf16) saves one SwiGLU pass in the backward; TRIDA_MLP_RECOMPUTE=1

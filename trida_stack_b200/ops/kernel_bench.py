@@ -57,6 +57,10 @@ def bench_gemm(a):
         A = torch.randn(K, M, device="cuda", dtype=torch.bfloat16)
         B = torch.randn(K, N, device="cuda", dtype=torch.bfloat16)
     D = torch.empty(M, N, device="cuda", dtype=torch.float32 if layout == 2 else torch.bfloat16)
+    if a.op == "gemm_swiglu":   # gate / up projection with SwiGLU in the epilogue (N = 2F)
+        act = torch.empty(M, N // 2, device="cuda", dtype=torch.bfloat16)
+        ms = _time(lambda: C.gemm_swiglu(A, B, D, act, a.tile), a.warmup, a.iters)
+        return ms, {"tflops": 2 * M * N * K / ms / 1e9}, 2 * M * N * K, None
     ms = _time(lambda: C.gemm(layout, A, B, D, None, 1.0, 0.0, a.tile), a.warmup, a.iters)
     return ms, {"tflops": 2 * M * N * K / ms / 1e9}, 2 * M * N * K, None
 
@@ -218,7 +222,7 @@ def bench_elementwise(a):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--op", required=True,
-                    choices=["gemm", "attn_fwd", "attn_bwd", "gdn_fwd", "gdn_bwd", "canvas_attn", "canvas_gdn",
+                    choices=["gemm", "gemm_swiglu", "attn_fwd", "attn_bwd", "gdn_fwd", "gdn_bwd", "canvas_attn", "canvas_gdn",
                              "rmsnorm_fwd", "rmsnorm_bwd", "qk_rope_fwd", "qk_rope_bwd", "swiglu_fwd", "swiglu_bwd"])
     ap.add_argument("--m", type=int, default=24576)
     ap.add_argument("--n", type=int, default=6144)
@@ -236,7 +240,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
     a = ap.parse_args()
-    if a.op == "gemm":
+    if a.op in ("gemm", "gemm_swiglu"):
         ms, extra, flops, nbytes = bench_gemm(a)
     elif a.op.startswith("attn"):
         ms, extra, flops, nbytes = bench_attn(a, a.op == "attn_bwd")
