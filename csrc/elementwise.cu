@@ -418,7 +418,7 @@ __device__ __forceinline__ void load_rope8(const float* cos_t, const float* sin_
 }
 
 template <int D>
-__global__ void __launch_bounds__(256) qk_norm_rope_fwd_vec_kernel(
+__global__ void __launch_bounds__(256, 3) qk_norm_rope_fwd_vec_kernel(
     const bf16* __restrict__ qkv, int64_t ldqkv, const bf16* __restrict__ qw, const bf16* __restrict__ kw,
     const float* __restrict__ cos_t, const float* __restrict__ sin_t, const int* __restrict__ pos,
     bf16* __restrict__ q, bf16* __restrict__ k, float* __restrict__ rstd, int M, int Hq, int Hkv, int rd,
@@ -430,51 +430,64 @@ __global__ void __launch_bounds__(256) qk_norm_rope_fwd_vec_kernel(
   const L ln(threadIdx.x & 31, rd);
   const int H = Hq + Hkv, half = rd >> 1;
   const bool norm = qw != nullptr;
-  float c[8], sn[8], wq[8], wk[8];
+  float c[8], sn[8];
   if (ln.roped) load_rope8(cos_t, sin_t, (int64_t)pos[tok] * half + (ln.first ? ln.e0 : ln.e0 - half), c, sn);
+  // the norm weights stay packed (bf16 pairs) and the loads in flight stay raw: 4 registers each
+  bf16x8 wq8, wk8;
   if (norm) {
-    load8(qw + ln.e0, wq);
-    load8(kw + ln.e0, wk);
+    wq8 = *reinterpret_cast<const bf16x8*>(qw + ln.e0);
+    wk8 = *reinterpret_cast<const bf16x8*>(kw + ln.e0);
   }
   const float sg = ln.first ? -1.f : 1.f;  // first half: x1 c - x2 s;  second half: x2 c + x1 s
   const bf16* src = qkv + (int64_t)tok * ldqkv + ln.e0;
   for (int hb = 0; hb < H; hb += L::HPW * UNR) {
-    float f[UNR][8];
+    bf16x8 raw[UNR];
 #pragma unroll
     for (int u = 0; u < UNR; ++u) {
       const int h = hb + u * L::HPW + ln.sub;
-      if (h < H) {
-        load8(src + (h < Hq ? (int64_t)h * qstride : (int64_t)Hq * qstride + (int64_t)(h - Hq) * D), f[u]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) f[u][i] = 0.f;
-      }
+      if (h < H)
+        raw[u] = *reinterpret_cast<const bf16x8*>(
+            src + (h < Hq ? (int64_t)h * qstride : (int64_t)Hq * qstride + (int64_t)(h - Hq) * D));
+      else
+        raw[u] = bf16x8{};
     }
 #pragma unroll
     for (int u = 0; u < UNR; ++u) {
       const int h = hb + u * L::HPW + ln.sub;
       const bool is_q = h < Hq;
+      float f[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 t = __bfloat1622float2(raw[u].h[i]);
+        f[2 * i] = t.x;
+        f[2 * i + 1] = t.y;
+      }
       float r = 1.f;
       if (norm) {
         float ss = 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) ss += f[u][i] * f[u][i];
+        for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
 #pragma unroll
         for (int o = L::LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         r = rsqrtf(ss / (float)D + eps);
+        const bf16x8& w8 = is_q ? wq8 : wk8;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) f[u][i] *= r * (is_q ? wq[i] : wk[i]);
+        for (int i = 0; i < 4; ++i) {
+          const float2 t = __bfloat1622float2(w8.h[i]);
+          f[2 * i] *= r * t.x;
+          f[2 * i + 1] *= r * t.y;
+        }
       }
       float px[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) px[i] = __shfl_sync(0xffffffffu, f[u][i], ln.partner);
+      for (int i = 0; i < 8; ++i) px[i] = __shfl_sync(0xffffffffu, f[i], ln.partner);
       if (ln.roped)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) f[u][i] = f[u][i] * c[i] + sg * px[i] * sn[i];
+        for (int i = 0; i < 8; ++i) f[i] = f[i] * c[i] + sg * px[i] * sn[i];
       if (h < H) {
         if (ln.e0 == 0) rstd[(int64_t)tok * H + h] = r;
         bf16* dst = is_q ? (q + ((int64_t)tok * Hq + h) * D) : (k + ((int64_t)tok * Hkv + (h - Hq)) * D);
-        store8(dst + ln.e0, f[u]);
+        store8(dst + ln.e0, f);
       }
     }
   }
