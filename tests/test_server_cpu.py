@@ -152,3 +152,18 @@ def test_router_fails_over_and_streams(server):
         assert requests.get(url + "/v1/models").json()["data"]
     finally:
         srv.should_exit = True
+
+
+def test_chat_with_tools_request_path(server):
+    """The request ``eval_fc.py`` sends (functions as OpenAI tools, greedy) is served; a random tiny
+    model emits no call, which scores as incorrect rather than failing."""
+    from trida_stack_b200.evals.function_call import score_case, to_openai_tools
+    funcs = [{"name": "lookup", "description": "find", "parameters": {
+        "type": "dict", "properties": {"city": {"type": "string"}}, "required": ["city"]}}]
+    r = requests.post(server + "/v1/chat/completions", json={
+        "messages": [{"role": "user", "content": "t1 t2"}], "tools": to_openai_tools(funcs), "max_tokens": 4,
+        "temperature": 0}).json()
+    msg = r["choices"][0]["message"]
+    res = score_case({"id": "simple_python_0", "function": funcs}, {"ground_truth": [{"lookup": {"city": ["x"]}}]},
+                     msg)
+    assert res["correct"] is False and res["category"] == "simple_python"
