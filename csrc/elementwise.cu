@@ -95,11 +95,12 @@ __global__ void rmsnorm_bwd_kernel(const bf16* __restrict__ dy, int64_t lddy, co
     }
 }
 
-// Row-per-CTA variants for D = 256 k (<= 8192 forward, <= 5120 backward): D / 8 threads, each owning the same 8 columns of
-// every row it visits (one 16-byte access per tensor and row), grid-stride over rows with the
-// next row's loads issued before the current row's block reduction, so every thread keeps two
+// Row-per-CTA variants for D = 256 k (<= 8192 forward, <= 5120 backward): D / 8 threads (D / 16
+// when D is a multiple of 512, two vectors each), each owning the same columns of every row it
+// visits (16-byte accesses), grid-stride over rows with the next row's loads issued before the
+// current row's block reduction, so every thread keeps two
 // rows of loads in flight.  The per-row sum goes through a double-buffered shared slot per warp
-// (one barrier per row).  The backward keeps its 8 columns of dw in registers across all rows
+// (one barrier per row).  The backward keeps its columns of dw in registers across all rows
 // and adds them once per CTA.
 __device__ __forceinline__ bf16x8 ld_stream8(const bf16* p) {
   uint4 v;
@@ -128,87 +129,128 @@ __device__ __forceinline__ float cta_row_sum(float v, float (*red)[32], int par)
   return t;
 }
 
+template <int VPT>
 __global__ void __launch_bounds__(1024) rmsnorm_fwd_cta_kernel(const bf16* __restrict__ x, int64_t ldx,
                                                                const bf16* __restrict__ w, bf16* __restrict__ y,
                                                                int64_t ldy, float* __restrict__ rstd_out, int M,
                                                                float eps) {
+  // VPT 16-byte vectors per thread, vector v at element (v * blockDim.x + threadIdx.x) * 8
   __shared__ float red[2][32];
-  const int D = blockDim.x * 8, e0 = threadIdx.x * 8;
-  float g[8];
-  load8(w + e0, g);
+  const int D = blockDim.x * 8 * VPT;
+  int e[VPT];
+  float g[VPT][8];
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    e[v] = (v * blockDim.x + threadIdx.x) * 8;
+    load8(w + e[v], g[v]);
+  }
   int row = blockIdx.x, par = 0;
-  bf16x8 cur = row < M ? ld_stream8(x + (int64_t)row * ldx + e0) : bf16x8{};
+  bf16x8 cur[VPT];
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) cur[v] = row < M ? ld_stream8(x + (int64_t)row * ldx + e[v]) : bf16x8{};
   for (; row < M; row += gridDim.x, par ^= 1) {
     const int nrow = row + gridDim.x;
-    const bf16x8 nxt = nrow < M ? ld_stream8(x + (int64_t)nrow * ldx + e0) : bf16x8{};
-    float f[8];
-    unpack8(cur, f);
+    bf16x8 nxt[VPT];
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) nxt[v] = nrow < M ? ld_stream8(x + (int64_t)nrow * ldx + e[v]) : bf16x8{};
+    float f[VPT][8];
     float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+    for (int v = 0; v < VPT; ++v) {
+      unpack8(cur[v], f[v]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += f[v][i] * f[v][i];
+    }
     const float r = rsqrtf(cta_row_sum(ss, red, par) / (float)D + eps);
     if (threadIdx.x == 0 && rstd_out) rstd_out[row] = r;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) f[i] = f[i] * r * g[i];
-    store8(y + (int64_t)row * ldy + e0, f);
-    cur = nxt;
+    for (int v = 0; v < VPT; ++v) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[v][i] = f[v][i] * r * g[v][i];
+      store8(y + (int64_t)row * ldy + e[v], f[v]);
+      cur[v] = nxt[v];
+    }
   }
 }
 
-__global__ void __launch_bounds__(640) rmsnorm_bwd_cta_kernel(const bf16* dy, int64_t lddy, const bf16* x,
+template <int VPT>
+__global__ void __launch_bounds__(VPT == 2 ? 320 : 640) rmsnorm_bwd_cta_kernel(const bf16* dy, int64_t lddy, const bf16* x,
                                                                int64_t ldx, const bf16* __restrict__ w,
                                                                const float* __restrict__ rstd, const bf16* dres,
                                                                int64_t lddres, bf16* dx, int64_t lddx,
                                                                float* __restrict__ dw, int M) {
   __shared__ float red[2][32];
-  const int D = blockDim.x * 8, e0 = threadIdx.x * 8;
-  float g[8], acc[8];
-  load8(w + e0, g);
+  const int D = blockDim.x * 8 * VPT;
+  int e[VPT];
+  float g[VPT][8], acc[VPT][8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int v = 0; v < VPT; ++v) {
+    e[v] = (v * blockDim.x + threadIdx.x) * 8;
+    load8(w + e[v], g[v]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[v][i] = 0.f;
+  }
   int row = blockIdx.x, par = 0;
-  bf16x8 cx{}, cd{}, cr{};
-  if (row < M) {
-    cx = ld_stream8(x + (int64_t)row * ldx + e0);
-    cd = ld_stream8(dy + (int64_t)row * lddy + e0);
-    if (dres) cr = ld_stream8(dres + (int64_t)row * lddres + e0);
+  bf16x8 cx[VPT], cd[VPT], cr[VPT];
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    cx[v] = bf16x8{}; cd[v] = bf16x8{}; cr[v] = bf16x8{};
+    if (row < M) {
+      cx[v] = ld_stream8(x + (int64_t)row * ldx + e[v]);
+      cd[v] = ld_stream8(dy + (int64_t)row * lddy + e[v]);
+      if (dres) cr[v] = ld_stream8(dres + (int64_t)row * lddres + e[v]);
+    }
   }
   for (; row < M; row += gridDim.x, par ^= 1) {
     const int nrow = row + gridDim.x;
-    bf16x8 nx{}, nd{}, nr{};
-    if (nrow < M) {
-      nx = ld_stream8(x + (int64_t)nrow * ldx + e0);
-      nd = ld_stream8(dy + (int64_t)nrow * lddy + e0);
-      if (dres) nr = ld_stream8(dres + (int64_t)nrow * lddres + e0);
+    bf16x8 nx[VPT], nd[VPT], nr[VPT];
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      nx[v] = bf16x8{}; nd[v] = bf16x8{}; nr[v] = bf16x8{};
+      if (nrow < M) {
+        nx[v] = ld_stream8(x + (int64_t)nrow * ldx + e[v]);
+        nd[v] = ld_stream8(dy + (int64_t)nrow * lddy + e[v]);
+        if (dres) nr[v] = ld_stream8(dres + (int64_t)nrow * lddres + e[v]);
+      }
     }
     const float r = rstd[row];
-    float f[8], d[8], o[8];
-    unpack8(cx, f);
-    unpack8(cd, d);
-    if (dres) {
-      unpack8(cr, o);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = 0.f;
-    }
+    float f[VPT][8], d[VPT][8];
     float dot = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) dot += d[i] * g[i] * f[i];
+    for (int v = 0; v < VPT; ++v) {
+      unpack8(cx[v], f[v]);
+      unpack8(cd[v], d[v]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dot += d[v][i] * g[v][i] * f[v][i];
+    }
     dot = cta_row_sum(dot, red, par) * r / (float)D;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float xh = f[i] * r;
-      o[i] += r * (d[i] * g[i] - xh * dot);
-      acc[i] += d[i] * xh;
+    for (int v = 0; v < VPT; ++v) {
+      float o[8];
+      if (dres) {
+        unpack8(cr[v], o);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float xh = f[v][i] * r;
+        o[i] += r * (d[v][i] * g[v][i] - xh * dot);
+        acc[v][i] += d[v][i] * xh;
+      }
+      store8(dx + (int64_t)row * lddx + e[v], o);
+      cx[v] = nx[v];
+      cd[v] = nd[v];
+      cr[v] = nr[v];
     }
-    store8(dx + (int64_t)row * lddx + e0, o);
-    cx = nx;
-    cd = nd;
-    cr = nr;
   }
   if (dw && blockIdx.x < M) {
-    atomicAdd(reinterpret_cast<float4*>(dw + e0), make_float4(acc[0], acc[1], acc[2], acc[3]));
-    atomicAdd(reinterpret_cast<float4*>(dw + e0 + 4), make_float4(acc[4], acc[5], acc[6], acc[7]));
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      atomicAdd(reinterpret_cast<float4*>(dw + e[v]), make_float4(acc[v][0], acc[v][1], acc[v][2], acc[v][3]));
+      atomicAdd(reinterpret_cast<float4*>(dw + e[v] + 4), make_float4(acc[v][4], acc[v][5], acc[v][6], acc[v][7]));
+    }
   }
 }
 
@@ -233,9 +275,15 @@ void rmsnorm_fwd(const bf16* x, int64_t ldx, const bf16* w, bf16* y, int64_t ldy
                  int D, float eps, cudaStream_t s) {
   const int warps = 8;
   if (cta_row_ok(D, 1024) && ldx % 8 == 0 && ldy % 8 == 0 && aligned16(x) && aligned16(y) && aligned16(w)) {
-    const int threads = D / 8;
-    rmsnorm_fwd_cta_kernel<<<cta_row_blocks((const void*)rmsnorm_fwd_cta_kernel, threads, M), threads, 0, s>>>(
-        x, ldx, w, y, ldy, rstd, M, eps);
+    if (D % 512 == 0) {   // two vectors per thread: half the per-row reduction work per byte
+      const int threads = D / 16;
+      rmsnorm_fwd_cta_kernel<2><<<cta_row_blocks((const void*)rmsnorm_fwd_cta_kernel<2>, threads, M), threads, 0,
+                                  s>>>(x, ldx, w, y, ldy, rstd, M, eps);
+    } else {
+      const int threads = D / 8;
+      rmsnorm_fwd_cta_kernel<1><<<cta_row_blocks((const void*)rmsnorm_fwd_cta_kernel<1>, threads, M), threads, 0,
+                                  s>>>(x, ldx, w, y, ldy, rstd, M, eps);
+    }
     return;
   }
   rmsnorm_fwd_kernel<<<ceil_div(M, warps), warps * 32, 0, s>>>(x, ldx, w, y, ldy, rstd, M, D, eps);
@@ -248,9 +296,15 @@ void rmsnorm_bwd(const bf16* dy, int64_t lddy, const bf16* x, int64_t ldx, const
   if (cta_row_ok(D, 640) && lddy % 8 == 0 && ldx % 8 == 0 && lddx % 8 == 0 && (!dres || lddres % 8 == 0) &&
       aligned16(dy) && aligned16(x) && aligned16(w) && aligned16(dx) && (!dres || aligned16(dres)) &&
       (!dw || aligned16(dw))) {
-    const int threads = D / 8;
-    rmsnorm_bwd_cta_kernel<<<cta_row_blocks((const void*)rmsnorm_bwd_cta_kernel, threads, M), threads, 0, s>>>(
-        dy, lddy, x, ldx, w, rstd, dres, lddres, dx, lddx, dw, M);
+    if (D % 512 == 0) {
+      const int threads = D / 16;
+      rmsnorm_bwd_cta_kernel<2><<<cta_row_blocks((const void*)rmsnorm_bwd_cta_kernel<2>, threads, M), threads, 0,
+                                  s>>>(dy, lddy, x, ldx, w, rstd, dres, lddres, dx, lddx, dw, M);
+    } else {
+      const int threads = D / 8;
+      rmsnorm_bwd_cta_kernel<1><<<cta_row_blocks((const void*)rmsnorm_bwd_cta_kernel<1>, threads, M), threads, 0,
+                                  s>>>(dy, lddy, x, ldx, w, rstd, dres, lddres, dx, lddx, dw, M);
+    }
     return;
   }
   const size_t smem = (size_t)warps * D * sizeof(float);

@@ -313,13 +313,24 @@ class Runtime:
 
     def _mlp(self, layer, x):
         h = self._rms(x, layer.post_norm)
-        gu = self._lin(h, layer.wgu)
         if self.cuda:
-            a = torch.empty(gu.shape[0], gu.shape[1] // 2, dtype=gu.dtype, device=gu.device)
-            self.C.swiglu_fwd(gu, a)
+            M, F2 = h.shape[0], layer.wgu.shape[0]
+            a = torch.empty(M, F2 // 2, dtype=h.dtype, device=h.device)
+            if F2 % 128 == 0 and 2 * (-(-M // 128)) * (F2 // 256) >= self._sm_count():
+                # enough 128 x 256 tiles to fill the GPU without splitting K: SwiGLU in the epilogue
+                gu = torch.empty(M, F2, dtype=h.dtype, device=h.device)
+                self.C.gemm_swiglu(h, layer.wgu, gu, a)
+            else:
+                gu = self._lin(h, layer.wgu)
+                self.C.swiglu_fwd(gu, a)
         else:
-            a = R.swiglu(gu)
+            a = R.swiglu(self._lin(h, layer.wgu))
         return self._out(a, layer.wdown, x, getattr(layer, "post_mlp_norm", None))
+
+    def _sm_count(self):
+        if getattr(self, "_sms", None) is None:
+            self._sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        return self._sms
 
     def _out(self, a, w, x, post_norm):
         """Sub-block output: ``x + a w^T`` (residual fused into the GEMM epilogue), or GLM's
