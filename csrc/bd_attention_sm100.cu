@@ -1,24 +1,29 @@
-// Block-diffusion attention forward on the 5th-generation tensor cores (tcgen05 + TMEM).
+// Block-diffusion attention on the 5th-generation tensor cores (tcgen05 + TMEM): forward and backward.
 //
-// CTA = one 128-row query tile of one head.  Warp roles (320 threads):
+// Forward.  CTA = one 128-row query tile of one head.  Warp roles (320 threads):
 //   warps 0-7  softmax, two warpgroups splitting every row: thread (half, r) owns columns
 //              [64 half, 64 half + 64) of query row r == TMEM lane r (warps w and w + 4 share a
 //              TMEM lane quarter), so two warps per SM sub-partition hide each other's exp /
-//              max / pack latencies.  Each reads its half S row with tcgen05.ld, applies the
-//              block-diffusion rule on PARTIAL tiles, exchanges its half-row max with its partner
-//              through shared memory (named barrier per warp pair), keeps the running max / sum,
-//              rescales its half of the O row in TMEM only when the max grows by more than 2^16,
-//              and writes its half P row (bf16) into shared memory in the UMMA K-major
-//              SWIZZLE_128B layout.  Control flow is identical in both halves (a timed-out wait
-//              skips work but keeps meeting the pair barrier), so a pair can never split.
-//   warp 8     MMA issuer (one thread): S_i = Q K_i^T into one of two TMEM S buffers, then
-//              O += P_{i-1} V_{i-1}; completion is signalled with tcgen05.commit on mbarriers.
-//   warp 9     TMA producer (one thread): Q once, K/V tiles into a 2-stage ring (plain per-CTA
-//              tensor loads, each CTA fetching its own tiles).
-// TMEM columns: S0 [0,128), S1 [128,256), O [256, 256+D).  The list of non-empty 128-key tiles
-// (and whether each is FULL or PARTIAL) comes from the same exact classification pass as the
-// other attention kernels.  Every mbarrier wait is bounded; a timeout records an error code in
-// a device word that the host checks, and the CTA still releases its TMEM.
+//              max / pack latencies.  At the start they copy their half of Q row r from the TMA
+//              tile into TMEM (the A operand of every S MMA).  Per key tile each reads its half S
+//              row with tcgen05.ld, applies the block-diffusion rule on PARTIAL tiles, exchanges
+//              its half-row max with its partner through shared memory (named barrier per warp
+//              pair), keeps the running max / sum, rescales its half of the O row in TMEM only when
+//              the max grows by more than 2^16, and writes its half P row as bf16 pairs over its
+//              own S columns in TMEM (the A operand of the PV MMA).  Control flow is identical in
+//              both halves (a timed-out wait skips work but keeps meeting the pair barrier), so a
+//              pair can never split.
+//   warp 8     MMA issuer (one thread): S_i = Q K_i^T into one of two TMEM S buffers (after PV_{i-2},
+//              which read P_{i-2} from the same columns, has completed), then O += P_{i-1} V_{i-1};
+//              only the K / V tiles are read from shared memory.  Completion is signalled with
+//              tcgen05.commit on mbarriers.
+//   warp 9     TMA producer (one thread): Q once, K and V tiles into rings of their own (plain
+//              per-CTA tensor loads, each CTA fetching its own tiles).
+// TMEM columns: S0 [0,128), S1 [128,256), O [256, 256+D), Q [256+D, 256+D+D/2).  O leaves through
+// the idle Q tile by TMA tensor stores.  The list of non-empty 128-key tiles (and whether each is
+// FULL or PARTIAL) comes from the same exact classification pass as the other attention kernels.
+// The backward is described above its kernel.  Every mbarrier wait is bounded; a timeout records
+// an error code in a device word that the host checks, and the CTA still releases its TMEM.
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
