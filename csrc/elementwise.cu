@@ -95,8 +95,8 @@ __global__ void rmsnorm_bwd_kernel(const bf16* __restrict__ dy, int64_t lddy, co
     }
 }
 
-// Row-per-CTA variants for D = 256 k (<= 8192 forward, <= 5120 backward): D / 8 threads (D / 16
-// when D is a multiple of 512, two vectors each), each owning the same columns of every row it
+// Row-per-CTA variants for D = 256 k (<= 8192 forward, <= 5120 backward): D / 8 threads (forward:
+// D / 16 when D is a multiple of 512, two vectors each), each owning the same columns of every row it
 // visits (16-byte accesses), grid-stride over rows with the next row's loads issued before the
 // current row's block reduction, so every thread keeps two
 // rows of loads in flight.  The per-row sum goes through a double-buffered shared slot per warp
@@ -296,15 +296,10 @@ void rmsnorm_bwd(const bf16* dy, int64_t lddy, const bf16* x, int64_t ldx, const
   if (cta_row_ok(D, 640) && lddy % 8 == 0 && ldx % 8 == 0 && lddx % 8 == 0 && (!dres || lddres % 8 == 0) &&
       aligned16(dy) && aligned16(x) && aligned16(w) && aligned16(dx) && (!dres || aligned16(dres)) &&
       (!dw || aligned16(dw))) {
-    if (D % 512 == 0) {
-      const int threads = D / 16;
-      rmsnorm_bwd_cta_kernel<2><<<cta_row_blocks((const void*)rmsnorm_bwd_cta_kernel<2>, threads, M), threads, 0,
-                                  s>>>(dy, lddy, x, ldx, w, rstd, dres, lddres, dx, lddx, dw, M);
-    } else {
-      const int threads = D / 8;
-      rmsnorm_bwd_cta_kernel<1><<<cta_row_blocks((const void*)rmsnorm_bwd_cta_kernel<1>, threads, M), threads, 0,
-                                  s>>>(dy, lddy, x, ldx, w, rstd, dres, lddres, dx, lddx, dw, M);
-    }
+    // one vector per thread: two (137 registers, 0.67 of HBM) lose to one (91 registers, 0.77)
+    const int threads = D / 8;
+    rmsnorm_bwd_cta_kernel<1><<<cta_row_blocks((const void*)rmsnorm_bwd_cta_kernel<1>, threads, M), threads, 0,
+                                s>>>(dy, lddy, x, ldx, w, rstd, dres, lddres, dx, lddx, dw, M);
     return;
   }
   const size_t smem = (size_t)warps * D * sizeof(float);
