@@ -2,10 +2,10 @@
  * Allocation-free C entry point of the global gradient-norm / clip-coefficient kernels.
  *
  * This interface has no counterpart in the reference (trida-stack has no native code at all).
- * It exists for callers that cannot allocate device memory: code running inside a CUDA graph
- * that is being captured with a fixed memory pool, custom allocators or runtimes that forbid
- * cudaMalloc/cudaFree on their hot path, and non-PyTorch hosts (plain C/C++ training loops) that
- * link this library without the PyTorch caching allocator.  The regular entry point gets its
+ * It exists for callers that cannot allocate device memory: runtimes or custom allocators that
+ * own all device memory and forbid cudaMalloc/cudaFree on their hot path, and non-PyTorch hosts
+ * (plain C/C++ training loops) that link this library without the PyTorch caching allocator and
+ * have no allocator of their own to hand it.  The regular entry point gets its
  * partial-sum scratch from PyTorch; this one uses a fixed scratch array compiled into the library
  * instead, so it calls no cudaMalloc, cudaFree or any allocating library routine.
  *

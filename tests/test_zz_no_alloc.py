@@ -1,7 +1,7 @@
 """The allocation-free grad-norm entry point, called through its exported C symbol.
 
-It serves callers that cannot allocate device memory (graph capture with a fixed pool, runtimes
-that forbid cudaMalloc on the hot path, non-PyTorch hosts).  Its results must equal the regular
+It serves callers that cannot allocate device memory (runtimes that own all device memory and
+forbid cudaMalloc on the hot path, non-PyTorch C/C++ hosts without an allocator to hand it).  Its results must equal the regular
 entry point's on two calls in a row (the second call reuses the library's fixed scratch array).
 This file is named so pytest collects it last."""
 import ctypes
