@@ -278,6 +278,63 @@ __global__ void canvas_conv_kernel(const bf16* x, int64_t ldx, const bf16* win, 
   }
 }
 
+// The same canvas convolution for the 4-tap kernel of the models served here: a thread owns 8
+// channels of a 16-row tile, loads its 32 weights once (one 64-byte run of the [C][4] weight) and
+// keeps the three previous input rows in registers, so each input row is read once per tile
+// instead of once per tap.
+constexpr int CONV4_ROWS = 16;
+__global__ void canvas_conv4_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ win,
+                                    const bf16* __restrict__ w, bf16* __restrict__ y, int64_t ldy,
+                                    const int* __restrict__ slot, int B, int blk, int C) {
+  const int C8 = C / 8;
+  const int tiles = (blk + CONV4_ROWS - 1) / CONV4_ROWS;
+  const int64_t n = (int64_t)B * tiles * C8;
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < n; g += (int64_t)gridDim.x * blockDim.x) {
+    const int c8 = (int)(g % C8) * 8;
+    const int64_t rest = g / C8;
+    const int tile = (int)(rest % tiles), b = (int)(rest / tiles);
+    const int j0 = tile * CONV4_ROWS, j1 = min(blk, j0 + CONV4_ROWS);
+    float wt[8][4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {          // 32 consecutive bf16: channel c8 + 2q, c8 + 2q + 1 x 4 taps
+      float f[8];
+      load8(w + (int64_t)c8 * 4 + q * 8, f);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        wt[2 * q][t] = f[t];
+        wt[2 * q + 1][t] = f[4 + t];
+      }
+    }
+    float h[3][8];                          // input rows j - 3, j - 2, j - 1
+#pragma unroll
+    for (int t = 0; t < 3; ++t) {
+      const int src = j0 - 3 + t;
+      if (src >= 0) load8(x + ((int64_t)b * blk + src) * ldx + c8, h[t]);
+      else load8(win + ((int64_t)slot[b] * 3 + (3 + src)) * C + c8, h[t]);
+    }
+    for (int j = j0; j < j1; ++j) {
+      float xv[8], out[8];
+      load8(x + ((int64_t)b * blk + j) * ldx + c8, xv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float acc = 0.f;
+        acc = fmaf(wt[e][0], h[0][e], acc);
+        acc = fmaf(wt[e][1], h[1][e], acc);
+        acc = fmaf(wt[e][2], h[2][e], acc);
+        acc = fmaf(wt[e][3], xv[e], acc);
+        out[e] = acc / (1.f + expf(-acc));
+      }
+      store8(y + ((int64_t)b * blk + j) * ldy + c8, out);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        h[0][e] = h[1][e];
+        h[1][e] = h[2][e];
+        h[2][e] = xv[e];
+      }
+    }
+  }
+}
+
 // window[slot] <- last K-1 rows of [window ; x rows 0..adv-1] (rows of entry b at x + b*rows_per*ldx)
 __global__ void conv_commit_kernel(const bf16* x, int64_t ldx, int rows_per, bf16* win, const int* slot,
                                    const int* adv, int B, int C, int K) {
@@ -443,6 +500,12 @@ void kv_append(const bf16* k, const bf16* v, int64_t ldv, bf16* kc, bf16* vc, co
 
 void canvas_conv(const bf16* x, int64_t ldx, const bf16* win, const bf16* w, bf16* y, int64_t ldy, const int* slot,
                  int B, int blk, int C, int K, cudaStream_t s) {
+  if (K == 4 && C % 8 == 0 && ldx % 8 == 0 && ldy % 8 == 0) {
+    const int64_t n4 = (int64_t)B * ((blk + serve::CONV4_ROWS - 1) / serve::CONV4_ROWS) * (C / 8);
+    const int blocks = (int)std::min<int64_t>((n4 + 255) / 256, 8192);
+    serve::canvas_conv4_kernel<<<blocks, 256, 0, s>>>(x, ldx, win, w, y, ldy, slot, B, blk, C);
+    return;
+  }
   const int64_t n = (int64_t)B * blk * (C / 8);
   const int blocks = (int)std::min<int64_t>((n + 255) / 256, 8192);
   serve::canvas_conv_kernel<<<blocks, 256, 0, s>>>(x, ldx, win, w, y, ldy, slot, B, blk, C, K);
