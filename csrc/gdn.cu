@@ -328,13 +328,32 @@ __device__ __forceinline__ void readout2(const float (&S0)[RPT], const float (&S
   o1 = rsum8(c0 + c1);
 }
 
-// v of column group cg for rows [0, n) into dst[n][CG]
-__device__ __forceinline__ void stage_v(const Args& a, float* dst, int b, int hv, int cg, int n) {
+// v of column group cg for rows [tok0, tok0 + n) into dst[n][CG]
+__device__ __forceinline__ void stage_v(const Args& a, float* dst, int b, int hv, int cg, int tok0, int n) {
   for (int idx = threadIdx.x; idx < n * CG; idx += NT) {
     const int j = idx / CG, c = idx % CG;
-    const int64_t row = (int64_t)b * a.T + j;
+    const int64_t row = (int64_t)b * a.T + tok0 + j;
     dst[idx] = __bfloat162float(a.mixed[row * a.ldm + 2 * a.Hk * DK + hv * DV + cg * CG + c]);
   }
+}
+
+// outputs of both groups for rows [tok0, tok0 + n) from the staging buffers
+__device__ __forceinline__ void store_o2(const Args& a, const Stage& s, const float* ob1, int b, int hv, int cg,
+                                         int tok0, int n) {
+  store_o(a, s, b, hv, cg, tok0, n);
+  for (int idx = threadIdx.x; idx < n * CG; idx += NT) {
+    const int j = idx / CG, c = idx % CG;
+    a.o[((int64_t)b * a.T + tok0 + j) * (a.Hv * DV) + hv * DV + (cg + 1) * CG + c] = __float2bfloat16(ob1[idx]);
+  }
+}
+
+// Rows are staged CANVAS_CHUNK at a time (about 21 KB of shared memory per CTA instead of 81 KB for
+// a 63-row canvas), so several CTAs share an SM and hide each other's step latency; the mask rows'
+// readouts (from the state after every row) take a second pass over their q rows.
+constexpr int CANVAS_CHUNK = 16;
+__host__ __device__ inline size_t canvas2_floats(int T) {
+  const int ch = T < CANVAS_CHUNK ? T : CANVAS_CHUNK;
+  return stage_floats(ch, false) + (size_t)ch * CG;
 }
 
 __global__ void __launch_bounds__(NT) canvas2_kernel(const Args a, const float* qk, const float* ab, const float* ssm,
@@ -342,9 +361,10 @@ __global__ void __launch_bounds__(NT) canvas2_kernel(const Args a, const float* 
   extern __shared__ float smem[];
   const int cg = 2 * blockIdx.x, hv = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, col = tid / RP, rp = tid % RP;
-  const Stage s = carve(smem, a.T, false);
+  const int ch = min(a.T, CANVAS_CHUNK);
+  const Stage s = carve(smem, ch, false);
   float* v1 = s.dO;
-  float* ob1 = smem + stage_floats(a.T, false);
+  float* ob1 = smem + stage_floats(ch, false);
   const float* base = ssm + (((int64_t)slot[b] * a.Hv + hv) * NCG + cg) * (RPT * NT);
   float S0[RPT], S1[RPT];
 #pragma unroll
@@ -352,33 +372,45 @@ __global__ void __launch_bounds__(NT) canvas2_kernel(const Args a, const float* 
     S0[i] = base[i * NT + tid];
     S1[i] = base[RPT * NT + i * NT + tid];
   }
-  stage_prepped(a, s, qk, ab, b, hv, cg, 0, a.T, -1, false);
-  stage_v(a, v1, b, hv, cg + 1, a.T);
-  __syncthreads();
-  for (int j = 0; j < a.T; ++j) {
-    fwd_step2(S0, S1, s.k + j * DK + rp * 4, s.al[j], s.be[j], s.v[j * CG + col], v1[j * CG + col]);
-    if (j < n_clean) {
+  for (int c0 = 0; c0 < a.T; c0 += ch) {
+    const int n = min(ch, a.T - c0);
+    __syncthreads();                       // the previous chunk's stage and outputs are consumed
+    stage_prepped(a, s, qk, ab, b, hv, cg, c0, n, -1, false);
+    stage_v(a, v1, b, hv, cg + 1, c0, n);
+    __syncthreads();
+    for (int j = 0; j < n; ++j) {
+      fwd_step2(S0, S1, s.k + j * DK + rp * 4, s.al[j], s.be[j], s.v[j * CG + col], v1[j * CG + col]);
+      if (c0 + j < n_clean) {
+        float o0, o1;
+        readout2(S0, S1, s.q + j * DK + rp * 4, o0, o1);
+        if (rp == 0) {
+          s.ob[j * CG + col] = o0;
+          ob1[j * CG + col] = o1;
+        }
+      }
+    }
+    __syncthreads();
+    const int nout = min(n, n_clean - c0);
+    if (nout > 0) store_o2(a, s, ob1, b, hv, cg, c0, nout);
+  }
+  const bool single = a.T <= ch;          // one chunk: the mask rows' q are still staged
+  for (int c0 = max(n_clean, 0); c0 < a.T; c0 += ch) {
+    const int n = min(ch, a.T - c0), off = single ? c0 : 0;
+    __syncthreads();
+    if (!single) {
+      stage_prepped(a, s, qk, ab, b, hv, cg, c0, n, -1, false);
+      __syncthreads();
+    }
+    for (int j = 0; j < n; ++j) {
       float o0, o1;
-      readout2(S0, S1, s.q + j * DK + rp * 4, o0, o1);
+      readout2(S0, S1, s.q + (off + j) * DK + rp * 4, o0, o1);
       if (rp == 0) {
         s.ob[j * CG + col] = o0;
         ob1[j * CG + col] = o1;
       }
     }
-  }
-  for (int j = n_clean; j < a.T; ++j) {
-    float o0, o1;
-    readout2(S0, S1, s.q + j * DK + rp * 4, o0, o1);
-    if (rp == 0) {
-      s.ob[j * CG + col] = o0;
-      ob1[j * CG + col] = o1;
-    }
-  }
-  __syncthreads();
-  store_o(a, s, b, hv, cg, 0, a.T);
-  for (int idx = threadIdx.x; idx < a.T * CG; idx += NT) {
-    const int j = idx / CG, c = idx % CG;
-    a.o[((int64_t)b * a.T + j) * (a.Hv * DV) + hv * DV + (cg + 1) * CG + c] = __float2bfloat16(ob1[idx]);
+    __syncthreads();
+    store_o2(a, s, ob1, b, hv, cg, c0, n);
   }
 }
 
@@ -387,9 +419,10 @@ __global__ void __launch_bounds__(NT) commit2_kernel(const Args a, const float* 
   extern __shared__ float smem[];
   const int cg = 2 * blockIdx.x, hv = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, col = tid / RP, rp = tid % RP;
-  const Stage s = carve(smem, a.T, false);
+  const int ch = min(a.T, CANVAS_CHUNK);
+  const Stage s = carve(smem, ch, false);
   float* v1 = s.dO;
-  const int n = min(adv[b], a.T);
+  const int total = min(adv[b], a.T);
   float* base = ssm + (((int64_t)slot[b] * a.Hv + hv) * NCG + cg) * (RPT * NT);
   float S0[RPT], S1[RPT];
 #pragma unroll
@@ -397,11 +430,15 @@ __global__ void __launch_bounds__(NT) commit2_kernel(const Args a, const float* 
     S0[i] = base[i * NT + tid];
     S1[i] = base[RPT * NT + i * NT + tid];
   }
-  stage_prepped(a, s, qk, ab, b, hv, cg, 0, n, -1, false);
-  stage_v(a, v1, b, hv, cg + 1, n);
-  __syncthreads();
-  for (int j = 0; j < n; ++j)
-    fwd_step2(S0, S1, s.k + j * DK + rp * 4, s.al[j], s.be[j], s.v[j * CG + col], v1[j * CG + col]);
+  for (int c0 = 0; c0 < total; c0 += ch) {
+    const int n = min(ch, total - c0);
+    __syncthreads();
+    stage_prepped(a, s, qk, ab, b, hv, cg, c0, n, -1, false);
+    stage_v(a, v1, b, hv, cg + 1, c0, n);
+    __syncthreads();
+    for (int j = 0; j < n; ++j)
+      fwd_step2(S0, S1, s.k + j * DK + rp * 4, s.al[j], s.be[j], s.v[j * CG + col], v1[j * CG + col]);
+  }
 #pragma unroll
   for (int i = 0; i < RPT; ++i) {
     base[i * NT + tid] = S0[i];
@@ -1056,8 +1093,7 @@ int gdn_canvas(const GdnParams& p, float* prep, const float* ssm, const int* slo
   Args a = make_args(p);
   static bool init = false;
   if (!init) {
-    const int mx = (int)(stage_floats(MAXCH, false) * sizeof(float));
-    const int mx2 = mx + (int)(MAXCH * CG * sizeof(float));
+    const int mx2 = (int)(canvas2_floats(MAXCH) * sizeof(float));
     cudaFuncSetAttribute(canvas2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, mx2);
     cudaFuncSetAttribute(commit2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, mx2);
     init = true;
@@ -1068,8 +1104,8 @@ int gdn_canvas(const GdnParams& p, float* prep, const float* ssm, const int* slo
   const int64_t warps = (int64_t)rows * (2 * a.Hk + 1);
   prep_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(a, qk, ab, rows);
   // two column groups per CTA (see canvas2_kernel)
-  canvas2_kernel<<<dim3(NCG / 2, a.Hv, a.B), NT, (stage_floats(a.T, false) + a.T * CG) * sizeof(float), st>>>(
-      a, qk, ab, ssm, slot, n_clean);
+  canvas2_kernel<<<dim3(NCG / 2, a.Hv, a.B), NT, canvas2_floats(a.T) * sizeof(float), st>>>(a, qk, ab, ssm, slot,
+                                                                                          n_clean);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
@@ -1080,8 +1116,8 @@ int gdn_commit(const GdnParams& p, const float* prep, float* ssm, const int* slo
   const int rows = a.B * a.T;
   const float* qk = prep;
   const float* ab = prep + (int64_t)rows * 2 * a.Hk * DK;
-  commit2_kernel<<<dim3(NCG / 2, a.Hv, a.B), NT, (stage_floats(a.T, false) + a.T * CG) * sizeof(float), st>>>(
-      a, qk, ab, ssm, slot, adv);
+  commit2_kernel<<<dim3(NCG / 2, a.Hv, a.B), NT, canvas2_floats(a.T) * sizeof(float), st>>>(a, qk, ab, ssm, slot,
+                                                                                          adv);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
