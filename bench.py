@@ -32,7 +32,7 @@ import torch
 import torch.distributed as dist
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-BASELINE_TPS = None  # BASELINE.md publishes no number for this config (H100 figures are other configs)
+BASELINE_TPS = None  # the reference publishes no number for this config (its H100 figures are for other configs)
 METRIC = "4B block-diffusion SFT tokens/s"
 PROMPT, RESP, MB, BD = 1024, 1024, 4, 32
 VOCAB = 151936
