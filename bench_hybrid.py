@@ -67,6 +67,9 @@ def main():
     ap.add_argument("--mb", type=int, default=1)
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--comm", choices=["fused", "nccl"], default="fused")
+    ap.add_argument("--kernel-breakdown", type=int, default=0, metavar="STEPS",
+                    help="after the timed steps, print the per-kernel device-time table of STEPS more steps "
+                         "(taken under the PyTorch profiler; not a benchmark number)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -132,6 +135,16 @@ def main():
                        "row": "[prompt 2048 | response 1024] as [x0 ; xt_1 ; xt_2] (9216 forward tokens)",
                        "bd_size": BD, "decision": "pointer head, every 4th step, weight 0.5",
                        "parallelism": f"dp{world}"}}), flush=True)
+    if args.kernel_breakdown > 0 and rank == 0 and world == 1:
+        from trida_stack_b200.utils.trace import kernel_breakdown
+        i0 = args.warmup + args.steps
+        extra = iter(range(args.kernel_breakdown))
+
+        def one():
+            j = next(extra)
+            engine.micro_step(batches[(i0 + j) % len(batches)])
+            engine.optimizer_step(i0 + j)
+        kernel_breakdown(one, args.kernel_breakdown)
     if world > 1:
         dist.destroy_process_group()
 

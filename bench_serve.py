@@ -47,6 +47,9 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-graphs", action="store_true", help="launch every kernel eagerly (no CUDA graphs)")
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel ranks (launch with torchrun)")
+    ap.add_argument("--kernel-breakdown", type=int, default=0, metavar="STEPS",
+                    help="after the timed run, print the per-kernel device-time table of STEPS eager decode "
+                         "steps of a fresh batch (taken under the PyTorch profiler; not a benchmark number)")
     ap.add_argument("--tp-fused", action="store_true",
                     help="TP all-reduce in the GEMM epilogue instead of a separate kernel after the GEMM")
     args = ap.parse_args()
@@ -125,6 +128,14 @@ def main():
                    "tp_allreduce": ("fused into the GEMM epilogue" if args.tp_fused else "separate peer-memory kernel")
                    if world > 1 else None},
         "data": "synthetic uniform prompts, random-init weights", "dtype": "bf16"}), flush=True)
+    if args.kernel_breakdown > 0 and world == 1:
+        from trida_stack_b200.utils.trace import kernel_breakdown
+        for p in prompts(args.requests):
+            eng.submit(__import__("trida_stack_b200.serve", fromlist=["Request"]).Request(
+                p, args.kernel_breakdown + 2, SamplingParams(temperature=0.0)))
+        eng._admit()
+        eng._decode()
+        kernel_breakdown(eng._decode, args.kernel_breakdown)
     _finish(rt, world)
 
 

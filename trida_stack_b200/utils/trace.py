@@ -110,3 +110,27 @@ class RequestTrace:
                "latency_s": None if req.t_done is None else round(req.t_done - req.t_submit, 4)}
         self._fh.write(json.dumps(rec) + "\n")
         self._fh.flush()
+
+
+def kernel_breakdown(fn, steps=1, top=16, out=None):
+    """Per-kernel device-time shares of ``steps`` calls of ``fn`` (CUDA activity of the PyTorch
+    profiler), printed as a table to ``out`` (stderr by default) and returned as rows of
+    (share, total ms, launches, kernel).  For finding where a step's time goes; the numbers are
+    taken under a profiler and are not benchmark values."""
+    import sys
+
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(steps):
+            fn()
+        torch.cuda.synchronize()
+    ev = [(e.device_time_total, e.count, e.key) for e in prof.key_averages() if e.device_time_total > 0]
+    ev.sort(reverse=True)
+    tot = sum(t for t, _, _ in ev) or 1.0
+    rows = [(t / tot, t / 1e3, c, k) for t, c, k in ev[:top]]
+    out = out or sys.stderr
+    print(f"kernel breakdown: {tot / 1e3:.1f} ms device time over {steps} step(s)", file=out)
+    for share, ms, c, k in rows:
+        print(f"{100 * share:5.1f}% {ms:9.2f} ms x{c:5d}  {k[:100]}", file=out)
+    return rows
