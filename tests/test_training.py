@@ -195,3 +195,14 @@ def test_step_tracer_and_request_trace(tmp_path, monkeypatch):
     eng.generate([[1, 2, 3], [4, 5, 6, 7]], max_new_tokens=6)
     lines = [_json.loads(l) for l in open(tmp_path / "req.jsonl")]
     assert len(lines) == 2 and all(l["output_tokens"] == 6 and l["forwards"] > 0 for l in lines)
+
+
+def test_kernel_breakdown_runs_and_reports(capsys):
+    """``--kernel-breakdown``'s helper: profiles the given steps and prints one table (on a CPU-only
+    machine it has no device kernels to list and returns no rows)."""
+    from trida_stack_b200.utils.trace import kernel_breakdown
+    calls = []
+    rows = kernel_breakdown(lambda: calls.append(torch.ones(64).sum()), steps=3)
+    assert len(calls) == 3
+    assert "kernel breakdown" in capsys.readouterr().err
+    assert all(0.0 <= r[0] <= 1.0 for r in rows)

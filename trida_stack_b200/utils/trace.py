@@ -120,11 +120,14 @@ def kernel_breakdown(fn, steps=1, top=16, out=None):
     import sys
 
     from torch.profiler import ProfilerActivity, profile
-    torch.cuda.synchronize()
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+    cuda = torch.cuda.is_available()
+    if cuda:
+        torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA] if cuda else [ProfilerActivity.CPU]) as prof:
         for _ in range(steps):
             fn()
-        torch.cuda.synchronize()
+        if cuda:
+            torch.cuda.synchronize()
     ev = [(e.device_time_total, e.count, e.key) for e in prof.key_averages() if e.device_time_total > 0]
     ev.sort(reverse=True)
     tot = sum(t for t, _, _ in ev) or 1.0
