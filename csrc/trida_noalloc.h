@@ -22,6 +22,14 @@
  *     Each call overwrites every scratch value it reads, so nothing needs clearing between calls.
  *   - The caller passes and owns every input (device pointers to fp32 gradient buffers, their
  *     element counts on the host) and both outputs (one device float each).
+ *   - Every gradient pointer must be 16-byte aligned (the kernels read float4 vectors).  A null or
+ *     misaligned pointer, a negative size or n_buffers <= 0 returns
+ *     TRIDA_NOALLOC_ERR_INVALID_ARGUMENT before anything is launched.
+ *   - A CUDA error already pending on entry (from the caller's own earlier work) is left in place
+ *     and reported as TRIDA_NOALLOC_ERR_PENDING; nothing is launched.
+ *   - The scratch address is looked up once per device number and cached for the life of the
+ *     process, so only each device's primary context is supported (the CUDA runtime's default,
+ *     also PyTorch's), and the device must not be reset (cudaDeviceReset) after the first call.
  */
 #ifndef TRIDA_NOALLOC_H_
 #define TRIDA_NOALLOC_H_
@@ -40,6 +48,7 @@ extern "C" {
 #define TRIDA_NOALLOC_ERR_NO_DEVICE 3
 #define TRIDA_NOALLOC_ERR_SYMBOL_ADDRESS 4
 #define TRIDA_NOALLOC_ERR_LAUNCH 5
+#define TRIDA_NOALLOC_ERR_PENDING 6
 
 /* norm_out = ||concat(grads)||_2 ; coef_out = min(1, max_norm / (norm + 1e-6)), both written on
  * the device in stream order (no host synchronisation).  Returns TRIDA_NOALLOC_OK or an error. */

@@ -63,6 +63,30 @@ def test_cuda_runtime_matches_cpu(cfg):
         assert _rel(a, b) < 3e-2, _rel(a, b)
 
 
+@pytest.mark.parametrize("cfg", [_hybrid(256), _hybrid(128)], ids=["hybrid-d256", "hybrid-d128"])
+def test_cuda_runtime_long_canvases_match_cpu(cfg):
+    """Canvases longer than one 16-row staging chunk (33 and 63 rows, token-causal row counts that
+    are not multiples of 16) and commits that cross a chunk boundary, vs the CPU statement."""
+    dec = _init(cfg)
+    dec_g = copy.deepcopy(dec).to("cuda", torch.bfloat16)
+    torch.manual_seed(3)
+    ids = torch.randint(0, 500, (3, 200))
+    out = {}
+    for name, d in (("cpu", dec), ("gpu", dec_g)):
+        rt = Runtime(d, max_slots=4, max_len=320)
+        slots = [rt.alloc() for _ in range(3)]
+        last = rt.prefill(slots, ids[:, :37].tolist())
+        lg = rt.canvas(slots, ids[:, 37:100], 32)         # draft block 32: 63 rows, 32 token-causal
+        rt.commit(slots, [20, 17, 32])
+        lg2 = rt.canvas(slots, ids[:, 100:133], 17)       # 33 rows, 17 token-causal
+        rt.commit(slots, [17, 5, 16])
+        lg3 = rt.canvas(slots, ids[:, 133:140], 4)
+        rt.commit(slots, [3, 4, 1])
+        out[name] = [t.float().cpu() for t in (last, lg, lg2, lg3)]
+    for a, b in zip(out["gpu"], out["cpu"]):
+        assert _rel(a, b) < 3e-2, _rel(a, b)
+
+
 @pytest.mark.parametrize("mode", ["self-spec", "causal", "diffusion"])
 def test_cuda_engine_graphs_match_eager(mode):
     dec = _init(_hybrid(256)).to("cuda", torch.bfloat16)
