@@ -837,6 +837,53 @@ void adamw(const at::Tensor& param, const c10::optional<at::Tensor>& master, con
 
 }  // namespace
 
+// Chunked gated-delta forward (gdn_chunk.cu).  bufs = [qk (bf16 [B*T, Hk, 2, 128]), gb (fp32
+// [B*T, Hv, 2]), wn, ut, kt, u (bf16 [B*T, Hv, 128] each), gamma (fp32 [B, Hv, nch]), ckpt (bf16
+// [B, Hv, nch, 128, 128])]; geo = [B, T, Hk, Hv, mode, L, V, C, causal_clean, causal_noisy].
+void gdn_chunk_fwd(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor& gb, const at::Tensor& A_log,
+                   const at::Tensor& dt_bias, const c10::optional<at::Tensor>& doc, const at::Tensor& o,
+                   std::vector<at::Tensor> bufs, const at::Tensor& err, std::vector<int64_t> geo, double scale,
+                   const c10::optional<at::Tensor>& final_state) {
+  TORCH_CHECK(geo.size() == 10 && bufs.size() == 8, "gdn_chunk_fwd: geo / bufs size");
+  const int64_t B = geo[0], T = geo[1], Hk = geo[2], Hv = geo[3], mode = geo[4], L = geo[5], V = geo[6], C = geo[7];
+  auto q = gdn_params(mixed, ga, gb, A_log, dt_bias, doc, B, T, Hk, Hv, mode, L, V, C, geo[8] != 0, geo[9] != 0,
+                      scale);
+  TORCH_CHECK(C == 16 || C == 32 || C == 64, "chunk length must be 16, 32 or 64");
+  const int64_t Lc = mode ? L : T;
+  TORCH_CHECK(!mode || L % C == 0, "two-stream: the stream length must be a multiple of the block");
+  TORCH_CHECK(mixed.stride(0) % 8 == 0, "mixed row stride must be a multiple of 8 (TMA)");
+  const int64_t nch = (Lc + C - 1) / C;
+  const int64_t rows = B * T;
+  auto need = [&](const at::Tensor& t, at::ScalarType ty, int64_t n, const char* what) {
+    CHECK_CUDA(t);
+    TORCH_CHECK(t.scalar_type() == ty && t.is_contiguous() && t.numel() >= n, "gdn_chunk_fwd: bad buffer ", what);
+  };
+  need(bufs[0], at::kBFloat16, rows * Hk * 2 * 128, "qk");
+  need(bufs[1], at::kFloat, rows * Hv * 2, "gb");
+  for (int i = 2; i < 6; ++i) need(bufs[i], at::kBFloat16, rows * Hv * 128, "rows");
+  need(bufs[6], at::kFloat, B * Hv * nch, "gamma");
+  need(bufs[7], at::kBFloat16, B * Hv * nch * 128 * 128, "ckpt");
+  CHECK_BF16(o); TORCH_CHECK(o.is_contiguous() && o.numel() == rows * Hv * 128, "o must be [B*T, Hv*128]");
+  TORCH_CHECK(err.scalar_type() == at::kInt && err.is_cuda(), "err must be an int32 CUDA word");
+  trida::GdnChunkParams p{};
+  p.B = B; p.T = T; p.Hk = Hk; p.Hv = Hv; p.mode = mode; p.L = L; p.V = V; p.C = C; p.nch = nch;
+  p.causal_clean = geo[8]; p.causal_noisy = geo[9];
+  p.doc = q.doc; p.mixed = q.mixed; p.ldm = q.ldm; p.ga = q.ga; p.gbeta = q.gb; p.ldg = q.ldg;
+  p.A_log = q.A_log; p.dt_bias = q.dt_bias; p.scale = (float)scale;
+  p.qk = mbf(bufs[0]); p.gb = bufs[1].data_ptr<float>();
+  p.wn = mbf(bufs[2]); p.ut = mbf(bufs[3]); p.kt = mbf(bufs[4]); p.u = mbf(bufs[5]);
+  p.gamma = bufs[6].data_ptr<float>(); p.ckpt = mbf(bufs[7]); p.o = mbf(o);
+  p.err = err.data_ptr<int>();
+  if (final_state.has_value() && final_state->defined()) {
+    TORCH_CHECK(final_state->scalar_type() == at::kFloat && final_state->is_contiguous() &&
+                final_state->numel() == B * Hv * 128 * 128, "final_state must be fp32 [B, Hv, 128, 128]");
+    p.final_state = final_state->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard g(mixed.device());
+  const int rc = trida::gdn_chunk_fwd(p, stream());
+  TORCH_CHECK(rc == 0, "gdn_chunk_fwd failed with code ", rc);
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "trida_stack_b200 sm_100a kernels";
   m.def("gemm", &gemm);
@@ -882,6 +929,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_norm_coef", &symm_norm_coef);
   m.def("symm_adamw_ag", &symm_adamw_ag);
   m.def("gdn_state_numel", &gdn_state_numel);
+  m.def("gdn_chunk_fwd", &gdn_chunk_fwd);
   m.def("gdn_fwd", &gdn_fwd, py::arg("mixed"), py::arg("ga"), py::arg("gb"), py::arg("A_log"), py::arg("dt_bias"),
         py::arg("doc"), py::arg("o"), py::arg("ckpt"), py::arg("B"), py::arg("T"), py::arg("Hk"), py::arg("Hv"),
         py::arg("mode"), py::arg("L"), py::arg("V"), py::arg("bd"), py::arg("causal_clean"), py::arg("causal_noisy"),

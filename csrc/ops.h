@@ -99,6 +99,27 @@ int gdn_canvas(const GdnParams& p, float* prep, const float* ssm, const int* slo
 int gdn_commit(const GdnParams& p, const float* prep, float* ssm, const int* slot, const int* adv, cudaStream_t s);
 int gdn_bwd(const GdnParams& p, bf16* dmixed, int64_t lddm, bf16* dga, bf16* dgb, int64_t lddg, float* dA_log,
             float* ddt_bias, cudaStream_t s);
+// ---- chunked (WY) gated-delta rule on tcgen05 (gdn_chunk.cu) ----
+// C: chunk length (64 causal; the diffusion block for the two-stream layout, 16 / 32 / 64).
+struct GdnChunkParams {
+  int B, T, Hk, Hv;
+  int mode, L, V, C, nch;     // nch: clean-stream chunks per row
+  int causal_clean, causal_noisy;
+  const uint8_t* doc;
+  const bf16* mixed; int64_t ldm;
+  const bf16* ga; const bf16* gbeta; int64_t ldg;
+  const float* A_log; const float* dt_bias;
+  float scale;
+  bf16* qk;        // [B*T, Hk, 2, 128] normalised q (times scale) / k
+  float* gb;       // [B*T, Hv, 2] log-decay, beta
+  bf16* wn; bf16* ut; bf16* kt; bf16* u;   // [B*T, Hv, 128] each
+  float* gamma;    // [B, Hv, nch]
+  bf16* ckpt;      // [B, Hv, nch, 128, 128]
+  bf16* o;         // [B*T, Hv*128]
+  float* final_state;
+  int* err;
+};
+int gdn_chunk_fwd(const GdnChunkParams& p, cudaStream_t s);
 struct ConvParams {
   int B, T, C, K;
   int mode, L, V, bd;

@@ -120,3 +120,33 @@ def gdn_block_cuda(x, layer, actx, cfg):
         raise NotImplementedError("the GDN kernels are built for 128-dim key/value heads and conv width <= 4")
     return _GdnBlock.apply(x, layer.input_norm, layer.w_in, layer.conv_w, layer.dt_bias, layer.A_log, layer.gnorm,
                            layer.w_out, actx, cfg)
+
+
+def chunk_len(lay):
+    """Chunk length of the tcgen05 chunk kernels for a layout (None: not supported, use the scan)."""
+    if lay.mode == "two_stream":
+        return lay.bd if lay.bd in (16, 32, 64) and lay.L % lay.bd == 0 else None
+    return 64
+
+
+def chunk_forward(mixed, ga, gb, A_log, dt_bias, doc, B, T, Hk, Hv, lay, scale, final_state=None):
+    """Chunked gated-delta forward on the tcgen05 kernels (``csrc/gdn_chunk.cu``).  ``mixed`` is the
+    conv output [B*T, >= 2*Hk*128 + Hv*128] (q | k | v columns), ``ga`` / ``gb`` the gate
+    pre-activation views [B*T, Hv].  Returns (o [B*T, Hv*128] bf16, saved buffers)."""
+    from .blocks import device_error_word
+    C = chunk_len(lay)
+    two = lay.mode == "two_stream"
+    L, V = (lay.L, lay.V) if two else (0, 0)
+    Lc = L if two else T
+    nch = (Lc + C - 1) // C
+    dev = mixed.device
+    rows = B * T
+    bf, f32 = torch.bfloat16, torch.float32
+    bufs = [torch.empty(rows * Hk * 2 * 128, dtype=bf, device=dev), torch.empty(rows * Hv * 2, dtype=f32, device=dev)]
+    bufs += [torch.empty(rows * Hv * 128, dtype=bf, device=dev) for _ in range(4)]
+    bufs += [torch.empty(B * Hv * nch, dtype=f32, device=dev), torch.empty(B * Hv * nch * 128 * 128, dtype=bf, device=dev)]
+    o = torch.empty(rows, Hv * 128, dtype=bf, device=dev)
+    geo = [B, T, Hk, Hv, 1 if two else 0, L, V, C, int(lay.causal_clean), int(lay.causal_noisy)]
+    ext().gdn_chunk_fwd(mixed, ga, gb, A_log.float().contiguous(), dt_bias.float().contiguous(), doc, o, bufs,
+                        device_error_word(dev), geo, scale, final_state)
+    return o, dict(bufs=bufs, geo=geo, C=C, nch=nch)
