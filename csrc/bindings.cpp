@@ -837,14 +837,12 @@ void adamw(const at::Tensor& param, const c10::optional<at::Tensor>& master, con
 
 }  // namespace
 
-// Chunked gated-delta forward (gdn_chunk.cu).  bufs = [qk (bf16 [B*T, Hk, 2, 128]), gb (fp32
-// [B*T, Hv, 2]), wn, ut, kt, u (bf16 [B*T, Hv, 128] each), gamma (fp32 [B, Hv, nch]), ckpt (bf16
-// [B, Hv, nch, 128, 128])]; geo = [B, T, Hk, Hv, mode, L, V, C, causal_clean, causal_noisy].
-void gdn_chunk_fwd(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor& gb, const at::Tensor& A_log,
-                   const at::Tensor& dt_bias, const c10::optional<at::Tensor>& doc, const at::Tensor& o,
-                   std::vector<at::Tensor> bufs, const at::Tensor& err, std::vector<int64_t> geo, double scale,
-                   const c10::optional<at::Tensor>& final_state) {
-  TORCH_CHECK(geo.size() == 10 && bufs.size() == 8, "gdn_chunk_fwd: geo / bufs size");
+static trida::GdnChunkParams chunk_params(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor& gb,
+                                          const at::Tensor& A_log, const at::Tensor& dt_bias,
+                                          const c10::optional<at::Tensor>& doc, const at::Tensor& o,
+                                          std::vector<at::Tensor>& bufs, const at::Tensor& err,
+                                          const std::vector<int64_t>& geo, double scale) {
+  TORCH_CHECK(geo.size() == 10 && bufs.size() == 8, "gdn_chunk: geo / bufs size");
   const int64_t B = geo[0], T = geo[1], Hk = geo[2], Hv = geo[3], mode = geo[4], L = geo[5], V = geo[6], C = geo[7];
   auto q = gdn_params(mixed, ga, gb, A_log, dt_bias, doc, B, T, Hk, Hv, mode, L, V, C, geo[8] != 0, geo[9] != 0,
                       scale);
@@ -852,11 +850,12 @@ void gdn_chunk_fwd(const at::Tensor& mixed, const at::Tensor& ga, const at::Tens
   const int64_t Lc = mode ? L : T;
   TORCH_CHECK(!mode || L % C == 0, "two-stream: the stream length must be a multiple of the block");
   TORCH_CHECK(mixed.stride(0) % 8 == 0, "mixed row stride must be a multiple of 8 (TMA)");
+  TORCH_CHECK(Hv % Hk == 0, "value heads must be a multiple of key heads");
   const int64_t nch = (Lc + C - 1) / C;
   const int64_t rows = B * T;
   auto need = [&](const at::Tensor& t, at::ScalarType ty, int64_t n, const char* what) {
     CHECK_CUDA(t);
-    TORCH_CHECK(t.scalar_type() == ty && t.is_contiguous() && t.numel() >= n, "gdn_chunk_fwd: bad buffer ", what);
+    TORCH_CHECK(t.scalar_type() == ty && t.is_contiguous() && t.numel() >= n, "gdn_chunk: bad buffer ", what);
   };
   need(bufs[0], at::kBFloat16, rows * Hk * 2 * 128, "qk");
   need(bufs[1], at::kFloat, rows * Hv * 2, "gb");
@@ -874,14 +873,59 @@ void gdn_chunk_fwd(const at::Tensor& mixed, const at::Tensor& ga, const at::Tens
   p.wn = mbf(bufs[2]); p.ut = mbf(bufs[3]); p.kt = mbf(bufs[4]); p.u = mbf(bufs[5]);
   p.gamma = bufs[6].data_ptr<float>(); p.ckpt = mbf(bufs[7]); p.o = mbf(o);
   p.err = err.data_ptr<int>();
+  return p;
+}
+
+// Chunked gated-delta forward (gdn_chunk.cu).  bufs = [qk (bf16 [B*T, Hk, 2, 128]), gb (fp32
+// [B*T, Hv, 2]), wn, ut, kt, u (bf16 [B*T, Hv, 128] each), gamma (fp32 [B, Hv, nch]), ckpt (bf16
+// [B, Hv, nch, 128, 128])]; geo = [B, T, Hk, Hv, mode, L, V, C, causal_clean, causal_noisy].
+void gdn_chunk_fwd(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor& gb, const at::Tensor& A_log,
+                   const at::Tensor& dt_bias, const c10::optional<at::Tensor>& doc, const at::Tensor& o,
+                   std::vector<at::Tensor> bufs, const at::Tensor& err, std::vector<int64_t> geo, double scale,
+                   const c10::optional<at::Tensor>& final_state) {
+  auto p = chunk_params(mixed, ga, gb, A_log, dt_bias, doc, o, bufs, err, geo, scale);
   if (final_state.has_value() && final_state->defined()) {
     TORCH_CHECK(final_state->scalar_type() == at::kFloat && final_state->is_contiguous() &&
-                final_state->numel() == B * Hv * 128 * 128, "final_state must be fp32 [B, Hv, 128, 128]");
+                final_state->numel() == (int64_t)p.B * p.Hv * 128 * 128, "final_state must be fp32 [B, Hv, 128, 128]");
     p.final_state = final_state->data_ptr<float>();
   }
   c10::cuda::CUDAGuard g(mixed.device());
   const int rc = trida::gdn_chunk_fwd(p, stream());
   TORCH_CHECK(rc == 0, "gdn_chunk_fwd failed with code ", rc);
+}
+
+// Chunked gated-delta backward (gdn_chunk_bwd.cu) from the forward's saved buffers.  Writes the
+// q / k / v gradient columns of dmixed and the gate pre-activation gradients; accumulates dA_log /
+// ddt_bias (fp32).
+void gdn_chunk_bwd(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor& gb, const at::Tensor& A_log,
+                   const at::Tensor& dt_bias, const c10::optional<at::Tensor>& doc, const at::Tensor& o,
+                   std::vector<at::Tensor> bufs, const at::Tensor& err, std::vector<int64_t> geo, double scale,
+                   const at::Tensor& d_o, const at::Tensor& dmixed, const at::Tensor& dga, const at::Tensor& dgb,
+                   const at::Tensor& dA_log, const at::Tensor& ddt_bias) {
+  trida::GdnChunkBwdParams p{};
+  p.fwd = chunk_params(mixed, ga, gb, A_log, dt_bias, doc, o, bufs, err, geo, scale);
+  const int64_t rows = (int64_t)p.fwd.B * p.fwd.T, Hv = p.fwd.Hv;
+  CHECK_BF16(d_o); TORCH_CHECK(d_o.is_contiguous() && d_o.numel() == rows * Hv * 128, "d_o must be [B*T, Hv*128]");
+  CHECK_BF16(dmixed); CHECK_ROWMAJOR(dmixed); CHECK_BF16(dga); CHECK_BF16(dgb); CHECK_ROWMAJOR(dga);
+  TORCH_CHECK(dga.stride(0) == dgb.stride(0), "gate-gradient views must share a row stride");
+  TORCH_CHECK(dA_log.scalar_type() == at::kFloat && ddt_bias.scalar_type() == at::kFloat, "fp32 gate grads");
+  auto bf = mixed.options().dtype(at::kBFloat16);
+  auto f32 = mixed.options().dtype(at::kFloat);
+  const int64_t nstate = (int64_t)p.fwd.B * Hv * p.fwd.nch * 128 * 128;
+  std::vector<at::Tensor> rowbufs;
+  for (int i = 0; i < 7; ++i) rowbufs.push_back(at::empty({rows * Hv * 128}, bf));
+  at::Tensor ds0 = at::empty({nstate}, bf), dckpt = at::empty({nstate}, bf);
+  at::Tensor sc = at::empty({rows * Hv * 2}, f32), dpart = at::empty({rows * Hv * 260}, f32);
+  p.d_o = cbf(d_o);
+  p.du0 = mbf(rowbufs[0]); p.du = mbf(rowbufs[1]); p.qg = mbf(rowbufs[2]); p.dpe = mbf(rowbufs[3]);
+  p.dae = mbf(rowbufs[4]); p.dw = mbf(rowbufs[5]); p.tt = mbf(rowbufs[6]);
+  p.ds0 = mbf(ds0); p.dckpt = mbf(dckpt); p.sc = sc.data_ptr<float>(); p.dpart = dpart.data_ptr<float>();
+  p.dmixed = mbf(dmixed); p.lddm = dmixed.stride(0);
+  p.dga = mbf(dga); p.dgb = mbf(dgb); p.lddg = dga.stride(0);
+  p.dA_log = dA_log.data_ptr<float>(); p.ddt_bias = ddt_bias.data_ptr<float>();
+  c10::cuda::CUDAGuard g(mixed.device());
+  const int rc = trida::gdn_chunk_bwd(p, stream());
+  TORCH_CHECK(rc == 0, "gdn_chunk_bwd failed with code ", rc);
 }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -930,6 +974,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_adamw_ag", &symm_adamw_ag);
   m.def("gdn_state_numel", &gdn_state_numel);
   m.def("gdn_chunk_fwd", &gdn_chunk_fwd);
+  m.def("gdn_chunk_bwd", &gdn_chunk_bwd);
   m.def("gdn_fwd", &gdn_fwd, py::arg("mixed"), py::arg("ga"), py::arg("gb"), py::arg("A_log"), py::arg("dt_bias"),
         py::arg("doc"), py::arg("o"), py::arg("ckpt"), py::arg("B"), py::arg("T"), py::arg("Hk"), py::arg("Hv"),
         py::arg("mode"), py::arg("L"), py::arg("V"), py::arg("bd"), py::arg("causal_clean"), py::arg("causal_noisy"),

@@ -29,251 +29,12 @@
 //   local (NOISY): per noisy tile of the two-stream layout: everything above from the stored clean
 //                 state at the block start (no scan: noisy blocks are independent).
 // Every mbarrier wait is bounded (error word, never a hang); no TMA load uses cluster multicast.
-#include "common.cuh"
-#include "ops.h"
-#include "sm100_common.cuh"
-
-#include <cudaTypedefs.h>
+#include "gdn_chunk.cuh"
 
 namespace trida {
 namespace gdnc {
 
 using namespace trida::sm100;
-
-constexpr int D = 128;            // key / value head dim
-constexpr int TR = 128;           // rows per tile
-constexpr int NT = 128;           // threads (one per tile row / TMEM lane)
-constexpr int TILE = 32768;       // bytes of a 128 x 128 bf16 tile
-constexpr int SUB = 16384;        // one [128][64] swizzled half
-constexpr int AF_LD = 65;         // fp32 row stride of the A blocks (conflict-free rows and columns)
-
-enum Mode { PREP = 0, NOISY = 1, OUT = 2 };
-
-// ---- tile algebra --------------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t toff(int r, int c) {
-  return (uint32_t)(c >> 6) * SUB + sw128_offset(r, c & 63);
-}
-
-// K-major view: MN index = tile row (from row0), K index = tile column (from k0).  `half` is the
-// byte distance between the two 64-column halves (SUB for a 128-row tile, rows * 128 otherwise).
-__device__ __forceinline__ uint64_t kdesc(uint32_t base, int row0, int k0, uint32_t half) {
-  return desc_sw128(base + (uint32_t)(k0 >> 6) * half + (uint32_t)row0 * 128u + (uint32_t)(k0 & 63) * 2u, 16, 1024);
-}
-// MN-major view: MN index = tile column, K index = tile row (from k0).
-__device__ __forceinline__ uint64_t mdesc(uint32_t base, int k0, uint32_t half) {
-  return desc_sw128(base + (uint32_t)k0 * 128u, half, 1024);
-}
-
-// D[128 x N] (+)= op(A) op(B) over K (multiple of 16).  a_mn / b_mn select the views above;
-// a_row0 / b_row0 offset the MN rows of a K-major operand, a_k0 / b_k0 the K range.
-struct Opnd {
-  uint32_t base;
-  int mn;      // 0: K-major view, 1: MN-major view
-  int row0;    // K-major only: first MN row
-  int k0;      // first K index
-  uint32_t half;
-};
-
-__device__ __forceinline__ void mma(uint32_t d, Opnd a, Opnd b, int N, int K, bool acc) {
-  const uint32_t id = idesc_bf16_f32(128, N, a.mn, b.mn);
-  for (int kk = 0; kk < K / 16; ++kk) {
-    const int ka = a.k0 + kk * 16, kb = b.k0 + kk * 16;
-    const uint64_t ad = a.mn ? mdesc(a.base, ka, a.half) : kdesc(a.base, a.row0, ka, a.half);
-    const uint64_t bd = b.mn ? mdesc(b.base, kb, b.half) : kdesc(b.base, b.row0, kb, b.half);
-    umma_f16(d, ad, bd, id, (acc || kk > 0) ? 1u : 0u);
-  }
-}
-
-__device__ __forceinline__ Opnd KM(uint32_t base, int row0 = 0, int k0 = 0, uint32_t half = SUB) {
-  return Opnd{base, 0, row0, k0, half};
-}
-__device__ __forceinline__ Opnd MN(uint32_t base, int k0 = 0, uint32_t half = SUB) { return Opnd{base, 1, 0, k0, half}; }
-
-// One row (128 fp32 TMEM columns from `col`) of an accumulator into registers.
-__device__ __forceinline__ void ld_row128(uint32_t tmem, int col, float (&x)[128]) {
-  const int w = threadIdx.x >> 5;
-  const uint32_t a = tmem + ((uint32_t)(32 * w) << 16) + col;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    uint32_t r[32];
-    tmem_ld32(a + 32 * j, r);
-    tmem_wait_ld();
-#pragma unroll
-    for (int i = 0; i < 32; ++i) x[32 * j + i] = __uint_as_float(r[i]);
-  }
-}
-
-__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
-  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
-
-// Row r of a tile from 128 fp32 values (first n columns; the rest written as zero).
-__device__ __forceinline__ void st_row(uint8_t* tile, int r, const float (&x)[128]) {
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    uint4 v;
-    v.x = pack_bf2(x[8 * j + 0], x[8 * j + 1]);
-    v.y = pack_bf2(x[8 * j + 2], x[8 * j + 3]);
-    v.z = pack_bf2(x[8 * j + 4], x[8 * j + 5]);
-    v.w = pack_bf2(x[8 * j + 6], x[8 * j + 7]);
-    *reinterpret_cast<uint4*>(tile + toff(r, 8 * j)) = v;
-  }
-}
-
-__device__ __forceinline__ void ld_row_bf(const uint8_t* tile, int r, float (&x)[128]) {
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const uint4 v = *reinterpret_cast<const uint4*>(tile + toff(r, 8 * j));
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
-      const float2 f = __bfloat1622float2(h);
-      x[8 * j + 2 * i] = f.x;
-      x[8 * j + 2 * i + 1] = f.y;
-    }
-  }
-}
-
-__device__ __forceinline__ void st_col(uint8_t* tile, int c, const float (&x)[128]) {
-#pragma unroll
-  for (int r = 0; r < 128; ++r) *reinterpret_cast<bf16*>(tile + toff(r, c)) = __float2bfloat16(x[r]);
-}
-
-__device__ __forceinline__ float ld_el(const uint8_t* tile, int r, int c) {
-  return __bfloat162float(*reinterpret_cast<const bf16*>(tile + toff(r, c)));
-}
-
-// ---- arguments ------------------------------------------------------------------------------------
-struct Args {
-  int B, T, Hk, Hv;
-  int mode;                 // layout: 0 causal, 1 two-stream
-  int L, V;                 // two-stream geometry (stream length, noisy views)
-  int nch;                  // clean chunks per row
-  int tok_clean, tok_noisy; // token-causal read-out of the clean / noisy streams
-  const uint8_t* doc;       // [B, Lc] document starts of the clean stream (or null)
-  const float* gb;          // [B*T, Hv, 2]: log-decay g, beta
-  bf16* o;                  // [B*T, Hv*D]
-  bf16* ckpt;               // [B, Hv, nch, D, D] clean chunk-start states (k rows, v columns)
-  float* gamma;             // [B, Hv, nch] chunk decay carry_last * e^{G_last}
-  float* final_state;       // optional [B, Hv, D, D] fp32 state after the last clean token
-  bf16* wn;                 // [B*T, Hv, D] -W rows (clean stream)
-  bf16* ut;                 // [B*T, Hv, D] U~ rows
-  bf16* kt;                 // [B*T, Hv, D] K~ rows
-  bf16* u;                  // [B*T, Hv, D] U rows (written by the scan)
-  int* err;
-};
-
-__device__ __forceinline__ int clean_len(const Args& a) { return a.mode ? a.L : a.T; }
-
-// Per-tile stream geometry.
-struct TileGeo {
-  int b, hv, hk;
-  int stream;               // 0 clean / causal, 1.. noisy view
-  int p0;                   // first stream position of the tile
-  int Ls;                   // stream length
-  int t0;                   // first row of the tile inside batch row b
-  bool tok;                 // token-causal read-out
-};
-
-__device__ __forceinline__ void store_row_bf(bf16* dst, const float (&x)[128], float scale) {
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    uint4 v;
-    v.x = pack_bf2(x[8 * j] * scale, x[8 * j + 1] * scale);
-    v.y = pack_bf2(x[8 * j + 2] * scale, x[8 * j + 3] * scale);
-    v.z = pack_bf2(x[8 * j + 4] * scale, x[8 * j + 5] * scale);
-    v.w = pack_bf2(x[8 * j + 6] * scale, x[8 * j + 7] * scale);
-    reinterpret_cast<uint4*>(dst)[j] = v;
-  }
-}
-
-// ---- per-row metadata ------------------------------------------------------------------------------
-struct Meta {
-  float* g; float* beta; float* G; float* Gr; float* carry; float* kts; int* seg; int* rd; int* rs; float* gam;
-  static constexpr int BYTES = 10 * 128 * 4;
-};
-
-__device__ __forceinline__ Meta carve_meta(uint8_t* p) {
-  Meta m;
-  float* f = reinterpret_cast<float*>(p);
-  m.g = f; m.beta = f + 128; m.G = f + 256; m.Gr = f + 384; m.carry = f + 512; m.kts = f + 640;
-  m.seg = reinterpret_cast<int*>(f + 768); m.rd = reinterpret_cast<int*>(f + 896);
-  m.rs = reinterpret_cast<int*>(f + 1024); m.gam = f + 1152;
-  return m;
-}
-
-// Thread r fills the metadata of tile row r: decay / beta (0 past the stream end), segment starts
-// from document starts, the segmented cumulative log-decay G, read-out row rd, Gr = G[rd], carry,
-// the K~ row scale and (thread of each chunk's first row) the chunk decay.
-template <int C>
-__device__ void tile_meta(const Args& a, const TileGeo& t, const Meta& m) {
-  const int r = threadIdx.x;
-  const int p = t.p0 + r;
-  float g = 0.f, be = 0.f;
-  int rs = 0;
-  if (p < t.Ls) {
-    const int64_t row = (int64_t)t.b * a.T + t.t0 + r;
-    const float2 v = *reinterpret_cast<const float2*>(a.gb + (row * a.Hv + t.hv) * 2);
-    g = v.x;
-    be = v.y;
-    if (a.doc != nullptr) {
-      const bool start = a.doc[(int64_t)t.b * clean_len(a) + p] != 0;   // noisy views share positions
-      rs = (t.stream == 0 || (r % C) == 0) ? (int)start : 0;
-    }
-  }
-  m.g[r] = g;
-  m.beta[r] = be;
-  m.rs[r] = rs;
-  __syncthreads();
-  const int cs = (r / C) * C;
-  int seg = 0, sst = cs;
-  for (int j = cs + 1; j <= r; ++j)
-    if (m.rs[j]) { ++seg; sst = j; }
-  float G = 0.f;
-  for (int j = sst; j <= r; ++j) G += m.g[j];
-  int rd = r;
-  if (!t.tok) {
-    rd = cs + C - 1;
-    for (int j = r + 1; j < cs + C; ++j)
-      if (m.rs[j]) { rd = j - 1; break; }
-  }
-  m.G[r] = G;
-  m.seg[r] = seg;
-  m.rd[r] = rd;
-  m.carry[r] = (seg == 0 && !m.rs[cs]) ? 1.f : 0.f;
-  __syncthreads();
-  const int last = cs + C - 1;
-  m.Gr[r] = m.G[rd];
-  m.kts[r] = (m.seg[r] == m.seg[last]) ? __expf(m.G[last] - G) : 0.f;
-  if (r == cs) m.gam[r / C] = m.carry[last] * __expf(m.G[last]);
-  __syncthreads();
-}
-
-// Column j of T = (I + A)^-1 for the chunk holding tile column j (forward substitution over the
-// fp32 A blocks [128][AF_LD], chunk-local columns), written into the T tile as bf16 (zero outside
-// the chunk's diagonal block).
-template <int C>
-__device__ __forceinline__ void invert_column(const float* Af, uint8_t* Tt) {
-  const int j = threadIdx.x, cs = (j / C) * C, jl = j - cs;
-  float x[C];
-#pragma unroll
-  for (int t = 0; t < C; ++t) x[t] = (t == jl) ? 1.f : 0.f;
-#pragma unroll
-  for (int t = 1; t < C; ++t) {
-    const float* arow = Af + (cs + t) * AF_LD;
-    float s = 0.f;
-#pragma unroll
-    for (int u = 0; u < t; ++u) s = fmaf(arow[u], x[u], s);
-    if (t > jl) x[t] = -s;
-  }
-#pragma unroll
-  for (int t = 0; t < C; ++t) *reinterpret_cast<bf16*>(Tt + toff(cs + t, j)) = __float2bfloat16(x[t]);
-  const bf16 z = __float2bfloat16(0.f);
-  for (int r = 0; r < 128; ++r)
-    if (r < cs || r >= cs + C) *reinterpret_cast<bf16*>(Tt + toff(r, j)) = z;
-}
 
 // ---- local kernel ----------------------------------------------------------------------------------
 struct LocalSmem {
@@ -433,11 +194,12 @@ __global__ void __launch_bounds__(NT, 1) local_kernel(const __grid_constant__ CU
       if (valid) store_row_bf(a.ut + (row * a.Hv + t.hv) * D, x, 1.f);
       if (r % C == 0 && valid) a.gamma[((int64_t)t.b * a.Hv + t.hv) * a.nch + (t.p0 + r) / C] = m.gam[r / C];
     } else {
-      // -W into R4 (the A blocks are dead after the inversion)
+      // -W into R4 (the A blocks are dead after the inversion) and, for the backward, its rows
       ld_row128(acc1, 0, x);
 #pragma unroll
       for (int i = 0; i < 128; ++i) x[i] = -x[i];
       st_row(sm + S::R4, r, x);
+      if (valid) store_row_bf(a.wn + (((int64_t)t.b * a.T + t.t0 + r) * a.Hv + t.hv) * D, x, 1.f);
     }
   }
 
@@ -509,6 +271,12 @@ __global__ void __launch_bounds__(NT, 1) local_kernel(const __grid_constant__ CU
     if (MODE == NOISY) {
       ld_row128(acc2, 0, x);
       st_row(sm + S::R3, r, x);
+      // U rows for the backward: thread r holds value column r of every tile row
+      bf16* ub = a.u + ((int64_t)t.b * a.T + t.t0) * a.Hv * D + t.hv * D + r;
+      const int nv = min(TR, t.Ls - t.p0);
+#pragma unroll
+      for (int tt = 0; tt < TR; ++tt)
+        if (tt < nv) ub[(int64_t)tt * a.Hv * D] = __float2bfloat16(x[tt]);
     }
     tmem_wait_ld();
     fence_async_smem();
@@ -741,48 +509,6 @@ __global__ void chunk_prep_kernel(const bf16* mixed, int64_t ldm, const bf16* ga
       gb[(row * Hv + h) * 2 + 1] = 1.f / (1.f + expf(-bv));
     }
   }
-}
-
-// ---- host -----------------------------------------------------------------------------------------
-static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    cudaDriverEntryPointQueryResult q;
-    void* ptr = nullptr;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  }
-  return fn;
-}
-
-static bool encode(CUtensorMap* m, const void* base, const cuuint64_t (&dims)[4], const cuuint64_t (&strides)[3],
-                   int box1, int box2) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  cuuint32_t box[4] = {64, (cuuint32_t)box1, (cuuint32_t)box2, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
-  cuuint64_t st[3] = {strides[0], strides[1], strides[2]};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), d, st, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// bf16 [B][T][H][D]: coordinates (d, h, t, b); box 64 x 1 head x box_rows tokens.  Tokens past T
-// read as zero.
-static bool map_heads(CUtensorMap* m, const void* base, int B, int T, int H, int box_rows) {
-  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
-  const cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)H * D * 2, (cuuint64_t)T * H * D * 2};
-  return encode(m, base, dims, strides, 1, box_rows);
-}
-
-// bf16 [B][T][ld] (first `cols` columns): coordinates (col, t, b, 0); box 64 x box_rows tokens.
-static bool map_cols(CUtensorMap* m, const void* base, int B, int T, int64_t cols, int64_t ld, int box_rows) {
-  const cuuint64_t dims[4] = {(cuuint64_t)cols, (cuuint64_t)T, (cuuint64_t)B, 1};
-  const cuuint64_t strides[3] = {(cuuint64_t)ld * 2, (cuuint64_t)T * ld * 2, (cuuint64_t)B * T * ld * 2};
-  return encode(m, base, dims, strides, box_rows, 1);
 }
 
 template <int C>

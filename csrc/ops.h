@@ -120,6 +120,18 @@ struct GdnChunkParams {
   int* err;
 };
 int gdn_chunk_fwd(const GdnChunkParams& p, cudaStream_t s);
+struct GdnChunkBwdParams {
+  GdnChunkParams fwd;        // the forward's geometry and saved buffers (o = forward output)
+  const bf16* d_o;
+  bf16* du0; bf16* du; bf16* qg; bf16* dpe; bf16* dae; bf16* dw; bf16* tt;   // [B*T, Hv, 128] scratch
+  bf16* ds0; bf16* dckpt;    // [B, Hv, nch, 128, 128] scratch
+  float* sc;                 // [B*T, Hv, 2]
+  float* dpart;              // [B*T, Hv, 260]
+  bf16* dmixed; int64_t lddm;
+  bf16* dga; bf16* dgb; int64_t lddg;
+  float* dA_log; float* ddt_bias;   // accumulated (zero them first)
+};
+int gdn_chunk_bwd(const GdnChunkBwdParams& p, cudaStream_t s);
 struct ConvParams {
   int B, T, C, K;
   int mode, L, V, bd;

@@ -192,3 +192,85 @@ def test_compat_names_and_decision_export(tmp_path):
     from safetensors import safe_open
     with safe_open(f"{out}/model.safetensors", "pt") as s:
         assert all(k.startswith("model.") for k in s.keys())
+
+
+def test_decision_export_round_trip(tmp_path):
+    """A tiny hybrid decoder saved with the trainer's own writer (several shards), plus a pointer head,
+    exported and read back: the text weights and the head survive unchanged, the config is flat, and
+    a head whose width does not match the backbone is refused before anything is written."""
+    import json
+
+    import pytest
+    import torch
+
+    from test_hybrid_cpu import tiny_qwen35
+    from trida_stack_b200 import checkpoint
+    from trida_stack_b200.export import ExportError, export
+    src = tmp_path / "src"
+    tiny_qwen35(str(src))
+    sd = checkpoint.read_hf_weights(str(src))
+    for f in src.glob("*.safetensors"):
+        f.unlink()
+    checkpoint.write_hf_weights(sd, str(src), max_shard_bytes=200_000)          # force several shards
+    assert (src / "model.safetensors.index.json").exists()
+    hidden = json.load(open(src / "config.json"))["hidden_size"]
+    g = torch.Generator().manual_seed(0)
+    head = {"q.weight": torch.randn(8, hidden, generator=g), "q.bias": torch.randn(8, generator=g),
+            "k.weight": torch.randn(8, hidden, generator=g), "k.bias": torch.randn(8, generator=g)}
+    torch.save({"head": head, "head_dim": 8}, src / "decision_head.pt")
+    out = export(str(src), str(tmp_path / "kev"), temperature=0.7, max_shard_bytes=150_000)
+    back = checkpoint.read_hf_weights(out)
+    text = {("model." + k[len("model."):]): v for k, v in sd.items() if k.startswith("model.")}
+    assert back.keys() == text.keys()
+    for k in text:
+        assert torch.equal(back[k], text[k]), k
+    meta = torch.load(f"{out}/head.pt")
+    assert set(meta) == {"base", "head", "head_dim", "weights", "weights_dtype", "temperature", "lora",
+                         "option_isolation", "special_embeddings", "holdout", "exported_from"}
+    assert meta["head_dim"] == 8 and meta["temperature"] == 0.7 and meta["weights"] == "full"
+    for k, v in head.items():
+        torch.testing.assert_close(meta["head"][k], v)
+    cfg = json.load(open(f"{out}/config.json"))
+    assert cfg["model_type"] == "qwen3_5_text" and cfg["architectures"] == ["Qwen3_5ForCausalLM"]
+    bad = tmp_path / "bad"
+    tiny_qwen35(str(bad))
+    torch.save({"head": {**head, "k.weight": torch.zeros(8, hidden + 1)}, "head_dim": 8}, bad / "jev_head.pt")
+    with pytest.raises(ExportError, match="k.weight"):
+        export(str(bad), str(tmp_path / "kev_bad"))
+    assert not (tmp_path / "kev_bad").exists()
+
+
+def test_decision_text_format_is_stable():
+    """The row text of requests (render / materialize / augmentation draws) equals the recorded
+    golden output: it is the format released checkpoints were trained on."""
+    import json
+    import os
+    import random
+
+    from trida_stack_b200.data import decision as D
+    gold = json.load(open(os.path.join(os.path.dirname(__file__), "fixtures", "decision_golden.json")))
+    v = {"name": "x", "items": [1, {"a": 2, "b": [3, "four", None]}, [5, 6]], "flag": True, "none": None,
+         "nested": {"deep": {"deeper": ["z", {"k": 1.5}]}}, "empty": {}, "elist": []}
+    req = {"state": {"user": "alice", "history": ["a", "b"], "meta": {"age": 30}},
+           "questions": {"q1": {"type": "choice", "instructions": {"task": "pick", "notes": ["n1"]},
+                                "criteria": {"red": "warm colour", "blue": {"why": "cold"}, "green": None},
+                                "label": "blue"},
+                         "q2": {"type": "noul", "instructions": "yes or no?",
+                                "criteria": {"true": "it is", "false": None}, "label": 1},
+                         "q3": {"type": "score", "instructions": None, "criteria": ["low", {"mid": 2}, 3], "label": 2},
+                         "q4": {"type": "choice", "instructions": "soft", "criteria": {"a": 1, "b": 2},
+                                "label": "a", "target": {"a": 3, "b": 1}}}}
+    assert D.render(v) == gold["render"]
+    assert D.render([1, [2, 3], {"x": [4]}]) == gold["render_list"]
+    assert json.loads(json.dumps(D.materialize(req))) == gold["materialize"]
+    rng = random.Random(5)
+    assert json.loads(json.dumps([D.materialize(x) for x in D.record_variants(req, rng, 1.0)])) == gold["variants"]
+
+
+def test_epoch_sampler_shards_cover_each_epoch():
+    from trida_stack_b200.data.sharding import EpochSampler
+    n, nshard = 10, 4
+    per = [EpochSampler(n, s, nshard, seed=3).epoch(0) for s in range(nshard)]
+    assert all(len(p) == 3 for p in per)                     # ceil(10 / 4), equal for every shard
+    assert set(i for p in per for i in p) == set(range(n))   # every record visited
+    assert EpochSampler(n, 0, nshard, 3).epoch(1) != per[0]  # a fresh order each epoch

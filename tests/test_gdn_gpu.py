@@ -70,8 +70,15 @@ def _run(cfg, lay_cpu, layout, B, T, seed=1):
         assert _rel(q.grad.cpu(), p.grad) < 4e-2, (n, _rel(q.grad.cpu(), p.grad))
 
 
+@pytest.fixture(params=["chunk", "scan"])
+def path(request, monkeypatch):
+    """Both gated-delta implementations: the chunked tcgen05 kernels and the per-token scan."""
+    monkeypatch.setenv("TRIDA_GDN", request.param)
+    return request.param
+
+
 @pytest.mark.parametrize("docs", [False, True])
-def test_gdn_causal_matches_reference(docs):
+def test_gdn_causal_matches_reference(docs, path):
     cfg = _cfg()
     lay = _layer(cfg)
     B, T = 2, 100
@@ -86,7 +93,7 @@ def test_gdn_causal_matches_reference(docs):
 
 @pytest.mark.parametrize("causal_clean,causal_noisy,docs", [(True, False, False), (False, False, False),
                                                             (True, True, False), (True, False, True)])
-def test_gdn_two_stream_matches_reference(causal_clean, causal_noisy, docs):
+def test_gdn_two_stream_matches_reference(causal_clean, causal_noisy, docs, path):
     cfg = _cfg()
     lay = _layer(cfg)
     B, L, V, bd = 2, 64, 2, 16
@@ -99,3 +106,31 @@ def test_gdn_two_stream_matches_reference(causal_clean, causal_noisy, docs):
     layout = LinearLayout("two_stream", L=L, V=V, bd=bd, causal_clean=causal_clean, causal_noisy=causal_noisy,
                           doc_start=doc)
     _run(cfg, lay, layout, B, (1 + V) * L)
+
+
+@pytest.mark.parametrize("T,docs", [(300, False), (300, True)])
+def test_gdn_chunk_causal_multi_tile(T, docs):
+    """Rows over several 128-row tiles (and a partial last chunk) on the chunk kernels."""
+    cfg = _cfg()
+    lay = _layer(cfg, seed=2)
+    B = 2
+    doc = None
+    if docs:
+        doc = torch.zeros(B, T, dtype=torch.bool)
+        doc[:, 0] = True
+        doc[0, 150] = doc[1, 64] = doc[1, 201] = True
+    _run(cfg, lay, LinearLayout("causal", doc_start=doc), B, T, seed=3)
+
+
+@pytest.mark.parametrize("bd,L,causal_noisy", [(32, 128, False), (32, 256, True), (64, 192, False)])
+def test_gdn_chunk_two_stream_blocks(bd, L, causal_noisy):
+    """Two-stream rows with diffusion blocks of 32 and 64 tokens on the chunk kernels."""
+    cfg = _cfg()
+    lay = _layer(cfg, seed=4)
+    B, V = 1, 2
+    doc = torch.zeros(B, L, dtype=torch.bool)
+    doc[:, 0] = True
+    doc[0, L // 2] = True
+    layout = LinearLayout("two_stream", L=L, V=V, bd=bd, causal_clean=True, causal_noisy=causal_noisy,
+                          doc_start=doc)
+    _run(cfg, lay, layout, B, (1 + V) * L, seed=5)

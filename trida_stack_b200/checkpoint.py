@@ -28,33 +28,56 @@ def _barrier():
         dist.barrier()
 
 
+class ShardWriter:
+    """Streams (name, tensor) pairs into safetensors shards of at most ``max_shard_bytes`` (HF
+    layout): one ``model.safetensors``, or numbered shards plus ``model.safetensors.index.json``.
+    Only the shard being filled is held in host memory; full shards are written under temporary
+    names and renamed once the shard count is known."""
+
+    def __init__(self, out_dir, max_shard_bytes=SHARD_BYTES):
+        self.out, self.max = out_dir, max_shard_bytes
+        os.makedirs(out_dir, exist_ok=True)
+        self.cur, self.size, self.done, self.count, self.total = {}, 0, [], 0, 0
+
+    def add(self, name, tensor):
+        t = tensor.detach().to("cpu").contiguous()
+        nbytes = t.numel() * t.element_size()
+        if self.cur and self.size + nbytes > self.max:
+            self._flush()
+        self.cur[name] = t
+        self.size += nbytes
+        self.count += 1
+        self.total += nbytes
+
+    def _flush(self):
+        from safetensors.torch import save_file
+        tmp = os.path.join(self.out, f".shard-{len(self.done):05d}.tmp")
+        save_file(self.cur, tmp, metadata={"format": "pt"})
+        self.done.append((tmp, list(self.cur)))
+        self.cur, self.size = {}, 0
+
+    def close(self):
+        if self.cur or not self.done:
+            self._flush()
+        n = len(self.done)
+        if n == 1:
+            os.replace(self.done[0][0], os.path.join(self.out, "model.safetensors"))
+            return
+        weight_map = {}
+        for i, (tmp, names) in enumerate(self.done):
+            fname = f"model-{i + 1:05d}-of-{n:05d}.safetensors"
+            os.replace(tmp, os.path.join(self.out, fname))
+            weight_map.update(dict.fromkeys(names, fname))
+        with open(os.path.join(self.out, "model.safetensors.index.json"), "w") as f:
+            json.dump({"metadata": {"total_size": self.total}, "weight_map": weight_map}, f, indent=2)
+
+
 def write_hf_weights(state, out_dir, max_shard_bytes=SHARD_BYTES):
     """Save ``state`` (name -> tensor) as safetensors shards + index (HF layout)."""
-    from safetensors.torch import save_file
-    os.makedirs(out_dir, exist_ok=True)
-    shards, cur, size = [], {}, 0
+    w = ShardWriter(out_dir, max_shard_bytes)
     for name in state:
-        t = state[name].detach().to("cpu").contiguous()
-        nbytes = t.numel() * t.element_size()
-        if cur and size + nbytes > max_shard_bytes:
-            shards.append(cur)
-            cur, size = {}, 0
-        cur[name] = t
-        size += nbytes
-    if cur:
-        shards.append(cur)
-    if len(shards) == 1:
-        save_file(shards[0], os.path.join(out_dir, "model.safetensors"), metadata={"format": "pt"})
-        return
-    index = {"metadata": {"total_size": sum(t.numel() * t.element_size() for s in shards for t in s.values())},
-             "weight_map": {}}
-    for i, sh in enumerate(shards):
-        fname = f"model-{i + 1:05d}-of-{len(shards):05d}.safetensors"
-        save_file(sh, os.path.join(out_dir, fname), metadata={"format": "pt"})
-        for k in sh:
-            index["weight_map"][k] = fname
-    with open(os.path.join(out_dir, "model.safetensors.index.json"), "w") as f:
-        json.dump(index, f, indent=2)
+        w.add(name, state[name])
+    w.close()
 
 
 def read_hf_weights(path):

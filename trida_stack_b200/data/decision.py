@@ -8,14 +8,15 @@ delimiter tokens, the none-of-the-above / distractor tables and the order of ran
 augmentation are part of the contract and are kept exactly; the code around them is this
 package's own.  Batches pack whole request variants into one causal row of documents.
 """
-import hashlib
 import json
 import os
 import random
 import re
 
 import torch
-from torch.utils.data import IterableDataset, get_worker_info
+from torch.utils.data import IterableDataset
+
+from .sharding import EpochSampler, mix_seed, worker_shard
 
 # delimiters: state, question, option open, option close, decide
 SPECIAL = ["<|fim_prefix|>", "<|fim_middle|>", "<|box_start|>", "<|box_end|>", "<|fim_suffix|>"]
@@ -36,56 +37,89 @@ class ContextOverflow(ValueError):
     pass
 
 
+class _Text:
+    """Text form of a JSON value inside a decision row: scalars as ``str()``, ``None`` as nothing,
+    mappings as ``key: value`` lines (nested values on the following lines, two more spaces of
+    indent), sequences as ``- item`` lines.  The exact text is part of the row format a released
+    checkpoint was trained on, so it must not change."""
+
+    @classmethod
+    def of(cls, value, depth=0):
+        if value is None:
+            return ""
+        if isinstance(value, (str, int, float, bool)):
+            return str(value)
+        lines = cls._seq(value, depth) if isinstance(value, list) else cls._map(value, depth)
+        return "\n".join(lines)
+
+    @classmethod
+    def _seq(cls, items, depth):
+        lead = "  " * depth + "- "
+        return [lead + cls.of(x, depth + 1).lstrip() for x in items]
+
+    @classmethod
+    def _map(cls, mapping, depth):
+        pad = "  " * depth
+        out = []
+        for key, x in mapping.items():
+            nested = isinstance(x, (dict, list))
+            out.append(f"{pad}{key}:\n{cls.of(x, depth + 1)}" if nested else f"{pad}{key}: {cls.of(x)}")
+        return out
+
+
 def render(v, indent=0):
-    """Text form of a str / number / list / dict value (field names kept as labels)."""
-    pad = "  " * indent
-    if v is None:
-        return ""
-    if isinstance(v, (str, int, float, bool)):
-        return str(v)
-    if isinstance(v, list):
-        return "\n".join(f"{pad}- {render(x, indent + 1).lstrip()}" for x in v)
-    lines = []
-    for k, x in v.items():
-        lines.append(f"{pad}{k}:\n{render(x, indent + 1)}" if isinstance(x, (dict, list)) else f"{pad}{k}: {render(x)}")
-    return "\n".join(lines)
+    """Text of a value for a decision row (see ``_Text``)."""
+    return _Text.of(v, indent)
 
 
 def option_text(name, desc):
-    return name if desc is None or desc == "" else f"{name}: {render(desc)}"
+    """An option line: the key alone when it has no description, else ``key: description``."""
+    has_desc = not (desc is None or desc == "")
+    return f"{name}: {render(desc)}" if has_desc else name
 
 
 def question_keys(qtype, criteria):
-    if qtype == "choice":
-        return list(criteria)
-    if qtype == "noul":
-        return ["false", "true"]
-    return [str(i) for i in range(len(criteria))]
+    """Option keys of a question, in row order (a yes/no question is ``false`` then ``true``)."""
+    return {"choice": lambda: list(criteria), "noul": lambda: ["false", "true"]}.get(
+        qtype, lambda: [str(i) for i in range(len(criteria))])()
+
+
+def _options(q):
+    """Option texts of a question, aligned with ``question_keys``."""
+    kind, crit = q["type"], q.get("criteria")
+    if kind == "noul":
+        crit = crit or {}
+        return [option_text(word, crit.get(key)) for word, key in (("no", "false"), ("yes", "true"))]
+    if kind == "choice":
+        return [option_text(k, d) for k, d in crit.items()]
+    return [render(x) for x in crit]
+
+
+def _soft_target(q, keys):
+    """Normalised soft-label distribution over ``keys`` (None when the question has no target)."""
+    tgt = q.get("target")
+    if tgt is None:
+        return None
+    mass = [float(tgt.get(k, 0.0)) for k in keys]
+    total = sum(mass)
+    if not total > 0:
+        raise ValueError(f"question {q.get('_id', '?')}: the soft target gives no option any weight")
+    return [m / total for m in mass]
 
 
 def materialize(req):
     """Labelled request -> {"state": text, "questions": [{instr, options, qid, qtype, keys, label, target?}]}."""
-    out = []
+    questions = []
     for qid, q in req["questions"].items():
         keys = question_keys(q["type"], q.get("criteria"))
-        if q["type"] == "noul":
-            crit = q.get("criteria") or {}
-            options = [option_text("no", crit.get("false")), option_text("yes", crit.get("true"))]
-        elif q["type"] == "choice":
-            options = [option_text(k, v) for k, v in q["criteria"].items()]
-        else:
-            options = [render(x) for x in q["criteria"]]
         label = keys.index(q["label"]) if q["type"] == "choice" else int(q["label"])
-        item = {"instr": render(q.get("instructions")), "options": options, "qid": qid, "qtype": q["type"],
+        item = {"instr": render(q.get("instructions")), "options": _options(q), "qid": qid, "qtype": q["type"],
                 "keys": keys, "label": label}
-        if q.get("target") is not None:
-            t = [float(q["target"].get(k, 0.0)) for k in keys]
-            tot = sum(t)
-            if tot <= 0:
-                raise ValueError(f"target for {qid} puts no mass on any option")
-            item["target"] = [x / tot for x in t]
-        out.append(item)
-    return {"state": render(req["state"]), "questions": out}
+        target = _soft_target({**q, "_id": qid}, keys)
+        if target is not None:
+            item["target"] = target
+        questions.append(item)
+    return {"state": render(req["state"]), "questions": questions}
 
 
 def augment(req, rng, p_none=0.1, p_none_distract=0.12, p_distract=0.15):
@@ -194,10 +228,6 @@ def load_decision_records(paths):
     return recs
 
 
-def _seed(*parts):
-    return int.from_bytes(hashlib.sha256(":".join(map(str, parts)).encode()).digest()[:8], "little")
-
-
 def pack_decision(variants, tok):
     """Variants (lists of rows) -> one packed causal row [1, T] (each question row a document)
     with flat <decide> / </opt> indices and the per-question loss bookkeeping."""
@@ -222,59 +252,70 @@ def pack_decision(variants, tok):
             "opts": torch.tensor(opts), "owner": torch.tensor(owner), "questions": questions}
 
 
+def _encode_variant(tok, variant, ctx, max_tokens):
+    """Row list of one augmented variant, or None when it does not fit the context budgets."""
+    try:
+        rows = encode_rows(tok, materialize(variant), **ctx)
+    except ContextOverflow:
+        return None
+    return rows if sum(len(r["ids"]) for r in rows) <= max_tokens else None
+
+
+def pack_by_budget(variants, max_tokens):
+    """Group a stream of variants (row lists) into micro-batches of at most ``max_tokens`` row
+    tokens, in arrival order; a variant larger than the budget becomes a micro-batch of its own."""
+    group, used = [], 0
+    for rows in variants:
+        size = sum(len(r["ids"]) for r in rows)
+        if size > max_tokens:
+            yield [rows]
+            continue
+        if group and used + size > max_tokens:
+            yield group
+            group, used = [], 0
+        group.append(rows)
+        used += size
+    if group:
+        yield group
+
+
 class DecisionRowDataset(IterableDataset):
-    """Endless stream of decision micro-batches: each epoch reshuffles, re-augments every record
-    (plus none pairs), encodes rows and packs whole variants up to ``max_tokens`` row tokens
-    (longer variants alone, up to ``max_variant_tokens``).  Records are sharded by (rank, worker)."""
+    """Endless stream of packed decision micro-batches.
+
+    Records are dealt to (rank x DataLoader worker) shards by ``sharding.EpochSampler`` (a fresh
+    permutation every epoch, equal counts per shard); every visit re-augments the record with a
+    generator seeded by (seed, epoch, record), encodes its variants, drops the ones over the
+    context budgets (counted in ``skipped``) and ``pack_by_budget`` groups them into micro-batches
+    of ``max_tokens`` row tokens (a larger variant, up to ``max_variant_tokens``, goes alone)."""
 
     def __init__(self, records, tokenizer, rank=0, world=1, seed=0, max_tokens=32768, max_state=7552,
                  p_none_pair=0.25, max_variant_tokens=None):
+        if not records:
+            raise ValueError("DecisionRowDataset needs at least one record")
         self.records, self.tok, self.rank, self.world, self.seed = records, tokenizer, rank, world, seed
         self.max_tokens, self.ctx, self.p_none_pair = max_tokens, training_context(max_state), p_none_pair
         self.max_variant_tokens = max(max_tokens, max_variant_tokens or 0)
         self.skipped = 0
 
-    def _variants(self, epoch, idx):
-        rng = random.Random(_seed(self.seed, epoch, idx))
-        for v in record_variants(self.records[idx], rng, self.p_none_pair):
-            try:
-                rows = encode_rows(self.tok, materialize(v), **self.ctx)
-            except ContextOverflow:
-                self.skipped += 1
-                continue
-            if sum(len(r["ids"]) for r in rows) > self.max_variant_tokens:
-                self.skipped += 1
-                continue
-            yield rows
+    def _variants(self, indices, epoch):
+        for idx in indices:
+            rng = random.Random(mix_seed(self.seed, epoch, idx))
+            for variant in record_variants(self.records[idx], rng, self.p_none_pair):
+                rows = _encode_variant(self.tok, variant, self.ctx, self.max_variant_tokens)
+                if rows is None:
+                    self.skipped += 1
+                else:
+                    yield rows
 
     def __iter__(self):
-        info = get_worker_info()
-        wid, nw = (info.id, info.num_workers) if info else (0, 1)
-        shard, nshard = self.rank * nw + wid, self.world * nw
-        n = len(self.records)
-        if n == 0:
-            raise ValueError("DecisionRowDataset has no records")
+        shard, nshard = worker_shard(self.rank, self.world)
+        sampler = EpochSampler(len(self.records), shard, nshard, self.seed)
         epoch = 0
         while True:
-            order = list(range(n))
-            random.Random(_seed(self.seed, "order", epoch)).shuffle(order)
-            batch, used, emitted = [], 0, False
-            for idx in (order[i % n] for i in range(shard, max(n, nshard), nshard)):
-                for rows in self._variants(epoch, idx):
-                    t = sum(len(r["ids"]) for r in rows)
-                    if t > self.max_tokens:
-                        emitted = True
-                        yield pack_decision([rows], self.tok)
-                        continue
-                    if batch and used + t > self.max_tokens:
-                        emitted = True
-                        yield pack_decision(batch, self.tok)
-                        batch, used = [], 0
-                    batch.append(rows)
-                    used += t
-            if batch:
-                emitted = True
-                yield pack_decision(batch, self.tok)
-            if not emitted:
-                raise RuntimeError(f"decision shard {shard}/{nshard} produced no micro-batch in epoch {epoch}")
+            produced = False
+            for group in pack_by_budget(self._variants(sampler.epoch(epoch), epoch), self.max_tokens):
+                produced = True
+                yield pack_decision(group, self.tok)
+            if not produced:
+                raise RuntimeError(f"decision shard {shard}/{nshard}: no record fits the budgets in epoch {epoch}")
             epoch += 1

@@ -51,16 +51,24 @@ class _GdnBlock(torch.autograd.Function):
         gb = proj[:, Cc + vd:Cc + vd + Hv]
         ga = proj[:, Cc + vd + Hv:Cc + vd + 2 * Hv]
         a_log, dtb = A_log.float().contiguous(), dt_bias.float().contiguous()
-        ckpt = torch.empty(C.gdn_state_numel(B, T, Hv, mode, L, bd), dtype=torch.float32, device=x.device)
-        o = torch.empty(M, vd, dtype=x.dtype, device=x.device)
         scale = dk ** -0.5
         flags = (lay.causal_clean, lay.causal_noisy)
-        C.gdn_fwd(mixed, ga, gb, a_log, dtb, doc, o, ckpt, B, T, Hk, Hv, mode, L, V, bd, flags[0], flags[1], scale)
+        chunked = use_chunk_kernels(lay)
+        if chunked:
+            o, saved = chunk_forward(mixed, ga, gb, a_log, dtb, doc, B, T, Hk, Hv, lay, scale)
+            ckpt = saved["bufs"]
+            ctx.chunk_geo = saved["geo"]
+        else:
+            ckpt = [torch.empty(C.gdn_state_numel(B, T, Hv, mode, L, bd), dtype=torch.float32, device=x.device)]
+            o = torch.empty(M, vd, dtype=x.dtype, device=x.device)
+            C.gdn_fwd(mixed, ga, gb, a_log, dtb, doc, o, ckpt[0], B, T, Hk, Hv, mode, L, V, bd, flags[0], flags[1],
+                      scale)
+        ctx.chunked = chunked
         y = torch.empty(M, vd, dtype=x.dtype, device=x.device)
         C.gdn_gnorm_fwd(o, z, gnorm, y, Hv, cfg.eps)
         out = torch.empty_like(x)
         gemm(TN, y, w_out, out, x, 1.0, 1.0)
-        ctx.save_for_backward(x, rstd, proj, mixed, o, ckpt)
+        ctx.save_for_backward(x, rstd, proj, mixed, o, *ckpt)
         ctx.params = (norm_w, w_in, conv_w, dt_bias, A_log, gnorm, w_out)   # see ops.blocks._AttnBlock
         ctx.geo = (B, T, Hk, Hv, dk, kd, vd, Cc, mode, L, V, bd, flags, scale)
         ctx.doc, ctx.eps = doc, cfg.eps
@@ -68,7 +76,7 @@ class _GdnBlock(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dout):
-        x, rstd, proj, mixed, o, ckpt = ctx.saved_tensors
+        x, rstd, proj, mixed, o, *ckpt = ctx.saved_tensors
         norm_w, w_in, conv_w, dt_bias, A_log, gnorm, w_out = ctx.params
         B, T, Hk, Hv, dk, kd, vd, Cc, mode, L, V, bd, flags, scale = ctx.geo
         doc, eps = ctx.doc, ctx.eps
@@ -94,9 +102,14 @@ class _GdnBlock(torch.autograd.Function):
         dmixed = torch.empty(M, Cc, dtype=x.dtype, device=x.device)
         dA = torch.zeros(Hv, dtype=torch.float32, device=x.device)
         ddt = torch.zeros(Hv, dtype=torch.float32, device=x.device)
-        C.gdn_bwd(mixed, ga, gb, A_log.float().contiguous(), dt_bias.float().contiguous(), doc, ckpt, do, dmixed,
-                  dproj[:, Cc + vd + Hv:Cc + vd + 2 * Hv], dproj[:, Cc + vd:Cc + vd + Hv], dA, ddt,
-                  B, T, Hk, Hv, mode, L, V, bd, flags[0], flags[1], scale)
+        dga, dgb = dproj[:, Cc + vd + Hv:Cc + vd + 2 * Hv], dproj[:, Cc + vd:Cc + vd + Hv]
+        if ctx.chunked:
+            from .blocks import device_error_word
+            C.gdn_chunk_bwd(mixed, ga, gb, A_log.float().contiguous(), dt_bias.float().contiguous(), doc, o, ckpt,
+                            device_error_word(x.device), ctx.chunk_geo, scale, do, dmixed, dga, dgb, dA, ddt)
+        else:
+            C.gdn_bwd(mixed, ga, gb, A_log.float().contiguous(), dt_bias.float().contiguous(), doc, ckpt[0], do,
+                      dmixed, dga, dgb, dA, ddt, B, T, Hk, Hv, mode, L, V, bd, flags[0], flags[1], scale)
         del do
         # conv
         g_conv = torch.zeros(conv_w.shape, dtype=torch.float32, device=x.device)
@@ -120,6 +133,13 @@ def gdn_block_cuda(x, layer, actx, cfg):
         raise NotImplementedError("the GDN kernels are built for 128-dim key/value heads and conv width <= 4")
     return _GdnBlock.apply(x, layer.input_norm, layer.w_in, layer.conv_w, layer.dt_bias, layer.A_log, layer.gnorm,
                            layer.w_out, actx, cfg)
+
+
+def use_chunk_kernels(lay):
+    """The chunked tcgen05 kernels serve every layout whose chunk length they support (override with
+    TRIDA_GDN=scan to run the per-token recurrent scan instead)."""
+    import os
+    return os.environ.get("TRIDA_GDN", "chunk") == "chunk" and chunk_len(lay) is not None
 
 
 def chunk_len(lay):
