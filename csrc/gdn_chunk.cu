@@ -43,8 +43,8 @@ struct LocalSmem {
   static constexpr int R2 = R1 + TILE;            // V -> Vb -> P
   static constexpr int R3 = R2 + TILE;            // T -> U^T (noisy) / U (out, TMA)
   static constexpr int R4 = R3 + TILE;            // A blocks (fp32) -> -W
-  static constexpr int R5 = R4 + 128 * AF_LD * 4; // state buffer 1 (R4 is 33,280 B: R5 stays 1 KB aligned below)
-  static constexpr int R5A = (R5 + 1023) / 1024 * 1024;
+  static constexpr int R5 = R4 + AF_BYTES;        // state buffer 1
+  static constexpr int R5A = R5;
   static constexpr int META = R5A + TILE;
   static constexpr int BARS = META + Meta::BYTES;
   static constexpr int TOTAL = BARS + 64;
@@ -151,7 +151,7 @@ __global__ void __launch_bounds__(NT, 1) local_kernel(const __grid_constant__ CU
       for (int s = 0; s < 128; ++s) {
         if (s >= cs && s < cs + C) {
           const float v = (s < r && m.seg[s] == sg) ? bt * x[s] * __expf(Gt - m.G[s]) : 0.f;
-          Af[r * AF_LD + (s - cs)] = v;
+          Af[af_idx(r, s - cs)] = v;
         }
       }
     }

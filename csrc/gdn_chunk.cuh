@@ -19,7 +19,12 @@ constexpr int TR = 128;           // rows per tile
 constexpr int NT = 128;           // threads (one per tile row / TMEM lane)
 constexpr int TILE = 32768;       // bytes of a 128 x 128 bf16 tile
 constexpr int SUB = 16384;        // one [128][64] swizzled half
-constexpr int AF_LD = 65;         // fp32 row stride of the A blocks (conflict-free rows and columns)
+constexpr int AF_BYTES = 128 * 64 * 4;   // fp32 A blocks: 128 rows x 64 chunk-local columns (one tile)
+
+// Index of A-block element (row, chunk-local column): 64-float rows with the column XOR-ed by the
+// row's low 5 bits, so a warp writing 32 rows of one column hits 32 banks while a warp reading one
+// row (every thread the same element) is a broadcast.
+__device__ __forceinline__ int af_idx(int row, int col) { return row * 64 + (col ^ (row & 31)); }
 
 enum Mode { PREP = 0, NOISY = 1, OUT = 2 };
 
@@ -150,6 +155,7 @@ struct Args {
   float* dpart;             // [B*T, Hv, RED]: dq | dk | dbeta | dg (per value head)
   bf16* dv; int64_t lddv;   // value-gradient rows (head columns at hv * D)
   const bf16* mixed; int64_t ldm;   // conv output (v rows for d beta)
+  const bf16* qk_rows;              // [B*T, Hk, 2, D] normalised q (times scale) / k
 };
 
 __device__ __forceinline__ int clean_len(const Args& a) { return a.mode ? a.L : a.T; }
@@ -239,7 +245,7 @@ __device__ void tile_meta(const Args& a, const TileGeo& t, const Meta& m) {
 }
 
 // Column j of T = (I + A)^-1 for the chunk holding tile column j (forward substitution over the
-// fp32 A blocks [128][AF_LD], chunk-local columns), written into the T tile as bf16 (zero outside
+// fp32 A blocks, chunk-local columns, see af_idx), written into the T tile as bf16 (zero outside
 // the chunk's diagonal block).
 template <int C>
 __device__ __forceinline__ void invert_column(const float* Af, uint8_t* Tt) {
@@ -249,10 +255,10 @@ __device__ __forceinline__ void invert_column(const float* Af, uint8_t* Tt) {
   for (int t = 0; t < C; ++t) x[t] = (t == jl) ? 1.f : 0.f;
 #pragma unroll
   for (int t = 1; t < C; ++t) {
-    const float* arow = Af + (cs + t) * AF_LD;
+    const int row = cs + t;
     float s = 0.f;
 #pragma unroll
-    for (int u = 0; u < t; ++u) s = fmaf(arow[u], x[u], s);
+    for (int u = 0; u < t; ++u) s = fmaf(Af[af_idx(row, u)], x[u], s);
     if (t > jl) x[t] = -s;
   }
 #pragma unroll

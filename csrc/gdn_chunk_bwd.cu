@@ -167,7 +167,7 @@ struct BwdSmem {
   static constexpr int S0 = 0, S1 = TILE, S2 = 2 * TILE, S3 = 3 * TILE, S4 = 4 * TILE, S5 = 5 * TILE;
   static constexpr int META = 6 * TILE;
   static constexpr int RED = META + Meta::BYTES;        // colsum scratch [4][128] + dG [128] + misc
-  static constexpr int BARS = RED + (4 * 128 + 128 + 64) * 4;
+  static constexpr int BARS = RED + (4 * 128 + 3 * 128) * 4;
   static constexpr int TOTAL = BARS + 64;
 };
 
@@ -539,7 +539,23 @@ __global__ void __launch_bounds__(NT, 1) scanb_kernel(const __grid_constant__ CU
   if (r < 32) tmem_dealloc(tmem, 256);
 }
 
-// ---- bwd1: T, dPE, dQ, dW, dT, dA ----------------------------------------------------------------------
+// Decay gradient of a pair term: thread t holds X[t][s] = dZ_ts Z_ts (fp32, zero outside its
+// chunk's mask) of a factor Z_ts proportional to exp(G_lim(t) - G_s).  Since G_lim(t) - G_s is the
+// sum of g_j over s < j <= lim(t), thread j receives sum_{t : lim(t) >= j} sum_{s < j} X[t][s]:
+// each pair enters once, so nothing cancels (the row-sum-minus-column-sum form would subtract two
+// large, differently rounded terms).
+__device__ __forceinline__ float pair_decay_grad(float (&x)[128], int lim, float* red) {
+  float run = 0.f;
+#pragma unroll
+  for (int j = 0; j < 128; ++j) {
+    const float v = x[j];
+    x[j] = (lim >= j) ? run : 0.f;
+    run += v;
+  }
+  return colsum128(x, red);
+}
+
+// ---- bwd1: T, dPE, dQ, dW, dT, dA and the pair / read-out parts of dg ------------------------------
 template <int C>
 __global__ void __launch_bounds__(NT, 1) bwd1_kernel(const __grid_constant__ CUtensorMap tm_qk,
                                                      const __grid_constant__ CUtensorMap tm_do,
@@ -556,7 +572,8 @@ __global__ void __launch_bounds__(NT, 1) bwd1_kernel(const __grid_constant__ CUt
   uint64_t* mma_bar = bars + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
   const Meta m = carve_meta(sm + S::META);
-  float* dG = reinterpret_cast<float*>(sm + S::RED) + 4 * 128;
+  float* red = reinterpret_cast<float*>(sm + S::RED);
+  float* inter = red + 4 * 128;          // [128] read-out decay term of the state part of each row
   const int r = threadIdx.x;
   const TileGeo t = tile_geo(a);
   constexpr int NCK = TR / C;
@@ -574,16 +591,16 @@ __global__ void __launch_bounds__(NT, 1) bwd1_kernel(const __grid_constant__ CUt
   const uint32_t sbase = smem_addr(sm);
   uint32_t mph = 0, lph = 0;
   bool ok = true;
-  // S0 K | S1 dO -> dOg -> V -> Y | S2 U -> states -> dW^T | S3 dU | S4 A (fp32) -> dPE -> dT | S5 T
+  // S0 K | S1 dO -> dOg -> V -> Y | S2 U -> states -> dW^T | S3 dU | S4 A (fp32) -> dPE -> dT | S5 Q -> T
   if (r == 0) {
-    mbar_expect_tx(ld_bar, 4 * TILE);
+    mbar_expect_tx(ld_bar, 5 * TILE);
     load_rows(sm + S::S0, &tm_qk, ld_bar, 2 * t.hk + 1, t.t0, t.b);
     load_cols(sm + S::S1, &tm_do, ld_bar, t.hv * D, t.t0, t.b);
     load_rows(sm + S::S2, &tm_u, ld_bar, t.hv, t.t0, t.b);
     load_rows(sm + S::S3, &tm_du, ld_bar, t.hv, t.t0, t.b);
+    load_rows(sm + S::S5, &tm_qk, ld_bar, 2 * t.hk, t.t0, t.b);
   }
   tile_meta<C>(a, t, m);
-  dG[r] = 0.f;
   WAIT_LD(231);
   const bool valid = t.p0 + r < t.Ls;
   const int cs = (r / C) * C;
@@ -602,11 +619,12 @@ __global__ void __launch_bounds__(NT, 1) bwd1_kernel(const __grid_constant__ CUt
     tc_fence_after();
     mma(acc0, KM(sbase + S::S0), KM(sbase + S::S0), 128, 128, false);        // KK^T (kept to the end)
     mma(acc1, KM(sbase + S::S1), KM(sbase + S::S2), 128, 128, false);        // dP = dO U^T
+    mma(acc3, KM(sbase + S::S5), KM(sbase + S::S0), 128, 128, false);        // QK^T
     umma_commit(mma_bar);
   }
   WAIT_MMA(232);
   float x[128];
-  // A blocks (fp32, XOR-swizzled 64-float rows) -> T
+  // A blocks (fp32, see af_idx) -> T (over Q, whose MMA is done)
   {
     float* Af = reinterpret_cast<float*>(sm + S::S4);
     ld_row128(acc0, 0, x);
@@ -616,36 +634,35 @@ __global__ void __launch_bounds__(NT, 1) bwd1_kernel(const __grid_constant__ CUt
     for (int s = 0; s < 128; ++s) {
       if (s >= cs && s < cs + C) {
         const float v = (s < r && m.seg[s] == sg) ? bt * x[s] * __expf(Gt - m.G[s]) : 0.f;
-        Af[r * AF_LD + (s - cs)] = v;
+        Af[af_idx(r, s - cs)] = v;
       }
     }
   }
   __syncthreads();
   invert_column<C>(reinterpret_cast<const float*>(sm + S::S4), sm + S::S5);
   __syncthreads();
-  // T rows for bwd2
   if (valid) {
     ld_row_bf(sm + S::S5, r, x);
     store_row_bf(a.tt + (grow(a, t, r) * a.Hv + t.hv) * D, x, 1.f);
   }
-  // dPE from dP (acc1); dGr = dO . O scattered to the read-out row
-  ld_row128(acc1, 0, x);
+  // dPE = dP . mask . e^{Gr_t - G_s} (tile + rows for bwd2); pair term dP . P of the decay gradient
+  float dg = 0.f;
   {
+    float qk[128];
+    ld_row128(acc1, 0, x);
+    ld_row128(acc3, 0, qk);
     const float Gr = m.Gr[r];
     const int rd = m.rd[r], sg = m.seg[r];
 #pragma unroll
     for (int s = 0; s < 128; ++s) {
       const bool on = (s >= cs) && (s <= rd) && (m.seg[s] == sg) && valid;
-      x[s] = on ? x[s] * __expf(Gr - m.G[s]) : 0.f;
+      const float e = on ? __expf(Gr - m.G[s]) : 0.f;
+      x[s] = x[s] * e;              // dPE
+      qk[s] = x[s] * qk[s];         // dP . P
     }
-  }
-  st_row(sm + S::S4, r, x);
-  if (valid) store_row_bf(a.dpe + (grow(a, t, r) * a.Hv + t.hv) * D, x, 1.f);
-  if (valid) {
-    float o[128];
-    ld_row_bf(sm + S::S1, r, o);
-    const float g = dot_gmem_bf(a.o_fwd + grow(a, t, r) * (int64_t)(a.Hv * D) + t.hv * D, o);
-    atomicAdd(&dG[m.rd[r]], g);
+    st_row(sm + S::S4, r, x);
+    if (valid) store_row_bf(a.dpe + (grow(a, t, r) * a.Hv + t.hv) * D, x, 1.f);
+    dg += pair_decay_grad(qk, valid ? rd : -1, red);
   }
   // dOg = carry e^{Gr} dO in place
   {
@@ -656,7 +673,7 @@ __global__ void __launch_bounds__(NT, 1) bwd1_kernel(const __grid_constant__ CUt
     st_row(sm + S::S1, r, x);
   }
   SYNC_FOR_MMA();
-  // dQ^T (acc2) = K^T dPE^T (+ per chunk S0 dOg^T); dW^T (acc3) per chunk = S0 dU^T (negated on read)
+  // dQ^T intra (acc2) = K^T dPE^T; per chunk: dQ^T inter (acc1) = S0 dOg^T, -dW^T (acc3) = S0 dU^T
   if (ok && r == 0) {
     tc_fence_after();
     mma(acc2, MN(sbase + S::S0), KM(sbase + S::S4), 128, 128, false);
@@ -672,7 +689,7 @@ __global__ void __launch_bounds__(NT, 1) bwd1_kernel(const __grid_constant__ CUt
       ok = mbar_wait(ld_bar, (lph + c) & 1, a.err, 234);
       if (!ok) break;
       tc_fence_after();
-      mma(acc2 + c * C, KM(sbase + S::S2), KM(sbase + S::S1, c * C), C, 128, true);
+      mma(acc1 + c * C, KM(sbase + S::S2), KM(sbase + S::S1, c * C), C, 128, false);
       mma(acc3 + c * C, KM(sbase + S::S2), KM(sbase + S::S3, c * C), C, 128, false);
     }
     umma_commit(mma_bar);
@@ -681,14 +698,32 @@ __global__ void __launch_bounds__(NT, 1) bwd1_kernel(const __grid_constant__ CUt
   mph += NCK;
   lph += NCK;
   WAIT_MMA(235);
-  // dq rows (lanes k of dQ^T: transposed, coalesced per row)
-  ld_row128(acc2, 0, x);
+  // dq rows = intra + inter (lanes k: transposed, coalesced per row); read-out decay term of the
+  // state part: inter_t = q_t . dq_inter_t (a column dot over k)
   {
-    float* dst = a.dpart + grow(a, t, 0) * a.Hv * RED + t.hv * RED + r;
+    float y[128];
+    ld_row128(acc1, 0, x);        // inter
+    ld_row128(acc2, 0, y);        // intra
     const int nv = min(TR, t.Ls - t.p0);
+    float* dst = a.dpart + grow(a, t, 0) * a.Hv * RED + t.hv * RED + r;
+    const bf16* qcol = a.qk_rows + ((grow(a, t, 0) * a.Hk + t.hk) * 2) * D + r;   // q[t][k = r]
 #pragma unroll
-    for (int s = 0; s < TR; ++s)
-      if (s < nv) dst[(int64_t)s * a.Hv * RED] = x[s];
+    for (int s = 0; s < TR; ++s) {
+      float qv = 0.f;
+      if (s < nv) {
+        dst[(int64_t)s * a.Hv * RED] = x[s] + y[s];
+        qv = __bfloat162float(qcol[(int64_t)s * a.Hk * 2 * D]);
+      }
+      y[s] = x[s] * qv;
+    }
+    inter[r] = colsum128(y, red);
+  }
+  __syncthreads();
+  {
+    // dg_j += sum of inter_t over rows t of j's segment that read out at or after j
+    const int sg = m.seg[r];
+    for (int tt = cs; tt < cs + C; ++tt)
+      if (m.seg[tt] == sg && m.rd[tt] >= r) dg += inter[tt];
   }
   // dW^T (negated) into S2 as [k][t]; dW rows to global
   ld_row128(acc3, 0, x);
@@ -758,15 +793,17 @@ __global__ void __launch_bounds__(NT, 1) bwd1_kernel(const __grid_constant__ CUt
       const bool on = (s >= cs) && (s < r) && (m.seg[s] == sg) && valid;
       const float e = on ? __expf(Gt - m.G[s]) : 0.f;
       const float da = on ? -x[s] : 0.f;
-      sa = fmaf(da, kk[s] * e, sa);             // dA . (KK E): d beta and the row part of dG
+      const float ke = kk[s] * e;
+      sa = fmaf(da, ke, sa);                    // d beta_t (A part)
+      kk[s] = da * bt * ke;                     // dA . A (pair term of the decay gradient)
       x[s] = da * bt * e;                       // dAE
     }
+    if (valid) store_row_bf(a.dae + (grow(a, t, r) * a.Hv + t.hv) * D, x, 1.f);
+    dg += pair_decay_grad(kk, valid ? r : -1, red);
     if (valid) {
-      // dG[r] is complete: its atomic adds (dGr) came before several CTA barriers
-      store_row_bf(a.dae + (grow(a, t, r) * a.Hv + t.hv) * D, x, 1.f);
       float* scp = a.sc + (grow(a, t, r) * a.Hv + t.hv) * 2;
       scp[0] = sa;
-      scp[1] = dG[r] + bt * sa;
+      scp[1] = dg;
     }
   }
   tmem_wait_ld();
@@ -776,7 +813,7 @@ __global__ void __launch_bounds__(NT, 1) bwd1_kernel(const __grid_constant__ CUt
   if (r < 32) tmem_dealloc(tmem, 512);
 }
 
-// ---- bwd2: dV, dKb, dK, d beta, dg -------------------------------------------------------------------
+// ---- bwd2: dV, dKb, dK, d beta, the one-sided parts of dg ------------------------------------------
 template <int C>
 __global__ void __launch_bounds__(NT, 1) bwd2_kernel(const __grid_constant__ CUtensorMap tm_qk,
                                                      const __grid_constant__ CUtensorMap tm_tt,
@@ -797,8 +834,9 @@ __global__ void __launch_bounds__(NT, 1) bwd2_kernel(const __grid_constant__ CUt
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
   const Meta m = carve_meta(sm + S::META);
   float* red = reinterpret_cast<float*>(sm + S::RED);
-  float* dG = red + 4 * 128;
-  float* misc = dG + 128;
+  float* kb = red + 4 * 128;     // [128] dKb_t . Kb_t
+  float* ksx = kb + 128;         // [128] k_s . (kts_s dS1 u_s) (clean stream)  (aliases the misc area)
+  float* misc = red;             // warp partial sums (the colsum scratch is idle then)
   const int r = threadIdx.x;
   const TileGeo t = tile_geo(a);
   constexpr int NCK = TR / C;
@@ -828,13 +866,13 @@ __global__ void __launch_bounds__(NT, 1) bwd2_kernel(const __grid_constant__ CUt
   const bool valid = t.p0 + r < t.Ls;
   const int cs = (r / C) * C;
   const int64_t row = grow(a, t, r);
-  float dbeta = 0.f;
-  dG[r] = 0.f;
+  float dbeta = 0.f, dg = 0.f;
   if (valid) {
     const float2 s1 = *reinterpret_cast<const float2*>(a.sc + (row * a.Hv + t.hv) * 2);
     dbeta = s1.x;
-    dG[r] = s1.y;
+    dg = s1.y;
   }
+  ksx[r] = 0.f;
   WAIT_LD(241);
   if (!valid) {
     const uint4 z = make_uint4(0, 0, 0, 0);
@@ -862,7 +900,7 @@ __global__ void __launch_bounds__(NT, 1) bwd2_kernel(const __grid_constant__ CUt
   }
   float x[128];
   float ks = 0.f;
-  // dV and the value part of d beta; the Kb parts of d beta and dG
+  // dV and the value part of d beta; the Kb parts of d beta and dg
   ld_row128(acc0, 0, x);
   if (valid) {
     const bf16* vrow = a.mixed + row * a.ldm + v_col0 + t.hv * D;
@@ -875,7 +913,7 @@ __global__ void __launch_bounds__(NT, 1) bwd2_kernel(const __grid_constant__ CUt
     const float ce = m.carry[r] * __expf(m.G[r]);
     ks = m.beta[r] * ce;
     dbeta += ce * kd;
-    dG[r] += ks * kd;
+    kb[r] = valid ? ks * kd : 0.f;
   }
   WAIT_LD(243);
   if (!valid) {
@@ -889,21 +927,16 @@ __global__ void __launch_bounds__(NT, 1) bwd2_kernel(const __grid_constant__ CUt
   SYNC_FOR_MMA();
   if (ok && r == 0) {
     tc_fence_after();
-    // column parts (lanes s): dPE^T Q + dAE^T K
+    // column parts (lanes s): dPE^T Q + dAE^T K;  row part: dAE K
     mma(acc2, MN(sbase + S::S2), MN(sbase + S::S1), 128, 128, false);
     mma(acc2, MN(sbase + S::S3), MN(sbase + S::S0), 128, 128, true);
-    // row part: dAE K
-    mma(acc3, KM(sbase + S::S3), MN(sbase + S::S0), 128, 128, false);
+    mma(acc2, KM(sbase + S::S3), MN(sbase + S::S0), 128, 128, true);
     umma_commit(mma_bar);
   }
   WAIT_MMA(244);
   ld_row128(acc2, 0, x);
-  dG[r] -= dot_row_bf(sm + S::S0, r, x);
   {
     float y[128];
-    ld_row128(acc3, 0, y);
-#pragma unroll
-    for (int i = 0; i < 128; ++i) x[i] += y[i];
     ld_row128(acc1, 0, y);
 #pragma unroll
     for (int i = 0; i < 128; ++i) x[i] += ks * y[i];
@@ -913,7 +946,9 @@ __global__ void __launch_bounds__(NT, 1) bwd2_kernel(const __grid_constant__ CUt
 #pragma unroll
     for (int i = 0; i < 128; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]);
   }
-  // end-state term of the clean chunks: dK_s += kts_s dS1 u_s, dG via k_s . (kts_s dS1 u_s)
+  // end-state term of the clean chunks: dK_s += kts_s dS1 u_s; decay parts from k_s . (kts_s dS1 u_s)
+  // and gamma <S0, dS1>
+  float gsd = 0.f;   // gamma_c <S0_c, dS1_c> of this thread's chunk
   if (t.stream == 0) {
     SYNC_FOR_MMA();
     if (ok && r == 0) {
@@ -945,7 +980,6 @@ __global__ void __launch_bounds__(NT, 1) bwd2_kernel(const __grid_constant__ CUt
         mma(acc0 + c * C, KM(sbase + S::S2), KM(sbase + S::S1, c * C), C, 128, false);
         umma_commit(mma_bar);
       }
-      // gamma_c <S0, dS1> for the chunk's last row
       {
         float srow[128];
         ld_row_bf(sm + S::S3, r, srow);
@@ -955,21 +989,16 @@ __global__ void __launch_bounds__(NT, 1) bwd2_kernel(const __grid_constant__ CUt
       }
       WAIT_MMA(247);
       __syncthreads();
-      if (r == 0 && real) {
-        const float tot = misc[0] + misc[1] + misc[2] + misc[3];
-        dG[c * C + C - 1] += a.gamma[sb + blk] * tot;
-      }
-      SYNC_FOR_MMA();   // S2 / S3 are reloaded next chunk
+      if (r / C == c && real) gsd = a.gamma[sb + blk] * (misc[0] + misc[1] + misc[2] + misc[3]);
+      SYNC_FOR_MMA();   // S2 / S3 are reloaded next chunk; misc is rewritten
     }
-    // X^T[k][s] (lanes k): column dots with K give k_s . (kts_s dS1 u_s)
+    // X^T[k][s] (lanes k): column dots with K give ksx_s = k_s . (kts_s dS1 u_s)
     ld_row128(acc0, 0, x);
     {
       float y[128];
 #pragma unroll
       for (int s = 0; s < 128; ++s) y[s] = x[s] * ld_el(sm + S::S0, s, r);
-      const float ksx = colsum128(y, red);       // thread r: column r = token r
-      atomicAdd(&dG[r], -ksx);
-      atomicAdd(&dG[cs + C - 1], ksx);
+      ksx[r] = colsum128(y, red);
     }
     __syncthreads();   // every dk row above is written
     {
@@ -981,17 +1010,19 @@ __global__ void __launch_bounds__(NT, 1) bwd2_kernel(const __grid_constant__ CUt
     }
   }
   __syncthreads();
-  // dg = reverse cumulative sum of dG inside the segment
+  // one-sided decay terms: Kb rows at or after j in j's segment; K~ rows before j and gamma when j
+  // lies in the chunk's last segment
   if (valid) {
-    float g = 0.f;
-    const int sg = m.seg[r];
-    for (int j = r; j < cs + C; ++j) {
-      if (m.seg[j] != sg) break;
-      g += dG[j];
+    const int sg = m.seg[r], last = cs + C - 1;
+    for (int tt = r; tt < cs + C && m.seg[tt] == sg; ++tt) dg += kb[tt];
+    if (sg == m.seg[last]) {
+      for (int s = cs; s < r; ++s)
+        if (m.seg[s] == sg) dg += ksx[s];
+      dg += gsd;
     }
     float* dst = a.dpart + (row * a.Hv + t.hv) * RED + 2 * D;
     dst[0] = dbeta;
-    dst[1] = g;
+    dst[1] = dg;
   }
   tmem_wait_ld();
   tc_fence_before();
@@ -1123,7 +1154,7 @@ int gdn_chunk_bwd(const GdnChunkBwdParams& p, cudaStream_t st) {
   a.o_fwd = f.o; a.d_o = p.d_o; a.du0 = p.du0; a.du = p.du; a.qg = p.qg; a.ds0 = p.ds0; a.dckpt = p.dckpt;
   a.dpe = p.dpe; a.dae = p.dae; a.dw = p.dw; a.tt = p.tt; a.sc = p.sc; a.dpart = p.dpart;
   a.dv = p.dmixed + 2 * f.Hk * D; a.lddv = p.lddm;
-  a.mixed = f.mixed; a.ldm = f.ldm;
+  a.mixed = f.mixed; a.ldm = f.ldm; a.qk_rows = f.qk;
   int rc;
   switch (f.C) {
     case 16: rc = launch_bwd<16>(p, a, st); break;

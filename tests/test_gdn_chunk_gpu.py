@@ -136,4 +136,9 @@ def test_chunk_backward_op(case):
     errs = {k: _rel(dmixed[:, s].cpu(), dm_r[:, s]) for k, s in parts.items()}
     errs["dbeta_pre"] = _rel(dgb.cpu(), db_r)
     errs["ddecay_pre"] = _rel(dga.cpu(), da_r)
-    assert all(v < 3e-2 for v in errs.values()), errs
+    if errs["ddecay_pre"] >= 3e-2:
+        a, r_ = dga.float().cpu(), da_r
+        print("ddecay rows (gpu / ref), head 0:", [(round(a[i, 0].item(), 4), round(r_[i, 0].item(), 4))
+                                                  for i in range(0, min(B * T, 24))])
+        print("ratio mean/std:", (a / r_).mean().item(), (a / r_).std().item())
+    assert all(v < 3e-2 for v in errs.values()), sorted(errs.items())
