@@ -60,6 +60,7 @@ __global__ void __launch_bounds__(NT, 1) local_kernel(const __grid_constant__ CU
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   using S = LocalSmem;
+  using WN = Win<C>;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::BARS);
   uint64_t* ld_bar = bars;          // TMA loads of Q / K / V (or U)
   uint64_t* mma_bar = bars + 1;     // tcgen05.commit
@@ -120,9 +121,8 @@ __global__ void __launch_bounds__(NT, 1) local_kernel(const __grid_constant__ CU
   const bool valid = t.p0 + r < t.Ls;
   if (MODE == OUT && !valid) {
     // rows past the clean stream hold other streams' (unwritten) U rows: zero them
-    const uint4 z = make_uint4(0, 0, 0, 0);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) *reinterpret_cast<uint4*>(sm + S::R3 + toff(r, 8 * j)) = z;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) sm_zero32(sm + S::R3, r, g);
   }
   fence_async_smem();
   __syncthreads();
@@ -138,39 +138,40 @@ __global__ void __launch_bounds__(NT, 1) local_kernel(const __grid_constant__ CU
   ++mph;
   tc_fence_after();
   const int cs = (r / C) * C;
-  float x[128];
+  const int64_t grow0 = (int64_t)t.b * a.T + t.t0;    // global row of tile row 0
+  float x[32];
 
   if (MODE != OUT) {
     // ---- A blocks (fp32, chunk-local columns) and T = (I + A)^-1 ---------------------------------
-    float* Af = reinterpret_cast<float*>(sm + S::R4);
-    ld_row128(acc0, 0, x);
     {
+      float* Af = reinterpret_cast<float*>(sm + S::R4);
       const float Gt = m.G[r], bt = m.beta[r];
       const int sg = m.seg[r];
+#pragma unroll 1
+      for (int g = WN::g0(); g < WN::g0() + WN::NG; ++g) {
+        tm_ld32(acc0, g, x);
 #pragma unroll
-      for (int s = 0; s < 128; ++s) {
-        if (s >= cs && s < cs + C) {
-          const float v = (s < r && m.seg[s] == sg) ? bt * x[s] * __expf(Gt - m.G[s]) : 0.f;
-          Af[af_idx(r, s - cs)] = v;
+        for (int i = 0; i < 32; ++i) {
+          const int s = 32 * g + i;
+          if (s >= cs && s < cs + C)
+            Af[af_idx(r, s - cs)] = (s < r && m.seg[s] == sg) ? bt * x[i] * __expf(Gt - m.G[s]) : 0.f;
         }
       }
     }
     __syncthreads();
-    invert_column<C>(Af, sm + S::R3);
+    invert_column<C>(reinterpret_cast<const float*>(sm + S::R4), sm + S::R3);
     // ---- K~ rows (PREP), Kb = diag(beta carry e^G) K and Vb = diag(beta) V in place ---------------
-    ld_row_bf(sm + S::R1, r, x);
-    if (MODE == PREP && valid)
-      store_row_bf(a.kt + (((int64_t)t.b * a.T + t.t0 + r) * a.Hv + t.hv) * D, x, m.kts[r]);
     {
-      const float ks = m.beta[r] * m.carry[r] * __expf(m.G[r]);
-#pragma unroll
-      for (int i = 0; i < 128; ++i) x[i] *= ks;
-      st_row(sm + S::R1, r, x);
-      ld_row_bf(sm + S::R2, r, x);
-      const float bs = m.beta[r];
-#pragma unroll
-      for (int i = 0; i < 128; ++i) x[i] *= bs;
-      st_row(sm + S::R2, r, x);
+      const float ks = m.beta[r] * m.carry[r] * __expf(m.G[r]), bs = m.beta[r];
+      bf16* kt_row = a.kt + ((grow0 + r) * a.Hv + t.hv) * D;
+#pragma unroll 1
+      for (int g = 0; g < 4; ++g) {
+        sm_ld32(sm + S::R1, r, g, x);
+        if (MODE == PREP && valid) gm_st32(kt_row + 32 * g, x, m.kts[r]);
+        sm_st32(sm + S::R1, r, g, x, ks);
+        sm_ld32(sm + S::R2, r, g, x);
+        sm_st32(sm + S::R2, r, g, x, bs);
+      }
     }
     fence_async_smem();
     tc_fence_before();
@@ -186,32 +187,34 @@ __global__ void __launch_bounds__(NT, 1) local_kernel(const __grid_constant__ CU
     ok = mbar_wait(mma_bar, mph & 1, a.err, 103) && ok;
     ++mph;
     tc_fence_after();
-    if (MODE == PREP) {
-      const int64_t row = (int64_t)t.b * a.T + t.t0 + r;
-      ld_row128(acc1, 0, x);
-      if (valid) store_row_bf(a.wn + (row * a.Hv + t.hv) * D, x, -1.f);
-      ld_row128(acc2, 0, x);
-      if (valid) store_row_bf(a.ut + (row * a.Hv + t.hv) * D, x, 1.f);
-      if (r % C == 0 && valid) a.gamma[((int64_t)t.b * a.Hv + t.hv) * a.nch + (t.p0 + r) / C] = m.gam[r / C];
-    } else {
-      // -W into R4 (the A blocks are dead after the inversion) and, for the backward, its rows
-      ld_row128(acc1, 0, x);
-#pragma unroll
-      for (int i = 0; i < 128; ++i) x[i] = -x[i];
-      st_row(sm + S::R4, r, x);
-      if (valid) store_row_bf(a.wn + (((int64_t)t.b * a.T + t.t0 + r) * a.Hv + t.hv) * D, x, 1.f);
+    {
+      bf16* wn_row = a.wn + ((grow0 + r) * a.Hv + t.hv) * D;
+      bf16* ut_row = a.ut + ((grow0 + r) * a.Hv + t.hv) * D;
+#pragma unroll 1
+      for (int g = 0; g < 4; ++g) {
+        tm_ld32(acc1, g, x);
+        if (valid) gm_st32(wn_row + 32 * g, x, -1.f);                // -W rows (scan / backward)
+        if (MODE == NOISY) sm_st32(sm + S::R4, r, g, x, -1.f);      // -W tile (A blocks are dead)
+        if (MODE == PREP) {
+          tm_ld32(acc2, g, x);
+          if (valid) gm_st32(ut_row + 32 * g, x);
+        }
+      }
     }
+    if (MODE == PREP && r % C == 0 && valid)
+      a.gamma[((int64_t)t.b * a.Hv + t.hv) * a.nch + (t.p0 + r) / C] = m.gam[r / C];
   }
 
   if (MODE != PREP) {
     // ---- Qg = diag(carry e^{Gr}) Q in place (QK^T has completed) ----------------------------------
-    ld_row_bf(sm + S::R0, r, x);
     {
       const float qs = m.carry[r] * __expf(m.Gr[r]);
-#pragma unroll
-      for (int i = 0; i < 128; ++i) x[i] *= qs;
+#pragma unroll 1
+      for (int g = 0; g < 4; ++g) {
+        sm_ld32(sm + S::R0, r, g, x);
+        sm_st32(sm + S::R0, r, g, x, qs);
+      }
     }
-    st_row(sm + S::R0, r, x);
     tmem_wait_ld();
     fence_async_smem();
     tc_fence_before();
@@ -256,33 +259,43 @@ __global__ void __launch_bounds__(NT, 1) local_kernel(const __grid_constant__ CU
     __syncthreads();
     mph += NCK;
     tc_fence_after();
-    // ---- P (from acc3) into R2; NOISY: U^T (acc2; row r = value column r) into R3 ------------------
-    ld_row128(acc3, 0, x);
+    // ---- P (window of acc3) into R2; NOISY: U^T (acc2; row r = value column r) into R3 + U rows -----
     {
       const float Gr = m.Gr[r];
       const int rd = m.rd[r], sg = m.seg[r];
+#pragma unroll 1
+      for (int g = 0; g < 4; ++g) {
+        if (g < WN::g0() || g >= WN::g0() + WN::NG) {
+          sm_zero32(sm + S::R2, r, g);
+          continue;
+        }
+        tm_ld32(acc3, g, x);
 #pragma unroll
-      for (int s = 0; s < 128; ++s) {
-        const bool on = (s >= cs) && (s <= rd) && (m.seg[s] == sg);
-        x[s] = on ? x[s] * __expf(Gr - m.G[s]) : 0.f;
+        for (int i = 0; i < 32; ++i) {
+          const int s = 32 * g + i;
+          const bool on = (s >= cs) && (s <= rd) && (m.seg[s] == sg);
+          x[i] = on ? x[i] * __expf(Gr - m.G[s]) : 0.f;
+        }
+        sm_st32(sm + S::R2, r, g, x);
       }
     }
-    st_row(sm + S::R2, r, x);
     if (MODE == NOISY) {
-      ld_row128(acc2, 0, x);
-      st_row(sm + S::R3, r, x);
-      // U rows for the backward: thread r holds value column r of every tile row
-      bf16* ub = a.u + ((int64_t)t.b * a.T + t.t0) * a.Hv * D + t.hv * D + r;
+      bf16* ub = a.u + grow0 * a.Hv * D + t.hv * D + r;
       const int nv = min(TR, t.Ls - t.p0);
+#pragma unroll 1
+      for (int g = 0; g < 4; ++g) {
+        tm_ld32(acc2, g, x);
+        sm_st32(sm + S::R3, r, g, x);
 #pragma unroll
-      for (int tt = 0; tt < TR; ++tt)
-        if (tt < nv) ub[(int64_t)tt * a.Hv * D] = __float2bfloat16(x[tt]);
+        for (int i = 0; i < 32; ++i)
+          if (32 * g + i < nv) ub[(int64_t)(32 * g + i) * a.Hv * D] = __float2bfloat16(x[i]);
+      }
     }
     tmem_wait_ld();
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    // ---- O^T += U^T P^T ---------------------------------------------------------------------------------
+    // ---- O^T += U^T P^T -----------------------------------------------------------------------------
     if (ok && r == 0) {
       tc_fence_after();
       if (MODE == NOISY) mma(acc1, KM(sbase + S::R3), KM(sbase + S::R2), 128, 128, true);
@@ -293,12 +306,19 @@ __global__ void __launch_bounds__(NT, 1) local_kernel(const __grid_constant__ CU
     ++mph;
     tc_fence_after();
     // ---- O: row r of acc1 is value column r; stage transposed in R0, then rows to global ------------
-    ld_row128(acc1, 0, x);
-    st_col(sm + S::R0, r, x);
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      tm_ld32(acc1, g, x);
+      sm_st_col32(sm + S::R0, r, g, x);
+    }
     __syncthreads();
     if (valid) {
-      ld_row_bf(sm + S::R0, r, x);
-      store_row_bf(a.o + ((int64_t)t.b * a.T + t.t0 + r) * (int64_t)(a.Hv * D) + t.hv * D, x, 1.f);
+      bf16* orow = a.o + (grow0 + r) * (int64_t)(a.Hv * D) + t.hv * D;
+#pragma unroll 1
+      for (int g = 0; g < 4; ++g) {
+        sm_ld32(sm + S::R0, r, g, x);
+        gm_st32(orow + 32 * g, x);
+      }
     }
   }
   tmem_wait_ld();
@@ -349,7 +369,6 @@ __global__ void __launch_bounds__(NT, 1) scan_kernel(const __grid_constant__ CUt
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t accS = tmem, accU = tmem + 128;
-  const uint32_t lane_off = (uint32_t)(32 * (r >> 5)) << 16;
   const uint32_t sbase = smem_addr(sm);
   auto stage = [&](int buf, int which) -> uint8_t* { return sm + S::STG + buf * S::STG_BYTES + which * S::STAGE_TILE; };
   auto issue = [&](int c) {
@@ -369,33 +388,30 @@ __global__ void __launch_bounds__(NT, 1) scan_kernel(const __grid_constant__ CUt
     issue(0);
     if (nch > 1) issue(1);
   }
-  {
-    uint32_t z[32];
+  float x[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) z[i] = 0u;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) tmem_st32(accS + lane_off + 32 * j, z);
-    tmem_wait_st();
-  }
+  for (int i = 0; i < 32; ++i) x[i] = 0.f;
+#pragma unroll 1
+  for (int g = 0; g < 4; ++g) tm_st32(accS, g, x);
+  tmem_wait_st();
   bool ok = true;
   uint32_t lph[2] = {0, 0}, mph = 0;
-  float x[128];
   const int64_t srow0 = ((int64_t)b * a.Hv + hv) * nch;
   for (int c = 0; c < nch && ok; ++c) {
     const int buf = c & 1;
     // the state entering chunk c: bf16 copy into SB and the checkpoint, then scaled by the chunk decay
     tc_fence_after();
-    ld_row128(accS, 0, x);
-    st_row(sm + S::SB, r, x);
-    store_row_bf(a.ckpt + ((srow0 + c) * D + r) * D, x, 1.f);
     {
       const float gam = a.gamma[srow0 + c];
+      bf16* ck = a.ckpt + ((srow0 + c) * D + r) * D;
+#pragma unroll 1
+      for (int g = 0; g < 4; ++g) {
+        tm_ld32(accS, g, x);
+        sm_st32(sm + S::SB, r, g, x);
+        gm_st32(ck + 32 * g, x);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(x[32 * j + i] * gam);
-        tmem_st32(accS + lane_off + 32 * j, v);
+        for (int i = 0; i < 32; ++i) x[i] *= gam;
+        tm_st32(accS, g, x);
       }
       tmem_wait_st();
     }
@@ -420,7 +436,7 @@ __global__ void __launch_bounds__(NT, 1) scan_kernel(const __grid_constant__ CUt
 #pragma unroll
     for (int j = 0; j < C / 16; ++j) {
       uint32_t v[16];
-      tmem_ld16(accU + lane_off + 16 * j, v);
+      tmem_ld16(accU + lane_base() + 16 * j, v);
       tmem_wait_ld();
 #pragma unroll
       for (int i = 0; i < 16; ++i) u[16 * j + i] = __uint_as_float(v[i]);
@@ -461,10 +477,14 @@ __global__ void __launch_bounds__(NT, 1) scan_kernel(const __grid_constant__ CUt
   }
   tc_fence_after();
   if (ok && a.final_state != nullptr) {
-    ld_row128(accS, 0, x);
     float* f = a.final_state + (((int64_t)b * a.Hv + hv) * D + r) * D;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      tm_ld32(accS, g, x);
 #pragma unroll
-    for (int i = 0; i < 128; i += 4) *reinterpret_cast<float4*>(f + i) = make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]);
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(f + 32 * g + i) = make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]);
+    }
   }
   tmem_wait_ld();
   tc_fence_before();

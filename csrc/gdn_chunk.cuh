@@ -124,6 +124,103 @@ __device__ __forceinline__ float ld_el(const uint8_t* tile, int r, int c) {
   return __bfloat162float(*reinterpret_cast<const bf16*>(tile + toff(r, c)));
 }
 
+// ---- 32-column groups -----------------------------------------------------------------------------
+// Row passes walk a 128-column row in groups of 32 columns with a rolled outer loop: the unrolled
+// inner body stays small (instruction cache) and 32 values live in registers instead of 128.
+__device__ __forceinline__ uint32_t lane_base() { return (uint32_t)(32 * (threadIdx.x >> 5)) << 16; }
+
+__device__ __forceinline__ void tm_ld32(uint32_t acc, int g, float (&x)[32]) {
+  uint32_t v[32];
+  tmem_ld32(acc + lane_base() + 32 * g, v);
+  tmem_wait_ld();
+#pragma unroll
+  for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(v[i]);
+}
+
+__device__ __forceinline__ void tm_st32(uint32_t acc, int g, const float (&x)[32]) {
+  uint32_t v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(x[i]);
+  tmem_st32(acc + lane_base() + 32 * g, v);
+}
+
+__device__ __forceinline__ void sm_st32(uint8_t* tile, int r, int g, const float (&x)[32], float sc = 1.f) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 v;
+    v.x = pack_bf2(x[8 * j] * sc, x[8 * j + 1] * sc);
+    v.y = pack_bf2(x[8 * j + 2] * sc, x[8 * j + 3] * sc);
+    v.z = pack_bf2(x[8 * j + 4] * sc, x[8 * j + 5] * sc);
+    v.w = pack_bf2(x[8 * j + 6] * sc, x[8 * j + 7] * sc);
+    *reinterpret_cast<uint4*>(tile + toff(r, 32 * g + 8 * j)) = v;
+  }
+}
+
+__device__ __forceinline__ void sm_zero32(uint8_t* tile, int r, int g) {
+  const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(tile + toff(r, 32 * g + 8 * j)) = z;
+}
+
+__device__ __forceinline__ void sm_ld32(const uint8_t* tile, int r, int g, float (&x)[32]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint4 v = *reinterpret_cast<const uint4*>(tile + toff(r, 32 * g + 8 * j));
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+      x[8 * j + 2 * i] = f.x;
+      x[8 * j + 2 * i + 1] = f.y;
+    }
+  }
+}
+
+__device__ __forceinline__ void gm_st32(bf16* dst, const float (&x)[32], float sc = 1.f) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 v;
+    v.x = pack_bf2(x[8 * j] * sc, x[8 * j + 1] * sc);
+    v.y = pack_bf2(x[8 * j + 2] * sc, x[8 * j + 3] * sc);
+    v.z = pack_bf2(x[8 * j + 4] * sc, x[8 * j + 5] * sc);
+    v.w = pack_bf2(x[8 * j + 6] * sc, x[8 * j + 7] * sc);
+    reinterpret_cast<uint4*>(dst)[j] = v;
+  }
+}
+
+// Transposed group store: rows 32g..32g+31 of tile column c.
+__device__ __forceinline__ void sm_st_col32(uint8_t* tile, int c, int g, const float (&x)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) *reinterpret_cast<bf16*>(tile + toff(32 * g + i, c)) = __float2bfloat16(x[i]);
+}
+
+// Sum of x[i] over the warp's 32 lanes for every i; lane l returns the sum for i = l (31 shuffles).
+__device__ __forceinline__ float warp_colsum32(float (&x)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int m = 16, n = 16; m >= 1; m >>= 1, n >>= 1) {
+    const bool hi = (lane & m) != 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (i < n) {
+        const float send = hi ? x[i] : x[n + i];
+        const float keep = hi ? x[n + i] : x[i];
+        x[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+      }
+    }
+  }
+  return x[0];
+}
+
+// Chunk-local C x C matrices are block diagonal in a 128-row tile: a row's nonzero columns lie in
+// its window of W = max(C, 32) columns (warp-uniform), i.e. groups [win_g0, win_g0 + W / 32).
+template <int C>
+struct Win {
+  static constexpr int W = C < 32 ? 32 : C;
+  static constexpr int NG = W / 32;
+  __device__ static int g0() { return ((int)threadIdx.x / W) * NG; }
+};
+
 // ---- arguments ------------------------------------------------------------------------------------
 struct Args {
   int B, T, Hk, Hv;

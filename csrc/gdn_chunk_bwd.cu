@@ -29,86 +29,6 @@ using namespace trida::sm100;
 
 constexpr int RED = 2 * D + 4;   // per (row, value head): dq | dk | dbeta | dg | pad
 
-// Column sums over the CTA's 128 threads of x[] (thread r holds row r): thread c gets column c.
-// Butterfly inside each warp (lane l ends with columns 4l..4l+3), then the 4 warps through smem.
-__device__ __forceinline__ float colsum128(float (&x)[128], float* red) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-#pragma unroll
-  for (int i = 0; i < 64; ++i) {
-    const bool hi = lane & 16;
-    const float send = hi ? x[i] : x[64 + i];
-    const float keep = hi ? x[64 + i] : x[i];
-    x[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-  }
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const bool hi = lane & 8;
-    const float send = hi ? x[i] : x[32 + i];
-    const float keep = hi ? x[32 + i] : x[i];
-    x[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const bool hi = lane & 4;
-    const float send = hi ? x[i] : x[16 + i];
-    const float keep = hi ? x[16 + i] : x[i];
-    x[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-  }
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const bool hi = lane & 2;
-    const float send = hi ? x[i] : x[8 + i];
-    const float keep = hi ? x[8 + i] : x[i];
-    x[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const bool hi = lane & 1;
-    const float send = hi ? x[i] : x[4 + i];
-    const float keep = hi ? x[4 + i] : x[i];
-    x[i] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) red[w * 128 + 4 * lane + i] = x[i];
-  __syncthreads();
-  const int c = threadIdx.x;
-  const float s = red[c] + red[128 + c] + red[256 + c] + red[384 + c];
-  __syncthreads();
-  return s;
-}
-
-__device__ __forceinline__ float dot_row_bf(const uint8_t* tile, int r, const float (&x)[128]) {
-  float s = 0.f;
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const uint4 v = *reinterpret_cast<const uint4*>(tile + toff(r, 8 * j));
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
-      s = fmaf(f.x, x[8 * j + 2 * i], s);
-      s = fmaf(f.y, x[8 * j + 2 * i + 1], s);
-    }
-  }
-  return s;
-}
-
-__device__ __forceinline__ float dot_gmem_bf(const bf16* p, const float (&x)[128]) {
-  float s = 0.f;
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const uint4 v = reinterpret_cast<const uint4*>(p)[j];
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
-      s = fmaf(f.x, x[8 * j + 2 * i], s);
-      s = fmaf(f.y, x[8 * j + 2 * i + 1], s);
-    }
-  }
-  return s;
-}
-
 // Stream geometry of the tile of blockIdx (stream index from blockIdx.z = b * nstreams + s).
 __device__ __forceinline__ TileGeo tile_geo(const Args& a) {
   TileGeo t;
@@ -167,7 +87,7 @@ struct BwdSmem {
   static constexpr int S0 = 0, S1 = TILE, S2 = 2 * TILE, S3 = 3 * TILE, S4 = 4 * TILE, S5 = 5 * TILE;
   static constexpr int META = 6 * TILE;
   static constexpr int RED = META + Meta::BYTES;        // colsum scratch [4][128] + dG [128] + misc
-  static constexpr int BARS = RED + (4 * 128 + 3 * 128) * 4;
+  static constexpr int BARS = RED + (4 * 128 + 3 * 128 + 8) * 4;
   static constexpr int TOTAL = BARS + 64;
 };
 
@@ -219,23 +139,31 @@ __global__ void __launch_bounds__(NT, 1) bwd0_kernel(const __grid_constant__ CUt
   WAIT_MMA(202);
   const int cs = (r / C) * C;
   const bool valid = t.p0 + r < t.Ls;
-  float x[128];
-  ld_row128(accP, 0, x);
+  using WN = Win<C>;
+  float x[32];
   {
     const float Gr = m.Gr[r];
     const int rd = m.rd[r], sg = m.seg[r];
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      if (g < WN::g0() || g >= WN::g0() + WN::NG) {
+        sm_zero32(sm + S::S3, r, g);
+        continue;
+      }
+      tm_ld32(accP, g, x);
 #pragma unroll
-    for (int s = 0; s < 128; ++s) {
-      const bool on = (s >= cs) && (s <= rd) && (m.seg[s] == sg) && valid;
-      x[s] = on ? x[s] * __expf(Gr - m.G[s]) : 0.f;
+      for (int i = 0; i < 32; ++i) {
+        const int s = 32 * g + i;
+        const bool on = (s >= cs) && (s <= rd) && (m.seg[s] == sg) && valid;
+        x[i] = on ? x[i] * __expf(Gr - m.G[s]) : 0.f;
+      }
+      sm_st32(sm + S::S3, r, g, x);
     }
   }
-  st_row(sm + S::S3, r, x);
   // zero dO rows past the stream (other streams' rows must not leak into dU)
   if (!valid) {
-    const uint4 z = make_uint4(0, 0, 0, 0);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) *reinterpret_cast<uint4*>(sm + S::S2 + toff(r, 8 * j)) = z;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) sm_zero32(sm + S::S2, r, g);
   }
   SYNC_FOR_MMA();
   // dU0^T[v][s] = sum_t dO[t][v] P[t][s]
@@ -246,17 +174,25 @@ __global__ void __launch_bounds__(NT, 1) bwd0_kernel(const __grid_constant__ CUt
   }
   // clean stream: the carry e^{Gr} q rows for the scan
   if (t.stream == 0 && valid) {
-    ld_row_bf(sm + S::S0, r, x);
-    store_row_bf(a.qg + (grow(a, t, r) * a.Hv + t.hv) * D, x, m.carry[r] * __expf(m.Gr[r]));
+    bf16* dst = a.qg + (grow(a, t, r) * a.Hv + t.hv) * D;
+    const float qs = m.carry[r] * __expf(m.Gr[r]);
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      sm_ld32(sm + S::S0, r, g, x);
+      gm_st32(dst + 32 * g, x, qs);
+    }
   }
   WAIT_MMA(203);
-  ld_row128(accU, 0, x);   // row r = value column r over the tile rows
   {
     bf16* dst = (t.stream == 0 ? a.du0 : a.du) + grow(a, t, 0) * a.Hv * D + t.hv * D + r;
     const int nv = min(TR, t.Ls - t.p0);
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      tm_ld32(accU, g, x);   // row r = value column r over the tile rows 32g..
 #pragma unroll
-    for (int s = 0; s < TR; ++s)
-      if (s < nv) dst[(int64_t)s * a.Hv * D] = __float2bfloat16(x[s]);
+      for (int i = 0; i < 32; ++i)
+        if (32 * g + i < nv) dst[(int64_t)(32 * g + i) * a.Hv * D] = __float2bfloat16(x[i]);
+    }
   }
   tmem_wait_ld();
   tc_fence_before();
@@ -352,9 +288,15 @@ __global__ void __launch_bounds__(NT, 1) ds0_kernel(const __grid_constant__ CUte
     ok = __syncthreads_and(ok) != 0;
     if (!ok) break;
   }
-  float x[128];
-  ld_row128(acc, 0, x);
-  store_row_bf(a.ds0 + ((((int64_t)b * a.Hv + hv) * a.nch + c) * D + r) * D, x, ok ? 1.f : 0.f);
+  {
+    float x[32];
+    bf16* dst = a.ds0 + ((((int64_t)b * a.Hv + hv) * a.nch + c) * D + r) * D;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      tm_ld32(acc, g, x);
+      gm_st32(dst + 32 * g, x, ok ? 1.f : 0.f);
+    }
+  }
   tmem_wait_ld();
   tc_fence_before();
   __syncthreads();
@@ -432,17 +374,14 @@ __global__ void __launch_bounds__(NT, 1) scanb_kernel(const __grid_constant__ CU
     issue(nch - 1);
     if (S::NST == 2 && nch > 1) issue(nch - 2);
   }
-  {
-    uint32_t z[32];
+  float x[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) z[i] = 0u;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) tmem_st32(accS + lane_off + 32 * j, z);
-    tmem_wait_st();
-  }
+  for (int i = 0; i < 32; ++i) x[i] = 0.f;
+#pragma unroll 1
+  for (int g = 0; g < 4; ++g) tm_st32(accS, g, x);
+  tmem_wait_st();
   bool ok = true;
   uint32_t lph[2] = {0, 0}, mph = 0;
-  float x[128];
   for (int c = nch - 1; c >= 0 && ok; --c) {
     const int buf = S::NST == 1 ? 0 : (c & 1);
     ok = mbar_wait(&ld_bar[buf], lph[buf] & 1, a.err, 221);
@@ -451,25 +390,19 @@ __global__ void __launch_bounds__(NT, 1) scanb_kernel(const __grid_constant__ CU
     if (!ok) break;
     // dS1 of chunk c: bf16 into SB and the checkpoint; then dS <- gamma dS + noisy(c)
     tc_fence_after();
-    ld_row128(accS, 0, x);
-    st_row(sm + S::SB, r, x);
-    store_row_bf(a.dckpt + ((srow0 + c) * D + r) * D, x, 1.f);
     {
       const float gam = a.gamma[srow0 + c];
+      bf16* ck = a.dckpt + ((srow0 + c) * D + r) * D;
+      float y[32];
+#pragma unroll 1
+      for (int g = 0; g < 4; ++g) {
+        tm_ld32(accS, g, x);
+        sm_st32(sm + S::SB, r, g, x);
+        gm_st32(ck + 32 * g, x);
+        if (NOISY) sm_ld32(stage(c, 5), r, g, y);
 #pragma unroll
-      for (int i = 0; i < 128; ++i) x[i] *= gam;
-      if (NOISY) {
-        float y[128];
-        ld_row_bf(stage(c, 5), r, y);
-#pragma unroll
-        for (int i = 0; i < 128; ++i) x[i] += y[i];
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(x[32 * j + i]);
-        tmem_st32(accS + lane_off + 32 * j, v);
+        for (int i = 0; i < 32; ++i) x[i] = x[i] * gam + (NOISY ? y[i] : 0.f);
+        tm_st32(accS, g, x);
       }
       tmem_wait_st();
     }
@@ -539,21 +472,37 @@ __global__ void __launch_bounds__(NT, 1) scanb_kernel(const __grid_constant__ CU
   if (r < 32) tmem_dealloc(tmem, 256);
 }
 
-// Decay gradient of a pair term: thread t holds X[t][s] = dZ_ts Z_ts (fp32, zero outside its
-// chunk's mask) of a factor Z_ts proportional to exp(G_lim(t) - G_s).  Since G_lim(t) - G_s is the
-// sum of g_j over s < j <= lim(t), thread j receives sum_{t : lim(t) >= j} sum_{s < j} X[t][s]:
-// each pair enters once, so nothing cancels (the row-sum-minus-column-sum form would subtract two
-// large, differently rounded terms).
-__device__ __forceinline__ float pair_decay_grad(float (&x)[128], int lim, float* red) {
+// Decay gradient of pair terms.  A factor Z_ts proportional to exp(G_lim(t) - G_s) contains g_j
+// for s < j <= lim(t), so the decay gradient of position j is sum_{t : lim(t) >= j} sum_{s < j}
+// dZ_ts Z_ts: each pair enters once and nothing cancels (the equivalent row-sum-minus-column-sum
+// form subtracts two large, differently rounded terms).  Pair terms are block diagonal, so a row's
+// pairs lie in its window; thread t walks its window groups with a running prefix over s and the
+// masked prefixes are summed over the rows of the window: inside the warp by warp_colsum32, across
+// the window's warps (C = 64) through red[warp][column].
+template <int C>
+struct PairSum {
   float run = 0.f;
+  // x: dZ . Z for columns 32g.. of this row; lim: the row's last position whose decay it carries
+  __device__ void group(float (&x)[32], int g, int lim, float* red) {
 #pragma unroll
-  for (int j = 0; j < 128; ++j) {
-    const float v = x[j];
-    x[j] = (lim >= j) ? run : 0.f;
-    run += v;
+    for (int i = 0; i < 32; ++i) {
+      const float v = x[i];
+      x[i] = (lim >= 32 * g + i) ? run : 0.f;
+      run += v;
+    }
+    const float cs = warp_colsum32(x);
+    red[(threadIdx.x >> 5) * 128 + 32 * g + (threadIdx.x & 31)] = cs;
   }
-  return colsum128(x, red);
-}
+  // after a CTA barrier: thread j's total over the warps of its window
+  __device__ static float total(const float* red) {
+    using WN = Win<C>;
+    const int j = threadIdx.x, w0 = (j / WN::W) * (WN::W / 32);
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < WN::W / 32; ++w) s += red[(w0 + w) * 128 + j];
+    return s;
+  }
+};
 
 // ---- bwd1: T, dPE, dQ, dW, dT, dA and the pair / read-out parts of dg ------------------------------
 template <int C>
@@ -567,6 +516,7 @@ __global__ void __launch_bounds__(NT, 1) bwd1_kernel(const __grid_constant__ CUt
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   using S = BwdSmem;
+  using WN = Win<C>;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::BARS);
   uint64_t* ld_bar = bars;
   uint64_t* mma_bar = bars + 1;
@@ -604,14 +554,14 @@ __global__ void __launch_bounds__(NT, 1) bwd1_kernel(const __grid_constant__ CUt
   WAIT_LD(231);
   const bool valid = t.p0 + r < t.Ls;
   const int cs = (r / C) * C;
+  const int64_t grow0 = grow(a, t, 0);
   if (!valid) {
     // rows past the stream: no gradient flows in, and other streams' rows must not leak
-    const uint4 z = make_uint4(0, 0, 0, 0);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      *reinterpret_cast<uint4*>(sm + S::S1 + toff(r, 8 * j)) = z;
-      *reinterpret_cast<uint4*>(sm + S::S2 + toff(r, 8 * j)) = z;
-      *reinterpret_cast<uint4*>(sm + S::S3 + toff(r, 8 * j)) = z;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      sm_zero32(sm + S::S1, r, g);
+      sm_zero32(sm + S::S2, r, g);
+      sm_zero32(sm + S::S3, r, g);
     }
   }
   SYNC_FOR_MMA();
@@ -623,18 +573,20 @@ __global__ void __launch_bounds__(NT, 1) bwd1_kernel(const __grid_constant__ CUt
     umma_commit(mma_bar);
   }
   WAIT_MMA(232);
-  float x[128];
+  float x[32], y[32];
   // A blocks (fp32, see af_idx) -> T (over Q, whose MMA is done)
   {
     float* Af = reinterpret_cast<float*>(sm + S::S4);
-    ld_row128(acc0, 0, x);
     const float Gt = m.G[r], bt = m.beta[r];
     const int sg = m.seg[r];
+#pragma unroll 1
+    for (int g = WN::g0(); g < WN::g0() + WN::NG; ++g) {
+      tm_ld32(acc0, g, x);
 #pragma unroll
-    for (int s = 0; s < 128; ++s) {
-      if (s >= cs && s < cs + C) {
-        const float v = (s < r && m.seg[s] == sg) ? bt * x[s] * __expf(Gt - m.G[s]) : 0.f;
-        Af[af_idx(r, s - cs)] = v;
+      for (int i = 0; i < 32; ++i) {
+        const int s = 32 * g + i;
+        if (s >= cs && s < cs + C)
+          Af[af_idx(r, s - cs)] = (s < r && m.seg[s] == sg) ? bt * x[i] * __expf(Gt - m.G[s]) : 0.f;
       }
     }
   }
@@ -642,35 +594,53 @@ __global__ void __launch_bounds__(NT, 1) bwd1_kernel(const __grid_constant__ CUt
   invert_column<C>(reinterpret_cast<const float*>(sm + S::S4), sm + S::S5);
   __syncthreads();
   if (valid) {
-    ld_row_bf(sm + S::S5, r, x);
-    store_row_bf(a.tt + (grow(a, t, r) * a.Hv + t.hv) * D, x, 1.f);
+    bf16* dst = a.tt + ((grow0 + r) * a.Hv + t.hv) * D;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      sm_ld32(sm + S::S5, r, g, x);
+      gm_st32(dst + 32 * g, x);
+    }
   }
   // dPE = dP . mask . e^{Gr_t - G_s} (tile + rows for bwd2); pair term dP . P of the decay gradient
   float dg = 0.f;
   {
-    float qk[128];
-    ld_row128(acc1, 0, x);
-    ld_row128(acc3, 0, qk);
     const float Gr = m.Gr[r];
     const int rd = m.rd[r], sg = m.seg[r];
+    bf16* dst = a.dpe + ((grow0 + r) * a.Hv + t.hv) * D;
+    PairSum<C> ps;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      if (g < WN::g0() || g >= WN::g0() + WN::NG) {
+        sm_zero32(sm + S::S4, r, g);
 #pragma unroll
-    for (int s = 0; s < 128; ++s) {
-      const bool on = (s >= cs) && (s <= rd) && (m.seg[s] == sg) && valid;
-      const float e = on ? __expf(Gr - m.G[s]) : 0.f;
-      x[s] = x[s] * e;              // dPE
-      qk[s] = x[s] * qk[s];         // dP . P
+        for (int i = 0; i < 32; ++i) x[i] = 0.f;
+        if (valid) gm_st32(dst + 32 * g, x);
+        continue;
+      }
+      tm_ld32(acc1, g, x);
+      tm_ld32(acc3, g, y);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int s = 32 * g + i;
+        const bool on = (s >= cs) && (s <= rd) && (m.seg[s] == sg) && valid;
+        x[i] = on ? x[i] * __expf(Gr - m.G[s]) : 0.f;    // dPE
+        y[i] = x[i] * y[i];                              // dP . P
+      }
+      sm_st32(sm + S::S4, r, g, x);
+      if (valid) gm_st32(dst + 32 * g, x);
+      ps.group(y, g, valid ? rd : -1, red);
     }
-    st_row(sm + S::S4, r, x);
-    if (valid) store_row_bf(a.dpe + (grow(a, t, r) * a.Hv + t.hv) * D, x, 1.f);
-    dg += pair_decay_grad(qk, valid ? rd : -1, red);
+    __syncthreads();
+    dg += PairSum<C>::total(red);
   }
   // dOg = carry e^{Gr} dO in place
   {
-    ld_row_bf(sm + S::S1, r, x);
     const float qs = m.carry[r] * __expf(m.Gr[r]);
-#pragma unroll
-    for (int i = 0; i < 128; ++i) x[i] *= qs;
-    st_row(sm + S::S1, r, x);
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      sm_ld32(sm + S::S1, r, g, x);
+      sm_st32(sm + S::S1, r, g, x, qs);
+    }
   }
   SYNC_FOR_MMA();
   // dQ^T intra (acc2) = K^T dPE^T; per chunk: dQ^T inter (acc1) = S0 dOg^T, -dW^T (acc3) = S0 dU^T
@@ -699,43 +669,49 @@ __global__ void __launch_bounds__(NT, 1) bwd1_kernel(const __grid_constant__ CUt
   lph += NCK;
   WAIT_MMA(235);
   // dq rows = intra + inter (lanes k: transposed, coalesced per row); read-out decay term of the
-  // state part: inter_t = q_t . dq_inter_t (a column dot over k)
+  // state part: inter_t = q_t . dq_inter_t (a column dot over the 128 threads k)
   {
-    float y[128];
-    ld_row128(acc1, 0, x);        // inter
-    ld_row128(acc2, 0, y);        // intra
     const int nv = min(TR, t.Ls - t.p0);
-    float* dst = a.dpart + grow(a, t, 0) * a.Hv * RED + t.hv * RED + r;
-    const bf16* qcol = a.qk_rows + ((grow(a, t, 0) * a.Hk + t.hk) * 2) * D + r;   // q[t][k = r]
+    float* dst = a.dpart + grow0 * a.Hv * RED + t.hv * RED + r;
+    const bf16* qcol = a.qk_rows + ((grow0 * a.Hk + t.hk) * 2) * D + r;   // q[t][k = r]
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      tm_ld32(acc1, g, x);        // inter
+      tm_ld32(acc2, g, y);        // intra
 #pragma unroll
-    for (int s = 0; s < TR; ++s) {
-      float qv = 0.f;
-      if (s < nv) {
-        dst[(int64_t)s * a.Hv * RED] = x[s] + y[s];
-        qv = __bfloat162float(qcol[(int64_t)s * a.Hk * 2 * D]);
+      for (int i = 0; i < 32; ++i) {
+        const int s = 32 * g + i;
+        float qv = 0.f;
+        if (s < nv) {
+          dst[(int64_t)s * a.Hv * RED] = x[i] + y[i];
+          qv = __bfloat162float(qcol[(int64_t)s * a.Hk * 2 * D]);
+        }
+        x[i] *= qv;
       }
-      y[s] = x[s] * qv;
+      red[(r >> 5) * 128 + 32 * g + (r & 31)] = warp_colsum32(x);
     }
-    inter[r] = colsum128(y, red);
-  }
-  __syncthreads();
-  {
+    __syncthreads();
+    inter[r] = red[r] + red[128 + r] + red[256 + r] + red[384 + r];
+    __syncthreads();
     // dg_j += sum of inter_t over rows t of j's segment that read out at or after j
     const int sg = m.seg[r];
     for (int tt = cs; tt < cs + C; ++tt)
       if (m.seg[tt] == sg && m.rd[tt] >= r) dg += inter[tt];
   }
   // dW^T (negated) into S2 as [k][t]; dW rows to global
-  ld_row128(acc3, 0, x);
-#pragma unroll
-  for (int i = 0; i < 128; ++i) x[i] = -x[i];
-  st_row(sm + S::S2, r, x);
   {
-    bf16* dst = a.dw + grow(a, t, 0) * a.Hv * D + t.hv * D + r;
+    bf16* dst = a.dw + grow0 * a.Hv * D + t.hv * D + r;
     const int nv = min(TR, t.Ls - t.p0);
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      tm_ld32(acc3, g, x);
 #pragma unroll
-    for (int s = 0; s < TR; ++s)
-      if (s < nv) dst[(int64_t)s * a.Hv * D] = __float2bfloat16(x[s]);
+      for (int i = 0; i < 32; ++i) x[i] = -x[i];
+      sm_st32(sm + S::S2, r, g, x);
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (32 * g + i < nv) dst[(int64_t)(32 * g + i) * a.Hv * D] = __float2bfloat16(x[i]);
+    }
   }
   SYNC_FOR_MMA();
   // V into S1 (dOg is dead)
@@ -744,7 +720,7 @@ __global__ void __launch_bounds__(NT, 1) bwd1_kernel(const __grid_constant__ CUt
     load_cols(sm + S::S1, &tm_v, ld_bar, v_col0 + t.hv * D, t.t0, t.b);
   }
   WAIT_LD(236);
-  // dT: acc1 = dU V^T, acc2 = dW K^T  ->  dT_ts = beta_s (acc1 + carry_s e^{G_s} acc2)
+  // dT: acc1 = dU V^T, acc2 = dW K^T  ->  dT_ts = beta_s (acc1 + carry_s e^{G_s} acc2), block diagonal
   if (ok && r == 0) {
     tc_fence_after();
     mma(acc1, KM(sbase + S::S3), KM(sbase + S::S1), 128, 128, false);
@@ -752,27 +728,39 @@ __global__ void __launch_bounds__(NT, 1) bwd1_kernel(const __grid_constant__ CUt
     umma_commit(mma_bar);
   }
   WAIT_MMA(237);
-  {
-    float y[128];
-    ld_row128(acc1, 0, x);
-    ld_row128(acc2, 0, y);
-#pragma unroll
-    for (int s = 0; s < 128; ++s) {
-      const bool on = (s >= cs) && (s < cs + C);
-      x[s] = on ? m.beta[s] * (x[s] + m.carry[s] * __expf(m.G[s]) * y[s]) : 0.f;
+#pragma unroll 1
+  for (int g = 0; g < 4; ++g) {
+    if (g < WN::g0() || g >= WN::g0() + WN::NG) {
+      sm_zero32(sm + S::S4, r, g);    // dPE is dead (dQ done, rows saved)
+      continue;
     }
+    tm_ld32(acc1, g, x);
+    tm_ld32(acc2, g, y);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int s = 32 * g + i;
+      const bool on = (s >= cs) && (s < cs + C);
+      x[i] = on ? m.beta[s] * (x[i] + m.carry[s] * __expf(m.G[s]) * y[i]) : 0.f;
+    }
+    sm_st32(sm + S::S4, r, g, x);
   }
-  st_row(sm + S::S4, r, x);   // dPE is dead (dQ done, rows saved)
   SYNC_FOR_MMA();
-  // Y = T^T dT (acc1)
+  // Y = T^T dT (acc1), block diagonal
   if (ok && r == 0) {
     tc_fence_after();
     mma(acc1, MN(sbase + S::S5), MN(sbase + S::S4), 128, 128, false);
     umma_commit(mma_bar);
   }
   WAIT_MMA(238);
-  ld_row128(acc1, 0, x);
-  st_row(sm + S::S1, r, x);   // V is dead
+#pragma unroll 1
+  for (int g = 0; g < 4; ++g) {
+    if (g < WN::g0() || g >= WN::g0() + WN::NG) {
+      sm_zero32(sm + S::S1, r, g);    // V is dead
+      continue;
+    }
+    tm_ld32(acc1, g, x);
+    sm_st32(sm + S::S1, r, g, x);
+  }
   SYNC_FOR_MMA();
   // -dA = Y T^T (acc2)
   if (ok && r == 0) {
@@ -782,26 +770,39 @@ __global__ void __launch_bounds__(NT, 1) bwd1_kernel(const __grid_constant__ CUt
   }
   WAIT_MMA(239);
   {
-    float kk[128];
-    ld_row128(acc2, 0, x);
-    ld_row128(acc0, 0, kk);
     const float Gt = m.G[r], bt = m.beta[r];
     const int sg = m.seg[r];
     float sa = 0.f;
+    bf16* dst = a.dae + ((grow0 + r) * a.Hv + t.hv) * D;
+    PairSum<C> ps;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      if (g < WN::g0() || g >= WN::g0() + WN::NG) {
 #pragma unroll
-    for (int s = 0; s < 128; ++s) {
-      const bool on = (s >= cs) && (s < r) && (m.seg[s] == sg) && valid;
-      const float e = on ? __expf(Gt - m.G[s]) : 0.f;
-      const float da = on ? -x[s] : 0.f;
-      const float ke = kk[s] * e;
-      sa = fmaf(da, ke, sa);                    // d beta_t (A part)
-      kk[s] = da * bt * ke;                     // dA . A (pair term of the decay gradient)
-      x[s] = da * bt * e;                       // dAE
+        for (int i = 0; i < 32; ++i) x[i] = 0.f;
+        if (valid) gm_st32(dst + 32 * g, x);
+        continue;
+      }
+      tm_ld32(acc2, g, x);
+      tm_ld32(acc0, g, y);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int s = 32 * g + i;
+        const bool on = (s >= cs) && (s < r) && (m.seg[s] == sg) && valid;
+        const float e = on ? __expf(Gt - m.G[s]) : 0.f;
+        const float da = on ? -x[i] : 0.f;
+        const float ke = y[i] * e;
+        sa = fmaf(da, ke, sa);                    // d beta_t (A part)
+        y[i] = da * bt * ke;                      // dA . A (pair term of the decay gradient)
+        x[i] = da * bt * e;                       // dAE
+      }
+      if (valid) gm_st32(dst + 32 * g, x);
+      ps.group(y, g, valid ? r : -1, red);
     }
-    if (valid) store_row_bf(a.dae + (grow(a, t, r) * a.Hv + t.hv) * D, x, 1.f);
-    dg += pair_decay_grad(kk, valid ? r : -1, red);
+    __syncthreads();
+    dg += PairSum<C>::total(red);
     if (valid) {
-      float* scp = a.sc + (grow(a, t, r) * a.Hv + t.hv) * 2;
+      float* scp = a.sc + ((grow0 + r) * a.Hv + t.hv) * 2;
       scp[0] = sa;
       scp[1] = dg;
     }
@@ -835,8 +836,8 @@ __global__ void __launch_bounds__(NT, 1) bwd2_kernel(const __grid_constant__ CUt
   const Meta m = carve_meta(sm + S::META);
   float* red = reinterpret_cast<float*>(sm + S::RED);
   float* kb = red + 4 * 128;     // [128] dKb_t . Kb_t
-  float* ksx = kb + 128;         // [128] k_s . (kts_s dS1 u_s) (clean stream)  (aliases the misc area)
-  float* misc = red;             // warp partial sums (the colsum scratch is idle then)
+  float* ksx = kb + 128;         // [128] k_s . (kts_s dS1 u_s) (clean stream)
+  float* misc = ksx + 128;       // [4] warp partial sums
   const int r = threadIdx.x;
   const TileGeo t = tile_geo(a);
   constexpr int NCK = TR / C;
@@ -850,7 +851,7 @@ __global__ void __launch_bounds__(NT, 1) bwd2_kernel(const __grid_constant__ CUt
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t acc0 = tmem, acc1 = tmem + 128, acc2 = tmem + 256, acc3 = tmem + 384;
+  const uint32_t acc0 = tmem, acc1 = tmem + 128, acc2 = tmem + 256;
   const uint32_t sbase = smem_addr(sm);
   uint32_t mph = 0, lph = 0;
   bool ok = true;
@@ -865,7 +866,7 @@ __global__ void __launch_bounds__(NT, 1) bwd2_kernel(const __grid_constant__ CUt
   tile_meta<C>(a, t, m);
   const bool valid = t.p0 + r < t.Ls;
   const int cs = (r / C) * C;
-  const int64_t row = grow(a, t, r);
+  const int64_t row = grow(a, t, r), grow0 = grow(a, t, 0);
   float dbeta = 0.f, dg = 0.f;
   if (valid) {
     const float2 s1 = *reinterpret_cast<const float2*>(a.sc + (row * a.Hv + t.hv) * 2);
@@ -875,12 +876,11 @@ __global__ void __launch_bounds__(NT, 1) bwd2_kernel(const __grid_constant__ CUt
   ksx[r] = 0.f;
   WAIT_LD(241);
   if (!valid) {
-    const uint4 z = make_uint4(0, 0, 0, 0);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      *reinterpret_cast<uint4*>(sm + S::S1 + toff(r, 8 * j)) = z;
-      *reinterpret_cast<uint4*>(sm + S::S2 + toff(r, 8 * j)) = z;
-      *reinterpret_cast<uint4*>(sm + S::S3 + toff(r, 8 * j)) = z;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      sm_zero32(sm + S::S1, r, g);
+      sm_zero32(sm + S::S2, r, g);
+      sm_zero32(sm + S::S3, r, g);
     }
   }
   SYNC_FOR_MMA();
@@ -898,53 +898,70 @@ __global__ void __launch_bounds__(NT, 1) bwd2_kernel(const __grid_constant__ CUt
     load_rows(sm + S::S2, &tm_dpe, ld_bar, t.hv, t.t0, t.b);
     load_rows(sm + S::S3, &tm_dae, ld_bar, t.hv, t.t0, t.b);
   }
-  float x[128];
-  float ks = 0.f;
+  float x[32], y[32];
+  const float ce = m.carry[r] * __expf(m.G[r]);
+  const float ks = m.beta[r] * ce;
   // dV and the value part of d beta; the Kb parts of d beta and dg
-  ld_row128(acc0, 0, x);
-  if (valid) {
-    const bf16* vrow = a.mixed + row * a.ldm + v_col0 + t.hv * D;
-    dbeta += dot_gmem_bf(vrow, x);
-    store_row_bf(a.dv + row * a.lddv + t.hv * D, x, m.beta[r]);
-  }
-  ld_row128(acc1, 0, x);
   {
-    const float kd = dot_row_bf(sm + S::S0, r, x);
-    const float ce = m.carry[r] * __expf(m.G[r]);
-    ks = m.beta[r] * ce;
+    const bf16* vrow = a.mixed + row * a.ldm + v_col0 + t.hv * D;
+    bf16* dvrow = a.dv + row * a.lddv + t.hv * D;
+    float kd = 0.f;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      tm_ld32(acc0, g, x);
+      if (valid) {
+        gm_st32(dvrow + 32 * g, x, m.beta[r]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint4 v = reinterpret_cast<const uint4*>(vrow + 32 * g)[j];
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+            dbeta = fmaf(f.x, x[8 * j + 2 * i], dbeta);
+            dbeta = fmaf(f.y, x[8 * j + 2 * i + 1], dbeta);
+          }
+        }
+      }
+      tm_ld32(acc1, g, x);
+      sm_ld32(sm + S::S0, r, g, y);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) kd = fmaf(x[i], y[i], kd);
+    }
     dbeta += ce * kd;
     kb[r] = valid ? ks * kd : 0.f;
   }
   WAIT_LD(243);
   if (!valid) {
-    const uint4 z = make_uint4(0, 0, 0, 0);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      *reinterpret_cast<uint4*>(sm + S::S2 + toff(r, 8 * j)) = z;
-      *reinterpret_cast<uint4*>(sm + S::S3 + toff(r, 8 * j)) = z;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      sm_zero32(sm + S::S2, r, g);
+      sm_zero32(sm + S::S3, r, g);
     }
   }
   SYNC_FOR_MMA();
   if (ok && r == 0) {
     tc_fence_after();
-    // column parts (lanes s): dPE^T Q + dAE^T K;  row part: dAE K
+    // dK (lanes s): dPE^T Q + dAE^T K (column parts) + dAE K (row part)
     mma(acc2, MN(sbase + S::S2), MN(sbase + S::S1), 128, 128, false);
     mma(acc2, MN(sbase + S::S3), MN(sbase + S::S0), 128, 128, true);
     mma(acc2, KM(sbase + S::S3), MN(sbase + S::S0), 128, 128, true);
     umma_commit(mma_bar);
   }
   WAIT_MMA(244);
-  ld_row128(acc2, 0, x);
   {
-    float y[128];
-    ld_row128(acc1, 0, y);
-#pragma unroll
-    for (int i = 0; i < 128; ++i) x[i] += ks * y[i];
-  }
-  if (valid) {
     float* dst = a.dpart + (row * a.Hv + t.hv) * RED + D;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      tm_ld32(acc2, g, x);
+      tm_ld32(acc1, g, y);
+      if (valid) {
 #pragma unroll
-    for (int i = 0; i < 128; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]);
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4*>(dst + 32 * g + i) =
+              make_float4(x[i] + ks * y[i], x[i + 1] + ks * y[i + 1], x[i + 2] + ks * y[i + 2], x[i + 3] + ks * y[i + 3]);
+      }
+    }
   }
   // end-state term of the clean chunks: dK_s += kts_s dS1 u_s; decay parts from k_s . (kts_s dS1 u_s)
   // and gamma <S0, dS1>
@@ -957,11 +974,12 @@ __global__ void __launch_bounds__(NT, 1) bwd2_kernel(const __grid_constant__ CUt
     }
     WAIT_LD(245);
     {
-      ld_row_bf(sm + S::S1, r, x);
       const float kt = valid ? m.kts[r] : 0.f;
-#pragma unroll
-      for (int i = 0; i < 128; ++i) x[i] *= kt;
-      st_row(sm + S::S1, r, x);
+#pragma unroll 1
+      for (int g = 0; g < 4; ++g) {
+        sm_ld32(sm + S::S1, r, g, x);
+        sm_st32(sm + S::S1, r, g, x, kt);
+      }
     }
     SYNC_FOR_MMA();
     const int64_t sb = ((int64_t)t.b * a.Hv + t.hv) * a.nch;
@@ -981,9 +999,14 @@ __global__ void __launch_bounds__(NT, 1) bwd2_kernel(const __grid_constant__ CUt
         umma_commit(mma_bar);
       }
       {
-        float srow[128];
-        ld_row_bf(sm + S::S3, r, srow);
-        float d = dot_row_bf(sm + S::S2, r, srow);
+        float d = 0.f;
+#pragma unroll 1
+        for (int g = 0; g < 4; ++g) {
+          sm_ld32(sm + S::S3, r, g, x);
+          sm_ld32(sm + S::S2, r, g, y);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) d = fmaf(x[i], y[i], d);
+        }
         d = warp_sum(d);
         if ((r & 31) == 0) misc[r >> 5] = d;
       }
@@ -992,21 +1015,26 @@ __global__ void __launch_bounds__(NT, 1) bwd2_kernel(const __grid_constant__ CUt
       if (r / C == c && real) gsd = a.gamma[sb + blk] * (misc[0] + misc[1] + misc[2] + misc[3]);
       SYNC_FOR_MMA();   // S2 / S3 are reloaded next chunk; misc is rewritten
     }
-    // X^T[k][s] (lanes k): column dots with K give ksx_s = k_s . (kts_s dS1 u_s)
-    ld_row128(acc0, 0, x);
+    // X^T[k][s] (lanes k): ksx_s = sum_k X^T[k][s] K[s][k]; dk rows += X^T (transposed)
     {
-      float y[128];
-#pragma unroll
-      for (int s = 0; s < 128; ++s) y[s] = x[s] * ld_el(sm + S::S0, s, r);
-      ksx[r] = colsum128(y, red);
-    }
-    __syncthreads();   // every dk row above is written
-    {
-      float* dst = a.dpart + grow(a, t, 0) * a.Hv * RED + t.hv * RED + D + r;
+      float* dst = a.dpart + grow0 * a.Hv * RED + t.hv * RED + D + r;
       const int nv = min(TR, t.Ls - t.p0);
+#pragma unroll 1
+      for (int g = 0; g < 4; ++g) {
+        tm_ld32(acc0, g, x);
 #pragma unroll
-      for (int s = 0; s < TR; ++s)
-        if (s < nv) dst[(int64_t)s * a.Hv * RED] += x[s];
+        for (int i = 0; i < 32; ++i) y[i] = x[i] * ld_el(sm + S::S0, 32 * g + i, r);
+        red[(r >> 5) * 128 + 32 * g + (r & 31)] = warp_colsum32(y);
+      }
+      __syncthreads();   // every dk row above is written (and the partial sums)
+      ksx[r] = red[r] + red[128 + r] + red[256 + r] + red[384 + r];
+#pragma unroll 1
+      for (int g = 0; g < 4; ++g) {
+        tm_ld32(acc0, g, x);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (32 * g + i < nv) dst[(int64_t)(32 * g + i) * a.Hv * RED] += x[i];
+      }
     }
   }
   __syncthreads();

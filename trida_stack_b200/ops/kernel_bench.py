@@ -2,7 +2,9 @@
 
     python -m trida_stack_b200.ops.kernel_bench --op gemm [--m 24576 --n 6144 --k 2560 --layout tn]
     python -m trida_stack_b200.ops.kernel_bench --op attn_fwd|attn_bwd [--rows 4]
-    python -m trida_stack_b200.ops.kernel_bench --op gdn_fwd|gdn_bwd [--length 3072]
+    python -m trida_stack_b200.ops.kernel_bench --op gdn_fwd|gdn_bwd [--length 3072] [--gdn-path chunk|scan]
+                                                     [--gdn-layout two_stream|causal]
+    python -m trida_stack_b200.ops.kernel_bench --op gdn_core_fwd|gdn_core_bwd [--length 3072]
     python -m trida_stack_b200.ops.kernel_bench --op canvas_attn|canvas_gdn [--requests 64 --blk 7]
     python -m trida_stack_b200.ops.kernel_bench --op rmsnorm_fwd|rmsnorm_bwd|qk_rope_fwd|qk_rope_bwd|
                                                      swiglu_fwd|swiglu_bwd [--m 24576 --hidden 2560]
@@ -131,9 +133,14 @@ def bench_gdn(a, backward):
                 p.copy_(torch.log(torch.empty_like(p, dtype=torch.float32).uniform_(1, 16)))
             else:
                 p.fill_(1.0)
-    L, V = a.length, 2
-    T = (1 + V) * L
-    actx = SimpleNamespace(B=1, T=T, linear=LinearLayout("two_stream", L=L, V=V, bd=32))
+    os.environ["TRIDA_GDN"] = a.gdn_path
+    if a.layout_gdn == "causal":
+        T = a.length
+        actx = SimpleNamespace(B=1, T=T, linear=LinearLayout("causal"))
+    else:
+        L, V = a.length, 2
+        T = (1 + V) * L
+        actx = SimpleNamespace(B=1, T=T, linear=LinearLayout("two_stream", L=L, V=V, bd=32))
     x = torch.randn(T, 2560, device="cuda", dtype=torch.bfloat16, requires_grad=backward)
     if not backward:
         with torch.no_grad():
@@ -143,7 +150,47 @@ def bench_gdn(a, backward):
         ms = _time(lambda: gdn_block_cuda(x, lay, actx, cfg).backward(dy), a.warmup, a.iters)
     # recurrence FLOPs per token and value head: 3 (dk x dv) multiply-adds forward
     flops = T * 32 * 3 * 2 * 128 * 128 * (3 if backward else 1)
-    return ms, {"recurrence_tflops": flops / ms / 1e9}, None, None
+    return ms, {"recurrence_tflops": flops / ms / 1e9, "path": a.gdn_path, "layout": a.layout_gdn,
+                "tokens": T}, None, None
+
+
+def bench_gdn_core(a, backward):
+    """The gated-delta core alone (chunk kernels: prep, local, scan, ...) on config-3 shapes: 16 key
+    / 32 value heads of 128, a [x0 ; xt_1 ; xt_2] row of streams of ``--length`` (two-stream, block
+    32) or one causal row."""
+    from types import SimpleNamespace
+
+    from ._ext import ext
+    from .blocks import device_error_word
+    from .gdn import LinearLayout
+    from .gdn_cuda import chunk_forward
+    Hk, Hv, D = 16, 32, 128
+    if a.layout_gdn == "causal":
+        T, lay = a.length, LinearLayout("causal")
+    else:
+        T, lay = 3 * a.length, LinearLayout("two_stream", L=a.length, V=2, bd=32)
+    dev = "cuda"
+    mixed = torch.randn(T, 2 * Hk * D + Hv * D, device=dev, dtype=torch.bfloat16)
+    gates = torch.randn(T, 2 * Hv, device=dev, dtype=torch.bfloat16)
+    ga, gb = gates[:, :Hv], gates[:, Hv:]
+    A_log = torch.log(torch.empty(Hv, device=dev).uniform_(1, 16))
+    dtb = torch.zeros(Hv, device=dev)
+    scale = D ** -0.5
+    o, saved = chunk_forward(mixed, ga, gb, A_log, dtb, None, 1, T, Hk, Hv, lay, scale)
+    if not backward:
+        ms = _time(lambda: chunk_forward(mixed, ga, gb, A_log, dtb, None, 1, T, Hk, Hv, lay, scale), a.warmup, a.iters)
+    else:
+        d_o = torch.randn_like(o)
+        dmixed = torch.empty_like(mixed)
+        dgates = torch.empty_like(gates)
+        dA, ddt = torch.zeros(Hv, device=dev), torch.zeros(Hv, device=dev)
+        err = device_error_word(mixed.device)
+        ms = _time(lambda: ext().gdn_chunk_bwd(mixed, ga, gb, A_log, dtb, None, o, saved["bufs"], err, saved["geo"],
+                                               scale, d_o, dmixed, dgates[:, :Hv], dgates[:, Hv:], dA, ddt),
+                   a.warmup, a.iters)
+    # chunk-form tensor-core FLOPs are layout dependent; report the recurrence-equivalent rate
+    flops = T * Hv * 3 * 2 * D * D * (2 if backward else 1)
+    return ms, {"recurrence_equiv_tflops": flops / ms / 1e9, "layout": a.layout_gdn, "tokens": T}, None, None
 
 
 def bench_canvas(a, which):
@@ -222,7 +269,8 @@ def bench_elementwise(a):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--op", required=True,
-                    choices=["gemm", "gemm_swiglu", "attn_fwd", "attn_bwd", "gdn_fwd", "gdn_bwd", "canvas_attn", "canvas_gdn",
+                    choices=["gemm", "gemm_swiglu", "attn_fwd", "attn_bwd", "gdn_fwd", "gdn_bwd", "gdn_core_fwd", "gdn_core_bwd",
+                             "canvas_attn", "canvas_gdn",
                              "rmsnorm_fwd", "rmsnorm_bwd", "qk_rope_fwd", "qk_rope_bwd", "swiglu_fwd", "swiglu_bwd"])
     ap.add_argument("--m", type=int, default=24576)
     ap.add_argument("--n", type=int, default=6144)
@@ -235,6 +283,9 @@ def main():
     ap.add_argument("--kv-heads", type=int, default=8)
     ap.add_argument("--rows", type=int, default=4, help="attention: forward rows (2 views x micro-batch)")
     ap.add_argument("--length", type=int, default=3072, help="gated delta: stream length L")
+    ap.add_argument("--gdn-path", dest="gdn_path", default="chunk", choices=["chunk", "scan"],
+                    help="gated delta sub-block: chunked tcgen05 kernels or the per-token scan")
+    ap.add_argument("--gdn-layout", dest="layout_gdn", default="two_stream", choices=["two_stream", "causal"])
     ap.add_argument("--requests", type=int, default=64)
     ap.add_argument("--blk", type=int, default=7)
     ap.add_argument("--warmup", type=int, default=3)
@@ -244,6 +295,8 @@ def main():
         ms, extra, flops, nbytes = bench_gemm(a)
     elif a.op.startswith("attn"):
         ms, extra, flops, nbytes = bench_attn(a, a.op == "attn_bwd")
+    elif a.op.startswith("gdn_core"):
+        ms, extra, flops, nbytes = bench_gdn_core(a, a.op == "gdn_core_bwd")
     elif a.op.startswith("gdn"):
         ms, extra, flops, nbytes = bench_gdn(a, a.op == "gdn_bwd")
     elif a.op.split("_")[0] in ("rmsnorm", "qk", "swiglu"):
