@@ -821,62 +821,115 @@ __device__ __forceinline__ int conv_src(const ConvArgs& a, int b, int t, int shi
   return (p % a.bd) >= shift ? t - shift : p - shift;   // in-block taps: noisy; earlier: clean
 }
 
-__global__ void conv_fwd_kernel(const ConvArgs a) {
-  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int cpr = a.C / 8;
-  if (gid >= (int64_t)a.B * a.T * cpr) return;
-  const int c8 = (int)(gid % cpr) * 8;
-  const int64_t row = gid / cpr;
-  const int b = (int)(row / a.T), t = (int)(row % a.T);
-  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int j = 0; j < a.K; ++j) {
-    const int src = conv_src(a, b, t, a.K - 1 - j);
-    if (src < 0) continue;
-    float xv[8];
-    load8(a.x + ((int64_t)b * a.T + src) * a.ldx + c8, xv);
+// The conv kernels give each thread 8 channels of a run of CONV_RUN consecutive tokens of one
+// batch row: the 4 x 8 weights stay in registers and the previous rows of the same stream ride in a
+// register ring, so a token costs one 16-byte load of x (a tap that reads another stream -- the
+// clean prefix of a noisy block -- or a row before the run is loaded on its own).
+constexpr int CONV_RUN = 16;
+
+template <int K>
+__device__ __forceinline__ void load_w8(const ConvArgs& a, int c8, float (&w)[4][8]) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = fmaf(__bfloat162float(a.w[(c8 + e) * a.K + j]), xv[e], acc[e]);
-  }
-  float out[8];
+  for (int e = 0; e < 8; ++e)
 #pragma unroll
-  for (int e = 0; e < 8; ++e) out[e] = acc[e] / (1.f + expf(-acc[e]));
-  store8(a.y + row * a.ldy + c8, out);
+    for (int j = 0; j < 4; ++j) w[j][e] = j < K ? __bfloat162float(a.w[(c8 + e) * K + j]) : 0.f;
 }
 
-// dpre = dy * silu'(pre) (fp32), and dw[c, j] += sum_t dpre * x[src]; block = 256 threads x 8
-// channels, looping over `tpb` tokens.
-__global__ void conv_bwd_pre_kernel(const ConvArgs a, const bf16* dy, int64_t lddy, float* dpre, float* dw, int tpb) {
-  const int c8 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
-  if (c8 >= a.C) return;
-  const int64_t r0 = (int64_t)blockIdx.y * tpb;
-  const int64_t rows = (int64_t)a.B * a.T;
-  float wacc[4][8];
+__device__ __forceinline__ void zero8(float (&v)[8]) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j)
+  for (int e = 0; e < 8; ++e) v[e] = 0.f;
+}
+
+// x rows feeding output t: xs[j] for tap j (shift K - 1 - j); ring[i] holds x[t - 1 - i] of the same
+// stream when t - 1 - i >= t0 (the run start).
+template <int K>
+__device__ __forceinline__ void conv_taps(const ConvArgs& a, int b, int t, int t0, int c8, const float (&cur)[8],
+                                          const float (&ring)[3][8], float (&xs)[4][8]) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) wacc[j][e] = 0.f;
-  for (int64_t row = r0; row < r0 + tpb && row < rows; ++row) {
-    const int b = (int)(row / a.T), t = (int)(row % a.T);
-    float xs[4][8], pre[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int j = 0; j < 4; ++j) {
+    const int shift = K - 1 - j;
+    if (j >= K) { zero8(xs[j]); continue; }
+    if (shift == 0) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int src = j < a.K ? conv_src(a, b, t, a.K - 1 - j) : -1;
-      if (src >= 0) {
-        load8(a.x + ((int64_t)b * a.T + src) * a.ldx + c8, xs[j]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) xs[j][e] = 0.f;
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (j < a.K) pre[e] = fmaf(__bfloat162float(a.w[(c8 + e) * a.K + j]), xs[j][e], pre[e]);
+      for (int e = 0; e < 8; ++e) xs[j][e] = cur[e];
+      continue;
     }
-    float g[8], dyv[8];
+    const int src = conv_src(a, b, t, shift);
+    if (src < 0) {
+      zero8(xs[j]);
+    } else if (src == t - shift && src >= t0) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) xs[j][e] = ring[shift - 1][e];
+    } else {
+      load8(a.x + ((int64_t)b * a.T + src) * a.ldx + c8, xs[j]);
+    }
+  }
+}
+
+__device__ __forceinline__ void ring_push(float (&ring)[3][8], const float (&cur)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    ring[2][e] = ring[1][e];
+    ring[1][e] = ring[0][e];
+    ring[0][e] = cur[e];
+  }
+}
+
+template <int K>
+__global__ void conv_fwd_kernel(const ConvArgs a) {
+  const int cpr = a.C / 8;
+  const int rpr = (a.T + CONV_RUN - 1) / CONV_RUN;
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (gid >= (int64_t)a.B * rpr * cpr) return;
+  const int c8 = (int)(gid % cpr) * 8;
+  const int64_t run = gid / cpr;
+  const int b = (int)(run / rpr), t0 = (int)(run % rpr) * CONV_RUN, t1 = min(t0 + CONV_RUN, a.T);
+  float w[4][8], ring[3][8], cur[8], xs[4][8];
+  load_w8<K>(a, c8, w);
+  for (int t = t0; t < t1; ++t) {
+    load8(a.x + ((int64_t)b * a.T + t) * a.ldx + c8, cur);
+    conv_taps<K>(a, b, t, t0, c8, cur, ring, xs);
+    float out[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc = fmaf(w[j][e], xs[j][e], acc);
+      out[e] = acc / (1.f + __expf(-acc));
+    }
+    store8(a.y + ((int64_t)b * a.T + t) * a.ldy + c8, out);
+    ring_push(ring, cur);
+  }
+}
+
+// dpre = dy * silu'(pre) (fp32), and dw[c, j] += sum_t dpre * x[src] (run partials, one atomic per
+// weight per run).
+template <int K>
+__global__ void conv_bwd_pre_kernel(const ConvArgs a, const bf16* dy, int64_t lddy, float* dpre, float* dw, int) {
+  const int cpr = a.C / 8;
+  const int rpr = (a.T + CONV_RUN - 1) / CONV_RUN;
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (gid >= (int64_t)a.B * rpr * cpr) return;
+  const int c8 = (int)(gid % cpr) * 8;
+  const int64_t run = gid / cpr;
+  const int b = (int)(run / rpr), t0 = (int)(run % rpr) * CONV_RUN, t1 = min(t0 + CONV_RUN, a.T);
+  float w[4][8], ring[3][8], cur[8], xs[4][8], wacc[4][8];
+  load_w8<K>(a, c8, w);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) zero8(wacc[j]);
+  for (int t = t0; t < t1; ++t) {
+    const int64_t row = (int64_t)b * a.T + t;
+    load8(a.x + row * a.ldx + c8, cur);
+    conv_taps<K>(a, b, t, t0, c8, cur, ring, xs);
+    float dyv[8], g[8];
     load8(dy + row * lddy + c8, dyv);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const float sg = 1.f / (1.f + expf(-pre[e]));
-      g[e] = dyv[e] * sg * (1.f + pre[e] * (1.f - sg));
+      float pre = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) pre = fmaf(w[j][e], xs[j][e], pre);
+      const float sg = 1.f / (1.f + __expf(-pre));
+      g[e] = dyv[e] * sg * (1.f + pre * (1.f - sg));
     }
     float4* dp = reinterpret_cast<float4*>(dpre + row * a.C + c8);
     dp[0] = make_float4(g[0], g[1], g[2], g[3]);
@@ -885,42 +938,76 @@ __global__ void conv_bwd_pre_kernel(const ConvArgs a, const bf16* dy, int64_t ld
     for (int j = 0; j < 4; ++j)
 #pragma unroll
       for (int e = 0; e < 8; ++e) wacc[j][e] = fmaf(g[e], xs[j][e], wacc[j][e]);
+    ring_push(ring, cur);
   }
 #pragma unroll
   for (int e = 0; e < 8; ++e)
-    for (int j = 0; j < a.K && j < 4; ++j) atomicAdd(dw + (c8 + e) * a.K + j, wacc[j][e]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (j < K) atomicAdd(dw + (c8 + e) * K + j, wacc[j][e]);
 }
 
-// dx[s] = sum over outputs t whose tap `shift` reads s of w[c, K-1-shift] * dpre[t].
+__device__ __forceinline__ void load8f(const float* p, float (&v)[8]) {
+  const float4 u0 = reinterpret_cast<const float4*>(p)[0], u1 = reinterpret_cast<const float4*>(p)[1];
+  v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w; v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
+}
+
+// dx[s] = sum over outputs t whose tap `shift` reads s of w[c, K-1-shift] * dpre[t].  Same-stream
+// outputs s .. s+3 come from a look-ahead ring of dpre rows; a clean row also feeds the first
+// in-block taps of every view's noisy block (looked up on their own).
+template <int K>
 __global__ void conv_bwd_dx_kernel(const ConvArgs a, const float* dpre, bf16* dx, int64_t lddx) {
-  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int cpr = a.C / 8;
-  if (gid >= (int64_t)a.B * a.T * cpr) return;
+  const int rpr = (a.T + CONV_RUN - 1) / CONV_RUN;
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (gid >= (int64_t)a.B * rpr * cpr) return;
   const int c8 = (int)(gid % cpr) * 8;
-  const int64_t row = gid / cpr;
-  const int b = (int)(row / a.T), s = (int)(row % a.T);
-  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  const int sstream = a.mode ? s / a.L : 0;
-  const int nview = (a.mode && sstream == 0) ? a.V : 0;
-  for (int shift = 0; shift < a.K; ++shift) {
-    float wv[8];
+  const int64_t run = gid / cpr;
+  const int b = (int)(run / rpr), s0 = (int)(run % rpr) * CONV_RUN, s1 = min(s0 + CONV_RUN, a.T);
+  float w[4][8], ahead[4][8];
+  load_w8<K>(a, c8, w);
+  const float* base = dpre + (int64_t)b * a.T * a.C + c8;
+  // ahead[i] = dpre[s + i] (rows past T read as zero)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) wv[e] = __bfloat162float(a.w[(c8 + e) * a.K + (a.K - 1 - shift)]);
-    // candidate outputs: same stream s + shift; for a clean source also each view's s + shift
-    for (int cnd = 0; cnd <= nview; ++cnd) {
-      const int t = cnd == 0 ? s + shift : cnd * a.L + s + shift;
-      const int lim = a.mode ? (cnd == 0 ? (sstream + 1) * a.L : (cnd + 1) * a.L) : a.T;
-      if (t >= lim) continue;
-      if (conv_src(a, b, t, shift) != s) continue;
-      const float4* dp = reinterpret_cast<const float4*>(dpre + ((int64_t)b * a.T + t) * a.C + c8);
-      const float4 u0 = dp[0], u1 = dp[1];
-      acc[0] = fmaf(wv[0], u0.x, acc[0]); acc[1] = fmaf(wv[1], u0.y, acc[1]);
-      acc[2] = fmaf(wv[2], u0.z, acc[2]); acc[3] = fmaf(wv[3], u0.w, acc[3]);
-      acc[4] = fmaf(wv[4], u1.x, acc[4]); acc[5] = fmaf(wv[5], u1.y, acc[5]);
-      acc[6] = fmaf(wv[6], u1.z, acc[6]); acc[7] = fmaf(wv[7], u1.w, acc[7]);
+  for (int i = 0; i < 3; ++i) {
+    if (s0 + i < a.T) load8f(base + (int64_t)(s0 + i) * a.C, ahead[i]);
+    else zero8(ahead[i]);
+  }
+  for (int s = s0; s < s1; ++s) {
+    if (s + 3 < a.T) load8f(base + (int64_t)(s + 3) * a.C, ahead[3]);
+    else zero8(ahead[3]);
+    float acc[8];
+    zero8(acc);
+    const int sstream = a.mode ? s / a.L : 0;
+    const int lim = a.mode ? (sstream + 1) * a.L : a.T;
+#pragma unroll
+    for (int shift = 0; shift < 4; ++shift) {
+      if (shift >= K) continue;
+      const int t = s + shift;
+      if (t < lim && conv_src(a, b, t, shift) == s) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = fmaf(w[K - 1 - shift][e], ahead[shift][e], acc[e]);
+      }
+      if (a.mode && sstream == 0) {
+        for (int v = 1; v <= a.V; ++v) {
+          const int tn = v * a.L + s + shift;
+          if (s + shift < a.L && conv_src(a, b, tn, shift) == s) {
+            float dv8[8];
+            load8f(base + (int64_t)tn * a.C, dv8);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] = fmaf(w[K - 1 - shift][e], dv8[e], acc[e]);
+          }
+        }
+      }
+    }
+    store8(dx + ((int64_t)b * a.T + s) * lddx + c8, acc);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      ahead[0][e] = ahead[1][e];
+      ahead[1][e] = ahead[2][e];
+      ahead[2][e] = ahead[3][e];
     }
   }
-  store8(dx + row * lddx + c8, acc);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -1132,8 +1219,14 @@ static gdn::ConvArgs conv_args(const ConvParams& p) {
 int gdn_conv_fwd(const ConvParams& p, cudaStream_t st) {
   if (p.C % 8 || p.K > 4 || p.K < 1) return -1;
   const gdn::ConvArgs a = conv_args(p);
-  const int64_t n = (int64_t)p.B * p.T * (p.C / 8);
-  gdn::conv_fwd_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a);
+  const int64_t n = (int64_t)p.B * ((p.T + gdn::CONV_RUN - 1) / gdn::CONV_RUN) * (p.C / 8);
+  const unsigned g = (unsigned)((n + 127) / 128);
+  switch (p.K) {
+    case 1: gdn::conv_fwd_kernel<1><<<g, 128, 0, st>>>(a); break;
+    case 2: gdn::conv_fwd_kernel<2><<<g, 128, 0, st>>>(a); break;
+    case 3: gdn::conv_fwd_kernel<3><<<g, 128, 0, st>>>(a); break;
+    default: gdn::conv_fwd_kernel<4><<<g, 128, 0, st>>>(a); break;
+  }
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
@@ -1141,12 +1234,18 @@ int gdn_conv_bwd(const ConvParams& p, const bf16* dy, int64_t lddy, float* dpre,
                  cudaStream_t st) {
   if (p.C % 8 || p.K > 4 || p.K < 1) return -1;
   const gdn::ConvArgs a = conv_args(p);
-  const int tpb = 64;
-  const int64_t rows = (int64_t)p.B * p.T;
-  dim3 g1((unsigned)((p.C / 8 + 255) / 256), (unsigned)((rows + tpb - 1) / tpb));
-  gdn::conv_bwd_pre_kernel<<<g1, 256, 0, st>>>(a, dy, lddy, dpre, dw, tpb);
-  const int64_t n = rows * (p.C / 8);
-  gdn::conv_bwd_dx_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a, dpre, dx, lddx);
+  const int64_t n = (int64_t)p.B * ((p.T + gdn::CONV_RUN - 1) / gdn::CONV_RUN) * (p.C / 8);
+  const unsigned g = (unsigned)((n + 127) / 128);
+#define TRIDA_CONV_BWD(KK)                                                          \
+  gdn::conv_bwd_pre_kernel<KK><<<g, 128, 0, st>>>(a, dy, lddy, dpre, dw, 0);       \
+  gdn::conv_bwd_dx_kernel<KK><<<g, 128, 0, st>>>(a, dpre, dx, lddx);
+  switch (p.K) {
+    case 1: TRIDA_CONV_BWD(1) break;
+    case 2: TRIDA_CONV_BWD(2) break;
+    case 3: TRIDA_CONV_BWD(3) break;
+    default: TRIDA_CONV_BWD(4) break;
+  }
+#undef TRIDA_CONV_BWD
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
