@@ -47,6 +47,9 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--layers", type=int, default=36, help="debug only: fewer layers (reported as reduced)")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--shard", choices=["full", "zero2"], default="full",
+                   help="full: decoder-layer weights sharded and gathered per layer over NVLink (FSDP full "
+                        "shard, the reference's setup); zero2: replicated weights")
     p.add_argument("--comm", choices=["fused", "nccl"], default="fused",
                    help="multi-GPU optimizer traffic: fused peer-memory kernels or NCCL collectives")
     return p.parse_args()
@@ -152,7 +155,9 @@ def run_ours(args, rank, world, local_rank):
     dec = Decoder(cfg, dtype=torch.bfloat16, device="cuda")
     model = BlockDiffusionLM(dec, mask_id=MASK_ID, pad_id=VOCAB - 2, bd_size=BD, ar_loss_weight=1.0)
     model.train()
-    engine = TrainEngine(model, lr=1e-5, warmup=50, max_steps=2000, device=torch.device("cuda"), comm=args.comm)
+    full = args.shard == "full" and world > 1
+    engine = TrainEngine(model, lr=1e-5, warmup=50, max_steps=2000, device=torch.device("cuda"), comm=args.comm,
+                         full_shard=full)
     batches = synthetic_batches(args.warmup + args.steps, seed=1234 + rank)
     rpad = host_rpad(batches[0]["labels"], BD, model.response_buckets)
     dev_batches = [{k: v.cuda(non_blocking=True) for k, v in b.items()} for b in batches]
@@ -344,15 +349,22 @@ def main():
                        "global_batch": world * MB, "seq_len": PROMPT + RESP,
                        "forward_row": "[S 1024 | x_t 1024 | x_0 1024] x 2 views",
                        "forward_tokens_per_step": world * MB * 2 * (PROMPT + 2 * RESP),
-                       "parallelism": f"dp{world} (sharded optimizer state; " + (
-                           "gradient reduce-scatter + AdamW + parameter all-gather fused over NVLink peer memory)"
-                           if args.comm == "fused" and world > 1 else "NCCL collectives)" if world > 1 else "single GPU)"),
+                       "parallelism": (f"dp{world} " + (
+                           ("(full shard: per-layer weight shards gathered over NVLink peer memory ahead of each "
+                            "layer, per-layer gradient reduce-scatter streamed under backward, sharded AdamW)"
+                            if args.shard == "full" else
+                            "(sharded optimizer state; gradient reduce-scatter + AdamW + parameter all-gather "
+                            "fused over NVLink peer memory)")
+                           if args.comm == "fused" else "(NCCL collectives)") if world > 1 else "dp1 (single GPU)"),
                        "bd_size": BD,
                        "ar_loss_weight": 1.0, "optimizer": "AdamW lr 1e-5 (warmup 50, cosine)",
                        "l2": "inputs larger than L2 (per-step working set >> 126 MB)",
                        "peak_mem_gb": round(peak_gb, 1)},
             "clocks": clk, "e2e": e2e,
         }
+        if clk and clk.get("sm_mhz"):
+            # clock-normalised step cost: comparable across power-capped and unthrottled runs
+            line["mcycles_per_step"] = round(ms * clk["sm_mhz"] / 1000.0, 1)
         if args.impl == "ours":
             line["gpu_launches"] = launches
         else:

@@ -262,6 +262,27 @@ void symm_adamw_ag(const std::vector<int64_t>& bufs, const std::vector<int64_t>&
   TORCH_CHECK(rc == 0, "symm_adamw_ag failed with code ", rc);
 }
 
+// Full-shard parameter all-gather: every rank's bf16 shard (bufs[r], shard_len elements) into this
+// rank's dst (world * shard_len elements) over NVLink.
+void symm_gather(const std::vector<int64_t>& bufs, int64_t rank, int64_t shard_len, const at::Tensor& dst,
+                 int64_t blocks) {
+  TORCH_CHECK(bufs.size() >= 1 && bufs.size() <= 8, "1..8 ranks");
+  CHECK_BF16(dst);
+  TORCH_CHECK(dst.is_contiguous() && dst.numel() >= (int64_t)bufs.size() * shard_len, "dst too small");
+  void* b[8];
+  for (size_t i = 0; i < bufs.size(); ++i) b[i] = reinterpret_cast<void*>(bufs[i]);
+  const int rc = trida::symm_gather_bf16(b, rank, bufs.size(), shard_len, mbf(dst), (int)blocks, stream());
+  TORCH_CHECK(rc == 0, "symm_gather failed with code ", rc);
+}
+
+void symm_barrier(const std::vector<int64_t>& flags, int64_t rank, int64_t epoch, int64_t slot, const at::Tensor& err) {
+  TORCH_CHECK(flags.size() >= 1 && flags.size() <= 8, "1..8 ranks");
+  unsigned* f[8];
+  for (size_t i = 0; i < flags.size(); ++i) f[i] = reinterpret_cast<unsigned*>(flags[i]);
+  const int rc = trida::symm_barrier(f, rank, flags.size(), (unsigned)epoch, (int)slot, err.data_ptr<int>(), stream());
+  TORCH_CHECK(rc == 0, "symm_barrier failed with code ", rc);
+}
+
 // Reads and clears the GEMM's device error word (host sync); 0 = no timed-out wait.
 int64_t gemm_error() {
   int* w = trida::gemm_error_word();
@@ -972,6 +993,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("err"), py::arg("accumulate") = false, py::arg("done") = py::none(), py::arg("close_slot") = -1);
   m.def("symm_norm_coef", &symm_norm_coef);
   m.def("symm_adamw_ag", &symm_adamw_ag);
+  m.def("symm_gather", &symm_gather);
+  m.def("symm_barrier", &symm_barrier);
   m.def("gdn_state_numel", &gdn_state_numel);
   m.def("gdn_chunk_fwd", &gdn_chunk_fwd);
   m.def("gdn_chunk_bwd", &gdn_chunk_bwd);

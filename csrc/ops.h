@@ -177,6 +177,8 @@ int symm_adamw_ag(void* const* bufs, unsigned* const* flags, int rank, int world
                   int64_t shard_len, const float* grad, float* master, float* m, float* v, float lr, float b1,
                   float b2, float eps, float wd, int step, const float* coef, unsigned* done, int* err, int sm_count,
                   cudaStream_t s);
+int symm_gather_bf16(void* const* bufs, int rank, int world, int64_t shard_len, bf16* dst, int blocks, cudaStream_t s);
+int symm_barrier(unsigned* const* flags, int rank, int world, unsigned epoch, int slot, int* err, cudaStream_t s);
 int symm_ipc_handle(void* ptr, unsigned char* out64);
 void* symm_ipc_open(const unsigned char* in64);
 void symm_ipc_close(void* p);

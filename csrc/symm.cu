@@ -207,7 +207,45 @@ __global__ void norm_coef_kernel(Peers P, int rank, int world, unsigned epoch, i
   }
 }
 
+// All-gather of one parameter group for full-shard data parallelism: rank r's bf16 shard lives
+// at bufs[r] (shard_len elements); every rank copies all shards, in rank order, into its own
+// `dst` with 16-byte P2P loads (plain loads through NVLink; no TMA, no multicast).  Consistency
+// comes from the callers: a shard only changes in the optimizer step, which ends with barrier();
+// the gathers of the next step run after it on every rank.
+__global__ void gather_kernel(Peers P, int rank, int world, int64_t shard_len, bf16* __restrict__ dst) {
+  const int64_t n8 = shard_len / 8;
+  const int64_t total = n8 * world;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t k = i / n8, j = i - k * n8;
+    const int src = (int)((k + rank) % world);      // stagger the peers each rank reads first
+    const uint4 v = reinterpret_cast<const uint4*>(P.buf[src])[j];
+    reinterpret_cast<uint4*>(dst + (int64_t)src * shard_len)[j] = v;
+  }
+}
+
+// A bare cross-rank barrier on `slot` (one CTA).
+__global__ void barrier_kernel(Peers P, int rank, int world, unsigned epoch, int slot, int* err) {
+  barrier(P, rank, world, epoch, slot, err, 260 + slot);
+}
+
 }  // namespace symm
+
+int symm_gather_bf16(void* const* bufs, int rank, int world, int64_t shard_len, bf16* dst, int blocks,
+                     cudaStream_t s) {
+  if (world > symm::MAXR || shard_len % 8) return -1;
+  symm::Peers P{};
+  for (int r = 0; r < world; ++r) P.buf[r] = bufs[r];
+  symm::gather_kernel<<<blocks, 256, 0, s>>>(P, rank, world, shard_len, dst);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int symm_barrier(unsigned* const* flags, int rank, int world, unsigned epoch, int slot, int* err, cudaStream_t s) {
+  if (world > symm::MAXR) return -1;
+  symm::Peers P{};
+  for (int r = 0; r < world; ++r) P.flag[r] = flags[r];
+  symm::barrier_kernel<<<1, 32, 0, s>>>(P, rank, world, epoch, slot, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
 
 int symm_norm_coef(void* const* partials, unsigned* const* flags, int rank, int world, unsigned epoch, int nblocks,
                    float max_norm, float* norm_out, float* coef_out, int* err, cudaStream_t s) {

@@ -133,3 +133,59 @@ def test_config1_world2_gloo_ranks_stay_in_sync(tmp_path):
         losses, same = res[r]
         assert same, "sharded optimizer left ranks with different parameters"
         assert all(l == l and l < 20 for l in losses)
+
+
+def _shard_main(rank, world, path, port, out):
+    """Full-shard (per-layer weight shards gathered around each layer) against replicated weights
+    with sharded optimizer state, on the same data: identical loss curves and final weights."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    res = {}
+    for mode in ("zero2", "full", "full_keep"):
+        cfg = ModelConfig.from_pretrained(path)
+        cfg.vocab_size = 1024
+        dec = Decoder(cfg, dtype=torch.float32)
+        torch.manual_seed(0)
+        dec.reset_parameters()
+        m = BlockDiffusionLM(dec, mask_id=1023, bd_size=16, ar_loss_weight=1.0, response_buckets=None)
+        full = mode != "zero2"
+        opt = ShardedAdamW(m.param_groups(per_layer=full), lr=LR, betas=(0.9, 0.95), weight_decay=WD,
+                           device=torch.device("cpu"), full_shard=full, keep_params=mode == "full_keep")
+        m.param_ring = opt.param_ring
+        losses = []
+        for step, (ids, labels, am) in enumerate(batches(4, seed=rank)):
+            torch.manual_seed(50 + step + 100 * rank)
+            loss, _ = m(ids[:1], labels[:1], am[:1])
+            loss.backward()
+            for g in opt.param_groups:
+                g["lr"] = lr_at(step)
+            opt.reduce_gradients()
+            opt.clip_grad_norm_(1.0)
+            opt.step()
+            opt.zero_grad()
+            losses.append(loss.item())
+        if opt.param_ring is not None:
+            opt.param_ring.materialize()
+            res[mode + "_shard_sizes"] = [g.shard_param().numel() for g in opt.groups if g.full_shard]
+        res[mode] = (losses, {n: p.detach().clone() for n, p in m.named_parameters()})
+    out[rank] = res
+    dist.destroy_process_group()
+
+
+def test_config1_world2_full_shard_matches_replicated(tmp_path):
+    make_tiny_qwen3(str(tmp_path), seed=0)
+    port = 29300 + os.getpid() % 300
+    with mp.Manager() as mgr:
+        out = mgr.dict()
+        mp.spawn(_shard_main, args=(2, str(tmp_path), port, out), nprocs=2, join=True)
+        res = dict(out)
+    for r in range(2):
+        ref_losses, ref_params = res[r]["zero2"]
+        for mode in ("full", "full_keep"):
+            losses, params = res[r][mode]
+            for a, b in zip(losses, ref_losses):
+                assert abs(a - b) <= 1e-5 * max(1.0, abs(b)), (mode, losses, ref_losses)
+            for n, p in params.items():
+                torch.testing.assert_close(p, ref_params[n], rtol=1e-5, atol=1e-6, msg=f"{mode}: {n}")
+        assert all(s > 0 for s in res[r]["full_shard_sizes"])   # every rank holds part of each layer

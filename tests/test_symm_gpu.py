@@ -176,3 +176,84 @@ def test_fused_gemm_allreduce_matches_nccl():
     for rank, err in res:
         assert err < 2e-2, (rank, err)
     assert all(p.exitcode == 0 for p in procs)
+
+
+def _shard_worker(rank, world, port, q):
+    """A tiny dense decoder (3 layers, CUDA blocks) trained for 3 steps with replicated weights
+    (fused optimizer collectives) and with full-shard weights gathered per layer over NVLink (with
+    and without keeping the gathered weights to backward): same losses, same final weights; the
+    P2P gather kernel itself against NCCL's all-gather."""
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from trida_stack_b200.engine import TrainEngine
+        from trida_stack_b200.models import BlockDiffusionLM, Decoder, qwen3_config
+        from trida_stack_b200.ops._ext import ext
+        from trida_stack_b200.parallel.symm import SymmetricHeap
+        heap = SymmetricHeap()
+        shard = torch.randn(4096, device="cuda").to(torch.bfloat16)
+        buf = heap.alloc(4096, torch.bfloat16)
+        buf.local.copy_(shard)
+        torch.cuda.synchronize()
+        dist.barrier()
+        got = torch.empty(world * 4096, device="cuda", dtype=torch.bfloat16)
+        ext().symm_gather(buf.ptrs, rank, 4096, got, 8)
+        ref = torch.empty_like(got)
+        dist.all_gather_into_tensor(ref, shard)
+        torch.cuda.synchronize()
+        gather_ok = torch.equal(got, ref)
+        res = {}
+        for mode in ("zero2", "full", "keep"):
+            cfg = qwen3_config(vocab_size=4096, hidden_size=256, intermediate_size=512, num_layers=3, n_heads=4,
+                               n_kv_heads=2, head_dim=128)
+            torch.manual_seed(0)
+            model = BlockDiffusionLM(Decoder(cfg, dtype=torch.bfloat16, device="cuda"), mask_id=4095, bd_size=32,
+                                     ar_loss_weight=1.0)
+            model.train()
+            eng = TrainEngine(model, lr=1e-3, warmup=0, device=torch.device("cuda"), comm="fused",
+                              full_shard=mode != "zero2", keep_params=mode == "keep")
+            g = torch.Generator().manual_seed(11 + rank)
+            losses = []
+            for step in range(3):
+                ids = torch.randint(0, 4094, (2, 256), generator=g)
+                labels = ids.clone()
+                labels[:, :128] = -100
+                loss, _, _, _ = eng.train_step([{"input_ids": ids, "labels": labels,
+                                                 "attention_mask": torch.ones_like(ids)}], step)
+                losses.append(loss.item())
+            if eng.optim.param_ring is not None:
+                eng.optim.param_ring.materialize()
+            torch.cuda.synchronize()
+            eng.optim.heap.check()
+            res[mode] = (losses, {n: p.detach().float().cpu() for n, p in model.named_parameters()})
+        lerr = max(abs(a - b) / max(1.0, abs(b)) for m in ("full", "keep")
+                   for a, b in zip(res[m][0], res["zero2"][0]))
+        werr = max(((res[m][1][n] - p).abs().max() / (p.abs().max() + 1e-6)).item()
+                   for m in ("full", "keep") for n, p in res["zero2"][1].items())
+        q.put((rank, gather_ok, lerr, werr))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_full_shard_training_matches_replicated():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_shard_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    res = [q.get(timeout=5) for _ in range(2)]
+    for rank, gather_ok, lerr, werr in res:
+        assert gather_ok, rank
+        assert lerr < 1e-3, (rank, lerr)
+        assert werr < 1e-2, (rank, werr)
+    assert all(p.exitcode == 0 for p in procs)

@@ -232,7 +232,14 @@ def save_checkpoint(model, optim, global_step, args):
     """Weights first, then the optional optimizer state, on every rank in the same order; rank 0
     then writes the integrity manifest."""
     tag = f"step_{global_step}"
-    save_hf(model, args, tag)
+    ring = getattr(optim, "param_ring", None)
+    if ring is not None:
+        ring.materialize()      # full-shard weights: every rank gathers every layer for the save
+    try:
+        save_hf(model, args, tag)
+    finally:
+        if ring is not None:
+            ring.release_all()
     save_train_state(model, optim, global_step, args, tag)
     _barrier()
     out = os.path.join(args.save_dir, tag) if getattr(args, "save_dir", None) else None

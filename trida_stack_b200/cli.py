@@ -57,7 +57,11 @@ def build_parser():
     p.add_argument("--fused_ce", action="store_true",
                    help="accepted for compatibility: the CUDA path always uses the fused linear CE")
     p.add_argument("--fsdp_keep_params", action="store_true",
-                   help="keep gathered layer weights resident between forward and backward")
+                   help="keep gathered layer weights resident between forward and backward (no reshard after "
+                        "forward)")
+    p.add_argument("--shard", choices=["full", "zero2"], default="full",
+                   help="full: decoder-layer weights sharded across ranks and gathered per layer (FSDP full "
+                        "shard); zero2: replicated weights, sharded gradients and optimizer state")
     p.add_argument("--compile_mlp", action="store_true", help="accepted for compatibility (no-op)")
     p.add_argument("--compile_glue", action="store_true", help="accepted for compatibility (no-op)")
     p.add_argument("--compile_layers", action="store_true", help="accepted for compatibility (no-op)")

@@ -136,13 +136,37 @@ class BlockDiffusionLM(nn.Module):
 
     def run_stack(self, x, actx):
         mode = self.activation_checkpoint
-        if mode == "layer" and self.training and torch.is_grad_enabled():
-            from torch.utils.checkpoint import checkpoint
+        ckpt = mode == "layer" and self.training and torch.is_grad_enabled()
+        ring = getattr(self, "param_ring", None)
+        if ring is None or not ring.active:
+            if ckpt:
+                from torch.utils.checkpoint import checkpoint
 
-            def hook(i, layer, h):
-                return checkpoint(layer, h, actx, self.cfg, use_reentrant=False)
-            return self.decoder(x, actx, layer_hook=hook)
-        return self.decoder(x, actx)
+                def hook(i, layer, h):
+                    return checkpoint(layer, h, actx, self.cfg, use_reentrant=False)
+                return self.decoder(x, actx, layer_hook=hook)
+            return self.decoder(x, actx)
+        # full-shard weights: gather layer i (prefetching i + 1) before it runs, drop it after; in
+        # backward the gradient of layer i's output arrives once layer i + 1's backward is done,
+        # which is when layer i is gathered again (prefetching i - 1)
+        n = len(self.decoder.layers)
+
+        def sharded(i, layer, h):
+            ring.fetch(i, i + 1 if i + 1 < n else None)
+            if ckpt:
+                from torch.utils.checkpoint import checkpoint
+                out = checkpoint(layer, h, actx, self.cfg, use_reentrant=False)
+            else:
+                out = layer(h, actx, self.cfg)
+            ring.done(i)
+            if out.requires_grad:
+                def before_backward(g, i=i):
+                    ring.done(i + 1)
+                    ring.fetch(i, i - 1 if i > 0 else None)
+                    return g
+                out.register_hook(before_backward)
+            return out
+        return self.decoder(x, actx, layer_hook=sharded)
 
     def _weights(self, rate_sel, pos_sel=None):
         n = rate_sel.numel()

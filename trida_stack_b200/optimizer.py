@@ -13,11 +13,20 @@ __all__ = ["get_lr", "build_optimizer", "apply_optimizer_step"]
 
 
 def build_optimizer(args, model, device=None):
+    """Sharded AdamW.  With several ranks the decoder layers are fully sharded (the reference's
+    FSDP ``fully_shard`` per layer, ``train/distributed.py:32-59``): each rank keeps 1/world of
+    every layer's bf16 weights and gathers a layer around its forward and backward;
+    ``--fsdp_keep_params`` keeps the gathered weights from forward to backward
+    (``reshard_after_forward=False``).  ``--shard zero2`` keeps replicated weights instead."""
+    from .distributed import world_size
+    full = getattr(args, "shard", "full") == "full" and world_size() > 1
     groups = model.param_groups(projector_lr_scale=args.projector_lr_scale,
-                                decision_head_lr_scale=args.decision_head_lr_scale)
+                                decision_head_lr_scale=args.decision_head_lr_scale, per_layer=full)
     opt = ShardedAdamW(groups, lr=args.lr, betas=(0.9, args.adam_beta2), weight_decay=args.weight_decay,
                        fp32_master=getattr(args, "fp32_master", False), device=device,
-                       comm=getattr(args, "comm", "nccl"))
+                       comm=getattr(args, "comm", "nccl"), full_shard=full,
+                       keep_params=getattr(args, "fsdp_keep_params", False))
+    model.param_ring = opt.param_ring
     for g, src in zip(opt.param_groups, groups):
         g.setdefault("lr_scale", src.get("lr_scale", 1.0))
     if len(groups) > 1:

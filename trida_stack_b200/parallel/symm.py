@@ -11,8 +11,10 @@ import torch.distributed as dist
 
 from ..ops._ext import ext
 
-NSLOTS = 5          # barrier slots: all-reduce, reduce-scatter, AdamW close, norm, streamed reduce-scatter close
+NSLOTS = 6          # barrier slots: all-reduce, reduce-scatter, AdamW close, norm, streamed reduce-scatter close,
+                    # full-shard update close
 RING_CLOSE_SLOT = 4
+SHARD_CLOSE_SLOT = 5
 MAXR = 8
 
 

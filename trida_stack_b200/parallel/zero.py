@@ -13,12 +13,19 @@ all-reduce, no host sync) -> fused AdamW on the shard with the clip coefficient 
 vanish and the same kernels run over the whole buffer.  The gradient reduce-scatter is bucketed
 per layer and can be issued from backward hooks, overlapping communication with the backward of
 earlier layers (``overlap=True``).
+
+Full shard (``full_shard=True``, the reference's FSDP ``fully_shard`` of every decoder layer,
+``train/distributed.py:32-59``): a decoder layer's bf16 weights persist only as this rank's 1/world
+shard; ``ParamRing`` gathers a layer into a local buffer right before it runs (prefetching the
+next layer on a side stream while the current one computes) and drops it afterwards -- again in
+backward -- unless ``keep_params`` keeps the gathered weights from forward to backward (the
+reference's ``--fsdp_keep_params``).  The update then touches only the local shard.
 """
 import torch
 import torch.distributed as dist
 
 from ..ops._ext import ext
-from .symm import RING_CLOSE_SLOT
+from .symm import RING_CLOSE_SLOT, SHARD_CLOSE_SLOT
 
 ALIGN = 64
 
@@ -35,8 +42,10 @@ class FlatGroup:
     """One optimizer group flattened into contiguous buffers (symmetric peer buffers when a heap
     is given, so the fused collectives can read and write them from every rank)."""
 
-    def __init__(self, params, lr_scale, world, rank, fp32_master, device, heap=None, stream=False):
+    def __init__(self, params, lr_scale, world, rank, fp32_master, device, heap=None, stream=False,
+                 full_shard=False):
         self.params = list(params)
+        self.full_shard = full_shard
         self.lr_scale = lr_scale
         self.world, self.rank = world, rank
         n = sum(p.numel() for p in self.params)
@@ -45,9 +54,11 @@ class FlatGroup:
         self.padded = (n + unit - 1) // unit * unit
         self.shard = self.padded // world
         dtype = self.params[0].dtype if self.params else torch.bfloat16
-        self.flat_sym = self.grad_sym = None
+        self.flat_sym = self.grad_sym = self.shard_sym = None
         self.stream = stream        # gradients live in a shared ring slot only while this group's backward runs
-        if heap is not None:
+        if full_shard:
+            self.flat = torch.zeros(self.padded, dtype=dtype, device=device)   # staging only, freed below
+        elif heap is not None:
             self.flat_sym = heap.alloc(self.padded, dtype)
             self.flat = self.flat_sym.local
             if not stream:
@@ -74,9 +85,22 @@ class FlatGroup:
         self.lo, self.hi = lo, lo + self.shard
         self.grad_shard = (torch.zeros(self.shard, dtype=torch.float32, device=device) if world > 1 or stream
                            else None)
+        if full_shard:
+            # keep only this rank's shard (in peer memory when the gathers run over NVLink)
+            if heap is not None:
+                self.shard_sym = heap.alloc(self.shard, dtype)
+                self.pshard = self.shard_sym.local
+            else:
+                self.pshard = torch.empty(self.shard, dtype=dtype, device=device)
+            self.pshard.copy_(self.flat[lo:lo + self.shard])
+            if world > 1:
+                self.flat = None
+                self.unbind_params()
+            else:
+                self.pshard = self.flat       # one rank: the shard is the whole buffer, params stay bound
         self.master = None
         if fp32_master:
-            self.master = self.flat[lo:lo + self.shard].float().clone()
+            self.master = self.shard_param().float().clone()
         self.m = torch.zeros(self.shard, dtype=torch.float32, device=device)
         self.v = torch.zeros(self.shard, dtype=torch.float32, device=device)
 
@@ -84,7 +108,20 @@ class FlatGroup:
         return self.grad if (self.world == 1 and not self.stream) else self.grad_shard
 
     def shard_param(self):
+        if self.full_shard:
+            return self.pshard if self.world > 1 else self.flat[self.lo:self.hi]
         return self.flat[self.lo:self.hi]
+
+    def bind_params(self, buf):
+        """Point every parameter's data into ``buf`` (this group's gathered flat weights)."""
+        for p, (off, k) in zip(self.params, self.offsets):
+            p.data = buf[off:off + k].view(p.shape)
+
+    def unbind_params(self):
+        """Leave every parameter without storage of its own (a zero-stride view of one element),
+        so nothing reads stale gathered weights."""
+        for p in self.params:
+            p.data = torch.zeros(1, dtype=p.dtype, device=p.device).expand(p.shape)
 
     def bind_grads(self, buf):
         """Point every parameter's ``main_grad`` into ``buf`` (a zeroed ring slot)."""
@@ -201,6 +238,115 @@ class LayerGradStream:
 
 
 
+class ParamRing:
+    """Gathered weights of full-shard layer groups.  Two local buffers serve as a ring: ``fetch(i,
+    nxt)`` waits for layer i's gather (issuing it now if it was not prefetched), binds its
+    parameters, and starts gathering layer ``nxt`` into the other buffer on a side stream;
+    ``done(i)`` marks the compute stream's last use of layer i's buffer, which the next gather into
+    that buffer waits for.  With ``keep`` (and always on CPU, where plain autograd saves the weight
+    tensors themselves) every layer gets its own buffer and a gather stays valid until the next
+    optimizer step (weights kept from forward to backward).
+
+    A gather is one ``symm_gather`` kernel (P2P loads of every rank's shard over NVLink) with the
+    fused collectives, ``all_gather_into_tensor`` otherwise; on one rank nothing is gathered."""
+
+    GATHER_BLOCKS = 32     # CTAs of a gather kernel: enough for NVLink, few SMs taken from compute
+
+    def __init__(self, opt, layer_groups, keep=False):
+        self.opt, self.map = opt, dict(layer_groups)
+        self.groups = opt.groups
+        first = self.groups[self.map[next(iter(self.map))]]
+        dev = first.grad_shard.device
+        self.keep = keep or dev.type != "cuda"
+        size = max(self.groups[gi].padded for gi in self.map.values())
+        nbuf = len(self.map) if self.keep else 2
+        self.bufs = [torch.empty(size, dtype=first.pshard.dtype, device=dev) for _ in range(nbuf)]
+        self.owner = [None] * nbuf        # group whose weights the buffer holds (valid until the next step)
+        self.ready = [None] * nbuf        # gather-complete events
+        self.free = [None] * nbuf         # last-use events on the compute stream
+        self.cuda = dev.type == "cuda"
+        self.stream = torch.cuda.Stream(device=dev) if self.cuda else None
+        self.active = opt.world > 1
+        self.cur = None                   # buffer of the layer bound last
+        self.order = list(self.map.values())
+
+    def _held(self, gi):
+        for bi, o in enumerate(self.owner):
+            if o == gi:
+                return bi
+        return None
+
+    def _gather_into(self, g, dst):
+        o = self.opt
+        if o.fused:
+            ext().symm_gather(g.shard_sym.ptrs, o.rank, g.shard, dst, self.GATHER_BLOCKS)
+        else:
+            dist.all_gather_into_tensor(dst, g.pshard, group=o.pg)
+
+    def _gather(self, gi, bi):
+        """Gather layer group gi into buffer bi (side stream) after the buffer's last use."""
+        g = self.groups[gi]
+        dst = self.bufs[bi][:g.padded]
+        if self.cuda:
+            self.stream.wait_stream(torch.cuda.current_stream())   # shard updates of the last step
+            if self.free[bi] is not None:
+                self.stream.wait_event(self.free[bi])
+            with torch.cuda.stream(self.stream):
+                self._gather_into(g, dst)
+                ev = torch.cuda.Event()
+                ev.record(self.stream)
+            self.ready[bi] = ev
+        else:
+            self._gather_into(g, dst)
+        self.owner[bi] = gi
+
+    def fetch(self, layer, nxt=None):
+        if not self.active or layer not in self.map:
+            return
+        gi = self.map[layer]
+        bi = self._held(gi)
+        if bi is None:
+            bi = self.order.index(gi) if self.keep else (0 if self.cur is None else 1 - self.cur)
+            self._gather(gi, bi)
+        self.cur = bi
+        if self.cuda and self.ready[bi] is not None:
+            torch.cuda.current_stream().wait_event(self.ready[bi])
+        self.groups[gi].bind_params(self.bufs[bi][:self.groups[gi].padded])
+        if nxt is not None and nxt in self.map:
+            gn = self.map[nxt]
+            if self._held(gn) is None:
+                self._gather(gn, self.order.index(gn) if self.keep else 1 - bi)
+
+    def done(self, layer):
+        if not self.active or layer not in self.map or self.keep or not self.cuda:
+            return
+        bi = self._held(self.map[layer])
+        if bi is not None:
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream())
+            self.free[bi] = ev
+
+    def invalidate(self):
+        """Every gathered copy is stale after an optimizer step."""
+        self.owner = [None] * len(self.owner)
+
+    def materialize(self):
+        """Bind every full-shard group to freshly gathered weights of its own (checkpointing)."""
+        if not self.active:
+            return
+        for gi in self.map.values():
+            g = self.groups[gi]
+            full = torch.empty(g.padded, dtype=g.pshard.dtype, device=g.pshard.device)
+            self._gather_into(g, full)
+            g.bind_params(full)
+
+    def release_all(self):
+        if not self.active:
+            return
+        for gi in self.map.values():
+            self.groups[gi].unbind_params()
+
+
 def _adamw_torch(param, master, grad, m, v, lr, b1, b2, eps, wd, step, coef):
     """CPU statement of the fused AdamW kernel (torch.optim.AdamW math, fp32 moments)."""
     p = master if master is not None else param.float()
@@ -220,7 +366,7 @@ class ShardedAdamW:
     NB = 296          # partial-sum blocks of the fused reduce-scatter (2 per SM)
 
     def __init__(self, groups, lr, betas=(0.9, 0.95), weight_decay=0.0, eps=1e-8, fp32_master=False,
-                 device=None, process_group=None, comm="nccl"):
+                 device=None, process_group=None, comm="nccl", full_shard=False, keep_params=False):
         self.world, self.rank = _world(), _rank()
         self.pg = process_group
         device = device or groups[0]["params"][0].device
@@ -233,8 +379,15 @@ class ShardedAdamW:
             self.heap = SymmetricHeap(process_group)
         groups = [g for g in groups if g["params"]]
         self.groups = [FlatGroup(g["params"], g.get("lr_scale", 1.0), self.world, self.rank, fp32_master, device,
-                                 self.heap, stream=bool(g.get("stream")))
+                                 self.heap, stream=bool(g.get("stream")),
+                                 full_shard=full_shard and bool(g.get("stream")))
                        for g in groups]
+        self.param_ring = None
+        if full_shard:
+            layer_groups = {gg["layer"]: i for i, gg in enumerate(groups) if gg.get("stream")}
+            if not layer_groups:
+                raise ValueError("full_shard needs per-layer parameter groups (param_groups(per_layer=True))")
+            self.param_ring = ParamRing(self, layer_groups, keep=keep_params)
         if self.fused:
             self.partials = self.heap.alloc(len(self.groups) * self.NB, torch.float32)
         self._clipped = False
@@ -284,15 +437,22 @@ class ShardedAdamW:
         self._clipped = False
         if self.ring is not None:
             self.ring.flush()       # a layer whose input needed no gradient never released its slot
-            for g in self.groups:   # plain-autograd (CPU) gradients of streamed groups, single process
+            for g in self.groups:   # plain-autograd (CPU) gradients of streamed groups
                 if not g.stream:
                     continue
+                if not any(p.grad is not None for p in g.params):
+                    continue
+                flat = torch.zeros(g.padded, dtype=torch.float32, device=g.grad_shard.device)
                 for p, (off, k) in zip(g.params, g.offsets):
                     if p.grad is not None:
-                        if self.world != 1:
-                            raise NotImplementedError("streamed gradients across ranks need the CUDA blocks")
-                        g.grad_shard[off:off + k].add_(p.grad.float().reshape(-1))
+                        flat[off:off + k].add_(p.grad.float().reshape(-1))
                         p.grad = None
+                if self.world == 1:
+                    g.grad_shard.add_(flat)
+                else:
+                    tmp = torch.empty(g.shard, dtype=torch.float32, device=flat.device)
+                    dist.reduce_scatter_tensor(tmp, flat, group=self.pg)
+                    g.grad_shard.add_(tmp.div_(self.world))
         if self.world == 1:
             return
         if self.fused:
@@ -343,18 +503,41 @@ class ShardedAdamW:
         return self.norm[0]
 
     # ---- update ----------------------------------------------------------------------------
+    def _step_full_shard(self, g, lr, b1, b2):
+        """AdamW on a full-shard group: only this rank's shard changes (no all-gather)."""
+        if self.coef.is_cuda:
+            ext().adamw(g.shard_param(), g.master, g.shard_grad(), g.m, g.v, lr, b1, b2, self.eps, self.wd,
+                        self.step_count, self.coef)
+        else:
+            _adamw_torch(g.shard_param(), g.master, g.shard_grad(), g.m, g.v, lr, b1, b2, self.eps, self.wd,
+                         self.step_count, self.coef)
+
     def step(self):
         self.step_count += 1
         b1, b2 = self.betas
+        if not self._clipped and self.param_ring is not None:
+            self.coef.fill_(1.0)
         if self.fused:
             h = self.heap
             coef = self.coef if self._clipped else None
             for g, pg in zip(self.groups, self.param_groups):
+                if g.full_shard:
+                    self._step_full_shard(g, pg["lr"], b1, b2)
+                    continue
                 ext().symm_adamw_ag(g.flat_sym.ptrs, h.flags.ptrs, h.rank, h.next_epoch(2), g.lo, g.shard,
                                     g.grad_shard, g.master, g.m, g.v, pg["lr"], b1, b2, self.eps, self.wd,
                                     self.step_count, coef, h.done, h.err)
+            if self.param_ring is not None:
+                # no rank gathers a shard that a peer is still updating
+                ext().symm_barrier(h.flags.ptrs, h.rank, h.next_epoch(SHARD_CLOSE_SLOT), SHARD_CLOSE_SLOT, h.err)
+                self.param_ring.invalidate()
             return
+        if self.param_ring is not None:
+            self.param_ring.invalidate()
         for g, pg in zip(self.groups, self.param_groups):
+            if g.full_shard:
+                self._step_full_shard(g, pg["lr"], b1, b2)
+                continue
             lr = pg["lr"]
             if self.coef.is_cuda:
                 ext().adamw(g.shard_param(), g.master, g.shard_grad(), g.m, g.v, lr, b1, b2, self.eps, self.wd,
@@ -364,6 +547,8 @@ class ShardedAdamW:
                              self.step_count, self.coef)
         if self.world > 1:
             for g in self.groups:
+                if g.full_shard:
+                    continue
                 # in place: this rank's input is its own slice of the output buffer
                 dist.all_gather_into_tensor(g.flat, g.flat[g.lo:g.hi], group=self.pg)
 
