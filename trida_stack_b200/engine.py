@@ -39,14 +39,15 @@ class TrainEngine:
     def __init__(self, model, lr=1e-5, betas=(0.9, 0.95), weight_decay=0.0, grad_clip=1.0, fp32_master=False,
                  warmup=50, max_steps=2000, lr_min_ratio=0.1, projector_lr_scale=0.1, decision_head_lr_scale=1.0,
                  device=None, comm="nccl", grad_stream=False, full_shard=False, keep_params=False):
-        """``full_shard``: decoder-layer weights sharded across ranks and gathered per layer
-        (implies per-layer gradient streaming); ``keep_params`` keeps gathered weights from
-        forward to backward."""
+        """``full_shard``: decoder-layer weights sharded across ranks and gathered per layer;
+        ``keep_params`` keeps gathered weights from forward to backward; ``grad_stream``: fp32
+        gradients of one layer at a time (a two-slot ring reduced under backward) instead of
+        resident gradient buffers."""
         self.model = model
         self.device = device or next(model.parameters()).device
         groups = model.param_groups(projector_lr_scale=projector_lr_scale,
                                     decision_head_lr_scale=decision_head_lr_scale,
-                                    per_layer=grad_stream or full_shard)
+                                    per_layer=grad_stream or full_shard, stream=grad_stream)
         self.optim = ShardedAdamW(groups, lr=lr, betas=betas, weight_decay=weight_decay, fp32_master=fp32_master,
                                   device=self.device, comm=comm, full_shard=full_shard, keep_params=keep_params)
         model.param_ring = self.optim.param_ring

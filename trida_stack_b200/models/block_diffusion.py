@@ -80,12 +80,13 @@ class BlockDiffusionLM(nn.Module):
     def cfg(self):
         return self.decoder.cfg
 
-    def param_groups(self, projector_lr_scale=1.0, decision_head_lr_scale=1.0, per_layer=False):
+    def param_groups(self, projector_lr_scale=1.0, decision_head_lr_scale=1.0, per_layer=False, stream=True):
         """Optimizer groups tagged with ``lr_scale`` (order: backbone, projector, decision head --
         the reference's frozen group order, ``block_diffusion.py:180-201``).  ``per_layer`` splits
-        the backbone into the non-layer parameters plus one group per decoder layer, tagged
-        ``stream`` (gradients streamed through a two-slot ring, for models whose full fp32
-        gradients do not fit next to the optimizer state)."""
+        the backbone into the non-layer parameters plus one group per decoder layer (tagged with
+        its ``layer`` index, the unit of full sharding), and with ``stream`` marks them for
+        gradients streamed through a two-slot ring (for models whose full fp32 gradients do not
+        fit next to the optimizer state)."""
         backbone, projector, head = [], [], []
         for name, p in self.named_parameters():
             if not p.requires_grad:
@@ -105,7 +106,7 @@ class BlockDiffusionLM(nn.Module):
             groups = [{"params": rest, "lr_scale": 1.0}]
             for i, layer in enumerate(self.decoder.layers):
                 groups.append({"params": [p for p in layer.parameters() if p.requires_grad], "lr_scale": 1.0,
-                               "stream": True, "layer": i})
+                               "stream": stream, "layer": i})
         else:
             groups = [{"params": backbone, "lr_scale": 1.0}]
         if projector:

@@ -21,7 +21,8 @@ def build_optimizer(args, model, device=None):
     from .distributed import world_size
     full = getattr(args, "shard", "full") == "full" and world_size() > 1
     groups = model.param_groups(projector_lr_scale=args.projector_lr_scale,
-                                decision_head_lr_scale=args.decision_head_lr_scale, per_layer=full)
+                                decision_head_lr_scale=args.decision_head_lr_scale, per_layer=full,
+                                stream=getattr(args, "grad_stream", False))
     opt = ShardedAdamW(groups, lr=args.lr, betas=(0.9, args.adam_beta2), weight_decay=args.weight_decay,
                        fp32_master=getattr(args, "fp32_master", False), device=device,
                        comm=getattr(args, "comm", "nccl"), full_shard=full,

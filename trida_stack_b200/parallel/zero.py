@@ -21,6 +21,8 @@ next layer on a side stream while the current one computes) and drops it afterwa
 backward -- unless ``keep_params`` keeps the gathered weights from forward to backward (the
 reference's ``--fsdp_keep_params``).  The update then touches only the local shard.
 """
+import os
+
 import torch
 import torch.distributed as dist
 
@@ -28,6 +30,7 @@ from ..ops._ext import ext
 from .symm import RING_CLOSE_SLOT, SHARD_CLOSE_SLOT
 
 ALIGN = 64
+GATHER_ENGINE = os.environ.get("TRIDA_GATHER", "copy")    # full-shard gathers: copy engines or a P2P kernel
 
 
 def _world():
@@ -61,15 +64,15 @@ class FlatGroup:
         elif heap is not None:
             self.flat_sym = heap.alloc(self.padded, dtype)
             self.flat = self.flat_sym.local
-            if not stream:
-                self.grad_sym = heap.alloc(self.padded, torch.float32)
-                self.grad = self.grad_sym.local
         else:
             self.flat = torch.zeros(self.padded, dtype=dtype, device=device)
-            if not stream:
+        self.grad = None
+        if not stream:
+            if heap is not None:
+                self.grad_sym = heap.alloc(self.padded, torch.float32)
+                self.grad = self.grad_sym.local
+            else:
                 self.grad = torch.zeros(self.padded, dtype=torch.float32, device=device)
-        if stream:
-            self.grad = None
         off = 0
         self.offsets = []
         with torch.no_grad():
@@ -247,8 +250,10 @@ class ParamRing:
     tensors themselves) every layer gets its own buffer and a gather stays valid until the next
     optimizer step (weights kept from forward to backward).
 
-    A gather is one ``symm_gather`` kernel (P2P loads of every rank's shard over NVLink) with the
-    fused collectives, ``all_gather_into_tensor`` otherwise; on one rank nothing is gathered."""
+    With the fused collectives a gather is one peer-to-peer copy per rank's shard on the copy
+    engines (``symm_gather_copy``: no SM is taken from the compute it overlaps), or with
+    ``TRIDA_GATHER=kernel`` one ``symm_gather`` kernel of P2P loads; ``all_gather_into_tensor``
+    otherwise; on one rank nothing is gathered."""
 
     GATHER_BLOCKS = 32     # CTAs of a gather kernel: enough for NVLink, few SMs taken from compute
 
@@ -256,7 +261,7 @@ class ParamRing:
         self.opt, self.map = opt, dict(layer_groups)
         self.groups = opt.groups
         first = self.groups[self.map[next(iter(self.map))]]
-        dev = first.grad_shard.device
+        dev = first.pshard.device
         self.keep = keep or dev.type != "cuda"
         size = max(self.groups[gi].padded for gi in self.map.values())
         nbuf = len(self.map) if self.keep else 2
@@ -278,7 +283,9 @@ class ParamRing:
 
     def _gather_into(self, g, dst):
         o = self.opt
-        if o.fused:
+        if o.fused and GATHER_ENGINE == "copy":
+            ext().symm_gather_copy(g.shard_sym.ptrs, o.rank, g.shard, dst)
+        elif o.fused:
             ext().symm_gather(g.shard_sym.ptrs, o.rank, g.shard, dst, self.GATHER_BLOCKS)
         else:
             dist.all_gather_into_tensor(dst, g.pshard, group=o.pg)
@@ -380,11 +387,11 @@ class ShardedAdamW:
         groups = [g for g in groups if g["params"]]
         self.groups = [FlatGroup(g["params"], g.get("lr_scale", 1.0), self.world, self.rank, fp32_master, device,
                                  self.heap, stream=bool(g.get("stream")),
-                                 full_shard=full_shard and bool(g.get("stream")))
+                                 full_shard=full_shard and "layer" in g)
                        for g in groups]
         self.param_ring = None
         if full_shard:
-            layer_groups = {gg["layer"]: i for i, gg in enumerate(groups) if gg.get("stream")}
+            layer_groups = {gg["layer"]: i for i, gg in enumerate(groups) if "layer" in gg}
             if not layer_groups:
                 raise ValueError("full_shard needs per-layer parameter groups (param_groups(per_layer=True))")
             self.param_ring = ParamRing(self, layer_groups, keep=keep_params)
