@@ -4,17 +4,24 @@ Model: Qwen3.5-4B-style hybrid (32 layers: 3 gated-delta then 1 full attention, 
 9216, vocab 248320, full layers 16 Q / 4 KV x 256 with output gate and partial RoPE, gated-delta
 16 key / 32 value heads x 128, conv 4), random init, bf16.  Rows [prompt 2048 | response 1024]
 run as the two-stream layout [x0 ; xt_1 ; xt_2] (9216 forward tokens per row), block size 32,
-diffusion + AR loss; joint training with the typed-decision pointer head: every 4th step adds a
-decision micro-step (a packed causal row of 2-4-option questions, loss weight 0.5).  Synthetic
-uniform tokens.  Launch like ``bench.py`` (torchrun for N > 1); prints one JSON line.
+diffusion + AR loss; joint training with the typed-decision pointer head: 25% of the rows (every
+fourth row) carry a question over 2-4 option positions with a uniform random label, whose pointer
+loss (weight 0.5) joins that row's loss in the same forward.  Synthetic uniform tokens.  Launch like
+``bench.py`` (torchrun for N > 1); prints one JSON line.
 
-    python bench_hybrid.py --steps 4 --warmup 3 [--mb 1] [--layers 32]
+``--linear-mode causal`` runs the reference's other hybrid objective instead (the dense [S | x_t |
+x_0] row; the linear layers scan [S | x_t] and [x_0] as two causal documents; no pointer rows), and
+``--impl reference --linear-mode causal`` times the unmodified reference trainer on it
+(``HFBlockDiffusionHybrid`` from ``baseline/_ref`` with its flex-attention mask and FLA's chunked
+gated-delta kernels; the short conv falls back to PyTorch since causal-conv1d is not installed).
+
+    python bench_hybrid.py --steps 4 --warmup 3 [--mb 1] [--layers 32] [--linear-mode causal]
 """
 import argparse
 import json
 import os
 import sys
-import time
+import tempfile
 
 import torch
 import torch.distributed as dist
@@ -25,87 +32,81 @@ sys.path.insert(0, ROOT)
 PROMPT, RESP, BD, VOCAB = 2048, 1024, 32, 248320
 
 
+def hybrid_hf_dict(layers):
+    return {"model_type": "qwen3_5_text", "vocab_size": VOCAB, "hidden_size": 2560, "intermediate_size": 9216,
+            "num_hidden_layers": layers, "num_attention_heads": 16, "num_key_value_heads": 4, "head_dim": 256,
+            "linear_num_key_heads": 16, "linear_num_value_heads": 32, "linear_key_head_dim": 128,
+            "linear_value_head_dim": 128, "linear_conv_kernel_dim": 4, "partial_rotary_factor": 0.25,
+            "rope_theta": 1e7, "layer_types": (["linear_attention"] * 3 + ["full_attention"]) * (layers // 4),
+            "tie_word_embeddings": True, "rms_norm_eps": 1e-6}
+
+
 def hybrid_cfg(layers):
     from trida_stack_b200.models.config import ModelConfig
-    return ModelConfig.from_hf_dict({
-        "model_type": "qwen3_5_text", "vocab_size": VOCAB, "hidden_size": 2560, "intermediate_size": 9216,
-        "num_hidden_layers": layers, "num_attention_heads": 16, "num_key_value_heads": 4, "head_dim": 256,
-        "linear_num_key_heads": 16, "linear_num_value_heads": 32, "linear_key_head_dim": 128,
-        "linear_value_head_dim": 128, "linear_conv_kernel_dim": 4, "partial_rotary_factor": 0.25,
-        "rope_theta": 1e7, "layer_types": (["linear_attention"] * 3 + ["full_attention"]) * (layers // 4),
-        "tie_word_embeddings": True, "rms_norm_eps": 1e-6})
+    return ModelConfig.from_hf_dict(hybrid_hf_dict(layers))
 
 
-def decision_batch(g, n_q=8, state=600):
-    """A packed causal row of n_q questions (2-4 options) over one random state."""
-    ids, seg, decide, opts, owner, questions = [], [], [], [], [], []
-    for qi in range(n_q):
+def pointer_rows(g, rows, L):
+    """A pointer question on every fourth row of the step (global row index ``rows[i]``): 2-4
+    option positions in the response, the decide position at the row's last token, a uniform
+    random label.  Returns the model's ``pointer`` argument (flat clean positions row * L + p)."""
+    decide, opts, owner, questions = [], [], [], []
+    for i, gr in enumerate(rows):
+        if gr % 4 != 3:
+            continue
         k = int(torch.randint(2, 5, (1,), generator=g))
-        base = len(ids)
-        row = torch.randint(0, VOCAB - 8, (state,), generator=g).tolist()
-        ends = []
-        for _ in range(k):
-            row += torch.randint(0, VOCAB - 8, (12,), generator=g).tolist()
-            ends.append(len(row) - 1)
-        row.append(VOCAB - 3)
-        ids += row
-        seg += [qi] * len(row)
-        decide.append(base + len(row) - 1)
+        pos = torch.randperm(RESP - 1, generator=g)[:k].sort().values + PROMPT
+        qi = len(questions)
         questions.append({"start": len(opts), "k": k, "label": int(torch.randint(0, k, (1,), generator=g)),
                           "variant": qi})
-        opts += [base + e for e in ends]
+        opts += [i * L + int(p) for p in pos]
         owner += [qi] * k
-    return {"input_ids": torch.tensor([ids]), "seg_id": torch.tensor([seg]), "decide": torch.tensor(decide),
-            "opts": torch.tensor(opts), "owner": torch.tensor(owner), "questions": questions}
+        decide.append(i * L + L - 1)
+    if not questions:
+        return None
+    return {"decide": torch.tensor(decide), "opts": torch.tensor(opts), "owner": torch.tensor(owner),
+            "questions": questions, "weight": 0.5}
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=4)
-    ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--mb", type=int, default=1)
-    ap.add_argument("--layers", type=int, default=32)
-    ap.add_argument("--comm", choices=["fused", "nccl"], default="fused")
-    ap.add_argument("--kernel-breakdown", type=int, default=0, metavar="STEPS",
-                    help="after the timed steps, print the per-kernel device-time table of STEPS more steps "
-                         "(taken under the PyTorch profiler; not a benchmark number)")
-    args = ap.parse_args()
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
-    from trida_stack_b200.engine import TrainEngine
-    from trida_stack_b200.models import Decoder
-    from trida_stack_b200.models.hybrid import HybridBlockDiffusionLM
-    from trida_stack_b200.ops._ext import ext
-    ext()
+def write_reference_checkpoint(path, layers):
+    """Random-init HF Qwen3.5 hybrid checkpoint of the config-3 shape + a word-level tokenizer whose
+    length, after the reference adds <|mask|>, is the 248320-token vocabulary."""
+    from tokenizers import Tokenizer, models, pre_tokenizers
+    from transformers import PreTrainedTokenizerFast
+    from transformers.models.qwen3_5 import Qwen3_5ForCausalLM, Qwen3_5TextConfig
+    d = hybrid_hf_dict(layers)
+    n = VOCAB - 1
+    d.pop("model_type")
+    rope = {"rope_theta": d.pop("rope_theta"), "rope_type": "default",
+            "partial_rotary_factor": d.pop("partial_rotary_factor")}
+    cfg = Qwen3_5TextConfig(**{**d, "vocab_size": n, "rope_parameters": rope, "max_position_embeddings": 32768})
     torch.manual_seed(0)
-    dec = Decoder(hybrid_cfg(args.layers), dtype=torch.bfloat16, device="cuda")
-    model = HybridBlockDiffusionLM(dec, mask_id=VOCAB - 1, pad_id=VOCAB - 2, bd_size=BD, ar_loss_weight=1.0,
-                                   decision_head_dim=256)
-    model.train()
-    engine = TrainEngine(model, lr=1e-5, warmup=50, max_steps=2000, device=torch.device("cuda"), comm=args.comm)
+    with torch.device("cuda"):
+        model = Qwen3_5ForCausalLM(cfg).to(torch.bfloat16)
+    model.save_pretrained(path)
+    del model
+    vocab = {f"t{i}": i for i in range(n - 1)}
+    vocab["<|endoftext|>"] = n - 1
+    tok = Tokenizer(models.WordLevel(vocab=vocab, unk_token="<|endoftext|>"))
+    tok.pre_tokenizer = pre_tokenizers.WhitespaceSplit()
+    PreTrainedTokenizerFast(tokenizer_object=tok, eos_token="<|endoftext|>",
+                            pad_token="<|endoftext|>").save_pretrained(path)
+
+
+def synthetic(args, rank, with_pointer):
     g = torch.Generator().manual_seed(1234 + rank)
-    batches, dec_batches = [], []
-    for _ in range(args.warmup + args.steps):
+    batches, pointers = [], []
+    for step in range(args.warmup + args.steps):
         ids = torch.randint(0, VOCAB - 8, (args.mb, PROMPT + RESP), generator=g)
         labels = ids.clone()
         labels[:, :PROMPT] = -100
-        batches.append({"input_ids": ids.cuda(), "labels": labels.cuda(), "attention_mask": torch.ones_like(ids).cuda()})
-        dec_batches.append({k: (v.cuda() if torch.is_tensor(v) else v) for k, v in decision_batch(g).items()})
+        batches.append({"input_ids": ids, "labels": labels, "attention_mask": torch.ones_like(ids)})
+        rows = [step * args.mb + i for i in range(args.mb)]
+        pointers.append(pointer_rows(g, rows, PROMPT + RESP) if with_pointer else None)
+    return batches, pointers
 
-    def step_fn(i, step):
-        engine.micro_step(batches[i])
-        if i % 4 == 3:           # 25% of steps add a decision micro-step (weight 0.5)
-            loss, _ = model(None, None, None, decision=dec_batches[i])
-            (0.5 * loss).backward()
-        engine.optimizer_step(step)
 
+def timed(step_fn, args, world):
     for i in range(args.warmup):
         step_fn(i, i)
     torch.cuda.synchronize()
@@ -123,18 +124,39 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = t.item()
         dist.barrier()
-    if rank == 0:
-        toks = world * args.mb * (PROMPT + RESP)
-        print(json.dumps({
-            "metric": "4B hybrid two-stream block-diffusion SFT tokens/s", "value": round(toks / (ms / 1e3), 1),
-            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms, 2), "higher_is_better": True, "scaling": "weak", "dtype": "bf16",
-            "data": "synthetic uniform token ids, random-init weights",
-            "peak_mem_gb": round(torch.cuda.max_memory_allocated() / 1e9, 1),
-            "config": {"model": f"Qwen3.5-4B-style hybrid ({args.layers}L)", "micro_batch": args.mb,
-                       "row": "[prompt 2048 | response 1024] as [x0 ; xt_1 ; xt_2] (9216 forward tokens)",
-                       "bd_size": BD, "decision": "pointer head, every 4th step, weight 0.5",
-                       "parallelism": f"dp{world}"}}), flush=True)
+    return ms
+
+
+def run_ours(args, world, rank):
+    from trida_stack_b200.engine import TrainEngine
+    from trida_stack_b200.models import Decoder
+    from trida_stack_b200.models.hybrid import HybridBlockDiffusionLM
+    from trida_stack_b200.ops._ext import ext
+    ext()
+    torch.manual_seed(0)
+    dec = Decoder(hybrid_cfg(args.layers), dtype=torch.bfloat16, device="cuda")
+    causal = args.linear_mode == "causal"
+    model = HybridBlockDiffusionLM(dec, mask_id=VOCAB - 1, pad_id=VOCAB - 2, bd_size=BD, ar_loss_weight=1.0,
+                                   decision_head_dim=0 if causal else 256, linear_block_mode=args.linear_mode)
+    model.train()
+    engine = TrainEngine(model, lr=1e-5, warmup=50, max_steps=2000, device=torch.device("cuda"), comm=args.comm,
+                         full_shard=args.shard == "full" and world > 1)
+    batches, pointers = synthetic(args, rank, not causal)
+    rpad = RESP if causal else None
+    dev_batches = []
+    for b, p in zip(batches, pointers):
+        db = {k: v.cuda() for k, v in b.items()}
+        if p is not None:
+            db["pointer"] = {k: (v.cuda() if torch.is_tensor(v) else v) for k, v in p.items()}
+        dev_batches.append(db)
+
+    def step_fn(i, step):
+        b = dev_batches[i]
+        loss, _ = model(b["input_ids"], b["labels"], b["attention_mask"], pointer=b.get("pointer"), rpad=rpad)
+        loss.backward()
+        engine.optimizer_step(step)
+
+    ms = timed(step_fn, args, world)
     if args.kernel_breakdown > 0 and rank == 0 and world == 1:
         from trida_stack_b200.utils.trace import kernel_breakdown
         i0 = args.warmup + args.steps
@@ -142,10 +164,108 @@ def main():
 
         def one():
             j = next(extra)
-            engine.micro_step(batches[(i0 + j) % len(batches)])
-            engine.optimizer_step(i0 + j)
+            step_fn((i0 + j) % len(dev_batches), i0 + j)
         kernel_breakdown(one, args.kernel_breakdown)
+    return ms
+
+
+def run_reference(args, world, rank):
+    if args.linear_mode != "causal":
+        raise RuntimeError("the reference's two-stream (bidirectional) kernels are fetched, not vendored: "
+                           "only --linear-mode causal has a reference arm")
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "train")):
+        raise FileNotFoundError("baseline/_ref/train missing (reference not installed)")
+    sys.path.insert(0, ref)
+    from train.cli import build_parser
+    from train.distributed import setup_distributed, shard_model
+    from train.models.build import build_model
+    from train.optimizer import apply_optimizer_step, build_optimizer
+    ckpt = os.environ.get("TRIDA_REF_HYBRID_CKPT") or os.path.join(tempfile.gettempdir(),
+                                                                    f"trida_ref_qwen35_l{args.layers}")
+    rargs = build_parser().parse_args([
+        "--model_id", ckpt, "--bd_size", str(BD), "--ar_loss_weight", "1.0", "--micro_batch_size", str(args.mb),
+        "--grad_accum", "1", "--lr", "1e-5", "--max_length", str(PROMPT + RESP), "--response_buckets", "1024",
+        "--linear_block_mode", "causal", "--allow_slow_linear", "--seed", "0"])
+    dev = setup_distributed(rargs)
+    if rank == 0 and not os.path.exists(os.path.join(ckpt, "config.json")):
+        write_reference_checkpoint(ckpt, args.layers)
     if world > 1:
+        dist.barrier()
+    model = build_model(rargs)
+    shard_model(model, rargs)
+    optim = build_optimizer(rargs, model)
+    batches, _ = synthetic(args, rank, False)
+    dev_batches = [{k: v.to(dev) for k, v in b.items()} for b in batches]
+
+    def step_fn(i, step):
+        b = dev_batches[i]
+        model.set_requires_gradient_sync(True)
+        loss, _ = model(b["input_ids"], b["labels"], b["attention_mask"])
+        loss.backward()
+        apply_optimizer_step(model, optim, step, rargs)
+
+    return timed(step_fn, args, world)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--mb", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--linear-mode", dest="linear_mode", choices=["bidirectional", "causal"], default="bidirectional",
+                    help="bidirectional: the two-stream objective (config 3); causal: region-split causal linear layers")
+    ap.add_argument("--shard", choices=["full", "zero2"], default="full")
+    ap.add_argument("--comm", choices=["fused", "nccl"], default="fused")
+    ap.add_argument("--kernel-breakdown", type=int, default=0, metavar="STEPS",
+                    help="after the timed steps, print the per-kernel device-time table of STEPS more steps "
+                         "(taken under the PyTorch profiler; not a benchmark number)")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if args.impl == "ours":
+        if world > 1:
+            import datetime
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local))
+        ms = run_ours(args, world, rank)
+    else:
+        for k, v in (("MASTER_ADDR", "127.0.0.1"), ("MASTER_PORT", "29533"), ("RANK", "0"), ("WORLD_SIZE", "1"),
+                     ("LOCAL_RANK", "0")):
+            os.environ.setdefault(k, v)
+        try:
+            ms = run_reference(args, world, rank)
+        except Exception as e:   # report, never fake a number
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": f"{type(e).__name__}: {e}"[:300]}))
+            if dist.is_initialized():
+                dist.destroy_process_group()
+            return
+    causal = args.linear_mode == "causal"
+    if rank == 0:
+        toks = world * args.mb * (PROMPT + RESP)
+        line = {
+            "metric": "4B hybrid " + ("causal-mode" if causal else "two-stream") + " block-diffusion SFT tokens/s",
+            "value": round(toks / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True, "scaling": "weak",
+            "dtype": "bf16", "data": "synthetic uniform token ids, random-init weights",
+            "peak_mem_gb": round(torch.cuda.max_memory_allocated() / 1e9, 1),
+            "config": {"model": f"Qwen3.5-4B-style hybrid ({args.layers}L)", "micro_batch": args.mb,
+                       "row": ("[S 2048 | x_t 1024 | x_0 1024] x 2 views, linear layers on [S | x_t] and [x_0]"
+                               if causal else "[prompt 2048 | response 1024] as [x0 ; xt_1 ; xt_2] (9216 forward tokens)"),
+                       "bd_size": BD,
+                       "decision": ("none" if causal else
+                                    "pointer head on 25% of rows (2-4 options, uniform label), weight 0.5, same forward"),
+                       "parallelism": f"dp{world}" + (f" ({args.shard} shard)" if world > 1 else "")}}
+        if args.impl == "reference":
+            line["impl"] = "reference"
+        print(json.dumps(line), flush=True)
+    if dist.is_initialized():
         dist.destroy_process_group()
 
 

@@ -130,3 +130,62 @@ def test_block_bidirectional_reference_scan():
     o5, _ = G.gdn_block_bidirectional(q, k, v2, g, beta, blocks)
     assert torch.allclose(o5[:, :4], o4[:, :4])                    # earlier block untouched
     assert not torch.allclose(o5[:, 4], o4[:, 4])                  # same block: read-out sees the future
+
+
+def test_causal_mode_matches_reference(tmp_path):
+    """``linear_block_mode="causal"``: the dense [S | x_t | x_0] row with the block-diffusion mask on
+    the full-attention layers and region A / region B scanned as separate causal documents by the
+    linear layers -- the same loss as the reference's HFBlockDiffusionHybrid (torch fallbacks, dense
+    additive mask in place of flex-attention) on the same noise draws."""
+    from helpers import import_reference, make_tokenizer, patch_flex_for_cpu, reference_available
+    if not reference_available():
+        pytest.skip("reference not installed in baseline/_ref")
+    patch_flex_for_cpu()
+    import_reference()
+    from test_config1_cpu import dense_block_mask
+    from train.models.hybrid import HFBlockDiffusionHybrid
+    tiny_qwen35(str(tmp_path))
+    make_tokenizer(str(tmp_path), 300)
+    ref = HFBlockDiffusionHybrid(model_id=str(tmp_path), bd_size=8, ar_loss_weight=1.0, dtype=torch.float32,
+                                 response_buckets=None, linear_block_mode="causal", attn_impl="eager",
+                                 require_kernels=False)
+    ref._build_block_mask = dense_block_mask
+    ref.train()
+    cfg = ModelConfig.from_pretrained(str(tmp_path))
+    cfg.vocab_size = ref.model.get_input_embeddings().weight.shape[0]
+    dec = Decoder(cfg, dtype=torch.float32)
+    dec.load_hf_state_dict(ref.model.state_dict())
+    ours = HybridBlockDiffusionLM(dec, mask_id=ref.mask_id, bd_size=8, ar_loss_weight=1.0, response_buckets=None,
+                                  linear_block_mode="causal")
+    ours.train()
+    g = torch.Generator().manual_seed(5)
+    ids = torch.randint(0, 298, (2, 48), generator=g)
+    labels = ids.clone()
+    labels[:, :24] = -100
+    am = torch.ones_like(ids)
+    torch.manual_seed(11)
+    lr_, _ = ref(ids, labels, am)
+    torch.manual_seed(11)
+    lo, _ = ours(ids, labels, am)
+    assert abs(lo.item() - lr_.item()) <= 2e-4 * max(1.0, abs(lr_.item())), (lo.item(), lr_.item())
+
+
+def test_pointer_rows_in_two_stream_forward():
+    """Pointer-head questions on some rows of a two-stream batch: the head's loss joins the row's
+    block-diffusion loss in the same forward, and its gradient reaches the head and the stack."""
+    hf = tiny_qwen35()
+    m = HybridBlockDiffusionLM(native_from(hf), mask_id=299, bd_size=8, ar_loss_weight=1.0, decision_head_dim=16)
+    ids = torch.randint(0, 298, (2, 32))
+    labels = ids.clone()
+    labels[:, :12] = -100
+    L = 32
+    pointer = {"decide": torch.tensor([1 * L + 30]), "opts": torch.tensor([1 * L + 14, 1 * L + 20, 1 * L + 26]),
+               "owner": torch.tensor([0, 0, 0]), "weight": 0.5,
+               "questions": [{"start": 0, "k": 3, "label": 2, "variant": 0}]}
+    torch.manual_seed(4)
+    base, _ = m(ids, labels, torch.ones_like(ids))
+    torch.manual_seed(4)
+    loss, logs = m(ids, labels, torch.ones_like(ids), pointer=pointer)
+    loss.backward()
+    torch.testing.assert_close(loss.detach(), base.detach() + 0.5 * logs["decision_loss"])
+    assert m.jev_head.q.weight.grad is not None and m.jev_head.k.weight.grad.abs().sum() > 0

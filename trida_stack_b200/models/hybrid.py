@@ -54,7 +54,8 @@ class HybridBlockDiffusionLM(BlockDiffusionLM):
 
     # ----------------------------------------------------------------------------------------
     def forward(self, input_ids, labels, attention_mask, seg_id=None, resp_pos=None, resp_block=None,
-                turn_id=None, decision=None, rpad=None, pixel_values=None, image_grid_thw=None, mrope_pos=None):
+                turn_id=None, decision=None, rpad=None, pixel_values=None, image_grid_thw=None, mrope_pos=None,
+                pointer=None):
         if decision is not None:
             return self.forward_decision(decision)
         images = pixel_values is not None
@@ -65,9 +66,30 @@ class HybridBlockDiffusionLM(BlockDiffusionLM):
             return self.forward_ar(input_ids, labels, attention_mask, seg_id=seg_id)
         if self.linear_block_mode == "bidirectional":
             return self.forward_flare(input_ids, labels, attention_mask, seg_id=seg_id, turn_id=turn_id,
-                                      pixel_values=pixel_values, image_grid_thw=image_grid_thw, mrope_pos=mrope_pos)
-        raise NotImplementedError("hybrid causal-mode block diffusion (region-split linear layers) is not "
-                                  "available in this build; use --linear_block_mode bidirectional")
+                                      pixel_values=pixel_values, image_grid_thw=image_grid_thw, mrope_pos=mrope_pos,
+                                      pointer=pointer)
+        if seg_id is not None or resp_pos is not None or resp_block is not None:
+            raise NotImplementedError("hybrid causal mode covers single-turn unpacked rows (as the reference's)")
+        if pointer is not None:
+            raise NotImplementedError("pointer-head rows are trained with --linear_block_mode bidirectional")
+        # causal mode (``train/models/hybrid.py`` ``linear_block_mode="causal"``): the dense
+        # [S | x_t | x_0] row with the block-diffusion mask on the full-attention layers, while the
+        # linear layers scan region A = [S | x_t] and region B = [x_0] as two causal documents
+        self._region_split = input_ids.shape[1]
+        try:
+            return self.forward_single(input_ids, labels, attention_mask, rpad=rpad)
+        finally:
+            self._region_split = None
+
+    def make_actx(self, seg, opos, rblk, segid, view, pos, x0_token_causal, pos3=None):
+        actx = super().make_actx(seg, opos, rblk, segid, view, pos, x0_token_causal, pos3=pos3)
+        split = getattr(self, "_region_split", None)
+        if split is not None:
+            doc = torch.zeros(seg.shape, dtype=torch.bool, device=seg.device)
+            doc[:, 0] = True
+            doc[:, split] = True
+            actx.linear = LinearLayout("causal", doc_start=doc)
+        return actx
 
     def _flare_views(self, input_ids, labels, answer, eps=1e-3):
         B, L = input_ids.shape
@@ -114,7 +136,11 @@ class HybridBlockDiffusionLM(BlockDiffusionLM):
         return x.index_put((where,), feats.index_select(0, fidx[where]))
 
     def forward_flare(self, input_ids, labels, attention_mask, seg_id=None, turn_id=None, pixel_values=None,
-                      image_grid_thw=None, mrope_pos=None):
+                      image_grid_thw=None, mrope_pos=None, pointer=None):
+        """Two-stream objective.  ``pointer`` (optional) trains the decision head on some of the same
+        rows: ``decide`` / ``opts`` are clean-stream positions ``row * L + p``, ``owner`` the question
+        of each option, ``questions`` the per-question records of ``decision_loss`` and ``weight``
+        the loss weight; the pointer loss is added to the row's block-diffusion loss."""
         dev = input_ids.device
         B, L = input_ids.shape
         assert L % self.bd_size == 0, "two-stream rows must be a multiple of bd_size (collator bucket)"
@@ -181,7 +207,19 @@ class HybridBlockDiffusionLM(BlockDiffusionLM):
         with torch.no_grad():
             diff = torch.dot(ce[:n_diff], w_diff) if n_diff else torch.zeros((), device=dev)
             ar = ce[n_diff:].mean() if n_ar else torch.zeros((), device=dev)
-        return loss, {"diff_loss": diff, "ar_loss": ar, "ntok": n_diff}
+        logs = {"diff_loss": diff, "ar_loss": ar, "ntok": n_diff}
+        if pointer is not None and pointer["questions"]:
+            if self.decision_head is None:
+                raise RuntimeError("pointer rows given but the model has no decision head (decision_head_dim=0)")
+
+            def clean(flat):          # clean-stream position row * L + p -> hidden row row * T + p
+                return (flat // L) * T + flat % L
+            z = self.decision_head(hidden.index_select(0, clean(pointer["decide"])),
+                                   hidden.index_select(0, clean(pointer["opts"])), pointer["owner"])
+            dloss, acc = decision_loss(z, pointer)
+            loss = loss + pointer.get("weight", 1.0) * dloss
+            logs.update(decision_loss=dloss.detach(), decision_acc=acc)
+        return loss, logs
 
     # ----------------------------------------------------------------------------------------
     def _causal_rows(self, input_ids, seg_id, valid=None):
