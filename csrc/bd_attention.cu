@@ -383,9 +383,11 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const bf16* __restrict__ 
         const int64_t bt = row / Hq;
         const int t = (int)(bt % T), b = (int)(bt / T);
         if (j == 0) dsum[((int64_t)b * Hq + h) * T + t] = acc;
-        float* q = dq_acc + row * D + j * 8;
-        reinterpret_cast<float4*>(q)[0] = z;
-        reinterpret_cast<float4*>(q)[1] = z;
+        if (dq_acc != nullptr) {   // the head_dim 256 tcgen05 backward writes dq without an accumulator
+          float* q = dq_acc + row * D + j * 8;
+          reinterpret_cast<float4*>(q)[0] = z;
+          reinterpret_cast<float4*>(q)[1] = z;
+        }
         if (dk_acc != nullptr && h % group == 0) {
           const int64_t kr = (bt * Hkv + h / group) * D + j * 8;
           reinterpret_cast<float4*>(dk_acc + kr)[0] = z;
@@ -765,7 +767,7 @@ void bd_attn_bwd_prep(const AttnTensors& t, const bf16* dout, int64_t do_tok, in
   }
   attn::bwd_dsum_kernel<<<ceil_div(rows, 8), 256, 0, s>>>(t.o, t.o_tok, t.o_b, dout, do_tok, do_b, dsum, t.B, t.T,
                                                            t.Hq, t.D);
-  cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * t.D, s);
+  if (dq_acc != nullptr) cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * t.D, s);
   if (dk_acc != nullptr) {
     cudaMemsetAsync(dk_acc, 0, sizeof(float) * (int64_t)t.B * t.T * t.Hkv * t.D, s);
     cudaMemsetAsync(dv_acc, 0, sizeof(float) * (int64_t)t.B * t.T * t.Hkv * t.D, s);

@@ -791,8 +791,35 @@ void bd_attn_bwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tenso
                        const at::Tensor& dv, const at::Tensor& meta, const at::Tensor& list128t,
                        const at::Tensor& cnt128t, const at::Tensor& colmask, int64_t flags, double scale,
                        const at::Tensor& err,
-                       const c10::optional<at::Tensor>& dbg) {
+                       const c10::optional<at::Tensor>& dbg,
+                       const c10::optional<at::Tensor>& list128, const c10::optional<at::Tensor>& cnt128,
+                       const c10::optional<at::Tensor>& rowmask) {
   auto a = attn_tensors(q, k, v, o, lse);
+  if (a.D == 256) {
+    // dK / dV kernel over the transposed lists + dQ kernel over the forward lists (bf16 dq directly)
+    TORCH_CHECK(list128.has_value() && cnt128.has_value() && rowmask.has_value(),
+                "head_dim 256 backward needs the forward tile lists and row masks");
+    for (auto* t : {&dout, &dq, &dk, &dv})
+      TORCH_CHECK(t->dim() == 4 && t->stride(3) == 1 && t->stride(2) == t->size(3), "attention grad layout");
+    for (auto* t : {&dout, &dq})
+      TORCH_CHECK((t->stride(0) * 2) % 16 == 0 && (t->stride(1) * 2) % 16 == 0 && ((uintptr_t)t->data_ptr() % 16) == 0,
+                  "dout / dq must be TMA-compatible");
+    auto dsum = at::empty({a.B, a.Hq, a.T}, lse.options());
+    auto dkv_acc = at::empty({2, a.B, a.T, a.Hkv, a.D}, lse.options());
+    float* dk_acc = dkv_acc.data_ptr<float>();
+    float* dv_acc = dk_acc + (int64_t)a.B * a.T * a.Hkv * a.D;
+    trida::bd_attn_bwd_prep(a, cbf(dout), dout.stride(1), dout.stride(0), dsum.data_ptr<float>(), nullptr, dk_acc,
+                            dv_acc, sm_count(), stream());
+    const int rc = trida::bd_attn_bwd_d256(
+        a, cbf(dout), dout.stride(1), dout.stride(0), dsum.data_ptr<float>(), dk_acc, dv_acc, mbf(dq), dq.stride(1),
+        dq.stride(0), list128t.data_ptr<int16_t>(), cnt128t.data_ptr<int>(),
+        reinterpret_cast<const uint4*>(colmask.data_ptr<int>()), list128->data_ptr<int16_t>(), cnt128->data_ptr<int>(),
+        reinterpret_cast<const uint4*>(rowmask->data_ptr<int>()), (float)scale, err.data_ptr<int>(), stream());
+    TORCH_CHECK(rc == 0, "bd_attn_bwd_d256 failed (code ", rc, ")");
+    trida::bd_attn_dq_convert(dk_acc, mbf(dk), dk.stride(1), dk.stride(0), a.B, a.T, a.Hkv, a.D, sm_count(), stream());
+    trida::bd_attn_dq_convert(dv_acc, mbf(dv), dv.stride(1), dv.stride(0), a.B, a.T, a.Hkv, a.D, sm_count(), stream());
+    return;
+  }
   long long* pdbg = nullptr;
   if (dbg.has_value() && dbg->defined()) pdbg = reinterpret_cast<long long*>(dbg->data_ptr<int64_t>());
   for (auto* t : {&dout, &dq, &dk, &dv})
@@ -1035,7 +1062,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bd_attn_bwd_sm100", &bd_attn_bwd_sm100, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"),
         py::arg("lse"), py::arg("dout"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("meta"),
         py::arg("list128t"), py::arg("cnt128t"), py::arg("colmask"), py::arg("flags"), py::arg("scale"), py::arg("err"),
-        py::arg("dbg") = py::none());
+        py::arg("dbg") = py::none(), py::arg("list128") = py::none(), py::arg("cnt128") = py::none(),
+        py::arg("rowmask") = py::none());
   m.def("ce_rows", &ce_rows);
   m.def("grad_norm", &grad_norm);
   m.def("adamw", &adamw);

@@ -65,6 +65,14 @@ void bd_attn_tile_masks(const int4* meta, const uint8_t* cls, int B, int T, int 
                         cudaStream_t s);
 int bd_attn_fwd_sm100(const AttnTensors& t, const int4* meta, const int16_t* list128, const int* cnt128,
                       const uint4* rowmask, int flags, float scale, int* err, cudaStream_t s, long long* dbg = nullptr);
+// head_dim 256 (bd_attention_d256.cu): forward, and backward as a dK / dV kernel (fp32 partials
+// added into dk_acc / dv_acc, which must be zeroed) plus a dQ kernel writing bf16 dq directly
+int bd_attn_fwd_d256(const AttnTensors& t, const int16_t* list128, const int* cnt128, const uint4* rowmask,
+                     const int4* meta, int flags, float scale, int* err, cudaStream_t s);
+int bd_attn_bwd_d256(const AttnTensors& t, const bf16* dout, int64_t do_tok, int64_t do_b, const float* dsum,
+                     float* dk_acc, float* dv_acc, bf16* dq, int64_t dq_tok, int64_t dq_b, const int16_t* list128t,
+                     const int* cnt128t, const uint4* colmask, const int16_t* list128, const int* cnt128,
+                     const uint4* rowmask, float scale, int* err, cudaStream_t s);
 
 // ---- gated-delta-rule linear attention (gdn.cu) ----
 struct GdnParams {

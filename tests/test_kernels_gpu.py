@@ -216,7 +216,7 @@ def test_bd_attention_fwd_bwd(d, x0tok, wbc, packed):
     assert rel_err(dv, vr.grad) < 2e-2
 
 
-@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("d", [64, 128, 256])
 @pytest.mark.parametrize("x0tok,wbc,packed", [(True, False, False), (False, True, False), (True, False, True)])
 def test_bd_attention_fwd_tcgen05(d, x0tok, wbc, packed):
     torch.manual_seed(0)
@@ -247,9 +247,11 @@ def test_bd_attention_fwd_tcgen05(d, x0tok, wbc, packed):
     assert (lse - lse2).abs().max().item() < 1e-2
 
 
-@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("d", [64, 128, 256])
 @pytest.mark.parametrize("x0tok,wbc,packed", [(True, False, False), (False, True, False), (True, False, True)])
 def test_bd_attention_bwd_tcgen05(d, x0tok, wbc, packed):
+    """head_dim 64 / 128: one kernel per (key tile, query head) with TMA-reduced fp32 dQ; head_dim
+    256: a dK / dV kernel per half of d plus a dQ kernel over the forward tile lists."""
     torch.manual_seed(0)
     B, P, Rr, bd, Hq, Hkv = 2, 160, 192, 32, 4, 2   # T = 544: ragged last 128-tile
     meta = bd_layout(B, P, Rr, bd, "cuda", packed)
@@ -275,8 +277,12 @@ def test_bd_attention_bwd_tcgen05(d, x0tok, wbc, packed):
     dk = torch.full_like(k, float("nan"))
     dkv = torch.zeros_like(kv)
     dv = dkv[:, :, Hkv:]
+    extra = {}
+    if d == 256:
+        l128, c128 = actx.plan128
+        extra = {"list128": l128, "cnt128": c128, "rowmask": actx.masks[0]}
     C().bd_attn_bwd_sm100(q, k, v, o, lse, do, dq, dk, dv, actx.meta, lt, ct, actx.masks[1], actx.flags, scale,
-                          device_error_word("cuda"))
+                          device_error_word("cuda"), **extra)
     torch.cuda.synchronize()
     check_device_errors()
     assert torch.isfinite(dq).all() and torch.isfinite(dk).all() and torch.isfinite(dv).all()

@@ -53,7 +53,7 @@ def check_device_errors():
 
 def use_tcgen05_attention(head_dim, which="FWD"):
     import os
-    return head_dim in (64, 128) and os.environ.get(f"TRIDA_ATTN_{which}", "tcgen05") == "tcgen05"
+    return head_dim in (64, 128, 256) and os.environ.get(f"TRIDA_ATTN_{which}", "tcgen05") == "tcgen05"
 
 
 def gemm(layout, a, b, d, c=None, alpha=1.0, beta=0.0, tile=0):
@@ -192,8 +192,12 @@ def attn_bwd(q, k, v, o, lse, do, dq, dk, dv, actx):
     d = q.shape[-1]
     if use_tcgen05_attention(d, "BWD"):
         lt, ct = actx.plan128t
+        extra = {}
+        if d == 256:   # the dQ kernel walks the forward lists with the row masks
+            l128, c128 = actx.plan128
+            extra = {"list128": l128, "cnt128": c128, "rowmask": actx.masks[0]}
         ext().bd_attn_bwd_sm100(q, k, v, o, lse, do, dq, dk, dv, actx.meta, lt, ct, actx.masks[1], actx.flags,
-                                1.0 / math.sqrt(d), device_error_word(q.device))
+                                1.0 / math.sqrt(d), device_error_word(q.device), **extra)
     else:
         _, _, _, bl, bc = actx.plan
         ext().bd_attn_bwd(q, k, v, o, lse, do, dq, dk, dv, actx.meta, bl, bc, actx.flags, 1.0 / math.sqrt(d))

@@ -1,7 +1,7 @@
 """Kernel microbenchmarks on the benchmark configs' shapes (device-timed with CUDA events).
 
     python -m trida_stack_b200.ops.kernel_bench --op gemm [--m 24576 --n 6144 --k 2560 --layout tn]
-    python -m trida_stack_b200.ops.kernel_bench --op attn_fwd|attn_bwd [--rows 4]
+    python -m trida_stack_b200.ops.kernel_bench --op attn_fwd|attn_bwd [--rows 4] [--heads 32 --kv-heads 8 --head-dim 128]
     python -m trida_stack_b200.ops.kernel_bench --op gdn_fwd|gdn_bwd [--length 3072] [--gdn-path chunk|scan]
                                                      [--gdn-layout two_stream|causal]
     python -m trida_stack_b200.ops.kernel_bench --op gdn_core_fwd|gdn_core_bwd [--length 3072]
@@ -85,7 +85,7 @@ def bench_attn(a, backward):
     from . import blocks
     dev = "cuda"
     actx, T = _bd_actx(a.rows, 1024, 1024, 32, dev)
-    B, Hq, Hkv, d = a.rows, 32, 8, 128
+    B, Hq, Hkv, d = a.rows, a.heads, a.kv_heads, a.head_dim
     q = torch.randn(B, T, Hq, d, device=dev, dtype=torch.bfloat16)
     k = torch.randn(B, T, Hkv, d, device=dev, dtype=torch.bfloat16)
     v = torch.randn(B, T, Hkv, d, device=dev, dtype=torch.bfloat16)
@@ -281,6 +281,7 @@ def main():
     ap.add_argument("--ffn", type=int, default=9728)
     ap.add_argument("--heads", type=int, default=32)
     ap.add_argument("--kv-heads", type=int, default=8)
+    ap.add_argument("--head-dim", dest="head_dim", type=int, default=128, help="attention head dim (64 / 128 / 256)")
     ap.add_argument("--rows", type=int, default=4, help="attention: forward rows (2 views x micro-batch)")
     ap.add_argument("--length", type=int, default=3072, help="gated delta: stream length L")
     ap.add_argument("--gdn-path", dest="gdn_path", default="chunk", choices=["chunk", "scan"],
