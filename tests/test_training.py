@@ -206,3 +206,36 @@ def test_kernel_breakdown_runs_and_reports(capsys):
     assert len(calls) == 3
     assert "kernel breakdown" in capsys.readouterr().err
     assert all(0.0 <= r[0] <= 1.0 for r in rows)
+
+
+def test_layer_checkpoint_and_offload_match_resident():
+    """Recomputing every layer in backward (``--activation_checkpoint layer``), with or without
+    ``--activation_offload``, gives the same update as keeping activations resident; ``auto``
+    keeps them resident when they fit (always on the host)."""
+    import copy
+
+    from trida_stack_b200.engine import TrainEngine
+    from trida_stack_b200.models import BlockDiffusionLM, Decoder, qwen3_config
+    torch.manual_seed(0)
+    cfg = qwen3_config(vocab_size=97, hidden_size=32, intermediate_size=64, num_layers=3, n_heads=2,
+                       n_kv_heads=1, head_dim=16)
+    dec = Decoder(cfg, dtype=torch.float32)
+    outs = []
+    for mode, offload in (("none", False), ("layer", False), ("layer", True), ("auto", True)):
+        m = BlockDiffusionLM(copy.deepcopy(dec), mask_id=96, pad_id=95, bd_size=4, ar_loss_weight=1.0,
+                             activation_checkpoint=mode, activation_offload=offload)
+        m.train()
+        eng = TrainEngine(m, lr=1e-2, warmup=0, max_steps=10, device=torch.device("cpu"))
+        g = torch.Generator().manual_seed(1)
+        torch.manual_seed(5)
+        for step in range(2):
+            ids = torch.randint(0, 95, (2, 16), generator=g)
+            labels = ids.clone()
+            labels[:, :8] = -100
+            eng.train_step([{"input_ids": ids, "labels": labels, "attention_mask": torch.ones_like(ids)}], step)
+        outs.append([p.detach().clone() for p in m.parameters()])
+    for other in outs[1:]:
+        for a, b in zip(outs[0], other):
+            torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6)
+    args = build_parser().parse_args(["--model_id", "x", "--activation_offload", "--activation_checkpoint", "layer"])
+    assert args.activation_offload and args.activation_checkpoint == "layer"

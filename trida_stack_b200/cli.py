@@ -53,7 +53,8 @@ def build_parser():
                    help="keep <think> reasoning on every assistant turn")
     p.add_argument("--pack", action="store_true", help="pack several documents per row (doc-isolated)")
     p.add_argument("--activation_offload", action="store_true",
-                   help="move checkpointed layer inputs to pinned host memory")
+                   help="with layer checkpointing active, keep each checkpointed layer's input in pinned "
+                        "host memory (copied on a side stream) until its backward")
     p.add_argument("--fused_ce", action="store_true",
                    help="accepted for compatibility: the CUDA path always uses the fused linear CE")
     p.add_argument("--fsdp_keep_params", action="store_true",

@@ -49,7 +49,7 @@ class BlockDiffusionLM(nn.Module):
                  pos_decay_gamma=0.0, full_mask=False, within_block_causal=False, mask_pattern="random",
                  response_buckets=(512, 1024, 2048, 4096), max_length=16384, max_response_length=4096,
                  merged_views=False, ar_only=False, activation_checkpoint="auto", ce_chunk=4096,
-                 tokenizer=None):
+                 tokenizer=None, activation_offload=False):
         super().__init__()
         assert loss_weighting in ("weighted", "uniform"), loss_weighting
         assert mask_pattern in ("random", "canvas"), mask_pattern
@@ -69,6 +69,8 @@ class BlockDiffusionLM(nn.Module):
         self.merged_views = merged_views
         self.ar_only = ar_only
         self.activation_checkpoint = activation_checkpoint
+        self.activation_offload = activation_offload
+        self._offload_pool = None
         self.ce_chunk = ce_chunk
         self.tokenizer = tokenizer
         self.is_vl = decoder.cfg.is_vl
@@ -135,9 +137,35 @@ class BlockDiffusionLM(nn.Module):
             actx.set_rope_angles(mrope_angles(pos3, c.rotary_dim, c.rope_theta, c.mrope_section))
         return actx
 
+    def _activations_fit(self, x):
+        """``activation_checkpoint="auto"``: do every layer's saved activations fit in the device
+        memory that is free now?  Per layer and token the block kernels keep about
+        4 D + 2 F + 2 (Hq + 2 Hkv) d bf16 values (the normed inputs, the q / k / v projections, the
+        attention output and the SwiGLU inputs), counted against 90 % of the free plus cached-unused
+        memory."""
+        if not x.is_cuda:
+            return True
+        c = self.cfg
+        per_tok = 4 * c.hidden_size + 2 * c.intermediate_size + 2 * (c.n_heads + 2 * c.n_kv_heads) * c.head_dim
+        need = x.shape[0] * per_tok * 2 * len(self.decoder.layers)
+        free = torch.cuda.mem_get_info(x.device)[0] + torch.cuda.memory_reserved(x.device) \
+            - torch.cuda.memory_allocated(x.device)
+        return need < 0.9 * free
+
     def run_stack(self, x, actx):
         mode = self.activation_checkpoint
-        ckpt = mode == "layer" and self.training and torch.is_grad_enabled()
+        train = self.training and torch.is_grad_enabled()
+        ckpt = train and (mode == "layer" or (mode == "auto" and not self._activations_fit(x)))
+        if ckpt and self.activation_offload:
+            # the checkpoint inputs (one [tokens, D] tensor per layer) wait in pinned host memory
+            from ..utils.offload import ActivationOffload, PinnedPool
+            if self._offload_pool is None:
+                self._offload_pool = PinnedPool()
+            with ActivationOffload(self._offload_pool):
+                return self._run_stack(x, actx, ckpt)
+        return self._run_stack(x, actx, ckpt)
+
+    def _run_stack(self, x, actx, ckpt):
         ring = getattr(self, "param_ring", None)
         if ring is None or not ring.active:
             if ckpt:

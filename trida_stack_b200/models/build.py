@@ -75,7 +75,8 @@ def build_model(args, device=None):
                   within_block_causal=args.within_block_causal, mask_pattern=args.mask_pattern,
                   response_buckets=parse_int_list(args.response_buckets), max_length=args.max_length,
                   max_response_length=args.max_response_length, merged_views=args.merged_views,
-                  ar_only=args.ar_only, activation_checkpoint=args.activation_checkpoint, tokenizer=tok)
+                  ar_only=args.ar_only, activation_checkpoint=args.activation_checkpoint, tokenizer=tok,
+                  activation_offload=getattr(args, "activation_offload", False))
     if dec.cfg.is_hybrid:
         from .hybrid import HybridBlockDiffusionLM
         log(f"[model] hybrid linear-attention decoder -> two-stream objective "
