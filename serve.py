@@ -124,6 +124,8 @@ def build(args):
                     max_steps=dcfg.get("max_steps"))
     if graphs:
         rt.use_graphs(tuple(int(b) for b in args.cuda_graph_bs.split()))
+    if decider is not None:
+        decider.gen_engine = engine      # reasoning-then-decide writes its reasoning with the same weights
     if not args.no_stats:
         engine.stats_interval = 10.0
     return engine, tok, name, decider

@@ -78,22 +78,58 @@ def test_chat_streaming(server):
 
 
 def test_systemone_decisions_and_validation(server):
-    body = {"state": {"user": "t1 t2"}, "questions": {
+    body = {"model": "m", "state": {"user": "t1 t2"}, "questions": {
         "q1": {"type": "choice", "instructions": "pick", "criteria": {"a": "t3", "b": "t4", "c": "t5"}},
         "q2": {"type": "noul", "criteria": {"true": "t6", "false": "t7"}},
         "q3": {"type": "score", "criteria": ["low", "mid", "high"]}}}
     r = requests.post(server + "/v1/systemone", json=body)
     assert r.status_code == 200, r.text
-    ans = r.json()["answers"]
-    assert ans["q1"]["choice"] in ("a", "b", "c")
-    assert abs(sum(ans["q1"]["probabilities"].values()) - 1) < 1e-4
-    assert isinstance(ans["q2"]["noul"], bool)
-    assert ans["q3"]["score"] in (0, 1, 2)
-    bad = requests.post(server + "/v1/systemone", json={"state": {}, "questions": {"q": {"type": "pick"}}})
+    out = r.json()
+    assert out["model"] and out["usage"]["input_tokens"] > 0 and out["usage"]["output_tokens"] == 0
+    ans = out["answers"]
+    assert ans["q1"]["type"] == "choice" and ans["q1"]["choice"] in ("a", "b", "c")
+    assert abs(sum(ans["q1"]["probabilities"].values()) - 1) < 1e-3
+    assert 0.0 <= ans["q1"]["confidence"] <= 1.0
+    assert ans["q2"]["type"] == "noul" and 0.0 <= ans["q2"]["noul"] <= 1.0
+    assert ans["q3"]["type"] == "score" and 0.0 <= ans["q3"]["score"] <= 2.0
+    assert ans["q3"]["legend"] == {"0": "low", "1": "mid", "2": "high"}
+    assert set(ans["q3"]["probabilities"]) == {"0", "1", "2"}
+    # a sharper temperature keeps the choice and moves its probability away from uniform
+    sharp = requests.post(server + "/v1/systemone", json={**body, "temperature": 0.05}).json()["answers"]
+    assert sharp["q1"]["choice"] == ans["q1"]["choice"]
+    assert sharp["q1"]["confidence"] >= ans["q1"]["confidence"] - 1e-4
+    bad = requests.post(server + "/v1/systemone", json={"model": "m", "state": {}, "questions": {"q": {"type": "pick"}}})
     assert bad.status_code == 422
     assert bad.json()["detail"][0]["loc"][-1] == "type"
-    alias = requests.post(server + "/v1/decide", json={"request": body})
+    assert requests.post(server + "/v1/systemone", json={k: v for k, v in body.items() if k != "model"}).status_code == 422
+    assert requests.post(server + "/v1/systemone", json={**body, "max_reasoning_tokens": 0}).status_code == 422
+    alias = requests.post(server + "/v1/decide", json={"request": {k: body[k] for k in ("state", "questions")}})
     assert alias.status_code == 200 and set(alias.json()["answers"]) == {"q1", "q2", "q3"}
+    assert alias.headers.get("Deprecation") == "true"
+    assert requests.post(server + "/v1/decide", json={"state": {}}).status_code == 400
+
+
+def test_systemone_concurrent_requests_share_forwards_and_reason(server):
+    """Concurrent requests are packed into shared forwards and answered as if scored alone;
+    reasoning first writes text with the generation engine and reports how it was used."""
+    from concurrent.futures import ThreadPoolExecutor
+    bodies = [{"model": "m", "state": {"user": f"t{i} t{i + 1}"}, "questions": {
+        "q": {"type": "choice", "criteria": {"a": "t3", "b": "t4"}},
+        "n": {"type": "noul"}}} for i in range(6)]
+    alone = [requests.post(server + "/v1/systemone", json=b).json()["answers"] for b in bodies]
+    with ThreadPoolExecutor(6) as ex:
+        together = [r.json()["answers"] for r in ex.map(lambda b: requests.post(server + "/v1/systemone", json=b),
+                                                          bodies)]
+    for a, b in zip(alone, together):
+        assert a["q"]["choice"] == b["q"]["choice"]
+        assert abs(a["n"]["noul"] - b["n"]["noul"]) < 1e-3
+    r = requests.post(server + "/v1/systemone", json={**bodies[0], "reasoning": True, "max_reasoning_tokens": 4})
+    assert r.status_code == 200, r.text
+    out = r.json()
+    assert "reasoning" in out and out["answers_source"] in ("direct", "reasoned")
+    assert out["usage"]["output_tokens"] <= 4
+    if out["answers_source"] == "direct":
+        assert out["cut"] in ("length", "empty", "state_limit")
 
 
 def test_eval_client_task_sweep_and_merge(server, tmp_path):
@@ -167,3 +203,22 @@ def test_chat_with_tools_request_path(server):
     res = score_case({"id": "simple_python_0", "function": funcs}, {"ground_truth": [{"lookup": {"city": ["x"]}}]},
                      msg)
     assert res["correct"] is False and res["category"] == "simple_python"
+
+
+def test_decision_answer_shapes_and_confidence():
+    from trida_stack_b200.serve.decide import confidence, systemone_response, to_answer, with_reasoning
+    assert abs(confidence("choice", [0.5, 0.25, 0.25]) - 0.25) < 1e-9
+    assert confidence("choice", [1 / 3] * 3) == 0.0 and confidence("choice", [1.0]) == 1.0
+    assert confidence("score", [0.0, 1.0, 0.0]) == 1.0
+    assert abs(confidence("score", [1 / 3] * 3)) < 1e-9
+    q = {"qtype": "score", "options": ["low", "high"], "keys": ["0", "1"]}
+    a = to_answer(q, [0.25, 0.75])
+    assert a == {"type": "score", "score": 0.75, "legend": ["low", "high"], "confidence": 0.5,
+                 "probabilities": {"0": 0.25, "1": 0.75}}
+    assert to_answer({"qtype": "noul", "options": [], "keys": ["false", "true"]}, [0.3, 0.7]) == \
+        {"type": "noul", "noul": 0.7}
+    r = systemone_response({"answers": {"s": a}, "usage": {"input_tokens": 9}, "timing_ms": 1.0}, "m")
+    assert r["answers"]["s"]["legend"] == {"0": "low", "1": "high"} and r["timing_ms"] == 1.0
+    assert r["usage"] == {"input_tokens": 9, "output_tokens": 0}
+    assert with_reasoning({"state": "x", "questions": {}}, "why")["state"] == {"situation": "x", "reasoning": "why"}
+    assert with_reasoning({"state": {"a": 1}, "questions": {}}, "why")["state"] == {"a": 1, "reasoning": "why"}

@@ -89,7 +89,7 @@ def build_app(engine, tokenizer, model_name, decider=None):
     from fastapi import FastAPI, Request as HTTPRequest
     from fastapi.responses import JSONResponse, StreamingResponse
 
-    from .decide import RequestError
+    from .decide import RequestError, systemone_request, systemone_response
     from .engine import Request, SamplingParams
 
     app = FastAPI()
@@ -197,26 +197,42 @@ def build_app(engine, tokenizer, model_name, decider=None):
 
         return StreamingResponse(gen(), media_type="text/event-stream")
 
-    async def _decide(body):
-        if decider is None:
-            return JSONResponse({"detail": "decisions need --mode decide and a decision checkpoint"}, status_code=400)
-        try:
-            out = await asyncio.get_running_loop().run_in_executor(None, decider.decide, body)
-        except RequestError as e:
-            return JSONResponse({"detail": e.detail()}, status_code=422)
-        return out
+    async def _decide(request, opts):
+        return await asyncio.get_running_loop().run_in_executor(
+            None, lambda: decider.decide(request, opts.get("temperature"), bool(opts.get("reasoning", False)),
+                                         opts.get("max_reasoning_tokens")))
+
+    def _no_decider():
+        return JSONResponse({"detail": "decisions need --mode decide and a decision checkpoint"}, status_code=400)
 
     @app.post("/v1/systemone")
     async def systemone(http: HTTPRequest):
+        if decider is None:
+            return _no_decider()
         body = await http.json()
-        out = await _decide(body)
-        if isinstance(out, dict):
-            out = {"model": body.get("model", model_name), **out}
-        return out
+        try:
+            request, opts = systemone_request(body, decider.reasoning_token_limit)
+            out = await _decide(request, opts)
+        except RequestError as e:
+            return JSONResponse({"detail": e.detail()}, status_code=422)
+        return systemone_response(out, model_name)
 
     @app.post("/v1/decide")
     async def decide_alias(http: HTTPRequest):
+        """Deprecated: ``{"request": {...}, "reasoning"?, "temperature"?, "max_reasoning_tokens"?}`` ->
+        the decision result itself (no System One envelope)."""
+        if decider is None:
+            return _no_decider()
         body = await http.json()
-        return await _decide(body.get("request", body))
+        headers = {"Deprecation": "true", "Link": '</v1/systemone>; rel="successor-version"'}
+        if not isinstance(body, dict) or "request" not in body:
+            return JSONResponse({"detail": 'body must be {"request": {...}, "reasoning"?: bool, "temperature"?: '
+                                           'float, "max_reasoning_tokens"?: int}'}, status_code=400, headers=headers)
+        opts = {k: body[k] for k in ("reasoning", "temperature", "max_reasoning_tokens") if body.get(k) is not None}
+        try:
+            out = await _decide(body["request"], opts)
+        except RequestError as e:
+            return JSONResponse({"detail": str(e)}, status_code=400, headers=headers)
+        return JSONResponse(out, headers=headers)
 
     return app
