@@ -222,3 +222,50 @@ def test_decision_answer_shapes_and_confidence():
     assert r["usage"] == {"input_tokens": 9, "output_tokens": 0}
     assert with_reasoning({"state": "x", "questions": {}}, "why")["state"] == {"situation": "x", "reasoning": "why"}
     assert with_reasoning({"state": {"a": 1}, "questions": {}}, "why")["state"] == {"a": 1, "reasoning": "why"}
+
+
+CHAT_TEMPLATE = ("{% for m in messages %}<|im_start|>{{ m['role'] }}\n{{ m['content'] }}<|im_end|>\n{% endfor %}"
+                 "{% if add_generation_prompt %}<|im_start|>assistant\n{% endif %}")
+
+
+def test_selfdistill_regenerates_assistant_turns(server, tmp_path):
+    """Self-distillation over the served engine: token-id prompts reach /v1/completions (a tiny random
+    model runs out of budget, so those conversations are dropped as truncated), and with a stand-in
+    completion every assistant turn is regenerated in order and round-trips."""
+    import asyncio
+
+    from trida_stack_b200.selfdistill import Distiller, select_rows
+    from helpers import make_tokenizer
+    tok = make_tokenizer(str(tmp_path / "tok"), 295)
+    tok.chat_template = CHAT_TEMPLATE
+    conv = {"id": "c", "messages": [{"role": "user", "content": "t1 t2"}, {"role": "assistant", "content": "t3"},
+                                    {"role": "user", "content": "t4"}, {"role": "assistant", "content": "t5 t6"}]}
+    src = tmp_path / "src"
+    src.mkdir()
+    (src / "chunk-000.jsonl").write_text("\n".join(json.dumps(dict(conv, id=str(i))) for i in range(6)) + "\n")
+    rows = list(select_rows(str(src), 2, 1, 2))
+    assert [r["id"] for r in rows] == ["2", "4"]
+    port = int(server.rsplit(":", 1)[1])
+    out = tmp_path / "o.jsonl"
+    d = Distiller(tok, [port], max_tokens=4, ctx_len=64, per_port=2, out=str(out))
+    d.max_tokens, d.ctx_len = 4, 64
+    with open(out, "w") as fo:
+        st = asyncio.run(d.run(rows, fo))
+    assert st["conv"] == 2 and st["errors"] == 0 and st["kept"] + st["truncated"] == 2
+
+    seen = []
+
+    async def fake_complete(sess, sems, prompt_ids):
+        seen.append(list(prompt_ids))
+        text = f"t{7 + len(seen)} t9"
+        return text, "stop", tok(text, add_special_tokens=False).input_ids
+    d2 = Distiller(tok, [port], out=str(out))
+    d2.complete = fake_complete
+    with open(out, "w") as fo:
+        st = asyncio.run(d2.run([conv], fo))
+    res = json.loads(out.read_text().splitlines()[0])
+    assert st["kept"] == 1 and st["turns"] == 2
+    assert res["messages"][1]["content"].endswith("t8 t9") and res["messages"][3]["content"].endswith("t9 t9")
+    assert res["messages"][2]["content"] == "t4"
+    # the second prompt holds the regenerated first turn, not the original
+    assert tok("t8", add_special_tokens=False).input_ids[0] in seen[1]

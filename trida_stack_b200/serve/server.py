@@ -136,11 +136,18 @@ def build_app(engine, tokenizer, model_name, decider=None):
     @app.post("/v1/completions")
     async def completions(http: HTTPRequest):
         body = await http.json()
-        ids = tokenizer(body.get("prompt", ""), add_special_tokens=False).input_ids
+        prompt = body.get("prompt", "")
+        if isinstance(prompt, list) and all(isinstance(t, int) for t in prompt):
+            ids = list(prompt)                    # token-id prompt (OpenAI completions allows it)
+        else:
+            ids = tokenizer(prompt, add_special_tokens=False).input_ids
         req = await run(ids, body)
         text = tokenizer.decode(req.output)
+        choice = {"index": 0, "text": text, "finish_reason": req.finish_reason}
+        if body.get("return_token_ids"):
+            choice["token_ids"] = list(req.output)
         return {"id": f"cmpl-{uuid.uuid4().hex[:16]}", "object": "text_completion", "created": int(time.time()),
-                "model": model_name, "choices": [{"index": 0, "text": text, "finish_reason": req.finish_reason}],
+                "model": model_name, "choices": [choice],
                 "usage": {"prompt_tokens": len(ids), "completion_tokens": len(req.output),
                           "total_tokens": len(ids) + len(req.output)}}
 
