@@ -33,6 +33,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--layers", type=int, default=64, help="debug only: fewer layers (reported as reduced)")
     ap.add_argument("--comm", choices=["fused", "nccl"], default="fused")
+    ap.add_argument("--shard", choices=["full", "stream"], default="stream",
+                    help="full: decoder-layer bf16 weights sharded and gathered per layer (FSDP full shard; fits 4 "
+                         "GPUs); stream: bf16 weights resident, fp32 gradients streamed per layer (8 GPUs)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -53,8 +56,9 @@ def main():
     model = BlockDiffusionLM(dec, mask_id=VOCAB - 1, pad_id=VOCAB - 2, bd_size=BD, ar_loss_weight=1.0,
                              activation_checkpoint="layer")
     model.train()
+    full = args.shard == "full" and world > 1
     engine = TrainEngine(model, lr=1e-5, warmup=50, max_steps=2000, device=torch.device("cuda"), comm=args.comm,
-                         grad_stream=True)
+                         grad_stream=True, full_shard=full)
     g = torch.Generator().manual_seed(1234 + rank)
     batches = []
     for _ in range(args.warmup + args.steps):
@@ -97,8 +101,10 @@ def main():
                        + ("" if args.layers == 64 else f" REDUCED to {args.layers} layers (not a valid bench)"),
                        "row": "[S 4096 | x_t 2048 | x_0 2048] x 2 views", "micro_batch": MB, "bd_size": BD,
                        "activation_checkpoint": "layer",
-                       "parallelism": f"dp{world}, bf16 weights resident, fp32 gradients streamed per layer and "
-                                      f"reduce-scattered ({args.comm}), sharded AdamW"}}), flush=True)
+                       "parallelism": f"dp{world}, " + ("bf16 weight shards gathered per layer over NVLink, "
+                                                         if full else "bf16 weights resident, ")
+                                      + f"fp32 gradients streamed per layer and reduce-scattered ({args.comm}), "
+                                        f"sharded AdamW"}}), flush=True)
     if world > 1:
         dist.destroy_process_group()
 

@@ -490,6 +490,75 @@ void gdn_commit(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor&
                                 adv.data_ptr<int>(), stream()) == 0, "gdn_commit failed");
 }
 
+// Tensor-core canvas step: state cache fp32 [slots, Hv, 128, 128] (k rows, v columns); writes o and the
+// commit inputs kbuf / ubuf (bf16 [B * blk, Hv, 128]) and gbuf (fp32 [B * blk, Hv]).
+void gdn_canvas_tc(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor& gb, const at::Tensor& A_log,
+                   const at::Tensor& dt_bias, const at::Tensor& o, const at::Tensor& kbuf, const at::Tensor& ubuf,
+                   const at::Tensor& gbuf, const at::Tensor& ssm, const at::Tensor& slot, int64_t blk, int64_t Hk,
+                   int64_t Hv, int64_t n_clean, double scale, const at::Tensor& err) {
+  const int64_t M = mixed.size(0), B = M / blk;
+  CHECK_BF16(mixed); CHECK_BF16(ga); CHECK_BF16(gb); CHECK_BF16(o); CHECK_BF16(kbuf); CHECK_BF16(ubuf);
+  TORCH_CHECK(M == B * blk && mixed.stride(1) == 1 && (mixed.stride(0) % 8) == 0 && (uintptr_t)mixed.data_ptr() % 16 == 0,
+              "mixed: rows of 16-byte aligned bf16");
+  TORCH_CHECK(mixed.size(1) >= (2 * Hk + Hv) * 128, "mixed: q | k | v columns");
+  TORCH_CHECK(ga.stride(1) == 1 && gb.stride(1) == 1 && ga.stride(0) == gb.stride(0) && ga.size(0) == M, "gate layout");
+  TORCH_CHECK(o.is_contiguous() && o.numel() == M * Hv * 128, "o layout");
+  TORCH_CHECK(kbuf.is_contiguous() && ubuf.is_contiguous() && kbuf.numel() == M * Hv * 128 && ubuf.numel() == M * Hv * 128,
+              "kbuf / ubuf layout");
+  TORCH_CHECK(gbuf.scalar_type() == at::kFloat && gbuf.is_contiguous() && gbuf.numel() == M * Hv, "gbuf layout");
+  TORCH_CHECK(ssm.scalar_type() == at::kFloat && ssm.is_contiguous() && ssm.dim() == 4 && ssm.size(1) == Hv &&
+                  ssm.size(2) == 128 && ssm.size(3) == 128, "state cache [slots, Hv, 128, 128] fp32");
+  TORCH_CHECK(A_log.scalar_type() == at::kFloat && dt_bias.scalar_type() == at::kFloat, "fp32 A_log / dt_bias");
+  check_i32(slot, B, "slot");
+  c10::cuda::CUDAGuard g(mixed.device());
+  TORCH_CHECK(trida::gdn_canvas_tc(cbf(mixed), mixed.stride(0), cbf(ga), cbf(gb), ga.stride(0), A_log.data_ptr<float>(),
+                                   dt_bias.data_ptr<float>(), ssm.data_ptr<float>(), slot.data_ptr<int>(), mbf(o),
+                                   mbf(kbuf), mbf(ubuf), gbuf.data_ptr<float>(), (int)B, (int)blk, (int)n_clean, (int)Hk,
+                                   (int)Hv, (float)scale, err.data_ptr<int>(), stream()) == 0,
+              "gdn_canvas_tc failed (canvas rows must be 1..64)");
+}
+
+void gdn_commit_tc(const at::Tensor& kbuf, const at::Tensor& ubuf, const at::Tensor& gbuf, const at::Tensor& ssm,
+                   const at::Tensor& slot, const at::Tensor& adv, int64_t blk, int64_t Hv, const at::Tensor& err) {
+  const int64_t M = gbuf.numel() / Hv, B = M / blk;
+  TORCH_CHECK(ssm.scalar_type() == at::kFloat && ssm.is_contiguous() && ssm.dim() == 4 && ssm.size(1) == Hv,
+              "state cache layout");
+  check_i32(slot, B, "slot"); check_i32(adv, B, "adv");
+  c10::cuda::CUDAGuard g(ssm.device());
+  TORCH_CHECK(trida::gdn_commit_tc(cbf(kbuf), cbf(ubuf), gbuf.data_ptr<float>(), ssm.data_ptr<float>(),
+                                   slot.data_ptr<int>(), adv.data_ptr<int>(), (int)B, (int)blk, (int)Hv,
+                                   err.data_ptr<int>(), stream()) == 0, "gdn_commit_tc failed");
+}
+
+// Sampled self-speculative step for a batch (see sampler.cu): candidate lists [B, blk, kc] (sorted
+// top-k of the canvas logits), per-request sampling parameters, per-slot draw counters and q lists.
+void spec_sample(const at::Tensor& vals, const at::Tensor& idx, const at::Tensor& temp, const at::Tensor& topk,
+                 const at::Tensor& topp, const at::Tensor& seed, const at::Tensor& counter, const at::Tensor& slot,
+                 const at::Tensor& specs, const at::Tensor& has_specs, const at::Tensor& q_idx,
+                 const at::Tensor& q_prob, const at::Tensor& out, int64_t n) {
+  TORCH_CHECK(vals.scalar_type() == at::kFloat && vals.is_contiguous() && vals.dim() == 3, "vals [B, blk, kc] fp32");
+  TORCH_CHECK(idx.scalar_type() == at::kLong && idx.is_contiguous() && idx.sizes() == vals.sizes(), "idx like vals");
+  const int64_t B = vals.size(0), blk = vals.size(1), kc = vals.size(2), K = n - 1;
+  TORCH_CHECK(temp.scalar_type() == at::kFloat && topp.scalar_type() == at::kFloat && temp.numel() == B &&
+                  topp.numel() == B, "temp / topp fp32 [B]");
+  check_i32(topk, B, "topk"); check_i32(slot, B, "slot"); check_i32(has_specs, B, "has_specs");
+  TORCH_CHECK(seed.scalar_type() == at::kLong && seed.numel() == B, "seed int64 [B]");
+  TORCH_CHECK(counter.scalar_type() == at::kLong && counter.is_contiguous(), "counter int64 [slots]");
+  TORCH_CHECK(specs.scalar_type() == at::kInt && specs.is_contiguous() && specs.numel() >= B * std::max<int64_t>(K, 1),
+              "specs int32 [B, K]");
+  TORCH_CHECK(q_idx.scalar_type() == at::kInt && q_prob.scalar_type() == at::kFloat && q_idx.dim() == 3 &&
+                  q_idx.size(1) == K && q_idx.size(2) == 64 && q_prob.sizes() == q_idx.sizes(),
+              "q lists [slots, K, 64]");
+  TORCH_CHECK(out.scalar_type() == at::kInt && out.is_contiguous() && out.numel() == B * (3 + K), "out int32 [B, 3 + K]");
+  c10::cuda::CUDAGuard g(vals.device());
+  TORCH_CHECK(trida::spec_sample(vals.data_ptr<float>(), idx.data_ptr<int64_t>(), (int)kc, temp.data_ptr<float>(),
+                                 topk.data_ptr<int>(), topp.data_ptr<float>(), seed.data_ptr<int64_t>(),
+                                 counter.data_ptr<int64_t>(), slot.data_ptr<int>(), specs.data_ptr<int>(),
+                                 has_specs.data_ptr<int>(), q_idx.data_ptr<int>(), q_prob.data_ptr<float>(),
+                                 out.data_ptr<int>(), (int)B, (int)blk, (int)n, stream()) == 0,
+              "spec_sample failed (1 <= candidates <= 64, n <= canvas rows)");
+}
+
 void argmax_rows(const at::Tensor& logits, const at::Tensor& out) {
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1, "fp32 logits rows");
   TORCH_CHECK(out.scalar_type() == at::kLong && out.is_contiguous() && out.numel() == logits.size(0), "out int64");
@@ -1052,6 +1121,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_prep_numel", &gdn_prep_numel);
   m.def("gdn_canvas", &gdn_canvas);
   m.def("gdn_commit", &gdn_commit);
+  m.def("gdn_canvas_tc", &gdn_canvas_tc);
+  m.def("spec_sample", &spec_sample);
+  m.def("gdn_commit_tc", &gdn_commit_tc);
   m.def("argmax_rows", &argmax_rows);
   m.def("conf_argmax_rows", &conf_argmax_rows);
   m.def("gdn_bwd", &gdn_bwd);

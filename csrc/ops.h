@@ -74,6 +74,19 @@ int bd_attn_bwd_d256(const AttnTensors& t, const bf16* dout, int64_t do_tok, int
                      const int* cnt128t, const uint4* colmask, const int16_t* list128, const int* cnt128,
                      const uint4* rowmask, float scale, int* err, cudaStream_t s);
 
+// ---- self-speculative sampler (sampler.cu) ----
+int spec_sample(const float* vals, const int64_t* idx, int kc, const float* temp, const int* topk, const float* topp,
+                const int64_t* seed, int64_t* counter, const int* slot, const int* specs, const int* has_specs,
+                int* q_idx, float* q_prob, int* out, int B, int blk, int n, cudaStream_t st);
+
+// ---- serving canvas gated-delta step on tensor cores (gdn_canvas_tc.cu) ----
+// state cache fp32 [slots, Hv, 128 (k), 128 (v)]; kbuf / ubuf bf16 [B * n, Hv, 128], gbuf fp32 [B * n, Hv]
+int gdn_canvas_tc(const bf16* mixed, int64_t ldm, const bf16* ga, const bf16* gb, int64_t ldg, const float* A_log,
+                  const float* dt_bias, const float* ssm, const int* slot, bf16* o, bf16* kbuf, bf16* ubuf, float* gbuf,
+                  int B, int n, int n_clean, int Hk, int Hv, float scale, int* err, cudaStream_t st);
+int gdn_commit_tc(const bf16* kbuf, const bf16* ubuf, const float* gbuf, float* ssm, const int* slot, const int* adv,
+                  int B, int n, int Hv, int* err, cudaStream_t st);
+
 // ---- gated-delta-rule linear attention (gdn.cu) ----
 struct GdnParams {
   int B, T, Hk, Hv, dk, dvh;  // dk, dvh: key / value head dims (128)

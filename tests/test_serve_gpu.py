@@ -63,10 +63,13 @@ def test_cuda_runtime_matches_cpu(cfg):
         assert _rel(a, b) < 3e-2, _rel(a, b)
 
 
+@pytest.mark.parametrize("canvas", ["tc", "scan"])
 @pytest.mark.parametrize("cfg", [_hybrid(256), _hybrid(128)], ids=["hybrid-d256", "hybrid-d128"])
-def test_cuda_runtime_long_canvases_match_cpu(cfg):
-    """Canvases longer than one 16-row staging chunk (33 and 63 rows, token-causal row counts that
-    are not multiples of 16) and commits that cross a chunk boundary, vs the CPU statement."""
+def test_cuda_runtime_long_canvases_match_cpu(cfg, canvas, monkeypatch):
+    """Canvases of 33 and 63 rows (token-causal row counts that are not multiples of 16) and commits
+    of 1 .. 32 accepted rows, vs the CPU statement: the tensor-core chunk step with its commit from
+    the stored U rows ("tc", the default) and the per-token scan kernels ("scan")."""
+    monkeypatch.setenv("TRIDA_GDN_CANVAS", canvas)
     dec = _init(cfg)
     dec_g = copy.deepcopy(dec).to("cuda", torch.bfloat16)
     torch.manual_seed(3)

@@ -87,6 +87,7 @@ class Request:
     rounds: int = 0
     specs: Optional[List[int]] = None
     spec_q: Optional[torch.Tensor] = None
+    sampler_seed: Optional[int] = None        # device sampler: the request's random stream
     gen: Optional[torch.Generator] = None
     on_tokens: Optional[object] = None      # callable(list[int]) for streaming
     done_event: threading.Event = field(default_factory=threading.Event)
@@ -143,6 +144,11 @@ class Engine:
         from ..utils.trace import RequestTrace
         self.trace = RequestTrace.from_env()  # $TRIDA_TRACE_JSONL: one line per finished request
         self._stats_t = time.perf_counter()
+        # sampled self-spec steps on the device sampler (top-k <= 64) unless TRIDA_SAMPLER=host
+        import os
+        self._dev_sampler = (runtime.cuda and self.mode == "self-spec" and
+                             os.environ.get("TRIDA_SAMPLER", "device") == "device")
+        self._sampler_state = None
 
     # ------------------------------------------------------------------ API
     def submit(self, req: Request) -> Request:
@@ -311,6 +317,8 @@ class Engine:
         logits = self.rt.canvas(slots, canv, n)
         self.stats["forwards"] += 1
         greedy = all(r.sampling.greedy for r in reqs)
+        if not greedy and self._device_sampling_ok(reqs):
+            return self._decode_spec_device(reqs, slots, logits)
         am = self.rt.argmax(logits).tolist() if greedy else None
         adv = []
         for b, r in enumerate(reqs):
@@ -341,6 +349,86 @@ class Engine:
                 self._emit(r, ([] if r.t0_emitted else [r.t0]) + [clean])
                 r.t0_emitted = True
                 r.pending, r.specs, r.spec_q = clean, new_specs, new_q
+        self.rt.commit(slots, adv)
+        self._reap()
+
+    # ------------------------------------------------------------------ device sampler
+    def _device_sampling_ok(self, reqs):
+        """Every sampled request truncates to at most 64 candidates (top-k 1 .. 64), and none carries
+        draft distributions from the host path."""
+        if not self._dev_sampler:
+            return False
+        for r in reqs:
+            if not r.sampling.greedy and not (0 < r.sampling.top_k <= 64):
+                return False
+            if r.specs is not None and r.spec_q is not None:
+                return False
+        return True
+
+    def _state(self):
+        """Per-slot draw counters and draft q lists of the device sampler (allocated once)."""
+        if self._sampler_state is None:
+            dev, S, K = self.rt.device, self.rt.max_slots + 1, self.n - 1
+            self._sampler_state = {
+                "ctr": torch.zeros(S, dtype=torch.long, device=dev),
+                "q_idx": torch.full((S, max(K, 1), 64), -1, dtype=torch.int32, device=dev),
+                "q_prob": torch.zeros(S, max(K, 1), 64, dtype=torch.float32, device=dev)}
+        return self._sampler_state
+
+    def _decode_spec_device(self, reqs, slots, logits):
+        """One sampled self-spec step for the whole batch: one top-k pass over the canvas logits and
+        one sampler launch (proposals, verification, corrections, new drafts and their q lists on the
+        device), then one host read of [B, 3 + K] integers."""
+        n, K = self.n, self.n - 1
+        st = self._state()
+        B = len(reqs)
+        kc = max((r.sampling.top_k if not r.sampling.greedy else 1) for r in reqs)
+        vals, idx = torch.topk(logits[:B].float(), kc, dim=-1, sorted=True)
+        host = torch.empty(B, 6, dtype=torch.float64)
+        specs = torch.zeros(B, max(K, 1), dtype=torch.int32)
+        for b, r in enumerate(reqs):
+            sp = r.sampling
+            if r.sampler_seed is None:
+                r.sampler_seed = sp.seed if sp.seed is not None else int(torch.randint(0, 2 ** 62, (1,)))
+                st["ctr"][r.slot] = 0
+            g = sp.greedy
+            host[b] = torch.tensor([1.0 if g else sp.temperature, 1 if g else sp.top_k, 1.0 if g else sp.top_p,
+                                    r.sampler_seed, r.slot, 1 if r.specs is not None else 0], dtype=torch.float64)
+            if r.specs is not None:
+                specs[b, :K] = torch.tensor(r.specs, dtype=torch.int32)
+        dev = logits.device
+        temp = host[:, 0].float().to(dev, non_blocking=True)
+        topk = host[:, 1].int().to(dev, non_blocking=True)
+        topp = host[:, 2].float().to(dev, non_blocking=True)
+        seed = torch.tensor([r.sampler_seed for r in reqs], dtype=torch.long).to(dev, non_blocking=True)
+        slot_t = host[:, 4].int().to(dev, non_blocking=True)
+        has = host[:, 5].int().to(dev, non_blocking=True)
+        out = torch.empty(B, 3 + K, dtype=torch.int32, device=dev)
+        self.rt.C.spec_sample(vals.contiguous(), idx.contiguous(), temp, topk, topp, seed, st["ctr"], slot_t,
+                              specs.to(dev, non_blocking=True), has, st["q_idx"], st["q_prob"], out, n)
+        res = out.tolist()
+        adv = []
+        for b, r in enumerate(reqs):
+            r.forwards += 1
+            acc, corr, clean, new_specs = res[b][0], res[b][1], res[b][2], res[b][3:3 + K]
+            if r.specs is not None:
+                if corr >= 0:
+                    adv.append(1 + acc)
+                    r.accept_hist[acc] += 1
+                    self._emit(r, r.specs[:acc] + [corr])
+                    r.t0, r.t0_emitted = corr, True
+                    r.pending, r.specs = None, None
+                else:
+                    adv.append(n)
+                    r.accept_hist[K] += 1
+                    self._emit(r, r.specs + [clean])
+                    r.pending, r.specs = clean, new_specs
+            else:
+                adv.append(1)
+                self._emit(r, ([] if r.t0_emitted else [r.t0]) + [clean])
+                r.t0_emitted = True
+                r.pending, r.specs = clean, new_specs
+            r.spec_q = None
         self.rt.commit(slots, adv)
         self._reap()
 

@@ -49,7 +49,8 @@ class Runtime:
                 self.vc[i] = torch.zeros(nslot, max_len, Hkv, d, dtype=self.dtype, device=self.device)
             else:
                 Cc = 2 * cfg.lin_k_heads * cfg.lin_k_dim + cfg.lin_v_heads * cfg.lin_v_dim
-                # fp32 state per value head; the CUDA kernels keep it in their thread-native order
+                # fp32 state per value head [k, v]; the per-token scan kernels (TRIDA_GDN_CANVAS=scan)
+                # keep it in their thread-native order instead
                 self.ssm[i] = torch.zeros(nslot, cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim,
                                           dtype=torch.float32, device=self.device)
                 self.win[i] = torch.zeros(nslot, cfg.conv_kernel - 1, Cc, dtype=self.dtype, device=self.device)
@@ -68,6 +69,11 @@ class Runtime:
             self.blocks = blocks
             self._gdn_f32 = {i: (decoder.layers[i].A_log.float().contiguous(),
                                  decoder.layers[i].dt_bias.float().contiguous()) for i in self.ssm}
+            import os
+            # canvas gated-delta step: the chunked form on tensor cores (commit from the stored U
+            # rows), or the per-token scan kernels (commit re-runs the accepted rows)
+            self.gdn_tc = os.environ.get("TRIDA_GDN_CANVAS", "tc") == "tc"
+            self.err = blocks.device_error_word(self.device)
 
     # ------------------------------------------------------------------ slots
     def alloc(self):
@@ -273,7 +279,13 @@ class Runtime:
         cfg = self.cfg
         for i, rec in st.gdn.items():
             layer = self.dec.layers[i]
-            if self.cuda:
+            if self.cuda and self.gdn_tc:
+                mixed, kbuf, ubuf, gbuf, proj = rec
+                self.C.gdn_commit_tc(kbuf, ubuf, gbuf, self.ssm[i], st.slot_t, adv_t, st.blk, cfg.lin_v_heads,
+                                     self.err)
+                Cc = mixed.shape[1]
+                self.C.conv_commit(proj[:, :Cc], st.blk, self.win[i], st.slot_t, adv_t)
+            elif self.cuda:
                 mixed, ga, gb, proj, prep = rec
                 a_log, dtb = self._gdn_f32[i]
                 self.C.gdn_commit(mixed, ga, gb, a_log, dtb, prep, self.ssm[i], st.slot_t, adv_t, st.blk,
@@ -436,12 +448,21 @@ class Runtime:
             self.C.canvas_conv(proj[:, :Cc], self.win[i], layer.conv_w, mixed, st.slot_t, blk)
             a_log, dtb = self._gdn_f32[i]
             o = torch.empty(M, vd, dtype=x.dtype, device=x.device)
-            prep = torch.empty(self.C.gdn_prep_numel(M, Hk, Hv), dtype=torch.float32, device=x.device)
-            self.C.gdn_canvas(mixed, ga, gb, a_log, dtb, o, prep, self.ssm[i], st.slot_t, blk, Hk, Hv, st.n_clean,
-                              dk ** -0.5)
+            if self.gdn_tc:
+                kbuf = torch.empty(M, Hv, dk, dtype=x.dtype, device=x.device)
+                ubuf = torch.empty(M, Hv, dv, dtype=x.dtype, device=x.device)
+                gbuf = torch.empty(M, Hv, dtype=torch.float32, device=x.device)
+                self.C.gdn_canvas_tc(mixed, ga, gb, a_log, dtb, o, kbuf, ubuf, gbuf, self.ssm[i], st.slot_t, blk,
+                                     Hk, Hv, st.n_clean, dk ** -0.5, self.err)
+                rec = (mixed, kbuf, ubuf, gbuf, proj)
+            else:
+                prep = torch.empty(self.C.gdn_prep_numel(M, Hk, Hv), dtype=torch.float32, device=x.device)
+                self.C.gdn_canvas(mixed, ga, gb, a_log, dtb, o, prep, self.ssm[i], st.slot_t, blk, Hk, Hv,
+                                  st.n_clean, dk ** -0.5)
+                rec = (mixed, ga, gb, proj, prep)
             y = torch.empty(M, vd, dtype=x.dtype, device=x.device)
             self.C.gdn_gnorm_fwd(o, z, layer.gnorm, y, Hv, cfg.eps)
-            st.gdn[i] = (mixed, ga, gb, proj, prep)
+            st.gdn[i] = rec
             return self._lin(y, layer.w_out, x)
         # CPU statement
         K1 = cfg.conv_kernel - 1
