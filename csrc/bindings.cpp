@@ -403,26 +403,40 @@ static void check_i32(const at::Tensor& t, int64_t n, const char* name) {
               " must be a contiguous int32 CUDA tensor of ", n, " elements");
 }
 
+// ptab (optional): int32 [slots, maxpages] page table of a paged cache kc / vc [pages, 64, Hkv, D]
+// (position p of slot s lives in page ptab[s, p / 64], row p % 64); without it the cache is dense
+// [slots, maxlen, Hkv, D].
+static int paged_maxlen(const at::Tensor& kc, const c10::optional<at::Tensor>& ptab, int64_t& maxpages) {
+  maxpages = 0;
+  if (!ptab.has_value() || !ptab->defined()) return kc.size(1);
+  TORCH_CHECK(ptab->scalar_type() == at::kInt && ptab->is_contiguous() && ptab->dim() == 2, "ptab int32 [slots, pages]");
+  TORCH_CHECK(kc.size(1) == 64, "a paged cache holds 64 positions per page");
+  maxpages = ptab->size(1);
+  return (int)(maxpages * 64);
+}
+
 void canvas_attention(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& slot,
                       const at::Tensor& pos, const at::Tensor& out, int64_t blk, int64_t n_clean, int64_t max_keys,
-                      double scale) {
+                      double scale, const c10::optional<at::Tensor>& ptab) {
   CHECK_BF16(q); CHECK_BF16(kc); CHECK_BF16(vc); CHECK_BF16(out);
   TORCH_CHECK(q.dim() == 3 && q.is_contiguous() && out.is_contiguous() && kc.dim() == 4 && kc.is_contiguous() &&
               vc.is_contiguous(), "canvas attention layouts");
   const int64_t B = q.size(0) / blk;
   check_i32(slot, B, "slot"); check_i32(pos, B, "pos");
-  const int Hq = q.size(1), D = q.size(2), Hkv = kc.size(2), maxlen = kc.size(1);
+  int64_t maxpages = 0;
+  const int Hq = q.size(1), D = q.size(2), Hkv = kc.size(2), maxlen = paged_maxlen(kc, ptab, maxpages);
   TORCH_CHECK(max_keys <= maxlen, "max_keys exceeds the cache length");
   at::Tensor work = at::empty({trida::canvas_work_floats(B, blk, Hq, D, max_keys)}, q.options().dtype(at::kFloat));
   c10::cuda::CUDAGuard g(q.device());
   const int rc = trida::canvas_attention(cbf(q), cbf(kc), cbf(vc), slot.data_ptr<int>(), pos.data_ptr<int>(), mbf(out),
                                          work.data_ptr<float>(), B, blk, n_clean, Hq, Hkv, D, maxlen, max_keys,
-                                         (float)scale, stream());
+                                         (float)scale, stream(), maxpages ? ptab->data_ptr<int>() : nullptr,
+                                         (int)maxpages);
   TORCH_CHECK(rc == 0, "canvas_attention failed with code ", rc);
 }
 
 void kv_append(const at::Tensor& k, const at::Tensor& v, const at::Tensor& kc, const at::Tensor& vc,
-               const at::Tensor& slot, const at::Tensor& pos, int64_t blk) {
+               const at::Tensor& slot, const at::Tensor& pos, int64_t blk, const c10::optional<at::Tensor>& ptab) {
   CHECK_BF16(k); CHECK_BF16(v); CHECK_ROWMAJOR(v);
   TORCH_CHECK(k.is_contiguous() && kc.is_contiguous() && vc.is_contiguous() && kc.dim() == 4, "kv_append layouts");
   const int Hkv = kc.size(2), D = kc.size(3);
@@ -430,8 +444,10 @@ void kv_append(const at::Tensor& k, const at::Tensor& v, const at::Tensor& kc, c
   TORCH_CHECK(v.size(0) == B * blk && v.size(1) == Hkv * D && v.stride(0) % 8 == 0, "v rows");
   check_i32(slot, B, "slot"); check_i32(pos, B, "pos");
   c10::cuda::CUDAGuard g(k.device());
+  int64_t maxpages = 0;
+  const int maxlen = paged_maxlen(kc, ptab, maxpages);
   trida::kv_append(cbf(k), cbf(v), v.stride(0), mbf(kc), mbf(vc), slot.data_ptr<int>(), pos.data_ptr<int>(), B, blk,
-                   Hkv, D, kc.size(1), stream());
+                   Hkv, D, maxlen, stream(), maxpages ? ptab->data_ptr<int>() : nullptr, (int)maxpages);
 }
 
 void canvas_conv(const at::Tensor& x, const at::Tensor& win, const at::Tensor& w, const at::Tensor& y,
@@ -1114,8 +1130,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("doc"), py::arg("o"), py::arg("ckpt"), py::arg("B"), py::arg("T"), py::arg("Hk"), py::arg("Hv"),
         py::arg("mode"), py::arg("L"), py::arg("V"), py::arg("bd"), py::arg("causal_clean"), py::arg("causal_noisy"),
         py::arg("scale"), py::arg("final_state") = py::none());
-  m.def("canvas_attention", &canvas_attention);
-  m.def("kv_append", &kv_append);
+  m.def("canvas_attention", &canvas_attention, py::arg("q"), py::arg("kc"), py::arg("vc"), py::arg("slot"),
+        py::arg("pos"), py::arg("out"), py::arg("blk"), py::arg("n_clean"), py::arg("max_keys"), py::arg("scale"),
+        py::arg("ptab") = py::none());
+  m.def("kv_append", &kv_append, py::arg("k"), py::arg("v"), py::arg("kc"), py::arg("vc"), py::arg("slot"),
+        py::arg("pos"), py::arg("blk"), py::arg("ptab") = py::none());
   m.def("canvas_conv", &canvas_conv);
   m.def("conv_commit", &conv_commit);
   m.def("gdn_prep_numel", &gdn_prep_numel);

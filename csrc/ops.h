@@ -172,10 +172,10 @@ int gdn_gnorm_bwd(const bf16* dy, const bf16* o, const bf16* z, int64_t ldz, con
 // ---- serving decode step (serve.cu) ----
 int canvas_attention(const bf16* q, const bf16* kc, const bf16* vc, const int* slot, const int* pos, bf16* out,
                      float* work, int B, int blk, int n_clean, int Hq, int Hkv, int D, int maxlen, int max_keys,
-                     float scale, cudaStream_t s);
+                     float scale, cudaStream_t s, const int* ptab = nullptr, int maxpages = 0);
 int64_t canvas_work_floats(int B, int blk, int Hq, int D, int max_keys);
 void kv_append(const bf16* k, const bf16* v, int64_t ldv, bf16* kc, bf16* vc, const int* slot, const int* pos, int B,
-               int blk, int Hkv, int D, int maxlen, cudaStream_t s);
+               int blk, int Hkv, int D, int maxlen, cudaStream_t s, const int* ptab = nullptr, int maxpages = 0);
 void canvas_conv(const bf16* x, int64_t ldx, const bf16* win, const bf16* w, bf16* y, int64_t ldy, const int* slot,
                  int B, int blk, int C, int K, cudaStream_t s);
 void conv_commit(const bf16* x, int64_t ldx, int rows_per, bf16* win, const int* slot, const int* adv, int B, int C,

@@ -32,6 +32,9 @@ struct CanvasAttnParams {
   const bf16* vc;
   const int* slot;        // [B]
   const int* pos;         // [B] cached prefix length (canvas keys start here)
+  const int* ptab;        // paged cache: [slots, maxpages] page of every 64 positions (kc / vc are
+                          // [pages, 64, Hkv, D]); null: dense [slots, maxlen, Hkv, D] cache
+  int maxpages;
   float* po;              // [B, nsplit, Hq, blk, D] partial outputs (unnormalised)
   float* pm;              // [B, nsplit, Hq, blk] running max (scaled, log2 domain)
   float* pl;              // [B, nsplit, Hq, blk] running sum
@@ -65,14 +68,19 @@ __global__ void __launch_bounds__(128) canvas_attn_kernel(const CanvasAttnParams
     const bf16* src = p.q + ((int64_t)(b * p.blk + i) * p.Hq + hk * G + g) * D + col;
     cp_async16(sQ + swz<D>(row, col), src, ok);
   }
-  const bf16* gk = p.kc + ((int64_t)slot * p.maxlen * p.Hkv + hk) * D;
-  const bf16* gv = p.vc + ((int64_t)slot * p.maxlen * p.Hkv + hk) * D;
   const int64_t ktok = (int64_t)p.Hkv * D;
   const int ntile = k1 > k0 ? (k1 - k0 + BN - 1) / BN : 0;
+  // first key row of tile `it` (a 64-key tile is exactly one page of a paged cache)
+  auto key_row = [&](int it) -> int64_t {
+    const int kp = k0 + it * BN;
+    if (p.ptab != nullptr) return ((int64_t)p.ptab[(int64_t)slot * p.maxpages + kp / BN] * BN) * ktok + hk * D;
+    return ((int64_t)slot * p.maxlen + kp) * ktok + hk * D;
+  };
   auto issue_kv = [&](int it) {
     const int buf = it & 1;
-    load_tile<D, BN, NT>(sK + buf * BN * D, gk + (int64_t)(k0 + it * BN) * ktok, ktok, 0, k1 - k0 - it * BN);
-    load_tile<D, BN, NT>(sV + buf * BN * D, gv + (int64_t)(k0 + it * BN) * ktok, ktok, 0, k1 - k0 - it * BN);
+    const int64_t r0 = key_row(it);
+    load_tile<D, BN, NT>(sK + buf * BN * D, p.kc + r0, ktok, 0, k1 - k0 - it * BN);
+    load_tile<D, BN, NT>(sV + buf * BN * D, p.vc + r0, ktok, 0, k1 - k0 - it * BN);
   };
   if (ntile > 0) issue_kv(0);
   cp_async_commit();
@@ -239,7 +247,8 @@ __global__ void canvas_combine_kernel(const float* po, const float* pm, const fl
 
 // cache[slot, pos + i] <- k / v of canvas row i (k: [B*blk, Hkv, D] contiguous; v: row-strided)
 __global__ void kv_append_kernel(const bf16* k, const bf16* v, int64_t ldv, bf16* kc, bf16* vc, const int* slot,
-                                 const int* pos, int B, int blk, int Hkv, int D, int maxlen) {
+                                 const int* pos, int B, int blk, int Hkv, int D, int maxlen, const int* ptab,
+                                 int maxpages) {
   const int64_t n8 = (int64_t)B * blk * Hkv * D / 8;
   for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < n8; g += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = g * 8;
@@ -248,7 +257,9 @@ __global__ void kv_append_kernel(const bf16* k, const bf16* v, int64_t ldv, bf16
     const int b = (int)(row / blk), i = (int)(row % blk);
     const int p = pos[b] + i;
     if (p >= maxlen) continue;
-    const int64_t dst = (((int64_t)slot[b] * maxlen + p) * Hkv) * D + rem;
+    const int64_t crow = ptab != nullptr ? (int64_t)ptab[(int64_t)slot[b] * maxpages + p / 64] * 64 + p % 64
+                                         : (int64_t)slot[b] * maxlen + p;
+    const int64_t dst = crow * Hkv * D + rem;
     *reinterpret_cast<uint4*>(kc + dst) = *reinterpret_cast<const uint4*>(k + row * Hkv * D + rem);
     *reinterpret_cast<uint4*>(vc + dst) = *reinterpret_cast<const uint4*>(v + row * ldv + rem);
   }
@@ -451,10 +462,10 @@ size_t canvas_smem() { return (size_t)(64 * D + 4 * 64 * D) * 2; }
 
 int canvas_attention(const bf16* q, const bf16* kc, const bf16* vc, const int* slot, const int* pos, bf16* out,
                      float* work, int B, int blk, int n_clean, int Hq, int Hkv, int D, int maxlen, int max_keys,
-                     float scale, cudaStream_t s) {
+                     float scale, cudaStream_t s, const int* ptab, int maxpages) {
   using namespace serve;
   CanvasAttnParams p;
-  p.q = q; p.kc = kc; p.vc = vc; p.slot = slot; p.pos = pos;
+  p.q = q; p.kc = kc; p.vc = vc; p.slot = slot; p.pos = pos; p.ptab = ptab; p.maxpages = maxpages;
   p.blk = blk; p.n_clean = n_clean; p.Hq = Hq; p.Hkv = Hkv; p.maxlen = maxlen;
   p.ks = 256;
   p.nsplit = (max_keys + p.ks - 1) / p.ks;
@@ -492,10 +503,10 @@ int64_t canvas_work_floats(int B, int blk, int Hq, int D, int max_keys) {
 }
 
 void kv_append(const bf16* k, const bf16* v, int64_t ldv, bf16* kc, bf16* vc, const int* slot, const int* pos, int B,
-               int blk, int Hkv, int D, int maxlen, cudaStream_t s) {
+               int blk, int Hkv, int D, int maxlen, cudaStream_t s, const int* ptab, int maxpages) {
   const int64_t n8 = (int64_t)B * blk * Hkv * D / 8;
   const int blocks = (int)std::min<int64_t>((n8 + 255) / 256, 4096);
-  serve::kv_append_kernel<<<blocks, 256, 0, s>>>(k, v, ldv, kc, vc, slot, pos, B, blk, Hkv, D, maxlen);
+  serve::kv_append_kernel<<<blocks, 256, 0, s>>>(k, v, ldv, kc, vc, slot, pos, B, blk, Hkv, D, maxlen, ptab, maxpages);
 }
 
 void canvas_conv(const bf16* x, int64_t ldx, const bf16* win, const bf16* w, bf16* y, int64_t ldy, const int* slot,

@@ -35,6 +35,9 @@ def parse_args(argv=None):
     ap.add_argument("--mem-fraction", type=float, default=0.8)
     ap.add_argument("--max-running", type=int, default=32)
     ap.add_argument("--max-len", type=int, default=8192)
+    ap.add_argument("--kv-pages", type=int, default=0,
+                    help="full-attention KV pool in pages of 64 positions shared by all requests (0: enough for "
+                         "every slot at --max-len)")
     ap.add_argument("--cuda-graph-bs", default="1 2 4 8")
     ap.add_argument("--dtype", default="bfloat16", choices=["bfloat16", "float32"])
     ap.add_argument("--config", default=None, help="decode YAML (block_size, gen_block_size, mask_id, ...)")
@@ -116,7 +119,8 @@ def build(args):
         from trida_stack_b200.serve.tp import TPContext, shard_decoder
         dec = shard_decoder(dec, dist.get_rank(), dist.get_world_size())
         tp = TPContext(max_rows=args.max_running * 64, hidden=dec.cfg.hidden_size)
-    rt = Runtime(dec, max_slots=args.max_running, max_len=args.max_len, device=dev, tp=tp)
+    rt = Runtime(dec, max_slots=args.max_running, max_len=args.max_len, device=dev, tp=tp,
+                 kv_pages=args.kv_pages or None)
     mode = args.mode if args.mode in ("self-spec", "diffusion") else "causal"
     graphs = dev.startswith("cuda") and not args.no_graphs
     engine = Engine(rt, mask_id=mask_id, mode=mode, n=n, max_running=args.max_running, graphs=graphs,

@@ -90,6 +90,38 @@ def test_cuda_runtime_long_canvases_match_cpu(cfg, canvas, monkeypatch):
         assert _rel(a, b) < 3e-2, _rel(a, b)
 
 
+def test_paged_kv_pool_is_shared_and_recycled():
+    """Full-attention KV in a pool of 64-position pages: a pool smaller than slots x max_len serves
+    requests while they fit, refuses growth past it, and takes pages back on release; outputs match
+    the CPU runtime's dense cache."""
+    cfg = _hybrid(128)
+    dec = _init(cfg)
+    dec_g = copy.deepcopy(dec).to("cuda", torch.bfloat16)
+    torch.manual_seed(5)
+    ids = torch.randint(0, 500, (2, 150))
+    rt = Runtime(dec_g, max_slots=4, max_len=1024, kv_pages=8)     # 8 pages: 512 positions in all
+    cpu = Runtime(dec, max_slots=4, max_len=1024)
+    s_g = [rt.alloc() for _ in range(2)]
+    s_c = [cpu.alloc() for _ in range(2)]
+    lg = rt.prefill(s_g, ids[:, :130].tolist())
+    lc = cpu.prefill(s_c, ids[:, :130].tolist())
+    assert _rel(lg, lc) < 3e-2
+    used = sum(len(p) for p in rt.slot_pages[:4])
+    assert used == 2 * 3                       # 130 positions (+ a canvas) -> 3 pages per request
+    a = rt.canvas(s_g, ids[:, 130:137], 4)
+    rt.commit(s_g, [4, 4])
+    b = cpu.canvas(s_c, ids[:, 130:137], 4)
+    cpu.commit(s_c, [4, 4])
+    assert _rel(a, b) < 3e-2
+    s3 = rt.alloc()
+    with pytest.raises(RuntimeError, match="page pool"):
+        rt.prefill([s3], [ids[0, :200].tolist()])
+    rt.pending = None
+    rt.release(s_g[0])
+    rt.release(s3)
+    assert len(rt.free_pages) >= 4
+
+
 @pytest.mark.parametrize("mode", ["self-spec", "causal", "diffusion"])
 def test_cuda_engine_graphs_match_eager(mode):
     dec = _init(_hybrid(256)).to("cuda", torch.bfloat16)

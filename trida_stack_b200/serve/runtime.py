@@ -24,12 +24,16 @@ from ..ops import gdn_reference as G
 from ..ops import reference as R
 
 PREFILL_CHUNK = 64
+PAGE = 64                 # positions per KV page
 
 
 class Runtime:
-    def __init__(self, decoder, max_slots=8, max_len=4096, device=None, tp=None):
+    def __init__(self, decoder, max_slots=8, max_len=4096, device=None, tp=None, kv_pages=None):
         """``tp``: a ``serve.tp.TPContext`` when ``decoder`` is this rank's tensor-parallel shard
-        (``serve.tp.shard_decoder``); greedy decoding only."""
+        (``serve.tp.shard_decoder``); greedy decoding only.  ``max_len`` caps one request's
+        positions; on CUDA the full-attention KV lives in a pool of ``kv_pages`` pages of 64
+        positions shared by all slots (default: enough for every slot at ``max_len``), so a few long
+        requests and many short ones share the same memory."""
         self.dec = decoder
         self.tp = tp
         self.cfg = cfg = decoder.cfg
@@ -43,10 +47,21 @@ class Runtime:
         self.kc, self.vc, self.ssm, self.win = {}, {}, {}, {}
         nslot = max_slots + 1              # + one scratch slot that pads graph-captured batches
         self.dummy = max_slots
+        # paged KV (CUDA): page tables [slot, max_len / 64] into per-layer pools [pages, 64, Hkv, d];
+        # the CPU statement keeps a dense [slot, max_len] cache
+        self.paged = self.cuda
+        self.max_pages = (max_len + PAGE - 1) // PAGE
+        if self.paged:
+            self.n_pages = kv_pages or nslot * self.max_pages
+            self.free_pages = list(range(self.n_pages))[::-1]
+            self.slot_pages = [[] for _ in range(nslot)]
+            self.ptab_host = torch.zeros(nslot, self.max_pages, dtype=torch.int32).pin_memory()
+            self.ptab = torch.zeros(nslot, self.max_pages, dtype=torch.int32, device=self.device)
         for i, kind in enumerate(self.kinds):
             if kind == "full_attention":
-                self.kc[i] = torch.zeros(nslot, max_len, Hkv, d, dtype=self.dtype, device=self.device)
-                self.vc[i] = torch.zeros(nslot, max_len, Hkv, d, dtype=self.dtype, device=self.device)
+                shape = (self.n_pages, PAGE, Hkv, d) if self.paged else (nslot, max_len, Hkv, d)
+                self.kc[i] = torch.zeros(*shape, dtype=self.dtype, device=self.device)
+                self.vc[i] = torch.zeros(*shape, dtype=self.dtype, device=self.device)
             else:
                 Cc = 2 * cfg.lin_k_heads * cfg.lin_k_dim + cfg.lin_v_heads * cfg.lin_v_dim
                 # fp32 state per value head [k, v]; the per-token scan kernels (TRIDA_GDN_CANVAS=scan)
@@ -90,6 +105,28 @@ class Runtime:
     def release(self, s):
         self.pos[s] = 0
         self.free.append(s)
+        if self.paged and s != self.dummy:
+            self.free_pages.extend(reversed(self.slot_pages[s]))
+            self.slot_pages[s] = []
+
+    def _ensure_pages(self, slots, blk):
+        """Pages for positions [0, pos + blk) of every slot (the scratch slot of padded graph
+        batches writes positions [0, blk)); the device page table is refreshed when it changed."""
+        if not self.paged or not self.kc:
+            return
+        changed = False
+        for s in list(slots) + [self.dummy]:
+            need = ((self.pos[s] if s < self.max_slots else 0) + blk + PAGE - 1) // PAGE
+            pages = self.slot_pages[s]
+            while len(pages) < need:
+                if not self.free_pages:
+                    raise RuntimeError(f"KV page pool exhausted ({self.n_pages} pages of {PAGE} positions)")
+                pg = self.free_pages.pop()
+                self.ptab_host[s, len(pages)] = pg
+                pages.append(pg)
+                changed = True
+        if changed:
+            self.ptab.copy_(self.ptab_host, non_blocking=True)
 
     # ------------------------------------------------------------------ public steps
     @torch.no_grad()
@@ -152,6 +189,7 @@ class Runtime:
         for s in slots:
             if self.pos[s] + blk > self.max_len:
                 raise RuntimeError(f"slot {s}: sequence exceeds the cache length {self.max_len}")
+        self._ensure_pages(slots, blk)
         r0, r1 = rows if rows is not None else (0, blk)
         if self._graphs is not None and (r0, r1) == (0, blk) and inject is None and rope_ang is None:
             return self._canvas_graph(slots, tokens, n_clean)
@@ -382,10 +420,11 @@ class Runtime:
             self.C.qk_norm_rope_fwd(qkv, layer.q_norm, layer.k_norm, cos_t, sin_t, rp, q, k,
                                     Hq, Hkv, d, cfg.rotary_dim, cfg.eps, qs)
             v = qkv[:, Hq * qs + Hkv * d:]
-            self.C.kv_append(k, v, self.kc[i], self.vc[i], st.slot_t, st.pos_t, blk)
+            ptab = self.ptab if self.paged else None
+            self.C.kv_append(k, v, self.kc[i], self.vc[i], st.slot_t, st.pos_t, blk, ptab)
             o = torch.empty(M, Hq, d, dtype=x.dtype, device=x.device)
             self.C.canvas_attention(q, self.kc[i], self.vc[i], st.slot_t, st.pos_t, o, blk, st.n_clean, st.max_keys,
-                                    1.0 / math.sqrt(d))
+                                    1.0 / math.sqrt(d), ptab)
             o = o.view(M, Hq * d)
             if cfg.attn_output_gate:
                 og = torch.empty_like(o)
