@@ -255,29 +255,28 @@ __global__ void __launch_bounds__(NTH, 1)
       named_sync(bar_id, 64);
       const float mx_s = mx * p.scale_log2;
       const bool grow = mx_s > m_run + RESCALE_THRESHOLD || (m_run == -INFINITY && mx_s > -INFINITY);
-      // O may be rescaled only after PV_{i-1} has completed
-      if (ok && grow && i > 0) {
-        ok = mbar_wait(&pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1, p.err, 9);
+      // O may be rescaled only after PV_{i-1} has completed.  TMEM loads / stores are
+      // warp-collective, so when any row of the warp rescales, every lane waits for PV_{i-1},
+      // loads and stores its O columns (alpha = 1 for rows that keep their max)
+      const bool resc = grow && i > 0 && m_run != -INFINITY;
+      if (__any_sync(0xffffffffu, resc && ok)) {
+        if (ok) ok = mbar_wait(&pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1, p.err, 9);
         tc_fence_after();
-      }
-      if (grow) {
-        if (ok && i > 0 && m_run != -INFINITY) {
-          const float alpha = exp2f(m_run - mx_s);
-          l_run *= alpha;
+        const float alpha = (resc && ok) ? exp2f(m_run - mx_s) : 1.f;
+        l_run *= alpha;
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {                 // this half's 128 columns of the O row
-            uint32_t t[32];
-            const uint32_t col = tO + lane_off + half * 128 + c * 32;
-            tmem_ld32(col, t);
-            tmem_wait_ld();
+        for (int c = 0; c < 4; ++c) {            // this half's columns of the O row
+          uint32_t t[32];
+          const uint32_t col = tO + lane_off + half * 128 + c * 32;
+          tmem_ld32(col, t);
+          tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) t[j] = __float_as_uint(__uint_as_float(t[j]) * alpha);
-            tmem_st32(col, t);
-          }
-          tmem_wait_st();
+          for (int j = 0; j < 32; ++j) t[j] = __float_as_uint(__uint_as_float(t[j]) * alpha);
+          tmem_st32(col, t);
         }
-        m_run = mx_s;
+        tmem_wait_st();
       }
+      if (grow) m_run = mx_s;
       if (ok) {
         // P_i (bf16 pairs) over this half's own S_i columns: 32 columns from column 64 half
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;

@@ -360,17 +360,19 @@ __global__ void __launch_bounds__(NT) canvas_kernel(const CanvasArgs a) {
     umma_commit(bar);
   }
   ok = ph.wait() && ok;
-  if (w < 2 && live && ok) {
+  if (w < 2) {                         // tcgen05.ld is warp-collective: every lane loads, live rows store
     float x[32];
     bf16* go = a.o + row * (int64_t)(a.Hv * 128) + hv * 128;
 #pragma unroll 1
     for (int g4 = 0; g4 < 4; ++g4) {
       tld32(tmem + 32 * g4, x);
+      if (live && ok) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        reinterpret_cast<uint4*>(go)[4 * g4 + j] =
-            make_uint4(pack_bf2(x[8 * j], x[8 * j + 1]), pack_bf2(x[8 * j + 2], x[8 * j + 3]),
-                       pack_bf2(x[8 * j + 4], x[8 * j + 5]), pack_bf2(x[8 * j + 6], x[8 * j + 7]));
+        for (int j = 0; j < 4; ++j)
+          reinterpret_cast<uint4*>(go)[4 * g4 + j] =
+              make_uint4(pack_bf2(x[8 * j], x[8 * j + 1]), pack_bf2(x[8 * j + 2], x[8 * j + 3]),
+                         pack_bf2(x[8 * j + 4], x[8 * j + 5]), pack_bf2(x[8 * j + 6], x[8 * j + 7]));
+      }
     }
   }
   tc_fence_before();
@@ -424,13 +426,14 @@ __global__ void __launch_bounds__(NT) commit_kernel(const CommitArgs a) {
   }
   const bool ok = mbar_wait(&bar, 0, a.err, 90);
   tc_fence_after();
-  if (ok) {
+  {  // every warp loads its 32 lanes (warp-collective tcgen05.ld); the state is written when ok
     const float gam = __expf(Gl);
     float* S = a.ssm + (((int64_t)a.slot[b] * a.Hv + hv) * 128 + t) * 128;   // state row t (k index t)
 #pragma unroll 1
     for (int g4 = 0; g4 < 4; ++g4) {
       float x[32];
       tld32(tmem + 32 * g4, x);
+      if (!ok) continue;
       float4* p = reinterpret_cast<float4*>(S + 32 * g4);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {

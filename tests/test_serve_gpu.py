@@ -193,3 +193,59 @@ def test_glm_ocr_runtime_cuda_matches_cpu():
         out[name] = [t.float().cpu() for t in (last, draft, ver, nxt)]
     for a, b in zip(out["gpu"], out["cpu"]):
         assert _rel(a, b) < 3e-2, _rel(a, b)
+
+
+@pytest.mark.parametrize("n,n_clean,adv", [(7, 4, [1, 4, 3]), (33, 17, [17, 5, 9]), (64, 64, [64, 20, 1])])
+def test_canvas_tc_kernels_match_recurrence(n, n_clean, adv):
+    """The tensor-core canvas step and its commit from the stored U rows against the fp32 per-token
+    recurrence (clean rows read their own state, the others the state after the canvas)."""
+    from trida_stack_b200.ops._ext import ext
+    from trida_stack_b200.ops.blocks import check_device_errors, device_error_word
+    C = ext()
+    torch.manual_seed(n)
+    B, Hk, Hv, D = 3, 2, 4, 128
+    dev = "cuda"
+    kd = Hk * D
+    mixed = (torch.randn(B * n, 2 * kd + Hv * D, device=dev) * 0.5).to(torch.bfloat16)
+    gates = torch.randn(B * n, 2 * Hv, device=dev).to(torch.bfloat16)
+    ga, gb = gates[:, :Hv], gates[:, Hv:]
+    A_log = torch.log(torch.empty(Hv, device=dev).uniform_(0.5, 4))
+    dtb = torch.randn(Hv, device=dev) * 0.1
+    ssm = torch.randn(5, Hv, D, D, device=dev) * 0.05
+    slot = torch.tensor([3, 0, 2], dtype=torch.int32, device=dev)
+    o = torch.empty(B * n, Hv * D, dtype=torch.bfloat16, device=dev)
+    kbuf = torch.empty(B * n, Hv, D, dtype=torch.bfloat16, device=dev)
+    ubuf = torch.empty_like(kbuf)
+    gbuf = torch.empty(B * n, Hv, device=dev)
+    S_before = ssm.clone()
+    err = device_error_word(dev)
+    C.gdn_canvas_tc(mixed, ga, gb, A_log, dtb, o, kbuf, ubuf, gbuf, ssm, slot, n, Hk, Hv, n_clean, D ** -0.5, err)
+    adv_t = torch.tensor(adv, dtype=torch.int32, device=dev)
+    C.gdn_commit_tc(kbuf, ubuf, gbuf, ssm, slot, adv_t, n, Hv, err)
+    torch.cuda.synchronize()
+    check_device_errors()
+    # fp32 statement
+    m = mixed.float().view(B, n, -1)
+    q = torch.nn.functional.normalize(m[..., :kd].view(B, n, Hk, D), dim=-1) * D ** -0.5
+    k = torch.nn.functional.normalize(m[..., kd:2 * kd].view(B, n, Hk, D), dim=-1)
+    v = m[..., 2 * kd:].view(B, n, Hv, D)
+    rep = Hv // Hk
+    q, k = q.repeat_interleave(rep, 2), k.repeat_interleave(rep, 2)
+    g = -A_log.exp() * torch.nn.functional.softplus(ga.float().view(B, n, Hv) + dtb)
+    beta = torch.sigmoid(gb.float().view(B, n, Hv))
+    o_ref = torch.zeros(B, n, Hv, D, device=dev)
+    for bi in range(B):
+        S = S_before[int(slot[bi])].clone()
+        states = []
+        for t in range(n):
+            a_t = g[bi, t].exp()[:, None, None]
+            u = beta[bi, t][:, None] * (v[bi, t] - a_t[:, :, 0] * torch.einsum("hkv,hk->hv", S, k[bi, t]))
+            S = a_t * S + torch.einsum("hk,hv->hkv", k[bi, t], u)
+            states.append(S.clone())
+        for t in range(n):
+            St = states[t if t < n_clean else n - 1]
+            o_ref[bi, t] = torch.einsum("hkv,hk->hv", St, q[bi, t])
+        ref_S = states[adv[bi] - 1]
+        got_S = ssm[int(slot[bi])]
+        assert _rel(got_S, ref_S) < 2e-2, (bi, _rel(got_S, ref_S))
+    assert _rel(o.view(B, n, Hv, D), o_ref) < 2e-2, _rel(o.view(B, n, Hv, D), o_ref)
