@@ -47,6 +47,9 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--layers", type=int, default=36, help="debug only: fewer layers (reported as reduced)")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--phase-split", type=int, default=0, metavar="STEPS",
+                   help="after the timed steps, STEPS more steps with CUDA events around forward, backward and "
+                        "the optimizer step (device ms, mean over steps, max over ranks) in the JSON line")
     p.add_argument("--shard", choices=["full", "zero2"], default="full",
                    help="full: decoder-layer weights sharded and gathered per layer over NVLink (FSDP full "
                         "shard, the reference's setup); zero2: replicated weights")
@@ -190,6 +193,28 @@ def run_ours(args, rank, world, local_rank):
     ms = max_over_ranks(ms)
     peak_gb = torch.cuda.max_memory_allocated() / 1e9
 
+    phases = None
+    if args.phase_split:
+        # forward / backward / optimizer of extra steps, each bracketed by events on the stream (not
+        # part of the timed region); with full shard the backward includes the streamed reduce-scatter
+        sums = {"forward": 0.0, "backward": 0.0, "optimizer": 0.0}
+        m = engine.model
+        for i in range(args.phase_split):
+            b = dev_batches[(args.warmup + i) % len(dev_batches)]
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            ev[0].record()
+            loss, _ = m(b["input_ids"], b["labels"], b["attention_mask"], rpad=rpad)
+            ev[1].record()
+            loss.backward()
+            ev[2].record()
+            engine.optimizer_step(step)
+            ev[3].record()
+            step += 1
+            torch.cuda.synchronize()
+            for k, (a, z) in zip(sums, ((0, 1), (1, 2), (2, 3))):
+                sums[k] += ev[a].elapsed_time(ev[z]) / args.phase_split
+        phases = {k: round(max_over_ranks(v), 2) for k, v in sums.items()}
+
     e2e = None
     if not args.no_e2e:
         # end to end through the public per-step API: host batch -> device, loss back to the host
@@ -206,7 +231,7 @@ def run_ours(args, rank, world, local_rank):
         e2e = {"value": world * MB * (PROMPT + RESP) / e2e_s, "unit": "tokens/s",
                "h2d_bytes_per_step": sum(v.numel() * v.element_size() for v in batches[0].values()),
                "d2h_bytes_per_step": 4}
-    return ms, clk, launches, e2e, peak_gb
+    return ms, clk, launches, e2e, peak_gb, phases
 
 
 # ------------------------------------------------------------------------------------------------
@@ -301,7 +326,7 @@ def run_reference(args, rank, world, local_rank):
         e2e = {"value": world * MB * (PROMPT + RESP) / e2e_s, "unit": "tokens/s",
                "h2d_bytes_per_step": sum(v.numel() * v.element_size() for v in batches[0].values()),
                "d2h_bytes_per_step": 4}
-    return ms, clk, None, e2e, peak_gb
+    return ms, clk, None, e2e, peak_gb, None
 
 
 # ------------------------------------------------------------------------------------------------
@@ -335,7 +360,7 @@ def main():
             if dist.is_initialized():
                 dist.destroy_process_group()
             return
-    ms, clk, launches, e2e, peak_gb = res
+    ms, clk, launches, e2e, peak_gb, phases = res
     tokens_per_step = world * MB * (PROMPT + RESP)
     value = tokens_per_step / (ms / 1000.0)
     if rank == 0:
@@ -365,6 +390,8 @@ def main():
         if clk and clk.get("sm_mhz"):
             # clock-normalised step cost: comparable across power-capped and unthrottled runs
             line["mcycles_per_step"] = round(ms * clk["sm_mhz"] / 1000.0, 1)
+        if phases:
+            line["phase_ms"] = phases
         if args.impl == "ours":
             line["gpu_launches"] = launches
         else:
