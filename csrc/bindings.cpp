@@ -511,7 +511,8 @@ void gdn_commit(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor&
 void gdn_canvas_tc(const at::Tensor& mixed, const at::Tensor& ga, const at::Tensor& gb, const at::Tensor& A_log,
                    const at::Tensor& dt_bias, const at::Tensor& o, const at::Tensor& kbuf, const at::Tensor& ubuf,
                    const at::Tensor& gbuf, const at::Tensor& ssm, const at::Tensor& slot, int64_t blk, int64_t Hk,
-                   int64_t Hv, int64_t n_clean, double scale, const at::Tensor& err) {
+                   int64_t Hv, int64_t n_clean, double scale, const at::Tensor& err,
+                   const c10::optional<at::Tensor>& z, const c10::optional<at::Tensor>& gnorm_w, double eps) {
   const int64_t M = mixed.size(0), B = M / blk;
   CHECK_BF16(mixed); CHECK_BF16(ga); CHECK_BF16(gb); CHECK_BF16(o); CHECK_BF16(kbuf); CHECK_BF16(ubuf);
   TORCH_CHECK(M == B * blk && mixed.stride(1) == 1 && (mixed.stride(0) % 8) == 0 && (uintptr_t)mixed.data_ptr() % 16 == 0,
@@ -526,11 +527,21 @@ void gdn_canvas_tc(const at::Tensor& mixed, const at::Tensor& ga, const at::Tens
                   ssm.size(2) == 128 && ssm.size(3) == 128, "state cache [slots, Hv, 128, 128] fp32");
   TORCH_CHECK(A_log.scalar_type() == at::kFloat && dt_bias.scalar_type() == at::kFloat, "fp32 A_log / dt_bias");
   check_i32(slot, B, "slot");
+  // optional fused gated RMSNorm: o receives rmsnorm(o) * w * silu(z) per value head
+  const bf16* pz = nullptr; const bf16* pw = nullptr; int64_t ldz = 0;
+  if (z.has_value() && z->defined()) {
+    TORCH_CHECK(gnorm_w.has_value() && gnorm_w->defined(), "the fused gated norm needs its weight");
+    CHECK_BF16((*z)); CHECK_BF16((*gnorm_w));
+    TORCH_CHECK(z->stride(1) == 1 && z->size(0) == M && z->size(1) >= Hv * 128 && z->stride(0) % 8 == 0 &&
+                    (uintptr_t)z->data_ptr() % 16 == 0, "z rows of 16-byte aligned bf16");
+    TORCH_CHECK(gnorm_w->is_contiguous() && gnorm_w->numel() == 128, "gated norm weight [128]");
+    pz = cbf(*z); pw = cbf(*gnorm_w); ldz = z->stride(0);
+  }
   c10::cuda::CUDAGuard g(mixed.device());
   TORCH_CHECK(trida::gdn_canvas_tc(cbf(mixed), mixed.stride(0), cbf(ga), cbf(gb), ga.stride(0), A_log.data_ptr<float>(),
                                    dt_bias.data_ptr<float>(), ssm.data_ptr<float>(), slot.data_ptr<int>(), mbf(o),
                                    mbf(kbuf), mbf(ubuf), gbuf.data_ptr<float>(), (int)B, (int)blk, (int)n_clean, (int)Hk,
-                                   (int)Hv, (float)scale, err.data_ptr<int>(), stream()) == 0,
+                                   (int)Hv, (float)scale, err.data_ptr<int>(), stream(), pz, ldz, pw, (float)eps) == 0,
               "gdn_canvas_tc failed (canvas rows must be 1..64)");
 }
 
@@ -1140,7 +1151,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_prep_numel", &gdn_prep_numel);
   m.def("gdn_canvas", &gdn_canvas);
   m.def("gdn_commit", &gdn_commit);
-  m.def("gdn_canvas_tc", &gdn_canvas_tc);
+  m.def("gdn_canvas_tc", &gdn_canvas_tc, py::arg("mixed"), py::arg("ga"), py::arg("gb"), py::arg("A_log"),
+        py::arg("dt_bias"), py::arg("o"), py::arg("kbuf"), py::arg("ubuf"), py::arg("gbuf"), py::arg("ssm"),
+        py::arg("slot"), py::arg("blk"), py::arg("Hk"), py::arg("Hv"), py::arg("n_clean"), py::arg("scale"),
+        py::arg("err"), py::arg("z") = py::none(), py::arg("gnorm_w") = py::none(), py::arg("eps") = 1e-6);
   m.def("spec_sample", &spec_sample);
   m.def("gdn_commit_tc", &gdn_commit_tc);
   m.def("argmax_rows", &argmax_rows);

@@ -72,7 +72,9 @@ struct CanvasArgs {
   const float* A_log; const float* dt_bias;      // [Hv]
   const float* ssm;                      // [slots, Hv, 128, 128] fp32 (k rows, v columns)
   const int* slot;                       // [B]
-  bf16* o;                               // [B * n, Hv * 128]
+  bf16* o;                               // [B * n, Hv * 128]: o, or y = rmsnorm(o) * w * silu(z) when
+  const bf16* z; int64_t ldz;            //   z (gate rows [B * n, ldz], value head h at column 128 h)
+  const bf16* gnorm_w; float eps;        //   and the norm weight [128] are given
   bf16* kbuf; bf16* ubuf;                // [B * n, Hv, 128] normalised k / U rows (commit inputs)
   float* gbuf;                           // [B * n, Hv] cumulative log decay G
   int* err;
@@ -94,29 +96,22 @@ __device__ __forceinline__ void ld8(const bf16* p, float (&f)[8]) {
   }
 }
 
-// 128 bf16 of src, times `mul`, as bf16 row r of a [64][128] tile (and to `gdst` when given)
-__device__ __forceinline__ void copy_row(const bf16* src, float mul, uint8_t* tile, int r, bf16* gdst) {
-#pragma unroll 4
+// 16 vectors of 8 bf16 (one 128-element row), times `mul`, as bf16 row r of a [64][128] tile (and to
+// `gdst` when given)
+__device__ __forceinline__ void store_row(const uint4 (&x)[16], float mul, uint8_t* tile, int r, bf16* gdst) {
+#pragma unroll
   for (int j = 0; j < 16; ++j) {
-    float f[8];
-    ld8(src + 8 * j, f);
-    const uint4 v = make_uint4(pack_bf2(f[0] * mul, f[1] * mul), pack_bf2(f[2] * mul, f[3] * mul),
-                               pack_bf2(f[4] * mul, f[5] * mul), pack_bf2(f[6] * mul, f[7] * mul));
+    const uint32_t w4[4] = {x[j].x, x[j].y, x[j].z, x[j].w};
+    uint32_t o4[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[i]));
+      o4[i] = pack_bf2(f.x * mul, f.y * mul);
+    }
+    const uint4 v = make_uint4(o4[0], o4[1], o4[2], o4[3]);
     *reinterpret_cast<uint4*>(tile + off64(r, 8 * j)) = v;
     if (gdst) reinterpret_cast<uint4*>(gdst)[j] = v;
   }
-}
-
-__device__ __forceinline__ float sumsq128(const bf16* src) {
-  float s = 0.f;
-#pragma unroll 4
-  for (int j = 0; j < 16; ++j) {
-    float f[8];
-    ld8(src + 8 * j, f);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) s = fmaf(f[i], f[i], s);
-  }
-  return s;
 }
 
 __device__ __forceinline__ void zero_row(uint8_t* tile, int r, int cols) {
@@ -169,33 +164,70 @@ __global__ void __launch_bounds__(NT) canvas_kernel(const CanvasArgs a) {
     fence_barrier_init();
   }
   if (w == 0) tmem_alloc(tslot, 256);
-  // ---- rows: normalised q / k, v, gates; the state as a bf16 tile ----
-  if (t < C) {
-    if (live) {
-      const bf16* rq = a.mixed + row * a.ldm + hk * 128;
-      const bf16* rk = rq + kd;
-      const float iq = rsqrtf(sumsq128(rq) + 1e-6f) * a.scale, ik = rsqrtf(sumsq128(rk) + 1e-6f);
-      copy_row(rq, iq, tQ, t, nullptr);
-      copy_row(rk, ik, tK, t, a.kbuf + (row * a.Hv + hv) * 128);
-      const float av = __bfloat162float(a.ga[row * a.ldg + hv]) + a.dt_bias[hv];
-      const float bv = __bfloat162float(a.gb[row * a.ldg + hv]);
-      gl[t] = -expf(a.A_log[hv]) * softplus_(av);
-      be[t] = 1.f / (1.f + expf(-bv));
+  // ---- rows: every load of a row is issued at once (16-byte vectors, one memory round trip): q and k
+  //      rows in threads 0-63, the v row in threads 64-127 (row t - 64); then the state rows ----
+  const int r2 = t & (C - 1);                          // canvas row this thread loads
+  const int64_t row2 = (int64_t)b * n + r2;
+  const bool live2 = r2 < n;
+  {
+    uint4 x0[16], x1[16];
+    float gav = 0.f, gbv = 0.f;
+    if (live2) {
+      const bf16* base = a.mixed + row2 * a.ldm;
+      const bf16* p0 = t < C ? base + hk * 128 : base + 2 * kd + hv * 128;   // q or v
+#pragma unroll
+      for (int j = 0; j < 16; ++j) x0[j] = reinterpret_cast<const uint4*>(p0)[j];
+      if (t < C) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) x1[j] = reinterpret_cast<const uint4*>(base + kd + hk * 128)[j];
+      }
+      gav = __bfloat162float(a.ga[row2 * a.ldg + hv]);
+      gbv = __bfloat162float(a.gb[row2 * a.ldg + hv]);
+    }
+    const float bet = live2 ? 1.f / (1.f + expf(-gbv)) : 0.f;
+    if (t < C) {
+      if (live2) {
+        auto sumsq = [](const uint4 (&x)[16]) {
+          float s2 = 0.f;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const uint32_t w4[4] = {x[j].x, x[j].y, x[j].z, x[j].w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[i]));
+              s2 = fmaf(f.x, f.x, fmaf(f.y, f.y, s2));
+            }
+          }
+          return s2;
+        };
+        const float iq = rsqrtf(sumsq(x0) + 1e-6f) * a.scale, ik = rsqrtf(sumsq(x1) + 1e-6f);
+        store_row(x0, iq, tQ, t, nullptr);
+        store_row(x1, ik, tK, t, a.kbuf + (row2 * a.Hv + hv) * 128);
+        gl[t] = -expf(a.A_log[hv]) * softplus_(gav + a.dt_bias[hv]);
+        be[t] = bet;
+      } else {
+        zero_row(tQ, t, 128);
+        zero_row(tK, t, 128);
+        gl[t] = 0.f;
+        be[t] = 0.f;
+      }
     } else {
-      zero_row(tQ, t, 128);
-      zero_row(tK, t, 128);
-      gl[t] = 0.f;
-      be[t] = 0.f;
+      if (live2) store_row(x0, bet, tV, r2, nullptr);          // Vb = diag(b) V
+      else zero_row(tV, r2, 128);
     }
   }
-  {  // S0 row t (k index t) as bf16
+  {  // S0 row t (k index t) as bf16: two batches of 16 vector loads
     const float* src = a.ssm + (((int64_t)a.slot[b] * a.Hv + hv) * 128 + t) * 128;
-#pragma unroll 4
-    for (int j = 0; j < 16; ++j) {
-      const float4 x0 = reinterpret_cast<const float4*>(src)[2 * j];
-      const float4 x1 = reinterpret_cast<const float4*>(src)[2 * j + 1];
-      *reinterpret_cast<uint4*>(tS + off128(t, 8 * j)) =
-          make_uint4(pack_bf2(x0.x, x0.y), pack_bf2(x0.z, x0.w), pack_bf2(x1.x, x1.y), pack_bf2(x1.z, x1.w));
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      float4 x[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) x[j] = reinterpret_cast<const float4*>(src)[16 * h2 + j];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<uint4*>(tS + off128(t, 64 * h2 + 8 * j)) =
+            make_uint4(pack_bf2(x[2 * j].x, x[2 * j].y), pack_bf2(x[2 * j].z, x[2 * j].w),
+                       pack_bf2(x[2 * j + 1].x, x[2 * j + 1].y), pack_bf2(x[2 * j + 1].z, x[2 * j + 1].w));
     }
   }
   __syncthreads();
@@ -212,9 +244,6 @@ __global__ void __launch_bounds__(NT) canvas_kernel(const CanvasArgs a) {
     Grt = G[rt < 0 ? 0 : rt];
     bt = be[t];
     Gr[t] = Grt;
-    // Vb = diag(b) V
-    if (live) copy_row(a.mixed + row * a.ldm + 2 * kd + hv * 128, bt, tV, t, nullptr);
-    else zero_row(tV, t, 128);
     if (live) a.gbuf[row * a.Hv + hv] = Gt;
   }
   tc_fence_before();
@@ -363,9 +392,32 @@ __global__ void __launch_bounds__(NT) canvas_kernel(const CanvasArgs a) {
   if (w < 2) {                         // tcgen05.ld is warp-collective: every lane loads, live rows store
     float x[32];
     bf16* go = a.o + row * (int64_t)(a.Hv * 128) + hv * 128;
+    float rs = 1.f;
+    if (a.z != nullptr) {              // gated RMSNorm of this head's row: first its mean square
+      float ss = 0.f;
+#pragma unroll 1
+      for (int g4 = 0; g4 < 4; ++g4) {
+        tld32(tmem + 32 * g4, x);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ss = fmaf(x[i], x[i], ss);
+      }
+      rs = rsqrtf(ss * (1.f / 128.f) + a.eps);
+    }
 #pragma unroll 1
     for (int g4 = 0; g4 < 4; ++g4) {
       tld32(tmem + 32 * g4, x);
+      if (a.z != nullptr && live) {
+        const bf16* zr = a.z + row * a.ldz + hv * 128 + 32 * g4;
+        const bf16* wr = a.gnorm_w + 32 * g4;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float zf[8], wf[8];
+          ld8(zr + 8 * j, zf);
+          ld8(wr + 8 * j, wf);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) x[8 * j + i] *= rs * wf[i] * (zf[i] / (1.f + __expf(-zf[i])));
+        }
+      }
       if (live && ok) {
 #pragma unroll
         for (int j = 0; j < 4; ++j)
@@ -403,12 +455,24 @@ __global__ void __launch_bounds__(NT) commit_kernel(const CommitArgs a) {
   }
   if (w == 0) tmem_alloc(&tslot, 128);
   const float Gl = m > 0 ? a.gbuf[((int64_t)b * a.n + m - 1) * a.Hv + hv] : 0.f;
+  // the state row of this thread (k index t) is loaded now, so its latency hides behind the rows
+  // and the product; threads 0-63 stage row t of K~ and U with all their loads in flight
+  float* S = a.ssm + (((int64_t)a.slot[b] * a.Hv + hv) * 128 + t) * 128;
+  float4 s0[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) s0[j] = reinterpret_cast<const float4*>(S)[j];
   if (t < C) {
     if (t < m) {
       const int64_t row = (int64_t)b * a.n + t;
+      uint4 xk[16], xu[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        xk[j] = reinterpret_cast<const uint4*>(a.kbuf + (row * a.Hv + hv) * 128)[j];
+        xu[j] = reinterpret_cast<const uint4*>(a.ubuf + (row * a.Hv + hv) * 128)[j];
+      }
       const float sc = __expf(Gl - a.gbuf[row * a.Hv + hv]);
-      copy_row(a.kbuf + (row * a.Hv + hv) * 128, sc, sk, t, nullptr);
-      copy_row(a.ubuf + (row * a.Hv + hv) * 128, 1.f, su, t, nullptr);
+      store_row(xk, sc, sk, t, nullptr);
+      store_row(xu, 1.f, su, t, nullptr);
     } else {
       zero_row(sk, t, 128);
       zero_row(su, t, 128);
@@ -428,8 +492,7 @@ __global__ void __launch_bounds__(NT) commit_kernel(const CommitArgs a) {
   tc_fence_after();
   {  // every warp loads its 32 lanes (warp-collective tcgen05.ld); the state is written when ok
     const float gam = __expf(Gl);
-    float* S = a.ssm + (((int64_t)a.slot[b] * a.Hv + hv) * 128 + t) * 128;   // state row t (k index t)
-#pragma unroll 1
+#pragma unroll
     for (int g4 = 0; g4 < 4; ++g4) {
       float x[32];
       tld32(tmem + 32 * g4, x);
@@ -437,12 +500,12 @@ __global__ void __launch_bounds__(NT) commit_kernel(const CommitArgs a) {
       float4* p = reinterpret_cast<float4*>(S + 32 * g4);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        float4 s0 = p[j];
-        s0.x = fmaf(gam, s0.x, x[4 * j]);
-        s0.y = fmaf(gam, s0.y, x[4 * j + 1]);
-        s0.z = fmaf(gam, s0.z, x[4 * j + 2]);
-        s0.w = fmaf(gam, s0.w, x[4 * j + 3]);
-        p[j] = s0;
+        float4 v = s0[8 * g4 + j];
+        v.x = fmaf(gam, v.x, x[4 * j]);
+        v.y = fmaf(gam, v.y, x[4 * j + 1]);
+        v.z = fmaf(gam, v.z, x[4 * j + 2]);
+        v.w = fmaf(gam, v.w, x[4 * j + 3]);
+        p[j] = v;
       }
     }
   }
@@ -456,10 +519,12 @@ __global__ void __launch_bounds__(NT) commit_kernel(const CommitArgs a) {
 
 int gdn_canvas_tc(const bf16* mixed, int64_t ldm, const bf16* ga, const bf16* gb, int64_t ldg, const float* A_log,
                   const float* dt_bias, const float* ssm, const int* slot, bf16* o, bf16* kbuf, bf16* ubuf, float* gbuf,
-                  int B, int n, int n_clean, int Hk, int Hv, float scale, int* err, cudaStream_t st) {
+                  int B, int n, int n_clean, int Hk, int Hv, float scale, int* err, cudaStream_t st, const bf16* z,
+                  int64_t ldz, const bf16* gnorm_w, float eps) {
   using namespace gdncv;
   if (n < 1 || n > C || Hv % Hk) return -1;
-  CanvasArgs a{mixed, ldm, ga, gb, ldg, A_log, dt_bias, ssm, slot, o, kbuf, ubuf, gbuf, err, n, n_clean, Hk, Hv, scale};
+  CanvasArgs a{mixed, ldm, ga, gb, ldg, A_log, dt_bias, ssm, slot, o, z, ldz, gnorm_w, eps, kbuf, ubuf, gbuf, err,
+               n, n_clean, Hk, Hv, scale};
   const int smem = CanvasSmem::TOTAL + 1024;
   static bool init = false;
   if (!init) {

@@ -83,7 +83,8 @@ int spec_sample(const float* vals, const int64_t* idx, int kc, const float* temp
 // state cache fp32 [slots, Hv, 128 (k), 128 (v)]; kbuf / ubuf bf16 [B * n, Hv, 128], gbuf fp32 [B * n, Hv]
 int gdn_canvas_tc(const bf16* mixed, int64_t ldm, const bf16* ga, const bf16* gb, int64_t ldg, const float* A_log,
                   const float* dt_bias, const float* ssm, const int* slot, bf16* o, bf16* kbuf, bf16* ubuf, float* gbuf,
-                  int B, int n, int n_clean, int Hk, int Hv, float scale, int* err, cudaStream_t st);
+                  int B, int n, int n_clean, int Hk, int Hv, float scale, int* err, cudaStream_t st,
+                  const bf16* z = nullptr, int64_t ldz = 0, const bf16* gnorm_w = nullptr, float eps = 0.f);
 int gdn_commit_tc(const bf16* kbuf, const bf16* ubuf, const float* gbuf, float* ssm, const int* slot, const int* adv,
                   int B, int n, int Hv, int* err, cudaStream_t st);
 

@@ -105,14 +105,14 @@ def test_paged_kv_pool_is_shared_and_recycled():
     s_c = [cpu.alloc() for _ in range(2)]
     lg = rt.prefill(s_g, ids[:, :130].tolist())
     lc = cpu.prefill(s_c, ids[:, :130].tolist())
-    assert _rel(lg, lc) < 3e-2
+    assert _rel(lg.cpu(), lc) < 3e-2
     used = sum(len(p) for p in rt.slot_pages[:4])
     assert used == 2 * 3                       # 130 positions (+ a canvas) -> 3 pages per request
     a = rt.canvas(s_g, ids[:, 130:137], 4)
     rt.commit(s_g, [4, 4])
     b = cpu.canvas(s_c, ids[:, 130:137], 4)
     cpu.commit(s_c, [4, 4])
-    assert _rel(a, b) < 3e-2
+    assert _rel(a.cpu(), b) < 3e-2
     s3 = rt.alloc()
     with pytest.raises(RuntimeError, match="page pool"):
         rt.prefill([s3], [ids[0, :200].tolist()])
@@ -220,6 +220,12 @@ def test_canvas_tc_kernels_match_recurrence(n, n_clean, adv):
     S_before = ssm.clone()
     err = device_error_word(dev)
     C.gdn_canvas_tc(mixed, ga, gb, A_log, dtb, o, kbuf, ubuf, gbuf, ssm, slot, n, Hk, Hv, n_clean, D ** -0.5, err)
+    # the same step with the gated RMSNorm fused into the epilogue
+    z = (torch.randn(B * n, Hv * D, device=dev)).to(torch.bfloat16)
+    gw = (1 + 0.1 * torch.randn(D, device=dev)).to(torch.bfloat16)
+    y = torch.empty_like(o)
+    C.gdn_canvas_tc(mixed, ga, gb, A_log, dtb, y, kbuf, ubuf, gbuf, ssm, slot, n, Hk, Hv, n_clean, D ** -0.5, err,
+                    z=z, gnorm_w=gw, eps=1e-6)
     adv_t = torch.tensor(adv, dtype=torch.int32, device=dev)
     C.gdn_commit_tc(kbuf, ubuf, gbuf, ssm, slot, adv_t, n, Hv, err)
     torch.cuda.synchronize()
@@ -249,3 +255,6 @@ def test_canvas_tc_kernels_match_recurrence(n, n_clean, adv):
         got_S = ssm[int(slot[bi])]
         assert _rel(got_S, ref_S) < 2e-2, (bi, _rel(got_S, ref_S))
     assert _rel(o.view(B, n, Hv, D), o_ref) < 2e-2, _rel(o.view(B, n, Hv, D), o_ref)
+    from trida_stack_b200.ops.gdn_reference import gated_rmsnorm
+    y_ref = gated_rmsnorm(o_ref, z.float().view(B, n, Hv, D), gw.float(), 1e-6)
+    assert _rel(y.view(B, n, Hv, D), y_ref) < 2e-2, _rel(y.view(B, n, Hv, D), y_ref)

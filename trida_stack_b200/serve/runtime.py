@@ -491,9 +491,11 @@ class Runtime:
                 kbuf = torch.empty(M, Hv, dk, dtype=x.dtype, device=x.device)
                 ubuf = torch.empty(M, Hv, dv, dtype=x.dtype, device=x.device)
                 gbuf = torch.empty(M, Hv, dtype=torch.float32, device=x.device)
+                # the gated RMSNorm rides in the canvas kernel's epilogue: o receives y directly
                 self.C.gdn_canvas_tc(mixed, ga, gb, a_log, dtb, o, kbuf, ubuf, gbuf, self.ssm[i], st.slot_t, blk,
-                                     Hk, Hv, st.n_clean, dk ** -0.5, self.err)
-                rec = (mixed, kbuf, ubuf, gbuf, proj)
+                                     Hk, Hv, st.n_clean, dk ** -0.5, self.err, z=z, gnorm_w=layer.gnorm, eps=cfg.eps)
+                st.gdn[i] = (mixed, kbuf, ubuf, gbuf, proj)
+                return self._lin(o, layer.w_out, x)
             else:
                 prep = torch.empty(self.C.gdn_prep_numel(M, Hk, Hv), dtype=torch.float32, device=x.device)
                 self.C.gdn_canvas(mixed, ga, gb, a_log, dtb, o, prep, self.ssm[i], st.slot_t, blk, Hk, Hv,
