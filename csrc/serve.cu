@@ -323,6 +323,8 @@ __global__ void canvas_conv4_kernel(const bf16* __restrict__ x, int64_t ldx, con
       if (src >= 0) load8(x + ((int64_t)b * blk + src) * ldx + c8, h[t]);
       else load8(win + ((int64_t)slot[b] * 3 + (3 + src)) * C + c8, h[t]);
     }
+    // the rows' loads do not depend on each other: unrolled, several are in flight at once
+#pragma unroll 4
     for (int j = j0; j < j1; ++j) {
       float xv[8], out[8];
       load8(x + ((int64_t)b * blk + j) * ldx + c8, xv);
