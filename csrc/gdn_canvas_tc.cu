@@ -96,6 +96,45 @@ __device__ __forceinline__ void ld8(const bf16* p, float (&f)[8]) {
   }
 }
 
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+
+// sum of squares of bf16 row r of a [64][128] tile
+__device__ __forceinline__ float rowsq(const uint8_t* tile, int r) {
+  float s2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const uint4 v = *reinterpret_cast<const uint4*>(tile + off64(r, 8 * j));
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[i]));
+      s2 = fmaf(f.x, f.x, fmaf(f.y, f.y, s2));
+    }
+  }
+  return s2;
+}
+
+// row r of a [64][128] tile times `mul`, in place (and to `gdst` when given)
+__device__ __forceinline__ void scale_row(uint8_t* tile, int r, float mul, bf16* gdst) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    uint4* p = reinterpret_cast<uint4*>(tile + off64(r, 8 * j));
+    const uint4 v = *p;
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o4[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[i]));
+      o4[i] = pack_bf2(f.x * mul, f.y * mul);
+    }
+    const uint4 o = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+    *p = o;
+    if (gdst) reinterpret_cast<uint4*>(gdst)[j] = o;
+  }
+}
+
 // 16 vectors of 8 bf16 (one 128-element row), times `mul`, as bf16 row r of a [64][128] tile (and to
 // `gdst` when given)
 __device__ __forceinline__ void store_row(const uint4 (&x)[16], float mul, uint8_t* tile, int r, bf16* gdst) {
@@ -164,56 +203,29 @@ __global__ void __launch_bounds__(NT) canvas_kernel(const CanvasArgs a) {
     fence_barrier_init();
   }
   if (w == 0) tmem_alloc(tslot, 256);
-  // ---- rows: every load of a row is issued at once (16-byte vectors, one memory round trip): q and k
-  //      rows in threads 0-63, the v row in threads 64-127 (row t - 64); then the state rows ----
-  const int r2 = t & (C - 1);                          // canvas row this thread loads
-  const int64_t row2 = (int64_t)b * n + r2;
-  const bool live2 = r2 < n;
-  {
-    uint4 x0[16], x1[16];
-    float gav = 0.f, gbv = 0.f;
-    if (live2) {
-      const bf16* base = a.mixed + row2 * a.ldm;
-      const bf16* p0 = t < C ? base + hk * 128 : base + 2 * kd + hv * 128;   // q or v
-#pragma unroll
-      for (int j = 0; j < 16; ++j) x0[j] = reinterpret_cast<const uint4*>(p0)[j];
-      if (t < C) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) x1[j] = reinterpret_cast<const uint4*>(base + kd + hk * 128)[j];
-      }
-      gav = __bfloat162float(a.ga[row2 * a.ldg + hv]);
-      gbv = __bfloat162float(a.gb[row2 * a.ldg + hv]);
-    }
-    const float bet = live2 ? 1.f / (1.f + expf(-gbv)) : 0.f;
-    if (t < C) {
-      if (live2) {
-        auto sumsq = [](const uint4 (&x)[16]) {
-          float s2 = 0.f;
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const uint32_t w4[4] = {x[j].x, x[j].y, x[j].z, x[j].w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[i]));
-              s2 = fmaf(f.x, f.x, fmaf(f.y, f.y, s2));
-            }
-          }
-          return s2;
-        };
-        const float iq = rsqrtf(sumsq(x0) + 1e-6f) * a.scale, ik = rsqrtf(sumsq(x1) + 1e-6f);
-        store_row(x0, iq, tQ, t, nullptr);
-        store_row(x1, ik, tK, t, a.kbuf + (row2 * a.Hv + hv) * 128);
-        gl[t] = -expf(a.A_log[hv]) * softplus_(gav + a.dt_bias[hv]);
-        be[t] = bet;
-      } else {
-        zero_row(tQ, t, 128);
-        zero_row(tK, t, 128);
-        gl[t] = 0.f;
-        be[t] = 0.f;
-      }
+  // ---- rows: the q / k / v rows land in their tile positions by cp.async (3 x 64 rows x 16 copies of
+  //      16 bytes, all in flight at once); rows past the canvas are zero.  Then, in shared memory,
+  //      q / k are L2-normalised (q times the scale) and v is scaled by beta ----
+  for (int it = t; it < 3 * C * 16; it += NT) {
+    const int kind = it / (C * 16), rem = it % (C * 16), r = rem >> 4, j = rem & 15;
+    uint8_t* dst = (kind == 0 ? tQ : kind == 1 ? tK : tV) + off64(r, 8 * j);
+    if (r < n) {
+      const int64_t col = kind == 0 ? hk * 128 : kind == 1 ? kd + hk * 128 : 2 * kd + hv * 128;
+      cp_async16(dst, a.mixed + ((int64_t)b * n + r) * a.ldm + col + 8 * j);
     } else {
-      if (live2) store_row(x0, bet, tV, r2, nullptr);          // Vb = diag(b) V
-      else zero_row(tV, r2, 128);
+      *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+  if (t < C) {
+    if (live) {
+      const float av = __bfloat162float(a.ga[row * a.ldg + hv]) + a.dt_bias[hv];
+      const float bv = __bfloat162float(a.gb[row * a.ldg + hv]);
+      gl[t] = -expf(a.A_log[hv]) * softplus_(av);
+      be[t] = 1.f / (1.f + expf(-bv));
+    } else {
+      gl[t] = 0.f;
+      be[t] = 0.f;
     }
   }
   {  // S0 row t (k index t) as bf16: two batches of 16 vector loads
@@ -230,7 +242,20 @@ __global__ void __launch_bounds__(NT) canvas_kernel(const CanvasArgs a) {
                        pack_bf2(x[2 * j + 1].x, x[2 * j + 1].y), pack_bf2(x[2 * j + 1].z, x[2 * j + 1].w));
     }
   }
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
   __syncthreads();
+  // threads 0-63: q row t (norm, times the scale), then v row t (times beta); threads 64-127: k row
+  // t - 64 (norm; also to kbuf for the commit)
+  {
+    const int r = t & (C - 1);
+    if (r < n) {
+      uint8_t* tile = t < C ? tQ : tK;
+      const float ss = rowsq(tile, r);
+      const float mul = rsqrtf(ss + 1e-6f) * (t < C ? a.scale : 1.f);
+      scale_row(tile, r, mul, t < C ? nullptr : a.kbuf + (((int64_t)b * n + r) * a.Hv + hv) * 128);
+      if (t < C) scale_row(tV, r, be[r], nullptr);
+    }
+  }
   if (t < C) {
     float s = 0.f;
     for (int j = 0; j <= t; ++j) s += gl[j];
@@ -302,10 +327,10 @@ __global__ void __launch_bounds__(NT) canvas_kernel(const CanvasArgs a) {
     for (int i = 0; i < C; ++i) xs[i] = (i == t) ? 1.f : 0.f;
 #pragma unroll
     for (int i = 1; i < C; ++i) {
-      float s = 0.f;
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};     // four independent chains instead of one of length i
 #pragma unroll
-      for (int u = 0; u < i; ++u) s = fmaf(Af[af_idx(i, u)], xs[u], s);
-      if (i > t) xs[i] = -s;
+      for (int u = 0; u < i; ++u) s4[u & 3] = fmaf(Af[af_idx(i, u)], xs[u], s4[u & 3]);
+      if (i > t) xs[i] = -((s4[0] + s4[1]) + (s4[2] + s4[3]));
     }
 #pragma unroll
     for (int i = 0; i < C; ++i) *reinterpret_cast<bf16*>(tT + sw128_offset(i, t)) = __float2bfloat16(xs[i]);

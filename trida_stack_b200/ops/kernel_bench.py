@@ -5,7 +5,8 @@
     python -m trida_stack_b200.ops.kernel_bench --op gdn_fwd|gdn_bwd [--length 3072] [--gdn-path chunk|scan]
                                                      [--gdn-layout two_stream|causal]
     python -m trida_stack_b200.ops.kernel_bench --op gdn_core_fwd|gdn_core_bwd [--length 3072]
-    python -m trida_stack_b200.ops.kernel_bench --op canvas_attn|canvas_gdn [--requests 64 --blk 7]
+    python -m trida_stack_b200.ops.kernel_bench --op canvas_attn|canvas_gdn|canvas_gdn_tc|commit_gdn_tc
+                                                     [--requests 64 --blk 7]
     python -m trida_stack_b200.ops.kernel_bench --op rmsnorm_fwd|rmsnorm_bwd|qk_rope_fwd|qk_rope_bwd|
                                                      swiglu_fwd|swiglu_bwd [--m 24576 --hidden 2560]
 
@@ -218,11 +219,29 @@ def bench_canvas(a, which):
     al, dtb = torch.zeros(Hv, device=dev), torch.zeros(Hv, device=dev)
     ssm = torch.zeros(B, Hv, 128, 128, device=dev)
     o = torch.empty(B * blk, Hv * 128, device=dev, dtype=torch.bfloat16)
-    prep = torch.empty(C.gdn_prep_numel(B * blk, Hk, Hv), device=dev)
     slot = torch.arange(B, device=dev, dtype=torch.int32)
+    nbytes = ssm.numel() * 4
+    if which in ("canvas_gdn_tc", "commit_gdn_tc"):
+        from .blocks import device_error_word
+        err = device_error_word(dev)
+        kbuf = torch.empty(B * blk, Hv, 128, device=dev, dtype=torch.bfloat16)
+        ubuf, gbuf = torch.empty_like(kbuf), torch.empty(B * blk, Hv, device=dev)
+        z = torch.randn(B * blk, Hv * 128, device=dev, dtype=torch.bfloat16)
+        gw = torch.ones(128, device=dev, dtype=torch.bfloat16)
+
+        def canvas():
+            C.gdn_canvas_tc(mixed, ga, gb, al, dtb, o, kbuf, ubuf, gbuf, ssm, slot, blk, Hk, Hv, (blk + 1) // 2,
+                            128 ** -0.5, err, z=z if a.fused_norm else None, gnorm_w=gw if a.fused_norm else None)
+        canvas()
+        if which == "canvas_gdn_tc":
+            ms = _time(canvas, a.warmup, a.iters)
+        else:
+            adv = torch.full((B,), (blk + 1) // 2, device=dev, dtype=torch.int32)
+            ms = _time(lambda: C.gdn_commit_tc(kbuf, ubuf, gbuf, ssm, slot, adv, blk, Hv, err), a.warmup, a.iters)
+        return ms, {"state_gbs": nbytes / ms / 1e6, "fused_norm": bool(a.fused_norm)}, None, nbytes
+    prep = torch.empty(C.gdn_prep_numel(B * blk, Hk, Hv), device=dev)
     ms = _time(lambda: C.gdn_canvas(mixed, ga, gb, al, dtb, o, prep, ssm, slot, blk, Hk, Hv, (blk + 1) // 2,
                                     128 ** -0.5), a.warmup, a.iters)
-    nbytes = ssm.numel() * 4
     return ms, {"state_gbs": nbytes / ms / 1e6}, None, nbytes
 
 
@@ -270,7 +289,7 @@ def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--op", required=True,
                     choices=["gemm", "gemm_swiglu", "attn_fwd", "attn_bwd", "gdn_fwd", "gdn_bwd", "gdn_core_fwd", "gdn_core_bwd",
-                             "canvas_attn", "canvas_gdn",
+                             "canvas_attn", "canvas_gdn", "canvas_gdn_tc", "commit_gdn_tc",
                              "rmsnorm_fwd", "rmsnorm_bwd", "qk_rope_fwd", "qk_rope_bwd", "swiglu_fwd", "swiglu_bwd"])
     ap.add_argument("--m", type=int, default=24576)
     ap.add_argument("--n", type=int, default=6144)
@@ -289,6 +308,7 @@ def main():
     ap.add_argument("--gdn-layout", dest="layout_gdn", default="two_stream", choices=["two_stream", "causal"])
     ap.add_argument("--requests", type=int, default=64)
     ap.add_argument("--blk", type=int, default=7)
+    ap.add_argument("--fused-norm", dest="fused_norm", type=int, default=1, help="canvas_gdn_tc: 1 fuses the gated norm")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
     a = ap.parse_args()
