@@ -282,3 +282,21 @@ def test_sampled_draft_verify_runs_and_respects_eos():
     reqs = eng.generate([[1, 2, 3, 4, 5]] * 2, max_new_tokens=25, sampling=sp, eos=(7,))
     for r in reqs:
         assert r.finish_reason in ("stop", "length") and 7 not in r.output
+
+
+def test_kv_page_allocator():
+    """Pages are taken from one pool as slots grow, never past the pool or the page table, and
+    come back on release in an order that reuses them."""
+    from trida_stack_b200.serve.runtime import PAGE, KVPages
+    p = KVPages(n_pages=5, n_slots=3, max_pages=4)
+    assert p.ensure(0, 1) and p.owned[0] == [0]
+    assert not p.ensure(0, PAGE)                   # still one page
+    assert p.ensure(0, PAGE + 1) and p.owned[0] == [0, 1]
+    assert p.ensure(1, 3 * PAGE) and p.owned[1] == [2, 3, 4]
+    assert p.table[1, :3].tolist() == [2, 3, 4] and p.used() == 5
+    with pytest.raises(RuntimeError, match="exhausted"):
+        p.ensure(2, 1)
+    with pytest.raises(RuntimeError, match="page table"):
+        p.ensure(0, 5 * PAGE)
+    p.release(1)
+    assert p.used() == 2 and p.ensure(2, 2 * PAGE) and p.owned[2] == [2, 3]

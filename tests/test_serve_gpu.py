@@ -106,7 +106,7 @@ def test_paged_kv_pool_is_shared_and_recycled():
     lg = rt.prefill(s_g, ids[:, :130].tolist())
     lc = cpu.prefill(s_c, ids[:, :130].tolist())
     assert _rel(lg.cpu(), lc) < 3e-2
-    used = sum(len(p) for p in rt.slot_pages[:4])
+    used = sum(len(p) for p in rt.pages.owned[:4])
     assert used == 2 * 3                       # 130 positions (+ a canvas) -> 3 pages per request
     a = rt.canvas(s_g, ids[:, 130:137], 4)
     rt.commit(s_g, [4, 4])
@@ -119,7 +119,7 @@ def test_paged_kv_pool_is_shared_and_recycled():
     rt.pending = None
     rt.release(s_g[0])
     rt.release(s3)
-    assert len(rt.free_pages) >= 4
+    assert len(rt.pages.free) >= 4
 
 
 @pytest.mark.parametrize("mode", ["self-spec", "causal", "diffusion"])

@@ -53,9 +53,7 @@ class Runtime:
         self.max_pages = (max_len + PAGE - 1) // PAGE
         if self.paged:
             self.n_pages = kv_pages or nslot * self.max_pages
-            self.free_pages = list(range(self.n_pages))[::-1]
-            self.slot_pages = [[] for _ in range(nslot)]
-            self.ptab_host = torch.zeros(nslot, self.max_pages, dtype=torch.int32).pin_memory()
+            self.pages = KVPages(self.n_pages, nslot, self.max_pages, pin=True)
             self.ptab = torch.zeros(nslot, self.max_pages, dtype=torch.int32, device=self.device)
         for i, kind in enumerate(self.kinds):
             if kind == "full_attention":
@@ -106,8 +104,7 @@ class Runtime:
         self.pos[s] = 0
         self.free.append(s)
         if self.paged and s != self.dummy:
-            self.free_pages.extend(reversed(self.slot_pages[s]))
-            self.slot_pages[s] = []
+            self.pages.release(s)
 
     def _ensure_pages(self, slots, blk):
         """Pages for positions [0, pos + blk) of every slot (the scratch slot of padded graph
@@ -116,17 +113,9 @@ class Runtime:
             return
         changed = False
         for s in list(slots) + [self.dummy]:
-            need = ((self.pos[s] if s < self.max_slots else 0) + blk + PAGE - 1) // PAGE
-            pages = self.slot_pages[s]
-            while len(pages) < need:
-                if not self.free_pages:
-                    raise RuntimeError(f"KV page pool exhausted ({self.n_pages} pages of {PAGE} positions)")
-                pg = self.free_pages.pop()
-                self.ptab_host[s, len(pages)] = pg
-                pages.append(pg)
-                changed = True
+            changed |= self.pages.ensure(s, (self.pos[s] if s < self.max_slots else 0) + blk)
         if changed:
-            self.ptab.copy_(self.ptab_host, non_blocking=True)
+            self.ptab.copy_(self.pages.table, non_blocking=True)
 
     # ------------------------------------------------------------------ public steps
     @torch.no_grad()
@@ -534,6 +523,42 @@ class Runtime:
         y = G.gated_rmsnorm(o, z.reshape(B, blk, Hv, dv), layer.gnorm, cfg.eps)
         st.gdn[i] = (q, k, v, g, beta, conv_in)
         return self._lin(y.reshape(M, vd), layer.w_out, x)
+
+
+class KVPages:
+    """Host allocator of a paged KV cache: pages of ``PAGE`` positions taken from one pool as a slot
+    grows and returned when it is released; ``table[slot, i]`` is the page of positions
+    ``[PAGE i, PAGE (i + 1))`` (the page table the KV kernels read)."""
+
+    def __init__(self, n_pages, n_slots, max_pages, pin=False):
+        self.n_pages = n_pages
+        self.free = list(range(n_pages))[::-1]
+        self.owned = [[] for _ in range(n_slots)]
+        t = torch.zeros(n_slots, max_pages, dtype=torch.int32)
+        self.table = t.pin_memory() if pin and torch.cuda.is_available() else t
+
+    def ensure(self, slot, upto):
+        """Pages covering positions [0, upto) of ``slot``; True when the table changed."""
+        need = (upto + PAGE - 1) // PAGE
+        pages = self.owned[slot]
+        if need > self.table.shape[1]:
+            raise RuntimeError(f"slot {slot}: {upto} positions exceed the page table ({self.table.shape[1]} pages)")
+        changed = False
+        while len(pages) < need:
+            if not self.free:
+                raise RuntimeError(f"KV page pool exhausted ({self.n_pages} pages of {PAGE} positions)")
+            pg = self.free.pop()
+            self.table[slot, len(pages)] = pg
+            pages.append(pg)
+            changed = True
+        return changed
+
+    def release(self, slot):
+        self.free.extend(reversed(self.owned[slot]))
+        self.owned[slot] = []
+
+    def used(self):
+        return self.n_pages - len(self.free)
 
 
 class _Step:
