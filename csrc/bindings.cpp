@@ -586,6 +586,24 @@ void spec_sample(const at::Tensor& vals, const at::Tensor& idx, const at::Tensor
               "spec_sample failed (1 <= candidates <= 64, n <= canvas rows)");
 }
 
+// Greedy tokens of h W^T (the LM head) without materialising the logits: out int64 [M].
+void gemm_argmax(const at::Tensor& A, const at::Tensor& B, const at::Tensor& out) {
+  CHECK_BF16(A); CHECK_BF16(B); CHECK_ROWMAJOR(A); CHECK_ROWMAJOR(B);
+  TORCH_CHECK(A.size(1) == B.size(1), "K mismatch");
+  TORCH_CHECK(out.scalar_type() == at::kLong && out.is_contiguous() && out.numel() == A.size(0), "out int64 [M]");
+  const int M = A.size(0), N = B.size(0), K = A.size(1);
+  const int nt = trida::gemm_argmax_tiles(N);
+  auto val = at::empty({M, nt}, A.options().dtype(at::kFloat));
+  auto idx = at::empty({M, nt}, A.options().dtype(at::kInt));
+  trida::GemmArgs a{};
+  a.M = M; a.N = N; a.K = K; a.A = A.data_ptr(); a.lda = A.stride(0); a.B = B.data_ptr(); a.ldb = B.stride(0);
+  a.C = nullptr; a.ldc = 0; a.D = nullptr; a.ldd = 0; a.alpha = 1.f; a.beta = 0.f; a.batch = 1;
+  c10::cuda::CUDAGuard g(A.device());
+  const int rc = trida::gemm_bf16_argmax(a, val.data_ptr<float>(), idx.data_ptr<int>(), out.data_ptr<int64_t>(),
+                                         sm_count(), stream());
+  TORCH_CHECK(rc == 0, "gemm_argmax failed with code ", rc);
+}
+
 void argmax_rows(const at::Tensor& logits, const at::Tensor& out) {
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1, "fp32 logits rows");
   TORCH_CHECK(out.scalar_type() == at::kLong && out.is_contiguous() && out.numel() == logits.size(0), "out int64");
@@ -1156,6 +1174,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("slot"), py::arg("blk"), py::arg("Hk"), py::arg("Hv"), py::arg("n_clean"), py::arg("scale"),
         py::arg("err"), py::arg("z") = py::none(), py::arg("gnorm_w") = py::none(), py::arg("eps") = 1e-6);
   m.def("spec_sample", &spec_sample);
+  m.def("gemm_argmax", &gemm_argmax);
   m.def("gdn_commit_tc", &gdn_commit_tc);
   m.def("argmax_rows", &argmax_rows);
   m.def("conf_argmax_rows", &conf_argmax_rows);

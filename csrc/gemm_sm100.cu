@@ -79,6 +79,12 @@ struct Params {
   // its B slice stacks the 128 gate rows over the matching 128 up rows, and the epilogue writes
   // both halves back to D = gu [M, 2 glu_f] plus E = silu(gate) * up [M, glu_f]
   int glu_f;
+  // argmax mode (am_val != null): D is not written; each output tile leaves, per row, the max of its
+  // columns and that column's index in am_val / am_idx [M, am_ld] (column = N tile); a second
+  // kernel reduces the row's tiles (greedy tokens without materialising the logits)
+  float* am_val;
+  int* am_idx;
+  int am_ld;
 };
 
 __device__ __forceinline__ void red_release_sys(unsigned* p, unsigned v) {
@@ -437,6 +443,31 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const uint32_t acc = tmem + (ab + h) * BN + lane_off;
       const int row = m0 + h * 128 + r;
       const bool rok = row < p.M;
+      if (p.am_val != nullptr) {
+        // argmax tile: the row's best column among this tile's (first index on ties)
+        float best = -INFINITY;
+        int bidx = n0;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(acc + c * 32, v);
+          tmem_wait_ld();
+          const int col0 = n0 + c * 32;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float x = __uint_as_float(v[j]);
+            if (col0 + j < p.N && x > best) {
+              best = x;
+              bidx = col0 + j;
+            }
+          }
+        }
+        if (rok) {
+          p.am_val[(int64_t)row * p.am_ld + n0 / BN] = best;
+          p.am_idx[(int64_t)row * p.am_ld + n0 / BN] = bidx;
+        }
+        continue;
+      }
       if (p.splits > 1) {
         // split-K partial: raw fp32 accumulator to the workspace (alpha / beta applied by the reduce)
         float* wrow = p.ws + ((int64_t)(u % p.splits) * p.M + row) * p.N;
@@ -716,6 +747,7 @@ int gemm_bf16(GemmLayout layout, bool d_fp32, const GemmArgs& a, int tile, int s
   p.ar_world = 1; p.ar_rank = 0; p.ar_tiles_cap = 0; p.ar_mcap = 0;
   p.ar_ctr = nullptr; p.ar_done = nullptr; p.ar_ws = nullptr; p.ar_tile_ctr = nullptr;
   for (int i = 0; i < 8; ++i) { p.ar_recv[i] = nullptr; p.ar_flag[i] = nullptr; }
+  p.am_val = nullptr; p.am_idx = nullptr; p.am_ld = 0;
   const int kb = (a.K + BK - 1) / BK;
   p.kb_per = (kb + splits - 1) / splits;
   p.splits = (kb + p.kb_per - 1) / p.kb_per;
@@ -769,6 +801,7 @@ int gemm_bf16_allreduce(const GemmArgs& a, const GemmAllreduce& ar, int sm_count
   p.alpha = a.alpha; p.beta = a.beta; p.d_fp32 = 0;
   p.err = err_word();
   p.glu_f = 0;
+  p.am_val = nullptr; p.am_idx = nullptr; p.am_ld = 0;
   // skinny products split K over otherwise idle SMs; the split partials are summed by the last
   // arriving CTA of each tile before the exchange (workspace: ws_units tiles of 128 x 256 fp32)
   const int kb = (a.K + BK - 1) / BK;
@@ -809,6 +842,7 @@ int gemm_bf16_swiglu(const GemmArgs& a, void* act, int64_t ld_act, int F, int ti
   p.alpha = a.alpha; p.beta = 0.f; p.d_fp32 = 0;
   p.err = err_word();
   p.glu_f = F;
+  p.am_val = nullptr; p.am_idx = nullptr; p.am_ld = 0;
   p.ar_world = 1; p.ar_rank = 0; p.ar_tiles_cap = 0; p.ar_mcap = 0;
   p.ar_ctr = nullptr; p.ar_done = nullptr; p.ar_ws = nullptr; p.ar_tile_ctr = nullptr;
   for (int i = 0; i < 8; ++i) { p.ar_recv[i] = nullptr; p.ar_flag[i] = nullptr; }
@@ -820,6 +854,66 @@ int gemm_bf16_swiglu(const GemmArgs& a, void* act, int64_t ld_act, int F, int ti
   if (!make_epi_map(&mD, a.D, a.M, a.N, a.ldd, false) || !make_epi_map(&mE, act, a.M, F, ld_act, false)) return -14;
   if (mh == 2) launch<2>(mA, mB, mD, mD, mE, p, sm_count, stream);
   else launch<1>(mA, mB, mD, mD, mE, p, sm_count, stream);
+  return cudaGetLastError() == cudaSuccess ? 0 : -13;
+}
+
+namespace gemm100 {
+// Greedy tokens from the argmax epilogue's per-tile partials: one warp per row, first index on ties.
+__global__ void argmax_tiles_kernel(const float* __restrict__ val, const int* __restrict__ idx, int M, int nt,
+                                    int64_t* __restrict__ out) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= M) return;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int t = lane; t < nt; t += 32) {
+    const float v = val[(int64_t)row * nt + t];
+    const int i = idx[(int64_t)row * nt + t];
+    if (v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (v2 > best || (v2 == best && i2 < bi)) {
+      best = v2;
+      bi = i2;
+    }
+  }
+  if (lane == 0) out[row] = bi;
+}
+}  // namespace gemm100
+
+int gemm_argmax_tiles(int N) { return (N + gemm100::BN - 1) / gemm100::BN; }
+
+int gemm_bf16_argmax(const GemmArgs& a, float* am_val, int* am_idx, int64_t* out, int sm_count, cudaStream_t stream) {
+  using namespace gemm100;
+  if (a.batch != 1) return -20;
+  const int tiles256 = ((a.M + 255) / 256) * ((a.N + BN - 1) / BN);
+  const int mh = 2 * tiles256 >= sm_count ? 2 : 1;
+  Params p;
+  p.M = a.M; p.N = a.N; p.K = a.K;
+  p.D = am_val; p.ldd = 0; p.C = nullptr; p.ldc = 0;
+  p.alpha = 1.f; p.beta = 0.f; p.d_fp32 = 1;
+  p.err = err_word();
+  p.glu_f = 0;
+  p.ar_world = 1; p.ar_rank = 0; p.ar_tiles_cap = 0; p.ar_mcap = 0;
+  p.ar_ctr = nullptr; p.ar_done = nullptr; p.ar_ws = nullptr; p.ar_tile_ctr = nullptr;
+  for (int i = 0; i < 8; ++i) { p.ar_recv[i] = nullptr; p.ar_flag[i] = nullptr; }
+  const int nt = (a.N + BN - 1) / BN;
+  p.am_val = am_val; p.am_idx = am_idx; p.am_ld = nt;
+  const int kb = (a.K + BK - 1) / BK;
+  p.splits = 1; p.kb_per = kb; p.ws = nullptr;
+  p.a_kmajor = 1; p.b_kmajor = 1;
+  CUtensorMap mA, mB, mD;
+  if (!make_map(&mA, a.A, a.M, a.K, a.lda, 128 * mh) || !make_map(&mB, a.B, a.N, a.K, a.ldb, BN)) return -12;
+  // D is never written in argmax mode; the epilogue map only has to be a valid descriptor (A's)
+  if (!make_map(&mD, a.A, a.M, a.K, a.lda, 32)) return -14;
+  if (mh == 2) launch<2>(mA, mB, mD, mD, mD, p, sm_count, stream);
+  else launch<1>(mA, mB, mD, mD, mD, p, sm_count, stream);
+  argmax_tiles_kernel<<<(a.M + 7) / 8, 256, 0, stream>>>(am_val, am_idx, a.M, nt, out);
   return cudaGetLastError() == cudaSuccess ? 0 : -13;
 }
 

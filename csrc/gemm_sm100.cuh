@@ -55,6 +55,12 @@ int gemm_bf16_allreduce(const GemmArgs& a, const GemmAllreduce& ar, int sm_count
 // Gate / up projection with SwiGLU in the epilogue (TN, bf16): B = [gate; up] ([2F, K], F a multiple
 // of 64), D = gu = alpha * A B^T ([M, 2F]) and act = silu(gu[:, :F]) * gu[:, F:] ([M, F]) from the
 // bf16-rounded gu values, in one kernel.  `tile`: 0 picks the tile height, 1 = 128 rows, 2 = 256.
+// Greedy tokens of D = A B^T (TN, the LM head) without writing D: the epilogue keeps, per row and
+// 256-column tile, the max and its column ([M, gemm_argmax_tiles(N)] in am_val / am_idx), and a
+// second kernel reduces the tiles into out[M] (int64; the first column on ties).
+int gemm_argmax_tiles(int N);
+int gemm_bf16_argmax(const GemmArgs& a, float* am_val, int* am_idx, int64_t* out, int sm_count, cudaStream_t stream);
+
 int gemm_bf16_swiglu(const GemmArgs& a, void* act, int64_t ld_act, int F, int tile, int sm_count,
                      cudaStream_t stream);
 

@@ -28,7 +28,7 @@ KERNELS_PER_CALL = {
     "bd_attn_bwd": 3, "ce_rows": 1, "adamw": 1, "bd_attn_lists128": 1, "bd_attn_fwd_sm100": 1, "bd_attn_bwd_sm100": 5, "bd_attn_tile_masks": 1,
     "gemm_error": 0, "gdn_state_numel": 0, "gdn_fwd": 2, "gdn_bwd": 3, "gdn_conv_fwd": 1, "gdn_conv_bwd": 2,
     "gdn_gnorm_fwd": 1, "gdn_gnorm_bwd": 1, "attn_gate_fwd": 1, "attn_gate_bwd": 1,
-    "canvas_attention": 2, "kv_append": 1, "canvas_conv": 1, "conv_commit": 1, "gdn_canvas": 2, "gdn_prep_numel": 0, "gdn_commit": 1, "gdn_canvas_tc": 1, "gdn_commit_tc": 1, "spec_sample": 1,
+    "canvas_attention": 2, "kv_append": 1, "canvas_conv": 1, "conv_commit": 1, "gdn_canvas": 2, "gdn_prep_numel": 0, "gdn_commit": 1, "gdn_canvas_tc": 1, "gdn_commit_tc": 1, "spec_sample": 1, "gemm_argmax": 2,
     "argmax_rows": 1, "conf_argmax_rows": 1, "gemm_swiglu": 1, "gemm_allreduce": 1, "symm_malloc": 0, "symm_free": 0, "symm_handle": 0, "symm_open": 0, "symm_close": 0,
     "symm_tensor": 0, "symm_allreduce": 1, "symm_rs_sumsq": 1, "symm_norm_coef": 1, "symm_adamw_ag": 1,
 }

@@ -295,10 +295,10 @@ class Engine:
         reqs = self.running
         slots = [r.slot for r in reqs]
         n, blk, K = self.n, self.blk, self.n - 1
+        greedy = all(r.sampling.greedy for r in reqs)
         if self.mode == "causal":
             toks = [[r.output[-1] if r.output else r.t0] for r in reqs]
-            logits = self.rt.canvas(slots, toks, 1)
-            greedy = all(r.sampling.greedy for r in reqs)
+            logits = self.rt.canvas(slots, toks, 1, greedy=greedy)
             am = self.rt.argmax(logits)[:, 0].tolist() if greedy else None
             picks = [[am[b]] if greedy else self._pick(logits[b], r) for b, r in enumerate(reqs)]
             self.rt.commit(slots, [1] * len(reqs))
@@ -314,9 +314,8 @@ class Engine:
                 canv.append([r.pending] + r.specs + [self.mask_id] * (n - 1))
             else:
                 canv.append([r.t0] + [self.mask_id] * (blk - 1))
-        logits = self.rt.canvas(slots, canv, n)
+        logits = self.rt.canvas(slots, canv, n, greedy=greedy)
         self.stats["forwards"] += 1
-        greedy = all(r.sampling.greedy for r in reqs)
         if not greedy and self._device_sampling_ok(reqs):
             return self._decode_spec_device(reqs, slots, logits)
         am = self.rt.argmax(logits).tolist() if greedy else None

@@ -168,10 +168,13 @@ class Runtime:
         self._graphs = {}
 
     @torch.no_grad()
-    def canvas(self, slots, tokens, n_clean, rows=None, inject=None, rope_ang=None):
+    def canvas(self, slots, tokens, n_clean, rows=None, inject=None, rope_ang=None, greedy=False):
         """One forward over a [B, blk] canvas per slot.  Returns fp32 logits [B, r1 - r0, V] for the
         canvas rows ``rows = (r0, r1)`` (all rows by default).  Call ``commit`` afterwards.  With
-        graphs on, the returned tensor is a static buffer valid until the next canvas."""
+        graphs on, the returned tensor is a static buffer valid until the next canvas.  ``greedy``
+        (CUDA, no tensor parallelism, all rows): the LM head's argmax is fused into its GEMM and the
+        result only carries the greedy tokens (``argmax`` reads them); no logits are written."""
+        greedy = greedy and self.cuda and self.tp is None and rows is None
         assert self.pending is None, "commit the previous canvas first"
         B = len(slots)
         blk = len(tokens[0])
@@ -181,7 +184,7 @@ class Runtime:
         self._ensure_pages(slots, blk)
         r0, r1 = rows if rows is not None else (0, blk)
         if self._graphs is not None and (r0, r1) == (0, blk) and inject is None and rope_ang is None:
-            return self._canvas_graph(slots, tokens, n_clean)
+            return self._canvas_graph(slots, tokens, n_clean, greedy)
         tokens = torch.as_tensor(tokens, dtype=torch.long, device=self.device)
         st = _Step(self, slots, B, blk, n_clean)
         st.inject, st.rope_ang = inject, rope_ang
@@ -189,14 +192,25 @@ class Runtime:
         self.pending = st
         if r1 <= r0:
             return torch.empty(B, 0, self.cfg.vocab_size, device=self.device)
+        if greedy:
+            return GreedyTokens(self._greedy_tokens(x).view(B, blk))
         h = x.view(B, blk, -1)[:, r0:r1].reshape(B * (r1 - r0), -1)
         return self._logits(h).view(B, r1 - r0, -1)
+
+    def _greedy_tokens(self, x):
+        """Greedy tokens of hidden rows: final norm, then the LM-head GEMM with its argmax epilogue."""
+        h = self._rms(x, self.dec.norm)
+        out = torch.empty(h.shape[0], dtype=torch.long, device=h.device)
+        self.C.gemm_argmax(h, self.dec.lm_weight, out)
+        return out
 
     def argmax(self, logits):
         """Greedy tokens [B, rows] of fp32 logits [B, rows, V] (the argmax kernel on CUDA; taken
         from the captured graph when ``logits`` is the graph's output)."""
+        if isinstance(logits, GreedyTokens):
+            return logits.tokens
         g = self.pending
-        if isinstance(g, _Graph) and logits.data_ptr() == g.logits.data_ptr():
+        if isinstance(g, _Graph) and g.logits is not None and logits.data_ptr() == g.logits.data_ptr():
             return g.am[:logits.shape[0]]
         if not self.cuda:
             out = logits.argmax(-1)
@@ -254,13 +268,13 @@ class Runtime:
             x = self._mlp(layer, x)
         return x
 
-    def _canvas_graph(self, slots, tokens, n_clean):
+    def _canvas_graph(self, slots, tokens, n_clean, greedy=False):
         B, blk = len(slots), len(tokens[0])
         Bp = next(b for b in self.graph_buckets if b >= B)
-        key = (Bp, blk, n_clean)
+        key = (Bp, blk, n_clean, greedy)
         g = self._graphs.get(key)
         if g is None:
-            g = self._graphs[key] = _Graph(self, Bp, blk, n_clean)
+            g = self._graphs[key] = _Graph(self, Bp, blk, n_clean, greedy)
         pad = Bp - B
         g.host_tok[:B] = torch.as_tensor(tokens, dtype=torch.long)
         g.host_tok[B:] = 0
@@ -276,7 +290,7 @@ class Runtime:
         g.fwd.replay()
         g.st.slots = list(slots)
         self.pending = g
-        return g.logits[:B]
+        return GreedyTokens(g.am[:B]) if greedy else g.logits[:B]
 
     @torch.no_grad()
     def commit(self, slots, adv):
@@ -525,6 +539,17 @@ class Runtime:
         return self._lin(y.reshape(M, vd), layer.w_out, x)
 
 
+class GreedyTokens:
+    """The result of a greedy canvas: the tokens [B, rows] in place of the logits."""
+
+    def __init__(self, tokens):
+        self.tokens = tokens
+        self.shape = tuple(tokens.shape)
+
+    def __getitem__(self, i):
+        return GreedyTokens(self.tokens[i])
+
+
 class KVPages:
     """Host allocator of a paged KV cache: pages of ``PAGE`` positions taken from one pool as a slot
     grows and returned when it is released; ``table[slot, i]`` is the page of positions
@@ -591,7 +616,7 @@ class _Graph:
     (padded batch, canvas rows, clean rows) shape.  Captured after one eager warm-up run on the
     scratch slot, which also initialises every kernel's launch attributes."""
 
-    def __init__(self, rt, B, blk, n_clean):
+    def __init__(self, rt, B, blk, n_clean, greedy=False):
         self.st = _Step(rt, [rt.dummy] * B, B, blk, n_clean, static=True)
         self.adv = torch.ones(B, dtype=torch.int32, device=rt.device)
         self.host_tok = torch.zeros(B, blk, dtype=torch.long).pin_memory()
@@ -602,6 +627,8 @@ class _Graph:
 
         def fwd():
             x = rt._forward(self.st, self.st.tokens)
+            if greedy:                   # tokens only: the LM head's argmax runs in its GEMM epilogue
+                return None, rt._greedy_tokens(x).view(B, blk)
             lg = rt._logits(x).view(B, blk, -1)
             return lg, rt.argmax(lg)
 
