@@ -50,6 +50,9 @@ def parse():
     p.add_argument("--phase-split", type=int, default=0, metavar="STEPS",
                    help="after the timed steps, STEPS more steps with CUDA events around forward, backward and "
                         "the optimizer step (device ms, mean over steps, max over ranks) in the JSON line")
+    p.add_argument("--kernel-breakdown", type=int, default=0, metavar="STEPS",
+                   help="after everything else, print the per-kernel device-time table of STEPS more steps "
+                        "(1 GPU; taken under the PyTorch profiler, not a benchmark number)")
     p.add_argument("--shard", choices=["full", "zero2"], default="full",
                    help="full: decoder-layer weights sharded and gathered per layer over NVLink (FSDP full "
                         "shard, the reference's setup); zero2: replicated weights")
@@ -214,6 +217,18 @@ def run_ours(args, rank, world, local_rank):
             for k, (a, z) in zip(sums, ((0, 1), (1, 2), (2, 3))):
                 sums[k] += ev[a].elapsed_time(ev[z]) / args.phase_split
         phases = {k: round(max_over_ranks(v), 2) for k, v in sums.items()}
+
+    if args.kernel_breakdown and world == 1:
+        from trida_stack_b200.utils.trace import kernel_breakdown
+        extra = iter(range(args.kernel_breakdown))
+
+        def one():
+            nonlocal step
+            j = next(extra)
+            engine.micro_step(dev_batches[(args.warmup + j) % len(dev_batches)], rpad=rpad)
+            engine.optimizer_step(step)
+            step += 1
+        kernel_breakdown(one, args.kernel_breakdown, top=24)
 
     e2e = None
     if not args.no_e2e:

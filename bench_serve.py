@@ -52,6 +52,9 @@ def main():
                          "steps of a fresh batch (taken under the PyTorch profiler; not a benchmark number)")
     ap.add_argument("--tp-fused", action="store_true",
                     help="TP all-reduce in the GEMM epilogue instead of a separate kernel after the GEMM")
+    ap.add_argument("--tp-allreduce", action="store_true",
+                    help="replicated residual with a one-shot all-reduce kernel after each row-parallel GEMM "
+                         "instead of the sequence-parallel reduce-scatter + norm + all-gather kernel")
     args = ap.parse_args()
 
     from trida_stack_b200.models import Decoder
@@ -77,7 +80,8 @@ def main():
         from trida_stack_b200.serve.tp import TPContext, shard_decoder
         dec = shard_decoder(dec, rank, world)
         torch.cuda.empty_cache()
-        tp = TPContext(max_rows=args.requests * 64, hidden=cfg.hidden_size, fused=args.tp_fused)
+        tp = TPContext(max_rows=args.requests * 64, hidden=cfg.hidden_size, fused=args.tp_fused,
+                        seq_parallel=not args.tp_allreduce)
     rt = Runtime(dec, max_slots=args.requests, max_len=max_len, tp=tp)
     eng = Engine(rt, mask_id=mask_id, mode=args.mode, n=args.gen_block, max_running=args.requests, graphs=not args.no_graphs)
     g = torch.Generator().manual_seed(args.seed)
@@ -125,7 +129,9 @@ def main():
                    "prompt": args.prompt, "max_new": args.max_new, "mode": args.mode, "n": args.gen_block,
                    "canvas_rows": 2 * args.gen_block - 1 if args.mode == "self-spec" else 1, "greedy": True,
                    "cuda_graphs": not args.no_graphs,
-                   "tp_allreduce": ("fused into the GEMM epilogue" if args.tp_fused else "separate peer-memory kernel")
+                   "tp_collective": ("all-reduce fused into the GEMM epilogue" if args.tp_fused else
+                                     "one-shot all-reduce kernel" if args.tp_allreduce else
+                                     "sequence-parallel reduce-scatter + RMSNorm + all-gather kernel")
                    if world > 1 else None},
         "data": "synthetic uniform prompts, random-init weights", "dtype": "bf16"}), flush=True)
     if args.kernel_breakdown > 0 and world == 1:

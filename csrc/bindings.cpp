@@ -144,6 +144,27 @@ void symm_allreduce(const std::vector<int64_t>& bufs, const std::vector<int64_t>
   TORCH_CHECK(rc == 0, "symm_allreduce failed with code ", rc);
 }
 
+// Sequence-parallel boundary (tensor-parallel serving): parts / gather are every rank's symmetric
+// partial [M, D] and gather [M, D] bf16 buffers; xs [nrows, D] bf16 is this rank's residual rows
+// starting at row0 (updated in place); ctr_done int32 [2], zero at start.
+void symm_rs_norm_ag(const std::vector<int64_t>& parts, const std::vector<int64_t>& gather,
+                     const std::vector<int64_t>& flags, int64_t rank, const at::Tensor& ctr_done, int64_t row0,
+                     const at::Tensor& xs, const at::Tensor& w, double eps, const at::Tensor& err) {
+  TORCH_CHECK(ctr_done.scalar_type() == at::kInt && ctr_done.numel() >= 2, "ctr_done must be int32 [2]");
+  TORCH_CHECK(gather.size() == parts.size(), "one gather buffer per rank");
+  auto a = ptr_arrays(parts, flags);
+  void* g[8] = {};
+  for (size_t i = 0; i < gather.size(); ++i) g[i] = reinterpret_cast<void*>(gather[i]);
+  CHECK_BF16(xs); CHECK_BF16(w);
+  TORCH_CHECK(xs.dim() == 2 && xs.is_contiguous() && w.is_contiguous() && w.numel() == xs.size(1),
+              "xs [rows, D] contiguous, w [D]");
+  TORCH_CHECK((uintptr_t)xs.data_ptr() % 16 == 0 && (uintptr_t)w.data_ptr() % 16 == 0, "16-byte aligned rows");
+  unsigned* cd = reinterpret_cast<unsigned*>(ctr_done.data_ptr<int>());
+  const int rc = trida::symm_rs_norm_ag(a.bufs, g, a.flags, rank, parts.size(), cd, xs.size(1), row0, xs.size(0),
+                                        mbf(xs), cbf(w), (float)eps, err.data_ptr<int>(), sm_count(), stream());
+  TORCH_CHECK(rc == 0, "symm_rs_norm_ag failed with code ", rc, " (D must be a multiple of 8, at most 8192)");
+}
+
 // Row-parallel GEMM with the tensor-parallel all-reduce in its epilogue:
 // D = sum over ranks of A_r B_r^T (+ residual).  recv / flags: every rank's receive buffer
 // ([2][world][mcap][N] bf16) and counters ([2][tiles_cap][4] u32); ctr_done: int32 [2], zero at start.
@@ -1140,6 +1161,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);
   m.def("symm_tensor", &symm_tensor);
+  m.def("symm_rs_norm_ag", &symm_rs_norm_ag);
   m.def("symm_allreduce", &symm_allreduce);
   m.def("gemm_allreduce", &gemm_allreduce, py::arg("A"), py::arg("B"), py::arg("D"), py::arg("residual"),
         py::arg("recv"), py::arg("flags"), py::arg("rank"), py::arg("ctr_done"), py::arg("mcap"),

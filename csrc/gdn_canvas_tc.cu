@@ -366,6 +366,13 @@ __global__ void __launch_bounds__(NT) canvas_kernel(const CanvasArgs a) {
     umma_commit(bar);
   }
   ok = ph.wait() && ok;
+  if (a.z != nullptr) {                // the fused norm's gate rows into the K tile (free once phase 2 ran),
+    for (int it = t; it < C * 16; it += NT) {      // in flight under phases 3 and 4
+      const int r = it >> 4, j = it & 15;
+      if (r < n) cp_async16(tK + off64(r, 8 * j), a.z + ((int64_t)b * n + r) * a.ldz + hv * 128 + 8 * j);
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+  }
   if (w < 2) {                         // -W over Vb (the U~ product has read it)
     float x[32];
 #pragma unroll 1
@@ -404,6 +411,7 @@ __global__ void __launch_bounds__(NT) canvas_kernel(const CanvasArgs a) {
     }
   }
   // ---- phase 4: O = Qg S0 + P U ----
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -432,12 +440,18 @@ __global__ void __launch_bounds__(NT) canvas_kernel(const CanvasArgs a) {
     for (int g4 = 0; g4 < 4; ++g4) {
       tld32(tmem + 32 * g4, x);
       if (a.z != nullptr && live) {
-        const bf16* zr = a.z + row * a.ldz + hv * 128 + 32 * g4;
         const bf16* wr = a.gnorm_w + 32 * g4;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           float zf[8], wf[8];
-          ld8(zr + 8 * j, zf);
+          const uint4 zv = *reinterpret_cast<const uint4*>(tK + off64(t, 32 * g4 + 8 * j));
+          const uint32_t z4[4] = {zv.x, zv.y, zv.z, zv.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&z4[i]));
+            zf[2 * i] = f.x;
+            zf[2 * i + 1] = f.y;
+          }
           ld8(wr + 8 * j, wf);
 #pragma unroll
           for (int i = 0; i < 8; ++i) x[8 * j + i] *= rs * wf[i] * (zf[i] / (1.f + __expf(-zf[i])));

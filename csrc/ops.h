@@ -187,6 +187,9 @@ void conf_argmax_rows(const float* logits, int rows, int rpb, int64_t sb, int64_
 
 // ---- symmetric peer memory collectives (symm.cu) ----
 // bufs / flags: one pointer per rank (this rank's own at index `rank`, peers' IPC-mapped).
+int symm_rs_norm_ag(void* const* parts, void* const* gather, unsigned* const* flags, int rank, int world,
+                    unsigned* ctr, int D, int64_t row0, int nrows, bf16* xs, const bf16* w, float eps, int* err,
+                    int sm_count, cudaStream_t s);
 int symm_allreduce_bf16(void* const* bufs, unsigned* const* flags, int rank, int world, unsigned* ctr, unsigned* done,
                         int64_t off, int64_t n, const bf16* residual, bf16* out, int* err, int sm_count,
                         cudaStream_t s);

@@ -19,6 +19,9 @@
 //   adamw_ag    sharded AdamW on the reduced shard with the bf16 result stored straight into
 //               every peer's parameter buffer (the all-gather fused into the update), then a
 //               closing barrier so no rank reads parameters that are still being written.
+//   rs_norm_ag  tensor-parallel sequence-parallel boundary: reduce-scatter of a row-parallel
+//               GEMM's partials, residual add and RMSNorm on the owned rows, all-gather of the
+//               normalised rows by P2P stores, between two barriers.
 // No collective here uses TMA or multicast; NCCL stays the baseline path.
 #include <cuda_runtime.h>
 
@@ -223,6 +226,94 @@ __global__ void gather_kernel(Peers P, int rank, int world, int64_t shard_len, b
   }
 }
 
+// Sequence-parallel boundary after a row-parallel GEMM (tensor-parallel serving).  Every rank holds
+// its partial product [M, D] in its symmetric buffer P.buf[rank]; rank r owns rows [row0, row0 +
+// nrows) of the residual stream (`xs`, bf16, local).  One kernel does the reduce-scatter, the
+// residual add, the next sublayer's RMSNorm and the all-gather of its input:
+//   opening barrier (every rank's partial is written), then per owned row: sum the W partial rows
+//   (P2P loads, fp32), add the residual row, round to bf16 into `xs`, RMSNorm with `w`, and store
+//   the normalised row into every rank's gather buffer H[k] (P2P stores); closing barrier (the last
+//   CTA of each rank signals every peer once all its rows are out and waits for theirs), so when
+//   the kernel completes this rank's gather buffer holds all M normalised rows and no peer still
+//   reads this rank's partial buffer.
+// Bytes per rank over NVLink: (W-1)/W of the partial in and (W-1)/W of the normalised rows out --
+// half of what a one-shot all-reduce reads at W = 2 and 2/W of it in general.  Each row is reduced
+// by exactly one rank, so every rank sees bitwise the same normalised rows.
+struct PeerBufs {
+  void* p[MAXR];
+};
+
+__device__ __forceinline__ uint32_t pk2(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+constexpr int SP_OPEN = 6, SP_CLOSE = 7;   // flag slots of the two barriers
+
+__global__ void rs_norm_ag_kernel(Peers P, PeerBufs H, int rank, int world, unsigned* ctr, int D, int64_t row0,
+                                  int nrows, bf16* __restrict__ xs, const bf16* __restrict__ w, float eps, int* err) {
+  const unsigned epoch = *reinterpret_cast<volatile unsigned*>(ctr) + 1;
+  barrier(P, rank, world, epoch, SP_OPEN, err, 270);
+  __shared__ float sred[32];
+  const int nv = D / 8, v = threadIdx.x;
+  for (int r = blockIdx.x; r < nrows; r += gridDim.x) {
+    const int64_t g = (row0 + r) * (int64_t)D + 8 * v;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float ss = 0.f;
+    if (v < nv) {
+      for (int k = 0; k < world; ++k) {
+        const int src = (rank + k) % world;        // stagger the peers each rank reads first
+        float t[8];
+        load8(reinterpret_cast<const bf16*>(P.buf[src]) + g, t);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += t[e];
+      }
+      bf16* xr = xs + (int64_t)r * D + 8 * v;
+      float res[8];
+      load8(xr, res);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        acc[e] = __bfloat162float(__float2bfloat16(acc[e] + res[e]));   // the stream is bf16
+        ss += acc[e] * acc[e];
+      }
+      store8(xr, acc);
+    }
+    const float rstd = rsqrtf(block_sum(ss, sred) / (float)D + eps);
+    if (v < nv) {
+      float wf[8];
+      load8(w + 8 * v, wf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = acc[e] * rstd * wf[e];
+      const uint4 o = make_uint4(pk2(acc[0], acc[1]), pk2(acc[2], acc[3]), pk2(acc[4], acc[5]), pk2(acc[6], acc[7]));
+      for (int k = 0; k < world; ++k) {
+        const int dst = (rank + k) % world;
+        *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(H.p[dst]) + g) = o;
+      }
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned* done = ctr + 1;
+    if (atomicAdd(done, 1u) == gridDim.x - 1) {
+      *done = 0u;
+      for (int k = 0; k < world; ++k) st_release(P.flag[k] + SP_CLOSE * MAXR + rank, epoch);
+      for (int k = 0; k < world; ++k) {
+        const unsigned* f = P.flag[rank] + SP_CLOSE * MAXR + k;
+        long long polls = 0;
+        while ((int)(ld_acquire(f) - epoch) < 0) {
+          if (++polls > kMaxPolls) {
+            atomicExch(err, 271);
+            break;
+          }
+          if (polls > 64) __nanosleep(128);
+        }
+      }
+      *ctr = epoch;
+      __threadfence();
+    }
+  }
+}
+
 // A bare cross-rank barrier on `slot` (one CTA).
 __global__ void barrier_kernel(Peers P, int rank, int world, unsigned epoch, int slot, int* err) {
   barrier(P, rank, world, epoch, slot, err, 260 + slot);
@@ -276,6 +367,19 @@ int symm_allreduce_bf16(void* const* bufs, unsigned* const* flags, int rank, int
   if (blocks < 1) blocks = 1;
   symm::allreduce_kernel<<<blocks, 256, 0, s>>>(make_peers(bufs, flags, world), rank, world, ctr, done, off, n,
                                                 residual, out, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int symm_rs_norm_ag(void* const* parts, void* const* gather, unsigned* const* flags, int rank, int world,
+                    unsigned* ctr, int D, int64_t row0, int nrows, bf16* xs, const bf16* w, float eps, int* err,
+                    int sm_count, cudaStream_t s) {
+  if (world > symm::MAXR || D % 8 || D / 8 > 1024 || nrows < 0) return -1;
+  symm::PeerBufs H{};
+  for (int r = 0; r < world; ++r) H.p[r] = gather[r];
+  const int threads = ((D / 8 + 31) / 32) * 32;
+  const int blocks = std::max(1, std::min(nrows, sm_count * 2));
+  symm::rs_norm_ag_kernel<<<blocks, threads, 0, s>>>(make_peers(parts, flags, world), H, rank, world, ctr, D, row0,
+                                                     nrows, xs, w, eps, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 

@@ -98,25 +98,47 @@ class _ThreadTP:
     """CPU stand-in for TPContext: W runtimes in W threads sum their row-parallel partials and
     gather their argmax pairs through shared slots and a barrier."""
 
-    def __init__(self, shared, rank, world):
-        self.s, self.rank, self.world = shared, rank, world
+    def __init__(self, shared, rank, world, seq_parallel=False):
+        self.s, self.rank, self.world, self.seq_parallel = shared, rank, world, seq_parallel
 
-    def _exchange(self, t):
+    def _exchange_list(self, t):
         self.s["slots"][self.rank] = t
         self.s["bar"].wait()
-        out = torch.stack(list(self.s["slots"]))
+        out = list(self.s["slots"])
         self.s["bar"].wait()
         return out
 
+    def _exchange(self, t):
+        return torch.stack(self._exchange_list(t))
+
     def row_parallel(self, x, w, residual):
         return residual + self._exchange(x @ w.t()).sum(0)
+
+    # sequence-parallel boundary, as TPContext.own_rows / shard / reduce_norm state it
+    def own_rows(self, rows):
+        per = -(-rows // self.world)
+        r0 = min(rows, self.rank * per)
+        return r0, min(rows, r0 + per) - r0
+
+    def shard(self, x):
+        r0, n = self.own_rows(x.shape[0])
+        return x[r0:r0 + n].clone()
+
+    def reduce_norm(self, a, w, xs, norm_w, eps):
+        from trida_stack_b200.ops import reference as R
+        tot = self._exchange(a @ w.t()).sum(0)
+        r0, n = self.own_rows(a.shape[0])
+        assert xs.shape[0] == n
+        xs = xs + tot[r0:r0 + n]
+        return xs, torch.cat(self._exchange_list(R.rmsnorm(xs, norm_w, eps)))
 
     def gather(self, t):
         return self._exchange(t)
 
 
+@pytest.mark.parametrize("seq_parallel", [False, True])
 @pytest.mark.parametrize("world", [2, 4])
-def test_tensor_parallel_shards_reproduce_full_model(world):
+def test_tensor_parallel_shards_reproduce_full_model(world, seq_parallel):
     import threading
 
     from trida_stack_b200.serve.tp import shard_decoder
@@ -135,7 +157,7 @@ def test_tensor_parallel_shards_reproduce_full_model(world):
     def run(r):
         try:
             local = shard_decoder(dec, r, world)
-            eng = Engine(Runtime(local, max_slots=4, max_len=128, tp=_ThreadTP(shared, r, world)), mask_id=96,
+            eng = Engine(Runtime(local, max_slots=4, max_len=128, tp=_ThreadTP(shared, r, world, seq_parallel)), mask_id=96,
                          mode="self-spec", n=3)
             outs[r] = [q.output for q in eng.generate(prompts, max_new_tokens=16)]
         except Exception as e:   # surface in the main thread

@@ -178,6 +178,124 @@ def test_fused_gemm_allreduce_matches_nccl():
     assert all(p.exitcode == 0 for p in procs)
 
 
+def _seqpar_worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from trida_stack_b200.serve.tp import TPContext
+        bf = torch.bfloat16
+        H, eps = 2560, 1e-6
+        tp = TPContext(max_rows=1200, hidden=H)
+        assert tp.seq_parallel
+        errs = []
+        g = torch.Generator("cuda").manual_seed(10 + rank)
+
+        def rel(a, b):
+            return ((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-6)).item()
+
+        def reference(a, w, res, nw):
+            part = (a.float() @ w.float().t()).to(bf)               # each rank's GEMM output is bf16
+            allp = [torch.zeros_like(part) for _ in range(world)]
+            dist.all_gather(allp, part)
+            x = (res.float() + sum(p.float() for p in allp)).to(bf).float()
+            return x, x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * nw.float()
+
+        for M, K in ((1, 512), (301, 512), (448, 1024), (1100, 512)):   # fewer rows than ranks, uneven split
+            a = torch.randn(M, K, device="cuda", dtype=bf, generator=g)
+            w = torch.randn(H, K, device="cuda", dtype=bf, generator=g) * 0.05
+            res = torch.randn(M, H, device="cuda", dtype=bf)
+            nw = (1 + 0.1 * torch.randn(H, device="cuda")).to(bf)
+            dist.broadcast(res, 0)
+            dist.broadcast(nw, 0)
+            x_ref, h_ref = reference(a, w, res, nw)
+            r0, n = tp.own_rows(M)
+            xs, h = tp.reduce_norm(a, w, res[r0:r0 + n].clone(), nw, eps)
+            if n:
+                errs.append(rel(xs, x_ref[r0:r0 + n]))
+            errs.append(rel(h, h_ref))
+            hs = [torch.zeros_like(h) for _ in range(world)]
+            dist.all_gather(hs, h.contiguous())
+            assert all(torch.equal(hs[0], t) for t in hs), "ranks hold different normalised rows"
+        # two boundaries in a row, replayed from a CUDA graph (the epoch counter lives on the device)
+        M, K = 448, 512
+        a = torch.randn(M, K, device="cuda", dtype=bf, generator=g)
+        w = torch.randn(H, K, device="cuda", dtype=bf, generator=g) * 0.05
+        res = torch.randn(M, H, device="cuda", dtype=bf)
+        nw = (1 + 0.1 * torch.randn(H, device="cuda")).to(bf)
+        dist.broadcast(res, 0)
+        dist.broadcast(nw, 0)
+        r0, n = tp.own_rows(M)
+        xs = res[r0:r0 + n].clone()
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=s):
+                tp.reduce_norm(a, w, xs, nw, eps)
+                _, h = tp.reduce_norm(a, w, xs, nw, eps)
+        x_full = res.clone()
+        for _ in range(3):
+            gr.replay()
+            torch.cuda.synchronize()
+            for _ in range(2):
+                x_next, h_ref = reference(a, w, x_full, nw)
+                x_full = x_next.to(bf)
+            errs.append(rel(xs, x_full[r0:r0 + n]))
+            errs.append(rel(h, h_ref))
+        del gr
+        tp.heap.check()
+        # a sharded hybrid decoder on the CUDA runtime reproduces the single-GPU logits
+        from test_serve_gpu import _hybrid, _init
+
+        from trida_stack_b200.serve import Runtime
+        from trida_stack_b200.serve.tp import shard_decoder
+        dec = _init(_hybrid(128)).to("cuda", bf)
+        torch.manual_seed(4)
+        prompts = [torch.randint(0, 500, (40,)).tolist() for _ in range(3)]
+        canv = [torch.randint(0, 500, (9,)).tolist() for _ in range(3)]
+        ref_rt = Runtime(dec, max_slots=4, max_len=256)
+        sl = [ref_rt.alloc() for _ in prompts]
+        ref_rt.prefill(sl, prompts)
+        want = ref_rt.canvas(sl, canv, 5).float()
+        ref_rt.discard()
+        local = shard_decoder(dec, rank, world)
+        rt = Runtime(local, max_slots=4, max_len=256, tp=TPContext(max_rows=512, hidden=dec.cfg.hidden_size))
+        sl = [rt.alloc() for _ in prompts]
+        rt.prefill(sl, prompts)
+        got = rt.canvas(sl, canv, 5).float()
+        vp = got.shape[-1]
+        errs.append(rel(got[..., :min(vp, want.shape[-1] - rank * vp)], want[..., rank * vp:(rank + 1) * vp]))
+        q.put((rank, max(errs)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_sequence_parallel_boundary_matches_reference():
+    """Reduce-scatter + residual + RMSNorm + all-gather in one kernel (tensor-parallel serving) vs an
+    fp32 statement over NCCL-gathered partials: uneven row splits, fewer rows than ranks, CUDA-graph
+    replay, and a sharded hybrid decoder's logits against the single-GPU runtime, on 2 GPUs."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_seqpar_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    res = [q.get(timeout=5) for _ in range(2)]
+    for rank, err in res:
+        assert err < 3e-2, (rank, err)
+    assert all(p.exitcode == 0 for p in procs)
+
+
 def _shard_worker(rank, world, port, q):
     """A tiny dense decoder (3 layers, CUDA blocks) trained for 3 steps with replicated weights
     (fused optimizer collectives) and with full-shard weights gathered per layer over NVLink (with

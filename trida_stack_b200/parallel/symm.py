@@ -11,8 +11,8 @@ import torch.distributed as dist
 
 from ..ops._ext import ext
 
-NSLOTS = 6          # barrier slots: all-reduce, reduce-scatter, AdamW close, norm, streamed reduce-scatter close,
-                    # full-shard update close
+NSLOTS = 8          # barrier slots: all-reduce, reduce-scatter, AdamW close, norm, streamed reduce-scatter close,
+                    # full-shard update close, tensor-parallel sequence-parallel open and close
 RING_CLOSE_SLOT = 4
 SHARD_CLOSE_SLOT = 5
 MAXR = 8

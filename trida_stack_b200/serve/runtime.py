@@ -86,6 +86,9 @@ class Runtime:
             # canvas gated-delta step: the chunked form on tensor cores (commit from the stored U
             # rows), or the per-token scan kernels (commit re-runs the accepted rows)
             self.gdn_tc = os.environ.get("TRIDA_GDN_CANVAS", "tc") == "tc"
+            # gated RMSNorm in the canvas kernel's epilogue (TRIDA_GDN_FUSED_NORM=1) or as its own
+            # kernel after it (default: measured 0.26 + 0.03 ms against 0.37 ms fused at 64 x 63 rows)
+            self.gdn_fused_norm = os.environ.get("TRIDA_GDN_FUSED_NORM", "0") == "1"
             self.err = blocks.device_error_word(self.device)
 
     # ------------------------------------------------------------------ slots
@@ -194,8 +197,10 @@ class Runtime:
             return torch.empty(B, 0, self.cfg.vocab_size, device=self.device)
         if greedy:
             return GreedyTokens(self._greedy_tokens(x).view(B, blk))
+        normed = isinstance(x, _SeqPar)
+        x = self._rms(x, self.dec.norm) if normed else x
         h = x.view(B, blk, -1)[:, r0:r1].reshape(B * (r1 - r0), -1)
-        return self._logits(h).view(B, r1 - r0, -1)
+        return self._logits(h, normed).view(B, r1 - r0, -1)
 
     def _greedy_tokens(self, x):
         """Greedy tokens of hidden rows: final norm, then the LM-head GEMM with its argmax epilogue."""
@@ -260,11 +265,19 @@ class Runtime:
             if bool(sel.any()):
                 x = x.clone()
                 x[sel] = feats[fidx.reshape(-1)[sel]].to(x.dtype)
-        for i, layer in enumerate(self.dec.layers):
+        layers = self.dec.layers
+        seqpar = self.tp is not None and getattr(self.tp, "seq_parallel", False)
+        if seqpar:     # this rank's residual rows; the first input norm runs on the replicated embedding
+            x = _SeqPar(self.tp.shard(x), self._rms(x, layers[0].input_norm), layers[0].input_norm)
+        for i, layer in enumerate(layers):
+            if seqpar:
+                x.next = layer.post_norm
             if self.kinds[i] == "full_attention":
                 x = self._attn(st, i, layer, x)
             else:
                 x = self._gdn(st, i, layer, x)
+            if seqpar:
+                x.next = layers[i + 1].input_norm if i + 1 < len(layers) else self.dec.norm
             x = self._mlp(layer, x)
         return x
 
@@ -345,6 +358,10 @@ class Runtime:
 
     # ------------------------------------------------------------------ layers
     def _rms(self, x, w):
+        if isinstance(x, _SeqPar):          # normalised and gathered by the previous sublayer's output
+            if x.norm is not w:
+                raise RuntimeError("sequence-parallel stream normalised with another weight")
+            return x.h
         if self.cuda:
             h = torch.empty_like(x)
             self.C.rmsnorm_fwd(x, w, self.cfg.eps, h)
@@ -352,6 +369,9 @@ class Runtime:
         return R.rmsnorm(x, w, self.cfg.eps)
 
     def _lin(self, x, w, residual=None):
+        if isinstance(residual, _SeqPar):
+            xs, h = self.tp.reduce_norm(x, w, residual.xs, residual.next, self.cfg.eps)
+            return _SeqPar(xs, h, residual.next)
         if self.tp is not None and residual is not None:
             return self.tp.row_parallel(x, w, residual)
         if self.cuda:
@@ -394,8 +414,9 @@ class Runtime:
             raise NotImplementedError("tensor parallelism for layers with output norms")
         return x + self._rms(self._lin(a, w), post_norm)
 
-    def _logits(self, h):
-        h = self._rms(h, self.dec.norm)
+    def _logits(self, h, normed=False):
+        if not normed:
+            h = self._rms(h, self.dec.norm)
         W = self.dec.lm_shard if self.tp is not None else self.dec.lm_weight
         if self.cuda:
             out = torch.empty(h.shape[0], W.shape[0], dtype=torch.float32, device=h.device)
@@ -494,11 +515,17 @@ class Runtime:
                 kbuf = torch.empty(M, Hv, dk, dtype=x.dtype, device=x.device)
                 ubuf = torch.empty(M, Hv, dv, dtype=x.dtype, device=x.device)
                 gbuf = torch.empty(M, Hv, dtype=torch.float32, device=x.device)
-                # the gated RMSNorm rides in the canvas kernel's epilogue: o receives y directly
-                self.C.gdn_canvas_tc(mixed, ga, gb, a_log, dtb, o, kbuf, ubuf, gbuf, self.ssm[i], st.slot_t, blk,
-                                     Hk, Hv, st.n_clean, dk ** -0.5, self.err, z=z, gnorm_w=layer.gnorm, eps=cfg.eps)
                 st.gdn[i] = (mixed, kbuf, ubuf, gbuf, proj)
-                return self._lin(o, layer.w_out, x)
+                if self.gdn_fused_norm:    # o receives the normalised, gated rows directly
+                    self.C.gdn_canvas_tc(mixed, ga, gb, a_log, dtb, o, kbuf, ubuf, gbuf, self.ssm[i], st.slot_t,
+                                         blk, Hk, Hv, st.n_clean, dk ** -0.5, self.err, z=z, gnorm_w=layer.gnorm,
+                                         eps=cfg.eps)
+                    return self._lin(o, layer.w_out, x)
+                self.C.gdn_canvas_tc(mixed, ga, gb, a_log, dtb, o, kbuf, ubuf, gbuf, self.ssm[i], st.slot_t, blk,
+                                     Hk, Hv, st.n_clean, dk ** -0.5, self.err)
+                y = torch.empty(M, vd, dtype=x.dtype, device=x.device)
+                self.C.gdn_gnorm_fwd(o, z, layer.gnorm, y, Hv, cfg.eps)
+                return self._lin(y, layer.w_out, x)
             else:
                 prep = torch.empty(self.C.gdn_prep_numel(M, Hk, Hv), dtype=torch.float32, device=x.device)
                 self.C.gdn_canvas(mixed, ga, gb, a_log, dtb, o, prep, self.ssm[i], st.slot_t, blk, Hk, Hv,
@@ -537,6 +564,23 @@ class Runtime:
         y = G.gated_rmsnorm(o, z.reshape(B, blk, Hv, dv), layer.gnorm, cfg.eps)
         st.gdn[i] = (q, k, v, g, beta, conv_in)
         return self._lin(y.reshape(M, vd), layer.w_out, x)
+
+
+class _SeqPar:
+    """The residual stream in tensor-parallel sequence-parallel form: this rank's rows ``xs`` of the
+    residual and ``h`` = RMSNorm(x) * ``norm`` over all rows (the gathered input of the next
+    sublayer).  ``next`` names the norm weight that the next row-parallel output applies."""
+
+    def __init__(self, xs, h, norm):
+        self.xs, self.h, self.norm, self.next = xs, h, norm, None
+
+    @property
+    def dtype(self):
+        return self.h.dtype
+
+    @property
+    def device(self):
+        return self.h.device
 
 
 class GreedyTokens:

@@ -8,9 +8,14 @@ Megatron-style split (survey P4; the reference leaves TP to SGLang's engine flag
                   ``out_proj`` row-parallel
   MLP             gate / up rows split, ``down_proj`` row-parallel
   LM head         vocabulary split; greedy tokens come from each rank's (max, argmax) pair
-Each row-parallel GEMM writes its partial sum into this rank's symmetric peer buffer and one
-all-reduce kernel (``csrc/symm.cu``) reads every rank's partial over NVLink, adds the residual and
-writes the layer output -- no NCCL on the decode path.
+Between sublayers the residual stream is sequence-parallel (``seq_parallel=True``, the default):
+rank r keeps only its block of rows of the residual, and after every row-parallel GEMM (partial sum
+in this rank's symmetric buffer) one kernel (``csrc/symm.cu``, ``rs_norm_ag``) reduce-scatters the
+partials to the owning ranks, adds the residual, applies the next sublayer's RMSNorm and
+all-gathers the normalised rows into every rank's input buffer of the next column-parallel GEMM --
+(W-1)/W of the activation crosses NVLink each way.  ``seq_parallel=False`` keeps replicated
+residuals with a one-shot all-reduce kernel (every rank reads all partials), and ``fused=True`` the
+all-reduce inside the GEMM epilogue.  No NCCL on the decode path.
 """
 import copy
 
@@ -102,7 +107,10 @@ class TPContext:
     """Per-process TP state: the process group, the symmetric buffers of the row-parallel
     all-reduces and the vocabulary-parallel greedy pick.
 
-    ``fused=False`` (default): the GEMM writes this rank's partial into its symmetric buffer and a
+    ``seq_parallel=True`` (default): the runtime keeps this rank's block of residual rows and calls
+    ``reduce_norm`` after every row-parallel GEMM (reduce-scatter + residual + RMSNorm + all-gather
+    in one kernel, two barriers).
+    ``seq_parallel=False``: the GEMM writes this rank's partial into its symmetric buffer and a
     one-shot all-reduce kernel pulls every rank's partial over NVLink and adds the residual.
     ``fused=True``: every row-parallel GEMM runs the all-reduce in its own epilogue
     (``csrc/gemm_sm100.cu``, ``gemm_bf16_allreduce``): partial tiles are pushed over NVLink into
@@ -111,14 +119,19 @@ class TPContext:
     is still about twice as slow as the two-kernel path on decode and prefill shapes, so it is
     opt-in until its exchange is faster."""
 
-    def __init__(self, max_rows, hidden, group=None, fused=False):
+    def __init__(self, max_rows, hidden, group=None, fused=False, seq_parallel=True):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.heap = SymmetricHeap(group)
         self.max_rows, self.hidden = max_rows, hidden
         self.fused = fused and hidden % 64 == 0
+        self.seq_parallel = seq_parallel and not self.fused and hidden % 8 == 0 and hidden <= 8192
         self.turn = 0
+        if self.seq_parallel:
+            self.part = self.heap.alloc(max_rows * hidden, torch.bfloat16)
+            self.gath = self.heap.alloc(max_rows * hidden, torch.bfloat16)
+            self.sp_ctr = torch.zeros(2, dtype=torch.int32, device="cuda")
         if self.fused:
             self.tiles_cap = -(-max_rows // 128) * -(-hidden // 256)
             self.recv = self.heap.alloc(2 * self.world * max_rows * hidden, torch.bfloat16)
@@ -128,12 +141,41 @@ class TPContext:
             sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
             self.ws = torch.empty(sms * 128 * 256, dtype=torch.float32, device="cuda")
             self.tile_ctr = torch.zeros(self.tiles_cap * 4, dtype=torch.int32, device="cuda")
-        else:
+        elif not self.seq_parallel:
             self.bufs = [self.heap.alloc(max_rows * hidden, torch.bfloat16) for _ in range(2)]
+
+    def own_rows(self, rows):
+        """(first row, count) of the residual rows this rank owns out of ``rows``."""
+        per = -(-rows // self.world)
+        r0 = min(rows, self.rank * per)
+        return r0, min(rows, r0 + per) - r0
+
+    def shard(self, x):
+        """This rank's rows of a replicated residual stream."""
+        r0, n = self.own_rows(x.shape[0])
+        return x[r0:r0 + n].contiguous()
+
+    def reduce_norm(self, a, w, xs, norm_w, eps):
+        """Row-parallel output at a sequence-parallel boundary: ``xs += rows of sum_r a_r w_r^T``
+        (this rank's rows, in place) and the all-gathered ``RMSNorm(x) * norm_w`` of every row,
+        returned as a view of this rank's gather buffer (valid until the next call)."""
+        from ..ops import blocks
+        M = a.shape[0]
+        if M > self.max_rows:
+            raise RuntimeError(f"{M} rows exceed the TP buffers ({self.max_rows})")
+        part = self.part.local[:M * self.hidden].view(M, self.hidden)
+        blocks.gemm(blocks.TN, a, w, part)
+        r0, n = self.own_rows(M)
+        assert xs.shape[0] == n
+        blocks.ext().symm_rs_norm_ag(self.part.ptrs, self.gath.ptrs, self.heap.flags.ptrs, self.rank, self.sp_ctr,
+                                     r0, xs, norm_w, eps, self.heap.err)
+        return xs, self.gath.local[:M * self.hidden].view(M, self.hidden)
 
     def next_buffer(self, rows):
         if rows > self.max_rows:
             raise RuntimeError(f"{rows} rows exceed the TP buffers ({self.max_rows})")
+        if not hasattr(self, "bufs"):      # replicated-residual calls in sequence-parallel mode (collective)
+            self.bufs = [self.heap.alloc(self.max_rows * self.hidden, torch.bfloat16) for _ in range(2)]
         b = self.bufs[self.turn]
         self.turn ^= 1
         return b, b.local[:rows * self.hidden].view(rows, self.hidden)
