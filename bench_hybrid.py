@@ -86,12 +86,16 @@ def timed(step_fn, args, world):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    from bench import ClockSampler, physical_gpu_index
+    clocks = ClockSampler(physical_gpu_index(int(os.environ.get("LOCAL_RANK", "0"))))
+    clocks.start()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for i in range(args.warmup, args.warmup + args.steps):
         step_fn(i, i)
     t1.record()
     torch.cuda.synchronize()
+    args.clocks = clocks.stop()
     ms = t0.elapsed_time(t1) / args.steps
     if world > 1:
         t = torch.tensor([ms], device="cuda")
@@ -201,6 +205,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True, "scaling": "weak",
             "dtype": "bf16", "data": "synthetic uniform token ids, random-init weights",
             "peak_mem_gb": round(torch.cuda.max_memory_allocated() / 1e9, 1),
+            "clocks": getattr(args, "clocks", None),
             "config": {"model": f"Qwen3.5-4B-style hybrid ({args.layers}L)", "micro_batch": args.mb,
                        "row": ("[S 2048 | x_t 1024 | x_0 1024] x 2 views, linear layers on [S | x_t] and [x_0]"
                                if causal else "[prompt 2048 | response 1024] as [x0 ; xt_1 ; xt_2] (9216 forward tokens)"),
