@@ -255,7 +255,9 @@ def _seqpar_worker(rank, world, port, q):
 
         from trida_stack_b200.serve import Runtime
         from trida_stack_b200.serve.tp import shard_decoder
-        dec = _init(_hybrid(128)).to("cuda", bf)
+        cfg = _hybrid(128)
+        cfg.lin_v_heads = 8          # per-rank in_proj width (2 x value heads in the gates) stays 16-byte aligned
+        dec = _init(cfg).to("cuda", bf)
         torch.manual_seed(4)
         prompts = [torch.randint(0, 500, (40,)).tolist() for _ in range(3)]
         canv = [torch.randint(0, 500, (9,)).tolist() for _ in range(3)]
