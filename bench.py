@@ -47,7 +47,7 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--layers", type=int, default=36, help="debug only: fewer layers (reported as reduced)")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--phase-split", type=int, default=0, metavar="STEPS",
+    p.add_argument("--phase-split", type=int, default=2, metavar="STEPS",
                    help="after the timed steps, STEPS more steps with CUDA events around forward, backward and "
                         "the optimizer step (device ms, mean over steps, max over ranks) in the JSON line")
     p.add_argument("--kernel-breakdown", type=int, default=0, metavar="STEPS",

@@ -80,10 +80,12 @@ __global__ void __launch_bounds__(NTH, 1)
   uint64_t* u_full = bars + 1;       // [RING]
   uint64_t* u_empty = bars + 6;      // [RING]
   uint64_t* s_full = bars + 11;      // [2]
+  // [2]: P_i written completes p_full[i & 1] (S_{i+1} is issued before PV_i, so a softmax warp can
+  // finish tile i+1 while another is still on tile i; one barrier per parity keeps their arrivals apart)
   uint64_t* p_full = bars + 13;
-  uint64_t* pv_done = bars + 14;     // [2]
-  uint64_t* drain = bars + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* pv_done = bars + 15;     // [2]
+  uint64_t* drain = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
 
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h / p.group;
@@ -101,7 +103,8 @@ __global__ void __launch_bounds__(NTH, 1)
     }
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
-    mbar_init(p_full, 2 * BM);
+    mbar_init(&p_full[0], 2 * BM);
+    mbar_init(&p_full[1], 2 * BM);
     mbar_init(&pv_done[0], 1);
     mbar_init(&pv_done[1], 1);
     mbar_init(drain, 1);
@@ -190,11 +193,11 @@ __global__ void __launch_bounds__(NTH, 1)
       if (ok && n > 0) ok = issue_s(0);
       for (int i = 1; ok && i < n; ++i) {
         if (!(ok = issue_s(i))) break;
-        if (!(ok = mbar_wait(p_full, (i - 1) & 1, p.err, 5))) break;
+        if (!(ok = mbar_wait(&p_full[(i - 1) & 1], ((i - 1) >> 1) & 1, p.err, 5))) break;
         tc_fence_after();
         ok = issue_pv(i - 1);
       }
-      if (ok && n > 0 && mbar_wait(p_full, (n - 1) & 1, p.err, 6)) {
+      if (ok && n > 0 && mbar_wait(&p_full[(n - 1) & 1], ((n - 1) >> 1) & 1, p.err, 6)) {
         tc_fence_after();
         issue_pv(n - 1);
       }
@@ -301,7 +304,7 @@ __global__ void __launch_bounds__(NTH, 1)
         l_run += ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
       }
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[i & 1]);
     }
     if (ok && n > 0) ok = mbar_wait(&pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1, p.err, 10);
     xch[half * BM + r] = l_run;

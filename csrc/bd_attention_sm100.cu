@@ -97,7 +97,11 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   uint64_t* v_full = bars + 11;    // [2]
   uint64_t* v_empty = bars + 13;   // [2]
   uint64_t* q_tmem = bars + 15;    // the softmax warps have copied Q into TMEM
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  // p_full[0] = bars + 7, p_full[1] = bars + 16: P_i written completes p_full[i & 1] (S_{i+1} is
+  // issued before PV_i, so a softmax warp can finish tile i+1 while another is still on tile i; one
+  // barrier per parity keeps their arrivals apart)
+  uint64_t* p_full1 = bars + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
 
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h / p.group;
@@ -120,6 +124,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
     mbar_init(p_full, 2 * BM);
+    mbar_init(p_full1, 2 * BM);
     mbar_init(q_tmem, 2 * BM);
     mbar_init(&pv_done[0], 1);
     mbar_init(&pv_done[1], 1);
@@ -208,13 +213,13 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         umma_commit(&k_empty[s]);
         if (i < 6) DBG_STAMP(3 + 4 * i);
         if (i > 0) {
-          if (!(ok = mbar_wait(p_full, (i - 1) & 1, p.err, 5))) break;
+          if (!(ok = mbar_wait(((i - 1) & 1) ? p_full1 : p_full, ((i - 1) >> 1) & 1, p.err, 5))) break;
           if (i < 6) DBG_STAMP(4 + 4 * i);
           tc_fence_after();
           if (!(ok = issue_pv(i - 1))) break;
         }
       }
-      if (ok && n > 0 && mbar_wait(p_full, (n - 1) & 1, p.err, 6)) {
+      if (ok && n > 0 && mbar_wait(((n - 1) & 1) ? p_full1 : p_full, ((n - 1) >> 1) & 1, p.err, 6)) {
         tc_fence_after();
         issue_pv(n - 1);
       }
@@ -345,7 +350,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         l_run += ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
       }
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive((i & 1) ? p_full1 : p_full);
       if (threadIdx.x == 0 && i < 6) DBG_STAMP(33 + 5 * i);
     }
     if (ok && n > 0) ok = mbar_wait(&pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1, p.err, 10);

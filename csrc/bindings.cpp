@@ -436,9 +436,10 @@ static int paged_maxlen(const at::Tensor& kc, const c10::optional<at::Tensor>& p
   return (int)(maxpages * 64);
 }
 
+// With `err` (the device error word) the tensor-core kernel runs; without it the warp-MMA kernel.
 void canvas_attention(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& slot,
                       const at::Tensor& pos, const at::Tensor& out, int64_t blk, int64_t n_clean, int64_t max_keys,
-                      double scale, const c10::optional<at::Tensor>& ptab) {
+                      double scale, const c10::optional<at::Tensor>& ptab, const c10::optional<at::Tensor>& err) {
   CHECK_BF16(q); CHECK_BF16(kc); CHECK_BF16(vc); CHECK_BF16(out);
   TORCH_CHECK(q.dim() == 3 && q.is_contiguous() && out.is_contiguous() && kc.dim() == 4 && kc.is_contiguous() &&
               vc.is_contiguous(), "canvas attention layouts");
@@ -447,8 +448,21 @@ void canvas_attention(const at::Tensor& q, const at::Tensor& kc, const at::Tenso
   int64_t maxpages = 0;
   const int Hq = q.size(1), D = q.size(2), Hkv = kc.size(2), maxlen = paged_maxlen(kc, ptab, maxpages);
   TORCH_CHECK(max_keys <= maxlen, "max_keys exceeds the cache length");
-  at::Tensor work = at::empty({trida::canvas_work_floats(B, blk, Hq, D, max_keys)}, q.options().dtype(at::kFloat));
   c10::cuda::CUDAGuard g(q.device());
+  if (err.has_value() && err->defined()) {
+    TORCH_CHECK(err->scalar_type() == at::kInt && err->is_cuda(), "err must be a CUDA int32 word");
+    const int64_t nw = trida::canvas_tc_work_floats(B, blk, Hq, Hkv, D, max_keys);
+    at::Tensor work = nw > 0 ? at::empty({nw}, q.options().dtype(at::kFloat)) : at::Tensor();
+    const int n_slots = maxpages ? (int)ptab->size(0) : (int)kc.size(0);
+    const int rc = trida::canvas_attention_tc(cbf(q), cbf(kc), cbf(vc), kc.size(0) * kc.size(1), n_slots, slot.data_ptr<int>(),
+                                              pos.data_ptr<int>(), mbf(out), nw > 0 ? work.data_ptr<float>() : nullptr,
+                                              B, blk, n_clean, Hq, Hkv, D, maxlen, max_keys, (float)scale,
+                                              err->data_ptr<int>(), stream(), maxpages ? ptab->data_ptr<int>() : nullptr,
+                                              (int)maxpages);
+    TORCH_CHECK(rc == 0, "canvas_attention_tc failed with code ", rc);
+    return;
+  }
+  at::Tensor work = at::empty({trida::canvas_work_floats(B, blk, Hq, D, max_keys)}, q.options().dtype(at::kFloat));
   const int rc = trida::canvas_attention(cbf(q), cbf(kc), cbf(vc), slot.data_ptr<int>(), pos.data_ptr<int>(), mbf(out),
                                          work.data_ptr<float>(), B, blk, n_clean, Hq, Hkv, D, maxlen, max_keys,
                                          (float)scale, stream(), maxpages ? ptab->data_ptr<int>() : nullptr,
@@ -1183,7 +1197,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale"), py::arg("final_state") = py::none());
   m.def("canvas_attention", &canvas_attention, py::arg("q"), py::arg("kc"), py::arg("vc"), py::arg("slot"),
         py::arg("pos"), py::arg("out"), py::arg("blk"), py::arg("n_clean"), py::arg("max_keys"), py::arg("scale"),
-        py::arg("ptab") = py::none());
+        py::arg("ptab") = py::none(), py::arg("err") = py::none());
   m.def("kv_append", &kv_append, py::arg("k"), py::arg("v"), py::arg("kc"), py::arg("vc"), py::arg("slot"),
         py::arg("pos"), py::arg("blk"), py::arg("ptab") = py::none());
   m.def("canvas_conv", &canvas_conv);

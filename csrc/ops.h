@@ -175,6 +175,16 @@ int canvas_attention(const bf16* q, const bf16* kc, const bf16* vc, const int* s
                      float* work, int B, int blk, int n_clean, int Hq, int Hkv, int D, int maxlen, int max_keys,
                      float scale, cudaStream_t s, const int* ptab = nullptr, int maxpages = 0);
 int64_t canvas_work_floats(int B, int blk, int Hq, int D, int max_keys);
+// merge of split-K partial rows (unnormalised o, scaled log2 max, sum) into bf16 out [B * blk, Hq, D]
+void canvas_combine(const float* po, const float* pm, const float* pl, bf16* out, int B, int nsplit, int Hq, int blk,
+                    int D, cudaStream_t s);
+// tensor-core canvas attention (canvas_attn_sm100.cu): cache viewed as [cache_rows, Hkv, D] (a paged
+// cache's pages * 64 rows, or slots * maxlen); `work` holds canvas_tc_work_floats floats (0: none needed)
+int canvas_attention_tc(const bf16* q, const bf16* kc, const bf16* vc, int64_t cache_rows, int n_slots,
+                        const int* slot, const int* pos, bf16* out, float* work, int B, int blk, int n_clean, int Hq,
+                        int Hkv, int D, int maxlen, int max_keys, float scale, int* err, cudaStream_t s,
+                        const int* ptab, int maxpages);
+int64_t canvas_tc_work_floats(int B, int blk, int Hq, int Hkv, int D, int max_keys);
 void kv_append(const bf16* k, const bf16* v, int64_t ldv, bf16* kc, bf16* vc, const int* slot, const int* pos, int B,
                int blk, int Hkv, int D, int maxlen, cudaStream_t s, const int* ptab = nullptr, int maxpages = 0);
 void canvas_conv(const bf16* x, int64_t ldx, const bf16* win, const bf16* w, bf16* y, int64_t ldy, const int* slot,

@@ -498,6 +498,13 @@ int canvas_attention(const bf16* q, const bf16* kc, const bf16* vc, const int* s
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
+void canvas_combine(const float* po, const float* pm, const float* pl, bf16* out, int B, int nsplit, int Hq, int blk,
+                    int D, cudaStream_t s) {
+  const int64_t warps = (int64_t)B * Hq * blk;
+  serve::canvas_combine_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(po, pm, pl, out, B, nsplit, Hq,
+                                                                                   blk, D);
+}
+
 int64_t canvas_work_floats(int B, int blk, int Hq, int D, int max_keys) {
   const int nsplit = (max_keys + 255) / 256;
   const int64_t rows = (int64_t)B * nsplit * Hq * blk;

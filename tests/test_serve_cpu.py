@@ -322,3 +322,43 @@ def test_kv_page_allocator():
         p.ensure(0, 5 * PAGE)
     p.release(1)
     assert p.used() == 2 and p.ensure(2, 2 * PAGE) and p.owned[2] == [2, 3]
+
+
+def test_guards_name_bad_steps():
+    """TRIDA_GUARDS=1 turns a bad slot, token, canvas shape, commit advance or page-table state into
+    a named error at the call (checked on the CPU runtime; the same checks run before CUDA steps)."""
+    from trida_stack_b200.serve.runtime import PAGE, KVPages
+    rt = Runtime(tiny_hybrid(), max_slots=3, max_len=64)
+    rt.guards = True
+    a, b = rt.alloc(), rt.alloc()
+    rt.prefill([a, b], [[1, 2, 3, 4], [5, 6, 7, 8]])
+    with pytest.raises(RuntimeError, match="twice"):
+        rt.canvas([a, a], [[1, 2], [3, 4]], 1)
+    free = rt.free[-1]
+    with pytest.raises(RuntimeError, match="not allocated"):
+        rt.canvas([a, free], [[1, 2], [3, 4]], 1)
+    with pytest.raises(RuntimeError, match="vocabulary"):
+        rt.canvas([a, b], [[1, 2], [3, 97]], 1)
+    with pytest.raises(RuntimeError, match="n_clean"):
+        rt.canvas([a, b], [[1, 2], [3, 4]], 3)
+    lg = rt.canvas([a, b], [[1, 2], [3, 4]], 1)
+    assert torch.isfinite(lg).all()
+    with pytest.raises(RuntimeError, match="outside"):
+        rt.commit([a, b], [1, 2])                  # advance past n_clean
+    with pytest.raises(RuntimeError, match="pending canvas has"):
+        rt.commit([b, a], [1, 1])
+    rt.commit([a, b], [1, 1])
+    with pytest.raises(RuntimeError, match="without a pending canvas"):
+        rt.commit([a, b], [1, 1])
+    # page-table ownership
+    p = KVPages(n_pages=6, n_slots=3, max_pages=4)
+    p.ensure(0, 2 * PAGE)
+    p.ensure(1, PAGE)
+    p.check([0, 1])
+    p.owned[1].append(p.owned[0][0])               # one page handed to two slots
+    with pytest.raises(RuntimeError, match="held by slots"):
+        p.check([0, 1])
+    p.owned[1].pop()
+    p.table[0, 1] = 5                              # table row disagrees with the owner list
+    with pytest.raises(RuntimeError, match="page table"):
+        p.check([0, 1])

@@ -5,7 +5,7 @@
     python -m trida_stack_b200.ops.kernel_bench --op gdn_fwd|gdn_bwd [--length 3072] [--gdn-path chunk|scan]
                                                      [--gdn-layout two_stream|causal]
     python -m trida_stack_b200.ops.kernel_bench --op gdn_core_fwd|gdn_core_bwd [--length 3072]
-    python -m trida_stack_b200.ops.kernel_bench --op canvas_attn|canvas_gdn|canvas_gdn_tc|commit_gdn_tc
+    python -m trida_stack_b200.ops.kernel_bench --op canvas_attn|canvas_attn_tc|canvas_gdn|canvas_gdn_tc|commit_gdn_tc
                                                      [--requests 64 --blk 7]
     python -m trida_stack_b200.ops.kernel_bench --op rmsnorm_fwd|rmsnorm_bwd|qk_rope_fwd|qk_rope_bwd|
                                                      swiglu_fwd|swiglu_bwd [--m 24576 --hidden 2560]
@@ -199,7 +199,7 @@ def bench_canvas(a, which):
     C = ext()
     B, blk = a.requests, a.blk
     dev = "cuda"
-    if which == "canvas_attn":
+    if which in ("canvas_attn", "canvas_attn_tc"):
         Hq, Hkv, d, maxlen = 16, 4, 256, 1088
         kc = torch.randn(B, maxlen, Hkv, d, device=dev, dtype=torch.bfloat16)
         vc = torch.randn_like(kc)
@@ -207,8 +207,12 @@ def bench_canvas(a, which):
         out = torch.empty_like(q)
         slot = torch.arange(B, device=dev, dtype=torch.int32)
         pos = torch.full((B,), maxlen - blk, device=dev, dtype=torch.int32)
+        err = None
+        if which == "canvas_attn_tc":          # the tensor-core kernel runs when given the error word
+            from .blocks import device_error_word
+            err = device_error_word(torch.device(dev))
         ms = _time(lambda: C.canvas_attention(q, kc, vc, slot, pos, out, blk, (blk + 1) // 2, maxlen,
-                                              1.0 / math.sqrt(d)), a.warmup, a.iters)
+                                              1.0 / math.sqrt(d), None, err), a.warmup, a.iters)
         nbytes = 2 * B * maxlen * Hkv * d * 2
         return ms, {"gbs": nbytes / ms / 1e6}, None, nbytes
     Hk, Hv = 16, 32
@@ -289,7 +293,7 @@ def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--op", required=True,
                     choices=["gemm", "gemm_swiglu", "attn_fwd", "attn_bwd", "gdn_fwd", "gdn_bwd", "gdn_core_fwd", "gdn_core_bwd",
-                             "canvas_attn", "canvas_gdn", "canvas_gdn_tc", "commit_gdn_tc",
+                             "canvas_attn", "canvas_attn_tc", "canvas_gdn", "canvas_gdn_tc", "commit_gdn_tc",
                              "rmsnorm_fwd", "rmsnorm_bwd", "qk_rope_fwd", "qk_rope_bwd", "swiglu_fwd", "swiglu_bwd"])
     ap.add_argument("--m", type=int, default=24576)
     ap.add_argument("--n", type=int, default=6144)

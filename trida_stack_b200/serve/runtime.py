@@ -16,6 +16,7 @@ the extension's kernels; on CPU the same step is stated in PyTorch (the oracle o
 the runtime of the CPU tests).
 """
 import math
+import os
 
 import torch
 import torch.nn.functional as F
@@ -25,6 +26,13 @@ from ..ops import reference as R
 
 PREFILL_CHUNK = 64
 PAGE = 64                 # positions per KV page
+# TRIDA_GUARDS=1: bounds guards on every step -- slot ids, token ids, positions, commit advances and
+# page-table ownership on the host, then the device error word and the logits after the step (a
+# device sync, which is why they are off unless asked).  A race or a bad index then surfaces as a
+# named error at the call that caused it instead of a corrupted cache or a fault in a later kernel.
+# The reference keeps the same kind of opt-in guards in its vLLM self-spec backend
+# (inference/zoro-1/vllm/vllm_native_diffusion/qwen3_5_diffusion.py:92-95, 1146, 1882-1888).
+GUARDS = os.environ.get("TRIDA_GUARDS") == "1"
 
 
 class Runtime:
@@ -36,6 +44,7 @@ class Runtime:
         requests and many short ones share the same memory."""
         self.dec = decoder
         self.tp = tp
+        self.guards = GUARDS
         self.cfg = cfg = decoder.cfg
         p = next(decoder.parameters())
         self.device = torch.device(device) if device is not None else p.device
@@ -89,6 +98,9 @@ class Runtime:
             # gated RMSNorm in the canvas kernel's epilogue (TRIDA_GDN_FUSED_NORM=1) or as its own
             # kernel after it (default: measured 0.26 + 0.03 ms against 0.37 ms fused at 64 x 63 rows)
             self.gdn_fused_norm = os.environ.get("TRIDA_GDN_FUSED_NORM", "0") == "1"
+            # canvas attention on tensor cores (TMA-gathered query tiles, tcgen05 S / PV with TMEM
+            # accumulators), or the split-K warp-MMA kernel (TRIDA_CANVAS_ATTN=mma)
+            self.attn_tc = os.environ.get("TRIDA_CANVAS_ATTN", "tc") == "tc"
             self.err = blocks.device_error_word(self.device)
 
     # ------------------------------------------------------------------ slots
@@ -181,13 +193,24 @@ class Runtime:
         assert self.pending is None, "commit the previous canvas first"
         B = len(slots)
         blk = len(tokens[0])
+        if self.guards:
+            self._guard_canvas(slots, tokens, n_clean, blk)
         for s in slots:
             if self.pos[s] + blk > self.max_len:
                 raise RuntimeError(f"slot {s}: sequence exceeds the cache length {self.max_len}")
         self._ensure_pages(slots, blk)
+        if self.guards and self.paged:
+            self.pages.check([s for s in range(self.max_slots) if s not in self.free] + [self.dummy])
         r0, r1 = rows if rows is not None else (0, blk)
         if self._graphs is not None and (r0, r1) == (0, blk) and inject is None and rope_ang is None:
-            return self._canvas_graph(slots, tokens, n_clean, greedy)
+            out = self._canvas_graph(slots, tokens, n_clean, greedy)
+        else:
+            out = self._canvas_eager(slots, tokens, n_clean, B, blk, r0, r1, inject, rope_ang, greedy)
+        if self.guards:
+            self._guard_after(out)
+        return out
+
+    def _canvas_eager(self, slots, tokens, n_clean, B, blk, r0, r1, inject, rope_ang, greedy):
         tokens = torch.as_tensor(tokens, dtype=torch.long, device=self.device)
         st = _Step(self, slots, B, blk, n_clean)
         st.inject, st.rope_ang = inject, rope_ang
@@ -305,10 +328,66 @@ class Runtime:
         self.pending = g
         return GreedyTokens(g.am[:B]) if greedy else g.logits[:B]
 
+    # ------------------------------------------------------------------ guards (TRIDA_GUARDS=1)
+    def _guard_canvas(self, slots, tokens, n_clean, blk):
+        if len(set(slots)) != len(slots):
+            raise RuntimeError(f"[guards] a slot appears twice in one canvas step: {list(slots)}")
+        for s in slots:
+            if not 0 <= s < self.max_slots:
+                raise RuntimeError(f"[guards] slot {s} outside [0, {self.max_slots})")
+            if s in self.free:
+                raise RuntimeError(f"[guards] slot {s} is not allocated (released or never taken)")
+        if not 1 <= n_clean <= blk:
+            raise RuntimeError(f"[guards] n_clean={n_clean} outside [1, canvas rows {blk}]")
+        t = torch.as_tensor(tokens)
+        if t.dim() != 2 or t.shape[0] != len(slots) or t.shape[1] != blk:
+            raise RuntimeError(f"[guards] tokens of shape {tuple(t.shape)} for {len(slots)} slots x {blk} rows")
+        lo, hi = int(t.min()), int(t.max())          # a device sync when the tokens live on the GPU
+        if lo < 0 or hi >= self.cfg.vocab_size:
+            raise RuntimeError(f"[guards] token ids span [{lo}, {hi}] outside the vocabulary [0, {self.cfg.vocab_size})")
+
+    def _guard_attention(self, i, st, q, o, blk):
+        """Canvas attention output of layer ``i``: every row written and finite (device sync)."""
+        code = int(self.err.item())
+        bad = ~torch.isfinite(o.float()).all(-1)          # [rows, heads]
+        if code or bool(bad.any()):
+            rows = bad.any(-1).nonzero().flatten()[:8].tolist()
+            pos = st.pos_t.tolist() if hasattr(st, "pos_t") else None
+            raise RuntimeError(
+                f"[guards] canvas attention, layer {i}: error word {code}, {int(bad.sum())} non-finite "
+                f"(row, head) outputs, first rows {rows}; q finite {bool(torch.isfinite(q).all())}, "
+                f"B={st.B} blk={blk} n_clean={st.n_clean} max_keys={st.max_keys} "
+                f"pos=[{min(pos) if pos else None}, {max(pos) if pos else None}] kernel="
+                f"{'tc' if self.attn_tc else 'mma'}")
+
+    def _guard_after(self, logits):
+        """Device error word and finite logits after a step (device sync)."""
+        if self.cuda:
+            code = int(self.err.item())
+            if code:
+                raise RuntimeError(f"[guards] a kernel of this step gave up a bounded wait (code {code})")
+        if torch.is_tensor(logits) and logits.numel() and not bool(torch.isfinite(logits).all()):
+            raise RuntimeError("[guards] non-finite logits after the canvas step")
+        if isinstance(logits, GreedyTokens) and logits.tokens.numel():
+            t = logits.tokens
+            lo, hi = int(t.min()), int(t.max())
+            if lo < 0 or hi >= self.cfg.vocab_size:
+                raise RuntimeError(f"[guards] greedy tokens span [{lo}, {hi}] outside the vocabulary "
+                                   f"(an all-NaN logits row has no argmax)")
+
     @torch.no_grad()
     def commit(self, slots, adv):
         """Keep the first ``adv[b]`` canvas rows of every slot (1 <= adv <= n_clean)."""
         st = self.pending
+        if self.guards:
+            if st is None:
+                raise RuntimeError("[guards] commit without a pending canvas")
+            nc = st.st.n_clean if isinstance(st, _Graph) else st.n_clean
+            pend = st.st.slots if isinstance(st, _Graph) else st.slots
+            if list(slots) != list(pend):
+                raise RuntimeError(f"[guards] commit for slots {list(slots)} but the pending canvas has {list(pend)}")
+            if len(adv) != len(slots) or not all(1 <= a <= nc for a in adv):
+                raise RuntimeError(f"[guards] commit advances {list(adv)} outside [1, n_clean={nc}]")
         if isinstance(st, _Graph):
             g = st
             assert list(slots) == g.st.slots and all(1 <= a <= g.st.n_clean for a in adv)
@@ -447,8 +526,12 @@ class Runtime:
             ptab = self.ptab if self.paged else None
             self.C.kv_append(k, v, self.kc[i], self.vc[i], st.slot_t, st.pos_t, blk, ptab)
             o = torch.empty(M, Hq, d, dtype=x.dtype, device=x.device)
+            if self.guards:
+                o.fill_(float("nan"))                # rows the kernel leaves unwritten stay NaN
             self.C.canvas_attention(q, self.kc[i], self.vc[i], st.slot_t, st.pos_t, o, blk, st.n_clean, st.max_keys,
-                                    1.0 / math.sqrt(d), ptab)
+                                    1.0 / math.sqrt(d), ptab, self.err if self.attn_tc else None)
+            if self.guards and not torch.cuda.is_current_stream_capturing():
+                self._guard_attention(i, st, q, o, blk)
             o = o.view(M, Hq * d)
             if cfg.attn_output_gate:
                 og = torch.empty_like(o)
@@ -625,6 +708,23 @@ class KVPages:
     def release(self, slot):
         self.free.extend(reversed(self.owned[slot]))
         self.owned[slot] = []
+
+    def check(self, live):
+        """Guard: the pages of the ``live`` slots are in range, owned by exactly one slot, not on
+        the free list, and the table rows say so (raises naming the first violation)."""
+        seen = {}
+        free = set(self.free)
+        for s in live:
+            for i, pg in enumerate(self.owned[s]):
+                if not 0 <= pg < self.n_pages:
+                    raise RuntimeError(f"[guards] slot {s} page {i}: page {pg} outside the pool of {self.n_pages}")
+                if pg in seen:
+                    raise RuntimeError(f"[guards] page {pg} held by slots {seen[pg]} and {s}")
+                if pg in free:
+                    raise RuntimeError(f"[guards] page {pg} of slot {s} is also on the free list")
+                if int(self.table[s, i]) != pg:
+                    raise RuntimeError(f"[guards] page table [{s}, {i}] = {int(self.table[s, i])}, slot owns page {pg}")
+                seen[pg] = s
 
     def used(self):
         return self.n_pages - len(self.free)
