@@ -700,6 +700,17 @@ static int* err_word() {
 
 }  // namespace gemm100
 
+// Tile height (128 or 256 rows) by estimated time: the persistent CTAs take ceil(tiles / SMs) tiles
+// each, and a 128 x 256 tile costs about 0.56 of a 256 x 256 one (half the FLOPs, at ~0.8 instead of
+// ~0.9 of the tensor peak: each B slice feeds one MMA instead of two).  So 4032 x 2560 (160 tiles
+// of 256 rows = two waves, the second 8 % full) takes 128-row tiles (320 = three full-ish waves),
+// while every training shape keeps 256-row tiles.
+static int pick_mh(int M, int ntn, int sm_count) {
+  const int64_t t2 = (int64_t)((M + 255) / 256) * ntn, t1 = (int64_t)((M + 127) / 128) * ntn;
+  const int64_t w2 = (t2 + sm_count - 1) / sm_count, w1 = (t1 + sm_count - 1) / sm_count;
+  return 100 * w2 <= 56 * w1 ? 2 : 1;
+}
+
 int gemm_splitk(int M, int N, int K, int sm_count) {
   using namespace gemm100;
   const int tiles = ((M + 127) / 128) * ((N + BN - 1) / BN);
@@ -732,9 +743,8 @@ int gemm_bf16(GemmLayout layout, bool d_fp32, const GemmArgs& a, int tile, int s
               int splits, float* ws) {
   using namespace gemm100;
   if (a.batch != 1) return -20;
-  // tile 1: 128 x 256 tiles; tile 2: 256 x 256; otherwise 256-row tiles when they still fill the GPU
-  const int tiles256 = ((a.M + 255) / 256) * ((a.N + BN - 1) / BN);
-  const int mh = tile == 1 ? 1 : tile == 2 ? 2 : (splits == 1 && 2 * tiles256 >= sm_count ? 2 : 1);
+  // tile 1: 128 x 256 tiles; tile 2: 256 x 256; otherwise by estimated time (pick_mh)
+  const int mh = tile == 1 ? 1 : tile == 2 ? 2 : (splits == 1 ? pick_mh(a.M, (a.N + BN - 1) / BN, sm_count) : 1);
   const int BM = 128 * mh;
   if (a.batch != 1) return -20;
   if (splits < 1 || (splits > 1 && ws == nullptr)) return -21;
@@ -834,8 +844,7 @@ int gemm_bf16_swiglu(const GemmArgs& a, void* act, int64_t ld_act, int F, int ti
   using namespace gemm100;
   if (a.batch != 1 || F <= 0 || F % 64 != 0 || a.N != 2 * F) return -40;
   if (a.C != nullptr && a.beta != 0.f) return -41;
-  const int tiles256 = ((a.M + 255) / 256) * ((F + 127) / 128);
-  const int mh = tile == 1 ? 1 : tile == 2 ? 2 : (2 * tiles256 >= sm_count ? 2 : 1);
+  const int mh = tile == 1 ? 1 : tile == 2 ? 2 : pick_mh(a.M, (F + 127) / 128, sm_count);
   Params p;
   p.M = a.M; p.N = a.N; p.K = a.K;
   p.D = a.D; p.ldd = a.ldd; p.C = nullptr; p.ldc = a.ldd;
@@ -891,8 +900,7 @@ int gemm_argmax_tiles(int N) { return (N + gemm100::BN - 1) / gemm100::BN; }
 int gemm_bf16_argmax(const GemmArgs& a, float* am_val, int* am_idx, int64_t* out, int sm_count, cudaStream_t stream) {
   using namespace gemm100;
   if (a.batch != 1) return -20;
-  const int tiles256 = ((a.M + 255) / 256) * ((a.N + BN - 1) / BN);
-  const int mh = 2 * tiles256 >= sm_count ? 2 : 1;
+  const int mh = pick_mh(a.M, (a.N + BN - 1) / BN, sm_count);
   Params p;
   p.M = a.M; p.N = a.N; p.K = a.K;
   p.D = am_val; p.ldd = 0; p.C = nullptr; p.ldc = 0;
