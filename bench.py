@@ -56,6 +56,9 @@ def parse():
     p.add_argument("--shard", choices=["full", "zero2"], default="full",
                    help="full: decoder-layer weights sharded and gathered per layer over NVLink (FSDP full "
                         "shard, the reference's setup); zero2: replicated weights")
+    p.add_argument("--ref-tuned", action="store_true",
+                   help="reference arm only: add the reference trainer's own performance flags "
+                        "(--fused_ce --fsdp_keep_params --compile_mlp) to its stock configuration")
     p.add_argument("--comm", choices=["fused", "nccl"], default="fused",
                    help="multi-GPU optimizer traffic: fused peer-memory kernels or NCCL collectives")
     return p.parse_args()
@@ -273,6 +276,11 @@ def write_reference_checkpoint(path, layers):
                             pad_token="<|endoftext|>").save_pretrained(path)
 
 
+# the reference trainer's own performance options (train/cli.py): Liger fused linear CE, gathered
+# layer weights kept from forward to backward, torch.compile of each layer's MLP and norms
+REF_TUNED = ["--fused_ce", "--fsdp_keep_params", "--compile_mlp"]
+
+
 def run_reference(args, rank, world, local_rank):
     ref = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "train")):
@@ -287,7 +295,7 @@ def run_reference(args, rank, world, local_rank):
     rargs = build_parser().parse_args([
         "--model_id", ckpt, "--bd_size", str(BD), "--ar_loss_weight", "1.0", "--micro_batch_size", str(MB),
         "--grad_accum", "1", "--lr", "1e-5", "--max_length", str(PROMPT + RESP),
-        "--response_buckets", "512,1024,2048,4096", "--seed", "0"])
+        "--response_buckets", "512,1024,2048,4096", "--seed", "0"] + (REF_TUNED if args.ref_tuned else []))
     dev = setup_distributed(rargs)   # the reference's own NCCL init (set_device, then device_id)
     if rank == 0 and not os.path.exists(os.path.join(ckpt, "config.json")):
         write_reference_checkpoint(ckpt, args.layers)
@@ -414,6 +422,7 @@ def main():
             line["config"]["reference_path"] = ("baseline/_ref train.models.build.build_model + "
                                                 "train.distributed.shard_model (FSDP2) + flex_attention + "
                                                 "train.optimizer.apply_optimizer_step")
+            line["config"]["reference_flags"] = REF_TUNED if args.ref_tuned else "stock defaults"
         print(json.dumps(line), flush=True)
     if dist.is_initialized():
         dist.destroy_process_group()
