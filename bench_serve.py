@@ -96,6 +96,9 @@ def main():
     reqs = [eng.submit(__import__("trida_stack_b200.serve", fromlist=["Request"]).Request(
         p, args.max_new, SamplingParams(temperature=0.0))) for p in prompts(args.requests)]
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    from bench import ClockSampler, physical_gpu_index
+    clocks = ClockSampler(physical_gpu_index(int(os.environ.get("LOCAL_RANK", "0"))))
+    clocks.start()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     ev[0].record()
@@ -107,6 +110,7 @@ def main():
     ev[2].record()
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
+    clk = clocks.stop()
     prefill_ms = ev[0].elapsed_time(ev[1])
     decode_ms = ev[1].elapsed_time(ev[2])
     if world > 1:      # device time, max over ranks
@@ -124,7 +128,7 @@ def main():
         "metric": "self-spec decode tokens/s", "value": round(toks / (decode_ms / 1e3), 1), "unit": "tokens/s",
         "tokens_per_forward": round(s["tokens_per_forward"], 3), "p50_ttft_ms": round(s["p50_ttft_s"] * 1e3, 2),
         "prefill_ms": round(prefill_ms, 2), "decode_ms": round(decode_ms, 2), "decode_steps": steps,
-        "ms_per_step": round(decode_ms / max(steps, 1), 3), "wall_s": round(wall, 2), "tp": world,
+        "ms_per_step": round(decode_ms / max(steps, 1), 3), "wall_s": round(wall, 2), "tp": world, "clocks": clk,
         "config": {"model": f"Qwen3.5-4B-style hybrid ({args.layers}L)", "requests": args.requests,
                    "prompt": args.prompt, "max_new": args.max_new, "mode": args.mode, "n": args.gen_block,
                    "canvas_rows": 2 * args.gen_block - 1 if args.mode == "self-spec" else 1, "greedy": True,
