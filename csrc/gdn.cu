@@ -840,6 +840,11 @@ __device__ __forceinline__ void zero8(float (&v)[8]) {
   for (int e = 0; e < 8; ++e) v[e] = 0.f;
 }
 
+// SiLU and the logistic function from the fast exp / divide intrinsics; the exponent is clamped so the
+// divisor stays finite (below 2^126, where the fast divide is exact enough for bf16 results).
+__device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.f, 1.f + __expf(fminf(-x, 80.f))); }
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f + __expf(fminf(-x, 80.f))); }
+
 // x rows feeding output t: xs[j] for tap j (shift K - 1 - j); ring[i] holds x[t - 1 - i] of the same
 // stream when t - 1 - i >= t0 (the run start).
 template <int K>
@@ -884,10 +889,14 @@ __global__ void conv_fwd_kernel(const ConvArgs a) {
   const int c8 = (int)(gid % cpr) * 8;
   const int64_t run = gid / cpr;
   const int b = (int)(run / rpr), t0 = (int)(run % rpr) * CONV_RUN, t1 = min(t0 + CONV_RUN, a.T);
-  float w[4][8], ring[3][8], cur[8], xs[4][8];
+  float w[4][8], ring[3][8], cur[8], nxt[8], xs[4][8];
   load_w8<K>(a, c8, w);
+  load8(a.x + ((int64_t)b * a.T + t0) * a.ldx + c8, nxt);
   for (int t = t0; t < t1; ++t) {
-    load8(a.x + ((int64_t)b * a.T + t) * a.ldx + c8, cur);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) cur[e] = nxt[e];
+    // the next row's load is in flight during this row's taps and math
+    if (t + 1 < t1) load8(a.x + ((int64_t)b * a.T + t + 1) * a.ldx + c8, nxt);
     conv_taps<K>(a, b, t, t0, c8, cur, ring, xs);
     float out[8];
 #pragma unroll
@@ -895,7 +904,7 @@ __global__ void conv_fwd_kernel(const ConvArgs a) {
       float acc = 0.f;
 #pragma unroll
       for (int j = 0; j < 4; ++j) acc = fmaf(w[j][e], xs[j][e], acc);
-      out[e] = acc / (1.f + __expf(-acc));
+      out[e] = silu_fast(acc);
     }
     store8(a.y + ((int64_t)b * a.T + t) * a.ldy + c8, out);
     ring_push(ring, cur);
@@ -913,22 +922,32 @@ __global__ void conv_bwd_pre_kernel(const ConvArgs a, const bf16* dy, int64_t ld
   const int c8 = (int)(gid % cpr) * 8;
   const int64_t run = gid / cpr;
   const int b = (int)(run / rpr), t0 = (int)(run % rpr) * CONV_RUN, t1 = min(t0 + CONV_RUN, a.T);
-  float w[4][8], ring[3][8], cur[8], xs[4][8], wacc[4][8];
+  float w[4][8], ring[3][8], cur[8], xs[4][8], wacc[4][8], nx[8], ndy[8];
   load_w8<K>(a, c8, w);
 #pragma unroll
   for (int j = 0; j < 4; ++j) zero8(wacc[j]);
+  load8(a.x + ((int64_t)b * a.T + t0) * a.ldx + c8, nx);
+  load8(dy + ((int64_t)b * a.T + t0) * lddy + c8, ndy);
   for (int t = t0; t < t1; ++t) {
     const int64_t row = (int64_t)b * a.T + t;
-    load8(a.x + row * a.ldx + c8, cur);
-    conv_taps<K>(a, b, t, t0, c8, cur, ring, xs);
     float dyv[8], g[8];
-    load8(dy + row * lddy + c8, dyv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      cur[e] = nx[e];
+      dyv[e] = ndy[e];
+    }
+    // the next row's x and dy loads are in flight during this row's taps and math
+    if (t + 1 < t1) {
+      load8(a.x + (row + 1) * a.ldx + c8, nx);
+      load8(dy + (row + 1) * lddy + c8, ndy);
+    }
+    conv_taps<K>(a, b, t, t0, c8, cur, ring, xs);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       float pre = 0.f;
 #pragma unroll
       for (int j = 0; j < 4; ++j) pre = fmaf(w[j][e], xs[j][e], pre);
-      const float sg = 1.f / (1.f + __expf(-pre));
+      const float sg = sigmoid_fast(pre);
       g[e] = dyv[e] * sg * (1.f + pre * (1.f - sg));
     }
     float4* dp = reinterpret_cast<float4*>(dpre + row * a.C + c8);

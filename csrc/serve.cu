@@ -335,7 +335,7 @@ __global__ void canvas_conv4_kernel(const bf16* __restrict__ x, int64_t ldx, con
         acc = fmaf(wt[e][1], h[1][e], acc);
         acc = fmaf(wt[e][2], h[2][e], acc);
         acc = fmaf(wt[e][3], xv[e], acc);
-        out[e] = acc / (1.f + expf(-acc));
+        out[e] = __fdividef(acc, 1.f + __expf(fminf(-acc, 80.f)));   // SiLU (fast exp / divide)
       }
       store8(y + ((int64_t)b * blk + j) * ldy + c8, out);
 #pragma unroll
