@@ -15,7 +15,8 @@ Metric: tokens/s over the whole job, counted like the reference trainer's ``tot_
 (``input_ids.numel()`` per micro-batch, summed over ranks).  ``value``: K steps device-timed with
 CUDA events between a barrier + synchronize on both sides, max over ranks.  ``e2e``: the same K
 steps through ``TrainEngine.train_step`` with each step's batch copied from pinned host memory and
-the loss read back to the host.  Each step's working set (activations ~60 GB) is far larger than
+every step's loss read back to the host (one step late, so the host never stalls the GPU between
+steps; the reference arm reads its losses the same way).  Each step's working set (activations ~60 GB) is far larger than
 the 126 MB L2, so no explicit flush is needed between steps.
 """
 import argparse
@@ -151,6 +152,38 @@ def synthetic_batches(n, seed):
     return out
 
 
+class LaggedLossReads:
+    """Reads every step's loss on the host one step late: the loss goes to pinned memory by an async
+    copy and is read after the next step has been issued, so the GPU never waits for the host between
+    steps (the way a training loop logs).  Both arms use it."""
+
+    def __init__(self):
+        self.bufs = [torch.empty((), dtype=torch.float32).pin_memory() for _ in range(2)]
+        self.pend = []
+        self.n = 0
+        self.values = []
+
+    def push(self, loss):
+        buf = self.bufs[self.n % 2]
+        buf.copy_(loss.detach().float().reshape(()), non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self.pend.append((buf, ev))
+        self.n += 1
+        if len(self.pend) > 1:
+            self._read()
+
+    def _read(self):
+        buf, ev = self.pend.pop(0)
+        ev.synchronize()
+        self.values.append(float(buf))
+
+    def finish(self):
+        while self.pend:
+            self._read()
+        return self.values
+
+
 # ------------------------------------------------------------------------------------------------
 def run_ours(args, rank, world, local_rank):
     sys.path.insert(0, ROOT)
@@ -239,10 +272,12 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
         barrier()
         w0 = time.perf_counter()
+        reads = LaggedLossReads()
         for i in range(args.steps):
             loss, logs, lr, gnorm = engine.train_step([batches[args.warmup + i]], step)
-            float(loss.item())
+            reads.push(loss)
             step += 1
+        assert len(reads.finish()) == args.steps
         torch.cuda.synchronize()
         barrier()
         e2e_s = max_over_ranks((time.perf_counter() - w0) / args.steps)
@@ -339,10 +374,12 @@ def run_reference(args, rank, world, local_rank):
         torch.cuda.synchronize()
         barrier()
         w0 = time.perf_counter()
+        reads = LaggedLossReads()
         for i in range(args.steps):
             b = {k: v.to(dev, non_blocking=True) for k, v in batches[args.warmup + i].items()}
-            float(ref_step(b, step).item())
+            reads.push(ref_step(b, step))
             step += 1
+        assert len(reads.finish()) == args.steps
         torch.cuda.synchronize()
         barrier()
         e2e_s = max_over_ranks((time.perf_counter() - w0) / args.steps)
