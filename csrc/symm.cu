@@ -215,14 +215,34 @@ __global__ void norm_coef_kernel(Peers P, int rank, int world, unsigned epoch, i
 // `dst` with 16-byte P2P loads (plain loads through NVLink; no TMA, no multicast).  Consistency
 // comes from the callers: a shard only changes in the optimizer step, which ends with barrier();
 // the gathers of the next step run after it on every rank.
+// Each thread keeps GU 16-byte peer loads in flight before storing them: a load over NVLink takes
+// microseconds, so the link needs megabytes in flight per GPU (32 CTAs x 256 threads x 16 x 16 B = 2 MB),
+// where one load per thread (128 KB) reached 46 GB/s.
+constexpr int GU = 16;
 __global__ void gather_kernel(Peers P, int rank, int world, int64_t shard_len, bf16* __restrict__ dst) {
   const int64_t n8 = shard_len / 8;
   const int64_t total = n8 * world;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t k = i / n8, j = i - k * n8;
-    const int src = (int)((k + rank) % world);      // stagger the peers each rank reads first
-    const uint4 v = reinterpret_cast<const uint4*>(P.buf[src])[j];
-    reinterpret_cast<uint4*>(dst + (int64_t)src * shard_len)[j] = v;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t base = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < total; base += stride * GU) {
+    uint4 v[GU];
+#pragma unroll
+    for (int u = 0; u < GU; ++u) {
+      const int64_t i = base + u * stride;
+      if (i < total) {
+        const int64_t k = i / n8, j = i - k * n8;
+        const int src = (int)((k + rank) % world);      // stagger the peers each rank reads first
+        v[u] = reinterpret_cast<const uint4*>(P.buf[src])[j];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < GU; ++u) {
+      const int64_t i = base + u * stride;
+      if (i < total) {
+        const int64_t k = i / n8, j = i - k * n8;
+        const int src = (int)((k + rank) % world);
+        reinterpret_cast<uint4*>(dst + (int64_t)src * shard_len)[j] = v[u];
+      }
+    }
   }
 }
 

@@ -130,8 +130,13 @@ def main():
     dst = torch.empty(P, device="cuda", dtype=torch.bfloat16)
     report("gather_copy", _time(lambda: C.symm_gather_copy(sh.ptrs, rank, shard, dst), args.warmup, args.iters),
            (N - 1) / N * P * 2, f"bf16 [{P}] layer gather, one peer copy per shard (copy engines)")
+    ref = dst.clone()
+    dst.zero_()
     report("gather_kernel", _time(lambda: C.symm_gather(sh.ptrs, rank, shard, dst, 32), args.warmup, args.iters),
            (N - 1) / N * P * 2, f"bf16 [{P}] layer gather, P2P-load kernel (32 CTAs)")
+    if not torch.equal(dst, ref):
+        raise RuntimeError("the P2P gather kernel and the copy-engine gather disagree")
+    del ref
     g = grad.local.clone()
     report("nccl_reduce_scatter", _time(lambda: dist.reduce_scatter_tensor(gshard, g), args.warmup, args.iters),
            (N - 1) / N * P * 4, f"fp32 [{P}]")
