@@ -362,3 +362,33 @@ def test_guards_name_bad_steps():
     p.table[0, 1] = 5                              # table row disagrees with the owner list
     with pytest.raises(RuntimeError, match="page table"):
         p.check([0, 1])
+
+
+def test_engine_picks_gdn_canvas_path_by_canvas_size(monkeypatch):
+    """Small canvases take the per-token scan kernels, large ones the tensor-core chunk kernels; the
+    choice is made only before any slot holds state and yields to TRIDA_GDN_CANVAS."""
+    from types import SimpleNamespace
+
+    from trida_stack_b200.serve.engine import GDN_SCAN_MAX_ROWS, choose_gdn_canvas_path
+    monkeypatch.delenv("TRIDA_GDN_CANVAS", raising=False)
+
+    def fresh():
+        return SimpleNamespace(cuda=True, gdn_tc=True, free=[3, 2, 1, 0], max_slots=4, pending=None)
+    rt = fresh()
+    choose_gdn_canvas_path(rt, 7)
+    assert rt.gdn_tc is False
+    choose_gdn_canvas_path(rt, 63)
+    assert rt.gdn_tc is True
+    choose_gdn_canvas_path(rt, GDN_SCAN_MAX_ROWS)
+    assert rt.gdn_tc is False
+    rt = fresh()
+    rt.free.pop()                                   # a slot in use: its state layout is fixed
+    choose_gdn_canvas_path(rt, 7)
+    assert rt.gdn_tc is True
+    rt = fresh()
+    monkeypatch.setenv("TRIDA_GDN_CANVAS", "tc")
+    choose_gdn_canvas_path(rt, 7)
+    assert rt.gdn_tc is True
+    cpu = SimpleNamespace(cuda=False, free=[0], max_slots=1, pending=None)
+    choose_gdn_canvas_path(cpu, 7)
+    assert not hasattr(cpu, "gdn_tc")
